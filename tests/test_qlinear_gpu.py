@@ -1,0 +1,144 @@
+"""GPU parity of the quantizers, decoders and quantized linear kernels.
+
+Tier 1 (bit-exact): GPU quantizer bytes == CPU oracle bytes; GPU decoder
+floats == oracle decoder floats.  Tier 2 (tolerance): the quantized linear
+against the oracle's direct block matvec (double accumulation over the same
+fp16 x and the same packed weights).  The tolerance is written below: the only
+approximation in the kernel is the 15-bit fixed-point x per 32 values plus the
+fp16 store, so the bound is |err| <= 2e-3 * (|ref| + rms(ref)).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+KINDS = ["q4_k", "q6_k", "q8_0"]
+
+
+def _weights(rng: np.random.Generator, n: int, k: int, special: bool = True) -> np.ndarray:
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    if special and n >= 8:
+        w[0] = 0.0                      # all-zero row
+        w[1] = 0.013                    # constant positive row
+        w[2, : k // 2] = -0.5           # large negative half
+        w[3] = np.abs(w[3])             # all non-negative (min clamps to 0)
+        w[4, ::7] = 3.0                 # outliers
+        w[5] = w[5] * 1e-7              # tiny values (fp16 subnormal scales)
+    return w
+
+
+def _tol_check(got: np.ndarray, ref: np.ndarray, rel: float = 2e-3) -> None:
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2))) + 1e-30
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    bound = rel * (np.abs(ref) + rms)
+    worst = np.argmax(err - bound)
+    assert np.all(err <= bound), f"max err {err.flat[worst]} > bound {bound.flat[worst]} (ref {ref.flat[worst]})"
+
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("shape", [(64, 256), (37, 1024), (8, 4096)])
+def test_quantize_bit_exact(oracle, kind, shape):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(hash((kind, shape)) % 2**32)
+    x = _weights(rng, *shape)
+    want = oracle.quantize(x, kind)
+    got = kernels.quantize(torch.from_numpy(x).cuda(), kind)
+    got_bytes = got.view(torch.uint8).cpu().numpy()
+    mismatch = np.argwhere(got_bytes != want)
+    assert mismatch.size == 0, f"{kind}: {len(mismatch)} bytes differ, first at {mismatch[:3].tolist()}"
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_dequantize_bit_exact(oracle, kind):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(7)
+    n, k = 48, 1024
+    packed = oracle.quantize(_weights(rng, n, k), kind)
+    want = oracle.dequantize(packed, kind, k)
+    got = kernels.dequantize(torch.from_numpy(packed).cuda(), kind, k).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8, 11])
+@pytest.mark.parametrize("nk", [(256, 1024), (1030, 2048), (96, 3072), (40, 12288)])
+def test_linear_parity(oracle, kind, m, nk):
+    from torch2vk_b200 import kernels
+
+    n, k = nk
+    rng = np.random.default_rng(n * 31 + k + m)
+    packed = oracle.quantize(_weights(rng, n, k), kind)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    ref = oracle.matvec(packed, kind, x)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), kind, k)
+    _tol_check(y.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("kind", ["q4_k", "q6_k"])
+def test_linear_residual(oracle, kind):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(3)
+    n, k, m = 512, 2048, 1
+    packed = oracle.quantize(_weights(rng, n, k), kind)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    ref = oracle.matvec(packed, kind, x) + res.astype(np.float32)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), kind, k,
+                       residual=torch.from_numpy(res).cuda())
+    _tol_check(y.float().cpu().numpy(), ref)
+
+
+def test_linear_multi_mixed_types_with_norm(oracle):
+    """QKV with a Q6_K v (LinearNobiasQ4QKQ6VMatvecProgram) and the fused RMSNorm prologue."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(11)
+    k = 1024
+    specs = [(2048, "q4_k"), (1024, "q4_k"), (1024, "q6_k")]
+    packed = [oracle.quantize(_weights(rng, n, k, special=False), kind) for n, kind in specs]
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    nw = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    xf = x.astype(np.float32)
+    xn = xf / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + 1e-6) * nw
+    outs = kernels.linear_multi(
+        torch.from_numpy(x).cuda(), [(torch.from_numpy(p).cuda(), kind) for p, (_, kind) in zip(packed, specs)], k,
+        norm_weight=torch.from_numpy(nw).cuda(), eps=1e-6)
+    for out, p, (_, kind) in zip(outs, packed, specs):
+        w = oracle.dequantize(p, kind, k).astype(np.float64)
+        ref = xn.astype(np.float64) @ w.T
+        _tol_check(out.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_linear_swiglu(oracle, m):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(5)
+    n, k = 3072, 1024
+    pg = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+    pu = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    g = oracle.matvec(pg, "q4_k", x).astype(np.float64)
+    u = oracle.matvec(pu, "q4_k", x).astype(np.float64)
+    ref = g / (1.0 + np.exp(-g)) * u
+    y = kernels.linear_swiglu(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(), torch.from_numpy(pu).cuda(),
+                              "q4_k", k)
+    _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
+
+
+def test_linear_rejects_bad_shapes():
+    from torch2vk_b200 import _lib, kernels
+
+    x = torch.zeros(1, 300, dtype=torch.float16, device="cuda")
+    w = torch.zeros(4, 36, dtype=torch.uint32, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.linear(x, w, "q4_k", 300)
+    with pytest.raises(_lib.T2CError):
+        _lib.lib().call("t2c_linear", _lib.Q4_K, _lib.ptr(x), None, None, _lib.ptr(x), 1, 4, 256, _lib.stream_ptr())

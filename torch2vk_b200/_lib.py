@@ -1,0 +1,122 @@
+"""ctypes binding of libt2c_sm100.so (the C ABI declared in include/t2c_sm100.h).
+
+The library is loaded from the package directory (built in-tree by
+``torch2vk_b200.build``).  There is no fallback: if the library or a CUDA
+device is missing, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libt2c_sm100.so"
+
+T2C_OK = 0
+STATUS_NAMES = {1: "EINVAL", 2: "EUNSUPPORTED", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESCRATCH"}
+
+Q8_0 = 8
+Q4_K = 12
+Q6_K = 14
+F16 = 1
+WTYPE_BY_NAME = {"q8_0": Q8_0, "q4_k": Q4_K, "q6_k": Q6_K, "f16": F16}
+
+_c = ctypes
+_vp = _c.c_void_p
+_i64 = _c.c_int64
+_i32 = _c.c_int
+_f32 = _c.c_float
+
+# name -> argtypes (all return int status unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "t2c_abi_version": [],
+    "t2c_device_sm_count": [],
+    "t2c_linear": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "t2c_linear_multi": [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _vp],
+    "t2c_linear_swiglu": [_i32, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _vp],
+    "t2c_quantize": [_i32, _vp, _vp, _i64, _i64, _vp],
+    "t2c_dequantize": [_i32, _vp, _vp, _i64, _i64, _vp],
+}
+_RESTYPES = {"t2c_last_error": _c.c_char_p}
+
+
+class T2CError(RuntimeError):
+    """A libt2c_sm100 entry point returned a non-zero status."""
+
+    def __init__(self, function: str, status: int, message: str) -> None:
+        super().__init__(f"{function} failed ({STATUS_NAMES.get(status, status)}): {message}")
+        self.function = function
+        self.status = status
+
+
+class _Library:
+    def __init__(self, path: Path) -> None:
+        if not path.exists():
+            raise FileNotFoundError(
+                f"{path} is missing: build it with `python -m torch2vk_b200.build` (nvcc, sm_100a)"
+            )
+        self.handle = ctypes.CDLL(str(path))
+        self.handle.t2c_last_error.argtypes = []
+        self.handle.t2c_last_error.restype = _c.c_char_p
+        for name, argtypes in _SIGNATURES.items():
+            fn = getattr(self.handle, name)
+            fn.argtypes = argtypes
+            fn.restype = _c.c_int
+
+    def call(self, name: str, *args) -> None:
+        status = getattr(self.handle, name)(*args)
+        if status != T2C_OK:
+            raise T2CError(name, status, self.handle.t2c_last_error().decode(errors="replace"))
+
+    def raw(self, name: str):
+        return getattr(self.handle, name)
+
+
+_LIB: _Library | None = None
+
+
+def lib() -> _Library:
+    global _LIB
+    if _LIB is None:
+        _LIB = _Library(LIB_PATH)
+    return _LIB
+
+
+def exported_symbols() -> list[str]:
+    return ["t2c_last_error", *_SIGNATURES.keys()]
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("libt2c_sm100 operands must be CUDA tensors")
+    return t.data_ptr()
+
+
+def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def ptr_array(values) -> ctypes.Array:
+    arr = (_vp * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = v
+    return arr
+
+
+def int_array(values) -> ctypes.Array:
+    arr = (_i32 * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = v
+    return arr
+
+
+def i64_array(values) -> ctypes.Array:
+    arr = (_i64 * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = v
+    return arr

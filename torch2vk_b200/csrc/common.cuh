@@ -1,0 +1,99 @@
+// Shared helpers for the sm_100a kernels of libt2c_sm100.so: status/error
+// reporting for the C ABI, fp16 bit helpers, and the few PTX instructions the
+// kernels use directly.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/t2c_sm100.h"
+
+namespace t2c {
+
+// Records a message for t2c_last_error() and returns `code`.
+int set_error(int code, const char *fmt, ...);
+int check_launch(const char *what);
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int sm_count();
+
+// Bytes per packed row of K values for a GGUF weight type, or -1.
+inline int64_t row_bytes(int wtype, int64_t K) {
+    switch (wtype) {
+        case T2C_Q4_K: return (K % 256) ? -1 : K / 256 * 144;
+        case T2C_Q6_K: return (K % 256) ? -1 : K / 256 * 210;
+        case T2C_Q8_0: return (K % 32) ? -1 : K / 32 * 34;
+        case T2C_F16: return K * 2;
+        default: return -1;
+    }
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+
+// d = dot(a bytes as u8, b bytes as s8) + c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// d = dot(a bytes as s8, b bytes as s8) + c
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u16(const void *p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+// Explicit-width stores.  Packing fp16 bit patterns byte by byte
+// (static_cast<uint8_t>(bits & 0xff) of a __half_as_ushort result) was
+// observed to store 0 for the low byte with nvcc 12.9 / sm_100a, so fp16
+// fields are always written with one 16- or 32-bit store.
+__device__ __forceinline__ void st_u16(void *p, uint32_t v) {
+    asm volatile("st.u16 [%0], %1;" ::"l"(p), "h"(static_cast<unsigned short>(v)) : "memory");
+}
+__device__ __forceinline__ void st_u32(void *p, uint32_t v) {
+    asm volatile("st.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Programmatic dependent launch: wait until the preceding kernel on the stream
+// has completed (or triggered); a no-op when launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace t2c
