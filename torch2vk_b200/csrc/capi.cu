@@ -6,6 +6,8 @@
 
 namespace t2c {
 
+cudaError_t status_qlinear(unsigned int *bits, int clear, cudaStream_t s);
+
 static thread_local char g_last_error[1024] = "";
 
 int set_error(int code, const char *fmt, ...) {
@@ -47,3 +49,13 @@ extern "C" const char *t2c_last_error(void) { return t2c::g_last_error; }
 extern "C" int t2c_abi_version(void) { return 1; }
 
 extern "C" int t2c_device_sm_count(void) { return t2c::sm_count(); }
+
+extern "C" int t2c_device_status(unsigned int *bits, int clear, void *stream) {
+    if (bits == nullptr) return t2c::set_error(T2C_EINVAL, "t2c_device_status: bits is NULL");
+    cudaStream_t s = t2c::as_stream(stream);
+    unsigned int value = 0;
+    cudaError_t err = t2c::status_qlinear(&value, clear, s);
+    if (err != cudaSuccess) return t2c::set_error(T2C_ECUDA, "t2c_device_status: %s", cudaGetErrorString(err));
+    *bits = value;
+    return T2C_OK;
+}

@@ -91,6 +91,73 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// ------------------------------------------------------------ mbarrier / TMA
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// try_wait with a suspend-time hint: the waiting thread sleeps until the phase
+// completes or ~64 us pass, instead of spinning through issue slots.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(65536u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait on an mbarrier phase: false after `limit_ns` without completion.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - start > limit_ns) return false;
+    }
+}
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`
+// (no multicast).  dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Device-side status word of this translation unit: kernels OR in 1 << T2C_E*
+// (e.g. T2C_ETIMEOUT after a bounded wait ran out).  Every .cu file with such
+// kernels exposes a reader (status_<file>) that t2c_device_status() combines.
+static __device__ unsigned int g_device_status = 0;
+__device__ __forceinline__ void report_device_error(unsigned int code) { atomicOr(&g_device_status, 1u << code); }
+
+static inline cudaError_t read_tu_status(unsigned int *bits, int clear, cudaStream_t s) {
+    unsigned int value = 0;
+    cudaError_t err = cudaMemcpyFromSymbolAsync(&value, g_device_status, sizeof(value), 0, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess && clear) {
+        static const unsigned int zero = 0;
+        err = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    }
+    if (err == cudaSuccess) *bits |= value;
+    return err;
+}
+
 // Programmatic dependent launch: wait until the preceding kernel on the stream
 // has completed (or triggered); a no-op when launched without the attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -1,19 +1,26 @@
 // Quantized linear for decode-sized batches (M <= 8 per launch chunk):
 // y[m, n] = sum_k x[m, k] * deq(W)[n, k] over GGUF Q4_K / Q6_K / Q8_0 rows.
 //
-// Design (B200, HBM-bound):
-//  * Each CTA first turns its x rows into 15-bit fixed point per 32-value
-//    sub-block (x ~= sx * (128 * xh + xl), xh int8, xl in [0,127]) in shared
-//    memory, optionally applying RMSNorm on the way (fused prologue).
-//  * Warps (or 16/8-lane sub-warps for short rows) then stream weight rows
-//    straight from HBM with coalesced 16-byte (Q4_K) or 4-byte funnel-aligned
-//    (Q6_K, Q8_0) loads, four rows at a time so every x fragment held in
-//    registers serves four rows.  Integer nibble/6-bit codes meet the int8 x
-//    planes in dp4a; the integer sub-block sums are exact, and the block scales
-//    (d * sc, dmin * m) are applied once per sub-block in fp32.
-//  * Partial row sums are reduced with warp shuffles; the epilogue adds the
-//    residual (matvec_add), or forms silu(gate) * up (SwiGLU pair), and stores
-//    fp16.
+// B200 design (HBM-bound):
+//  * x prologue: each CTA turns its x rows into 15-bit fixed point per
+//    32-value sub-block (x ~= sx * (128 * xh + xl), xh int8, xl in [0,127])
+//    in shared memory, optionally applying RMSNorm on the way.
+//  * Streamed kernel (qmv_tma_kernel): persistent CTAs; a producer warp
+//    streams row blocks of the packed weight matrix HBM -> shared memory with
+//    1-D bulk async copies (cp.async.bulk, completion on mbarriers) through a
+//    ring of stages, while four consumer warps decode the staged blocks.  The
+//    copies need no registers, so the bytes in flight per SM are set by the
+//    ring depth, not by occupancy.
+//  * Decode: integer nibble / 6-bit / int8 codes meet the int8 x planes in
+//    dp4a (exact integer sub-block sums); the block scales d*sc and dmin*m
+//    are applied once per sub-block in fp32.  Each lane keeps four rows'
+//    partial sums so one x fragment serves four rows; partial sums are
+//    reduced with warp shuffles.
+//  * Epilogues: + residual (matvec_add), silu(gate) * up (SwiGLU pair), fp16
+//    store.
+//  * Direct kernel (qmv_direct_kernel): the same decode reading weights
+//    straight from global memory; used when a layout cannot be bulk-copied
+//    (16-byte alignment).
 // Semantics follow the reference matvec shaders
 // (src/models/quantized_qwen3/shaders/linear_nobias_q4_k_matvec_f32.py:107-197,
 //  linear_nobias_q6_k_matvec_f32.py:116-193, linear_nobias_q8_0_matvec_f32.py:84-119):
@@ -27,10 +34,10 @@
 namespace t2c {
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 128;  // x-prologue / consumer threads
 constexpr int kWarps = kThreads / 32;
-constexpr int kRows = 4;  // rows per row-set (x fragments are reused across them)
 constexpr int kMaxStreams = 3;
+constexpr int kMaxStages = 8;
 
 enum Mode : int { MODE_ROWS = 0, MODE_SWIGLU = 1 };
 
@@ -40,8 +47,15 @@ struct QStream {
     const __half *res;
     int64_t n;
     int64_t row_bytes;
-    int64_t rs_begin;
+    int64_t rs_begin;  // first row-set (direct) / row block (streamed) index of this stream
     int fmt;
+    // streamed-kernel geometry
+    int rb;            // rows per row block (SwiGLU: gate + up rows)
+    int seg_blocks;    // GGUF blocks per staged row segment
+    int seg_bytes;     // bytes per staged row segment
+    int chunks;        // segments per row (K / (seg_blocks * block_values))
+    int lpr;           // lanes per row group
+    int whole;         // 1: a stage is rb full contiguous rows (one copy)
 };
 
 struct QParams {
@@ -53,49 +67,82 @@ struct QParams {
     float eps;
     int M;         // tokens in this launch chunk (<= MT)
     int K;
-    int units;     // 64-value units per row
-    int lpr;       // lanes per row-set (4, 8, 16 or 32)
-    int64_t total_rowsets;
+    int units;     // 64-value units per row (direct kernel)
+    int lpr;       // lanes per row-set (direct kernel)
+    int64_t total_rowsets;  // direct: row-sets; streamed: row blocks
+    int stages;
+    int stage_bytes;
 };
 
-// Four weight rows: rows 0,1 start at base0 (+ r * row_bytes), rows 2,3 at base1.
-struct RowSet {
-    const uint8_t *base0;
-    const uint8_t *base1;
-    int64_t row_bytes;
-    int valid;  // bit r set when row r exists
-    __device__ __forceinline__ const uint8_t *row(int r) const {
-        return ((valid >> r) & 1) ? ((r < 2 ? base0 : base1) + (r & 1) * row_bytes) : nullptr;
-    }
-};
-
+// x planes in shared memory.  xh/xl rows are padded by 16 bytes after every
+// 64 values (row stride KP = K * 5 / 4) so that the 16-byte fragments that
+// consecutive lanes read for consecutive 64-value units fall in distinct
+// banks.
 struct XPlanes {
-    const int8_t *xh;   // [MT][K]
-    const int8_t *xl;   // [MT][K]
-    const float *sx;    // [MT][K/32]
-    const int *xq16;    // [MT][K/16] integer sums of (128 xh + xl) over 16 values
+    const int8_t *xh;    // [MT][KP]
+    const int8_t *xl;    // [MT][KP]
+    const float *sx;     // [MT][K/32]
+    const int *xq16;     // [MT][K/16] integer sums of (128 xh + xl) over 16 values
+    const float4 *meta;  // [MT][K/64]: sx[2u], sx[2u+1], xsum[2u], xsum[2u+1]
+    int kp;
+    __device__ __forceinline__ int off(int m, int k) const { return m * kp + k + ((k >> 6) << 4); }
 };
 
-__device__ __forceinline__ uint32_t funnel16(uint32_t lo, uint32_t hi, uint32_t sh) {
-    return __funnelshift_r(lo, hi, sh);
+__host__ __device__ __forceinline__ int padded_k(int K) { return K + (K >> 2); }
+
+// ------------------------------------------------------------- loads
+template <bool SMEM>
+__device__ __forceinline__ uint4 ld_v4(const uint8_t *p) {
+    if constexpr (SMEM) {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(smem_u32(p)));
+        return v;
+    } else {
+        return ldg_nc_v4(p);
+    }
+}
+template <bool SMEM>
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t *p) {
+    if constexpr (SMEM) {
+        uint32_t v;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+        return v;
+    } else {
+        return ldg_nc_u32(p);
+    }
+}
+template <bool SMEM>
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) {
+    if constexpr (SMEM) {
+        unsigned short v;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(smem_u32(p)));
+        return v;
+    } else {
+        return ldg_nc_u16(p);
+    }
 }
 
-// Loads 16 bytes starting at a 2-byte aligned global address.
-__device__ __forceinline__ uint4 load16_u2(const uint8_t *p) {
+// 16 bytes starting at a 2-byte aligned address (aligned words + funnel shift).
+template <bool SMEM>
+__device__ __forceinline__ uint4 ld16_a2(const uint8_t *p) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint8_t *base = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(3));
     const uint32_t sh = static_cast<uint32_t>(a & 3) * 8u;
-    uint32_t w0 = ldg_nc_u32(base + 0), w1 = ldg_nc_u32(base + 1), w2 = ldg_nc_u32(base + 2);
-    uint32_t w3 = ldg_nc_u32(base + 3);
-    uint32_t w4 = sh ? ldg_nc_u32(base + 4) : 0u;
-    return make_uint4(funnel16(w0, w1, sh), funnel16(w1, w2, sh), funnel16(w2, w3, sh), funnel16(w3, w4, sh));
+    const uint32_t w0 = ld_u32<SMEM>(base), w1 = ld_u32<SMEM>(base + 4), w2 = ld_u32<SMEM>(base + 8);
+    const uint32_t w3 = ld_u32<SMEM>(base + 12);
+    const uint32_t w4 = sh ? ld_u32<SMEM>(base + 16) : 0u;
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
 }
 
 // ---------------------------------------------------------------- x prologue
 // Chunks of 8 fp16 values (16 bytes).  Thread t owns chunks t, t + kThreads,
 // ...; the four chunks of a 32-value sub-block sit on four consecutive lanes,
 // so sub-block maxima and 16-value sums are two/one xor-shuffles away.  Loads
-// are issued kRound chunks at a time so their latencies overlap.
+// are issued kRound chunks at a time so their latencies overlap.  Only the
+// kThreads consumer threads run this (CONSUMER_BAR: sync on named barrier 1).
 constexpr int kRound = 4;
 
 __device__ __forceinline__ void unpack8(const uint4 &v, float f[8]) {
@@ -108,10 +155,24 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float f[8]) {
     }
 }
 
-template <int MT>
-__device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, int *xq16, float *red) {
+template <int MT, int NT>
+__device__ __forceinline__ void sync_threads_nt() {
+    if constexpr (NT == kThreads) {
+        __syncthreads();
+    } else {
+        asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+    }
+}
+
+// NT threads (0..NT-1) build the x planes; ends with a barrier over them.
+template <int MT, int NT>
+__device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, int *xq16, float4 *meta, float *red) {
+    constexpr int kThreads = NT;
+    constexpr int kWarps = NT / 32;
     const int K = p.K;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int KP = padded_k(K);
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int chunks_per_row = K >> 3;
     const int total = MT * chunks_per_row;
     const uint4 *xv = reinterpret_cast<const uint4 *>(p.x);
@@ -126,13 +187,13 @@ __device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, i
             uint4 v[kRound];
 #pragma unroll
             for (int i = 0; i < kRound; ++i) {
-                const int c = base + i * kThreads + threadIdx.x;
+                const int c = base + i * kThreads + tid;
                 const int m = c / chunks_per_row;
                 v[i] = (c < total && m < p.M) ? xv[c] : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
             for (int i = 0; i < kRound; ++i) {
-                const int c = base + i * kThreads + threadIdx.x;
+                const int c = base + i * kThreads + tid;
                 const int m = c / chunks_per_row;
                 float f[8];
                 unpack8(v[i], f);
@@ -149,7 +210,7 @@ __device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, i
             const float t = warp_sum(ss[m]);
             if (lane == 0) red[warp * MT + m] = t;
         }
-        __syncthreads();
+        sync_threads_nt<MT, NT>();
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             float t = 0.0f;
@@ -161,13 +222,13 @@ __device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, i
         uint4 v[kRound];
 #pragma unroll
         for (int i = 0; i < kRound; ++i) {
-            const int c = base + i * kThreads + threadIdx.x;
+            const int c = base + i * kThreads + tid;
             const int m = c / chunks_per_row;
             v[i] = (c < total && m < p.M) ? xv[c] : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int i = 0; i < kRound; ++i) {
-            const int c = base + i * kThreads + threadIdx.x;
+            const int c = base + i * kThreads + tid;
             if (base + i * kThreads >= total) break;  // uniform across the CTA
             const int m = c / chunks_per_row;
             const int k = (c - m * chunks_per_row) * 8;
@@ -202,85 +263,90 @@ __device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, i
             }
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             if (c < total) {
-                *reinterpret_cast<uint2 *>(xh + c * 8) = make_uint2(hw[0], hw[1]);
-                *reinterpret_cast<uint2 *>(xl + c * 8) = make_uint2(lw[0], lw[1]);
+                const int o = m * KP + k + ((k >> 6) << 4);
+                *reinterpret_cast<uint2 *>(xh + o) = make_uint2(hw[0], hw[1]);
+                *reinterpret_cast<uint2 *>(xl + o) = make_uint2(lw[0], lw[1]);
                 if ((lane & 1) == 0) xq16[c >> 1] = sum;
                 if ((lane & 3) == 0) sx[c >> 2] = amax / 16383.0f;
             }
         }
     }
+    sync_threads_nt<MT, NT>();
+    // per-64-value unit metadata (two sub-blocks)
+    const int units = MT * (K >> 6);
+    for (int u = tid; u < units; u += NT) {
+        const float s0 = sx[2 * u], s1 = sx[2 * u + 1];
+        const float x0 = s0 * static_cast<float>(xq16[4 * u] + xq16[4 * u + 1]);
+        const float x1 = s1 * static_cast<float>(xq16[4 * u + 2] + xq16[4 * u + 3]);
+        meta[u] = make_float4(s0, s1, x0, x1);
+    }
+    sync_threads_nt<MT, NT>();
 }
 
 // ------------------------------------------------------------- Q4_K unit
-// Unit u of a row = group G (32 bytes) of block b: low nibbles are sub-block
-// 2G (k0 .. k0+31), high nibbles sub-block 2G+1 (k0+32 .. k0+63).
-template <int MT>
-__device__ __forceinline__ void unit_q4k(const RowSet &rows, int u, int K, const XPlanes &xp,
-                                         float acc[kRows][MT]) {
-    const int b = u >> 2, G = u & 3;
-    const int k0 = b * 256 + G * 64;
+// Unit = group G (32 bytes) of block b: low nibbles are sub-block 2G
+// (k0 .. k0+31), high nibbles sub-block 2G+1 (k0+32 .. k0+63).
+// rows[r]: start of the row segment holding block b (nullptr: no row);
+// kbase: absolute k of block 0 of the segment.
+template <int MT, int NR, bool SMEM>
+__device__ __forceinline__ void unit_q4k(const uint8_t *const rows[NR], int b, int G, int kbase, int K,
+                                         const XPlanes &xp, float acc[NR][MT]) {
+    const int k0 = kbase + b * 256 + G * 64;
     const int j0 = k0 >> 5;
-    uint4 hdr[kRows], q0[kRows], q1[kRows];
+    (void)K;
+    uint4 hdr[NR], q0[NR], q1[NR];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-        if ((rows.valid >> r) & 1) {
-            const uint8_t *blk = rows.row(r) + b * 144;
-            hdr[r] = ldg_nc_v4(blk);
-            q0[r] = ldg_nc_v4(blk + 16 + G * 32);
-            q1[r] = ldg_nc_v4(blk + 32 + G * 32);
+    for (int r = 0; r < NR; ++r) {
+        if (rows[r] != nullptr) {
+            const uint8_t *blk = rows[r] + b * 144;
+            hdr[r] = ld_v4<SMEM>(blk);
+            q0[r] = ld_v4<SMEM>(blk + 16 + G * 32);
+            q1[r] = ld_v4<SMEM>(blk + 32 + G * 32);
         } else {
             hdr[r] = make_uint4(0, 0, 0, 0);
             q0[r] = hdr[r];
             q1[r] = hdr[r];
         }
     }
-    // 6-bit scale/min codes for sub-blocks 2G and 2G+1 (quantize/vulkan.py:331-342 packing)
-    float ds0[kRows], ds1[kRows], dm0[kRows], dm1[kRows];
+    // 6-bit scale/min codes for sub-blocks 2G and 2G+1 (quantize/vulkan.py:331-342
+    // packing), decoded without divergent branches; small integers become
+    // floats through the 2^23 mantissa trick.
+    const int i0 = (2 * G) & 3;
+    const bool low = G < 2;
+    float ds0[NR], ds1[NR], dm0[NR], dm1[NR];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
+    for (int r = 0; r < NR; ++r) {
         const float d = half_bits_to_float(hdr[r].x);
         const float dmin = half_bits_to_float(hdr[r].x >> 16);
-        uint32_t sc0, sc1, mn0, mn1;
-        const int j = 2 * G;
-        if (G < 2) {
-            sc0 = (hdr[r].y >> (8 * j)) & 63u;
-            sc1 = (hdr[r].y >> (8 * j + 8)) & 63u;
-            mn0 = (hdr[r].z >> (8 * j)) & 63u;
-            mn1 = (hdr[r].z >> (8 * j + 8)) & 63u;
-        } else {
-            const int i0 = j - 4;
-            const uint32_t lo0 = (hdr[r].w >> (8 * i0)) & 0xffu, lo1 = (hdr[r].w >> (8 * i0 + 8)) & 0xffu;
-            const uint32_t s0 = (hdr[r].y >> (8 * i0)) & 0xffu, s1 = (hdr[r].y >> (8 * i0 + 8)) & 0xffu;
-            const uint32_t m0 = (hdr[r].z >> (8 * i0)) & 0xffu, m1 = (hdr[r].z >> (8 * i0 + 8)) & 0xffu;
-            sc0 = (lo0 & 15u) | ((s0 >> 6) << 4);
-            sc1 = (lo1 & 15u) | ((s1 >> 6) << 4);
-            mn0 = (lo0 >> 4) | ((m0 >> 6) << 4);
-            mn1 = (lo1 >> 4) | ((m1 >> 6) << 4);
-        }
-        ds0[r] = d * static_cast<float>(sc0);
-        ds1[r] = d * static_cast<float>(sc1) * 0.0625f;  // high nibbles enter dp4a as 16*q
-        dm0[r] = dmin * static_cast<float>(mn0);
-        dm1[r] = dmin * static_cast<float>(mn1);
+        const uint32_t y = hdr[r].y >> (8 * i0), z = hdr[r].z >> (8 * i0), w = hdr[r].w >> (8 * i0);
+        const uint32_t hi_sc = ((y >> 6) & 0x3u) | (((y >> 14) & 0x3u) << 8);      // 2 high bits, bytes 0/1
+        const uint32_t hi_mn = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
+        const uint32_t sc_pair = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hi_sc << 4));
+        const uint32_t mn_pair = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hi_mn << 4));
+        const float sc0 = __uint_as_float(0x4B000000u | (sc_pair & 0xffu)) - 8388608.0f;
+        const float sc1 = __uint_as_float(0x4B000000u | (sc_pair >> 8)) - 8388608.0f;
+        const float mn0 = __uint_as_float(0x4B000000u | (mn_pair & 0xffu)) - 8388608.0f;
+        const float mn1 = __uint_as_float(0x4B000000u | (mn_pair >> 8)) - 8388608.0f;
+        ds0[r] = d * sc0;
+        ds1[r] = d * sc1 * 0.0625f;  // high nibbles enter dp4a as 16*q
+        dm0[r] = dmin * mn0;
+        dm1[r] = dmin * mn1;
     }
-    const int sub_per_row = K >> 5;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        const int4 *xhv = reinterpret_cast<const int4 *>(xp.xh + m * K + k0);
-        const int4 *xlv = reinterpret_cast<const int4 *>(xp.xl + m * K + k0);
+        const int4 *xhv = reinterpret_cast<const int4 *>(xp.xh + xp.off(m, k0));
+        const int4 *xlv = reinterpret_cast<const int4 *>(xp.xl + xp.off(m, k0));
         const int4 hA0 = xhv[0], hA1 = xhv[1], hB0 = xhv[2], hB1 = xhv[3];
         const int4 lA0 = xlv[0], lA1 = xlv[1], lB0 = xlv[2], lB1 = xlv[3];
-        const float s0 = xp.sx[m * sub_per_row + j0];
-        const float s1 = xp.sx[m * sub_per_row + j0 + 1];
-        const int *q16 = xp.xq16 + (m * sub_per_row + j0) * 2;
-        const float xs0 = s0 * static_cast<float>(q16[0] + q16[1]);
-        const float xs1 = s1 * static_cast<float>(q16[2] + q16[3]);
+        const float4 mt = xp.meta[m * (K >> 6) + (j0 >> 1)];
+        const float s0 = mt.x, s1 = mt.y, xs0 = mt.z, xs1 = mt.w;
+        const int xhA[8] = {hA0.x, hA0.y, hA0.z, hA0.w, hA1.x, hA1.y, hA1.z, hA1.w};
+        const int xlA[8] = {lA0.x, lA0.y, lA0.z, lA0.w, lA1.x, lA1.y, lA1.z, lA1.w};
+        const int xhB[8] = {hB0.x, hB0.y, hB0.z, hB0.w, hB1.x, hB1.y, hB1.z, hB1.w};
+        const int xlB[8] = {lB0.x, lB0.y, lB0.z, lB0.w, lB1.x, lB1.y, lB1.z, lB1.w};
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
+        for (int r = 0; r < NR; ++r) {
             const uint32_t wA[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
-            const int xhA[8] = {hA0.x, hA0.y, hA0.z, hA0.w, hA1.x, hA1.y, hA1.z, hA1.w};
-            const int xlA[8] = {lA0.x, lA0.y, lA0.z, lA0.w, lA1.x, lA1.y, lA1.z, lA1.w};
-            const int xhB[8] = {hB0.x, hB0.y, hB0.z, hB0.w, hB1.x, hB1.y, hB1.z, hB1.w};
-            const int xlB[8] = {lB0.x, lB0.y, lB0.z, lB0.w, lB1.x, lB1.y, lB1.z, lB1.w};
             int hiL = 0, loL = 0, hiH = 0, loH = 0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -304,26 +370,26 @@ __device__ __forceinline__ void unit_q4k(const RowSet &rows, int u, int K, const
 }
 
 // ------------------------------------------------------------- Q6_K unit
-// Unit u = (block b, half s, l-half lh): values i = 128 s + 32 c + 16 lh + l,
+// Unit = (block b, half s, l-half lh): values i = 128 s + 32 c + 16 lh + l,
 // c = 0..3, l = 0..15 (quantize/vulkan.py:542-564 layout).
-template <int MT>
-__device__ __forceinline__ void unit_q6k(const RowSet &rows, int u, int K, const XPlanes &xp,
-                                         float acc[kRows][MT]) {
-    const int b = u >> 2, s = (u >> 1) & 1, lh = u & 1;
-    const int kbase = b * 256 + s * 128 + lh * 16;
-    uint4 qa[kRows], qb[kRows], qh[kRows];
-    float dsc[kRows][4];
+template <int MT, int NR, bool SMEM>
+__device__ __forceinline__ void unit_q6k(const uint8_t *const rows[NR], int b, int sl, int kbase, int K,
+                                         const XPlanes &xp, float acc[NR][MT]) {
+    const int s = sl >> 1, lh = sl & 1;
+    const int kk = kbase + b * 256 + s * 128 + lh * 16;
+    uint4 qa[NR], qb[NR], qh[NR];
+    float dsc[NR][4];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-        if ((rows.valid >> r) & 1) {
-            const uint8_t *blk = rows.row(r) + b * 210;
-            qa[r] = load16_u2(blk + 64 * s + 16 * lh);
-            qb[r] = load16_u2(blk + 64 * s + 32 + 16 * lh);
-            qh[r] = load16_u2(blk + 128 + 32 * s + 16 * lh);
-            const float d = half_bits_to_float(ldg_nc_u16(blk + 208));
+    for (int r = 0; r < NR; ++r) {
+        if (rows[r] != nullptr) {
+            const uint8_t *blk = rows[r] + b * 210;
+            qa[r] = ld16_a2<SMEM>(blk + 64 * s + 16 * lh);
+            qb[r] = ld16_a2<SMEM>(blk + 64 * s + 32 + 16 * lh);
+            qh[r] = ld16_a2<SMEM>(blk + 128 + 32 * s + 16 * lh);
+            const float d = half_bits_to_float(ld_u16<SMEM>(blk + 208));
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                const uint32_t pair = ldg_nc_u16(blk + 192 + 8 * s + 2 * c);
+                const uint32_t pair = ld_u16<SMEM>(blk + 192 + 8 * s + 2 * c);
                 const int8_t code = static_cast<int8_t>((pair >> (8 * lh)) & 0xffu);
                 dsc[r][c] = d * static_cast<float>(code);
             }
@@ -340,15 +406,15 @@ __device__ __forceinline__ void unit_q6k(const RowSet &rows, int u, int K, const
     for (int m = 0; m < MT; ++m) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const int k = kbase + 32 * c;
-            const int4 xh4 = *reinterpret_cast<const int4 *>(xp.xh + m * K + k);
-            const int4 xl4 = *reinterpret_cast<const int4 *>(xp.xl + m * K + k);
+            const int k = kk + 32 * c;
+            const int4 xh4 = *reinterpret_cast<const int4 *>(xp.xh + xp.off(m, k));
+            const int4 xl4 = *reinterpret_cast<const int4 *>(xp.xl + xp.off(m, k));
             const float sxv = xp.sx[m * sub_per_row + (k >> 5)];
             const int q16 = xp.xq16[m * sub_per_row * 2 + (k >> 4)];
             const int xhw[4] = {xh4.x, xh4.y, xh4.z, xh4.w};
             const int xlw[4] = {xl4.x, xl4.y, xl4.z, xl4.w};
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) {
+            for (int r = 0; r < NR; ++r) {
                 const uint4 ql = (c & 1) ? qb[r] : qa[r];
                 const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
                 const uint32_t hw[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
@@ -369,24 +435,24 @@ __device__ __forceinline__ void unit_q6k(const RowSet &rows, int u, int K, const
 }
 
 // ------------------------------------------------------------- Q8_0 unit
-// Unit u = blocks 2u and 2u+1 (68 bytes, 4-byte aligned when K % 64 == 0).
-template <int MT>
-__device__ __forceinline__ void unit_q8_0(const RowSet &rows, int u, int K, const XPlanes &xp,
-                                          float acc[kRows][MT]) {
-    uint32_t qa[kRows][8], qb[kRows][8];
-    float da[kRows], db[kRows];
+// Unit = blocks 2u and 2u+1 of the segment (68 bytes, 4-byte aligned).
+template <int MT, int NR, bool SMEM>
+__device__ __forceinline__ void unit_q8_0(const uint8_t *const rows[NR], int u, int kbase, int K,
+                                          const XPlanes &xp, float acc[NR][MT]) {
+    uint32_t qa[NR][8], qb[NR][8];
+    float da[NR], db[NR];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-        if ((rows.valid >> r) & 1) {
-            const uint32_t *p = reinterpret_cast<const uint32_t *>(rows.row(r) + u * 68);
+    for (int r = 0; r < NR; ++r) {
+        if (rows[r] != nullptr) {
+            const uint8_t *p = rows[r] + u * 68;
             uint32_t w[17];
 #pragma unroll
-            for (int i = 0; i < 17; ++i) w[i] = ldg_nc_u32(p + i);
+            for (int i = 0; i < 17; ++i) w[i] = ld_u32<SMEM>(p + 4 * i);
             da[r] = half_bits_to_float(w[0]);
             db[r] = half_bits_to_float(w[8] >> 16);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                qa[r][i] = funnel16(w[i], w[i + 1], 16);
+                qa[r][i] = __funnelshift_r(w[i], w[i + 1], 16);
                 qb[r][i] = w[9 + i];
             }
         } else {
@@ -399,22 +465,21 @@ __device__ __forceinline__ void unit_q8_0(const RowSet &rows, int u, int K, cons
             }
         }
     }
-    const int sub_per_row = K >> 5;
-    const int k0 = u * 64;
+    const int k0 = kbase + u * 64;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        const int4 *xhv = reinterpret_cast<const int4 *>(xp.xh + m * K + k0);
-        const int4 *xlv = reinterpret_cast<const int4 *>(xp.xl + m * K + k0);
+        const int4 *xhv = reinterpret_cast<const int4 *>(xp.xh + xp.off(m, k0));
+        const int4 *xlv = reinterpret_cast<const int4 *>(xp.xl + xp.off(m, k0));
         const int4 h0 = xhv[0], h1 = xhv[1], h2 = xhv[2], h3 = xhv[3];
         const int4 l0 = xlv[0], l1 = xlv[1], l2 = xlv[2], l3 = xlv[3];
         const int xhA[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
         const int xlA[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
         const int xhB[8] = {h2.x, h2.y, h2.z, h2.w, h3.x, h3.y, h3.z, h3.w};
         const int xlB[8] = {l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
-        const float sA = xp.sx[m * sub_per_row + (k0 >> 5)];
-        const float sB = xp.sx[m * sub_per_row + (k0 >> 5) + 1];
+        const float4 mt = xp.meta[m * (K >> 6) + (k0 >> 6)];
+        const float sA = mt.x, sB = mt.y;
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
+        for (int r = 0; r < NR; ++r) {
             int hA = 0, lA = 0, hB = 0, lB = 0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -431,156 +496,558 @@ __device__ __forceinline__ void unit_q8_0(const RowSet &rows, int u, int K, cons
     }
 }
 
+// Runs unit `u` of a row segment starting at absolute k `kbase` for NR rows.
+// Q4_K / Q6_K: 4 units per block; Q8_0: u indexes block pairs.
+template <int MT, int NR, bool SMEM>
+__device__ __forceinline__ void run_unit(int fmt, const uint8_t *const rows[NR], int u, int kbase, int K,
+                                         const XPlanes &xp, float acc[NR][MT]) {
+    if (fmt == T2C_Q4_K) {
+        unit_q4k<MT, NR, SMEM>(rows, u >> 2, u & 3, kbase, K, xp, acc);
+    } else if (fmt == T2C_Q6_K) {
+        unit_q6k<MT, NR, SMEM>(rows, u >> 2, u & 3, kbase, K, xp, acc);
+    } else {
+        unit_q8_0<MT, NR, SMEM>(rows, u, kbase, K, xp, acc);
+    }
+}
+
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
 
-// FMT: the weight type of every stream, or 0 when streams mix types.
+// Epilogue for NR rows.  ROWS mode: row r is output n[r] of stream st.
+// SWIGLU mode: rows (r, r+1) are (gate, up) of output n[r].  n < 0: no row.
+template <int MT, int NR>
+__device__ __forceinline__ void store_rows(const QParams &p, const QStream &st, const int64_t n[NR],
+                                           const float acc[NR][MT], bool swiglu) {
+    if (swiglu) {
+#pragma unroll
+        for (int r = 0; r + 1 < NR; r += 2) {
+            if (n[r] < 0) continue;
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < p.M) st.y[m * st.n + n[r]] = __float2half_rn(silu(acc[r][m]) * acc[r + 1][m]);
+        }
+        return;
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        if (n[r] < 0) continue;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < p.M) {
+                const int64_t o = m * st.n + n[r];
+                float v = acc[r][m];
+                if (st.res) v += __half2float(st.res[o]);
+                st.y[o] = __float2half_rn(v);
+            }
+        }
+    }
+}
+
+template <int MT, int NR>
+__device__ __forceinline__ void reduce_lanes(float acc[NR][MT], int lpr) {
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float v = acc[r][m];
+            for (int o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            acc[r][m] = v;
+        }
+}
+
+// =============================================================== direct kernel
+// A row-set = 2 rows (ROWS: rows n0, n0+1 of one stream; SWIGLU: gate row n0
+// and up row n0), processed by `lpr` lanes that split the 64-value units.
+constexpr int kDirectRows = 2;
+
 template <int MT, int FMT>
-__global__ void __launch_bounds__(kThreads, (MT == 1 ? 2 : 1)) qmv_kernel(const QParams p) {
-    extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, (MT == 1 ? 5 : 2)) qmv_direct_kernel(const QParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
     const int K = p.K;
-    int8_t *xh = reinterpret_cast<int8_t *>(smem);
-    int8_t *xl = xh + MT * K;
-    float *sx = reinterpret_cast<float *>(xl + MT * K);
+    float4 *meta = reinterpret_cast<float4 *>(smem);
+    int8_t *xh = reinterpret_cast<int8_t *>(meta + MT * (K >> 6));
+    int8_t *xl = xh + MT * padded_k(K);
+    float *sx = reinterpret_cast<float *>(xl + MT * padded_k(K));
     int *xq16 = reinterpret_cast<int *>(sx + MT * (K >> 5));
     float *red = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
 
     pdl_wait();
-    prepare_x<MT>(p, xh, xl, sx, xq16, red);
-    __syncthreads();
+    prepare_x<MT, kThreads>(p, xh, xl, sx, xq16, meta, red);
     pdl_trigger();
 
-    const XPlanes xp{xh, xl, sx, xq16};
+    const XPlanes xp{xh, xl, sx, xq16, meta, padded_k(K)};
     const int lane = threadIdx.x & 31;
     const int lpr = p.lpr;
-    const int sub = lane / lpr;              // sub-warp index
-    const int sub_lane = lane - sub * lpr;   // lane within the sub-warp
+    const int sub = lane / lpr;
+    const int sub_lane = lane - sub * lpr;
     const int subs_per_warp = 32 / lpr;
     const int64_t gsub = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * subs_per_warp + sub;
     const int64_t gsub_stride = static_cast<int64_t>(gridDim.x) * kWarps * subs_per_warp;
+    const bool swiglu = p.mode == MODE_SWIGLU;
 
-    // Every sub-warp runs the same number of iterations so the shuffles below
-    // always see full warps; row-sets past the end are masked out.
+    // Every sub-warp runs the same number of iterations so the shuffles always
+    // see full warps; row-sets past the end are masked out.
     const int64_t iters = (p.total_rowsets + gsub_stride - 1) / gsub_stride;
     for (int64_t it = 0; it < iters; ++it) {
         const int64_t rs = gsub + it * gsub_stride;
-        RowSet rows{nullptr, nullptr, 0, 0};
+        const uint8_t *rows[kDirectRows] = {nullptr, nullptr};
+        int64_t n[kDirectRows] = {-1, -1};
         int fmt = T2C_Q4_K;
         int si = 0;
-        int64_t n0 = 0;
         if (rs < p.total_rowsets) {
-            if (p.mode == MODE_SWIGLU) {
-                // rows 0,1: gate rows n0, n0+1; rows 2,3: up rows n0, n0+1
+            if (swiglu) {
                 fmt = p.s[0].fmt;
-                n0 = rs * 2;
-                const int64_t nv = p.s[0].n - n0;
-                rows.base0 = p.s[0].w + n0 * p.s[0].row_bytes;
-                rows.base1 = p.s[1].w + n0 * p.s[1].row_bytes;
-                rows.row_bytes = p.s[0].row_bytes;
-                rows.valid = nv >= 2 ? 0xF : 0x5;
+                rows[0] = p.s[0].w + rs * p.s[0].row_bytes;
+                rows[1] = p.s[1].w + rs * p.s[1].row_bytes;
+                n[0] = rs;
+                n[1] = rs;
             } else {
 #pragma unroll
                 for (int i = 1; i < kMaxStreams; ++i)
                     if (i < p.nstreams && rs >= p.s[i].rs_begin) si = i;
                 const QStream &st = p.s[si];
                 fmt = st.fmt;
-                n0 = (rs - st.rs_begin) * kRows;
-                const int64_t nv = st.n - n0;
-                rows.base0 = st.w + n0 * st.row_bytes;
-                rows.base1 = rows.base0 + 2 * st.row_bytes;
-                rows.row_bytes = st.row_bytes;
-                rows.valid = nv >= 4 ? 0xF : ((1 << nv) - 1);
+                const int64_t n0 = (rs - st.rs_begin) * kDirectRows;
+                rows[0] = st.w + n0 * st.row_bytes;
+                n[0] = n0;
+                if (n0 + 1 < st.n) {
+                    rows[1] = rows[0] + st.row_bytes;
+                    n[1] = n0 + 1;
+                }
             }
         }
-        float acc[kRows][MT];
+        if (FMT != 0) fmt = FMT;
+        float acc[kDirectRows][MT];
 #pragma unroll
-        for (int r = 0; r < kRows; ++r)
+        for (int r = 0; r < kDirectRows; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
-        if (FMT != 0) fmt = FMT;
         if (rs < p.total_rowsets) {
-            if (fmt == T2C_Q4_K) {
-                for (int u = sub_lane; u < p.units; u += lpr) unit_q4k<MT>(rows, u, K, xp, acc);
-            } else if (fmt == T2C_Q6_K) {
-                for (int u = sub_lane; u < p.units; u += lpr) unit_q6k<MT>(rows, u, K, xp, acc);
-            } else {
-                for (int u = sub_lane; u < p.units; u += lpr) unit_q8_0<MT>(rows, u, K, xp, acc);
-            }
+            for (int u = sub_lane; u < p.units; u += lpr) run_unit<MT, kDirectRows, false>(fmt, rows, u, 0, K, xp, acc);
         }
+        reduce_lanes<MT, kDirectRows>(acc, lpr);
+        if (sub_lane == 0 && rs < p.total_rowsets) store_rows<MT, kDirectRows>(p, p.s[si], n, acc, swiglu);
+    }
+}
+
+// ============================================================= streamed kernel
+// Persistent CTAs of four warps, several CTAs per SM.  Every warp runs its
+// own pipeline: lane 0 streams the warp's row blocks HBM -> shared memory with
+// 1-D bulk async copies into a private ring of `stages` buffers (completion
+// on one mbarrier per buffer) and refills a buffer as soon as the warp has
+// decoded it, so each warp keeps `stages` copies in flight and no warp waits
+// for another.  Stage = one row block x one K segment: rb rows, each a
+// contiguous segment of seg_bytes (or, for `whole` streams, rb full rows
+// copied at once).  Row group g of kNR rows is served by lpr lanes (one
+// 64-value unit per lane per stage; x fragments reused across the kNR rows).
+// SwiGLU row blocks hold rb/2 gate rows then the rb/2 matching up rows; a
+// row group is then two outputs (gate, up, gate, up).
+constexpr int kNR = 4;
+constexpr int kConsumerWarps = kWarps;
+constexpr int kConsumerThreads = kThreads;
+constexpr size_t kStageHead = 512;  // full barriers [kWarps][kMaxStages]
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+// 16 bytes at a 2-byte aligned shared address.
+__device__ __forceinline__ uint4 lds128_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12);
+    const uint32_t w4 = sh ? lds32(b + 16) : 0u;
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+__device__ __forceinline__ float small_u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+// x planes as shared addresses.
+struct XS {
+    uint32_t xh, xl, meta, sx, xq16;
+    int kp, u64, s32;  // padded row stride, K/64, K/32
+    __device__ __forceinline__ uint32_t off(int m, int k) const {
+        return static_cast<uint32_t>(m * kp + k + ((k >> 6) << 4));
+    }
+};
+
+// Q4_K: rows[r] = shared address of the 144-byte block, G = group, k0 = first value.
+template <int MT>
+__device__ __forceinline__ void lane_q4k(const uint32_t rows[kNR], int G, int k0, const XS &x,
+                                         float acc[kNR][MT]) {
+    const int i0 = (2 * G) & 3;
+    const bool low = G < 2;
+    uint4 q0[kNR], q1[kNR];
+    float ds0[kNR], ds1[kNR], dm0[kNR], dm1[kNR];
 #pragma unroll
-        for (int r = 0; r < kRows; ++r)
+    for (int r = 0; r < kNR; ++r) {
+        const uint4 h = lds128(rows[r]);
+        q0[r] = lds128(rows[r] + 16 + 32 * G);
+        q1[r] = lds128(rows[r] + 32 + 32 * G);
+        const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+        const uint32_t y = h.y >> (8 * i0), z = h.z >> (8 * i0), w = h.w >> (8 * i0);
+        const uint32_t hs = ((y >> 6) & 0x3u) | (((y >> 14) & 0x3u) << 8);
+        const uint32_t hm = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
+        const uint32_t scp = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hs << 4));
+        const uint32_t mnp = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hm << 4));
+        ds0[r] = d * small_u2f(scp & 0xffu);
+        ds1[r] = d * small_u2f(scp >> 8) * 0.0625f;  // high nibbles enter dp4a as 16*q
+        dm0[r] = dmin * small_u2f(mnp & 0xffu);
+        dm1[r] = dmin * small_u2f(mnp >> 8);
+    }
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                float v = acc[r][m];
-                for (int o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                acc[r][m] = v;
+    for (int m = 0; m < MT; ++m) {
+        const uint32_t xo = x.off(m, k0);
+        const uint4 hA0 = lds128(x.xh + xo), hA1 = lds128(x.xh + xo + 16), hB0 = lds128(x.xh + xo + 32),
+                    hB1 = lds128(x.xh + xo + 48);
+        const uint4 lA0 = lds128(x.xl + xo), lA1 = lds128(x.xl + xo + 16), lB0 = lds128(x.xl + xo + 32),
+                    lB1 = lds128(x.xl + xo + 48);
+        const uint4 mt = lds128(x.meta + 16u * static_cast<uint32_t>(m * x.u64 + (k0 >> 6)));
+        const float s0 = __uint_as_float(mt.x), s1 = __uint_as_float(mt.y);
+        const float xs0 = __uint_as_float(mt.z), xs1 = __uint_as_float(mt.w);
+        const uint32_t xhA[8] = {hA0.x, hA0.y, hA0.z, hA0.w, hA1.x, hA1.y, hA1.z, hA1.w};
+        const uint32_t xlA[8] = {lA0.x, lA0.y, lA0.z, lA0.w, lA1.x, lA1.y, lA1.z, lA1.w};
+        const uint32_t xhB[8] = {hB0.x, hB0.y, hB0.z, hB0.w, hB1.x, hB1.y, hB1.z, hB1.w};
+        const uint32_t xlB[8] = {lB0.x, lB0.y, lB0.z, lB0.w, lB1.x, lB1.y, lB1.z, lB1.w};
+#pragma unroll
+        for (int r = 0; r < kNR; ++r) {
+            const uint32_t wq[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
+            int hiL = 0, loL = 0, hiH = 0, loH = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t lo4 = wq[i] & 0x0F0F0F0Fu, hi4 = wq[i] & 0xF0F0F0F0u;
+                hiL = dp4a_us(lo4, static_cast<int>(xhA[i]), hiL);
+                loL = dp4a_us(lo4, static_cast<int>(xlA[i]), loL);
+                hiH = dp4a_us(hi4, static_cast<int>(xhB[i]), hiH);
+                loH = dp4a_us(hi4, static_cast<int>(xlB[i]), loH);
             }
-        if (sub_lane == 0 && rs < p.total_rowsets) {
-            if (p.mode == MODE_SWIGLU) {
-                __half *y = p.s[0].y;
-                const int64_t N = p.s[0].n;
+            float a = acc[r][m];
+            a = fmaf(ds0[r] * s0, static_cast<float>(hiL * 128 + loL), a);
+            a = fmaf(ds1[r] * s1, static_cast<float>(hiH * 128 + loH), a);
+            a = fmaf(-dm0[r], xs0, a);
+            a = fmaf(-dm1[r], xs1, a);
+            acc[r][m] = a;
+        }
+    }
+}
+
+// Q6_K: rows[r] = shared address of the 210-byte block; sl = 2 s + lh; kk = value index of (s, lh, c=0, l=0).
+template <int MT>
+__device__ __forceinline__ void lane_q6k(const uint32_t rows[kNR], int sl, int kk, const XS &x,
+                                         float acc[kNR][MT]) {
+    const int s = sl >> 1, lh = sl & 1;
+    uint4 qa[kNR], qb[kNR], qh[kNR];
+    float dsc[kNR][4];
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    if ((rows.valid >> r) & 1) {
+    for (int r = 0; r < kNR; ++r) {
+        qa[r] = lds128_a2(rows[r] + 64 * s + 16 * lh);
+        qb[r] = lds128_a2(rows[r] + 64 * s + 32 + 16 * lh);
+        qh[r] = lds128_a2(rows[r] + 128 + 32 * s + 16 * lh);
+        const float d = half_bits_to_float(lds16(rows[r] + 208));
 #pragma unroll
-                        for (int m = 0; m < MT; ++m)
-                            if (m < p.M) y[m * N + n0 + r] = __float2half_rn(silu(acc[r][m]) * acc[r + 2][m]);
-                    }
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t pair = lds16(rows[r] + 192 + 8 * s + 2 * c);
+            dsc[r][c] = d * static_cast<float>(static_cast<int8_t>((pair >> (8 * lh)) & 0xffu));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int k = kk + 32 * c;
+            const uint4 xh4 = lds128(x.xh + x.off(m, k)), xl4 = lds128(x.xl + x.off(m, k));
+            const float sxv = __uint_as_float(lds32(x.sx + 4u * static_cast<uint32_t>(m * x.s32 + (k >> 5))));
+            const int q16 = static_cast<int>(lds32(x.xq16 + 4u * static_cast<uint32_t>(m * x.s32 * 2 + (k >> 4))));
+            const uint32_t xhw[4] = {xh4.x, xh4.y, xh4.z, xh4.w};
+            const uint32_t xlw[4] = {xl4.x, xl4.y, xl4.z, xl4.w};
+#pragma unroll
+            for (int r = 0; r < kNR; ++r) {
+                const uint4 ql = (c & 1) ? qb[r] : qa[r];
+                const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
+                const uint32_t hw[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
+                int hi = 0, lo = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t l4 = (c >> 1) ? ((lw[i] >> 4) & 0x0F0F0F0Fu) : (lw[i] & 0x0F0F0F0Fu);
+                    const uint32_t level = l4 | (((hw[i] >> (2 * c)) & 0x03030303u) << 4);
+                    hi = dp4a_us(level, static_cast<int>(xhw[i]), hi);
+                    lo = dp4a_us(level, static_cast<int>(xlw[i]), lo);
                 }
-            } else {
-                const QStream &st = p.s[si];
-#pragma unroll
-                for (int r = 0; r < kRows; ++r) {
-                    if (!((rows.valid >> r) & 1)) continue;
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) {
-                        if (m < p.M) {
-                            const int64_t o = m * st.n + n0 + r;
-                            float v = acc[r][m];
-                            if (st.res) v += __half2float(st.res[o]);
-                            st.y[o] = __float2half_rn(v);
-                        }
-                    }
-                }
+                acc[r][m] = fmaf(dsc[r][c] * sxv, static_cast<float>(hi * 128 + lo - 32 * q16), acc[r][m]);
             }
         }
     }
 }
 
-size_t smem_bytes(int MT, int K) {
-    return static_cast<size_t>(MT) * K * 2 + static_cast<size_t>(MT) * (K / 32) * 4 +
-           static_cast<size_t>(MT) * (K / 16) * 4 + static_cast<size_t>(kWarps) * 8 * 4;
+// Q8_0: rows[r] = shared address of the block pair (68 bytes, 4-byte aligned); k0 = first value.
+template <int MT>
+__device__ __forceinline__ void lane_q8_0(const uint32_t rows[kNR], int k0, const XS &x, float acc[kNR][MT]) {
+    uint32_t qa[kNR][8], qb[kNR][8];
+    float da[kNR], db[kNR];
+#pragma unroll
+    for (int r = 0; r < kNR; ++r) {
+        uint32_t w[17];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) w[i] = lds32(rows[r] + 4 * i);
+        da[r] = half_bits_to_float(w[0]);
+        db[r] = half_bits_to_float(w[8] >> 16);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qa[r][i] = __funnelshift_r(w[i], w[i + 1], 16);
+            qb[r][i] = w[9 + i];
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        const uint32_t xo = x.off(m, k0);
+        const uint4 h0 = lds128(x.xh + xo), h1 = lds128(x.xh + xo + 16), h2 = lds128(x.xh + xo + 32),
+                    h3 = lds128(x.xh + xo + 48);
+        const uint4 l0 = lds128(x.xl + xo), l1 = lds128(x.xl + xo + 16), l2 = lds128(x.xl + xo + 32),
+                    l3 = lds128(x.xl + xo + 48);
+        const uint4 mt = lds128(x.meta + 16u * static_cast<uint32_t>(m * x.u64 + (k0 >> 6)));
+        const float sA = __uint_as_float(mt.x), sB = __uint_as_float(mt.y);
+        const uint32_t xhA[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t xlA[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const uint32_t xhB[8] = {h2.x, h2.y, h2.z, h2.w, h3.x, h3.y, h3.z, h3.w};
+        const uint32_t xlB[8] = {l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+#pragma unroll
+        for (int r = 0; r < kNR; ++r) {
+            int hA = 0, lA = 0, hB = 0, lB = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                hA = dp4a_ss(static_cast<int>(qa[r][i]), static_cast<int>(xhA[i]), hA);
+                lA = dp4a_ss(static_cast<int>(qa[r][i]), static_cast<int>(xlA[i]), lA);
+                hB = dp4a_ss(static_cast<int>(qb[r][i]), static_cast<int>(xhB[i]), hB);
+                lB = dp4a_ss(static_cast<int>(qb[r][i]), static_cast<int>(xlB[i]), lB);
+            }
+            float a = acc[r][m];
+            a = fmaf(da[r] * sA, static_cast<float>(hA * 128 + lA), a);
+            a = fmaf(db[r] * sB, static_cast<float>(hB * 128 + lB), a);
+            acc[r][m] = a;
+        }
+    }
 }
 
-int pick_mt(int64_t M, int K) {
-    const size_t budget = 160 * 1024;
-    int mt = 8;
-    while (mt > 1 && (mt / 2 >= M || smem_bytes(mt, K) > budget)) mt /= 2;
-    return mt;
+__device__ __forceinline__ int stream_of(const QParams &p, int64_t block) {
+    int si = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxStreams; ++i)
+        if (i < p.nstreams && block >= p.s[i].rs_begin) si = i;
+    return si;
+}
+
+__device__ __forceinline__ int64_t block_first_row(const QParams &p, int si, int64_t block) {
+    const int rows = p.mode == MODE_SWIGLU ? p.s[0].rb / 2 : p.s[si].rb;
+    return (block - p.s[si].rs_begin) * rows;
+}
+
+// Issues the bulk copies of one stage and arms its full barrier.
+__device__ __forceinline__ void issue_stage(const QParams &p, int64_t block, int chunk, uint8_t *stage,
+                                            uint64_t *bar) {
+    const int si = stream_of(p, block);
+    const int64_t row0 = block_first_row(p, si, block);
+    const QStream &st = p.s[si];
+    if (p.mode == MODE_SWIGLU) {
+        const int half = st.rb / 2;
+        const int64_t left = p.s[0].n - row0;
+        const int nv = left < half ? static_cast<int>(left) : half;
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nv) * 2u * st.seg_bytes);
+        for (int g = 0; g < 2; ++g) {
+            const QStream &sg = p.s[g];
+            for (int r = 0; r < nv; ++r) {
+                const uint8_t *src = sg.w + (row0 + r) * sg.row_bytes + static_cast<int64_t>(chunk) * st.seg_bytes;
+                bulk_g2s(stage + (g * half + r) * st.seg_bytes, src, st.seg_bytes, bar);
+            }
+        }
+        return;
+    }
+    const int64_t left = st.n - row0;
+    const int nv = left < st.rb ? static_cast<int>(left) : st.rb;
+    if (st.whole) {
+        const uint32_t bytes = static_cast<uint32_t>(nv * st.row_bytes);
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(stage, st.w + row0 * st.row_bytes, bytes, bar);
+        return;
+    }
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nv) * st.seg_bytes);
+    for (int r = 0; r < nv; ++r) {
+        const uint8_t *src = st.w + (row0 + r) * st.row_bytes + static_cast<int64_t>(chunk) * st.seg_bytes;
+        bulk_g2s(stage + r * st.seg_bytes, src, st.seg_bytes, bar);
+    }
+}
+
+// Advances a warp's item cursor (row block, K segment) by one.
+__device__ __forceinline__ void next_item(const QParams &p, int64_t &block, int &chunk, int64_t block_stride) {
+    if (++chunk == p.s[stream_of(p, block)].chunks) {
+        chunk = 0;
+        block += block_stride;
+    }
 }
 
 template <int MT, int FMT>
-int launch_mt(QParams p, cudaStream_t stream) {
-    const size_t smem = smem_bytes(MT, p.K);
-    static bool configured[64] = {false};
-    int device = 0;
-    cudaGetDevice(&device);
-    if (device < 0 || device >= 64) return set_error(T2C_EINVAL, "device index %d out of range", device);
-    if (!configured[device]) {
-        if (cudaFuncSetAttribute(qmv_kernel<MT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+__global__ void __launch_bounds__(kConsumerThreads) qmv_tma_kernel(const QParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int K = p.K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
+    uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
+    float4 *meta = reinterpret_cast<float4 *>(smem + kStageHead + static_cast<size_t>(kWarps) * S * p.stage_bytes);
+    int8_t *xh = reinterpret_cast<int8_t *>(meta + MT * (K >> 6));
+    int8_t *xl = xh + MT * padded_k(K);
+    float *sx = reinterpret_cast<float *>(xl + MT * padded_k(K));
+    int *xq16 = reinterpret_cast<int *>(sx + MT * (K >> 5));
+    float *red = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
+    const int64_t block_stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    const int64_t first_block = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+
+    // Weights are static: start streaming before the dependency on the
+    // previous kernel in the stream resolves.
+    if (lane == 0) {
+        for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+        fence_mbar_init();
+        int64_t block = first_block;
+        int chunk = 0;
+        for (int i = 0; i < S && block < p.total_rowsets; ++i) {
+            issue_stage(p, block, chunk, stages + static_cast<size_t>(i) * p.stage_bytes, &full[i]);
+            next_item(p, block, chunk, block_stride);
+        }
+    }
+    pdl_wait();
+    prepare_x<MT, kConsumerThreads>(p, xh, xl, sx, xq16, meta, red);  // ends with __syncthreads
+    pdl_trigger();
+    const XS x{smem_u32(xh), smem_u32(xl), smem_u32(meta), smem_u32(sx), smem_u32(xq16), padded_k(K), K >> 6,
+               K >> 5};
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const uint32_t stages_addr = smem_u32(stages);
+
+    int s = 0;
+    uint32_t phase = 0;
+    int64_t ahead_block = first_block;  // cursor S items ahead of the one consumed
+    int ahead_chunk = 0;
+    for (int i = 0; i < S; ++i) next_item(p, ahead_block, ahead_chunk, block_stride);
+    for (int64_t block = first_block; block < p.total_rowsets; block += block_stride) {
+        const int si = stream_of(p, block);
+        const QStream &st = p.s[si];
+        const int64_t row0 = block_first_row(p, si, block);
+        const int fmt = FMT != 0 ? FMT : st.fmt;
+        const int lpr = st.lpr;
+        const int group = lane / lpr, glane = lane - group * lpr;
+        const int units = fmt == T2C_Q8_0 ? st.seg_blocks / 2 : st.seg_blocks * 4;
+        const int seg_stride = st.whole ? static_cast<int>(st.row_bytes) : st.seg_bytes;
+        const int seg_values = st.seg_blocks * (fmt == T2C_Q8_0 ? 32 : 256);
+        uint32_t roff[kNR];
+        int64_t n[kNR];
+#pragma unroll
+        for (int r = 0; r < kNR; ++r) {
+            int srow;
+            if (swiglu) {
+                const int o = 2 * group + (r >> 1);
+                srow = (r & 1) * (st.rb / 2) + o;
+                n[r] = row0 + o < p.s[0].n ? row0 + o : -1;
+            } else {
+                srow = group * kNR + r;
+                n[r] = row0 + srow < st.n ? row0 + srow : -1;
+            }
+            roff[r] = static_cast<uint32_t>(srow * seg_stride);
+        }
+        float acc[kNR][MT];
+#pragma unroll
+        for (int r = 0; r < kNR; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
+        for (int c = 0; c < st.chunks; ++c) {
+            if (!mbar_wait(&full[s], phase)) {
+                // Copies never completed: report and leave without touching the stage.
+                report_device_error(T2C_ETIMEOUT);
+                return;
+            }
+            const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
+            const int kseg = c * seg_values;
+            for (int u = glane; u < units; u += lpr) {
+                uint32_t rows[kNR];
+                if (fmt == T2C_Q4_K) {
+#pragma unroll
+                    for (int r = 0; r < kNR; ++r) rows[r] = stage + roff[r] + (u >> 2) * 144;
+                    lane_q4k<MT>(rows, u & 3, kseg + (u >> 2) * 256 + (u & 3) * 64, x, acc);
+                } else if (fmt == T2C_Q6_K) {
+#pragma unroll
+                    for (int r = 0; r < kNR; ++r) rows[r] = stage + roff[r] + (u >> 2) * 210;
+                    const int sl = u & 3;
+                    lane_q6k<MT>(rows, sl, kseg + (u >> 2) * 256 + (sl >> 1) * 128 + (sl & 1) * 16, x, acc);
+                } else {
+#pragma unroll
+                    for (int r = 0; r < kNR; ++r) rows[r] = stage + roff[r] + u * 68;
+                    lane_q8_0<MT>(rows, kseg + u * 64, x, acc);
+                }
+            }
+            // Refill this buffer with the item S positions ahead (async-proxy
+            // writes after the warp's generic reads).
+            __syncwarp();
+            if (lane == 0 && ahead_block < p.total_rowsets) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_stage(p, ahead_block, ahead_chunk, stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
+            }
+            next_item(p, ahead_block, ahead_chunk, block_stride);
+            if (++s == S) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+        reduce_lanes<MT, kNR>(acc, lpr);
+        if (glane == 0) store_rows<MT, kNR>(p, st, n, acc, swiglu);
+    }
+}
+
+// ================================================================== launchers
+size_t x_smem_bytes(int MT, int K) {
+    return static_cast<size_t>(MT) * (K / 64) * 16 + static_cast<size_t>(MT) * padded_k(K) * 2 +
+           static_cast<size_t>(MT) * (K / 32) * 4 + static_cast<size_t>(MT) * (K / 16) * 4 +
+           static_cast<size_t>(kConsumerWarps) * 8 * 4;
+}
+
+constexpr size_t kSmemLimit = 220 * 1024;
+
+int pick_mt(int64_t M, int K) {
+    const size_t budget = 96 * 1024;
+    int mt = 8;
+    while (mt > 1 && (mt / 2 >= M || x_smem_bytes(mt, K) > budget)) mt /= 2;
+    return mt;
+}
+
+template <typename Kernel>
+int ensure_smem_attr(Kernel kernel, bool &configured_flag) {
+    if (!configured_flag) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)) !=
             cudaSuccess) {
             return set_error(T2C_ECUDA, "qmv: cudaFuncSetAttribute failed");
         }
-        configured[device] = true;
+        configured_flag = true;
     }
-    const int sms = sm_count();
-    const int subs_per_block = kWarps * (32 / p.lpr);
-    int64_t blocks = (p.total_rowsets + subs_per_block - 1) / subs_per_block;
-    const int64_t max_blocks = static_cast<int64_t>(sms) * (smem > 100 * 1024 ? 1 : 2);
-    if (blocks > max_blocks) blocks = max_blocks;
-    if (blocks < 1) blocks = 1;
+    return T2C_OK;
+}
+
+int device_slot() {
+    int device = 0;
+    cudaGetDevice(&device);
+    return device < 0 ? 0 : (device > 63 ? 63 : device);
+}
+
+template <typename Kernel>
+int launch_pdl(Kernel kernel, int blocks, int threads, size_t smem, cudaStream_t stream, const QParams &p) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -588,34 +1055,104 @@ int launch_mt(QParams p, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, qmv_kernel<MT, FMT>, p);
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, p);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "qmv launch: %s", cudaGetErrorString(err));
     return T2C_OK;
 }
 
+template <int MT, int FMT>
+int launch_direct(QParams p, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    const size_t smem = x_smem_bytes(MT, p.K);
+    int rc = ensure_smem_attr(qmv_direct_kernel<MT, FMT>, configured[device_slot()]);
+    if (rc) return rc;
+    const int subs_per_block = kWarps * (32 / p.lpr);
+    int64_t blocks = (p.total_rowsets + subs_per_block - 1) / subs_per_block;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmv_direct_kernel<MT, FMT>, kThreads, smem) !=
+            cudaSuccess ||
+        per_sm < 1) {
+        per_sm = 1;
+    }
+    const int64_t max_blocks = static_cast<int64_t>(sm_count()) * per_sm;
+    if (blocks > max_blocks) blocks = max_blocks;
+    if (blocks < 1) blocks = 1;
+    return launch_pdl(qmv_direct_kernel<MT, FMT>, static_cast<int>(blocks), kThreads, smem, stream, p);
+}
+
+int tma_stages(int mt, const QParams &p);
+
+template <int MT, int FMT>
+int launch_tma(QParams p, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    p.stages = tma_stages(MT, p);
+    if (p.stages < 2) return set_error(T2C_EUNSUPPORTED, "qmv: stage of %d bytes does not fit", p.stage_bytes);
+    const size_t smem =
+        kStageHead + static_cast<size_t>(kWarps) * p.stages * p.stage_bytes + x_smem_bytes(MT, p.K);
+    int rc = ensure_smem_attr(qmv_tma_kernel<MT, FMT>, configured[device_slot()]);
+    if (rc) return rc;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmv_tma_kernel<MT, FMT>, kConsumerThreads, smem) !=
+            cudaSuccess ||
+        per_sm < 1) {
+        per_sm = 1;
+    }
+    int64_t blocks = (p.total_rowsets + kWarps - 1) / kWarps;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+    if (blocks > cap) blocks = cap;
+    return launch_pdl(qmv_tma_kernel<MT, FMT>, static_cast<int>(blocks), kConsumerThreads, smem, stream, p);
+}
+
 template <int FMT>
-int launch_fmt_mt(const QParams &c, int mt, cudaStream_t stream) {
+int launch_fmt_mt(const QParams &c, int mt, bool tma, cudaStream_t stream) {
+    if (tma) {
+        switch (mt) {
+            case 1: return launch_tma<1, FMT>(c, stream);
+            case 2: return launch_tma<2, FMT>(c, stream);
+            case 4: return launch_tma<4, FMT>(c, stream);
+            default: return launch_tma<8, FMT>(c, stream);
+        }
+    }
     switch (mt) {
-        case 1: return launch_mt<1, FMT>(c, stream);
-        case 2: return launch_mt<2, FMT>(c, stream);
-        case 4: return launch_mt<4, FMT>(c, stream);
-        default: return launch_mt<8, FMT>(c, stream);
+        case 1: return launch_direct<1, FMT>(c, stream);
+        case 2: return launch_direct<2, FMT>(c, stream);
+        case 4: return launch_direct<4, FMT>(c, stream);
+        default: return launch_direct<8, FMT>(c, stream);
     }
 }
 
-int launch_fmt(const QParams &c, int mt, cudaStream_t stream) {
+int launch_fmt(const QParams &c, int mt, bool tma, cudaStream_t stream) {
     int fmt = c.s[0].fmt;
     for (int i = 1; i < c.nstreams; ++i)
         if (c.s[i].fmt != fmt) fmt = 0;
     switch (fmt) {
-        case T2C_Q4_K: return launch_fmt_mt<T2C_Q4_K>(c, mt, stream);
-        case T2C_Q6_K: return launch_fmt_mt<T2C_Q6_K>(c, mt, stream);
-        case T2C_Q8_0: return launch_fmt_mt<T2C_Q8_0>(c, mt, stream);
-        default: return launch_fmt_mt<0>(c, mt, stream);
+        case T2C_Q4_K: return launch_fmt_mt<T2C_Q4_K>(c, mt, tma, stream);
+        case T2C_Q6_K: return launch_fmt_mt<T2C_Q6_K>(c, mt, tma, stream);
+        case T2C_Q8_0: return launch_fmt_mt<T2C_Q8_0>(c, mt, tma, stream);
+        default: return launch_fmt_mt<0>(c, mt, tma, stream);
     }
 }
 
-int launch_chunked(QParams p, int64_t M, cudaStream_t stream) {
+// Ring depth per warp of the streamed kernel: about kStreamBytesPerSm of
+// weights in flight per SM, spread over the CTAs that fit (>= 2 buffers per
+// warp, 0 when nothing fits).
+constexpr size_t kSmPerSmem = 227 * 1024;
+constexpr size_t kStreamBytesPerSm = 160 * 1024;
+
+int tma_stages(int mt, const QParams &p) {
+    const size_t xbytes = x_smem_bytes(mt, p.K);
+    const size_t stage = static_cast<size_t>(p.stage_bytes);
+    for (int ctas = 4; ctas >= 1; --ctas) {
+        int stages = static_cast<int>(kStreamBytesPerSm / ctas / (kWarps * stage));
+        if (stages < 2) stages = 2;
+        if (stages > kMaxStages) stages = kMaxStages;
+        const size_t per_cta = kStageHead + kWarps * stages * stage + xbytes + 1024;
+        if (per_cta * ctas <= kSmPerSmem && per_cta <= kSmemLimit) return stages;
+    }
+    return 0;
+}
+
+int launch_chunked(QParams p, int64_t M, bool tma, cudaStream_t stream) {
     const int mt = pick_mt(M, p.K);
     const int64_t K = p.K;
     for (int64_t m0 = 0; m0 < M; m0 += mt) {
@@ -626,7 +1163,7 @@ int launch_chunked(QParams p, int64_t M, cudaStream_t stream) {
             if (c.s[i].y) c.s[i].y = p.s[i].y + m0 * p.s[i].n;
             if (c.s[i].res) c.s[i].res = p.s[i].res + m0 * p.s[i].n;
         }
-        int rc = launch_fmt(c, mt, stream);
+        int rc = launch_fmt(c, mt, tma, stream);
         if (rc != T2C_OK) return rc;
     }
     return T2C_OK;
@@ -635,7 +1172,7 @@ int launch_chunked(QParams p, int64_t M, cudaStream_t stream) {
 int validate_common(int64_t M, int64_t K, const void *x) {
     if (x == nullptr) return set_error(T2C_EINVAL, "x is NULL");
     if (M <= 0 || K <= 0) return set_error(T2C_EINVAL, "M=%lld K=%lld must be positive", (long long)M, (long long)K);
-    if (K % 256 != 0 && K % 64 != 0) return set_error(T2C_EINVAL, "K=%lld must be a multiple of 64", (long long)K);
+    if (K % 64 != 0) return set_error(T2C_EINVAL, "K=%lld must be a multiple of 64", (long long)K);
     if (K > 65536) return set_error(T2C_EUNSUPPORTED, "K=%lld above 65536", (long long)K);
     if (reinterpret_cast<uintptr_t>(x) % 16 != 0) return set_error(T2C_EINVAL, "x must be 16-byte aligned");
     return T2C_OK;
@@ -658,13 +1195,96 @@ int validate_weight(int wtype, const void *w, int64_t K) {
     return T2C_OK;
 }
 
-int lanes_per_row(int units) {
+int lanes_for(int units) {
     int lpr = 32;
     while (lpr > 4 && lpr > units) lpr >>= 1;
     return lpr;
 }
 
+// Streamed geometry of one stream, or false when it cannot be bulk-copied
+// (every copy must start 16-byte aligned and move a multiple of 16 bytes).
+// Rows per row block: 4 consumer warps x (32 / lpr) groups x 4 rows.
+bool tma_geometry(QStream &st, int64_t K, bool swiglu) {
+    if (reinterpret_cast<uintptr_t>(st.w) % 16) return false;
+    const int block_values = st.fmt == T2C_Q8_0 ? 32 : 256;
+    const int block_bytes = st.fmt == T2C_Q4_K ? 144 : (st.fmt == T2C_Q6_K ? 210 : 34);
+    const int nb = static_cast<int>(K / block_values);
+    int seg_blocks = st.fmt == T2C_Q8_0 ? 32 : 8;
+    if (seg_blocks > nb) seg_blocks = nb;
+    while (nb % seg_blocks) --seg_blocks;
+    const bool seg_ok = (st.row_bytes % 16 == 0) && ((seg_blocks * block_bytes) % 16 == 0) &&
+                        (st.fmt != T2C_Q8_0 || seg_blocks % 2 == 0);
+    if (seg_ok) {
+        st.whole = 0;
+        st.seg_blocks = seg_blocks;
+        st.seg_bytes = seg_blocks * block_bytes;
+        st.chunks = nb / seg_blocks;
+    } else {
+        if (swiglu) return false;
+        if (st.fmt == T2C_Q8_0 && nb % 2) return false;
+        st.whole = 1;
+        st.seg_blocks = nb;
+        st.seg_bytes = static_cast<int>(st.row_bytes);
+        st.chunks = 1;
+    }
+    const int units = st.fmt == T2C_Q8_0 ? st.seg_blocks / 2 : st.seg_blocks * 4;
+    st.lpr = lanes_for(units);
+    if (st.lpr < 8) return false;
+    st.rb = (32 / st.lpr) * kNR;
+    if (st.whole && ((st.rb * st.row_bytes) % 16 != 0 || st.n % st.rb != 0)) return false;
+    return true;
+}
+
+// Chooses the streamed kernel when every stream can be bulk-copied.
+int run_linear(QParams p, int64_t M, cudaStream_t stream) {
+    bool tma = true;
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    int stage_bytes = 0;
+    for (int i = 0; i < p.nstreams && tma; ++i) {
+        QStream &st = p.s[i];
+        if (!tma_geometry(st, p.K, swiglu)) {
+            tma = false;
+            break;
+        }
+        const int bytes = st.rb * st.seg_bytes;
+        if (bytes > stage_bytes) stage_bytes = bytes;
+    }
+    if (tma) {
+        p.stage_bytes = stage_bytes;
+        if (tma_stages(pick_mt(M, p.K), p) < 2) tma = false;
+    }
+    if (tma) {
+        int64_t blocks = 0;
+        for (int i = 0; i < p.nstreams; ++i) {
+            QStream &st = p.s[i];
+            st.rs_begin = blocks;
+            const int64_t rows_per_block = swiglu ? st.rb / 2 : st.rb;
+            blocks += (st.n + rows_per_block - 1) / rows_per_block;
+            if (swiglu) break;  // gate and up form one stream of outputs
+        }
+        if (swiglu) p.s[1].rs_begin = blocks;  // never selected
+        p.total_rowsets = blocks;
+        p.stage_bytes = stage_bytes;
+        return launch_chunked(p, M, true, stream);
+    }
+    // direct kernel: row-sets of 2 rows (ROWS) or 1 output (SWIGLU)
+    p.units = p.K / 64;
+    p.lpr = lanes_for(p.units);
+    int64_t rs = 0;
+    for (int i = 0; i < p.nstreams; ++i) {
+        p.s[i].rs_begin = rs;
+        rs += swiglu ? p.s[i].n : (p.s[i].n + kDirectRows - 1) / kDirectRows;
+        if (swiglu) break;
+    }
+    if (swiglu) p.s[1].rs_begin = rs;
+    p.total_rowsets = rs;
+    return launch_chunked(p, M, false, stream);
+}
+
 }  // namespace
+
+cudaError_t status_qlinear(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
+
 }  // namespace t2c
 
 using namespace t2c;
@@ -682,9 +1302,6 @@ extern "C" int t2c_linear_multi(int count, const int *wtypes, const void *const 
     p.norm_w = norm_weight;
     p.eps = eps;
     p.K = static_cast<int>(K);
-    p.units = static_cast<int>(K / 64);
-    p.lpr = lanes_per_row(p.units);
-    int64_t rs = 0;
     for (int i = 0; i < count; ++i) {
         if ((rc = validate_weight(wtypes[i], ws[i], K))) return rc;
         if (ys[i] == nullptr || Ns[i] <= 0) return set_error(T2C_EINVAL, "stream %d: bad output or N", i);
@@ -694,11 +1311,8 @@ extern "C" int t2c_linear_multi(int count, const int *wtypes, const void *const 
         p.s[i].n = Ns[i];
         p.s[i].row_bytes = row_bytes(wtypes[i], K);
         p.s[i].fmt = wtypes[i];
-        p.s[i].rs_begin = rs;
-        rs += (Ns[i] + kRows - 1) / kRows;
     }
-    p.total_rowsets = rs;
-    return launch_chunked(p, M, as_stream(stream));
+    return run_linear(p, M, as_stream(stream));
 }
 
 extern "C" int t2c_linear(int wtype, const void *x, const void *w, const void *residual, void *y, int64_t M,
@@ -725,11 +1339,14 @@ extern "C" int t2c_linear_swiglu(int wtype, const void *x, const void *w_gate, c
     p.norm_w = norm_weight;
     p.eps = eps;
     p.K = static_cast<int>(K);
-    p.units = static_cast<int>(K / 64);
-    p.lpr = lanes_per_row(p.units);
     const int64_t rb = row_bytes(wtype, K);
-    p.s[0] = QStream{static_cast<const uint8_t *>(w_gate), static_cast<__half *>(y), nullptr, N, rb, 0, wtype};
-    p.s[1] = QStream{static_cast<const uint8_t *>(w_up), nullptr, nullptr, N, rb, 0, wtype};
-    p.total_rowsets = (N + 1) / 2;
-    return launch_chunked(p, M, as_stream(stream));
+    p.s[0].w = static_cast<const uint8_t *>(w_gate);
+    p.s[0].y = static_cast<__half *>(y);
+    p.s[0].n = N;
+    p.s[0].row_bytes = rb;
+    p.s[0].fmt = wtype;
+    p.s[1] = p.s[0];
+    p.s[1].w = static_cast<const uint8_t *>(w_up);
+    p.s[1].y = nullptr;
+    return run_linear(p, M, as_stream(stream));
 }
