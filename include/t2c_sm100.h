@@ -42,6 +42,10 @@ enum { T2C_Q8_0 = 8, T2C_Q4_K = 12, T2C_Q6_K = 14, T2C_F16 = 1 };
 
 const char *t2c_last_error(void);
 int t2c_abi_version(void);
+/* Reads (and with clear != 0 resets) the device status bits that kernels set
+ * with 1 << T2C_E* (e.g. T2C_ETIMEOUT when a bounded wait ran out).  Synchronises
+ * the stream. */
+int t2c_device_status(unsigned int *bits, int clear, void *stream);
 /* Number of SMs of the current device (grid sizing helper for callers). */
 int t2c_device_sm_count(void);
 
@@ -88,6 +92,119 @@ int t2c_linear_multi(int count, const int *wtypes, const void *const *ws, void *
 int t2c_linear_swiglu(int wtype, const void *x, const void *w_gate, const void *w_up, void *y,
                       const float *norm_weight, float eps, int64_t M, int64_t N, int64_t K,
                       void *stream);
+
+/*
+ * LM head with the greedy-select partial epilogue: for every token m and every
+ * group of 4 consecutive vocabulary rows g, partial_scores[m, g] / partial_tokens[m, g]
+ * hold the best fp32 logit and its row (ties -> lower row), G = ceil(N / 4).
+ * Replaces LmHeadQ6KArgmaxPartialF16Program
+ *   src/torch2vk/export/shaders/lm_head_q6_k_argmax_partial_f16.py (batch 1 there;
+ *   here M tokens).  norm_weight as in t2c_linear_multi (final RMSNorm fused).
+ */
+int t2c_lm_head_argmax(int wtype, const void *x, const void *w, float *partial_scores,
+                       uint32_t *partial_tokens, const float *norm_weight, float eps, int64_t M,
+                       int64_t N, int64_t K, void *stream);
+
+/* ---------------------------------------------------------- greedy select
+ * Reduces G partials per token to the winning token (ties -> lower id) and
+ * flags it done when it equals one of the E eos ids.
+ * Replaces Qwen3TokenSelectReduceF32Program / Qwen3TokenSelectReduceChunksF32Program
+ *   src/torch2vk/export/shaders/qwen3_token_select_reduce_f32.py:21-241
+ * partial_* are [M, G]; next_token int64 [M]; done uint32 [M].
+ */
+int t2c_token_select(const float *partial_scores, const uint32_t *partial_tokens, int64_t M, int64_t G,
+                     const int64_t *eos_ids, int64_t E, int64_t *next_token, uint32_t *done, void *stream);
+
+/*
+ * Appends next_token[b] at generated_tokens[b, token_index] (capacity G) and
+ * updates generated_length / stopped, honouring stop_on_eos.  token_index is
+ * read from device memory (token_index_dev, int32) when non-NULL so a
+ * captured graph can replay it, else taken from token_index.
+ * Replaces Qwen3TokenStoreEosProgram / Qwen3TokenStoreProgram
+ *   src/torch2vk/export/shaders/qwen3_token_store.py:1-145
+ */
+int t2c_token_store(const int64_t *next_token, const uint32_t *done, int64_t *generated_tokens,
+                    uint32_t *generated_length, uint32_t *stopped, int64_t B, int64_t G, int32_t token_index,
+                    const int32_t *token_index_dev, int stop_on_eos, void *stream);
+
+/* ------------------------------------------------------------------ norms
+ * y = fp16(x * rsqrt(mean(x^2) + eps) * w); x, y fp16 [rows, cols], w fp32 [cols].
+ * Replaces ExportRmsNormF32WeightProgram / OptimizedQwen3RmsNormMulF16F32Program
+ *   src/models/quantized_qwen3/shaders/rms_norm_f32w_f32.py:21-94
+ *   src/models/optimized_qwen3/shaders/rms_norm_mul_f16_f32.py:22-115
+ */
+int t2c_rms_norm(const void *x, const float *w, void *y, int64_t rows, int64_t cols, float eps, void *stream);
+
+/*
+ * Fused per-head RMSNorm (q_norm / k_norm) + rotate-half RoPE + cache write
+ * for one attention layer, M = B * T tokens:
+ *   q[m, h, :]  <- rope(rmsnorm(q_in[m, h, :]) * q_w)          (h < NH)
+ *   k_cache[b, pos, kh, :] <- rope(rmsnorm(k_in[m, kh, :]) * k_w)
+ *   v_cache[b, pos, kh, :] <- v_in[m, kh, :]
+ * with pos = positions[b] + t, angle_i = pos * inv_freq[i] (fp32, i < D/2; the
+ * caller supplies inv_freq[i] = theta^(-2 i / D) as its model computes it).
+ * Caches are addressed by element strides (batch, position, head) so both
+ * the head-major [B, NK, S, D] and token-major [B, S, NK, D] layouts work.
+ * q_out may alias q_in.  Replaces the q/k-norm + RoPE + cache-write chain
+ *   src/models/optimized_qwen3/shaders/rms_norm_rope_transpose_f16.py:22-146,
+ *   rms_norm_rope_token_f32.py:22, token_major_kv_cache_write_f16_pair.py:20-105,
+ *   src/models/quantized_qwen3/shaders/kv_cache_write_f16.py:22-92, src/torch2vk/runtime/rope_table.py:31-121
+ */
+int t2c_qk_norm_rope_cache(const void *q_in, const void *k_in, const void *v_in, const float *q_w,
+                           const float *k_w, void *q_out, void *k_cache, void *v_cache,
+                           const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t D,
+                           int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride,
+                           const float *inv_freq, float eps, void *stream);
+
+/* ------------------------------------------------------------- attention
+ * Decode attention (one query token per batch row) over a KV cache:
+ * out[b, h, :] = softmax(q[b, h] . K[b, 0..len_b)^T / sqrt(D)) V, GQA
+ * kv head = h / (NH / NK), len_b = positions[b] + 1.  Split-K over cache
+ * positions in `splits` parts (max_len / splits positions each); the partial
+ * (max, sum, acc) go to `workspace` (fp32, B * NH * splits * (D + 2) floats,
+ * caller-provided; unused when splits == 1) and a combine pass writes out.
+ * Replaces ExportSdpaDecodeCacheF16Program / SdpaDecodeCacheWriteF32Program
+ *   src/models/quantized_qwen3/shaders/sdpa_decode_cache_f16.py:22-136
+ *   src/models/optimized_qwen3/shaders/sdpa_decode_cache_write_f32.py:22-171
+ */
+int t2c_attn_decode(const void *q, const void *k_cache, const void *v_cache, void *out,
+                    const int32_t *positions, int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t max_len,
+                    int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride, int64_t splits,
+                    float *workspace, int64_t workspace_floats, void *stream);
+
+/*
+ * Causal prefill attention: q [B, T, NH, D] (token-major), keys/values read
+ * from the caches for positions 0 .. positions[b] + T - 1 (the current chunk
+ * already written by t2c_qk_norm_rope_cache); query t of batch b attends to
+ * cache positions <= positions[b] + t.  out [B, T, NH, D] fp16.
+ * Replaces ExportSdpaProgram (causal)
+ *   src/models/quantized_qwen3/shaders/sdpa_causal_f32.py:22-142
+ */
+int t2c_attn_prefill(const void *q, const void *k_cache, const void *v_cache, void *out,
+                     const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t D,
+                     int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride, void *stream);
+
+/* ---------------------------------------------------------------- misc
+ * Embedding gather: out[i, :] = deq(weight[ids[i], :]) for F16 or Q4_K rows.
+ * Replaces ExportEmbeddingQ4_KProgram
+ *   src/models/quantized_qwen3/shaders/embedding_q4_k_f32.py:25-121
+ */
+int t2c_embedding(int wtype, const void *weight, const int64_t *ids, void *out, int64_t n_ids, int64_t vocab,
+                  int64_t H, void *stream);
+/* y = x + r (fp16, n elements).  Replaces ExportAddF32Program (add_f32*.py). */
+int t2c_add(const void *x, const void *r, void *y, int64_t n, void *stream);
+/* y = fp16(silu(g)) * u (fp16).  Replaces OptimizedQwen3SwiGLUF16Program
+ *   src/models/optimized_qwen3/shaders/swiglu_f16.py:20-80 */
+int t2c_swiglu(const void *g, const void *u, void *y, int64_t n, void *stream);
+
+/*
+ * End-of-step bookkeeping for a captured decode graph: positions[b] += 1 for
+ * b < B and *token_index += 1 (both int32, device memory).  Replaces the
+ * host-side push-constant updates of the reference replay loop
+ *   src/torch2vk/runtime/replay.py:321 (stage_replay_step_inputs) /
+ *   src/models/quantized_qwen3/run.py:357-388
+ */
+int t2c_advance_positions(int32_t *positions, int64_t B, int32_t *token_index, void *stream);
 
 /* ------------------------------------------------------------- quantizers
  * fp32 [R, K] -> packed blocks, bit-exact with the reference quantizer's

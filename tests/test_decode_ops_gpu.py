@@ -1,0 +1,216 @@
+"""GPU parity of the decode-path kernels against plain PyTorch fp32 references.
+
+Tolerances are written per test: fp16 storage of results bounds every
+comparison at a few fp16 ulps of the reference magnitude.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got: torch.Tensor, ref: torch.Tensor, rel: float = 4e-3, abs_: float = 2e-3) -> None:
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    err = (got - ref).abs()
+    bound = rel * ref.abs() + abs_
+    bad = err > bound
+    assert not bool(bad.any()), f"max err {float(err.max())} (bound at worst {float(bound.flatten()[err.argmax()])})"
+
+
+def test_rms_norm():
+    from torch2vk_b200 import kernels
+
+    torch.manual_seed(0)
+    x = torch.randn(37, 1024, device="cuda", dtype=torch.float16) * 3
+    w = torch.rand(1024, device="cuda") + 0.5
+    y = kernels.rms_norm(x, w, 1e-6)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    _close(y, ref)
+
+
+def _rope_ref(x: torch.Tensor, w: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, eps: float) -> torch.Tensor:
+    # x [M, H, D] fp32; pos [M]
+    xn = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+    ang = pos.float()[:, None] * inv_freq[None, :]
+    emb = torch.cat([ang, ang], dim=-1)
+    cos, sin = emb.cos()[:, None, :], emb.sin()[:, None, :]
+    half = x.shape[-1] // 2
+    rot = torch.cat([-xn[..., half:], xn[..., :half]], dim=-1)
+    return xn * cos + rot * sin
+
+
+@pytest.mark.parametrize("layout", ["token_major", "head_major"])
+def test_qk_norm_rope_cache(layout):
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, inv_freq
+
+    torch.manual_seed(1)
+    B, T, NH, NK, D, S = 2, 5, 16, 8, 128, 64
+    cfg = Qwen3Config(hidden=1024, layers=1, heads=NH, kv_heads=NK, head_dim=D, intermediate=3072, vocab=16)
+    freqs = inv_freq(cfg)
+    q = torch.randn(B * T, NH * D, device="cuda", dtype=torch.float16)
+    k = torch.randn(B * T, NK * D, device="cuda", dtype=torch.float16)
+    v = torch.randn(B * T, NK * D, device="cuda", dtype=torch.float16)
+    qw = torch.rand(D, device="cuda") + 0.5
+    kw = torch.rand(D, device="cuda") + 0.5
+    shape = (B, S, NK, D) if layout == "token_major" else (B, NK, S, D)
+    kc = torch.zeros(shape, device="cuda", dtype=torch.float16)
+    vc = torch.zeros(shape, device="cuda", dtype=torch.float16)
+    positions = torch.tensor([3, 40], device="cuda", dtype=torch.int32)
+    qo = kernels.qk_norm_rope_cache(q, k, v, qw, kw, kc, vc, positions, freqs.cuda(), batch=B, tokens=T, n_heads=NH,
+                                    n_kv=NK, head_dim=D, layout=layout)
+    pos = (positions.cpu()[:, None] + torch.arange(T)[None, :]).reshape(-1)
+    ref_q = _rope_ref(q.float().cpu().view(B * T, NH, D), qw.cpu(), pos, freqs, 1e-6)
+    ref_k = _rope_ref(k.float().cpu().view(B * T, NK, D), kw.cpu(), pos, freqs, 1e-6)
+    _close(qo.view(B * T, NH, D), ref_q)
+    kc_t = kc if layout == "token_major" else kc.transpose(1, 2)
+    vc_t = vc if layout == "token_major" else vc.transpose(1, 2)
+    for b in range(B):
+        for t in range(T):
+            p = int(positions[b]) + t
+            _close(kc_t[b, p], ref_k[b * T + t])
+            _close(vc_t[b, p], v.float().cpu().view(B * T, NK, D)[b * T + t], rel=0, abs_=0)
+
+
+def _attn_ref(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, lens: list[int], NH: int, NK: int) -> torch.Tensor:
+    # q [B, NH, D]; caches [B, S, NK, D]
+    B, _, D = q.shape
+    out = torch.empty(B, NH, D)
+    g = NH // NK
+    for b in range(B):
+        kk = kc[b, : lens[b]].float().cpu()  # [L, NK, D]
+        vv = vc[b, : lens[b]].float().cpu()
+        for h in range(NH):
+            s = (kk[:, h // g, :] @ q[b, h].float().cpu()) / math.sqrt(D)
+            p = torch.softmax(s, dim=0)
+            out[b, h] = p @ vv[:, h // g, :]
+    return out
+
+
+@pytest.mark.parametrize("NH,NK", [(16, 8), (32, 8)])
+@pytest.mark.parametrize("splits", [1, 4, 16])
+def test_attn_decode(NH, NK, splits):
+    from torch2vk_b200 import kernels
+
+    torch.manual_seed(2)
+    B, D, S = 3, 128, 700
+    q = torch.randn(B, NH * D, device="cuda", dtype=torch.float16)
+    kc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    vc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    positions = torch.tensor([0, 255, 699], device="cuda", dtype=torch.int32)
+    out = kernels.attn_decode(q, kc, vc, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                              splits=splits)
+    ref = _attn_ref(q.view(B, NH, D), kc, vc, [1, 256, 700], NH, NK)
+    _close(out.view(B, NH, D), ref)
+
+
+def test_attn_prefill():
+    from torch2vk_b200 import kernels
+
+    torch.manual_seed(3)
+    B, T, NH, NK, D, S = 2, 37, 16, 8, 128, 96
+    base = [0, 20]
+    q = torch.randn(B * T, NH * D, device="cuda", dtype=torch.float16)
+    kc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    vc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    positions = torch.tensor(base, device="cuda", dtype=torch.int32)
+    out = kernels.attn_prefill(q, kc, vc, positions, batch=B, tokens=T, n_heads=NH, n_kv=NK, head_dim=D)
+    qq = q.view(B, T, NH, D)
+    ref = torch.empty(B, T, NH, D)
+    for b in range(B):
+        for t in range(T):
+            ref[b, t] = _attn_ref(qq[b, t][None], kc[b:b + 1], vc[b:b + 1], [base[b] + t + 1], NH, NK)[0]
+    _close(out.view(B, T, NH, D), ref)
+
+
+def test_embedding_f16_and_q4k(oracle):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(4)
+    V, H = 300, 512
+    w = (rng.standard_normal((V, H)) * 0.02).astype(np.float32)
+    ids = torch.tensor([0, 299, 17, 17, 150], dtype=torch.int64, device="cuda")
+    emb16 = torch.from_numpy(w.astype(np.float16)).cuda()
+    out = kernels.embedding(emb16, "f16", ids, H, V)
+    assert torch.equal(out.cpu(), emb16.cpu()[ids.cpu()])
+    packed = oracle.quantize(w, "q4_k")
+    out = kernels.embedding(torch.from_numpy(packed).cuda(), "q4_k", ids, H, V)
+    want = oracle.dequantize(packed, "q4_k", H)[ids.cpu().numpy()].astype(np.float16)
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("kind,K", [("q6_k", 1024), ("q6_k", 4096), ("q4_k", 1024)])
+def test_lm_head_argmax_and_select(oracle, kind, K):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(5)
+    N, M = 4096 + 16, 2
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    w[777] = w[123]          # an exact duplicate row: tie -> lower id
+    packed = oracle.quantize(w, kind)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    x[1] = x[0]
+    logits = oracle.matvec(packed, kind, x)
+    xg = torch.from_numpy(x).cuda()
+    ps, pt = kernels.lm_head_argmax(xg, torch.from_numpy(packed).cuda(), kind, K)
+    assert ps.shape == (M, (N + 3) // 4)
+    ps_c, pt_c = ps.cpu().numpy(), pt.cpu().numpy()
+    for m in range(M):
+        for g in range(ps_c.shape[1]):
+            rows = logits[m, 4 * g:4 * g + 4]
+            assert pt_c[m, g] == 4 * g + int(np.argmax(rows)) or abs(float(rows.max()) - float(ps_c[m, g])) < 1e-3
+        assert abs(float(ps_c[m].max()) - float(logits[m].max())) <= 2e-3 * (abs(float(logits[m].max())) + 1)
+    eos = torch.tensor([int(pt_c[0, np.argmax(ps_c[0])]), 5], dtype=torch.int64, device="cuda")
+    nxt, done = kernels.token_select(ps, pt, eos)
+    assert int(nxt[0]) == int(np.argmax(logits[0])) or logits[0].max() - np.sort(logits[0])[-2] < 1e-3
+    assert int(nxt[0]) == int(nxt[1]) and int(done[0]) == 1 and int(done[1]) == 1
+
+
+def test_token_select_tie_breaks_to_lower_id():
+    from torch2vk_b200 import kernels
+
+    G = 5000
+    ps = torch.full((1, G), -1.0, device="cuda")
+    pt = torch.arange(G, dtype=torch.int32, device="cuda")[None].contiguous()
+    ps[0, 4321] = 3.0
+    ps[0, 1234] = 3.0
+    nxt, done = kernels.token_select(ps, pt, torch.tensor([-1], dtype=torch.int64, device="cuda"))
+    assert int(nxt[0]) == 1234 and int(done[0]) == 0
+
+
+def test_token_store_and_advance():
+    from torch2vk_b200 import kernels
+
+    B, G = 2, 4
+    gen = torch.zeros(B, G, dtype=torch.int64, device="cuda")
+    length = torch.zeros(B, dtype=torch.int32, device="cuda")
+    stopped = torch.zeros(B, dtype=torch.int32, device="cuda")
+    idx = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([7, 9], dtype=torch.int32, device="cuda")
+    seq = [([11, 21], [0, 0]), ([12, 22], [1, 0]), ([13, 23], [0, 0]), ([14, 24], [0, 0]), ([15, 25], [0, 0])]
+    for toks, dn in seq:
+        kernels.token_store(torch.tensor(toks, device="cuda"), torch.tensor(dn, dtype=torch.int32, device="cuda"),
+                            gen, length, stopped, token_index_dev=idx, stop_on_eos=True)
+        kernels.advance_positions(pos, idx)
+    assert gen.cpu().tolist() == [[11, 12, 0, 0], [21, 22, 23, 24]]
+    assert length.cpu().tolist() == [2, 4] and stopped.cpu().tolist() == [1, 0]
+    assert pos.cpu().tolist() == [12, 14] and int(idx[0]) == 5
+
+
+def test_elementwise_add_swiglu():
+    from torch2vk_b200 import kernels
+
+    torch.manual_seed(6)
+    a = torch.randn(1027, device="cuda", dtype=torch.float16)
+    b = torch.randn(1027, device="cuda", dtype=torch.float16)
+    _close(kernels.add(a, b), a.float() + b.float())
+    silu = (a.float() / (1 + torch.exp(-a.float()))).half().float()
+    _close(kernels.swiglu(a, b), silu * b.float())

@@ -38,6 +38,20 @@ _SIGNATURES: dict[str, list] = {
     "t2c_linear_swiglu": [_i32, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _vp],
     "t2c_quantize": [_i32, _vp, _vp, _i64, _i64, _vp],
     "t2c_dequantize": [_i32, _vp, _vp, _i64, _i64, _vp],
+    "t2c_device_status": [_vp, _i32, _vp],
+    "t2c_lm_head_argmax": [_i32, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _vp],
+    "t2c_token_select": [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp],
+    "t2c_token_store": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _c.c_int32, _vp, _i32, _vp],
+    "t2c_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _vp],
+    "t2c_qk_norm_rope_cache": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                               _i64, _i64, _i64, _vp, _f32, _vp],
+    "t2c_attn_decode": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                        _i64, _vp],
+    "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "t2c_embedding": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "t2c_add": [_vp, _vp, _vp, _i64, _vp],
+    "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],
+    "t2c_advance_positions": [_vp, _i64, _vp, _vp],
 }
 _RESTYPES = {"t2c_last_error": _c.c_char_p}
 

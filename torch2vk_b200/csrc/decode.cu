@@ -1,0 +1,726 @@
+// Decode-step kernels around the quantized linears: RMSNorm, fused q/k-norm +
+// RoPE + KV-cache write, split-K decode attention, causal prefill attention,
+// embedding gather, elementwise add / SwiGLU, and the greedy token select /
+// store pair.  fp16 storage, fp32 arithmetic throughout.
+#include <float.h>
+
+#include "common.cuh"
+
+namespace t2c {
+namespace {
+
+__device__ __forceinline__ float4 h4_to_f4(uint2 v) {
+    const __half2 a = *reinterpret_cast<const __half2 *>(&v.x);
+    const __half2 b = *reinterpret_cast<const __half2 *>(&v.y);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+__device__ __forceinline__ uint2 f4_to_h4(float4 f) {
+    const __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+    return make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// One warp per row; lanes stride the row in 8-value chunks.
+__global__ void rms_norm_kernel(const __half *__restrict__ x, const float *__restrict__ w, __half *__restrict__ y,
+                                int64_t rows, int cols, float eps) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    pdl_wait();
+    const __half *xr = x + row * cols;
+    float ss = 0.0f;
+    for (int c = lane * 4; c < cols; c += 128) {
+        const float4 v = h4_to_f4(*reinterpret_cast<const uint2 *>(xr + c));
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+    __half *yr = y + row * cols;
+    for (int c = lane * 4; c < cols; c += 128) {
+        float4 v = h4_to_f4(*reinterpret_cast<const uint2 *>(xr + c));
+        const float4 g = *reinterpret_cast<const float4 *>(w + c);
+        v = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+        *reinterpret_cast<uint2 *>(yr + c) = f4_to_h4(v);
+    }
+}
+
+// ------------------------------------------------ q/k norm + RoPE + cache
+// One warp per (token, head) vector of D values (D/32 per lane, D <= 256).
+// Heads [0, NH): q; [NH, NH+NK): k (norm + rope -> k cache); [NH+NK, NH+2NK): v copy.
+// Rotate-half partners d and d +- D/2 sit on lanes l and l ^ 16.
+template <int E>
+__global__ void qk_norm_rope_cache_kernel(const __half *__restrict__ q_in, const __half *__restrict__ k_in,
+                                          const __half *__restrict__ v_in, const float *__restrict__ q_w,
+                                          const float *__restrict__ k_w, __half *q_out, __half *__restrict__ k_cache,
+                                          __half *__restrict__ v_cache, const int32_t *__restrict__ positions,
+                                          int B, int T, int NH, int NK, int64_t cb, int64_t cs, int64_t ch,
+                                          const float *__restrict__ inv_freq, float eps) {
+    constexpr int D = E * 32;
+    const int64_t vec = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int heads = NH + 2 * NK;
+    const int64_t total = static_cast<int64_t>(B) * T * heads;
+    if (vec >= total) return;
+    pdl_wait();
+    const int64_t m = vec / heads;
+    const int h = static_cast<int>(vec - m * heads);
+    const int b = static_cast<int>(m / T), t = static_cast<int>(m - static_cast<int64_t>(b) * T);
+    const int pos = positions[b] + t;
+    const int d0 = lane * E;
+    float v[E];
+    const __half *src;
+    if (h < NH) {
+        src = q_in + (m * NH + h) * D;
+    } else if (h < NH + NK) {
+        src = k_in + (m * NK + (h - NH)) * D;
+    } else {
+        src = v_in + (m * NK + (h - NH - NK)) * D;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = __half2float(src[d0 + e]);
+    if (h >= NH + NK) {
+        __half *dst = v_cache + b * cb + static_cast<int64_t>(pos) * cs + (h - NH - NK) * ch;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dst[d0 + e] = __float2half_rn(v[e]);
+        return;
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += v[e] * v[e];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / static_cast<float>(D) + eps);
+    const float *w = h < NH ? q_w : k_w;
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = v[e] * inv * w[d0 + e];
+    float out[E];
+    const bool first_half = lane < 16;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        const int i = (d0 + e) & (D / 2 - 1);
+        float sn, cs_;
+        sincosf(static_cast<float>(pos) * inv_freq[i], &sn, &cs_);
+        out[e] = first_half ? v[e] * cs_ - partner * sn : v[e] * cs_ + partner * sn;
+    }
+    __half *dst;
+    if (h < NH) {
+        dst = q_out + (m * NH + h) * D;
+    } else {
+        dst = k_cache + b * cb + static_cast<int64_t>(pos) * cs + (h - NH) * ch;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[d0 + e] = __float2half_rn(out[e]);
+}
+
+// ------------------------------------------------------- decode attention
+// CTA = 4 warps on (batch b, kv head kh, split sp): cache positions
+// [sp * chunk, min((sp+1) * chunk, len_b)).  The G = NH / NK query heads of
+// the group share every K/V load.  Scores: lane j of a warp owns position j
+// of a 32-position tile (full D-length dot products, q from shared memory);
+// values: lanes split D.  Each warp keeps an online softmax (max, sum, acc);
+// the four warps merge in shared memory and write either the final output
+// (one split) or the split's partial (max, sum, acc) to the workspace.
+constexpr int kAttnWarps = 4;
+constexpr int kMaxGroup = 8;
+
+template <int E, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
+    const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
+    __half *__restrict__ out, const int32_t *__restrict__ positions, int NH, int NK, int64_t cb, int64_t cs,
+    int64_t ch, int chunk, int splits, float *__restrict__ ws, float scale) {
+    constexpr int D = E * 32;
+    __shared__ float qs[G][D];
+    __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+    __shared__ float wacc[kAttnWarps][G][D];
+    const int sp = blockIdx.x % splits;
+    const int kh = (blockIdx.x / splits) % NK;
+    const int b = blockIdx.x / (splits * NK);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    const int len = positions[b] + 1;
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i - g * D;
+        qs[g][d] = __half2float(q[(static_cast<int64_t>(b) * NH + kh * G + g) * D + d]) * scale;
+    }
+    __syncthreads();
+    const int p0 = sp * chunk;
+    const int p1 = min(len, p0 + chunk);
+    float m_run[G], l_run[G], acc[G][E];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m_run[g] = -FLT_MAX;
+        l_run[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
+    }
+    const __half *kbase = kc + b * cb + kh * ch;
+    const __half *vbase = vc + b * cb + kh * ch;
+    for (int t0 = p0 + warp * 32; t0 < p1; t0 += kAttnWarps * 32) {
+        const int pos = t0 + lane;
+        const bool valid = pos < p1;
+        float s[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[g] = 0.0f;
+        if (valid) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kbase + static_cast<int64_t>(pos) * cs);
+#pragma unroll 4
+            for (int c = 0; c < D / 8; ++c) {
+                const uint4 raw = kr[c];
+                const float4 lo = h4_to_f4(make_uint2(raw.x, raw.y));
+                const float4 hi = h4_to_f4(make_uint2(raw.z, raw.w));
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float *qq = &qs[g][c * 8];
+                    s[g] += lo.x * qq[0] + lo.y * qq[1] + lo.z * qq[2] + lo.w * qq[3] + hi.x * qq[4] + hi.y * qq[5] +
+                            hi.z * qq[6] + hi.w * qq[7];
+                }
+            }
+        }
+        float p[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float sv = valid ? s[g] : -FLT_MAX;
+            const float tile_max = warp_max(sv);
+            const float m_new = fmaxf(m_run[g], tile_max);
+            const float corr = __expf(m_run[g] - m_new);
+            p[g] = valid ? __expf(sv - m_new) : 0.0f;
+            l_run[g] = l_run[g] * corr + warp_sum(p[g]);
+            m_run[g] = m_new;
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[g][e] *= corr;
+        }
+        const int n_valid = min(32, p1 - t0);
+        for (int j = 0; j < n_valid; ++j) {
+            const __half *vr = vbase + static_cast<int64_t>(t0 + j) * cs + lane * E;
+            float vv[E];
+            if constexpr (E == 4) {
+                const float4 f = h4_to_f4(*reinterpret_cast<const uint2 *>(vr));
+                vv[0] = f.x;
+                vv[1] = f.y;
+                vv[2] = f.z;
+                vv[3] = f.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) vv[e] = __half2float(vr[e]);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pj = __shfl_sync(0xffffffffu, p[g], j);
+#pragma unroll
+                for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pj, vv[e], acc[g][e]);
+            }
+        }
+    }
+    // merge the warps
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m_run[g];
+            wl[warp][g] = l_run[g];
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) wacc[warp][g][lane * E + e] = acc[g][e];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i - g * D;
+        float mx = -FLT_MAX;
+        for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w][g]);
+        float l = 0.0f, a = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = wm[w][g] == -FLT_MAX ? 0.0f : __expf(wm[w][g] - mx);
+            l += wl[w][g] * f;
+            a += wacc[w][g][d] * f;
+        }
+        const int h = kh * G + g;
+        if (splits == 1) {
+            out[(static_cast<int64_t>(b) * NH + h) * D + d] = __float2half_rn(l > 0.0f ? a / l : 0.0f);
+        } else {
+            float *rec = ws + ((static_cast<int64_t>(b) * NH + h) * splits + sp) * (D + 2);
+            rec[2 + d] = a;
+            if (d == 0) {
+                rec[0] = mx;
+                rec[1] = l;
+            }
+        }
+    }
+}
+
+template <int E>
+__global__ void attn_combine_kernel(const float *__restrict__ ws, __half *__restrict__ out, int B, int NH, int splits) {
+    constexpr int D = E * 32;
+    const int64_t bh = blockIdx.x;  // b * NH + h
+    if (bh >= static_cast<int64_t>(B) * NH) return;
+    const float *rec = ws + bh * splits * (D + 2);
+    float mx = -FLT_MAX;
+    for (int s = 0; s < splits; ++s) mx = fmaxf(mx, rec[s * (D + 2)]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float l = 0.0f, a = 0.0f;
+        for (int s = 0; s < splits; ++s) {
+            const float m = rec[s * (D + 2)];
+            const float f = m == -FLT_MAX ? 0.0f : __expf(m - mx);
+            l += rec[s * (D + 2) + 1] * f;
+            a += rec[s * (D + 2) + 2 + d] * f;
+        }
+        out[bh * D + d] = __float2half_rn(l > 0.0f ? a / l : 0.0f);
+    }
+}
+
+// ------------------------------------------------------ prefill attention
+// CTA = 4 warps on (b, head h, 16-query tile).  Keys are processed in tiles
+// of 32: warp w owns queries 4w..4w+3 of the tile; lane j scores key j of the
+// key tile against those queries (q from shared memory), then lanes split D
+// to accumulate P V with the probabilities broadcast by shuffles.
+constexpr int kPfQ = 16;
+
+template <int E>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *__restrict__ q, const __half *__restrict__ kc,
+                                                           const __half *__restrict__ vc, __half *__restrict__ out,
+                                                           const int32_t *__restrict__ positions, int T, int NH,
+                                                           int NK, int64_t cb, int64_t cs, int64_t ch, float scale) {
+    constexpr int D = E * 32;
+    constexpr int QW = kPfQ / 4;  // queries per warp
+    __shared__ float qs[kPfQ][D];
+    const int qtiles = (T + kPfQ - 1) / kPfQ;
+    const int qt = blockIdx.x % qtiles;
+    const int h = (blockIdx.x / qtiles) % NH;
+    const int b = blockIdx.x / (qtiles * NH);
+    const int kh = h / (NH / NK);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    const int base = positions[b];
+    for (int i = threadIdx.x; i < kPfQ * D; i += blockDim.x) {
+        const int qi = i / D, d = i - qi * D;
+        const int t = qt * kPfQ + qi;
+        qs[qi][d] = t < T ? __half2float(q[((static_cast<int64_t>(b) * T + t) * NH + h) * D + d]) * scale : 0.0f;
+    }
+    __syncthreads();
+    float m_run[QW], l_run[QW], acc[QW][E];
+#pragma unroll
+    for (int i = 0; i < QW; ++i) {
+        m_run[i] = -FLT_MAX;
+        l_run[i] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[i][e] = 0.0f;
+    }
+    const int q_first = qt * kPfQ + warp * QW;           // chunk-local index of this warp's first query
+    const int last_key = base + min(T - 1, q_first + QW - 1);  // keys 0..last_key are visible to some query
+    const __half *kbase = kc + b * cb + kh * ch;
+    const __half *vbase = vc + b * cb + kh * ch;
+    if (q_first < T) {
+        for (int k0 = 0; k0 <= last_key; k0 += 32) {
+            const int key = k0 + lane;
+            float s[QW];
+#pragma unroll
+            for (int i = 0; i < QW; ++i) s[i] = 0.0f;
+            if (key <= last_key) {
+                const uint4 *kr = reinterpret_cast<const uint4 *>(kbase + static_cast<int64_t>(key) * cs);
+#pragma unroll 4
+                for (int c = 0; c < D / 8; ++c) {
+                    const uint4 raw = kr[c];
+                    const float4 lo = h4_to_f4(make_uint2(raw.x, raw.y));
+                    const float4 hi = h4_to_f4(make_uint2(raw.z, raw.w));
+#pragma unroll
+                    for (int i = 0; i < QW; ++i) {
+                        const float *qq = &qs[warp * QW + i][c * 8];
+                        s[i] += lo.x * qq[0] + lo.y * qq[1] + lo.z * qq[2] + lo.w * qq[3] + hi.x * qq[4] +
+                                hi.y * qq[5] + hi.z * qq[6] + hi.w * qq[7];
+                    }
+                }
+            }
+            float p[QW];
+#pragma unroll
+            for (int i = 0; i < QW; ++i) {
+                const bool vis = key <= base + q_first + i && q_first + i < T;
+                const float sv = vis ? s[i] : -FLT_MAX;
+                const float tmax = warp_max(sv);
+                const float m_new = fmaxf(m_run[i], tmax);
+                const float corr = m_run[i] == -FLT_MAX ? 0.0f : __expf(m_run[i] - m_new);
+                p[i] = vis ? __expf(sv - m_new) : 0.0f;
+                l_run[i] = l_run[i] * corr + warp_sum(p[i]);
+                m_run[i] = m_new;
+#pragma unroll
+                for (int e = 0; e < E; ++e) acc[i][e] *= corr;
+            }
+            const int n_keys = min(32, last_key - k0 + 1);
+            for (int j = 0; j < n_keys; ++j) {
+                const __half *vr = vbase + static_cast<int64_t>(k0 + j) * cs + lane * E;
+                float vv[E];
+#pragma unroll
+                for (int e = 0; e < E; ++e) vv[e] = __half2float(vr[e]);
+#pragma unroll
+                for (int i = 0; i < QW; ++i) {
+                    const float pj = __shfl_sync(0xffffffffu, p[i], j);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc[i][e] = fmaf(pj, vv[e], acc[i][e]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < QW; ++i) {
+            const int t = q_first + i;
+            if (t >= T) continue;
+            __half *o = out + ((static_cast<int64_t>(b) * T + t) * NH + h) * D + lane * E;
+            const float invl = l_run[i] > 0.0f ? 1.0f / l_run[i] : 0.0f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) o[e] = __float2half_rn(acc[i][e] * invl);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- misc
+__global__ void embedding_f16_kernel(const __half *__restrict__ w, const int64_t *__restrict__ ids,
+                                     __half *__restrict__ out, int64_t n_ids, int64_t vocab, int H) {
+    const int64_t row = blockIdx.x;
+    if (row >= n_ids) return;
+    pdl_wait();
+    int64_t id = ids[row];
+    if (id < 0 || id >= vocab) {
+        report_device_error(T2C_EINVAL);
+        id = 0;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(w + id * H);
+    uint4 *dst = reinterpret_cast<uint4 *>(out + row * H);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+// Q4_K row decode (embedding_q4_k_f32.py:96-110): w = (d * sc) * q - dmin * m.
+__global__ void embedding_q4k_kernel(const uint8_t *__restrict__ w, const int64_t *__restrict__ ids,
+                                     __half *__restrict__ out, int64_t n_ids, int64_t vocab, int H) {
+    const int64_t row = blockIdx.x;
+    if (row >= n_ids) return;
+    pdl_wait();
+    int64_t id = ids[row];
+    if (id < 0 || id >= vocab) {
+        report_device_error(T2C_EINVAL);
+        id = 0;
+    }
+    const uint8_t *src = w + id * (H / 256) * 144;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+        const uint8_t *blk = src + (k >> 8) * 144;
+        const int i = k & 255, j = i >> 5;
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+        const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[2] | (blk[3] << 8))));
+        uint32_t sc, m;
+        if (j < 4) {
+            sc = blk[4 + j] & 63u;
+            m = blk[8 + j] & 63u;
+        } else {
+            sc = (blk[8 + j] & 15u) | ((blk[j] >> 6) << 4);
+            m = (blk[8 + j] >> 4) | ((blk[4 + j] >> 6) << 4);
+        }
+        const uint8_t byte = blk[16 + (i >> 6) * 32 + (i & 31)];
+        const uint32_t qv = (i & 32) ? (byte >> 4) : (byte & 15u);
+        out[row * H + k] = __float2half_rn((d * static_cast<float>(sc)) * static_cast<float>(qv) - dmin * static_cast<float>(m));
+    }
+}
+
+__global__ void add_kernel(const __half *__restrict__ x, const __half *__restrict__ r, __half *__restrict__ y, int64_t n) {
+    pdl_wait();
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 a = h4_to_f4(*reinterpret_cast<const uint2 *>(x + i));
+        const float4 c = h4_to_f4(*reinterpret_cast<const uint2 *>(r + i));
+        *reinterpret_cast<uint2 *>(y + i) = f4_to_h4(make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w));
+    } else {
+        for (int64_t j = i; j < n; ++j) y[j] = __float2half_rn(__half2float(x[j]) + __half2float(r[j]));
+    }
+}
+
+__device__ __forceinline__ float silu_h(float g) { return __half2float(__float2half_rn(g / (1.0f + __expf(-g)))); }
+
+__global__ void swiglu_kernel(const __half *__restrict__ g, const __half *__restrict__ u, __half *__restrict__ y, int64_t n) {
+    pdl_wait();
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 a = h4_to_f4(*reinterpret_cast<const uint2 *>(g + i));
+        const float4 c = h4_to_f4(*reinterpret_cast<const uint2 *>(u + i));
+        *reinterpret_cast<uint2 *>(y + i) =
+            f4_to_h4(make_float4(silu_h(a.x) * c.x, silu_h(a.y) * c.y, silu_h(a.z) * c.z, silu_h(a.w) * c.w));
+    } else {
+        for (int64_t j = i; j < n; ++j) y[j] = __float2half_rn(silu_h(__half2float(g[j])) * __half2float(u[j]));
+    }
+}
+
+// ------------------------------------------------------------ greedy select
+__device__ __forceinline__ bool better(float s, uint32_t t, float bs, uint32_t bt) {
+    return s > bs || (s == bs && t < bt);
+}
+
+__global__ void __launch_bounds__(1024) token_select_kernel(const float *__restrict__ ps, const uint32_t *__restrict__ pt,
+                                                            int64_t G, const int64_t *__restrict__ eos, int64_t E,
+                                                            int64_t *__restrict__ next_token, uint32_t *__restrict__ done) {
+    __shared__ float ss[32];
+    __shared__ uint32_t st[32];
+    const int64_t m = blockIdx.x;
+    pdl_wait();
+    float best = -FLT_MAX;
+    uint32_t tok = 0xffffffffu;
+    for (int64_t g = threadIdx.x; g < G; g += blockDim.x) {
+        const float s = ps[m * G + g];
+        const uint32_t t = pt[m * G + g];
+        if (better(s, t, best, tok)) {
+            best = s;
+            tok = t;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float s = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t t = __shfl_xor_sync(0xffffffffu, tok, o);
+        if (better(s, t, best, tok)) {
+            best = s;
+            tok = t;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        ss[warp] = best;
+        st[warp] = tok;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int nw = blockDim.x >> 5;
+        for (int w = 1; w < nw; ++w)
+            if (better(ss[w], st[w], best, tok)) {
+                best = ss[w];
+                tok = st[w];
+            }
+        next_token[m] = static_cast<int64_t>(tok);
+        uint32_t is_done = 0;
+        for (int64_t e = 0; e < E; ++e)
+            if (static_cast<int64_t>(tok) == eos[e]) is_done = 1;
+        done[m] = is_done;
+    }
+}
+
+__global__ void token_store_kernel(const int64_t *__restrict__ next_token, const uint32_t *__restrict__ done,
+                                   int64_t *__restrict__ gen, uint32_t *__restrict__ gen_len, uint32_t *__restrict__ stopped,
+                                   int64_t B, int64_t G, int32_t index_value, const int32_t *__restrict__ index_dev,
+                                   int stop_on_eos) {
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    pdl_wait();
+    const int64_t index = index_dev ? index_dev[0] : index_value;
+    if (index < 0 || index >= G) return;
+    if (stop_on_eos && stopped[b]) return;
+    gen[b * G + index] = next_token[b];
+    gen_len[b] = static_cast<uint32_t>(index + 1);
+    if (stop_on_eos && done[b]) stopped[b] = 1u;
+}
+
+__global__ void advance_kernel(int32_t *positions, int64_t B, int32_t *token_index) {
+    pdl_wait();
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b < B) positions[b] += 1;
+    if (b == 0 && token_index) token_index[0] += 1;
+}
+
+template <typename Kernel, typename... Args>
+int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args...);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "launch: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+cudaError_t status_decode(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
+
+}  // namespace t2c
+
+using namespace t2c;
+
+extern "C" int t2c_rms_norm(const void *x, const float *w, void *y, int64_t rows, int64_t cols, float eps, void *stream) {
+    if (!x || !w || !y) return set_error(T2C_EINVAL, "rms_norm: NULL pointer");
+    if (rows <= 0 || cols <= 0 || cols % 4) return set_error(T2C_EINVAL, "rms_norm: cols must be a positive multiple of 4");
+    if (!aligned(x, 8) || !aligned(y, 8) || !aligned(w, 16)) return set_error(T2C_EINVAL, "rms_norm: misaligned operand");
+    const int warps = 8;
+    return launch(rms_norm_kernel, dim3(static_cast<unsigned>((rows + warps - 1) / warps)), dim3(warps * 32), 0,
+                  as_stream(stream), static_cast<const __half *>(x), w, static_cast<__half *>(y), rows,
+                  static_cast<int>(cols), eps);
+}
+
+extern "C" int t2c_qk_norm_rope_cache(const void *q_in, const void *k_in, const void *v_in, const float *q_w,
+                                      const float *k_w, void *q_out, void *k_cache, void *v_cache,
+                                      const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK,
+                                      int64_t D, int64_t cb, int64_t cs, int64_t ch, const float *inv_freq, float eps,
+                                      void *stream) {
+    if (!q_in || !k_in || !v_in || !q_w || !k_w || !q_out || !k_cache || !v_cache || !positions || !inv_freq)
+        return set_error(T2C_EINVAL, "qk_norm_rope_cache: NULL pointer");
+    if (B <= 0 || T <= 0 || NH <= 0 || NK <= 0 || NH % NK) return set_error(T2C_EINVAL, "qk_norm_rope_cache: bad heads");
+    const int64_t vecs = B * T * (NH + 2 * NK);
+    const int warps = 8;
+    const dim3 grid(static_cast<unsigned>((vecs + warps - 1) / warps)), block(warps * 32);
+    const cudaStream_t s = as_stream(stream);
+#define T2C_QKR(E)                                                                                                   \
+    return launch(qk_norm_rope_cache_kernel<E>, grid, block, 0, s, static_cast<const __half *>(q_in),                  \
+                  static_cast<const __half *>(k_in), static_cast<const __half *>(v_in), q_w, k_w,                     \
+                  static_cast<__half *>(q_out), static_cast<__half *>(k_cache), static_cast<__half *>(v_cache),       \
+                  positions, static_cast<int>(B), static_cast<int>(T), static_cast<int>(NH), static_cast<int>(NK),    \
+                  cb, cs, ch, inv_freq, eps)
+    switch (D) {
+        case 64: T2C_QKR(2);
+        case 128: T2C_QKR(4);
+        case 256: T2C_QKR(8);
+        default: return set_error(T2C_EUNSUPPORTED, "qk_norm_rope_cache: D=%lld", (long long)D);
+    }
+#undef T2C_QKR
+}
+
+extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v_cache, void *out,
+                               const int32_t *positions, int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t max_len,
+                               int64_t cb, int64_t cs, int64_t ch, int64_t splits, float *workspace,
+                               int64_t workspace_floats, void *stream) {
+    if (!q || !k_cache || !v_cache || !out || !positions) return set_error(T2C_EINVAL, "attn_decode: NULL pointer");
+    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || max_len <= 0 || splits <= 0)
+        return set_error(T2C_EINVAL, "attn_decode: bad shape");
+    const int G = static_cast<int>(NH / NK);
+    if (G > kMaxGroup) return set_error(T2C_EUNSUPPORTED, "attn_decode: group %d > %d", G, kMaxGroup);
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cs % 8 || cb % 8 || ch % 8)
+        return set_error(T2C_EINVAL, "attn_decode: cache rows must be 16-byte aligned");
+    if (splits > 1) {
+        const int64_t need = B * NH * splits * (D + 2);
+        if (!workspace || workspace_floats < need)
+            return set_error(T2C_ESCRATCH, "attn_decode: workspace needs %lld floats", (long long)need);
+    }
+    const int chunk = static_cast<int>((max_len + splits - 1) / splits);
+    const float scale = 1.0f / sqrtf(static_cast<float>(D));
+    const cudaStream_t s = as_stream(stream);
+    const dim3 grid(static_cast<unsigned>(B * NK * splits)), block(kAttnWarps * 32);
+    int rc = T2C_OK;
+#define T2C_ATT(E, GG)                                                                                           \
+    rc = launch(attn_decode_kernel<E, GG>, grid, block, 0, s, static_cast<const __half *>(q),                      \
+                static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache), static_cast<__half *>(out), \
+                positions, static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, chunk, static_cast<int>(splits),  \
+                workspace, scale)
+    if (D == 128) {
+        switch (G) {
+            case 1: T2C_ATT(4, 1); break;
+            case 2: T2C_ATT(4, 2); break;
+            case 4: T2C_ATT(4, 4); break;
+            case 8: T2C_ATT(4, 8); break;
+            default: return set_error(T2C_EUNSUPPORTED, "attn_decode: group %d", G);
+        }
+    } else if (D == 64) {
+        switch (G) {
+            case 1: T2C_ATT(2, 1); break;
+            case 2: T2C_ATT(2, 2); break;
+            case 4: T2C_ATT(2, 4); break;
+            case 8: T2C_ATT(2, 8); break;
+            default: return set_error(T2C_EUNSUPPORTED, "attn_decode: group %d", G);
+        }
+    } else {
+        return set_error(T2C_EUNSUPPORTED, "attn_decode: D=%lld", (long long)D);
+    }
+#undef T2C_ATT
+    if (rc != T2C_OK || splits == 1) return rc;
+    if (D == 128)
+        return launch(attn_combine_kernel<4>, dim3(static_cast<unsigned>(B * NH)), dim3(128), 0, s,
+                      static_cast<const float *>(workspace), static_cast<__half *>(out), static_cast<int>(B),
+                      static_cast<int>(NH), static_cast<int>(splits));
+    return launch(attn_combine_kernel<2>, dim3(static_cast<unsigned>(B * NH)), dim3(64), 0, s,
+                  static_cast<const float *>(workspace), static_cast<__half *>(out), static_cast<int>(B),
+                  static_cast<int>(NH), static_cast<int>(splits));
+}
+
+extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *v_cache, void *out,
+                                const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t D,
+                                int64_t cb, int64_t cs, int64_t ch, void *stream) {
+    if (!q || !k_cache || !v_cache || !out || !positions) return set_error(T2C_EINVAL, "attn_prefill: NULL pointer");
+    if (B <= 0 || T <= 0 || NH <= 0 || NK <= 0 || NH % NK) return set_error(T2C_EINVAL, "attn_prefill: bad shape");
+    if (!aligned(k_cache, 16) || cs % 8 || cb % 8 || ch % 8)
+        return set_error(T2C_EINVAL, "attn_prefill: cache rows must be 16-byte aligned");
+    const float scale = 1.0f / sqrtf(static_cast<float>(D));
+    const int64_t qtiles = (T + kPfQ - 1) / kPfQ;
+    const dim3 grid(static_cast<unsigned>(B * NH * qtiles)), block(128);
+    const cudaStream_t s = as_stream(stream);
+    if (D == 128)
+        return launch(attn_prefill_kernel<4>, grid, block, 0, s, static_cast<const __half *>(q),
+                      static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache),
+                      static_cast<__half *>(out), positions, static_cast<int>(T), static_cast<int>(NH),
+                      static_cast<int>(NK), cb, cs, ch, scale);
+    if (D == 64)
+        return launch(attn_prefill_kernel<2>, grid, block, 0, s, static_cast<const __half *>(q),
+                      static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache),
+                      static_cast<__half *>(out), positions, static_cast<int>(T), static_cast<int>(NH),
+                      static_cast<int>(NK), cb, cs, ch, scale);
+    return set_error(T2C_EUNSUPPORTED, "attn_prefill: D=%lld", (long long)D);
+}
+
+extern "C" int t2c_embedding(int wtype, const void *weight, const int64_t *ids, void *out, int64_t n_ids,
+                             int64_t vocab, int64_t H, void *stream) {
+    if (!weight || !ids || !out) return set_error(T2C_EINVAL, "embedding: NULL pointer");
+    if (n_ids <= 0 || vocab <= 0 || H <= 0) return set_error(T2C_EINVAL, "embedding: bad shape");
+    const cudaStream_t s = as_stream(stream);
+    if (wtype == T2C_F16) {
+        if (H % 8 || !aligned(weight, 16) || !aligned(out, 16)) return set_error(T2C_EINVAL, "embedding: alignment");
+        return launch(embedding_f16_kernel, dim3(static_cast<unsigned>(n_ids)), dim3(128), 0, s,
+                      static_cast<const __half *>(weight), ids, static_cast<__half *>(out), n_ids, vocab,
+                      static_cast<int>(H));
+    }
+    if (wtype == T2C_Q4_K) {
+        if (H % 256) return set_error(T2C_EINVAL, "embedding: Q4_K needs H %% 256 == 0");
+        return launch(embedding_q4k_kernel, dim3(static_cast<unsigned>(n_ids)), dim3(256), 0, s,
+                      static_cast<const uint8_t *>(weight), ids, static_cast<__half *>(out), n_ids, vocab,
+                      static_cast<int>(H));
+    }
+    return set_error(T2C_EUNSUPPORTED, "embedding: weight type %d", wtype);
+}
+
+extern "C" int t2c_add(const void *x, const void *r, void *y, int64_t n, void *stream) {
+    if (!x || !r || !y || n < 0) return set_error(T2C_EINVAL, "add: bad argument");
+    if (n == 0) return T2C_OK;
+    if (!aligned(x, 8) || !aligned(r, 8) || !aligned(y, 8)) return set_error(T2C_EINVAL, "add: misaligned");
+    const int64_t threads = (n + 3) / 4;
+    return launch(add_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, as_stream(stream),
+                  static_cast<const __half *>(x), static_cast<const __half *>(r), static_cast<__half *>(y), n);
+}
+
+extern "C" int t2c_swiglu(const void *g, const void *u, void *y, int64_t n, void *stream) {
+    if (!g || !u || !y || n < 0) return set_error(T2C_EINVAL, "swiglu: bad argument");
+    if (n == 0) return T2C_OK;
+    if (!aligned(g, 8) || !aligned(u, 8) || !aligned(y, 8)) return set_error(T2C_EINVAL, "swiglu: misaligned");
+    const int64_t threads = (n + 3) / 4;
+    return launch(swiglu_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, as_stream(stream),
+                  static_cast<const __half *>(g), static_cast<const __half *>(u), static_cast<__half *>(y), n);
+}
+
+extern "C" int t2c_token_select(const float *partial_scores, const uint32_t *partial_tokens, int64_t M, int64_t G,
+                                const int64_t *eos_ids, int64_t E, int64_t *next_token, uint32_t *done, void *stream) {
+    if (!partial_scores || !partial_tokens || !next_token || !done || (E > 0 && !eos_ids))
+        return set_error(T2C_EINVAL, "token_select: NULL pointer");
+    if (M <= 0 || G <= 0 || E < 0) return set_error(T2C_EINVAL, "token_select: bad shape");
+    return launch(token_select_kernel, dim3(static_cast<unsigned>(M)), dim3(1024), 0, as_stream(stream), partial_scores,
+                  partial_tokens, G, eos_ids, E, next_token, done);
+}
+
+extern "C" int t2c_token_store(const int64_t *next_token, const uint32_t *done, int64_t *generated_tokens,
+                               uint32_t *generated_length, uint32_t *stopped, int64_t B, int64_t G, int32_t token_index,
+                               const int32_t *token_index_dev, int stop_on_eos, void *stream) {
+    if (!next_token || !done || !generated_tokens || !generated_length || !stopped)
+        return set_error(T2C_EINVAL, "token_store: NULL pointer");
+    if (B <= 0 || G <= 0) return set_error(T2C_EINVAL, "token_store: bad shape");
+    return launch(token_store_kernel, dim3(static_cast<unsigned>((B + 127) / 128)), dim3(128), 0, as_stream(stream),
+                  next_token, done, generated_tokens, generated_length, stopped, B, G, token_index, token_index_dev,
+                  stop_on_eos);
+}
+
+extern "C" int t2c_advance_positions(int32_t *positions, int64_t B, int32_t *token_index, void *stream) {
+    if (!positions || B <= 0) return set_error(T2C_EINVAL, "advance_positions: bad argument");
+    return launch(advance_kernel, dim3(static_cast<unsigned>((B + 127) / 128)), dim3(128), 0, as_stream(stream),
+                  positions, B, token_index);
+}

@@ -39,7 +39,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxStreams = 3;
 constexpr int kMaxStages = 8;
 
-enum Mode : int { MODE_ROWS = 0, MODE_SWIGLU = 1 };
+enum Mode : int { MODE_ROWS = 0, MODE_SWIGLU = 1, MODE_ARGMAX = 2 };
 
 struct QStream {
     const uint8_t *w;
@@ -72,6 +72,10 @@ struct QParams {
     int64_t total_rowsets;  // direct: row-sets; streamed: row blocks
     int stages;
     int stage_bytes;
+    // MODE_ARGMAX: best (score, row) per group of 4 rows, [M, G]
+    float *ps;
+    uint32_t *pt;
+    int64_t G;
 };
 
 // x planes in shared memory.  xh/xl rows are padded by 16 bytes after every
@@ -517,6 +521,27 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g));
 template <int MT, int NR>
 __device__ __forceinline__ void store_rows(const QParams &p, const QStream &st, const int64_t n[NR],
                                            const float acc[NR][MT], bool swiglu) {
+    if (p.mode == MODE_ARGMAX) {
+        // rows n[0..NR) are consecutive and start on a multiple of 4
+        if (n[0] < 0) return;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m >= p.M) continue;
+            float best = acc[0][m];
+            uint32_t tok = static_cast<uint32_t>(n[0]);
+#pragma unroll
+            for (int r = 1; r < NR; ++r) {
+                if (n[r] >= 0 && acc[r][m] > best) {
+                    best = acc[r][m];
+                    tok = static_cast<uint32_t>(n[r]);
+                }
+            }
+            const int64_t g = n[0] >> 2;
+            p.ps[m * p.G + g] = best;
+            p.pt[m * p.G + g] = tok;
+        }
+        return;
+    }
     if (swiglu) {
 #pragma unroll
         for (int r = 0; r + 1 < NR; r += 2) {
@@ -1163,6 +1188,10 @@ int launch_chunked(QParams p, int64_t M, bool tma, cudaStream_t stream) {
             if (c.s[i].y) c.s[i].y = p.s[i].y + m0 * p.s[i].n;
             if (c.s[i].res) c.s[i].res = p.s[i].res + m0 * p.s[i].n;
         }
+        if (p.mode == MODE_ARGMAX) {
+            c.ps = p.ps + m0 * p.G;
+            c.pt = p.pt + m0 * p.G;
+        }
         int rc = launch_fmt(c, mt, tma, stream);
         if (rc != T2C_OK) return rc;
     }
@@ -1267,6 +1296,7 @@ int run_linear(QParams p, int64_t M, cudaStream_t stream) {
         p.stage_bytes = stage_bytes;
         return launch_chunked(p, M, true, stream);
     }
+    if (p.mode == MODE_ARGMAX) return set_error(T2C_EUNSUPPORTED, "lm_head_argmax: weight layout cannot be streamed");
     // direct kernel: row-sets of 2 rows (ROWS) or 1 output (SWIGLU)
     p.units = p.K / 64;
     p.lpr = lanes_for(p.units);
@@ -1348,5 +1378,29 @@ extern "C" int t2c_linear_swiglu(int wtype, const void *x, const void *w_gate, c
     p.s[1] = p.s[0];
     p.s[1].w = static_cast<const uint8_t *>(w_up);
     p.s[1].y = nullptr;
+    return run_linear(p, M, as_stream(stream));
+}
+
+extern "C" int t2c_lm_head_argmax(int wtype, const void *x, const void *w, float *partial_scores,
+                                  uint32_t *partial_tokens, const float *norm_weight, float eps, int64_t M,
+                                  int64_t N, int64_t K, void *stream) {
+    int rc = validate_common(M, K, x);
+    if (rc) return rc;
+    if ((rc = validate_weight(wtype, w, K))) return rc;
+    if (!partial_scores || !partial_tokens || N <= 0) return set_error(T2C_EINVAL, "lm_head_argmax: bad output");
+    QParams p = {};
+    p.nstreams = 1;
+    p.mode = MODE_ARGMAX;
+    p.x = static_cast<const __half *>(x);
+    p.norm_w = norm_weight;
+    p.eps = eps;
+    p.K = static_cast<int>(K);
+    p.s[0].w = static_cast<const uint8_t *>(w);
+    p.s[0].n = N;
+    p.s[0].row_bytes = row_bytes(wtype, K);
+    p.s[0].fmt = wtype;
+    p.ps = partial_scores;
+    p.pt = partial_tokens;
+    p.G = (N + 3) / 4;
     return run_linear(p, M, as_stream(stream));
 }

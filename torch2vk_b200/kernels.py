@@ -9,6 +9,8 @@ Weights are the GGUF packed tensors in the reference's physical dtypes
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from torch2vk_b200 import _lib
@@ -120,3 +122,158 @@ def dequantize(w: torch.Tensor, kind: str | int, k: int) -> torch.Tensor:
     out = torch.empty(r, k, dtype=torch.float32, device=w.device)
     _lib.lib().call("t2c_dequantize", wtype, _lib.ptr(w), _lib.ptr(out), r, k, _lib.stream_ptr())
     return out
+
+
+# ---------------------------------------------------------------- decode ops
+def _check(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA {dtype} tensor")
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the last dim: fp16 x, fp32 w."""
+    _check(x, torch.float16, "x")
+    _check(w, torch.float32, "w")
+    cols = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _lib.lib().call("t2c_rms_norm", _lib.ptr(x), _lib.ptr(w), _lib.ptr(out), x.numel() // cols, cols, float(eps),
+                    _lib.stream_ptr())
+    return out
+
+
+def cache_strides(cache: torch.Tensor, layout: str) -> tuple[int, int, int]:
+    """(batch, position, head) element strides of a KV cache tensor.
+
+    layout "token_major": [B, S, NK, D]; "head_major": [B, NK, S, D].
+    """
+    if layout == "token_major":
+        return cache.stride(0), cache.stride(1), cache.stride(2)
+    if layout == "head_major":
+        return cache.stride(0), cache.stride(2), cache.stride(1)
+    raise ValueError(layout)
+
+
+def qk_norm_rope_cache(q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor, q_w: torch.Tensor,
+                       k_w: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor,
+                       inv_freq: torch.Tensor, *, batch: int, tokens: int, n_heads: int, n_kv: int, head_dim: int,
+                       layout: str = "token_major", eps: float = 1e-6,
+                       q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """q/k RMSNorm + RoPE; rotated k and raw v written into the caches at positions[b] + t."""
+    for t, n in ((q_in, "q_in"), (k_in, "k_in"), (v_in, "v_in")):
+        _check(t, torch.float16, n)
+    _check(positions, torch.int32, "positions")
+    _check(inv_freq, torch.float32, "inv_freq")
+    q_out = torch.empty_like(q_in) if q_out is None else q_out
+    cb, cs, ch = cache_strides(k_cache, layout)
+    _lib.lib().call("t2c_qk_norm_rope_cache", _lib.ptr(q_in), _lib.ptr(k_in), _lib.ptr(v_in), _lib.ptr(q_w),
+                    _lib.ptr(k_w), _lib.ptr(q_out), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(positions),
+                    batch, tokens, n_heads, n_kv, head_dim, cb, cs, ch, _lib.ptr(inv_freq), float(eps),
+                    _lib.stream_ptr())
+    return q_out
+
+
+def attn_decode_workspace_floats(batch: int, n_heads: int, head_dim: int, splits: int) -> int:
+    return batch * n_heads * splits * (head_dim + 2) if splits > 1 else 0
+
+
+def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor, *,
+                batch: int, n_heads: int, n_kv: int, head_dim: int, max_len: int, splits: int = 1,
+                layout: str = "token_major", workspace: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """One query token per batch row against cache positions 0..positions[b]."""
+    _check(q, torch.float16, "q")
+    out = torch.empty_like(q) if out is None else out
+    need = attn_decode_workspace_floats(batch, n_heads, head_dim, splits)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.float32, device=q.device)
+    cb, cs, ch = cache_strides(k_cache, layout)
+    _lib.lib().call("t2c_attn_decode", _lib.ptr(q), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(out),
+                    _lib.ptr(positions), batch, n_heads, n_kv, head_dim, max_len, cb, cs, ch, splits,
+                    _lib.ptr(workspace), workspace.numel() if workspace is not None else 0, _lib.stream_ptr())
+    return out
+
+
+def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor, *,
+                 batch: int, tokens: int, n_heads: int, n_kv: int, head_dim: int, layout: str = "token_major",
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of `tokens` new queries (already cached) over positions 0..positions[b]+t."""
+    _check(q, torch.float16, "q")
+    out = torch.empty_like(q) if out is None else out
+    cb, cs, ch = cache_strides(k_cache, layout)
+    _lib.lib().call("t2c_attn_prefill", _lib.ptr(q), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(out),
+                    _lib.ptr(positions), batch, tokens, n_heads, n_kv, head_dim, cb, cs, ch, _lib.stream_ptr())
+    return out
+
+
+def embedding(weight: torch.Tensor, kind: str | int, ids: torch.Tensor, hidden: int, vocab: int,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(ids, torch.int64, "ids")
+    wtype = wtype_of(kind)
+    out = torch.empty(*ids.shape, hidden, dtype=torch.float16, device=ids.device) if out is None else out
+    _lib.lib().call("t2c_embedding", wtype, _lib.ptr(weight), _lib.ptr(ids), _lib.ptr(out), ids.numel(), vocab,
+                    hidden, _lib.stream_ptr())
+    return out
+
+
+def add(x: torch.Tensor, r: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty_like(x) if out is None else out
+    _lib.lib().call("t2c_add", _lib.ptr(x), _lib.ptr(r), _lib.ptr(out), x.numel(), _lib.stream_ptr())
+    return out
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty_like(g) if out is None else out
+    _lib.lib().call("t2c_swiglu", _lib.ptr(g), _lib.ptr(u), _lib.ptr(out), g.numel(), _lib.stream_ptr())
+    return out
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, kind: str | int, k: int, *,
+                   norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                   partial_scores: torch.Tensor | None = None,
+                   partial_tokens: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-4-row best (score, token) partials [M, ceil(N/4)] of x @ deq(W)^T."""
+    wtype = wtype_of(kind)
+    n = _check_weight(w, wtype, k)
+    m = _check_x(x, k)
+    g = (n + 3) // 4
+    if partial_scores is None:
+        partial_scores = torch.empty(m, g, dtype=torch.float32, device=x.device)
+        partial_tokens = torch.empty(m, g, dtype=torch.int32, device=x.device)
+    _lib.lib().call("t2c_lm_head_argmax", wtype, _lib.ptr(x), _lib.ptr(w), _lib.ptr(partial_scores),
+                    _lib.ptr(partial_tokens), _lib.ptr(norm_weight), float(eps), m, n, k, _lib.stream_ptr())
+    return partial_scores, partial_tokens
+
+
+def token_select(partial_scores: torch.Tensor, partial_tokens: torch.Tensor, eos_ids: torch.Tensor, *,
+                 next_token: torch.Tensor | None = None,
+                 done: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    m, g = partial_scores.shape
+    if next_token is None:
+        next_token = torch.empty(m, dtype=torch.int64, device=partial_scores.device)
+        done = torch.empty(m, dtype=torch.int32, device=partial_scores.device)
+    _lib.lib().call("t2c_token_select", _lib.ptr(partial_scores), _lib.ptr(partial_tokens), m, g, _lib.ptr(eos_ids),
+                    eos_ids.numel(), _lib.ptr(next_token), _lib.ptr(done), _lib.stream_ptr())
+    return next_token, done
+
+
+def token_store(next_token: torch.Tensor, done: torch.Tensor, generated: torch.Tensor, generated_length: torch.Tensor,
+                stopped: torch.Tensor, *, token_index: int = 0, token_index_dev: torch.Tensor | None = None,
+                stop_on_eos: bool = True) -> None:
+    b, cap = generated.shape
+    _lib.lib().call("t2c_token_store", _lib.ptr(next_token), _lib.ptr(done), _lib.ptr(generated),
+                    _lib.ptr(generated_length), _lib.ptr(stopped), b, cap, int(token_index),
+                    _lib.ptr(token_index_dev), 1 if stop_on_eos else 0, _lib.stream_ptr())
+
+
+def advance_positions(positions: torch.Tensor, token_index: torch.Tensor | None = None) -> None:
+    """positions += 1 (and token_index += 1) on the device, for replayed decode graphs."""
+    _check(positions, torch.int32, "positions")
+    _lib.lib().call("t2c_advance_positions", _lib.ptr(positions), positions.numel(), _lib.ptr(token_index),
+                    _lib.stream_ptr())
+
+
+def device_status(clear: bool = True) -> int:
+    """Status bits (1 << T2C_E*) that kernels reported since the last clear."""
+    bits = ctypes.c_uint(0)
+    _lib.lib().call("t2c_device_status", ctypes.addressof(bits), 1 if clear else 0, _lib.stream_ptr())
+    return int(bits.value)
