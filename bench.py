@@ -1,0 +1,372 @@
+"""Headline benchmark: int4 Qwen3-8B decode tok/s on B200 (+ bs32 decode, prefill, qmatvec roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload (BASELINE config 4 on one GPU): Qwen3-8B architecture (36 layers,
+hidden 4096, 32 Q / 8 KV heads, head_dim 128, SwiGLU 12288, vocab 151936),
+seeded N(0, 0.02) weights generated on the GPU and quantized by this repo's
+sm_100a implementation of the reference quantizer: every linear Q4_K (int4,
+32-value sub-blocks with 6-bit scales under fp16 super-block scales), LM head
+Q6_K (the Q4_K_M head type), embeddings F16, norms F32.  A 1024-token random
+prompt is prefilled, then one "step" = one greedy decode token per sequence,
+replayed from a CUDA graph.  `value` = decode tokens/s over all ranks.
+
+N > 1: one independent replica per GPU (weak scaling, no collective); the
+tensor-parallel path is not part of this run.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PROMPT = 1024
+BATCH_LARGE = 32
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.lines: list[str] = []
+        self._thread: threading.Thread | None = None
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._thread = threading.Thread(target=self._read, daemon=True)
+            self._thread.start()
+            time.sleep(0.15)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+            if self._thread is not None:
+                self._thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 6:
+                continue
+            try:
+                mhz.append(float(parts[0]))
+                max_mhz = max(max_mhz, float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[2:]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max_mhz or None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- helpers
+def events_time(fn, reps: int, stream: torch.cuda.Stream) -> float:
+    """Seconds per rep of fn() measured with CUDA events on `stream`."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(reps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) * 1e-3 / reps
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def traffic_from_profile() -> float | None:
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = REPO / "profiles" / "qmv_swiglu_q4k_qwen3_8b.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(sample_layers: int = 3, steps: int = 6) -> dict:
+    """The reference PyTorch CPU path (HF fp32 Qwen3, dequantized-weight math) timed on the host cores.
+
+    Bounded sample: HF Qwen3-8B-shaped models with 1 and `sample_layers`
+    decoder layers (plus the full embedding / LM head) decode `steps` tokens
+    each after a 32-token prompt; the median per-token times give the head
+    cost and the per-layer cost, and the per-token time is that of 36 layers
+    plus the head.  Weight values do not change the fp32 arithmetic cost, so
+    the sample uses the HF default N(0, 0.02) init.
+    """
+    from oracle import qwen3_ref
+    from transformers import Qwen3ForCausalLM
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    @torch.no_grad()
+    def per_token(layers: int) -> float:
+        torch.manual_seed(0)
+        cfg = qwen3_ref.hf_config(4096, layers, 32, 8, 128, 12288, 151936)
+        model = Qwen3ForCausalLM(cfg).float().eval()
+        ids = qwen3_ref.prompt_ids(32, 151936, seed=0)
+        out = model(input_ids=ids, use_cache=True)
+        past, nxt = out.past_key_values, out.logits[:, -1:, :].argmax(-1)
+        times = []
+        for _ in range(steps + 1):
+            t0 = time.perf_counter()
+            out = model(input_ids=nxt, past_key_values=past, use_cache=True)
+            past, nxt = out.past_key_values, out.logits[:, -1:, :].argmax(-1)
+            times.append(time.perf_counter() - t0)
+        times = sorted(times[1:])
+        return times[len(times) // 2]
+
+    t1 = per_token(1)
+    tn = per_token(sample_layers)
+    per_layer = max((tn - t1) / (sample_layers - 1), 0.0)
+    head = max(t1 - per_layer, 0.0)
+    token = head + 36 * per_layer
+    return {"value": 1.0 / token, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"HF fp32 Qwen3-8B shapes with 1 and {sample_layers} layers + full head on CPU, median of "
+                      f"{steps} decode tokens after a 32-token prompt; per-layer {per_layer * 1e3:.1f} ms x 36 + "
+                      f"head {head * 1e3:.1f} ms"}
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    base = cpu_baseline()
+    line = {"impl": "reference", "metric": "qwen3_8b_int4_decode_tok_s_bs1", "value": base["value"], "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic", "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config": {"workload": "Qwen3-8B decode bs1 (reference PyTorch fp32 CPU path)"}}
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, Qwen3Runner, random_weights, weight_bytes
+
+    cfg = Qwen3Config.qwen3_8b()
+    dev = torch.device("cuda", local)
+    weights = random_weights(cfg, seed=rank, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
+    torch.cuda.synchronize()
+    wb = weight_bytes(weights)
+    steps, warm = args.steps, args.warmup
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- prefill (1024-token prompt), timed with events
+    runner = Qwen3Runner(cfg, weights, batch=1, max_seq=PROMPT + steps + warm + 64, max_new_tokens=steps + warm + 8)
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (1, PROMPT), generator=gen).to(dev)
+    runner.prefill(prompt)  # warm-up of every prefill launch path
+    t_prefill = events_time(lambda: runner.prefill(prompt), 1, stream)
+    runner.capture()
+
+    # ---- bs1 decode: W warm-up replays, then K timed replays
+    for _ in range(warm):
+        runner.step()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_step = events_time(runner.step, steps, stream)
+    barrier(world)
+    t_step = max_over_ranks(t_step, world)
+    status = kernels.device_status()
+
+    # ---- e2e: host token in (pinned H2D), graph step, host token out (D2H), every step
+    host_in = torch.zeros(1, dtype=torch.int64).pin_memory()
+    host_out = torch.zeros(1, dtype=torch.int64).pin_memory()
+    host_out.copy_(runner.next_token.cpu())
+
+    def e2e_step() -> None:
+        host_in.copy_(host_out)
+        runner.next_token.copy_(host_in, non_blocking=True)
+        runner.step()
+        host_out.copy_(runner.next_token, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    t0 = time.perf_counter()
+    e2e_reps = min(steps, 200)
+    for _ in range(e2e_reps):
+        e2e_step()
+    t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_reps, world)
+
+    # ---- dominant kernel: gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096), all 36 layers' weights in turn
+    x = torch.randn(1, cfg.hidden, device=dev, dtype=torch.float16)
+    act = torch.empty(1, cfg.intermediate, device=dev, dtype=torch.float16)
+
+    def swiglu_all() -> None:
+        for lw in weights.layers:
+            kernels.linear_swiglu(x, lw.gate.data, lw.up.data, "q4_k", cfg.hidden, norm_weight=lw.post_norm,
+                                  out=act)
+
+    swiglu_all()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        swiglu_all()
+    for _ in range(3):
+        g.replay()
+    t_kernel = events_time(g.replay, 10, stream) / cfg.layers
+    kbytes = (weights.layers[0].gate.data.numel() * 4 * 2) + 2 * cfg.hidden + 2 * cfg.intermediate
+    pk, pk_kind = peaks()
+
+    # ---- bs32 decode on a synthetic 1024-position KV cache (same kernels, M = 32)
+    del runner
+    torch.cuda.empty_cache()
+    big = Qwen3Runner(cfg, weights, batch=BATCH_LARGE, max_seq=PROMPT + steps + warm + 64,
+                      max_new_tokens=steps + warm + 8)
+    for kc, vc in zip(big.k_cache, big.v_cache):
+        kc.normal_(0, 0.5)
+        vc.normal_(0, 0.5)
+    big.positions.fill_(PROMPT)
+    big.next_token.random_(0, cfg.vocab)
+    big.capture()
+    for _ in range(warm):
+        big.step()
+    reps32 = max(8, steps // 8)
+    t_step32 = max_over_ranks(events_time(big.step, reps32, stream), world)
+
+    per_step_launches = cfg.layers * (6 + (1 if big.decode_splits > 1 else 0)) + 5
+    clk = clocks.summary()
+    line = {
+        "metric": "qwen3_8b_int4_decode_tok_s_bs1",
+        "value": world / t_step,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": t_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 x int8 dp4a, f32 accumulate",
+        "data": "synthetic (seeded random weights, random prompt ids)",
+        "config": {"workload": "Qwen3-8B decode, batch 1, 1024-token prompt, Q4_K linears + Q6_K head",
+                   "model": "qwen3-8b-arch", "global_batch": world, "seq_len": PROMPT,
+                   "parallelism": f"{world} replica(s)", "l2": "weights (4.3 GB) larger than L2 every step"},
+        "e2e": {"value": world / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "gpu_launches": per_step_launches * steps,
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "qmv_tma_kernel (gate/up + SwiGLU, Q4_K 2x12288x4096)",
+            "achieved": kbytes / t_kernel / 1e9,
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": kbytes / t_kernel / 1e9 / pk["hbm_gbs"],
+            "peak_source": pk_kind,
+            "traffic": traffic_from_profile(),
+            "algorithmic_bytes_per_launch": kbytes,
+        },
+        "step_roofline": {
+            "bytes_per_step": wb["linears"] + wb["lm_head"],
+            "achieved_gbs": (wb["linears"] + wb["lm_head"]) / t_step / 1e9,
+            "frac": (wb["linears"] + wb["lm_head"]) / t_step / 1e9 / pk["hbm_gbs"],
+        },
+        "decode_bs32_tok_s": world * BATCH_LARGE / t_step32,
+        "prefill_tok_s": world * PROMPT / t_prefill,
+        "device_status_bits": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
