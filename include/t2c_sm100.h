@@ -173,6 +173,32 @@ int t2c_attn_decode(const void *q, const void *k_cache, const void *v_cache, voi
                     float *workspace, int64_t workspace_floats, void *stream);
 
 /*
+ * t2c_attn_decode for callers that cannot allocate device memory: the same
+ * split-K decode attention, with its split partials kept in a fixed 16 MiB
+ * device array inside the library instead of a caller workspace.  Meant for
+ * hosts that own every device allocation themselves and forbid a plugin to
+ * call cudaMalloc (fixed-budget serving executors, embedding runtimes that
+ * pre-plan all memory, code that runs where allocation is not allowed).
+ * This entry point has no counterpart in the reference (its shaders receive
+ * all scratch as bound buffers).
+ *   - Limit: B * NH * splits * (D + 2) <= 4194304 floats, else T2C_ESCRATCH
+ *     (splits == 1 needs no scratch).
+ *   - Allocates nothing: no cudaMalloc / cudaFree / allocating library call.
+ *     The array exists on every GPU that loads the library, until exit.
+ *   - The first call on a device resolves the array's device address on the
+ *     current device (cudaGetSymbolAddress); make that first call before any
+ *     stream capture.
+ *   - All calls share the one array, which keeps the last call's contents;
+ *     every split record is fully rewritten before it is read, so nothing
+ *     needs clearing, but calls that overlap on the GPU (other streams or
+ *     threads) race on it and must be serialised by the caller.
+ */
+int t2c_attn_decode_static(const void *q, const void *k_cache, const void *v_cache, void *out,
+                           const int32_t *positions, int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t max_len,
+                           int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride, int64_t splits,
+                           void *stream);
+
+/*
  * Causal prefill attention: q [B, T, NH, D] (token-major), keys/values read
  * from the caches for positions 0 .. positions[b] + T - 1 (the current chunk
  * already written by t2c_qk_norm_rope_cache); query t of batch b attends to

@@ -52,6 +52,7 @@ _SIGNATURES: dict[str, list] = {
     "t2c_add": [_vp, _vp, _vp, _i64, _vp],
     "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],
     "t2c_advance_positions": [_vp, _i64, _vp, _vp],
+    "t2c_attn_decode_static": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
 }
 _RESTYPES = {"t2c_last_error": _c.c_char_p}
 

@@ -4,6 +4,8 @@
 // store pair.  fp16 storage, fp32 arithmetic throughout.
 #include <float.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace t2c {
@@ -723,4 +725,48 @@ extern "C" int t2c_advance_positions(int32_t *positions, int64_t B, int32_t *tok
     if (!positions || B <= 0) return set_error(T2C_EINVAL, "advance_positions: bad argument");
     return launch(advance_kernel, dim3(static_cast<unsigned>((B + 127) / 128)), dim3(128), 0, as_stream(stream),
                   positions, B, token_index);
+}
+
+// ------------------------------------------------ decode attention, no allocation
+// Fixed scratch for t2c_attn_decode_static: a file-scope device array that
+// every GPU which loads this library holds until the process exits.
+static constexpr int64_t kStaticAttnScratchFloats = 4 * 1024 * 1024;  // 16 MiB
+static __device__ __align__(256) float g_static_attn_scratch[kStaticAttnScratchFloats];
+
+namespace {
+std::mutex g_static_scratch_mutex;
+float *g_static_scratch_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int t2c_attn_decode_static(const void *q, const void *k_cache, const void *v_cache, void *out,
+                                      const int32_t *positions, int64_t B, int64_t NH, int64_t NK, int64_t D,
+                                      int64_t max_len, int64_t cb, int64_t cs, int64_t ch, int64_t splits,
+                                      void *stream) {
+    const int64_t need = splits > 1 ? B * NH * splits * (D + 2) : 0;
+    if (need > kStaticAttnScratchFloats) {
+        return set_error(T2C_ESCRATCH,
+                         "attn_decode_static: B*NH*splits*(D+2) = %lld floats exceeds the fixed scratch of %lld floats "
+                         "(16 MiB); lower splits or use t2c_attn_decode with a caller workspace",
+                         (long long)need, (long long)kStaticAttnScratchFloats);
+    }
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "attn_decode_static: cudaGetDevice: %s", cudaGetErrorString(err));
+    if (device < 0 || device >= 64) return set_error(T2C_EINVAL, "attn_decode_static: device %d out of range", device);
+    float *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+        if (g_static_scratch_ptr[device] == nullptr) {
+            // One-time set-up on this device (the device is current): the
+            // host-side symbol is only a stand-in, so fetch the device address.
+            void *ptr = nullptr;
+            err = cudaGetSymbolAddress(&ptr, g_static_attn_scratch);
+            if (err != cudaSuccess)
+                return set_error(T2C_ECUDA, "attn_decode_static: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
+            g_static_scratch_ptr[device] = static_cast<float *>(ptr);
+        }
+        scratch = g_static_scratch_ptr[device];
+    }
+    return t2c_attn_decode(q, k_cache, v_cache, out, positions, B, NH, NK, D, max_len, cb, cs, ch, splits, scratch,
+                           kStaticAttnScratchFloats, stream);
 }
