@@ -199,16 +199,66 @@ int t2c_attn_decode_static(const void *q, const void *k_cache, const void *v_cac
                            void *stream);
 
 /*
- * Causal prefill attention: q [B, T, NH, D] (token-major), keys/values read
- * from the caches for positions 0 .. positions[b] + T - 1 (the current chunk
- * already written by t2c_qk_norm_rope_cache); query t of batch b attends to
- * cache positions <= positions[b] + t.  out [B, T, NH, D] fp16.
+ * Causal prefill attention: T queries per batch row, keys/values read from
+ * the caches for positions 0 .. positions[b] + T - 1 (the current chunk
+ * already written); query t of batch b attends to cache positions
+ * <= positions[b] + t.  q and out are addressed by element strides
+ * (batch, token, head): token-major [B, T, NH, D] or head-major [B, NH, T, D].
  * Replaces ExportSdpaProgram (causal)
  *   src/models/quantized_qwen3/shaders/sdpa_causal_f32.py:22-142
  */
 int t2c_attn_prefill(const void *q, const void *k_cache, const void *v_cache, void *out,
                      const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t D,
-                     int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride, void *stream);
+                     int64_t cache_b_stride, int64_t cache_s_stride, int64_t cache_h_stride, int64_t q_b_stride,
+                     int64_t q_t_stride, int64_t q_h_stride, int64_t out_b_stride, int64_t out_t_stride,
+                     int64_t out_h_stride, void *stream);
+
+/* ---------------------------------------------------- exported-graph ops
+ * Strided 4-D copy dst[i] = src[i] (element size 1/2/4/8 bytes; strides in
+ * elements).  Serves the slice / cat / transpose / contiguous-view contracts
+ * (ExportSliceProgram, ExportCat2Program, ExportTransposeProgram,
+ *  SliceLastTokenF16Program) of src/models/quantized_qwen3/shaders/{slice_f32,
+ *  cat_2_f32,transpose_f32_*,slice_last_token_f16}.py.
+ */
+int t2c_copy4d(int elem_bytes, const void *src, const int64_t *src_strides, void *dst, const int64_t *dst_strides,
+               const int64_t *shape, void *stream);
+/*
+ * Broadcasting 4-D elementwise op (0 add, 1 mul, 2 neg, 3 silu) on fp16
+ * (is_f32 = 0) or fp32 tensors; zero strides broadcast.  Serves
+ * ExportAddF32Program, ExportMulF32Program, ExportMulBroadcastProgram,
+ * ExportNegF32Program, ExportSiluF32Program (src/models/quantized_qwen3/shaders/).
+ */
+int t2c_elementwise4d(int op, int is_f32, const void *a, const int64_t *a_strides, const void *b,
+                      const int64_t *b_strides, void *out, const int64_t *out_strides, const int64_t *shape,
+                      void *stream);
+/* RoPE cos/sin tables [B, T, D] fp16 (src/torch2vk/runtime/rope_table.py:31-121). */
+int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                   int64_t start_position, float attention_scaling, void *stream);
+/*
+ * Per-row RMSNorm + rotate-half RoPE from fp16 cos/sin tables [B, T, D]; x
+ * [B, T, G, D] fp16, out addressed by strides (b, g, t).  Replaces
+ * OptimizedQwen3RmsNormRopeTransposeF16Program
+ *   src/models/optimized_qwen3/shaders/rms_norm_rope_transpose_f16.py:22-146
+ */
+int t2c_rms_norm_rope(const void *x, const float *w, const void *cos_t, const void *sin_t, void *out, int64_t B,
+                      int64_t T, int64_t G, int64_t D, int64_t out_b_stride, int64_t out_g_stride,
+                      int64_t out_t_stride, float eps, void *stream);
+/*
+ * cache[b, pos, h, :] = src[b, t, h, :] with pos = positions[t] (int64 [T]) or,
+ * when positions is NULL, position + t; cache of S positions, both addressed
+ * by element strides.  Replaces ExportKvCacheWriteF16Program (both variants)
+ * and the token-major pair/triple writes
+ *   src/models/quantized_qwen3/shaders/kv_cache_write_f16.py:22-92, kv_cache_write_decode_f16.py:23-85
+ *   src/models/optimized_qwen3/shaders/token_major_kv_cache_write_f16_pair.py:20-105
+ */
+int t2c_kv_cache_write(void *cache, const void *src, const int64_t *positions, int64_t position, int64_t B,
+                       int64_t H, int64_t T, int64_t D, int64_t S, int64_t cache_b_stride, int64_t cache_s_stride,
+                       int64_t cache_h_stride, int64_t src_b_stride, int64_t src_t_stride, int64_t src_h_stride,
+                       void *stream);
+/* Best (score, token) per chunk of 1024 partials (ties -> lower token); C = ceil(G / 1024) outputs.
+ * Replaces Qwen3TokenSelectReduceChunksF32Program (qwen3_token_select_reduce_f32.py:21-148). */
+int t2c_token_select_chunks(const float *scores, const uint32_t *tokens, int64_t G, float *chunk_scores,
+                            uint32_t *chunk_tokens, void *stream);
 
 /* ---------------------------------------------------------------- misc
  * Embedding gather: out[i, :] = deq(weight[ids[i], :]) for F16 or Q4_K rows.

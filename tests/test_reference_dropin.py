@@ -1,0 +1,265 @@
+"""Drop-in conformance on the CPU (no kernels run).
+
+1. Every op declaration in torch2vk_b200.runtime.variants equals the reference
+   ShaderVariant of the same name: class_name, fields (name, io kind, role,
+   dtype, symbolic shape, layout), push constants and dispatch grid.
+2. The reference's own generated Qwen3 model code (models/quantized_qwen3 and
+   models/optimized_qwen3: tensors/, dispatch/, shaders/) imported through
+   torch2vk_b200.compat drives a prefill + decode step through RuntimeSession's
+   validation; every contract class it dispatches has a CUDA op.
+3. RuntimeSession.dispatch raises the reference dispatcher's errors.
+
+Parts 1-2 read the reference sources and skip when they are absent.
+"""
+
+from __future__ import annotations
+
+import importlib
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REF_SRC = Path("/root/reference/src")
+needs_ref = pytest.mark.skipif(not (REF_SRC / "models" / "quantized_qwen3").is_dir(),
+                               reason="reference sources not present")
+
+
+@pytest.fixture()
+def ref_modules():
+    """Installs the torch2vk aliases and the reference `models` package; undoes both after."""
+    saved = {k: v for k, v in sys.modules.items() if k == "torch2vk" or k.startswith(("torch2vk.", "models"))}
+    for k in saved:
+        del sys.modules[k]
+    from torch2vk_b200 import compat
+
+    compat.install()
+    sys.path.append(str(REF_SRC))
+    try:
+        yield
+    finally:
+        sys.path.remove(str(REF_SRC))
+        for k in [k for k in sys.modules if k == "torch2vk" or k.startswith(("torch2vk.", "models"))]:
+            del sys.modules[k]
+        sys.modules.update(saved)
+
+
+def _variant_names():
+    from torch2vk_b200.runtime import variants
+
+    return sorted(variants.all_variants())
+
+
+# The reference generator names transposes by a hash of their source; this one
+# is the dim-1/2 swap that every transpose of the Qwen3 export uses.
+REF_NAME = {"transpose_f32": "transpose_f32_9884b7b82d"}
+
+
+@needs_ref
+@pytest.mark.parametrize("name", _variant_names())
+def test_variant_contract_matches_reference(ref_modules, name):
+    from torch2vk_b200.runtime import variants
+
+    ours = variants.all_variants()[name]
+    if name == "rope_table_f32":
+        pytest.skip("torch2vk.runtime.rope_table is itself aliased to this package")
+    ref_name = REF_NAME.get(name, name)
+    ref = None
+    for pkg in ("models.quantized_qwen3.shaders", "models.optimized_qwen3.shaders"):
+        try:
+            ref = getattr(importlib.import_module(f"{pkg}.{ref_name}"), ref_name.upper())
+            break
+        except ModuleNotFoundError:
+            continue
+    assert ref is not None, f"no reference variant {ref_name}"
+    a, b = ours.contract, ref.contract
+    assert a.class_name == b.class_name
+    assert a.fields == b.fields
+    assert a.push_constants == b.push_constants
+    assert a.dispatch == b.dispatch
+
+
+def _drive_quantized_qwen3(rt, mt, cache_position):
+    from models.quantized_qwen3.dispatch.decode_embed import run_decode_embed
+    from models.quantized_qwen3.dispatch.decode_layer import run_decode_layer
+    from models.quantized_qwen3.dispatch.decode_norm import run_decode_norm
+    from models.quantized_qwen3.dispatch.embed_tokens import run_embed_tokens
+    from models.quantized_qwen3.dispatch.text_layer import run_text_layer
+    from models.quantized_qwen3.dispatch.text_norm import run_text_norm
+    from models.quantized_qwen3.shaders.lm_head_q6_k_argmax_partial_f16 import LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16
+    from models.quantized_qwen3.shaders.qwen3_token_select_reduce_chunks_f32 import (
+        QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32,
+    )
+    from models.quantized_qwen3.shaders.qwen3_token_select_reduce_f32 import QWEN3_TOKEN_SELECT_REDUCE_F32
+    from models.quantized_qwen3.shaders.qwen3_token_store_eos import QWEN3_TOKEN_STORE_EOS
+    from models.quantized_qwen3.shaders.slice_last_token_f16 import SLICE_LAST_TOKEN_F16
+    from torch2vk.runtime.rope_table import ROPE_TABLE_F32
+
+    def head(x):
+        LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16(rt, x=x, weight=mt.lm_head.p_weight, partial_scores=mt.lm_head_partial_scores,
+                                        partial_tokens=mt.lm_head_partial_tokens)
+        QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32(rt, scores=mt.lm_head_partial_scores, tokens=mt.lm_head_partial_tokens,
+                                             chunk_scores=mt.lm_head_chunk_scores,
+                                             chunk_tokens=mt.lm_head_chunk_tokens)
+        QWEN3_TOKEN_SELECT_REDUCE_F32(rt, partial_scores=mt.lm_head_chunk_scores,
+                                      partial_tokens=mt.lm_head_chunk_tokens, eos_token_ids=mt.eos_token_ids,
+                                      next_token=mt.next_token, done=mt.done)
+
+    def store(index):
+        QWEN3_TOKEN_STORE_EOS(rt, next_token=mt.next_token, token_index=index, done=mt.done,
+                              generated_tokens=mt.generated_tokens, generated_length=mt.generated_length,
+                              stopped=mt.stopped)
+
+    # the order of models/quantized_qwen3/run.py:_run_prefill and _run_decode_step
+    with rt.frame("qwen3.prefill"):
+        ROPE_TABLE_F32(rt, start_position=0, theta=1e6, cos=mt.prefill_rope.cos, sin=mt.prefill_rope.sin)
+        run_embed_tokens(rt)
+        for i in range(len(mt.text_layers)):
+            run_text_layer(rt, i)
+        run_text_norm(rt)
+        SLICE_LAST_TOKEN_F16(rt, x=mt.text_norm.rms_norm, output=mt.prefill_lm_head_input)
+        head(mt.prefill_lm_head_input)
+        store(0)
+    with rt.frame("qwen3.decode.0000"):
+        ROPE_TABLE_F32(rt, start_position=cache_position, theta=1e6, cos=mt.decode_rope.cos, sin=mt.decode_rope.sin)
+        run_decode_embed(rt)
+        for i in range(len(mt.decode_layers)):
+            run_decode_layer(rt, i, cache_position=cache_position)
+        run_decode_norm(rt)
+        head(mt.decode_norm.rms_norm)
+        store(1)
+
+
+@needs_ref
+def test_reference_quantized_qwen3_dispatch_through_session(ref_modules):
+    from models.quantized_qwen3.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+
+    P = 8
+    mt = create_model_tensors(prompt_length=P, max_sequence_length=64, num_hidden_layers=28, num_key_value_heads=8,
+                              head_dim=128, max_new_tokens=4, eos_token_count=2, vocab_size=151936)
+    rt = DrySession(mt)
+    rt.initialize_session_tensors({mt.eos_token_ids: np.array([151643, 151645], np.int64)})
+    zero = np.zeros((1, 8, 64, 128), np.float16)
+    state = {c: zero for c in mt.key_caches + mt.value_caches}
+    state.update({mt.generated_tokens: np.zeros((1, 4), np.int64), mt.generated_length: np.zeros(1, np.uint32),
+                  mt.stopped: np.zeros(1, np.uint32)})
+    with rt.request(inputs={mt.input_ids.name: np.zeros((1, P), np.int64),
+                            mt.text_layers[0].cache_position.name: np.arange(P, dtype=np.int64)}, state=state):
+        _drive_quantized_qwen3(rt, mt, cache_position=P)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    assert len(rt.calls) > 2000
+    decode = [c for c in rt.calls if c[0] == "sdpa_decode_cache_f16"]
+    assert len(decode) == 28 and all(c[3]["cache_position"] == P for c in decode)
+    lin = [c for c in rt.calls if c[0] == "linear_nobias_q4_k_matvec_f32"]
+    assert {c[2]["K"] for c in lin} == {1024, 2048, 3072}
+
+
+@needs_ref
+def test_reference_optimized_qwen3_decode_through_session(ref_modules):
+    from models.optimized_qwen3.dispatch.decode_embed import run_decode_embed
+    from models.optimized_qwen3.dispatch.decode_layer import run_decode_layer
+    from models.optimized_qwen3.dispatch.decode_norm import run_decode_norm
+    from models.optimized_qwen3.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+
+    # sizes as models/optimized_qwen3/run.py derives them for an 8-token prompt
+    mt = create_model_tensors(prompt_length=8, prefill_chunk_length=512, prefill_tail_length=8,
+                              prefill_attention_length=64, max_sequence_length=192, num_hidden_layers=28,
+                              num_key_value_heads=8, head_dim=128, max_new_tokens=4, eos_token_count=2,
+                              vocab_size=151936)
+    rt = DrySession(mt)
+    state = {c: np.zeros(c.concrete_shape, np.float16) for c in mt.decode_key_caches + mt.decode_value_caches}
+    state[mt.decode_rope.cos] = np.zeros((1, 1, 128), np.float16)
+    state[mt.decode_rope.sin] = np.zeros((1, 1, 128), np.float16)
+    state[mt.next_token] = np.zeros((1, 1), np.int64)
+    with rt.request(state=state):
+        with rt.frame("qwen3.decode.0000"):
+            run_decode_embed(rt)
+            for i in range(len(mt.decode_layers)):
+                run_decode_layer(rt, i, cache_position=8)
+            run_decode_norm(rt)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    assert "SdpaDecodeCacheWriteF32Program" in classes and "LinearNobiasQ4KQKVMatvecProgram" in classes or \
+        "LinearNobiasQ4QKQ6VMatvecProgram" in classes
+
+
+# ---------------------------------------------------------------- validation errors
+def _tensors():
+    from torch2vk_b200.runtime.logical import LogicalTensor, MemoryClass, TensorLifetime, TensorRole
+    from torch2vk_b200.runtime.types import TensorSpec, q4_k_words_layout
+
+    def t(name, dtype, shape, role=TensorRole.ACTIVATION, **kw):
+        mem = {TensorRole.ACTIVATION: MemoryClass.FRAME_WORKSPACE, TensorRole.INPUT: MemoryClass.HOST_INPUT,
+               TensorRole.WEIGHT: MemoryClass.MODEL_WEIGHT}[role]
+        life = TensorLifetime.MODEL if role is TensorRole.WEIGHT else TensorLifetime.FRAME
+        return LogicalTensor(spec=TensorSpec(dtype, shape), role=role, memory=mem, lifetime=life, name=name, **kw)
+
+    x = t("x", "float16", (1, 2, 512), TensorRole.INPUT)
+    w = t("w", "uint32", (256, 72), TensorRole.WEIGHT, checkpoint_key="w", layout=q4_k_words_layout(logical_k=512))
+    y = t("y", "float16", (1, 2, 256))
+    return t, x, w, y
+
+
+def test_dispatch_validation_errors():
+    from tests.dry_session import DrySession
+    from torch2vk_b200.runtime import variants as V
+    from torch2vk_b200.runtime.logical import bind_logical_tensor_alias
+
+    t, x, w, y = _tensors()
+    rt = DrySession()
+    rt.register_host_inputs({x: np.zeros((1, 2, 512), np.float16)})
+    with pytest.raises(RuntimeError, match="active rt.frame"):
+        V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=w, output=y)
+    with rt.frame("f"):
+        with pytest.raises(ValueError, match="missing tensor fields"):
+            V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=w)
+        with pytest.raises(ValueError, match="unexpected fields"):
+            V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=w, output=y, bias=y)
+        with pytest.raises(ValueError, match="missing push constant inputs"):
+            V.SDPA_DECODE_CACHE_F16(rt, q=y, k=y, v=y, output=y)
+        with pytest.raises(TypeError, match="expects LogicalTensor"):
+            V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=np.zeros(3), weight=w, output=y)
+        with pytest.raises(ValueError, match="expects dtype"):
+            V.LINEAR_NOBIAS_Q6_K_MATVEC_F32(rt, x=x, weight=w, output=y)
+        bad_y = t("bad_y", "float16", (1, 3, 256))
+        with pytest.raises(ValueError, match="Shape symbol X1 bound to both"):
+            V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=w, output=bad_y)
+        bad_w = t("bad_w", "uint32", (256, 36), checkpoint_key="bw", role=__import__(
+            "torch2vk_b200.runtime.logical", fromlist=["TensorRole"]).TensorRole.WEIGHT,
+            layout=__import__("torch2vk_b200.runtime.types", fromlist=["q4_k_words_layout"]).q4_k_words_layout(
+                logical_k=512))
+        with pytest.raises(ValueError, match="expects dim"):
+            V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=bad_w, output=y)
+        z = t("z", "float16", (1, 2, 256))
+        with pytest.raises(RuntimeError, match="cannot be read before"):
+            V.ADD_F32_18(rt, x=z, y=z, output=y)
+        V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=x, weight=w, output=y)
+        view = t("view", "float16", (1, 2, 256))
+        bind_logical_tensor_alias(y, view)
+        with pytest.raises(RuntimeError, match="cannot be written"):
+            V.ADD_F32_18(rt, x=y, y=y, output=view)
+        assert rt.dispatch_records[-1].shader == "linear_nobias_q4_k_matvec_f32"
+        assert y.writer is not None and y.writer.shader == "linear_nobias_q4_k_matvec_f32"
+    assert y.buffer is None  # frame workspace released at frame exit
+    with pytest.raises(ValueError, match="byte size differs"):
+        bind_logical_tensor_alias(y, t("small", "float16", (1, 2, 2)))
+
+
+def test_declaration_rules():
+    from torch2vk_b200.runtime.logical import LogicalTensor, MemoryClass, TensorLifetime, TensorRole
+    from torch2vk_b200.runtime.types import TensorSpec
+
+    w = LogicalTensor(spec=TensorSpec("uint32", (4, 36)), role=TensorRole.WEIGHT, memory=MemoryClass.MODEL_WEIGHT,
+                      lifetime=TensorLifetime.MODEL, name="w")
+    with pytest.raises(ValueError, match="checkpoint_key"):
+        w.validate_declaration()
+    a = LogicalTensor(spec=TensorSpec("float16", (4,)), role=TensorRole.ACTIVATION,
+                      memory=MemoryClass.REQUEST_STATE, lifetime=TensorLifetime.FRAME, name="a")
+    with pytest.raises(ValueError, match="FRAME_WORKSPACE"):
+        a.validate_declaration()
+    with pytest.raises(RuntimeError, match="runtime state"):
+        a.buffer = object()

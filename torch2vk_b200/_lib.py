@@ -47,7 +47,15 @@ _SIGNATURES: dict[str, list] = {
                                _i64, _i64, _i64, _vp, _f32, _vp],
     "t2c_attn_decode": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                         _i64, _vp],
-    "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                         _i64, _i64, _i64, _i64, _vp],
+    "t2c_copy4d": [_i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    "t2c_elementwise4d": [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "t2c_rope_table": [_vp, _vp, _i64, _i64, _i64, _f32, _i64, _f32, _vp],
+    "t2c_rms_norm_rope": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp],
+    "t2c_kv_cache_write": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                           _vp],
+    "t2c_token_select_chunks": [_vp, _vp, _i64, _vp, _vp, _vp],
     "t2c_embedding": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "t2c_add": [_vp, _vp, _vp, _i64, _vp],
     "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],

@@ -158,8 +158,12 @@ static inline cudaError_t read_tu_status(unsigned int *bits, int clear, cudaStre
     return err;
 }
 
-// Programmatic dependent launch: wait until the preceding kernel on the stream
-// has completed (or triggered); a no-op when launched without the attribute.
+// Programmatic dependent launch.  pdl_wait(): block until the preceding
+// kernel in the stream has completed and its memory is visible (a no-op when
+// launched without the attribute).  pdl_trigger(): allow the next kernel to
+// launch now; it still waits in its own pdl_wait() for this kernel to finish,
+// so only work that needs nothing from this kernel (weight prefetch) runs
+// early.  Every kernel here triggers right after its wait.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -30,6 +30,7 @@ __global__ void rms_norm_kernel(const __half *__restrict__ x, const float *__res
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     pdl_wait();
+    pdl_trigger();
     const __half *xr = x + row * cols;
     float ss = 0.0f;
     for (int c = lane * 4; c < cols; c += 128) {
@@ -65,6 +66,7 @@ __global__ void qk_norm_rope_cache_kernel(const __half *__restrict__ q_in, const
     const int64_t total = static_cast<int64_t>(B) * T * heads;
     if (vec >= total) return;
     pdl_wait();
+    pdl_trigger();
     const int64_t m = vec / heads;
     const int h = static_cast<int>(vec - m * heads);
     const int b = static_cast<int>(m / T), t = static_cast<int>(m - static_cast<int64_t>(b) * T);
@@ -125,6 +127,7 @@ __global__ void qk_norm_rope_cache_kernel(const __half *__restrict__ q_in, const
 // (one split) or the split's partial (max, sum, acc) to the workspace.
 constexpr int kAttnWarps = 4;
 constexpr int kMaxGroup = 8;
+constexpr int kMaxSplits = 64;
 
 template <int E, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const int b = blockIdx.x / (splits * NK);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
+    pdl_trigger();
     const int len = positions[b] + 1;
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
         const int g = i / D, d = i - g * D;
@@ -161,22 +165,48 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     for (int t0 = p0 + warp * 32; t0 < p1; t0 += kAttnWarps * 32) {
         const int pos = t0 + lane;
         const bool valid = pos < p1;
+        // scores: lane = position; the whole K row is requested at once
         float s[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.0f;
         if (valid) {
             const uint4 *kr = reinterpret_cast<const uint4 *>(kbase + static_cast<int64_t>(pos) * cs);
-#pragma unroll 4
+            uint4 kraw[D / 8];
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) kraw[c] = kr[c];
+#pragma unroll
             for (int c = 0; c < D / 8; ++c) {
-                const uint4 raw = kr[c];
-                const float4 lo = h4_to_f4(make_uint2(raw.x, raw.y));
-                const float4 hi = h4_to_f4(make_uint2(raw.z, raw.w));
+                const float4 lo = h4_to_f4(make_uint2(kraw[c].x, kraw[c].y));
+                const float4 hi = h4_to_f4(make_uint2(kraw[c].z, kraw[c].w));
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float *qq = &qs[g][c * 8];
-                    s[g] += lo.x * qq[0] + lo.y * qq[1] + lo.z * qq[2] + lo.w * qq[3] + hi.x * qq[4] + hi.y * qq[5] +
-                            hi.z * qq[6] + hi.w * qq[7];
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][c * 8]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][c * 8 + 4]);
+                    s[g] += lo.x * qa.x + lo.y * qa.y + lo.z * qa.z + lo.w * qa.w + hi.x * qb.x + hi.y * qb.y +
+                            hi.z * qb.z + hi.w * qb.w;
                 }
+            }
+        }
+        // values: lane = E dims; the 32 V fragments of the tile are requested at once
+        const int n_valid = min(32, p1 - t0);
+        float vf[32][E];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < n_valid) {
+                const __half *vr = vbase + static_cast<int64_t>(t0 + j) * cs + lane * E;
+                if constexpr (E == 4) {
+                    const float4 f = h4_to_f4(*reinterpret_cast<const uint2 *>(vr));
+                    vf[j][0] = f.x;
+                    vf[j][1] = f.y;
+                    vf[j][2] = f.z;
+                    vf[j][3] = f.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) vf[j][e] = __half2float(vr[e]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) vf[j][e] = 0.0f;
             }
         }
         float p[G];
@@ -192,25 +222,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
 #pragma unroll
             for (int e = 0; e < E; ++e) acc[g][e] *= corr;
         }
-        const int n_valid = min(32, p1 - t0);
-        for (int j = 0; j < n_valid; ++j) {
-            const __half *vr = vbase + static_cast<int64_t>(t0 + j) * cs + lane * E;
-            float vv[E];
-            if constexpr (E == 4) {
-                const float4 f = h4_to_f4(*reinterpret_cast<const uint2 *>(vr));
-                vv[0] = f.x;
-                vv[1] = f.y;
-                vv[2] = f.z;
-                vv[3] = f.w;
-            } else {
 #pragma unroll
-                for (int e = 0; e < E; ++e) vv[e] = __half2float(vr[e]);
-            }
+        for (int j = 0; j < 32; ++j) {
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float pj = __shfl_sync(0xffffffffu, p[g], j);
 #pragma unroll
-                for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pj, vv[e], acc[g][e]);
+                for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pj, vf[j][e], acc[g][e]);
             }
         }
     }
@@ -252,20 +270,49 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
 template <int E>
 __global__ void attn_combine_kernel(const float *__restrict__ ws, __half *__restrict__ out, int B, int NH, int splits) {
     constexpr int D = E * 32;
+    __shared__ float wts[kMaxSplits];
+    __shared__ float total;
     const int64_t bh = blockIdx.x;  // b * NH + h
     if (bh >= static_cast<int64_t>(B) * NH) return;
+    pdl_wait();
+    pdl_trigger();
     const float *rec = ws + bh * splits * (D + 2);
-    float mx = -FLT_MAX;
-    for (int s = 0; s < splits; ++s) mx = fmaxf(mx, rec[s * (D + 2)]);
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float l = 0.0f, a = 0.0f;
-        for (int s = 0; s < splits; ++s) {
-            const float m = rec[s * (D + 2)];
-            const float f = m == -FLT_MAX ? 0.0f : __expf(m - mx);
-            l += rec[s * (D + 2) + 1] * f;
-            a += rec[s * (D + 2) + 2 + d] * f;
+    if (threadIdx.x < 32) {
+        // split weights exp(m_s - max) and the combined softmax sum
+        float m[kMaxSplits / 32], l[kMaxSplits / 32];
+        float mx = -FLT_MAX;
+#pragma unroll
+        for (int i = 0; i < kMaxSplits / 32; ++i) {
+            const int sp = threadIdx.x + 32 * i;
+            m[i] = sp < splits ? rec[sp * (D + 2)] : -FLT_MAX;
+            l[i] = sp < splits ? rec[sp * (D + 2) + 1] : 0.0f;
+            mx = fmaxf(mx, m[i]);
         }
-        out[bh * D + d] = __float2half_rn(l > 0.0f ? a / l : 0.0f);
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMaxSplits / 32; ++i) {
+            const int sp = threadIdx.x + 32 * i;
+            const float w = m[i] == -FLT_MAX ? 0.0f : __expf(m[i] - mx);
+            if (sp < splits) wts[sp] = w;
+            sum += w * l[i];
+        }
+        sum = warp_sum(sum);
+        if (threadIdx.x == 0) total = sum;
+    }
+    __syncthreads();
+    const float inv = total > 0.0f ? 1.0f / total : 0.0f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int sp = 0;
+        for (; sp + 4 <= splits; sp += 4) {
+            a0 = fmaf(wts[sp], rec[sp * (D + 2) + 2 + d], a0);
+            a1 = fmaf(wts[sp + 1], rec[(sp + 1) * (D + 2) + 2 + d], a1);
+            a2 = fmaf(wts[sp + 2], rec[(sp + 2) * (D + 2) + 2 + d], a2);
+            a3 = fmaf(wts[sp + 3], rec[(sp + 3) * (D + 2) + 2 + d], a3);
+        }
+        for (; sp < splits; ++sp) a0 = fmaf(wts[sp], rec[sp * (D + 2) + 2 + d], a0);
+        out[bh * D + d] = __float2half_rn((a0 + a1 + a2 + a3) * inv);
     }
 }
 
@@ -280,7 +327,9 @@ template <int E>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *__restrict__ q, const __half *__restrict__ kc,
                                                            const __half *__restrict__ vc, __half *__restrict__ out,
                                                            const int32_t *__restrict__ positions, int T, int NH,
-                                                           int NK, int64_t cb, int64_t cs, int64_t ch, float scale) {
+                                                           int NK, int64_t cb, int64_t cs, int64_t ch, int64_t q_sb,
+                                                           int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st,
+                                                           int64_t o_sh, float scale) {
     constexpr int D = E * 32;
     constexpr int QW = kPfQ / 4;  // queries per warp
     __shared__ float qs[kPfQ][D];
@@ -291,11 +340,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *__restr
     const int kh = h / (NH / NK);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
+    pdl_trigger();
     const int base = positions[b];
     for (int i = threadIdx.x; i < kPfQ * D; i += blockDim.x) {
         const int qi = i / D, d = i - qi * D;
         const int t = qt * kPfQ + qi;
-        qs[qi][d] = t < T ? __half2float(q[((static_cast<int64_t>(b) * T + t) * NH + h) * D + d]) * scale : 0.0f;
+        qs[qi][d] = t < T ? __half2float(q[b * q_sb + t * q_st + h * q_sh + d]) * scale : 0.0f;
     }
     __syncthreads();
     float m_run[QW], l_run[QW], acc[QW][E];
@@ -363,7 +413,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *__restr
         for (int i = 0; i < QW; ++i) {
             const int t = q_first + i;
             if (t >= T) continue;
-            __half *o = out + ((static_cast<int64_t>(b) * T + t) * NH + h) * D + lane * E;
+            __half *o = out + b * o_sb + t * o_st + h * o_sh + lane * E;
             const float invl = l_run[i] > 0.0f ? 1.0f / l_run[i] : 0.0f;
 #pragma unroll
             for (int e = 0; e < E; ++e) o[e] = __float2half_rn(acc[i][e] * invl);
@@ -377,6 +427,7 @@ __global__ void embedding_f16_kernel(const __half *__restrict__ w, const int64_t
     const int64_t row = blockIdx.x;
     if (row >= n_ids) return;
     pdl_wait();
+    pdl_trigger();
     int64_t id = ids[row];
     if (id < 0 || id >= vocab) {
         report_device_error(T2C_EINVAL);
@@ -393,6 +444,7 @@ __global__ void embedding_q4k_kernel(const uint8_t *__restrict__ w, const int64_
     const int64_t row = blockIdx.x;
     if (row >= n_ids) return;
     pdl_wait();
+    pdl_trigger();
     int64_t id = ids[row];
     if (id < 0 || id >= vocab) {
         report_device_error(T2C_EINVAL);
@@ -420,6 +472,7 @@ __global__ void embedding_q4k_kernel(const uint8_t *__restrict__ w, const int64_
 
 __global__ void add_kernel(const __half *__restrict__ x, const __half *__restrict__ r, __half *__restrict__ y, int64_t n) {
     pdl_wait();
+    pdl_trigger();
     const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i + 3 < n) {
         const float4 a = h4_to_f4(*reinterpret_cast<const uint2 *>(x + i));
@@ -434,6 +487,7 @@ __device__ __forceinline__ float silu_h(float g) { return __half2float(__float2h
 
 __global__ void swiglu_kernel(const __half *__restrict__ g, const __half *__restrict__ u, __half *__restrict__ y, int64_t n) {
     pdl_wait();
+    pdl_trigger();
     const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i + 3 < n) {
         const float4 a = h4_to_f4(*reinterpret_cast<const uint2 *>(g + i));
@@ -457,6 +511,7 @@ __global__ void __launch_bounds__(1024) token_select_kernel(const float *__restr
     __shared__ uint32_t st[32];
     const int64_t m = blockIdx.x;
     pdl_wait();
+    pdl_trigger();
     float best = -FLT_MAX;
     uint32_t tok = 0xffffffffu;
     for (int64_t g = threadIdx.x; g < G; g += blockDim.x) {
@@ -504,6 +559,7 @@ __global__ void token_store_kernel(const int64_t *__restrict__ next_token, const
     const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (b >= B) return;
     pdl_wait();
+    pdl_trigger();
     const int64_t index = index_dev ? index_dev[0] : index_value;
     if (index < 0 || index >= G) return;
     if (stop_on_eos && stopped[b]) return;
@@ -514,6 +570,7 @@ __global__ void token_store_kernel(const int64_t *__restrict__ next_token, const
 
 __global__ void advance_kernel(int32_t *positions, int64_t B, int32_t *token_index) {
     pdl_wait();
+    pdl_trigger();
     const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (b < B) positions[b] += 1;
     if (b == 0 && token_index) token_index[0] += 1;
@@ -592,6 +649,7 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
         return set_error(T2C_EINVAL, "attn_decode: bad shape");
     const int G = static_cast<int>(NH / NK);
     if (G > kMaxGroup) return set_error(T2C_EUNSUPPORTED, "attn_decode: group %d > %d", G, kMaxGroup);
+    if (splits > kMaxSplits) return set_error(T2C_EUNSUPPORTED, "attn_decode: splits %lld > %d", (long long)splits, kMaxSplits);
     if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cs % 8 || cb % 8 || ch % 8)
         return set_error(T2C_EINVAL, "attn_decode: cache rows must be 16-byte aligned");
     if (splits > 1) {
@@ -641,7 +699,8 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
 
 extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *v_cache, void *out,
                                 const int32_t *positions, int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t D,
-                                int64_t cb, int64_t cs, int64_t ch, void *stream) {
+                                int64_t cb, int64_t cs, int64_t ch, int64_t qb, int64_t qt, int64_t qh, int64_t ob,
+                                int64_t ot, int64_t oh, void *stream) {
     if (!q || !k_cache || !v_cache || !out || !positions) return set_error(T2C_EINVAL, "attn_prefill: NULL pointer");
     if (B <= 0 || T <= 0 || NH <= 0 || NK <= 0 || NH % NK) return set_error(T2C_EINVAL, "attn_prefill: bad shape");
     if (!aligned(k_cache, 16) || cs % 8 || cb % 8 || ch % 8)
@@ -654,12 +713,12 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
         return launch(attn_prefill_kernel<4>, grid, block, 0, s, static_cast<const __half *>(q),
                       static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache),
                       static_cast<__half *>(out), positions, static_cast<int>(T), static_cast<int>(NH),
-                      static_cast<int>(NK), cb, cs, ch, scale);
+                      static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh, scale);
     if (D == 64)
         return launch(attn_prefill_kernel<2>, grid, block, 0, s, static_cast<const __half *>(q),
                       static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache),
                       static_cast<__half *>(out), positions, static_cast<int>(T), static_cast<int>(NH),
-                      static_cast<int>(NK), cb, cs, ch, scale);
+                      static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh, scale);
     return set_error(T2C_EUNSUPPORTED, "attn_prefill: D=%lld", (long long)D);
 }
 

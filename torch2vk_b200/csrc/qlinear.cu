@@ -596,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, (MT == 1 ? 5 : 2)) qmv_direct_kernel
     float *red = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
 
     pdl_wait();
-    prepare_x<MT, kThreads>(p, xh, xl, sx, xq16, meta, red);
     pdl_trigger();
+    prepare_x<MT, kThreads>(p, xh, xl, sx, xq16, meta, red);
 
     const XPlanes xp{xh, xl, sx, xq16, meta, padded_k(K)};
     const int lane = threadIdx.x & 31;
@@ -949,8 +949,8 @@ __global__ void __launch_bounds__(kConsumerThreads) qmv_tma_kernel(const QParams
         }
     }
     pdl_wait();
-    prepare_x<MT, kConsumerThreads>(p, xh, xl, sx, xq16, meta, red);  // ends with __syncthreads
     pdl_trigger();
+    prepare_x<MT, kConsumerThreads>(p, xh, xl, sx, xq16, meta, red);  // ends with __syncthreads
     const XS x{smem_u32(xh), smem_u32(xl), smem_u32(meta), smem_u32(sx), smem_u32(xq16), padded_k(K), K >> 6,
                K >> 5};
     const bool swiglu = p.mode == MODE_SWIGLU;

@@ -1,0 +1,351 @@
+// Kernels that serve the remaining torch2vk shader contracts of the exported
+// (unfused) Qwen3 graph: strided 4-D copies (slice / cat / transpose /
+// contiguous views), broadcasting 4-D elementwise ops (add / mul / neg /
+// silu), the RoPE cos/sin table, table-driven RMSNorm + RoPE, KV-cache
+// writes at given positions, and the chunked greedy-select reduction.
+#include <float.h>
+
+#include "common.cuh"
+
+namespace t2c {
+namespace {
+
+struct Shape4 {
+    int64_t n[4];
+    int64_t a[4];  // strides of operand a / src (elements)
+    int64_t b[4];  // strides of operand b
+    int64_t o[4];  // strides of the output / dst
+};
+
+__device__ __forceinline__ void unravel(int64_t i, const int64_t n[4], int64_t idx[4]) {
+    idx[3] = i % n[3];
+    i /= n[3];
+    idx[2] = i % n[2];
+    i /= n[2];
+    idx[1] = i % n[1];
+    idx[0] = i / n[1];
+}
+
+template <typename T>
+__global__ void copy4d_kernel(const T *__restrict__ src, T *__restrict__ dst, Shape4 s, int64_t total) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t idx[4];
+        unravel(i, s.n, idx);
+        const int64_t si = idx[0] * s.a[0] + idx[1] * s.a[1] + idx[2] * s.a[2] + idx[3] * s.a[3];
+        const int64_t di = idx[0] * s.o[0] + idx[1] * s.o[1] + idx[2] * s.o[2] + idx[3] * s.o[3];
+        dst[di] = src[si];
+    }
+}
+
+__device__ __forceinline__ float ld_f(const void *p, int64_t i, int f32) {
+    return f32 ? static_cast<const float *>(p)[i] : __half2float(static_cast<const __half *>(p)[i]);
+}
+__device__ __forceinline__ void st_f(void *p, int64_t i, float v, int f32) {
+    if (f32) {
+        static_cast<float *>(p)[i] = v;
+    } else {
+        static_cast<__half *>(p)[i] = __float2half_rn(v);
+    }
+}
+
+enum { EW_ADD = 0, EW_MUL = 1, EW_NEG = 2, EW_SILU = 3 };
+
+__global__ void elementwise4d_kernel(int op, int f32, const void *__restrict__ a, const void *__restrict__ b,
+                                     void *__restrict__ out, Shape4 s, int64_t total) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t idx[4];
+        unravel(i, s.n, idx);
+        const float x = ld_f(a, idx[0] * s.a[0] + idx[1] * s.a[1] + idx[2] * s.a[2] + idx[3] * s.a[3], f32);
+        float r;
+        if (op == EW_ADD || op == EW_MUL) {
+            const float y = ld_f(b, idx[0] * s.b[0] + idx[1] * s.b[1] + idx[2] * s.b[2] + idx[3] * s.b[3], f32);
+            r = op == EW_ADD ? x + y : x * y;
+        } else if (op == EW_NEG) {
+            r = -x;
+        } else {
+            r = x / (1.0f + __expf(-x));
+        }
+        st_f(out, idx[0] * s.o[0] + idx[1] * s.o[1] + idx[2] * s.o[2] + idx[3] * s.o[3], r, f32);
+    }
+}
+
+// cos/sin [B, T, D] fp16: angle = (start + t) * theta^(-2 (d mod D/2) / D), times attention_scaling
+// (src/torch2vk/runtime/rope_table.py:31-121 arithmetic).
+__global__ void rope_table_kernel(__half *__restrict__ cos_out, __half *__restrict__ sin_out, int64_t B, int T, int D,
+                                  float theta, int64_t start, float scaling) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= B * T * D) return;
+    const int64_t td = i % (static_cast<int64_t>(T) * D);
+    const int t = static_cast<int>(td / D);
+    const int d = static_cast<int>(td - static_cast<int64_t>(t) * D);
+    const int f = d % (D / 2);
+    const float exponent = (2.0f * static_cast<float>(f)) / static_cast<float>(D);
+    const float inv_freq = powf(theta, -exponent);
+    const float angle = static_cast<float>(start + t) * inv_freq;
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    cos_out[i] = __float2half_rn(cs * scaling);
+    sin_out[i] = __float2half_rn(sn * scaling);
+}
+
+// One warp per (b, t, g) row of D values: RMSNorm with fp32 weight, then
+// rotate-half RoPE with fp16 cos/sin tables [B, T, D]; output addressed by
+// strides (b, g, t) so head-major [B, G, T, D] or token-major layouts work.
+template <int E>
+__global__ void rms_norm_rope_kernel(const __half *__restrict__ x, const float *__restrict__ w,
+                                     const __half *__restrict__ cos_t, const __half *__restrict__ sin_t,
+                                     __half *__restrict__ out, int B, int T, int G, int64_t ob, int64_t og,
+                                     int64_t ot, float eps) {
+    constexpr int D = E * 32;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= static_cast<int64_t>(B) * T * G) return;
+    pdl_wait();
+    pdl_trigger();
+    const int g = static_cast<int>(row % G);
+    const int t = static_cast<int>((row / G) % T);
+    const int b = static_cast<int>(row / (static_cast<int64_t>(G) * T));
+    const int d0 = lane * E;
+    float v[E];
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        v[e] = __half2float(x[row * D + d0 + e]);
+        ss += v[e] * v[e];
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = v[e] * inv * w[d0 + e];
+    const int64_t trow = (static_cast<int64_t>(b) * T + t) * D;
+    __half *o = out + b * ob + g * og + t * ot;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        const float c = __half2float(cos_t[trow + d0 + e]), s = __half2float(sin_t[trow + d0 + e]);
+        o[d0 + e] = __float2half_rn(lane < 16 ? v[e] * c - partner * s : v[e] * c + partner * s);
+    }
+}
+
+// cache[b, pos_t, h, :] = src[b, t, h, :] with pos_t = positions[t] (int64) or `position` + t.
+__global__ void kv_write_kernel(__half *__restrict__ cache, const __half *__restrict__ src,
+                                const int64_t *__restrict__ positions, int64_t position, int B, int H, int T, int D,
+                                int64_t cb, int64_t cs, int64_t ch, int64_t sb, int64_t st, int64_t sh, int64_t S) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(B) * H * T * D) return;
+    const int d = static_cast<int>(i % D);
+    int64_t r = i / D;
+    const int t = static_cast<int>(r % T);
+    r /= T;
+    const int h = static_cast<int>(r % H);
+    const int b = static_cast<int>(r / H);
+    const int64_t pos = positions ? positions[t] : position + t;
+    if (pos < 0 || pos >= S) {
+        report_device_error(T2C_EINVAL);
+        return;
+    }
+    cache[b * cb + pos * cs + h * ch + d] = src[b * sb + t * st + h * sh + d];
+}
+
+__device__ __forceinline__ bool better(float s, uint32_t t, float bs, uint32_t bt) {
+    return s > bs || (s == bs && t < bt);
+}
+
+// One CTA of 1024 threads per chunk of 1024 partials
+// (qwen3_token_select_reduce_f32.py:21-148 chunk stage).
+__global__ void __launch_bounds__(1024) select_chunks_kernel(const float *__restrict__ scores,
+                                                             const uint32_t *__restrict__ tokens, int64_t G,
+                                                             float *__restrict__ cs, uint32_t *__restrict__ ct) {
+    __shared__ float ss[32];
+    __shared__ uint32_t st[32];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 1024 + threadIdx.x;
+    float best = i < G ? scores[i] : -FLT_MAX;
+    uint32_t tok = i < G ? tokens[i] : 0xffffffffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float s = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t t = __shfl_xor_sync(0xffffffffu, tok, o);
+        if (better(s, t, best, tok)) {
+            best = s;
+            tok = t;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        ss[threadIdx.x >> 5] = best;
+        st[threadIdx.x >> 5] = tok;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 32; ++w)
+            if (better(ss[w], st[w], best, tok)) {
+                best = ss[w];
+                tok = st[w];
+            }
+        cs[blockIdx.x] = best;
+        ct[blockIdx.x] = tok;
+    }
+}
+
+template <typename Kernel, typename... Args>
+int launch(Kernel kernel, int64_t threads_total, int block, cudaStream_t stream, Args... args) {
+    int64_t grid = (threads_total + block - 1) / block;
+    if (grid < 1) grid = 1;
+    if (grid > 148LL * 64) grid = 148LL * 64;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(block);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args...);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "launch: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+int fill_shape(Shape4 &s, const int64_t *shape, const int64_t *a, const int64_t *b, const int64_t *o, int64_t &total) {
+    total = 1;
+    for (int i = 0; i < 4; ++i) {
+        if (shape[i] < 0) return set_error(T2C_EINVAL, "negative extent");
+        s.n[i] = shape[i] > 0 ? shape[i] : 1;
+        s.a[i] = a ? a[i] : 0;
+        s.b[i] = b ? b[i] : 0;
+        s.o[i] = o[i];
+        total *= shape[i];
+    }
+    return T2C_OK;
+}
+
+}  // namespace
+
+cudaError_t status_surface(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
+
+}  // namespace t2c
+
+using namespace t2c;
+
+extern "C" int t2c_copy4d(int elem_bytes, const void *src, const int64_t *src_strides, void *dst,
+                          const int64_t *dst_strides, const int64_t *shape, void *stream) {
+    if (!src || !dst || !src_strides || !dst_strides || !shape) return set_error(T2C_EINVAL, "copy4d: NULL pointer");
+    Shape4 s;
+    int64_t total = 0;
+    int rc = fill_shape(s, shape, src_strides, nullptr, dst_strides, total);
+    if (rc) return rc;
+    if (total == 0) return T2C_OK;
+    const cudaStream_t st = as_stream(stream);
+    switch (elem_bytes) {
+        case 2: return launch(copy4d_kernel<uint16_t>, total, 256, st, static_cast<const uint16_t *>(src),
+                              static_cast<uint16_t *>(dst), s, total);
+        case 4: return launch(copy4d_kernel<uint32_t>, total, 256, st, static_cast<const uint32_t *>(src),
+                              static_cast<uint32_t *>(dst), s, total);
+        case 8: return launch(copy4d_kernel<uint64_t>, total, 256, st, static_cast<const uint64_t *>(src),
+                              static_cast<uint64_t *>(dst), s, total);
+        case 1: return launch(copy4d_kernel<uint8_t>, total, 256, st, static_cast<const uint8_t *>(src),
+                              static_cast<uint8_t *>(dst), s, total);
+        default: return set_error(T2C_EUNSUPPORTED, "copy4d: element size %d", elem_bytes);
+    }
+}
+
+extern "C" int t2c_elementwise4d(int op, int is_f32, const void *a, const int64_t *a_strides, const void *b,
+                                 const int64_t *b_strides, void *out, const int64_t *out_strides, const int64_t *shape,
+                                 void *stream) {
+    if (!a || !out || !a_strides || !out_strides || !shape) return set_error(T2C_EINVAL, "elementwise4d: NULL pointer");
+    if (op < EW_ADD || op > EW_SILU) return set_error(T2C_EINVAL, "elementwise4d: op %d", op);
+    if ((op == EW_ADD || op == EW_MUL) && (!b || !b_strides)) return set_error(T2C_EINVAL, "elementwise4d: b is NULL");
+    Shape4 s;
+    int64_t total = 0;
+    int rc = fill_shape(s, shape, a_strides, b_strides, out_strides, total);
+    if (rc) return rc;
+    if (total == 0) return T2C_OK;
+    return launch(elementwise4d_kernel, total, 256, as_stream(stream), op, is_f32, a, b, out, s, total);
+}
+
+extern "C" int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                              int64_t start_position, float attention_scaling, void *stream) {
+    if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table: bad arguments");
+    return launch(rope_table_kernel, B * T * D, 256, as_stream(stream), static_cast<__half *>(cos_out),
+                  static_cast<__half *>(sin_out), B, static_cast<int>(T), static_cast<int>(D), theta, start_position,
+                  attention_scaling);
+}
+
+extern "C" int t2c_rms_norm_rope(const void *x, const float *w, const void *cos_t, const void *sin_t, void *out,
+                                 int64_t B, int64_t T, int64_t G, int64_t D, int64_t out_b_stride, int64_t out_g_stride,
+                                 int64_t out_t_stride, float eps, void *stream) {
+    if (!x || !w || !cos_t || !sin_t || !out) return set_error(T2C_EINVAL, "rms_norm_rope: NULL pointer");
+    if (B <= 0 || T <= 0 || G <= 0) return set_error(T2C_EINVAL, "rms_norm_rope: bad shape");
+    const int64_t rows = B * T * G;
+    const int warps = 8;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + warps - 1) / warps));
+    cfg.blockDim = dim3(warps * 32);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err;
+    const __half *xp = static_cast<const __half *>(x);
+    const __half *cp = static_cast<const __half *>(cos_t);
+    const __half *sp = static_cast<const __half *>(sin_t);
+    __half *op = static_cast<__half *>(out);
+    if (D == 128) {
+        err = cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<4>, xp, w, cp, sp, op, static_cast<int>(B), static_cast<int>(T),
+                                 static_cast<int>(G), out_b_stride, out_g_stride, out_t_stride, eps);
+    } else if (D == 64) {
+        err = cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<2>, xp, w, cp, sp, op, static_cast<int>(B), static_cast<int>(T),
+                                 static_cast<int>(G), out_b_stride, out_g_stride, out_t_stride, eps);
+    } else {
+        return set_error(T2C_EUNSUPPORTED, "rms_norm_rope: D=%lld", (long long)D);
+    }
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "rms_norm_rope: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+extern "C" int t2c_kv_cache_write(void *cache, const void *src, const int64_t *positions, int64_t position, int64_t B,
+                                  int64_t H, int64_t T, int64_t D, int64_t S, int64_t cache_b_stride,
+                                  int64_t cache_s_stride, int64_t cache_h_stride, int64_t src_b_stride,
+                                  int64_t src_t_stride, int64_t src_h_stride, void *stream) {
+    if (!cache || !src) return set_error(T2C_EINVAL, "kv_cache_write: NULL pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || D <= 0 || S <= 0) return set_error(T2C_EINVAL, "kv_cache_write: bad shape");
+    if (!positions && (position < 0 || position + T > S))
+        return set_error(T2C_EINVAL, "kv_cache_write: position %lld + %lld outside cache of %lld", (long long)position,
+                         (long long)T, (long long)S);
+    return launch(kv_write_kernel, B * H * T * D, 256, as_stream(stream), static_cast<__half *>(cache),
+                  static_cast<const __half *>(src), positions, position, static_cast<int>(B), static_cast<int>(H),
+                  static_cast<int>(T), static_cast<int>(D), cache_b_stride, cache_s_stride, cache_h_stride,
+                  src_b_stride, src_t_stride, src_h_stride, S);
+}
+
+extern "C" int t2c_token_select_chunks(const float *scores, const uint32_t *tokens, int64_t G, float *chunk_scores,
+                                       uint32_t *chunk_tokens, void *stream) {
+    if (!scores || !tokens || !chunk_scores || !chunk_tokens || G <= 0)
+        return set_error(T2C_EINVAL, "token_select_chunks: bad arguments");
+    const int64_t chunks = (G + 1023) / 1024;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(chunks));
+    cfg.blockDim = dim3(1024);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, select_chunks_kernel, scores, tokens, G, chunk_scores, chunk_tokens);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "token_select_chunks: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}

@@ -195,13 +195,22 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
 
 def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor, *,
                  batch: int, tokens: int, n_heads: int, n_kv: int, head_dim: int, layout: str = "token_major",
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal attention of `tokens` new queries (already cached) over positions 0..positions[b]+t."""
+                 q_layout: str = "token_major", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of `tokens` new queries (already cached) over positions 0..positions[b]+t.
+
+    q / out are token-major [B, T, NH, D] or, with q_layout="head_major", [B, NH, T, D].
+    """
     _check(q, torch.float16, "q")
     out = torch.empty_like(q) if out is None else out
     cb, cs, ch = cache_strides(k_cache, layout)
+    D = head_dim
+    if q_layout == "token_major":
+        qs = (tokens * n_heads * D, n_heads * D, D)
+    else:
+        qs = (n_heads * tokens * D, D, tokens * D)
     _lib.lib().call("t2c_attn_prefill", _lib.ptr(q), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(out),
-                    _lib.ptr(positions), batch, tokens, n_heads, n_kv, head_dim, cb, cs, ch, _lib.stream_ptr())
+                    _lib.ptr(positions), batch, tokens, n_heads, n_kv, head_dim, cb, cs, ch, *qs, *qs,
+                    _lib.stream_ptr())
     return out
 
 
@@ -277,3 +286,66 @@ def device_status(clear: bool = True) -> int:
     bits = ctypes.c_uint(0)
     _lib.lib().call("t2c_device_status", ctypes.addressof(bits), 1 if clear else 0, _lib.stream_ptr())
     return int(bits.value)
+
+
+def _i64x4(values) -> ctypes.Array:
+    vals = list(values)
+    if len(vals) != 4:
+        raise ValueError("expected 4 values")
+    return _lib.i64_array(vals)
+
+
+def copy4d(src: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    """dst[...] = src[...] for 4-D views (strides taken from the tensors)."""
+    if src.shape != dst.shape or src.dim() != 4 or src.element_size() != dst.element_size():
+        raise ValueError("copy4d needs equal 4-D shapes and element sizes")
+    _lib.lib().call("t2c_copy4d", src.element_size(), _lib.ptr(src), _i64x4(src.stride()), _lib.ptr(dst),
+                    _i64x4(dst.stride()), _i64x4(dst.shape), _lib.stream_ptr())
+    return dst
+
+
+EW_OPS = {"add": 0, "mul": 1, "neg": 2, "silu": 3}
+
+
+def elementwise4d(op: str, a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+    """out = op(a[, b]) over 4-D views; size-1 dims of a/b broadcast."""
+    if out.dim() != 4 or a.dim() != 4:
+        raise ValueError("elementwise4d needs 4-D views")
+
+    def bstrides(t: torch.Tensor) -> list[int]:
+        return [0 if t.shape[i] == 1 and out.shape[i] != 1 else t.stride(i) for i in range(4)]
+
+    is_f32 = 1 if out.dtype == torch.float32 else 0
+    _lib.lib().call("t2c_elementwise4d", EW_OPS[op], is_f32, _lib.ptr(a), _i64x4(bstrides(a)), _lib.ptr(b),
+                    _i64x4(bstrides(b)) if b is not None else None, _lib.ptr(out), _i64x4(out.stride()),
+                    _i64x4(out.shape), _lib.stream_ptr())
+    return out
+
+
+def rope_table(cos_out: torch.Tensor, sin_out: torch.Tensor, *, theta: float, start_position: int,
+               attention_scaling: float = 1.0) -> None:
+    b, t, d = cos_out.shape
+    _lib.lib().call("t2c_rope_table", _lib.ptr(cos_out), _lib.ptr(sin_out), b, t, d, float(theta), int(start_position),
+                    float(attention_scaling), _lib.stream_ptr())
+
+
+def rms_norm_rope(x: torch.Tensor, w: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor, out: torch.Tensor, *,
+                  out_strides: tuple[int, int, int], eps: float = 1e-6) -> torch.Tensor:
+    """x [B, T, G, D] -> rope(rmsnorm(x) * w), out addressed by strides (b, g, t)."""
+    b, t, g, d = x.shape
+    _lib.lib().call("t2c_rms_norm_rope", _lib.ptr(x), _lib.ptr(w), _lib.ptr(cos_t), _lib.ptr(sin_t), _lib.ptr(out),
+                    b, t, g, d, *out_strides, float(eps), _lib.stream_ptr())
+    return out
+
+
+def kv_cache_write(cache: torch.Tensor, src: torch.Tensor, *, cache_strides_bsh: tuple[int, int, int], seq_len: int,
+                   src_strides_bth: tuple[int, int, int], batch: int, heads: int, tokens: int, head_dim: int,
+                   positions: torch.Tensor | None = None, position: int = 0) -> None:
+    _lib.lib().call("t2c_kv_cache_write", _lib.ptr(cache), _lib.ptr(src), _lib.ptr(positions), int(position), batch,
+                    heads, tokens, head_dim, seq_len, *cache_strides_bsh, *src_strides_bth, _lib.stream_ptr())
+
+
+def token_select_chunks(scores: torch.Tensor, tokens: torch.Tensor, chunk_scores: torch.Tensor,
+                        chunk_tokens: torch.Tensor) -> None:
+    _lib.lib().call("t2c_token_select_chunks", _lib.ptr(scores), _lib.ptr(tokens), scores.numel(),
+                    _lib.ptr(chunk_scores), _lib.ptr(chunk_tokens), _lib.stream_ptr())

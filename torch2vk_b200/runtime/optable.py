@@ -1,0 +1,303 @@
+"""CUDA op table: contract class_name -> launcher of libt2c_sm100 kernels.
+
+RuntimeSession.dispatch validates a ShaderVariant call exactly like the
+reference dispatcher (src/torch2vk/runtime/dispatcher.py:28-172), then calls
+OPS[contract.class_name](rt, variant, buffers, symbols, push) on the
+session's CUDA stream.  `buffers` maps field names to the materialized torch
+CUDA tensors (declared shape and dtype), `symbols` holds the bound shape
+symbols and `push` the resolved push-constant values.  Each entry states the
+reference program whose semantics it reproduces.  A class without an entry
+raises NotImplementedError at dispatch; nothing falls back to a host path.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+
+from torch2vk_b200 import kernels
+
+OpFn = Callable[..., None]
+OPS: dict[str, OpFn] = {}
+
+
+def op(*class_names: str) -> Callable[[OpFn], OpFn]:
+    def deco(fn: OpFn) -> OpFn:
+        for name in class_names:
+            OPS[name] = fn
+        return fn
+    return deco
+
+
+def _positions(rt, batch: int, value: int) -> torch.Tensor:
+    return torch.full((batch,), int(value), dtype=torch.int32, device=rt.device)
+
+
+def _kind_of(weight: torch.Tensor, class_name: str) -> str:
+    if "Q6K" in class_name or "Q6_K" in class_name:
+        return "q6_k"
+    if "Q8_0" in class_name:
+        return "q8_0"
+    return "q4_k"
+
+
+# --------------------------------------------------------------------- linear
+@op("ExportLinearNobiasQ4KMatvecProgram", "ExportLinearNobiasQ4KProgram",
+    "ExportLinearNobiasQ6KMatvecProgram", "ExportLinearNobiasQ6KProgram",
+    "ExportLinearNobiasQ8_0MatvecProgram", "ExportLinearNobiasQ8_0Program")
+def _linear(rt, variant, b, s, pc):
+    """y = x @ deq(W)^T (linear_nobias_{q4_k,q6_k,q8_0}[_matvec]_f32.py)."""
+    kernels.linear(b["x"], b["weight"], _kind_of(b["weight"], variant.contract.class_name), s["K"], out=b["output"])
+
+
+@op("OptimizedLinearNobiasQ4KMatvecAddProgram", "OptimizedLinearNobiasQ6KMatvecAddProgram")
+def _linear_add(rt, variant, b, s, pc):
+    """y = residual + x @ deq(W)^T (linear_nobias_q{4,6}_k_matvec_add_f32.py:45-97)."""
+    kind = "q6_k" if "Q6K" in variant.contract.class_name else "q4_k"
+    kernels.linear(b["x"], b["weight"], kind, s["K"], residual=b["residual"], out=b["output"])
+
+
+@op("LinearNobiasQ4KQKVMatvecProgram", "LinearNobiasQ4QKQ6VMatvecProgram", "LinearNobiasQ4KQKMatvecProgram")
+def _linear_multi(rt, variant, b, s, pc):
+    """One x, two or three weight streams (linear_nobias_q4_k_qkv / q4_qk_q6_v / q4_k_qk)."""
+    parts = [p for p in ("q", "k", "v") if f"{p}_weight" in b]
+    kinds = {"q": "q4_k", "k": "q4_k",
+             "v": "q6_k" if variant.contract.class_name == "LinearNobiasQ4QKQ6VMatvecProgram" else "q4_k"}
+    kernels.linear_multi(b["x"], [(b[f"{p}_weight"], kinds[p]) for p in parts], s["K"],
+                         outs=[b[f"{p}_output"] for p in parts])
+
+
+# ---------------------------------------------------------------------- norms
+@op("ExportRmsNormF32WeightProgram", "OptimizedQwen3RmsNormMulF16F32Program")
+def _rms_norm(rt, variant, b, s, pc):
+    """fp16(x * rsqrt(mean(x^2) + eps) * w) per row (rms_norm_f32w_f32.py, rms_norm_mul_f16_f32.py:109)."""
+    x, out = b["x"], b["output"]
+    if x.numel() != out.numel() or b["weight"].numel() != x.shape[-1]:
+        raise ValueError(f"{variant.name}: output / weight do not match x {tuple(x.shape)}")
+    kernels.rms_norm(x, b["weight"], float(pc.get("eps", 1e-6)), out=out)
+
+
+@op("OptimizedQwen3RmsNormRopeTransposeF16Program")
+def _rms_norm_rope_transpose(rt, variant, b, s, pc):
+    """x [B,T,G,D] -> rope(rmsnorm(x)*w) written head-major [B,G,T,D] (rms_norm_rope_transpose_f16.py:22-146)."""
+    B, T, G, D = (s[k] for k in ("B", "T", "G", "D"))
+    kernels.rms_norm_rope(b["x"], b["weight"], b["cos"], b["sin"], b["output"],
+                          out_strides=(G * T * D, T * D, D))
+
+
+@op("RopeTableF32Program")
+def _rope_table(rt, variant, b, s, pc):
+    """cos/sin [B,T,D] fp16 at positions start_position + t (runtime/rope_table.py:31-121)."""
+    kernels.rope_table(b["cos"], b["sin"], theta=float(pc["theta"]), start_position=int(pc["start_position"]),
+                       attention_scaling=float(pc.get("attention_scaling", 1.0)))
+
+
+# ---------------------------------------------------------------- elementwise
+def _as4(t: torch.Tensor) -> torch.Tensor:
+    while t.dim() < 4:
+        t = t.unsqueeze(0)
+    return t
+
+
+@op("ExportAddF32Program")
+def _add(rt, variant, b, s, pc):
+    kernels.elementwise4d("add", _as4(b["x"]), _as4(b["y"]), _as4(b["output"]))
+
+
+@op("ExportMulF32Program", "ExportMulBroadcastProgram")
+def _mul(rt, variant, b, s, pc):
+    kernels.elementwise4d("mul", _as4(b["x"]), _as4(b["y"]), _as4(b["output"]))
+
+
+@op("ExportNegF32Program")
+def _neg(rt, variant, b, s, pc):
+    kernels.elementwise4d("neg", _as4(b["x"]), None, _as4(b["output"]))
+
+
+@op("ExportSiluF32Program")
+def _silu(rt, variant, b, s, pc):
+    kernels.elementwise4d("silu", _as4(b["x"]), None, _as4(b["output"]))
+
+
+@op("OptimizedQwen3SwiGLUF16Program")
+def _swiglu(rt, variant, b, s, pc):
+    """fp16(silu(gate)) * up (swiglu_f16.py:20-80)."""
+    kernels.swiglu(b["gate"], b["up"], out=b["output"])
+
+
+# ---------------------------------------------------------------------- views
+@op("ExportSliceProgram")
+def _slice(rt, variant, b, s, pc):
+    """out row r = x row r, columns OFFSET .. OFFSET+O3 (slice_f32*.py: IN_STRIDE / OUT_STRIDE / OFFSET)."""
+    x, out = b["x"], b["output"]
+    in_stride, out_stride, offset = int(pc["IN_STRIDE"]), int(pc["OUT_STRIDE"]), int(pc["OFFSET"])
+    rows = out.numel() // out_stride
+    if x.numel() != rows * in_stride or offset + out_stride > in_stride:
+        raise ValueError(f"{variant.name}: slice of {tuple(x.shape)} to {tuple(out.shape)} at {offset} is not a row slice")
+    src = x.reshape(1, 1, rows, in_stride)[..., offset:offset + out_stride]
+    kernels.copy4d(src, out.reshape(1, 1, rows, out_stride))
+
+
+@op("ExportCat2Program")
+def _cat2(rt, variant, b, s, pc):
+    """Last-dim concatenation (cat_2_f32.py: END0 / STRIDE0 / END1 / STRIDE1)."""
+    x0, x1, out = b["x0"], b["x1"], b["output"]
+    w0, w1, w = int(pc["STRIDE0"]), int(pc["STRIDE1"]), int(pc["OUT_STRIDE"])
+    rows = out.numel() // w
+    if w0 + w1 != w or x0.numel() != rows * w0 or x1.numel() != rows * w1:
+        raise ValueError(f"{variant.name}: cat of {tuple(x0.shape)} and {tuple(x1.shape)} to {tuple(out.shape)}")
+    o = out.reshape(1, 1, rows, w)
+    kernels.copy4d(x0.reshape(1, 1, rows, w0), o[..., :w0])
+    kernels.copy4d(x1.reshape(1, 1, rows, w1), o[..., w0:])
+
+
+@op("ExportTransposeProgram")
+def _transpose(rt, variant, b, s, pc):
+    """out[c0,c1,c2,c3] = x[...] with the variant's dim permutation (transpose_f32_*.py)."""
+    from torch2vk_b200.runtime.variants import TRANSPOSE_PERMUTATIONS
+
+    x, out = b["x"], b["output"]
+    perm = TRANSPOSE_PERMUTATIONS.get(variant.name)
+    if perm is None and variant.name.startswith("transpose_f32"):
+        perm = (0, 2, 1, 3)
+    if perm is None:
+        raise NotImplementedError(f"{variant.name}: unknown transpose permutation")
+    src = x.permute(*perm)
+    if tuple(src.shape) != tuple(out.shape):
+        raise ValueError(f"{variant.name}: permuted {tuple(src.shape)} != output {tuple(out.shape)}")
+    kernels.copy4d(src, out)
+
+
+@op("SliceLastTokenF16Program")
+def _slice_last(rt, variant, b, s, pc):
+    """out[b,0,:] = x[b,S-1,:] (slice_last_token_f16.py)."""
+    x, out = b["x"], b["output"]
+    kernels.copy4d(x[:, -1:, :].unsqueeze(0), out.unsqueeze(0))
+
+
+# ---------------------------------------------------------- KV cache / attention
+@op("ExportKvCacheWriteF16Program")
+def _kv_write(rt, variant, b, s, pc):
+    """cache[b,h,pos_t,:] = src[b,h,t,:], pos_t from cache_position[T] or push constant + t
+    (kv_cache_write_f16.py:22-92, kv_cache_write_decode_f16.py:23-85)."""
+    cache, src = b["cache"], b["src"]
+    B, H, S, D, T = (s[k] for k in ("B", "H", "S", "D", "T"))
+    pos_t = b.get("cache_position")
+    kernels.kv_cache_write(cache, src, cache_strides_bsh=(H * S * D, D, S * D), seq_len=S,
+                           src_strides_bth=(H * T * D, D, T * D), batch=B, heads=H, tokens=T, head_dim=D,
+                           positions=pos_t, position=int(pc.get("cache_position", 0)))
+
+
+@op("OptimizedQwen3TokenMajorKvCacheWriteF16PairProgram", "OptimizedQwen3TokenMajorKvCacheWriteF16TripleProgram")
+def _kv_write_token_major(rt, variant, b, s, pc):
+    """src [B,T,H,D] written into each token-major cache [B,S?,H,D] at cache_position[t]
+    (token_major_kv_cache_write_f16_{pair,triple}.py)."""
+    src, pos_t = b["src"], b["cache_position"]
+    B, H, D, T = (s[k] for k in ("B", "H", "D", "T"))
+    for c in ("a", "b", "c"):
+        cache = b.get(f"cache_{c}")
+        if cache is None:
+            continue
+        S = s[f"S{c.upper()}"]
+        kernels.kv_cache_write(cache, src, cache_strides_bsh=(S * H * D, H * D, D), seq_len=S,
+                               src_strides_bth=(T * H * D, H * D, D), batch=B, heads=H, tokens=T, head_dim=D,
+                               positions=pos_t)
+
+
+@op("ExportSdpaProgram")
+def _sdpa_causal(rt, variant, b, s, pc):
+    """Causal GQA attention, q [B,NH,T,D] over k/v [B,NK,S,D] from position 0 (sdpa_causal_f32.py:22-142)."""
+    if "causal" not in variant.name:
+        raise NotImplementedError(f"{variant.name}: only causal ExportSdpaProgram variants are served")
+    q, k, v, out = b["q"], b["k"], b["v"], b["output"]
+    B, NH, T, D = q.shape
+    NK, S = k.shape[1], k.shape[2]
+    if S < T or tuple(out.shape) != tuple(q.shape) or tuple(v.shape) != tuple(k.shape):
+        raise ValueError(f"{variant.name}: q {tuple(q.shape)} k {tuple(k.shape)} out {tuple(out.shape)}")
+    kernels.attn_prefill(q, k, v, _positions(rt, B, 0), batch=B, tokens=T, n_heads=NH, n_kv=NK, head_dim=D,
+                         layout="head_major", q_layout="head_major", out=out)
+
+
+def _decode_splits(max_len: int) -> int:
+    return max(1, min(64, max_len // 256))
+
+
+@op("ExportSdpaDecodeCacheF16Program")
+def _sdpa_decode(rt, variant, b, s, pc):
+    """One query per head over head-major cache[0..cache_position] (sdpa_decode_cache_f16.py:22-136)."""
+    q, k, v, out = b["q"], b["k"], b["v"], b["output"]
+    B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
+    if s["T"] != 1:
+        raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
+    pos = min(int(pc["cache_position"]), S - 1)
+    kernels.attn_decode(q, k, v, _positions(rt, B, pos), batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                        splits=_decode_splits(pos + 1), layout="head_major", out=out)
+
+
+@op("SdpaDecodeCacheWriteF32Program")
+def _sdpa_decode_write(rt, variant, b, s, pc):
+    """Write new k (head-major) / v (token-major) at cache_position into token-major caches, then
+    attend over 0..cache_position (sdpa_decode_cache_write_f32.py:22-171)."""
+    q, out = b["q"], b["output"]
+    B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
+    if s["T"] != 1:
+        raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
+    pos = int(pc["cache_position"])
+    if pos < S:
+        cs = (S * NK * D, NK * D, D)
+        kernels.kv_cache_write(b["k_cache"], b["new_k"], cache_strides_bsh=cs, seq_len=S,
+                               src_strides_bth=(NK * D, D, D), batch=B, heads=NK, tokens=1, head_dim=D, position=pos)
+        kernels.kv_cache_write(b["v_cache"], b["new_v"], cache_strides_bsh=cs, seq_len=S,
+                               src_strides_bth=(NK * D, NK * D, D), batch=B, heads=NK, tokens=1, head_dim=D,
+                               position=pos)
+    last = min(pos, S - 1)
+    kernels.attn_decode(q, b["k_cache"], b["v_cache"], _positions(rt, B, last), batch=B, n_heads=NH, n_kv=NK,
+                        head_dim=D, max_len=S, splits=_decode_splits(last + 1), layout="token_major", out=out)
+
+
+# -------------------------------------------------------- embedding / LM head / tokens
+@op("ExportEmbeddingQ4_KProgram")
+def _embedding_q4k(rt, variant, b, s, pc):
+    """out[i,:] = deq(W)[ids[i],:] (embedding_q4_k_f32.py:25-121)."""
+    w, ids, out = b["weight"], b["indices"], b["output"]
+    kernels.embedding(w, "q4_k", ids, s["H"], w.shape[0], out=out)
+
+
+@op("LmHeadQ6KArgmaxPartialF16Program")
+def _lm_head(rt, variant, b, s, pc):
+    """Per-4-row best (score, token) of x @ deq(W)^T (lm_head_q6_k_argmax_partial_f16.py)."""
+    G = s["G"]
+    if G != (s["N"] + 3) // 4:
+        raise ValueError(f"{variant.name}: G={G} but ceil(N/4)={(s['N'] + 3) // 4}")
+    kernels.lm_head_argmax(b["x"].reshape(1, s["K"]), b["weight"], "q6_k", s["K"],
+                           partial_scores=b["partial_scores"].view(1, G),
+                           partial_tokens=b["partial_tokens"].view(torch.int32).view(1, G))
+
+
+@op("Qwen3TokenSelectReduceChunksF32Program")
+def _select_chunks(rt, variant, b, s, pc):
+    """Chunks of 1024 partials -> one (score, token) each (qwen3_token_select_reduce_f32.py:21-120)."""
+    kernels.token_select_chunks(b["scores"], b["tokens"].view(torch.int32), b["chunk_scores"],
+                                b["chunk_tokens"].view(torch.int32))
+
+
+@op("Qwen3TokenSelectReduceF32Program")
+def _select(rt, variant, b, s, pc):
+    """Final argmax (lowest token id on ties) and EOS flag (qwen3_token_select_reduce_f32.py:122-241)."""
+    G = s["G"]
+    kernels.token_select(b["partial_scores"].view(1, G), b["partial_tokens"].view(torch.int32).view(1, G),
+                         b["eos_token_ids"], next_token=b["next_token"].view(1),
+                         done=b["done"].view(torch.int32).view(1))
+
+
+@op("Qwen3TokenStoreEosProgram", "Qwen3TokenStoreEosF32Program")
+def _store(rt, variant, b, s, pc):
+    """generated_tokens[token_index] = next_token unless stopped; EOS stops (qwen3_token_store.py)."""
+    kernels.token_store(b["next_token"].view(1), b["done"].view(torch.int32).view(1), b["generated_tokens"],
+                        b["generated_length"].view(torch.int32).view(1), b["stopped"].view(torch.int32).view(1),
+                        token_index=int(pc["token_index"]), stop_on_eos=bool(pc.get("stop_on_eos", 1)))
+
+
+def served_class_names() -> tuple[str, ...]:
+    return tuple(sorted(OPS))
