@@ -217,6 +217,58 @@ def run_reference(args, world: int, rank: int) -> None:
 
 
 # -------------------------------------------------------------------- main
+def run_profile(args, local: int) -> None:
+    """Workloads for ncu, bracketed by cudaProfilerStart/Stop (use --profile-from-start off).
+
+    decode: the Qwen3-8B bs1 decode graph (Q4_K linears, Q6_K head), --steps replays.
+    qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
+            in turn (226 MB, larger than L2), --steps launches.
+    """
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, Qwen3Runner, random_weights
+
+    cfg = Qwen3Config.qwen3_8b()
+    dev = torch.device("cuda", local)
+    cudart = torch.cuda.cudart()
+    if args.profile == "decode":
+        weights = random_weights(cfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
+        runner = Qwen3Runner(cfg, weights, batch=1, max_seq=PROMPT + args.steps + args.warmup + 64,
+                             max_new_tokens=args.steps + args.warmup + 8)
+        prompt = torch.randint(0, cfg.vocab, (1, PROMPT), generator=torch.Generator().manual_seed(0)).to(dev)
+        runner.prefill(prompt)
+        runner.capture()
+        for _ in range(args.warmup):
+            runner.step()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for _ in range(args.steps):
+            runner.step()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    else:
+        gen = torch.Generator(device=dev).manual_seed(0)
+        pairs = []
+        for _ in range(4):
+            g = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
+            u = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
+            pairs.append((g, u))
+        x = torch.randn(1, cfg.hidden, device=dev, dtype=torch.float16)
+        nw = torch.ones(cfg.hidden, device=dev)
+        out = torch.empty(1, cfg.intermediate, device=dev, dtype=torch.float16)
+        for i in range(args.warmup):
+            g, u = pairs[i % 4]
+            kernels.linear_swiglu(x, g, u, "q4_k", cfg.hidden, norm_weight=nw, out=out)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for i in range(args.steps):
+            g, u = pairs[i % 4]
+            kernels.linear_swiglu(x, g, u, "q4_k", cfg.hidden, norm_weight=nw, out=out)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    if kernels.device_status() != 0:
+        raise SystemExit("device status bit set")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -224,12 +276,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["decode", "qmv"], default=None,
+                    help="profiling workload only (no JSON): the profiler range opens after warm-up")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.profile:
+        run_profile(args, local)
         return
 
     from torch2vk_b200 import kernels

@@ -147,12 +147,15 @@ def test_embedding_f16_and_q4k(oracle):
     assert np.array_equal(out.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("kind,K", [("q6_k", 1024), ("q6_k", 4096), ("q4_k", 1024)])
-def test_lm_head_argmax_and_select(oracle, kind, K):
+# (q6_k, 512) and (q8_0, 1088) have rows whose byte length is not a multiple of
+# 16, so they take the direct (non-bulk-copy) kernel; N = 4099 leaves a ragged group.
+@pytest.mark.parametrize("kind,K,N", [("q6_k", 1024, 4112), ("q6_k", 4096, 4112), ("q4_k", 1024, 4112),
+                                      ("q6_k", 512, 4099), ("q8_0", 1088, 4099)])
+def test_lm_head_argmax_and_select(oracle, kind, K, N):
     from torch2vk_b200 import kernels
 
     rng = np.random.default_rng(5)
-    N, M = 4096 + 16, 2
+    M = 2
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     w[777] = w[123]          # an exact duplicate row: tie -> lower id
     packed = oracle.quantize(w, kind)

@@ -650,6 +650,35 @@ __global__ void __launch_bounds__(kThreads, (MT == 1 ? 5 : 2)) qmv_direct_kernel
             for (int u = sub_lane; u < p.units; u += lpr) run_unit<MT, kDirectRows, false>(fmt, rows, u, 0, K, xp, acc);
         }
         reduce_lanes<MT, kDirectRows>(acc, lpr);
+        if (p.mode == MODE_ARGMAX) {
+            // Rows 4g..4g+3 are row-sets 2g and 2g+1, held by sub-warps sub and
+            // sub+1 of this warp (lpr <= 16, so row-set parity = sub parity).
+            // The even sub-warp merges its partner's best; ties keep the lower id.
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                float best = -INFINITY;
+                uint32_t tok = 0xffffffffu;
+                if (rs < p.total_rowsets && m < p.M) {
+                    best = acc[0][m];
+                    tok = static_cast<uint32_t>(n[0]);
+                    if (n[1] >= 0 && acc[1][m] > best) {
+                        best = acc[1][m];
+                        tok = static_cast<uint32_t>(n[1]);
+                    }
+                }
+                const float other = __shfl_down_sync(0xffffffffu, best, lpr);
+                const uint32_t other_tok = __shfl_down_sync(0xffffffffu, tok, lpr);
+                if (sub_lane == 0 && (sub & 1) == 0 && rs < p.total_rowsets && m < p.M) {
+                    if (other_tok != 0xffffffffu && other > best) {
+                        best = other;
+                        tok = other_tok;
+                    }
+                    p.ps[m * p.G + (rs >> 1)] = best;
+                    p.pt[m * p.G + (rs >> 1)] = tok;
+                }
+            }
+            continue;
+        }
         if (sub_lane == 0 && rs < p.total_rowsets) store_rows<MT, kDirectRows>(p, p.s[si], n, acc, swiglu);
     }
 }
@@ -1296,10 +1325,10 @@ int run_linear(QParams p, int64_t M, cudaStream_t stream) {
         p.stage_bytes = stage_bytes;
         return launch_chunked(p, M, true, stream);
     }
-    if (p.mode == MODE_ARGMAX) return set_error(T2C_EUNSUPPORTED, "lm_head_argmax: weight layout cannot be streamed");
-    // direct kernel: row-sets of 2 rows (ROWS) or 1 output (SWIGLU)
+    // direct kernel: row-sets of 2 rows (ROWS, ARGMAX) or 1 output (SWIGLU)
     p.units = p.K / 64;
     p.lpr = lanes_for(p.units);
+    if (p.mode == MODE_ARGMAX && p.lpr > 16) p.lpr = 16;  // row-set pairs share a warp
     int64_t rs = 0;
     for (int i = 0; i < p.nstreams; ++i) {
         p.s[i].rs_begin = rs;
