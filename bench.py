@@ -59,7 +59,7 @@ class ClockSampler:
     def __enter__(self) -> "ClockSampler":
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
@@ -221,6 +221,8 @@ def run_profile(args, local: int) -> None:
     """Workloads for ncu, bracketed by cudaProfilerStart/Stop (use --profile-from-start off).
 
     decode: the Qwen3-8B bs1 decode graph (Q4_K linears, Q6_K head), --steps replays.
+    attn:   the fused decode attention of Qwen3-8B (32 Q / 8 KV heads, D 128) at position 1040 over
+            48 layers' KV caches in turn (288 MB, larger than L2), --steps launches.
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
             in turn (226 MB, larger than L2), --steps launches.
     """
@@ -243,6 +245,35 @@ def run_profile(args, local: int) -> None:
         cudart.cudaProfilerStart()
         for _ in range(args.steps):
             runner.step()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "attn":
+        B, NH, NK, D, S, L = 1, cfg.heads, cfg.kv_heads, cfg.head_dim, 1536, 48
+        caches = [(torch.randn(B, S, NK, D, device=dev, dtype=torch.float16),
+                   torch.randn(B, S, NK, D, device=dev, dtype=torch.float16)) for _ in range(L)]
+        q = torch.randn(B, NH * D, device=dev, dtype=torch.float16)
+        k = torch.randn(B, NK * D, device=dev, dtype=torch.float16)
+        v = torch.randn(B, NK * D, device=dev, dtype=torch.float16)
+        w = torch.ones(D, device=dev)
+        from torch2vk_b200.qwen3 import inv_freq
+
+        inv = inv_freq(cfg).to(dev)
+        pos = torch.full((B,), 1040, device=dev, dtype=torch.int32)
+        splits = max(1, min(32, (PROMPT + 400 + 10 + 64) // 64))
+        ws = kernels.attn_decode_fused_workspace(B, NH, NK, D, splits, dev)
+        out = torch.empty(B, NH * D, device=dev, dtype=torch.float16)
+
+        def one(i: int) -> None:
+            kc, vc = caches[i % L]
+            kernels.attn_decode_fused(q, k, v, w, w, inv, kc, vc, pos, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
+                                      splits=splits, workspace=ws, out=out)
+
+        for i in range(args.warmup):
+            one(i)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for i in range(args.steps):
+            one(i)
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
     else:
@@ -276,7 +307,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "qmv"], default=None,
+    ap.add_argument("--profile", choices=["decode", "qmv", "attn"], default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -374,7 +405,7 @@ def main() -> None:
     reps32 = max(8, steps // 8)
     t_step32 = max_over_ranks(events_time(big.step, reps32, stream), world)
 
-    per_step_launches = cfg.layers * (6 + (1 if big.decode_splits > 1 else 0)) + 5
+    per_step_launches = cfg.layers * (5 if big.fused_attention else 6 + (1 if big.decode_splits > 1 else 0)) + 5
     clk = clocks.summary()
     line = {
         "metric": "qwen3_8b_int4_decode_tok_s_bs1",

@@ -173,6 +173,30 @@ int t2c_attn_decode(const void *q, const void *k_cache, const void *v_cache, voi
                     float *workspace, int64_t workspace_floats, void *stream);
 
 /*
+ * One decode step of attention in one launch (T = 1 query per batch row):
+ * q / k RMSNorm (fp32 weights q_w / k_w [D]) and RoPE (inv_freq [D/2]) of the
+ * raw projections, the new k / v written into the caches at positions[b],
+ * split-K attention over cache positions 0..positions[b] and the split
+ * combine.  Replaces the chain rms_norm_rope_transpose_f16 ->
+ * token_major_kv_cache_write_f16_pair -> sdpa_decode_cache_write_f32
+ * (src/models/optimized_qwen3/dispatch/decode_layer.py:36-128) and
+ * sdpa_decode_cache_f16.py:22-136.  q_in [B, NH*D], k_in / v_in [B, NK*D] with
+ * batch strides q_sb / k_sb / v_sb (elements); out [B, NH*D] with o_sb.  D = 128.
+ * max_len: cache rows per sequence; a position outside [0, max_len) makes the
+ * kernel touch nothing and set T2C_EINVAL in t2c_device_status.
+ * splits > 1 needs t2c_attn_decode_fused_workspace(...) words of workspace whose
+ * last B*NH words (arrival counters) are zero before the first call; every
+ * call leaves them zero.
+ */
+int t2c_attn_decode_fused(const void *q_in, const void *k_in, const void *v_in, int64_t q_sb, int64_t k_sb,
+                          int64_t v_sb, const float *q_w, const float *k_w, const float *inv_freq, float eps,
+                          void *k_cache, void *v_cache, int64_t cache_b_stride, int64_t cache_s_stride,
+                          int64_t cache_h_stride, void *out, int64_t o_sb, const int32_t *positions, int64_t B,
+                          int64_t NH, int64_t NK, int64_t D, int64_t max_len, int64_t splits, float *workspace,
+                          int64_t workspace_floats, void *stream);
+int64_t t2c_attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits);
+
+/*
  * t2c_attn_decode for callers that cannot allocate device memory: the same
  * split-K decode attention, with its split partials kept in a fixed 16 MiB
  * device array inside the library instead of a caller workspace.  Meant for

@@ -217,3 +217,58 @@ def test_elementwise_add_swiglu():
     _close(kernels.add(a, b), a.float() + b.float())
     silu = (a.float() / (1 + torch.exp(-a.float()))).half().float()
     _close(kernels.swiglu(a, b), silu * b.float())
+
+
+@pytest.mark.parametrize("layout", ["token_major", "head_major"])
+@pytest.mark.parametrize("NH,NK,splits", [(32, 8, 1), (32, 8, 5), (32, 8, 23), (16, 8, 7), (8, 8, 3), (64, 8, 9)])
+def test_attn_decode_fused_matches_unfused_chain(NH, NK, splits, layout):
+    """One-launch decode attention == qk_norm_rope_cache + attn_decode (same caches after, outputs close)."""
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, inv_freq
+
+    torch.manual_seed(7)
+    B, D, S = 3, 128, 700
+    cfg = Qwen3Config.qwen3_0_6b()
+    inv = inv_freq(cfg).cuda()
+    q = torch.randn(B, NH * D, device="cuda", dtype=torch.float16)
+    k = torch.randn(B, NK * D, device="cuda", dtype=torch.float16)
+    v = torch.randn(B, NK * D, device="cuda", dtype=torch.float16)
+    qw = 1 + 0.1 * torch.randn(D, device="cuda")
+    kw = 1 + 0.1 * torch.randn(D, device="cuda")
+    shape = (B, S, NK, D) if layout == "token_major" else (B, NK, S, D)
+    kc = torch.randn(shape, device="cuda", dtype=torch.float16)
+    vc = torch.randn(shape, device="cuda", dtype=torch.float16)
+    positions = torch.tensor([0, 255, 699], device="cuda", dtype=torch.int32)
+    kc2, vc2 = kc.clone(), vc.clone()
+    qr = kernels.qk_norm_rope_cache(q, k, v, qw, kw, kc2, vc2, positions, inv, batch=B, tokens=1, n_heads=NH,
+                                    n_kv=NK, head_dim=D, layout=layout)
+    ref = kernels.attn_decode(qr, kc2, vc2, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                              splits=1, layout=layout)
+    ws = kernels.attn_decode_fused_workspace(B, NH, NK, D, splits)
+    for _ in range(2):  # the second call checks that the arrival counters were reset
+        out = kernels.attn_decode_fused(q, k, v, qw, kw, inv, kc, vc, positions, batch=B, n_heads=NH, n_kv=NK,
+                                        head_dim=D, splits=splits, workspace=ws, layout=layout)
+        torch.cuda.synchronize()
+        assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+        _close(out, ref.float(), rel=2e-3, abs_=2e-3)
+        if ws is not None:
+            assert int(ws[-B * NH:].view(torch.int32).abs().sum()) == 0
+    assert kernels.device_status() == 0
+
+
+def test_attn_decode_fused_rejects_bad_arguments():
+    from torch2vk_b200 import kernels
+    from torch2vk_b200._lib import T2CError
+
+    B, NH, NK, D = 1, 32, 8, 128
+    t = torch.zeros(B, NH * D, device="cuda", dtype=torch.float16)
+    kv = torch.zeros(B, NK * D, device="cuda", dtype=torch.float16)
+    c = torch.zeros(B, 64, NK, D, device="cuda", dtype=torch.float16)
+    w = torch.ones(D, device="cuda")
+    pos = torch.zeros(B, device="cuda", dtype=torch.int32)
+    with pytest.raises(T2CError, match="workspace"):
+        kernels.attn_decode_fused(t, kv, kv, w, w, w[:64], c, c, pos, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
+                                  splits=4, workspace=None)
+    with pytest.raises(T2CError, match="D=64"):
+        kernels.attn_decode_fused(t, kv, kv, w, w, w[:64], c, c, pos, batch=B, n_heads=NH * 2, n_kv=NK * 2,
+                                  head_dim=64, splits=1, workspace=None)

@@ -10,6 +10,8 @@ fp16 store, so the bound is |err| <= 2e-3 * (|ref| + rms(ref)).
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -142,3 +144,48 @@ def test_linear_rejects_bad_shapes():
         kernels.linear(x, w, "q4_k", 300)
     with pytest.raises(_lib.T2CError):
         _lib.lib().call("t2c_linear", _lib.Q4_K, _lib.ptr(x), None, None, _lib.ptr(x), 1, 4, 256, _lib.stream_ptr())
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_linear_multi_q4k_tensor_core_path(oracle, m):
+    """All-Q4_K QKV (the tensor-core kernel) with the fused RMSNorm prologue and ragged row counts."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(17)
+    k = 2048
+    specs = [2064, 1000, 24]
+    packed = [oracle.quantize(_weights(rng, n, k), "q4_k") for n in specs]
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    nw = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    xf = x.astype(np.float32)
+    xn = xf / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + 1e-6) * nw
+    outs = kernels.linear_multi(torch.from_numpy(x).cuda(), [(torch.from_numpy(p).cuda(), "q4_k") for p in packed], k,
+                                norm_weight=torch.from_numpy(nw).cuda(), eps=1e-6)
+    for out, p in zip(outs, packed):
+        ref = xn.astype(np.float64) @ oracle.dequantize(p, "q4_k", k).astype(np.float64).T
+        _tol_check(out.float().cpu().numpy(), ref)
+
+
+def test_q4k_dp4a_kernel_still_matches(tmp_path):
+    """The dp4a streamed kernel (forced with T2C_QMV_DP4A=1) on the shapes the tensor-core kernel now serves."""
+    import os
+    import subprocess
+    import sys
+
+    script = tmp_path / "dp4a.py"
+    script.write_text(
+        "import numpy as np, torch\n"
+        "from oracle import oracle\n"
+        "from torch2vk_b200 import kernels\n"
+        "rng = np.random.default_rng(2)\n"
+        "for m, n, k in ((1, 1030, 2048), (4, 96, 3072)):\n"
+        "    p = oracle.quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32), 'q4_k')\n"
+        "    x = rng.standard_normal((m, k)).astype(np.float16)\n"
+        "    ref = oracle.matvec(p, 'q4_k', x)\n"
+        "    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(p).cuda(), 'q4_k', k).float().cpu().numpy()\n"
+        "    rms = np.sqrt(np.mean(ref ** 2))\n"
+        "    assert np.all(np.abs(y - ref) <= 2e-3 * (np.abs(ref) + rms)), float(np.abs(y - ref).max())\n"
+        "print('ok')\n")
+    env = dict(os.environ, T2C_QMV_DP4A="1", PYTHONPATH=str(Path(__file__).resolve().parents[1]))
+    r = subprocess.run([sys.executable, str(script)], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]

@@ -47,6 +47,9 @@ _SIGNATURES: dict[str, list] = {
                                _i64, _i64, _i64, _vp, _f32, _vp],
     "t2c_attn_decode": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                         _i64, _vp],
+    "t2c_attn_decode_fused": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _c.c_float, _vp, _vp, _i64, _i64,
+                              _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp],
+    "t2c_attn_decode_fused_workspace": [_i64, _i64, _i64, _i64, _i64],
     "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i64, _vp],
     "t2c_copy4d": [_i32, _vp, _vp, _vp, _vp, _vp, _vp],
@@ -62,7 +65,7 @@ _SIGNATURES: dict[str, list] = {
     "t2c_advance_positions": [_vp, _i64, _vp, _vp],
     "t2c_attn_decode_static": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
 }
-_RESTYPES = {"t2c_last_error": _c.c_char_p}
+_RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64}
 
 
 class T2CError(RuntimeError):
@@ -86,7 +89,7 @@ class _Library:
         for name, argtypes in _SIGNATURES.items():
             fn = getattr(self.handle, name)
             fn.argtypes = argtypes
-            fn.restype = _c.c_int
+            fn.restype = _RESTYPES.get(name, _c.c_int)
 
     def call(self, name: str, *args) -> None:
         status = getattr(self.handle, name)(*args)

@@ -139,6 +139,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// 2-D tiled TMA load (no multicast) of a box at element coordinates (x, y) of the
+// tensor map `tmap` (a __grid_constant__ kernel parameter) into shared memory.
+// x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Device-side status word of this translation unit: kernels OR in 1 << T2C_E*
 // (e.g. T2C_ETIMEOUT after a bounded wait ran out).  Every .cu file with such
 // kernels exposes a reader (status_<file>) that t2c_device_status() combines.

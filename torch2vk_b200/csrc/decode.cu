@@ -316,6 +316,232 @@ __global__ void attn_combine_kernel(const float *__restrict__ ws, __half *__rest
     }
 }
 
+// ------------------------------------------- fused decode attention (T = 1)
+// One launch per layer for a decode step: q/k RMSNorm + RoPE, KV-cache write
+// of the new position, split-K attention and the split combine.
+// CTA = G warps on (batch b, kv head kh, split sp); warp g owns query head
+// kh*G + g over the CTA's cache positions [sp * chunk, min((sp+1) * chunk, len)),
+// chunk = ceil(len / splits) from the device-side length.  The G warps read
+// the same K / V rows (L1 shares them) and never wait for each other: no
+// CTA barrier anywhere.  Cache rows of earlier steps do not depend on the
+// preceding kernel, so the first K / V tile is requested before
+// griddepcontrol.wait; the raw q / k / v of this step (from the preceding QKV
+// matvec) are read after it.  In the CTA whose range holds the new position,
+// every warp computes the new k (normed, rotated) itself and warp 0 writes
+// k / v into the cache.  Splits leave (max, sum, acc) partials per head; the
+// last warp to arrive for a head (arrival counter) combines them and resets
+// the counter to zero.  Scores use base-2 exponentials with q pre-scaled by
+// log2(e) / sqrt(D).  Lane j scores position j of a 32-position tile (whole
+// K row per lane, q broadcast from shared memory); lanes split D for P V.
+__device__ __forceinline__ void norm_rope_lane(const uint2 raw, const float *__restrict__ w,
+                                               const float *__restrict__ inv_freq, int pos, float eps, int lane,
+                                               float r[4]) {
+    constexpr int D = 128;
+    const float4 f = h4_to_f4(raw);
+    float v[4] = {f.x, f.y, f.z, f.w};
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float inv = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = v[e] * inv * w[lane * 4 + e];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        float sn, cs_;
+        sincosf(static_cast<float>(pos) * inv_freq[(lane * 4 + e) & (D / 2 - 1)], &sn, &cs_);
+        r[e] = lane < 16 ? v[e] * cs_ - partner * sn : v[e] * cs_ + partner * sn;
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(G * 32) attn_decode_fused_kernel(
+    const __half *__restrict__ q_in, const __half *__restrict__ k_in, const __half *__restrict__ v_in, int64_t q_sb,
+    int64_t k_sb, int64_t v_sb, const float *__restrict__ q_w, const float *__restrict__ k_w,
+    const float *__restrict__ inv_freq, float eps, __half *kc, __half *vc, int64_t cb, int64_t cs, int64_t ch,
+    __half *__restrict__ out, int64_t o_sb, const int32_t *__restrict__ positions, int NK, int max_len, int splits,
+    float *__restrict__ ws, int *__restrict__ counters, float qscale) {
+    constexpr int D = 128, E = 4;
+    __shared__ __align__(16) float qs[G][D];
+    __shared__ __align__(16) float ps[G][32];
+    __shared__ __align__(16) __half knew[G][D];
+    __shared__ float cw[G][kMaxSplits];
+    const int sp = blockIdx.x % splits;
+    const int kh = (blockIdx.x / splits) % NK;
+    const int b = blockIdx.x / (splits * NK);
+    const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NH = NK * G;
+    const int h = kh * G + g;
+    const int pos = positions[b];
+    if (pos < 0 || pos >= max_len) {  // no cache row to write: report, touch nothing
+        pdl_wait();
+        pdl_trigger();
+        if (threadIdx.x == 0) report_device_error(T2C_EINVAL);
+        return;
+    }
+    const int len = pos + 1;
+    const int chunk = (len + splits - 1) / splits;
+    const int p0 = sp * chunk, p1 = min(len, p0 + chunk);
+    const bool owner = p0 <= pos && pos < p1;
+    const __half *kbase = kc + b * cb + kh * ch;
+    const __half *vbase = vc + b * cb + kh * ch;
+
+    int t0 = p0;
+    uint4 kraw[D / 8];
+    uint2 vraw[32];
+    auto load_tile = [&](int base) {
+        const int pk = base + lane;
+        if (pk < p1) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kbase + static_cast<int64_t>(pk) * cs);
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) kraw[c] = kr[c];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (base + j < p1)
+                vraw[j] = *reinterpret_cast<const uint2 *>(vbase + static_cast<int64_t>(base + j) * cs + lane * E);
+    };
+    if (t0 < p1) load_tile(t0);
+
+    pdl_wait();
+    pdl_trigger();
+    {
+        float r[4];
+        norm_rope_lane(*reinterpret_cast<const uint2 *>(q_in + b * q_sb + static_cast<int64_t>(h) * D + lane * E), q_w,
+                       inv_freq, pos, eps, lane, r);
+#pragma unroll
+        for (int e = 0; e < E; ++e) qs[g][lane * E + e] = __half2float(__float2half_rn(r[e])) * qscale;
+    }
+    uint2 vnew = make_uint2(0u, 0u);
+    if (owner) {
+        float r[4];
+        norm_rope_lane(*reinterpret_cast<const uint2 *>(k_in + b * k_sb + static_cast<int64_t>(kh) * D + lane * E), k_w,
+                       inv_freq, pos, eps, lane, r);
+        const uint2 kh4 = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
+        vnew = *reinterpret_cast<const uint2 *>(v_in + b * v_sb + static_cast<int64_t>(kh) * D + lane * E);
+        *reinterpret_cast<uint2 *>(&knew[g][lane * E]) = kh4;
+        if (g == 0) {
+            *reinterpret_cast<uint2 *>(kc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = kh4;
+            *reinterpret_cast<uint2 *>(vc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = vnew;
+        }
+    }
+    __syncwarp();
+
+    float m_run = -FLT_MAX, l_run = 0.0f;
+    float acc[E] = {0.0f, 0.0f, 0.0f, 0.0f};
+    while (t0 < p1) {
+        const int pk = t0 + lane;
+        const bool valid = pk < p1;
+        if (owner && pk == pos) {
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) kraw[c] = reinterpret_cast<const uint4 *>(knew[g])[c];
+        }
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+            const float4 lo = h4_to_f4(make_uint2(kraw[c].x, kraw[c].y));
+            const float4 hi = h4_to_f4(make_uint2(kraw[c].z, kraw[c].w));
+            const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][c * 8]);
+            const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][c * 8 + 4]);
+            s0 = fmaf(lo.x, qa.x, s0);
+            s1 = fmaf(lo.y, qa.y, s1);
+            s0 = fmaf(lo.z, qa.z, s0);
+            s1 = fmaf(lo.w, qa.w, s1);
+            s0 = fmaf(hi.x, qb.x, s0);
+            s1 = fmaf(hi.y, qb.y, s1);
+            s0 = fmaf(hi.z, qb.z, s0);
+            s1 = fmaf(hi.w, qb.w, s1);
+        }
+        const float sv = valid ? s0 + s1 : -FLT_MAX;
+        const float m_new = fmaxf(m_run, warp_max(sv));
+        const float corr = exp2f(m_run - m_new);
+        const float p = valid ? exp2f(sv - m_new) : 0.0f;
+        l_run = l_run * corr + p;  // per-lane partial sums, reduced once at the end
+        m_run = m_new;
+        ps[g][lane] = p;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] *= corr;
+        __syncwarp();
+        const int n_valid = min(32, p1 - t0);
+#pragma unroll
+        for (int j4 = 0; j4 < 32; j4 += 4) {
+            const float4 pj = *reinterpret_cast<const float4 *>(&ps[g][j4]);
+            const float pv[4] = {pj.x, pj.y, pj.z, pj.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = j4 + jj;
+                if (j < n_valid) {
+                    const uint2 raw = owner && t0 + j == pos ? vnew : vraw[j];
+                    const float4 vf = h4_to_f4(raw);
+                    acc[0] = fmaf(pv[jj], vf.x, acc[0]);
+                    acc[1] = fmaf(pv[jj], vf.y, acc[1]);
+                    acc[2] = fmaf(pv[jj], vf.z, acc[2]);
+                    acc[3] = fmaf(pv[jj], vf.w, acc[3]);
+                }
+            }
+        }
+        __syncwarp();
+        t0 += 32;
+        if (t0 < p1) load_tile(t0);
+    }
+    const float l_tot = warp_sum(l_run);
+    __half *orow = out + b * o_sb + static_cast<int64_t>(h) * D + lane * E;
+    if (splits == 1) {
+        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+        *reinterpret_cast<uint2 *>(orow) = f4_to_h4(make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv));
+        return;
+    }
+    // partial of this split for head h; the last warp to arrive combines
+    float *head_base = ws + (static_cast<int64_t>(b) * NH + h) * splits * (D + 4);
+    float *rec = head_base + static_cast<int64_t>(sp) * (D + 4);
+    *reinterpret_cast<float4 *>(rec + 4 + lane * E) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (lane == 0) *reinterpret_cast<float2 *>(rec) = make_float2(m_run, l_tot);
+    __threadfence();
+    __syncwarp();
+    int ticket = 0;
+    if (lane == 0) ticket = atomicAdd(&counters[b * NH + h], 1);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != splits - 1) return;
+    __threadfence();
+    float mx = -FLT_MAX;
+    for (int s2 = lane; s2 < splits; s2 += 32) mx = fmaxf(mx, __ldcg(head_base + static_cast<int64_t>(s2) * (D + 4)));
+    mx = warp_max(mx);
+    float lsum = 0.0f;
+    for (int s2 = lane; s2 < splits; s2 += 32) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(head_base + static_cast<int64_t>(s2) * (D + 4)));
+        const float w = ml.x == -FLT_MAX ? 0.0f : exp2f(ml.x - mx);
+        cw[g][s2] = w;
+        lsum = fmaf(w, ml.y, lsum);
+    }
+    lsum = warp_sum(lsum);
+    __syncwarp();
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float *col = head_base + 4 + lane * E;
+    int s2 = 0;
+    for (; s2 + 8 <= splits; s2 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(reinterpret_cast<const float4 *>(col + static_cast<int64_t>(s2 + u) * (D + 4)));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const float w = cw[g][s2 + u];
+            a.x = fmaf(w, v[u].x, a.x);
+            a.y = fmaf(w, v[u].y, a.y);
+            a.z = fmaf(w, v[u].z, a.z);
+            a.w = fmaf(w, v[u].w, a.w);
+        }
+    }
+    for (; s2 < splits; ++s2) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(col + static_cast<int64_t>(s2) * (D + 4)));
+        const float w = cw[g][s2];
+        a.x = fmaf(w, v.x, a.x);
+        a.y = fmaf(w, v.y, a.y);
+        a.z = fmaf(w, v.z, a.z);
+        a.w = fmaf(w, v.w, a.w);
+    }
+    const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+    *reinterpret_cast<uint2 *>(orow) = f4_to_h4(make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv));
+    if (lane == 0) counters[b * NH + h] = 0;
+}
+
 // ------------------------------------------------------ prefill attention
 // CTA = 4 warps on (b, head h, 16-query tile).  Keys are processed in tiles
 // of 32: warp w owns queries 4w..4w+3 of the tile; lane j scores key j of the
@@ -595,6 +821,13 @@ int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t strea
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Split partials (max, sum, 2 pad words, acc[D]) for every (b, head, split),
+// then one arrival counter per (b, head) in the last B * NH words.
+int64_t attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits) {
+    (void)NK;
+    return splits > 1 ? B * NH * splits * (D + 4) + B * NH : 0;
+}
+
 }  // namespace
 
 cudaError_t status_decode(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
@@ -695,6 +928,54 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
     return launch(attn_combine_kernel<2>, dim3(static_cast<unsigned>(B * NH)), dim3(64), 0, s,
                   static_cast<const float *>(workspace), static_cast<__half *>(out), static_cast<int>(B),
                   static_cast<int>(NH), static_cast<int>(splits));
+}
+
+extern "C" int t2c_attn_decode_fused(const void *q_in, const void *k_in, const void *v_in, int64_t q_sb, int64_t k_sb,
+                                     int64_t v_sb, const float *q_w, const float *k_w, const float *inv_freq, float eps,
+                                     void *k_cache, void *v_cache, int64_t cb, int64_t cs, int64_t ch, void *out,
+                                     int64_t o_sb, const int32_t *positions, int64_t B, int64_t NH, int64_t NK,
+                                     int64_t D, int64_t max_len, int64_t splits, float *workspace,
+                                     int64_t workspace_floats, void *stream) {
+    if (!q_in || !k_in || !v_in || !q_w || !k_w || !inv_freq || !k_cache || !v_cache || !out || !positions)
+        return set_error(T2C_EINVAL, "attn_decode_fused: NULL pointer");
+    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || splits <= 0 || max_len <= 0 || max_len > INT32_MAX)
+        return set_error(T2C_EINVAL, "attn_decode_fused: bad shape");
+    if (D != 128) return set_error(T2C_EUNSUPPORTED, "attn_decode_fused: D=%lld (128 only)", (long long)D);
+    const int G = static_cast<int>(NH / NK);
+    if (splits > kMaxSplits) return set_error(T2C_EUNSUPPORTED, "attn_decode_fused: splits %lld > %d", (long long)splits, kMaxSplits);
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || cs % 8 || cb % 8 || ch % 8)
+        return set_error(T2C_EINVAL, "attn_decode_fused: cache rows must be 16-byte aligned");
+    if (!aligned(q_in, 8) || !aligned(k_in, 8) || !aligned(v_in, 8) || q_sb % 4 || k_sb % 4 || v_sb % 4 || !aligned(q_w, 16) ||
+        !aligned(k_w, 16))
+        return set_error(T2C_EINVAL, "attn_decode_fused: q/k/v rows must be 8-byte aligned");
+    int *counters = nullptr;
+    if (splits > 1) {
+        const int64_t need = attn_decode_fused_workspace(B, NH, NK, D, splits);
+        if (!workspace || workspace_floats < need)
+            return set_error(T2C_ESCRATCH, "attn_decode_fused: workspace needs %lld words", (long long)need);
+        counters = reinterpret_cast<int *>(workspace + (need - B * NH));
+    }
+    const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+    const cudaStream_t s = as_stream(stream);
+    const dim3 grid(static_cast<unsigned>(B * NK * splits));
+#define T2C_FUSED(GG)                                                                                              \
+    return launch(attn_decode_fused_kernel<GG>, grid, dim3(GG * 32), 0, s, static_cast<const __half *>(q_in),               \
+                  static_cast<const __half *>(k_in), static_cast<const __half *>(v_in), q_sb, k_sb, v_sb, q_w, k_w,  \
+                  inv_freq, eps, static_cast<__half *>(k_cache), static_cast<__half *>(v_cache), cb, cs, ch,         \
+                  static_cast<__half *>(out), o_sb, positions, static_cast<int>(NK), static_cast<int>(max_len),     \
+                  static_cast<int>(splits), workspace, counters, qscale)
+    switch (G) {
+        case 1: T2C_FUSED(1);
+        case 2: T2C_FUSED(2);
+        case 4: T2C_FUSED(4);
+        case 8: T2C_FUSED(8);
+        default: return set_error(T2C_EUNSUPPORTED, "attn_decode_fused: group %d", G);
+    }
+#undef T2C_FUSED
+}
+
+extern "C" int64_t t2c_attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits) {
+    return attn_decode_fused_workspace(B, NH, NK, D, splits);
 }
 
 extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *v_cache, void *out,

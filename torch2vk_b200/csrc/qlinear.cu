@@ -27,6 +27,8 @@
 // fp32 accumulation of x * (d*sc*q - dmin*m); only the rounding of x to
 // 15 bits per 32-value sub-block differs (relative error <= 2^-15 of the
 // sub-block maximum).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdio.h>
 
 #include "common.cuh"
@@ -59,6 +61,9 @@ struct QStream {
 };
 
 struct QParams {
+    // tensor-core kernel: 2-D TMA maps of the Q4_K weights (u32 words, [N, row_bytes / 4],
+    // box 72 x 16 = 16 rows x one 288-byte segment)
+    alignas(64) CUtensorMap tmap[kMaxStreams];
     QStream s[kMaxStreams];
     int nstreams;
     int mode;
@@ -76,6 +81,10 @@ struct QParams {
     float *ps;
     uint32_t *pt;
     int64_t G;
+    // tensor-core kernel: row-block groups of wpb warps, bpc groups per CTA, nseg segments per row
+    int wpb;
+    int bpc;
+    int nseg;
 };
 
 // x planes in shared memory.  xh/xl rows are padded by 16 bytes after every
@@ -1063,6 +1072,399 @@ __global__ void __launch_bounds__(kConsumerThreads) qmv_tma_kernel(const QParams
     }
 }
 
+// ============================================================ tensor-core kernel
+// Q4_K matvec for M <= 4 with int8 tensor-core tiles (mma.sync m16n8k32
+// s8 x s8 -> s32): one instruction forms the 16-row x 32-value integer dot
+// products of a sub-block for all (batch row, x plane) columns, so a warp
+// spends ~0.05 instructions per weight instead of ~0.13 with dp4a.
+//   A (16 x 32): weight nibbles of 16 rows for one 32-value sub-block.  Lane
+//     (g = lane/4, t = lane%4) takes bytes 8t..8t+7 of the sub-block's 32-byte
+//     group for rows g and g+8; low nibbles form sub-block 2q, high nibbles 2q+1.
+//     The k order inside the tile is permuted (slots 4t..4t+3 <- values
+//     8t..8t+3, slots 16+4t.. <- 8t+4..8t+7) identically for A and B.
+//   B (32 x 8): column n = 2m + plane holds x plane (xh, xl) of batch row m.
+//   D: lane (g, t) receives rows g, g+8 for batch row m = t, both planes, and
+//     applies the sub-block scale d*sc (taken by shuffle from the lane that
+//     decoded it), the x scale and the min term.
+// Streaming is the same as qmv_tma_kernel (warp-private rings of 1-D bulk
+// copies into shared memory, bounded mbarrier waits, weights requested before
+// griddepcontrol.wait), with 16-row blocks and 2-super-block (288-byte) row
+// segments (a 288-byte row stride keeps the 8-byte fragment reads free of
+// bank conflicts).  K is split across the warps of a CTA: the 8 warps form
+// bpc groups of wpb warps; group j takes row block (iteration base + j) and
+// its warps take segments w, w + wpb, ...; the partial sums meet in shared
+// memory at the end of every CTA iteration.
+constexpr int kMmaWarps = 8;
+constexpr int kMmaThreads = kMmaWarps * 32;
+constexpr int kMmaSegBlocks = 2;
+constexpr int kMmaSegBytes = kMmaSegBlocks * 144;
+constexpr int kMmaRows = 16;
+
+__device__ __forceinline__ void mma_s8_16832(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+
+// Scales of sub-blocks 2t, 2t+1 of one Q4_K block header (d*sc, dmin*m).
+__device__ __forceinline__ void q4k_pair_scales(const uint4 h, int t, float &ds0, float &ds1, float &dm0, float &dm1) {
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const int i0 = (2 * t) & 3;
+    const bool low = t < 2;
+    const uint32_t y = h.y >> (8 * i0), z = h.z >> (8 * i0), w = h.w >> (8 * i0);
+    const uint32_t hs = ((y >> 6) & 0x3u) | (((y >> 14) & 0x3u) << 8);
+    const uint32_t hm = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
+    const uint32_t scp = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hs << 4));
+    const uint32_t mnp = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hm << 4));
+    ds0 = d * small_u2f(scp & 0xffu);
+    ds1 = d * small_u2f(scp >> 8);
+    dm0 = dmin * small_u2f(mnp & 0xffu);
+    dm1 = dmin * small_u2f(mnp >> 8);
+}
+
+// One 144-byte super-block of a 16-row group: acc[0] row g, acc[1] row g+8 (batch row t).
+// rowg: shared address of the block in row g; xk: x offset (values) of the block.
+__device__ __forceinline__ void mma_q4k_block(uint32_t rowg, uint32_t row_stride, int kabs, const XS &x, int lane,
+                                              int M, float acc[2]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t rowg8 = rowg + 8u * row_stride;
+    const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
+    float ds[2][2], dm[2][2];
+    q4k_pair_scales(hg, t, ds[0][0], ds[0][1], dm[0][0], dm[0][1]);
+    q4k_pair_scales(hg8, t, ds[1][0], ds[1][1], dm[1][0], dm[1][1]);
+    // B column g: batch row g/2, plane g%2 (zero for absent batch rows)
+    const bool bcol = (g >> 1) < M;
+    const uint32_t xplane = (g & 1) ? x.xl : x.xh;
+    const int bm = bcol ? (g >> 1) : 0;
+    const bool dcol = t < M;
+    const int dmrow = dcol ? t : 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint2 wg = lds64(rowg + 16 + 32 * q + 8 * t);
+        const uint2 wg8 = lds64(rowg8 + 16 + 32 * q + 8 * t);
+        const int k0 = kabs + 64 * q + 8 * t;
+        const uint2 b_lo = bcol ? lds64(xplane + x.off(bm, k0)) : make_uint2(0u, 0u);
+        const uint2 b_hi = bcol ? lds64(xplane + x.off(bm, k0 + 32)) : make_uint2(0u, 0u);
+        const uint4 mt = lds128(x.meta + 16u * static_cast<uint32_t>(dmrow * x.u64 + ((kabs >> 6) + q)));
+        const uint32_t a_lo[4] = {wg.x & 0x0F0F0F0Fu, wg8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu, wg8.y & 0x0F0F0F0Fu};
+        const uint32_t a_hi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (wg8.x >> 4) & 0x0F0F0F0Fu, (wg.y >> 4) & 0x0F0F0F0Fu,
+                                  (wg8.y >> 4) & 0x0F0F0F0Fu};
+        int d_lo[4], d_hi[4];
+        mma_s8_16832(d_lo, a_lo, b_lo.x, b_lo.y);
+        mma_s8_16832(d_hi, a_hi, b_hi.x, b_hi.y);
+        // scales of sub-blocks 2q, 2q+1 live in lane (g, q)
+        const int src = (lane & ~3) | q;
+        const float s0g = __shfl_sync(0xffffffffu, ds[0][0], src), s1g = __shfl_sync(0xffffffffu, ds[0][1], src);
+        const float m0g = __shfl_sync(0xffffffffu, dm[0][0], src), m1g = __shfl_sync(0xffffffffu, dm[0][1], src);
+        const float s0h = __shfl_sync(0xffffffffu, ds[1][0], src), s1h = __shfl_sync(0xffffffffu, ds[1][1], src);
+        const float m0h = __shfl_sync(0xffffffffu, dm[1][0], src), m1h = __shfl_sync(0xffffffffu, dm[1][1], src);
+        const float sx0 = dcol ? __uint_as_float(mt.x) : 0.0f, sx1 = dcol ? __uint_as_float(mt.y) : 0.0f;
+        const float xs0 = dcol ? __uint_as_float(mt.z) : 0.0f, xs1 = dcol ? __uint_as_float(mt.w) : 0.0f;
+        acc[0] = fmaf(s0g * sx0, static_cast<float>(d_lo[0] * 128 + d_lo[1]), acc[0]);
+        acc[1] = fmaf(s0h * sx0, static_cast<float>(d_lo[2] * 128 + d_lo[3]), acc[1]);
+        acc[0] = fmaf(s1g * sx1, static_cast<float>(d_hi[0] * 128 + d_hi[1]), acc[0]);
+        acc[1] = fmaf(s1h * sx1, static_cast<float>(d_hi[2] * 128 + d_hi[3]), acc[1]);
+        acc[0] = fmaf(-m0g, xs0, fmaf(-m1g, xs1, acc[0]));
+        acc[1] = fmaf(-m0h, xs0, fmaf(-m1h, xs1, acc[1]));
+    }
+}
+
+// M = 1 variant: the 8 columns are 4 sub-blocks x 2 x planes.  A group of 4
+// sub-blocks (quarters 2G, 2G+1 of the block: low nibbles -> sub-blocks 4G,
+// 4G+2, high nibbles -> 4G+1, 4G+3) takes 4 accumulating mma: in mma i, lane
+// (g, t) feeds k-slots 4t..4t+3 from sub-block 4G + t/2 and k-slots 16+4t..
+// from sub-block 4G + 2 + t/2, values 16*(t%2) + 4i .. +3 of the sub-block, so a
+// lane's four A words of one (row, quarter) are one 16-byte load.  High
+// nibbles enter unshifted (16 q, unsigned A operand); 1/16 is folded into the
+// scale of the odd (high-nibble) sub-blocks.  B column s*2 + plane carries x
+// of sub-block 4G + s only (zero rows elsewhere), so D column pair t of lane
+// (g, t) is sub-block 4G + t, and each lane applies the scales of its own two
+// sub-blocks (t and 4 + t); the four lanes of a quad are summed per row block.
+__device__ __forceinline__ void mma_u8s8_16832_acc(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Scales of sub-blocks t and t + 4 of one Q4_K header: d*sc, dmin*m.
+__device__ __forceinline__ void q4k_lane_scales(const uint4 h, int t, float ds[2], float dm[2]) {
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const uint32_t y = (h.y >> (8 * t)) & 0xffu, z = (h.z >> (8 * t)) & 0xffu, w = (h.w >> (8 * t)) & 0xffu;
+    ds[0] = d * small_u2f(y & 63u);
+    dm[0] = dmin * small_u2f(z & 63u);
+    ds[1] = d * small_u2f((w & 15u) | ((y >> 6) << 4));
+    dm[1] = dmin * small_u2f((w >> 4) | ((z >> 6) << 4));
+}
+
+// x fragments of one block for this lane: X[G] = 16 bytes of plane (g & 1),
+// sub-block 4G + (g >> 1), values 16 (t & 1) .. +15, or zero when the lane's
+// k-slots do not belong to that sub-block.
+struct M1X {
+    uint4 X[2];
+    uint32_t m0, m1;  // b0 / b1 masks
+};
+
+__device__ __forceinline__ M1X m1_x(const XS &x, int kabs, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int s = g >> 1;
+    const bool active = (t >> 1) == (s & 1);
+    M1X r;
+    r.m0 = (active && s < 2) ? 0xffffffffu : 0u;
+    r.m1 = (active && s >= 2) ? 0xffffffffu : 0u;
+    const uint32_t plane = (g & 1) ? x.xl : x.xh;
+#pragma unroll
+    for (int G = 0; G < 2; ++G)
+        r.X[G] = active ? lds128(plane + x.off(0, kabs + 32 * (4 * G + s) + 16 * (t & 1))) : make_uint4(0u, 0u, 0u, 0u);
+    return r;
+}
+
+// One 144-byte block of a 16-row group (M = 1); acc[0] row g, acc[1] row g+8.
+__device__ __forceinline__ void mma_q4k_block_m1(uint32_t rowg, uint32_t row_stride, int kabs, const XS &x,
+                                                 const M1X &xf, int lane, float acc[2]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t rowg8 = rowg + 8u * row_stride;
+    const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
+    float dsg[2], dmg[2], dsh[2], dmh[2];
+    q4k_lane_scales(hg, t, dsg, dmg);
+    q4k_lane_scales(hg8, t, dsh, dmh);
+    // A: this lane's k-slots hold sub-blocks 4G + t/2 and 4G + 2 + t/2 (high nibbles when t/2 = 1);
+    // D: column pair t is sub-block 4G + t (high nibbles when t is odd)
+    const uint32_t nib = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+    const float hi_scale = (t & 1) ? 0.0625f : 1.0f;
+    // x scale / sum of this lane's sub-blocks j = t (G 0) and 4 + t (G 1)
+    const uint4 mt0 = lds128(x.meta + 16u * static_cast<uint32_t>((kabs >> 6) + (t >> 1)));
+    const uint4 mt1 = lds128(x.meta + 16u * static_cast<uint32_t>((kabs >> 6) + 2 + (t >> 1)));
+    const float sx[2] = {__uint_as_float((t & 1) ? mt0.y : mt0.x), __uint_as_float((t & 1) ? mt1.y : mt1.x)};
+    const float xs[2] = {__uint_as_float((t & 1) ? mt0.w : mt0.z), __uint_as_float((t & 1) ? mt1.w : mt1.z)};
+    const uint32_t off = 16u + 16u * static_cast<uint32_t>(t & 1);
+#pragma unroll
+    for (int G = 0; G < 2; ++G) {
+        const uint4 qa = lds128(rowg + off + 64 * G), qb = lds128(rowg + off + 64 * G + 32);
+        const uint4 ra = lds128(rowg8 + off + 64 * G), rb = lds128(rowg8 + off + 64 * G + 32);
+        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+        const uint32_t va[4] = {ra.x, ra.y, ra.z, ra.w}, vb[4] = {rb.x, rb.y, rb.z, rb.w};
+        const uint32_t xw[4] = {xf.X[G].x, xf.X[G].y, xf.X[G].z, xf.X[G].w};
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t a[4] = {wa[i] & nib, va[i] & nib, wb[i] & nib, vb[i] & nib};
+            mma_u8s8_16832_acc(d, a, xw[i] & xf.m0, xw[i] & xf.m1);
+        }
+        const float f = sx[G] * hi_scale;
+        acc[0] = fmaf(dsg[G] * f, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], xs[G], acc[0]));
+        acc[1] = fmaf(dsh[G] * f, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], xs[G], acc[1]));
+    }
+}
+
+// Item cursor of one warp: CTA iteration `it`, j-th segment of the warp.
+struct MmaCursor {
+    int64_t it;
+    int j;
+};
+
+__device__ __forceinline__ int64_t mma_block(const QParams &p, int64_t it, int warp) {
+    return (static_cast<int64_t>(blockIdx.x) + it * gridDim.x) * p.bpc + warp / p.wpb;
+}
+
+// Next existing item at or after c (segment index = warp % wpb + j * wpb); false when exhausted.
+__device__ __forceinline__ bool mma_valid(const QParams &p, const MmaCursor &c, int warp, int64_t iters) {
+    return c.it < iters && mma_block(p, c.it, warp) < p.total_rowsets;
+}
+
+__device__ __forceinline__ void mma_advance(const QParams &p, MmaCursor &c, int warp) {
+    if (warp % p.wpb + (c.j + 1) * p.wpb < p.nseg) {
+        ++c.j;
+    } else {
+        c.j = 0;
+        ++c.it;
+    }
+}
+
+__device__ __forceinline__ void mma_issue(const QParams &p, int64_t block, int seg, uint8_t *stage, uint64_t *bar) {
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int si = swiglu ? 0 : stream_of(p, block);
+    const int row0 = static_cast<int>((block - p.s[si].rs_begin) * kMmaRows);
+    const int groups = swiglu ? 2 : 1;
+    // rows past N are zero-filled by the TMA unit and still count toward the transaction bytes
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(groups * kMmaRows * kMmaSegBytes));
+    for (int gi = 0; gi < groups; ++gi)
+        tma_load_2d(stage + gi * kMmaRows * kMmaSegBytes, &p.tmap[swiglu ? gi : si], seg * (kMmaSegBytes / 4), row0, bar);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_constant__ QParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int K = p.K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.stages;
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int R = swiglu ? 2 : 1;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
+    uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
+    float *red = reinterpret_cast<float *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes);
+    float4 *meta = reinterpret_cast<float4 *>(red + kMmaWarps * 32 * 4);
+    int8_t *xh = reinterpret_cast<int8_t *>(meta + MT * (K >> 6));
+    int8_t *xl = xh + MT * padded_k(K) + 32;  // +32: xh / xl fragments of one k on different banks
+    float *sx = reinterpret_cast<float *>(xl + MT * padded_k(K));
+    int *xq16 = reinterpret_cast<int *>(sx + MT * (K >> 5));
+    float *pred = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
+    const int64_t iters = (p.total_rowsets + static_cast<int64_t>(gridDim.x) * p.bpc - 1) /
+                          (static_cast<int64_t>(gridDim.x) * p.bpc);
+    const int seg0 = warp % p.wpb;
+
+    MmaCursor ahead{0, 0};
+    if (lane == 0) {
+        for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+        fence_mbar_init();
+        for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) {
+            mma_issue(p, mma_block(p, ahead.it, warp), seg0 + ahead.j * p.wpb,
+                      stages + static_cast<size_t>(i) * p.stage_bytes, &full[i]);
+            mma_advance(p, ahead, warp);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    prepare_x<MT, kMmaThreads>(p, xh, xl, sx, xq16, meta, pred);  // ends with a CTA barrier
+    const XS x{smem_u32(xh), smem_u32(xl), smem_u32(meta), smem_u32(sx), smem_u32(xq16), padded_k(K), K >> 6,
+               K >> 5};
+    ahead = MmaCursor{0, 0};
+    for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) mma_advance(p, ahead, warp);
+
+    const uint32_t stages_addr = smem_u32(stages);
+    int s = 0;
+    uint32_t phase = 0;
+    bool failed = false;
+    for (int64_t it = 0; it < iters; ++it) {
+        const int64_t block = mma_block(p, it, warp);
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        if (block < p.total_rowsets) {
+            for (int seg = seg0; seg < p.nseg; seg += p.wpb) {
+                if (!failed && !mbar_wait(&full[s], phase)) {
+                    report_device_error(T2C_ETIMEOUT);
+                    failed = true;
+                }
+                if (!failed) {
+                    const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
+                    const int kseg = seg * kMmaSegBlocks * 256;
+                    const int g = lane >> 2;
+#pragma unroll
+                    for (int sb = 0; sb < kMmaSegBlocks; ++sb) {
+                        if constexpr (MT == 1) {
+                            const M1X xf = m1_x(x, kseg + sb * 256, lane);
+#pragma unroll
+                            for (int r = 0; r < 2; ++r) {
+                                if (r < R)
+                                    mma_q4k_block_m1(
+                                        stage + static_cast<uint32_t>((r * kMmaRows + g) * kMmaSegBytes + sb * 144),
+                                        kMmaSegBytes, kseg + sb * 256, x, xf, lane, acc[r]);
+                            }
+                        } else {
+#pragma unroll
+                            for (int r = 0; r < 2; ++r) {
+                                if (r < R)
+                                    mma_q4k_block(
+                                        stage + static_cast<uint32_t>((r * kMmaRows + g) * kMmaSegBytes + sb * 144),
+                                        kMmaSegBytes, kseg + sb * 256, x, lane, p.M, acc[r]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0 && mma_valid(p, ahead, warp, iters)) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        mma_issue(p, mma_block(p, ahead.it, warp), seg0 + ahead.j * p.wpb,
+                                  stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
+                    }
+                    if (mma_valid(p, ahead, warp, iters)) mma_advance(p, ahead, warp);
+                }
+                if (++s == S) {
+                    s = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        if constexpr (MT == 1) {
+            // the four lanes of a quad hold disjoint sub-blocks of the same rows
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 1);
+                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
+                }
+        }
+        // combine the wpb warps of each row block
+        *reinterpret_cast<float4 *>(red + (warp * 32 + lane) * 4) = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+        __syncthreads();
+        if (seg0 == 0 && block < p.total_rowsets) {
+            for (int w = warp + 1; w < warp + p.wpb; ++w) {
+                const float4 o = *reinterpret_cast<const float4 *>(red + (w * 32 + lane) * 4);
+                acc[0][0] += o.x;
+                acc[0][1] += o.y;
+                acc[1][0] += o.z;
+                acc[1][1] += o.w;
+            }
+            const int g = lane >> 2, t = lane & 3;
+            const int si = swiglu ? 0 : stream_of(p, block);
+            const QStream &st = p.s[si];
+            const int64_t row0 = (block - st.rs_begin) * kMmaRows;
+            const int64_t na = row0 + g, nb = row0 + g + 8;
+            if (p.mode == MODE_ARGMAX) {
+                // groups of 4 rows: lanes (g, t) with g in one quad; ties keep the lower row
+                float best[2] = {na < st.n ? acc[0][0] : -INFINITY, nb < st.n ? acc[0][1] : -INFINITY};
+                uint32_t tok[2] = {static_cast<uint32_t>(na), static_cast<uint32_t>(nb)};
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                    for (int o = 4; o <= 8; o <<= 1) {
+                        const float ob = __shfl_xor_sync(0xffffffffu, best[h], o);
+                        const uint32_t ot = __shfl_xor_sync(0xffffffffu, tok[h], o);
+                        if (ob > best[h] || (ob == best[h] && ot < tok[h])) {
+                            best[h] = ob;
+                            tok[h] = ot;
+                        }
+                    }
+                }
+                if ((g & 3) == 0 && t < p.M) {
+                    if (na < st.n) {
+                        p.ps[t * p.G + (na >> 2)] = best[0];
+                        p.pt[t * p.G + (na >> 2)] = tok[0];
+                    }
+                    if (nb < st.n) {
+                        p.ps[t * p.G + (nb >> 2)] = best[1];
+                        p.pt[t * p.G + (nb >> 2)] = tok[1];
+                    }
+                }
+            } else if (t < p.M) {
+                const int64_t rows[2] = {na, nb};
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (rows[h] >= st.n) continue;
+                    const int64_t o = t * st.n + rows[h];
+                    float v;
+                    if (swiglu) {
+                        v = silu(acc[0][h]) * acc[1][h];
+                    } else {
+                        v = acc[0][h];
+                        if (st.res) v += __half2float(st.res[o]);
+                    }
+                    st.y[o] = __float2half_rn(v);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // ================================================================== launchers
 size_t x_smem_bytes(int MT, int K) {
     return static_cast<size_t>(MT) * (K / 64) * 16 + static_cast<size_t>(MT) * padded_k(K) * 2 +
@@ -1294,7 +1696,97 @@ bool tma_geometry(QStream &st, int64_t K, bool swiglu) {
 }
 
 // Chooses the streamed kernel when every stream can be bulk-copied.
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+int encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes) {
+    static PFN_cuTensorMapEncodeTiled encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+    }();
+    if (encode == nullptr || row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return T2C_EUNSUPPORTED;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {kMmaSegBytes / 4, kMmaRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? T2C_OK : T2C_EUNSUPPORTED;
+}
+
+size_t mma_fixed_smem(int MT, int K) {
+    return kStageHead + static_cast<size_t>(kMmaWarps) * 32 * 4 * 4 + static_cast<size_t>(MT) * (K / 64) * 16 +
+           2 * static_cast<size_t>(MT) * padded_k(K) + 32 + static_cast<size_t>(MT) * (K / 32) * 4 +
+           static_cast<size_t>(MT) * (K / 16) * 4 + static_cast<size_t>(kMmaWarps) * MT * 4;
+}
+
+template <int MT>
+int launch_mma(QParams p, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    const size_t fixed = mma_fixed_smem(MT, p.K);
+    const size_t per_stage = static_cast<size_t>(kMmaWarps) * p.stage_bytes;
+    p.stages = fixed >= kSmemLimit ? 0 : static_cast<int>((kSmemLimit - fixed) / per_stage);
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    if (p.stages < 2) return set_error(T2C_EUNSUPPORTED, "qmv_mma: stages do not fit");
+    const size_t smem = fixed + per_stage * p.stages;
+    int rc = ensure_smem_attr(qmv_mma_kernel<MT>, configured[device_slot()]);
+    if (rc) return rc;
+    int64_t blocks = (p.total_rowsets + p.bpc - 1) / p.bpc;
+    const int64_t cap = sm_count();
+    if (blocks > cap) blocks = cap;
+    return launch_pdl(qmv_mma_kernel<MT>, static_cast<int>(blocks), kMmaThreads, smem, stream, p);
+}
+
+bool mma_disabled() {
+    static const bool off = [] {
+        const char *v = getenv("T2C_QMV_DP4A");
+        return v != nullptr && v[0] == '1';
+    }();
+    return off;
+}
+
+// Tensor-core path when every stream is Q4_K, M <= 4 and K splits into 512-value segments.
+int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
+    used = false;
+    if (mma_disabled() || M > 4 || p.K % (kMmaSegBlocks * 256) != 0) return T2C_OK;
+    for (int i = 0; i < p.nstreams; ++i)
+        if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int MT = M <= 1 ? 1 : (M <= 2 ? 2 : 4);
+    p.stage_bytes = (swiglu ? 2 : 1) * kMmaRows * kMmaSegBytes;
+    if (mma_fixed_smem(MT, p.K) + 2 * static_cast<size_t>(kMmaWarps) * p.stage_bytes > kSmemLimit) return T2C_OK;
+    p.nseg = p.K / (kMmaSegBlocks * 256);
+    p.wpb = 1;
+    while (p.wpb * 2 <= kMmaWarps && p.wpb * 2 <= p.nseg) p.wpb *= 2;
+    p.bpc = kMmaWarps / p.wpb;
+    int64_t blocks = 0;
+    for (int i = 0; i < p.nstreams; ++i) {
+        p.s[i].rs_begin = blocks;
+        blocks += (p.s[i].n + kMmaRows - 1) / kMmaRows;
+        if (swiglu) break;
+    }
+    if (swiglu) p.s[1].rs_begin = blocks;
+    p.total_rowsets = blocks;
+    p.M = static_cast<int>(M);
+    for (int i = 0; i < (swiglu ? 2 : p.nstreams); ++i) {
+        if (p.s[i].n > INT32_MAX || encode_weight_map(&p.tmap[i], p.s[i].w, p.s[i].n, p.s[i].row_bytes) != T2C_OK)
+            return T2C_OK;  // no map: the dp4a kernels serve this call
+    }
+    used = true;
+    switch (MT) {
+        case 1: return launch_mma<1>(p, stream);
+        case 2: return launch_mma<2>(p, stream);
+        default: return launch_mma<4>(p, stream);
+    }
+}
+
 int run_linear(QParams p, int64_t M, cudaStream_t stream) {
+    bool used = false;
+    const int rc_mma = try_mma(p, M, stream, used);
+    if (used) return rc_mma;
     bool tma = true;
     const bool swiglu = p.mode == MODE_SWIGLU;
     int stage_bytes = 0;

@@ -193,6 +193,40 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
     return out
 
 
+def attn_decode_fused_workspace(batch: int, n_heads: int, n_kv: int, head_dim: int, splits: int,
+                                device: torch.device | str = "cuda") -> torch.Tensor | None:
+    """Zeroed workspace (split partials + arrival counters) for attn_decode_fused, or None for one split."""
+    n = int(_lib.lib().raw("t2c_attn_decode_fused_workspace")(batch, n_heads, n_kv, head_dim, splits))
+    return torch.zeros(n, dtype=torch.float32, device=device) if n else None
+
+
+def attn_decode_fused(q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor, q_w: torch.Tensor,
+                      k_w: torch.Tensor, inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      positions: torch.Tensor, *, batch: int, n_heads: int, n_kv: int, head_dim: int, splits: int,
+                      workspace: torch.Tensor | None, layout: str = "token_major", eps: float = 1e-6,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """q/k norm + RoPE, KV write at positions[b], attention over 0..positions[b], one launch (T = 1).
+
+    q_in [B, NH*D], k_in / v_in [B, NK*D] (row views of the QKV outputs are fine: batch stride taken
+    from stride(0)); workspace from attn_decode_fused_workspace when splits > 1.
+    """
+    for t, n in ((q_in, "q_in"), (k_in, "k_in"), (v_in, "v_in")):
+        if t.dtype != torch.float16 or not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError(f"{n} must be a CUDA float16 tensor with unit last stride")
+    _check(positions, torch.int32, "positions")
+    out = torch.empty(batch, n_heads * head_dim, dtype=torch.float16, device=q_in.device) if out is None else out
+    cb, cs, ch = cache_strides(k_cache, layout)
+    max_len = k_cache.shape[1] if layout == "token_major" else k_cache.shape[2]
+    if v_cache.shape != k_cache.shape or k_cache.dtype != torch.float16:
+        raise ValueError("k_cache / v_cache must be float16 tensors of one shape")
+    _lib.lib().call("t2c_attn_decode_fused", _lib.ptr(q_in), _lib.ptr(k_in), _lib.ptr(v_in), q_in.stride(0),
+                    k_in.stride(0), v_in.stride(0), _lib.ptr(q_w), _lib.ptr(k_w), _lib.ptr(inv_freq), float(eps),
+                    _lib.ptr(k_cache), _lib.ptr(v_cache), cb, cs, ch, _lib.ptr(out), out.stride(0),
+                    _lib.ptr(positions), batch, n_heads, n_kv, head_dim, max_len, splits, _lib.ptr(workspace),
+                    workspace.numel() if workspace is not None else 0, _lib.stream_ptr())
+    return out
+
+
 def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor, *,
                  batch: int, tokens: int, n_heads: int, n_kv: int, head_dim: int, layout: str = "token_major",
                  q_layout: str = "token_major", out: torch.Tensor | None = None) -> torch.Tensor:

@@ -122,6 +122,7 @@ class Qwen3Runner:
     max_new_tokens: int = 256
     eos_ids: tuple[int, ...] = ()
     decode_splits: int = 0
+    fused_attention: bool = True
     k_cache: list[torch.Tensor] = field(init=False)
     v_cache: list[torch.Tensor] = field(init=False)
 
@@ -141,9 +142,11 @@ class Qwen3Runner:
         self.stopped = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self.eos = torch.tensor(list(self.eos_ids) or [-1], dtype=torch.int64, device=dev)
         if self.decode_splits <= 0:
-            self.decode_splits = max(1, min(64, self.max_seq // 128))
+            self.decode_splits = max(1, min(32 if self.fused_attention else 64, self.max_seq // (64 if self.fused_attention else 128)))
         ws = kernels.attn_decode_workspace_floats(self.batch, cfg.heads, cfg.head_dim, self.decode_splits)
         self.attn_workspace = torch.empty(max(ws, 1), dtype=torch.float32, device=dev)
+        self.fused_workspace = kernels.attn_decode_fused_workspace(self.batch, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                                                   self.decode_splits, dev)
         self.decode = self._alloc(self.batch)
         self._graph: torch.cuda.CUDAGraph | None = None
 
@@ -171,18 +174,25 @@ class Qwen3Runner:
         h = b.h
         kernels.linear_multi(h, [(lw.q.data, lw.q.kind), (lw.k.data, lw.k.kind), (lw.v.data, lw.v.kind)], cfg.hidden,
                              norm_weight=lw.input_norm, eps=cfg.eps, outs=[b.q, b.k, b.v])
-        kernels.qk_norm_rope_cache(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.k_cache[i], self.v_cache[i],
-                                   self.positions, self.inv_freq, batch=self.batch, tokens=tokens_per_seq,
-                                   n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, eps=cfg.eps,
-                                   q_out=b.qr)
-        if decode:
-            kernels.attn_decode(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
-                                n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, max_len=self.max_seq,
-                                splits=self.decode_splits, workspace=self.attn_workspace, out=b.attn)
+        if decode and self.fused_attention:
+            kernels.attn_decode_fused(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.inv_freq, self.k_cache[i],
+                                      self.v_cache[i], self.positions, batch=self.batch, n_heads=cfg.heads,
+                                      n_kv=cfg.kv_heads, head_dim=cfg.head_dim, splits=self.decode_splits,
+                                      workspace=self.fused_workspace, eps=cfg.eps, out=b.attn)
         else:
-            kernels.attn_prefill(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
-                                 tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim,
-                                 out=b.attn)
+            kernels.qk_norm_rope_cache(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.k_cache[i], self.v_cache[i],
+                                       self.positions, self.inv_freq, batch=self.batch, tokens=tokens_per_seq,
+                                       n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, eps=cfg.eps,
+                                       q_out=b.qr)
+            if decode:
+                kernels.attn_decode(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
+                                    n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim,
+                                    max_len=self.max_seq, splits=self.decode_splits, workspace=self.attn_workspace,
+                                    out=b.attn)
+            else:
+                kernels.attn_prefill(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
+                                     tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=cfg.kv_heads,
+                                     head_dim=cfg.head_dim, out=b.attn)
         kernels.linear(b.attn, lw.o.data, lw.o.kind, cfg.heads * cfg.head_dim, residual=h, out=h)
         kernels.linear_swiglu(h, lw.gate.data, lw.up.data, lw.gate.kind, cfg.hidden, norm_weight=lw.post_norm,
                               eps=cfg.eps, out=b.act)
