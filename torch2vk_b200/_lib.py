@@ -8,11 +8,15 @@ device is missing, calls raise.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "libt2c_sm100.so"
+# Alternative build of the same library (for A/B timing of kernel variants); default: the in-tree build.
+if os.environ.get("T2C_LIBRARY"):
+    LIB_PATH = Path(os.environ["T2C_LIBRARY"]).resolve()
 
 T2C_OK = 0
 STATUS_NAMES = {1: "EINVAL", 2: "EUNSUPPORTED", 3: "ECUDA", 4: "ETIMEOUT", 5: "ESCRATCH"}

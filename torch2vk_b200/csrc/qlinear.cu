@@ -85,6 +85,7 @@ struct QParams {
     int wpb;
     int bpc;
     int nseg;
+    int xseg_per_warp;  // M = 1 kernel: x segments held per warp
 };
 
 // x planes in shared memory.  xh/xl rows are padded by 16 bytes after every
@@ -1206,67 +1207,9 @@ __device__ __forceinline__ void q4k_lane_scales(const uint4 h, int t, float ds[2
     dm[1] = dmin * small_u2f((w >> 4) | ((z >> 6) << 4));
 }
 
-// x fragments of one block for this lane: X[G] = 16 bytes of plane (g & 1),
-// sub-block 4G + (g >> 1), values 16 (t & 1) .. +15, or zero when the lane's
-// k-slots do not belong to that sub-block.
-struct M1X {
-    uint4 X[2];
-    uint32_t m0, m1;  // b0 / b1 masks
-};
-
-__device__ __forceinline__ M1X m1_x(const XS &x, int kabs, int lane) {
-    const int g = lane >> 2, t = lane & 3;
-    const int s = g >> 1;
-    const bool active = (t >> 1) == (s & 1);
-    M1X r;
-    r.m0 = (active && s < 2) ? 0xffffffffu : 0u;
-    r.m1 = (active && s >= 2) ? 0xffffffffu : 0u;
-    const uint32_t plane = (g & 1) ? x.xl : x.xh;
-#pragma unroll
-    for (int G = 0; G < 2; ++G)
-        r.X[G] = active ? lds128(plane + x.off(0, kabs + 32 * (4 * G + s) + 16 * (t & 1))) : make_uint4(0u, 0u, 0u, 0u);
-    return r;
-}
-
-// One 144-byte block of a 16-row group (M = 1); acc[0] row g, acc[1] row g+8.
-__device__ __forceinline__ void mma_q4k_block_m1(uint32_t rowg, uint32_t row_stride, int kabs, const XS &x,
-                                                 const M1X &xf, int lane, float acc[2]) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t rowg8 = rowg + 8u * row_stride;
-    const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
-    float dsg[2], dmg[2], dsh[2], dmh[2];
-    q4k_lane_scales(hg, t, dsg, dmg);
-    q4k_lane_scales(hg8, t, dsh, dmh);
-    // A: this lane's k-slots hold sub-blocks 4G + t/2 and 4G + 2 + t/2 (high nibbles when t/2 = 1);
-    // D: column pair t is sub-block 4G + t (high nibbles when t is odd)
-    const uint32_t nib = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-    const float hi_scale = (t & 1) ? 0.0625f : 1.0f;
-    // x scale / sum of this lane's sub-blocks j = t (G 0) and 4 + t (G 1)
-    const uint4 mt0 = lds128(x.meta + 16u * static_cast<uint32_t>((kabs >> 6) + (t >> 1)));
-    const uint4 mt1 = lds128(x.meta + 16u * static_cast<uint32_t>((kabs >> 6) + 2 + (t >> 1)));
-    const float sx[2] = {__uint_as_float((t & 1) ? mt0.y : mt0.x), __uint_as_float((t & 1) ? mt1.y : mt1.x)};
-    const float xs[2] = {__uint_as_float((t & 1) ? mt0.w : mt0.z), __uint_as_float((t & 1) ? mt1.w : mt1.z)};
-    const uint32_t off = 16u + 16u * static_cast<uint32_t>(t & 1);
-#pragma unroll
-    for (int G = 0; G < 2; ++G) {
-        const uint4 qa = lds128(rowg + off + 64 * G), qb = lds128(rowg + off + 64 * G + 32);
-        const uint4 ra = lds128(rowg8 + off + 64 * G), rb = lds128(rowg8 + off + 64 * G + 32);
-        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
-        const uint32_t va[4] = {ra.x, ra.y, ra.z, ra.w}, vb[4] = {rb.x, rb.y, rb.z, rb.w};
-        const uint32_t xw[4] = {xf.X[G].x, xf.X[G].y, xf.X[G].z, xf.X[G].w};
-        int d[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t a[4] = {wa[i] & nib, va[i] & nib, wb[i] & nib, vb[i] & nib};
-            mma_u8s8_16832_acc(d, a, xw[i] & xf.m0, xw[i] & xf.m1);
-        }
-        const float f = sx[G] * hi_scale;
-        acc[0] = fmaf(dsg[G] * f, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], xs[G], acc[0]));
-        acc[1] = fmaf(dsh[G] * f, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], xs[G], acc[1]));
-    }
-}
-
-// Item cursor of one warp: CTA iteration `it`, j-th segment of the warp.
+// Item cursor of one warp: CTA iteration `it`, j-th item of the warp in that
+// iteration.  Items of a row block are its segments seg0, seg0 + wpb, ...;
+// with SwiGLU every segment is two items (gate rows, then up rows).
 struct MmaCursor {
     int64_t it;
     int j;
@@ -1276,29 +1219,106 @@ __device__ __forceinline__ int64_t mma_block(const QParams &p, int64_t it, int w
     return (static_cast<int64_t>(blockIdx.x) + it * gridDim.x) * p.bpc + warp / p.wpb;
 }
 
-// Next existing item at or after c (segment index = warp % wpb + j * wpb); false when exhausted.
+__device__ __forceinline__ int mma_items(const QParams &p, int warp) {
+    const int segs = (p.nseg - warp % p.wpb + p.wpb - 1) / p.wpb;
+    return p.mode == MODE_SWIGLU ? 2 * segs : segs;
+}
+
 __device__ __forceinline__ bool mma_valid(const QParams &p, const MmaCursor &c, int warp, int64_t iters) {
     return c.it < iters && mma_block(p, c.it, warp) < p.total_rowsets;
 }
 
 __device__ __forceinline__ void mma_advance(const QParams &p, MmaCursor &c, int warp) {
-    if (warp % p.wpb + (c.j + 1) * p.wpb < p.nseg) {
-        ++c.j;
-    } else {
+    if (++c.j == mma_items(p, warp)) {
         c.j = 0;
         ++c.it;
     }
 }
 
-__device__ __forceinline__ void mma_issue(const QParams &p, int64_t block, int seg, uint8_t *stage, uint64_t *bar) {
+// Issues item j of a row block: one 16-row x 288-byte TMA box.
+__device__ __forceinline__ void mma_issue(const QParams &p, int warp, int64_t block, int j, uint8_t *stage,
+                                          uint64_t *bar) {
     const bool swiglu = p.mode == MODE_SWIGLU;
-    const int si = swiglu ? 0 : stream_of(p, block);
-    const int row0 = static_cast<int>((block - p.s[si].rs_begin) * kMmaRows);
-    const int groups = swiglu ? 2 : 1;
+    const int si = swiglu ? (j & 1) : stream_of(p, block);
+    const int seg = warp % p.wpb + (swiglu ? (j >> 1) : j) * p.wpb;
+    const int row0 = static_cast<int>((block - p.s[swiglu ? 0 : si].rs_begin) * kMmaRows);
     // rows past N are zero-filled by the TMA unit and still count toward the transaction bytes
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(groups * kMmaRows * kMmaSegBytes));
-    for (int gi = 0; gi < groups; ++gi)
-        tma_load_2d(stage + gi * kMmaRows * kMmaSegBytes, &p.tmap[swiglu ? gi : si], seg * (kMmaSegBytes / 4), row0, bar);
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kMmaRows * kMmaSegBytes));
+    tma_load_2d(stage, &p.tmap[si], seg * (kMmaSegBytes / 4), row0, bar);
+}
+
+// Split-K partials of a row block meet in a shared-memory slot: each warp of the
+// block's group adds its rows, and the last to arrive applies the epilogue.
+// Slot (iteration % kMmaSlots, group) is reused once the previous use is done
+// (generation counter); the wait for that is bounded.
+constexpr int kMmaSlots = 4;
+struct MmaSlot {
+    float v[2][kMmaRows][4];  // [gate/up or value][row][batch row]
+    int arrived;
+    int gen;
+};
+
+__device__ __forceinline__ bool slot_wait_gen(volatile int *gen, int want) {
+    if (*gen == want) return true;
+    const uint64_t start = global_timer_ns();
+    while (*gen != want) {
+        __nanosleep(64);
+        if (global_timer_ns() - start > 2000000000ull) return false;
+    }
+    return true;
+}
+
+template <int MT>
+__device__ __forceinline__ void mma_finish_block(const QParams &p, int64_t block, const float v[2][2], int lane) {
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int g = lane >> 2, t = lane & 3;
+    const int si = swiglu ? 0 : stream_of(p, block);
+    const QStream &st = p.s[si];
+    const int64_t row0 = (block - st.rs_begin) * kMmaRows;
+    const int64_t na = row0 + g, nb = row0 + g + 8;
+    if (p.mode == MODE_ARGMAX) {
+        // groups of 4 rows: lanes (g, t) with g in one quad; ties keep the lower row
+        float best[2] = {na < st.n ? v[0][0] : -INFINITY, nb < st.n ? v[0][1] : -INFINITY};
+        uint32_t tok[2] = {static_cast<uint32_t>(na), static_cast<uint32_t>(nb)};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int o = 4; o <= 8; o <<= 1) {
+                const float ob = __shfl_xor_sync(0xffffffffu, best[h], o);
+                const uint32_t ot = __shfl_xor_sync(0xffffffffu, tok[h], o);
+                if (ob > best[h] || (ob == best[h] && ot < tok[h])) {
+                    best[h] = ob;
+                    tok[h] = ot;
+                }
+            }
+        }
+        if ((g & 3) == 0 && t < p.M) {
+            if (na < st.n) {
+                p.ps[t * p.G + (na >> 2)] = best[0];
+                p.pt[t * p.G + (na >> 2)] = tok[0];
+            }
+            if (nb < st.n) {
+                p.ps[t * p.G + (nb >> 2)] = best[1];
+                p.pt[t * p.G + (nb >> 2)] = tok[1];
+            }
+        }
+        return;
+    }
+    if (t >= p.M) return;
+    const int64_t rows[2] = {na, nb};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (rows[h] >= st.n) continue;
+        const int64_t o = t * st.n + rows[h];
+        float val;
+        if (swiglu) {
+            val = silu(v[0][h]) * v[1][h];
+        } else {
+            val = v[0][h];
+            if (st.res) val += __half2float(st.res[o]);
+        }
+        st.y[o] = __float2half_rn(val);
+    }
 }
 
 template <int MT>
@@ -1308,11 +1328,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.stages;
     const bool swiglu = p.mode == MODE_SWIGLU;
-    const int R = swiglu ? 2 : 1;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
     uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
-    float *red = reinterpret_cast<float *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes);
-    float4 *meta = reinterpret_cast<float4 *>(red + kMmaWarps * 32 * 4);
+    MmaSlot *slots = reinterpret_cast<MmaSlot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes);
+    float4 *meta = reinterpret_cast<float4 *>(slots + kMmaSlots * kMmaWarps);
     int8_t *xh = reinterpret_cast<int8_t *>(meta + MT * (K >> 6));
     int8_t *xl = xh + MT * padded_k(K) + 32;  // +32: xh / xl fragments of one k on different banks
     float *sx = reinterpret_cast<float *>(xl + MT * padded_k(K));
@@ -1320,18 +1339,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
     float *pred = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
     const int64_t iters = (p.total_rowsets + static_cast<int64_t>(gridDim.x) * p.bpc - 1) /
                           (static_cast<int64_t>(gridDim.x) * p.bpc);
-    const int seg0 = warp % p.wpb;
+    const int group = warp / p.wpb;
 
     MmaCursor ahead{0, 0};
     if (lane == 0) {
         for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
         fence_mbar_init();
         for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) {
-            mma_issue(p, mma_block(p, ahead.it, warp), seg0 + ahead.j * p.wpb,
-                      stages + static_cast<size_t>(i) * p.stage_bytes, &full[i]);
+            mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j, stages + static_cast<size_t>(i) * p.stage_bytes,
+                      &full[i]);
             mma_advance(p, ahead, warp);
         }
     }
+    for (int i = threadIdx.x; i < kMmaSlots * kMmaWarps * static_cast<int>(sizeof(MmaSlot) / 4); i += kMmaThreads)
+        reinterpret_cast<int *>(slots)[i] = 0;
     pdl_wait();
     pdl_trigger();
     prepare_x<MT, kMmaThreads>(p, xh, xl, sx, xq16, meta, pred);  // ends with a CTA barrier
@@ -1341,127 +1362,345 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
     for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) mma_advance(p, ahead, warp);
 
     const uint32_t stages_addr = smem_u32(stages);
+    const int items = mma_items(p, warp);
+    const int g = lane >> 2, t = lane & 3;
     int s = 0;
     uint32_t phase = 0;
     bool failed = false;
     for (int64_t it = 0; it < iters; ++it) {
         const int64_t block = mma_block(p, it, warp);
+        if (block >= p.total_rowsets) break;  // later iterations have no block either
         float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-        if (block < p.total_rowsets) {
-            for (int seg = seg0; seg < p.nseg; seg += p.wpb) {
-                if (!failed && !mbar_wait(&full[s], phase)) {
-                    report_device_error(T2C_ETIMEOUT);
-                    failed = true;
-                }
-                if (!failed) {
-                    const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
-                    const int kseg = seg * kMmaSegBlocks * 256;
-                    const int g = lane >> 2;
+        for (int j = 0; j < items; ++j) {
+            if (!failed && !mbar_wait(&full[s], phase)) {
+                report_device_error(T2C_ETIMEOUT);
+                failed = true;
+            }
+            if (!failed) {
+                const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
+                const bool up = swiglu && (j & 1);
+                const int seg = warp % p.wpb + (swiglu ? (j >> 1) : j) * p.wpb;
+                const int kseg = seg * kMmaSegBlocks * 256;
+                float part[2] = {0.0f, 0.0f};
 #pragma unroll
-                    for (int sb = 0; sb < kMmaSegBlocks; ++sb) {
-                        if constexpr (MT == 1) {
-                            const M1X xf = m1_x(x, kseg + sb * 256, lane);
-#pragma unroll
-                            for (int r = 0; r < 2; ++r) {
-                                if (r < R)
-                                    mma_q4k_block_m1(
-                                        stage + static_cast<uint32_t>((r * kMmaRows + g) * kMmaSegBytes + sb * 144),
-                                        kMmaSegBytes, kseg + sb * 256, x, xf, lane, acc[r]);
-                            }
-                        } else {
-#pragma unroll
-                            for (int r = 0; r < 2; ++r) {
-                                if (r < R)
-                                    mma_q4k_block(
-                                        stage + static_cast<uint32_t>((r * kMmaRows + g) * kMmaSegBytes + sb * 144),
-                                        kMmaSegBytes, kseg + sb * 256, x, lane, p.M, acc[r]);
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0 && mma_valid(p, ahead, warp, iters)) {
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        mma_issue(p, mma_block(p, ahead.it, warp), seg0 + ahead.j * p.wpb,
-                                  stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
-                    }
-                    if (mma_valid(p, ahead, warp, iters)) mma_advance(p, ahead, warp);
+                for (int sb = 0; sb < kMmaSegBlocks; ++sb)
+                    mma_q4k_block(stage + static_cast<uint32_t>(g * kMmaSegBytes + sb * 144), kMmaSegBytes,
+                                  kseg + sb * 256, x, lane, p.M, part);
+                acc[0][0] += up ? 0.0f : part[0];
+                acc[0][1] += up ? 0.0f : part[1];
+                acc[1][0] += up ? part[0] : 0.0f;
+                acc[1][1] += up ? part[1] : 0.0f;
+                __syncwarp();
+                if (lane == 0 && mma_valid(p, ahead, warp, iters)) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j,
+                              stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
                 }
-                if (++s == S) {
-                    s = 0;
-                    phase ^= 1u;
-                }
+                if (mma_valid(p, ahead, warp, iters)) mma_advance(p, ahead, warp);
+            }
+            if (++s == S) {
+                s = 0;
+                phase ^= 1u;
             }
         }
-        if constexpr (MT == 1) {
-            // the four lanes of a quad hold disjoint sub-blocks of the same rows
-#pragma unroll
-            for (int r = 0; r < 2; ++r)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 1);
-                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
-                }
+        if (p.wpb == 1) {
+            mma_finish_block<MT>(p, block, acc, lane);
+            continue;
         }
-        // combine the wpb warps of each row block
-        *reinterpret_cast<float4 *>(red + (warp * 32 + lane) * 4) = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+        MmaSlot *slot = slots + (it % kMmaSlots) * kMmaWarps + group;
+        if (!slot_wait_gen(&slot->gen, static_cast<int>(it / kMmaSlots))) {
+            report_device_error(T2C_ETIMEOUT);
+            failed = true;
+            continue;
+        }
+        if (t < p.M) {  // lane (g, t) holds rows g, g+8 of batch row t
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                atomicAdd(&slot->v[r][g][t], acc[r][0]);
+                atomicAdd(&slot->v[r][g + 8][t], acc[r][1]);
+            }
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&slot->arrived, 1) == p.wpb - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence_block();
+        float v[2][2];
+        const int tm = t < p.M ? t : 0;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            v[r][0] = *reinterpret_cast<volatile float *>(&slot->v[r][g][tm]);
+            v[r][1] = *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][tm]);
+        }
+        mma_finish_block<MT>(p, block, v, lane);
+        __syncwarp();
+        if (t < p.M) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                slot->v[r][g][t] = 0.0f;
+                slot->v[r][g + 8][t] = 0.0f;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            slot->arrived = 0;
+            __threadfence_block();
+            *reinterpret_cast<volatile int *>(&slot->gen) = slot->gen + 1;
+        }
+    }
+}
+
+// ------------------------------------------------ M = 1 kernel, per-warp x
+// Same streaming and split-K as qmv_mma_kernel, but each warp quantizes only
+// the x values of its own K-segments (after, when there is a fused RMSNorm,
+// a warp-local sum of squares over the whole row), so the prologue has no
+// CTA barrier and x costs ~1.2 KB of shared memory per segment: two CTAs fit
+// on an SM.  Per segment: xh[512], 32-byte gap, xl[512], then (sx, xs) per
+// 32-value sub-block.
+constexpr int kM1SegX = 512 + 32 + 512 + 32;      // plane bytes (+ gaps)
+constexpr int kM1SegBytes = kM1SegX + 16 * 8;    // + meta
+constexpr int kM1MaxSegs = 16;                   // per warp (K <= 65536)
+
+// Quantizes values [k0, k0 + 512) of x into one segment area.
+__device__ __forceinline__ void m1_prepare_segment(const QParams &p, int k0, float inv_rms, uint8_t *area, int lane) {
+    const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + k0 + 16 * lane);
+    float f[16];
+    unpack8(xv[0], f);
+    unpack8(xv[1], f + 8);
+    if (p.norm_w != nullptr) {
+        const float4 *wv = reinterpret_cast<const float4 *>(p.norm_w + k0 + 16 * lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 w4 = wv[i];
+            f[4 * i] *= inv_rms * w4.x;
+            f[4 * i + 1] *= inv_rms * w4.y;
+            f[4 * i + 2] *= inv_rms * w4.z;
+            f[4 * i + 3] *= inv_rms * w4.w;
+        }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));  // lanes 2i, 2i+1 = sub-block i
+    const float inv = amax > 0.0f ? 16383.0f / amax : 0.0f;
+    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        int q = __float2int_rn(f[e] * inv);
+        q = max(-16383, min(16383, q));
+        sum += q;
+        hw[e >> 2] |= (static_cast<uint32_t>(q >> 7) & 0xffu) << (8 * (e & 3));
+        lw[e >> 2] |= static_cast<uint32_t>(q & 127) << (8 * (e & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    *reinterpret_cast<uint4 *>(area + 16 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(area + 512 + 32 + 16 * lane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    if ((lane & 1) == 0) {
+        const float sx = amax / 16383.0f;
+        *reinterpret_cast<float2 *>(area + kM1SegX + 8 * (lane >> 1)) = make_float2(sx, sx * static_cast<float>(sum));
+    }
+}
+
+// One 144-byte block (values voff .. voff+255 of the segment) of a 16-row group.
+__device__ __forceinline__ void m1_block(uint32_t rowg, uint32_t row_stride, uint32_t seg_area, int voff, int lane,
+                                         float acc[2]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t rowg8 = rowg + 8u * row_stride;
+    const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
+    float dsg[2], dmg[2], dsh[2], dmh[2];
+    q4k_lane_scales(hg, t, dsg, dmg);
+    q4k_lane_scales(hg8, t, dsh, dmh);
+    const uint32_t nib = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+    const float hi_scale = (t & 1) ? 0.0625f : 1.0f;
+    // B fragments: column s*2 + plane carries plane (g & 1) of sub-block 4G + s, values
+    // 16 (t & 1) .. +15, in the lanes whose k-slots belong to that sub-block (else zero)
+    const int s = g >> 1;
+    const bool active = (t >> 1) == (s & 1);
+    const uint32_t m0 = (active && s < 2) ? 0xffffffffu : 0u, m1 = (active && s >= 2) ? 0xffffffffu : 0u;
+    const uint32_t plane = seg_area + ((g & 1) ? 512u + 32u : 0u) + static_cast<uint32_t>(voff + 16 * (t & 1));
+    const uint32_t meta = seg_area + kM1SegX + 8u * static_cast<uint32_t>((voff >> 5) + t);
+    const uint32_t off = 16u + 16u * static_cast<uint32_t>(t & 1);
+#pragma unroll
+    for (int G = 0; G < 2; ++G) {
+        const uint4 X = active ? lds128(plane + 32u * static_cast<uint32_t>(4 * G + s)) : make_uint4(0u, 0u, 0u, 0u);
+        const uint2 mt = lds64(meta + 32u * G);  // (sx, xs) of sub-block 4G + t
+        const uint4 qa = lds128(rowg + off + 64 * G), qb = lds128(rowg + off + 64 * G + 32);
+        const uint4 ra = lds128(rowg8 + off + 64 * G), rb = lds128(rowg8 + off + 64 * G + 32);
+        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
+        const uint32_t va[4] = {ra.x, ra.y, ra.z, ra.w}, vb[4] = {rb.x, rb.y, rb.z, rb.w};
+        const uint32_t xw[4] = {X.x, X.y, X.z, X.w};
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t a[4] = {wa[i] & nib, va[i] & nib, wb[i] & nib, vb[i] & nib};
+            mma_u8s8_16832_acc(d, a, xw[i] & m0, xw[i] & m1);
+        }
+        const float f = __uint_as_float(mt.x) * hi_scale, xs = __uint_as_float(mt.y);
+        acc[0] = fmaf(dsg[G] * f, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], xs, acc[0]));
+        acc[1] = fmaf(dsh[G] * f, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], xs, acc[1]));
+    }
+}
+
+__global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_constant__ QParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.stages;
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int nsegw = (p.nseg - warp % p.wpb + p.wpb - 1) / p.wpb;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
+    uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
+    uint8_t *xarea = smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
+                     static_cast<size_t>(warp) * p.xseg_per_warp * kM1SegBytes;
+    MmaSlot *slots = reinterpret_cast<MmaSlot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
+                                                 static_cast<size_t>(kMmaWarps) * p.xseg_per_warp * kM1SegBytes);
+    const int64_t iters = (p.total_rowsets + static_cast<int64_t>(gridDim.x) * p.bpc - 1) /
+                          (static_cast<int64_t>(gridDim.x) * p.bpc);
+    const int group = warp / p.wpb;
+
+    MmaCursor ahead{0, 0};
+    if (lane == 0) {
+        for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+        fence_mbar_init();
+        for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) {
+            mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j, stages + static_cast<size_t>(i) * p.stage_bytes,
+                      &full[i]);
+            mma_advance(p, ahead, warp);
+        }
+    }
+    for (int i = threadIdx.x; i < kMmaSlots * p.bpc * static_cast<int>(sizeof(MmaSlot) / 4); i += kMmaThreads)
+        reinterpret_cast<int *>(slots)[i] = 0;
+    __syncthreads();  // mbarrier init and slot zeroing visible to every warp
+    pdl_wait();
+    pdl_trigger();
+    // this warp's x segments; with a fused RMSNorm the wpb warps of a group
+    // (which together hold every segment of the row) add their sums of squares
+    // through shared memory (one CTA barrier)
+    float inv_rms = 1.0f;
+    if (p.norm_w != nullptr) {
+        float ss = 0.0f;
+        for (int j = 0; j < nsegw; ++j) {
+            const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + (warp % p.wpb + j * p.wpb) * (kMmaSegBlocks * 256));
+            float f[16];
+            unpack8(xv[2 * lane], f);
+            unpack8(xv[2 * lane + 1], f + 8);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ss = fmaf(f[e], f[e], ss);
+        }
+        ss = warp_sum(ss);
+        float *sq = reinterpret_cast<float *>(slots + kMmaSlots * p.bpc);
+        if (lane == 0) sq[warp] = ss;
         __syncthreads();
-        if (seg0 == 0 && block < p.total_rowsets) {
-            for (int w = warp + 1; w < warp + p.wpb; ++w) {
-                const float4 o = *reinterpret_cast<const float4 *>(red + (w * 32 + lane) * 4);
-                acc[0][0] += o.x;
-                acc[0][1] += o.y;
-                acc[1][0] += o.z;
-                acc[1][1] += o.w;
+        float tot = 0.0f;
+        for (int w = group * p.wpb; w < (group + 1) * p.wpb; ++w) tot += sq[w];
+        inv_rms = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
+    }
+    for (int j = 0; j < nsegw; ++j)
+        m1_prepare_segment(p, (warp % p.wpb + j * p.wpb) * (kMmaSegBlocks * 256), inv_rms, xarea + j * kM1SegBytes,
+                           lane);
+    __syncwarp();
+    ahead = MmaCursor{0, 0};
+    for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) mma_advance(p, ahead, warp);
+
+    const uint32_t stages_addr = smem_u32(stages), x_addr = smem_u32(xarea);
+    const int items = mma_items(p, warp);
+    const int g = lane >> 2, t = lane & 3;
+    int s = 0;
+    uint32_t phase = 0;
+    bool failed = false;
+    for (int64_t it = 0; it < iters; ++it) {
+        const int64_t block = mma_block(p, it, warp);
+        if (block >= p.total_rowsets) break;  // later iterations have no block either
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        for (int j = 0; j < items; ++j) {
+            if (!failed && !mbar_wait(&full[s], phase)) {
+                report_device_error(T2C_ETIMEOUT);
+                failed = true;
             }
-            const int g = lane >> 2, t = lane & 3;
-            const int si = swiglu ? 0 : stream_of(p, block);
-            const QStream &st = p.s[si];
-            const int64_t row0 = (block - st.rs_begin) * kMmaRows;
-            const int64_t na = row0 + g, nb = row0 + g + 8;
-            if (p.mode == MODE_ARGMAX) {
-                // groups of 4 rows: lanes (g, t) with g in one quad; ties keep the lower row
-                float best[2] = {na < st.n ? acc[0][0] : -INFINITY, nb < st.n ? acc[0][1] : -INFINITY};
-                uint32_t tok[2] = {static_cast<uint32_t>(na), static_cast<uint32_t>(nb)};
+            if (!failed) {
+                const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
+                const bool up = swiglu && (j & 1);
+                const int jl = swiglu ? (j >> 1) : j;
+                float part[2] = {0.0f, 0.0f};
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                    for (int o = 4; o <= 8; o <<= 1) {
-                        const float ob = __shfl_xor_sync(0xffffffffu, best[h], o);
-                        const uint32_t ot = __shfl_xor_sync(0xffffffffu, tok[h], o);
-                        if (ob > best[h] || (ob == best[h] && ot < tok[h])) {
-                            best[h] = ob;
-                            tok[h] = ot;
-                        }
-                    }
+                for (int sb = 0; sb < kMmaSegBlocks; ++sb)
+                    m1_block(stage + static_cast<uint32_t>(g * kMmaSegBytes + sb * 144), kMmaSegBytes,
+                             x_addr + static_cast<uint32_t>(jl * kM1SegBytes), sb * 256, lane, part);
+                acc[0][0] += up ? 0.0f : part[0];
+                acc[0][1] += up ? 0.0f : part[1];
+                acc[1][0] += up ? part[0] : 0.0f;
+                acc[1][1] += up ? part[1] : 0.0f;
+                __syncwarp();
+                if (lane == 0 && mma_valid(p, ahead, warp, iters)) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j,
+                              stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
                 }
-                if ((g & 3) == 0 && t < p.M) {
-                    if (na < st.n) {
-                        p.ps[t * p.G + (na >> 2)] = best[0];
-                        p.pt[t * p.G + (na >> 2)] = tok[0];
-                    }
-                    if (nb < st.n) {
-                        p.ps[t * p.G + (nb >> 2)] = best[1];
-                        p.pt[t * p.G + (nb >> 2)] = tok[1];
-                    }
-                }
-            } else if (t < p.M) {
-                const int64_t rows[2] = {na, nb};
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (rows[h] >= st.n) continue;
-                    const int64_t o = t * st.n + rows[h];
-                    float v;
-                    if (swiglu) {
-                        v = silu(acc[0][h]) * acc[1][h];
-                    } else {
-                        v = acc[0][h];
-                        if (st.res) v += __half2float(st.res[o]);
-                    }
-                    st.y[o] = __float2half_rn(v);
-                }
+                if (mma_valid(p, ahead, warp, iters)) mma_advance(p, ahead, warp);
+            }
+            if (++s == S) {
+                s = 0;
+                phase ^= 1u;
             }
         }
-        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 1);
+                acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
+            }
+        if (p.wpb == 1) {
+            mma_finish_block<1>(p, block, acc, lane);
+            continue;
+        }
+        MmaSlot *slot = slots + (it % kMmaSlots) * p.bpc + group;
+        if (!slot_wait_gen(&slot->gen, static_cast<int>(it / kMmaSlots))) {
+            report_device_error(T2C_ETIMEOUT);
+            failed = true;
+            continue;
+        }
+        if (t == 0) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                atomicAdd(&slot->v[r][g][0], acc[r][0]);
+                atomicAdd(&slot->v[r][g + 8][0], acc[r][1]);
+            }
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&slot->arrived, 1) == p.wpb - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence_block();
+        float v[2][2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            v[r][0] = *reinterpret_cast<volatile float *>(&slot->v[r][g][0]);
+            v[r][1] = *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][0]);
+        }
+        mma_finish_block<1>(p, block, v, lane);
+        __syncwarp();
+        if (t == 0) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                slot->v[r][g][0] = 0.0f;
+                slot->v[r][g + 8][0] = 0.0f;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            slot->arrived = 0;
+            __threadfence_block();
+            *reinterpret_cast<volatile int *>(&slot->gen) = slot->gen + 1;
+        }
     }
 }
 
@@ -1718,7 +1957,7 @@ int encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row
 }
 
 size_t mma_fixed_smem(int MT, int K) {
-    return kStageHead + static_cast<size_t>(kMmaWarps) * 32 * 4 * 4 + static_cast<size_t>(MT) * (K / 64) * 16 +
+    return kStageHead + kMmaSlots * kMmaWarps * sizeof(MmaSlot) + static_cast<size_t>(MT) * (K / 64) * 16 +
            2 * static_cast<size_t>(MT) * padded_k(K) + 32 + static_cast<size_t>(MT) * (K / 32) * 4 +
            static_cast<size_t>(MT) * (K / 16) * 4 + static_cast<size_t>(kMmaWarps) * MT * 4;
 }
@@ -1734,10 +1973,37 @@ int launch_mma(QParams p, cudaStream_t stream) {
     const size_t smem = fixed + per_stage * p.stages;
     int rc = ensure_smem_attr(qmv_mma_kernel<MT>, configured[device_slot()]);
     if (rc) return rc;
-    int64_t blocks = (p.total_rowsets + p.bpc - 1) / p.bpc;
-    const int64_t cap = sm_count();
-    if (blocks > cap) blocks = cap;
+    // the same number of CTA iterations for every CTA
+    const int64_t groups = (p.total_rowsets + p.bpc - 1) / p.bpc;
+    const int64_t iters = (groups + sm_count() - 1) / sm_count();
+    const int64_t blocks = (groups + iters - 1) / iters;
     return launch_pdl(qmv_mma_kernel<MT>, static_cast<int>(blocks), kMmaThreads, smem, stream, p);
+}
+
+int launch_m1(QParams p, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    p.xseg_per_warp = (p.nseg + p.wpb - 1) / p.wpb;
+    if (p.xseg_per_warp > kM1MaxSegs) return set_error(T2C_EUNSUPPORTED, "qmv_m1: K too large");
+    const size_t fixed = kStageHead + static_cast<size_t>(kMmaWarps) * p.xseg_per_warp * kM1SegBytes +
+                         static_cast<size_t>(kMmaSlots) * p.bpc * sizeof(MmaSlot) + kMmaWarps * sizeof(float);
+    const size_t per_stage = static_cast<size_t>(kMmaWarps) * p.stage_bytes;
+    // two CTAs per SM when two stages per warp fit in half of the shared memory, else one CTA with more stages
+    const size_t half = 113 * 1024;
+    int per_sm = 1;
+    if (fixed + 2 * per_stage <= half) {
+        per_sm = 2;
+        p.stages = static_cast<int>((half - fixed) / per_stage);
+    } else {
+        p.stages = fixed >= kSmemLimit ? 0 : static_cast<int>((kSmemLimit - fixed) / per_stage);
+    }
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    if (p.stages < 2) return set_error(T2C_EUNSUPPORTED, "qmv_m1: stages do not fit");
+    const size_t smem = fixed + per_stage * p.stages;
+    int rc = ensure_smem_attr(qmv_m1_kernel, configured[device_slot()]);
+    if (rc) return rc;
+    int64_t blocks = (p.total_rowsets + p.bpc - 1) / p.bpc;
+    if (blocks > static_cast<int64_t>(sm_count()) * per_sm) blocks = static_cast<int64_t>(sm_count()) * per_sm;
+    return launch_pdl(qmv_m1_kernel, static_cast<int>(blocks), kMmaThreads, smem, stream, p);
 }
 
 bool mma_disabled() {
@@ -1756,7 +2022,7 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
         if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
     const bool swiglu = p.mode == MODE_SWIGLU;
     const int MT = M <= 1 ? 1 : (M <= 2 ? 2 : 4);
-    p.stage_bytes = (swiglu ? 2 : 1) * kMmaRows * kMmaSegBytes;
+    p.stage_bytes = kMmaRows * kMmaSegBytes;
     if (mma_fixed_smem(MT, p.K) + 2 * static_cast<size_t>(kMmaWarps) * p.stage_bytes > kSmemLimit) return T2C_OK;
     p.nseg = p.K / (kMmaSegBlocks * 256);
     p.wpb = 1;
@@ -1777,7 +2043,7 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     }
     used = true;
     switch (MT) {
-        case 1: return launch_mma<1>(p, stream);
+        case 1: return launch_m1(p, stream);
         case 2: return launch_mma<2>(p, stream);
         default: return launch_mma<4>(p, stream);
     }
