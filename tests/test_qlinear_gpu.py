@@ -189,3 +189,41 @@ def test_q4k_dp4a_kernel_still_matches(tmp_path):
     env = dict(os.environ, T2C_QMV_DP4A="1", PYTHONPATH=str(Path(__file__).resolve().parents[1]))
     r = subprocess.run([sys.executable, str(script)], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 128, 256), (16, 1030, 1024), (64, 384, 4096), (300, 200, 2048),
+                                   (33, 96, 12288)])
+def test_q4k_gemm_tensor_cores(oracle, m, n, k):
+    """M > 4: the tcgen05 GEMM (weights dequantized to fp16 in shared memory, fp32 TMEM accumulators)."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m * 7 + n + k)
+    packed = oracle.quantize(_weights(rng, n, k), "q4_k")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    w = oracle.dequantize(packed, "q4_k", k).astype(np.float16).astype(np.float64)  # fp16 operands
+    ref = x.astype(np.float64) @ w.T + res
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q4_k", k,
+                       residual=torch.from_numpy(res).cuda())
+    _tol_check(y.float().cpu().numpy(), ref, rel=3e-3)
+
+
+@pytest.mark.parametrize("m", [7, 130])
+def test_q4k_gemm_swiglu_and_norm(oracle, m):
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m)
+    n, k = 640, 1024
+    pg = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+    pu = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    nw = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    xf = x.astype(np.float32)
+    xn = (xf / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + 1e-6) * nw).astype(np.float16).astype(np.float64)
+    g = xn @ oracle.dequantize(pg, "q4_k", k).astype(np.float16).astype(np.float64).T
+    u = xn @ oracle.dequantize(pu, "q4_k", k).astype(np.float16).astype(np.float64).T
+    ref = g / (1.0 + np.exp(-g)) * u
+    y = kernels.linear_swiglu(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(), torch.from_numpy(pu).cuda(),
+                              "q4_k", k, norm_weight=torch.from_numpy(nw).cuda())
+    _tol_check(y.float().cpu().numpy(), ref, rel=5e-3)
+    assert kernels.device_status() == 0

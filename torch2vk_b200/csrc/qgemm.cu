@@ -1,0 +1,379 @@
+// Q4_K GEMM on tcgen05 tensor cores with TMEM accumulators (M > 4 tokens:
+// prefill, batched decode).  The weights are the A operand: a CTA owns 128
+// weight rows (UMMA M = 128) and mt tokens (UMMA N = mt, <= 256), so
+//   D[n, m] = sum_k deq(W)[n, k] * x[m, k]     (fp32 in TMEM, 128 lanes x mt columns)
+// and the epilogue writes y[m, n] (+ residual) or silu(gate) * up.
+//
+// Per K chunk of 64 values (one 128-byte row of a 128B-swizzled K-major atom):
+//  * raw Q4_K super-blocks of the 128 rows arrive by 2-D TMA (box 144 B x 128
+//    rows, two stages; requested before griddepcontrol.wait: weights are static);
+//  * x[mt, 64] fp16 arrives by 2-D TMA with 128-byte swizzle (three buffers,
+//    two chunks ahead);
+//  * the 128 threads dequantize one row each, d*sc*q - dmin*m in fp32 rounded
+//    to fp16, straight into the swizzled K-major A layout (three buffers);
+//  * one thread issues 4 x tcgen05.mma kind::f16 (K = 16 each) and commits
+//    them to the buffer's mbarrier, which also tells when A / x may be reused.
+// Descriptors (PTX ISA "shared memory descriptor" / "instruction descriptor"):
+// K-major SWIZZLE_128B: start >> 4, LBO 1, SBO 1024 >> 4, version 1, layout 2;
+// a K step of 16 fp16 advances the start address by 32 bytes.
+// Every wait is bounded; on a timeout the kernel reports T2C_ETIMEOUT, stops
+// issuing, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "qgemm.cuh"
+
+namespace t2c {
+namespace {
+
+constexpr int kRowsT = 128;                 // weight rows per CTA (UMMA M)
+constexpr int kKC = 64;                     // values per K chunk
+constexpr int kNB = 3;                      // A / x buffers
+constexpr int kRawBytes = kRowsT * 144;     // one super-block of 128 rows
+constexpr int kABytes = kRowsT * kKC * 2;   // 16 KB of fp16
+constexpr int kThreadsG = 128;
+
+struct GemmParams {
+    alignas(64) CUtensorMap wmap;  // raw Q4_K words [N, row_bytes / 4], box 36 x 128
+    alignas(64) CUtensorMap umap;  // up weight (SwiGLU)
+    alignas(64) CUtensorMap xmap;  // x fp16 [M, K], box 64 x mt, 128-byte swizzle
+    __half *y;
+    const __half *res;
+    int64_t N, M;
+    int K, mt, swiglu, tmem_cols;
+};
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1u) << 16) |
+           (static_cast<uint64_t>(1024u >> 4) << 32) | (static_cast<uint64_t>(1u) << 46) |
+           (static_cast<uint64_t>(2u) << 61);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc ? 1u : 0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float small_u2f_g(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+// Row r of one 64-value quarter q of a 144-byte Q4_K block -> 8 swizzled 16-byte chunks of fp16.
+__device__ __forceinline__ void dequant_quarter(uint32_t raw_row, int q, uint32_t a_row, int r) {
+    uint4 h;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(h.x), "=r"(h.y), "=r"(h.z), "=r"(h.w) : "r"(raw_row));
+    uint4 n0, n1;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(n0.x), "=r"(n0.y), "=r"(n0.z), "=r"(n0.w)
+                 : "r"(raw_row + 16 + 32 * q));
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(n1.x), "=r"(n1.y), "=r"(n1.z), "=r"(n1.w)
+                 : "r"(raw_row + 32 + 32 * q));
+    // 6-bit codes of sub-blocks 2q (low nibbles) and 2q+1 (high nibbles), packing of quantize/vulkan.py:331-342
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const int i0 = (2 * q) & 3;
+    const bool low = q < 2;
+    const uint32_t y = h.y >> (8 * i0), z = h.z >> (8 * i0), w = h.w >> (8 * i0);
+    const uint32_t hs = ((y >> 6) & 0x3u) | (((y >> 14) & 0x3u) << 8);
+    const uint32_t hm = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
+    const uint32_t scp = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hs << 4));
+    const uint32_t mnp = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hm << 4));
+    const float ds[2] = {d * small_u2f_g(scp & 0xffu), d * small_u2f_g(scp >> 8)};
+    const float dm[2] = {dmin * small_u2f_g(mnp & 0xffu), dmin * small_u2f_g(mnp >> 8)};
+    const uint32_t wq[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const int half_sel = c >> 2;  // 0: low nibbles (values 0..31), 1: high nibbles (32..63)
+        const uint32_t w0 = wq[2 * (c & 3)], w1 = wq[2 * (c & 3) + 1];
+        uint32_t packed[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t src = e < 2 ? w0 : w1;
+            const int sh = 16 * (e & 1) + 4 * half_sel;
+            const float v0 = fmaf(ds[half_sel], small_u2f_g((src >> sh) & 0xFu), -dm[half_sel]);
+            const float v1 = fmaf(ds[half_sel], small_u2f_g((src >> (sh + 8)) & 0xFu), -dm[half_sel]);
+            const __half2 hv = __floats2half2_rn(v0, v1);
+            packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
+        }
+        const uint32_t dst = a_row + static_cast<uint32_t>(((c ^ (r & 7)) << 4));
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
+                     "r"(packed[2]), "r"(packed[3])
+                     : "memory");
+    }
+}
+
+__global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_constant__ GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand tiles
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = p.mt;
+    const bool swiglu = p.swiglu != 0;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRowsT;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * mt;
+    const int nsb = p.K / 256, nch = p.K / kKC;
+    const int xbytes = mt * 128;
+
+    uint8_t *ptr = smem;
+    const uint32_t a_base = smem_u32(ptr);
+    ptr += kNB * kABytes;
+    const uint32_t aup_base = smem_u32(ptr);
+    if (swiglu) ptr += kNB * kABytes;
+    const uint32_t x_base = smem_u32(ptr);
+    ptr += kNB * xbytes;
+    uint8_t *raw_ptr = ptr;
+    ptr += 2 * kRawBytes;
+    uint8_t *rawup_ptr = ptr;
+    if (swiglu) ptr += 2 * kRawBytes;
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(ptr);
+    uint64_t *x_full = raw_full + 2;
+    uint64_t *mma_done = x_full + kNB;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + kNB);
+    __shared__ int failed;
+
+    if (tid == 0) {
+        failed = 0;
+        for (int i = 0; i < 2; ++i) mbar_init(&raw_full[i], 1);
+        for (int i = 0; i < kNB; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&mma_done[i], 1);
+        }
+        fence_mbar_init();
+        // static weights: first two super-blocks before the dependency on the previous kernel
+        for (int s = 0; s < 2 && s < nsb; ++s) {
+            const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
+            mbar_arrive_expect_tx(&raw_full[s], bytes);
+            tma_load_2d(raw_ptr + s * kRawBytes, &p.wmap, s * 36, static_cast<int>(n0), &raw_full[s]);
+            if (swiglu) tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, s * 36, static_cast<int>(n0), &raw_full[s]);
+        }
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(static_cast<uint32_t>(p.tmem_cols))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0) {
+        for (int c = 0; c < kNB - 1 && c < nch; ++c) {
+            mbar_arrive_expect_tx(&x_full[c], static_cast<uint32_t>(xbytes));
+            tma_load_2d(smem + (x_base - a_base) + c * xbytes, &p.xmap, c * kKC, static_cast<int>(m0), &x_full[c]);
+        }
+    }
+    const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(mt >> 3) << 17) | (static_cast<uint32_t>(kRowsT >> 4) << 24);
+
+    for (int kc = 0; kc < nch; ++kc) {
+        const int sb = kc >> 2, q = kc & 3, b = kc % kNB;
+        if (q == 0 && !failed) {
+            if (!mbar_wait(&raw_full[sb & 1], static_cast<uint32_t>((sb >> 1) & 1))) failed = 1;
+        }
+        if (kc >= kNB && !failed) {
+            if (!mbar_wait(&mma_done[b], static_cast<uint32_t>(((kc - kNB) / kNB) & 1))) failed = 1;
+        }
+        __syncthreads();
+        if (failed) break;
+        const uint32_t raw_row = smem_u32(raw_ptr) + static_cast<uint32_t>((sb & 1) * kRawBytes + tid * 144);
+        dequant_quarter(raw_row, q, a_base + static_cast<uint32_t>(b * kABytes + tid * 128), tid);
+        if (swiglu) {
+            const uint32_t up_row = smem_u32(rawup_ptr) + static_cast<uint32_t>((sb & 1) * kRawBytes + tid * 144);
+            dequant_quarter(up_row, q, aup_base + static_cast<uint32_t>(b * kABytes + tid * 128), tid);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            if (q == 3 && sb + 2 < nsb) {
+                // every thread has read this raw stage: refill it with super-block sb + 2
+                const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
+                mbar_arrive_expect_tx(&raw_full[sb & 1], bytes);
+                tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb + 2) * 36, static_cast<int>(n0),
+                            &raw_full[sb & 1]);
+                if (swiglu)
+                    tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb + 2) * 36, static_cast<int>(n0),
+                                &raw_full[sb & 1]);
+            }
+            if (!mbar_wait(&x_full[b], static_cast<uint32_t>((kc / kNB) & 1))) {
+                failed = 1;
+            } else {
+                tc_fence_after();
+                const uint32_t xa = x_base + static_cast<uint32_t>(b * xbytes);
+                const uint32_t aa = a_base + static_cast<uint32_t>(b * kABytes);
+#pragma unroll
+                for (int s = 0; s < kKC / 16; ++s)
+                    umma_f16(tmem, sw128_desc(aa + 32 * s), sw128_desc(xa + 32 * s), idesc, kc > 0 || s > 0);
+                if (swiglu) {
+                    const uint32_t au = aup_base + static_cast<uint32_t>(b * kABytes);
+#pragma unroll
+                    for (int s = 0; s < kKC / 16; ++s)
+                        umma_f16(tmem + static_cast<uint32_t>(mt), sw128_desc(au + 32 * s), sw128_desc(xa + 32 * s),
+                                 idesc, kc > 0 || s > 0);
+                }
+                umma_commit(&mma_done[b]);
+                // x for chunk kc + 2 goes into the buffer of chunk kc - 1 once its MMAs are done
+                const int nx = kc + kNB - 1;
+                if (nx < nch) {
+                    const int bx = nx % kNB;
+                    if (kc >= 1 && !mbar_wait(&mma_done[bx], static_cast<uint32_t>(((kc - 1) / kNB) & 1))) {
+                        failed = 1;
+                    } else {
+                        mbar_arrive_expect_tx(&x_full[bx], static_cast<uint32_t>(xbytes));
+                        tma_load_2d(smem + (x_base - a_base) + bx * xbytes, &p.xmap, nx * kKC, static_cast<int>(m0),
+                                    &x_full[bx]);
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    bool ok = !failed;
+    if (ok) ok = mbar_wait(&mma_done[(nch - 1) % kNB], static_cast<uint32_t>(((nch - 1) / kNB) & 1));
+    if (!ok) {
+        if (tid == 0) report_device_error(T2C_ETIMEOUT);
+    } else {
+        tc_fence_after();
+        // epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane
+        const int64_t n = n0 + 32 * warp + lane;
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+        for (int c = 0; c < mt; c += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld16(lane_addr + static_cast<uint32_t>(c), g);
+            if (swiglu) tmem_ld16(lane_addr + static_cast<uint32_t>(mt + c), u);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int64_t m = m0 + c + j;
+                if (m < p.M && n < p.N) {
+                    const int64_t o = m * p.N + n;
+                    float v = __uint_as_float(g[j]);
+                    if (swiglu) {
+                        v = v / (1.0f + __expf(-v)) * __uint_as_float(u[j]);
+                    } else if (p.res != nullptr) {
+                        v += __half2float(p.res[o]);
+                    }
+                    p.y[o] = __float2half_rn(v);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(static_cast<uint32_t>(p.tmem_cols))
+                     : "memory");
+}
+
+PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+    }();
+    return encode;
+}
+
+bool encode_raw(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes) {
+    const auto enc = tensor_map_encoder();
+    if (!enc || row_bytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {36, kRowsT};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_x(CUtensorMap *map, const __half *x, int64_t m, int64_t k, int mt) {
+    const auto enc = tensor_map_encoder();
+    if (!enc || reinterpret_cast<uintptr_t>(x) % 16 || (k * 2) % 16) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k * 2)};
+    const cuuint32_t box[2] = {kKC, static_cast<cuuint32_t>(mt)};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
+    if (a.M <= 4 || a.K % 256 || a.K > 65536 || a.N <= 0 || a.N > INT32_MAX || a.M > INT32_MAX) return T2C_EUNSUPPORTED;
+    GemmParams p = {};
+    p.swiglu = a.w_up != nullptr;
+    const int cap = p.swiglu ? 128 : 256;
+    int64_t mt = (a.M + 15) / 16 * 16;
+    if (mt > cap) mt = cap;
+    p.mt = static_cast<int>(mt);
+    const int64_t row_bytes = a.K / 256 * 144;
+    if (!encode_raw(&p.wmap, a.w, a.N, row_bytes)) return T2C_EUNSUPPORTED;
+    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N, row_bytes)) return T2C_EUNSUPPORTED;
+    if (!encode_x(&p.xmap, a.x, a.M, a.K, p.mt)) return T2C_EUNSUPPORTED;
+    p.y = a.y;
+    p.res = a.res;
+    p.N = a.N;
+    p.M = a.M;
+    p.K = static_cast<int>(a.K);
+    int cols = 32;
+    while (cols < (p.swiglu ? 2 : 1) * p.mt) cols *= 2;
+    p.tmem_cols = cols;
+    const size_t smem = 1024 + static_cast<size_t>(kNB) * kABytes * (p.swiglu ? 2 : 1) +
+                        static_cast<size_t>(kNB) * p.mt * 128 + 2 * static_cast<size_t>(kRawBytes) * (p.swiglu ? 2 : 1) +
+                        (2 + 2 * kNB) * 8 + 16;
+    constexpr size_t kLimit = 226 * 1024;  // dynamic bytes; the kernel's static words sit beside them
+    if (smem > kLimit) return T2C_EUNSUPPORTED;
+    static bool configured[64] = {false};
+    int device = 0;
+    cudaGetDevice(&device);
+    const int slot = device < 0 ? 0 : (device > 63 ? 63 : device);
+    if (!configured[slot]) {
+        if (cudaFuncSetAttribute(qgemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kLimit)) !=
+            cudaSuccess)
+            return set_error(T2C_ECUDA, "qgemm: cudaFuncSetAttribute failed");
+        configured[slot] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((a.N + kRowsT - 1) / kRowsT), static_cast<unsigned>((a.M + p.mt - 1) / p.mt));
+    cfg.blockDim = dim3(kThreadsG);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, qgemm_q4k_kernel, p);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "qgemm launch: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+cudaError_t status_qgemm(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
+
+}  // namespace t2c

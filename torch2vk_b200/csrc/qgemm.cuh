@@ -1,0 +1,26 @@
+// Quantized GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) for
+// M > 4 tokens: y[m, n] = sum_k x[m, k] * deq(W)[n, k] (+ residual), or the
+// SwiGLU of two weights.  Internal interface between qlinear.cu and qgemm.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cuda_fp16.h>
+
+namespace t2c {
+
+struct QGemmArgs {
+    const uint8_t *w;      // Q4_K rows (row_bytes = K / 256 * 144), 16-byte aligned
+    const uint8_t *w_up;   // SwiGLU: the up weight (same shape), else nullptr
+    int64_t N, K, M;
+    const __half *x;       // [M, K], 16-byte aligned rows
+    __half *y;             // [M, N]
+    const __half *res;     // [M, N] or nullptr
+};
+
+// Returns T2C_OK, or T2C_EUNSUPPORTED when the shape is not served (caller falls back).
+int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream);
+cudaError_t status_qgemm(unsigned int *bits, int clear, cudaStream_t s);
+
+}  // namespace t2c

@@ -31,6 +31,8 @@
 #include <cudaTypedefs.h>
 #include <stdio.h>
 
+#include "qgemm.cuh"
+
 #include "common.cuh"
 
 namespace t2c {
@@ -2049,8 +2051,44 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     }
 }
 
+// M > 4, every stream Q4_K, no fused RMSNorm, not argmax: tcgen05 GEMM per stream.
+int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
+    used = false;
+    if (mma_disabled() || M <= 4 || p.mode == MODE_ARGMAX || p.norm_w != nullptr) return T2C_OK;
+    for (int i = 0; i < p.nstreams; ++i)
+        if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
+    QGemmArgs a = {};
+    a.K = p.K;
+    a.M = M;
+    a.x = p.x;
+    if (p.mode == MODE_SWIGLU) {
+        a.w = p.s[0].w;
+        a.w_up = p.s[1].w;
+        a.N = p.s[0].n;
+        a.y = p.s[0].y;
+        const int rc = qgemm_q4k(a, stream);
+        if (rc == T2C_EUNSUPPORTED) return T2C_OK;
+        used = true;
+        return rc;
+    }
+    for (int i = 0; i < p.nstreams; ++i) {
+        a.w = p.s[i].w;
+        a.w_up = nullptr;
+        a.N = p.s[i].n;
+        a.y = p.s[i].y;
+        a.res = p.s[i].res;
+        const int rc = qgemm_q4k(a, stream);
+        if (rc == T2C_EUNSUPPORTED && i == 0) return T2C_OK;  // nothing launched yet: fall back
+        if (rc != T2C_OK) return rc == T2C_EUNSUPPORTED ? set_error(T2C_EUNSUPPORTED, "qgemm: stream %d", i) : rc;
+    }
+    used = true;
+    return T2C_OK;
+}
+
 int run_linear(QParams p, int64_t M, cudaStream_t stream) {
     bool used = false;
+    const int rc_gemm = try_gemm(p, M, stream, used);
+    if (used) return rc_gemm;
     const int rc_mma = try_mma(p, M, stream, used);
     if (used) return rc_mma;
     bool tma = true;

@@ -70,6 +70,9 @@ def linear_multi(x: torch.Tensor, weights: list[tuple[torch.Tensor, str | int]],
                  outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
     """One x, up to three weights (fused QKV / gate-up); optional fused RMSNorm prologue."""
     m = _check_x(x, k)
+    if norm_weight is not None and m > 4:
+        # the tensor-core GEMM for M > 4 reads x as it is: normalize first (torch-allocated temporary)
+        x, norm_weight = rms_norm(x, norm_weight, eps), None
     wtypes, wptrs, ns = [], [], []
     for w, kind in weights:
         wt = wtype_of(kind)
@@ -99,6 +102,8 @@ def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, kin
     m = _check_x(x, k)
     if out is None:
         out = torch.empty(*x.shape[:-1], n, dtype=torch.float16, device=x.device)
+    if norm_weight is not None and m > 4:
+        x, norm_weight = rms_norm(x, norm_weight, eps), None
     _lib.lib().call("t2c_linear_swiglu", wtype, _lib.ptr(x), _lib.ptr(w_gate), _lib.ptr(w_up), _lib.ptr(out),
                     _lib.ptr(norm_weight), float(eps), m, n, k, _lib.stream_ptr())
     return out
