@@ -221,6 +221,8 @@ def run_profile(args, local: int) -> None:
     """Workloads for ncu, bracketed by cudaProfilerStart/Stop (use --profile-from-start off).
 
     decode: the Qwen3-8B bs1 decode graph (Q4_K linears, Q6_K head), --steps replays.
+    decode32: the same at batch 32 on a synthetic 1024-position KV cache.
+    prefill: --steps prefills of the 1024-token prompt (batch 1).
     attn:   the fused decode attention of Qwen3-8B (32 Q / 8 KV heads, D 128) at position 1040 over
             48 layers' KV caches in turn (288 MB, larger than L2), --steps launches.
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
@@ -232,12 +234,28 @@ def run_profile(args, local: int) -> None:
     cfg = Qwen3Config.qwen3_8b()
     dev = torch.device("cuda", local)
     cudart = torch.cuda.cudart()
-    if args.profile == "decode":
+    if args.profile in ("decode", "decode32", "prefill"):
         weights = random_weights(cfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
-        runner = Qwen3Runner(cfg, weights, batch=1, max_seq=PROMPT + args.steps + args.warmup + 64,
+        batch = BATCH_LARGE if args.profile == "decode32" else 1
+        runner = Qwen3Runner(cfg, weights, batch=batch, max_seq=PROMPT + args.steps + args.warmup + 64,
                              max_new_tokens=args.steps + args.warmup + 8)
-        prompt = torch.randint(0, cfg.vocab, (1, PROMPT), generator=torch.Generator().manual_seed(0)).to(dev)
-        runner.prefill(prompt)
+        prompt = torch.randint(0, cfg.vocab, (batch, PROMPT), generator=torch.Generator().manual_seed(0)).to(dev)
+        if args.profile == "prefill":
+            runner.prefill(prompt)
+            torch.cuda.synchronize()
+            cudart.cudaProfilerStart()
+            for _ in range(args.steps):
+                runner.prefill(prompt)
+            torch.cuda.synchronize()
+            cudart.cudaProfilerStop()
+            return
+        if args.profile == "decode32":
+            for kc, vc in zip(runner.k_cache, runner.v_cache):
+                kc.normal_(0, 0.5)
+                vc.normal_(0, 0.5)
+            runner.positions.fill_(PROMPT)
+        else:
+            runner.prefill(prompt)
         runner.capture()
         for _ in range(args.warmup):
             runner.step()
@@ -307,7 +325,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "qmv", "attn"], default=None,
+    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn"], default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -16,6 +16,10 @@
 // Descriptors (PTX ISA "shared memory descriptor" / "instruction descriptor"):
 // K-major SWIZZLE_128B: start >> 4, LBO 1, SBO 1024 >> 4, version 1, layout 2;
 // a K step of 16 fp16 advances the start address by 32 bytes.
+// When (row tile, token tile) pairs are too few to fill the GPU (small M), a
+// cluster of up to 8 CTAs splits K; each parks its fp32 partials in its own
+// shared memory and the cluster leader sums them over distributed shared
+// memory (mapa / ld.shared::cluster) before the epilogue.
 // Every wait is bounded; on a timeout the kernel reports T2C_ETIMEOUT, stops
 // issuing, frees its TMEM and returns.
 #include <cuda.h>
@@ -42,6 +46,7 @@ struct GemmParams {
     const __half *res;
     int64_t N, M;
     int K, mt, swiglu, tmem_cols;
+    int ksplit;  // CTAs of a cluster splitting K (1: no split)
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -128,9 +133,12 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = p.mt;
     const bool swiglu = p.swiglu != 0;
-    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRowsT;
+    const int kpart = blockIdx.x % p.ksplit;  // rank in the cluster
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x / p.ksplit) * kRowsT;
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * mt;
-    const int nsb = p.K / 256, nch = p.K / kKC;
+    const int nsb = p.K / 256 / p.ksplit;     // super-blocks of this CTA's K range
+    const int sb0 = kpart * nsb;
+    const int nch = nsb * 4, kc0 = sb0 * 4;
     const int xbytes = mt * 128;
 
     uint8_t *ptr = smem;
@@ -162,8 +170,9 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
         for (int s = 0; s < 2 && s < nsb; ++s) {
             const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
             mbar_arrive_expect_tx(&raw_full[s], bytes);
-            tma_load_2d(raw_ptr + s * kRawBytes, &p.wmap, s * 36, static_cast<int>(n0), &raw_full[s]);
-            if (swiglu) tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, s * 36, static_cast<int>(n0), &raw_full[s]);
+            tma_load_2d(raw_ptr + s * kRawBytes, &p.wmap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
+            if (swiglu)
+                tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
         }
     }
     if (warp == 0) {
@@ -182,7 +191,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     if (tid == 0) {
         for (int c = 0; c < kNB - 1 && c < nch; ++c) {
             mbar_arrive_expect_tx(&x_full[c], static_cast<uint32_t>(xbytes));
-            tma_load_2d(smem + (x_base - a_base) + c * xbytes, &p.xmap, c * kKC, static_cast<int>(m0), &x_full[c]);
+            tma_load_2d(smem + (x_base - a_base) + c * xbytes, &p.xmap, (kc0 + c) * kKC, static_cast<int>(m0),
+                        &x_full[c]);
         }
     }
     const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(mt >> 3) << 17) | (static_cast<uint32_t>(kRowsT >> 4) << 24);
@@ -210,10 +220,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                 // every thread has read this raw stage: refill it with super-block sb + 2
                 const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
                 mbar_arrive_expect_tx(&raw_full[sb & 1], bytes);
-                tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb + 2) * 36, static_cast<int>(n0),
+                tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
                             &raw_full[sb & 1]);
                 if (swiglu)
-                    tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb + 2) * 36, static_cast<int>(n0),
+                    tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
                                 &raw_full[sb & 1]);
             }
             if (!mbar_wait(&x_full[b], static_cast<uint32_t>((kc / kNB) & 1))) {
@@ -241,8 +251,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                         failed = 1;
                     } else {
                         mbar_arrive_expect_tx(&x_full[bx], static_cast<uint32_t>(xbytes));
-                        tma_load_2d(smem + (x_base - a_base) + bx * xbytes, &p.xmap, nx * kKC, static_cast<int>(m0),
-                                    &x_full[bx]);
+                        tma_load_2d(smem + (x_base - a_base) + bx * xbytes, &p.xmap, (kc0 + nx) * kKC,
+                                    static_cast<int>(m0), &x_full[bx]);
                     }
                 }
             }
@@ -251,13 +261,75 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     __syncthreads();
     bool ok = !failed;
     if (ok) ok = mbar_wait(&mma_done[(nch - 1) % kNB], static_cast<uint32_t>(((nch - 1) / kNB) & 1));
-    if (!ok) {
-        if (tid == 0) report_device_error(T2C_ETIMEOUT);
-    } else {
+    if (!ok && tid == 0) report_device_error(T2C_ETIMEOUT);
+    const int64_t n = n0 + 32 * warp + lane;  // TMEM lane quadrant of warp w: weight rows 32w..32w+31
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    if (p.ksplit > 1) {
+        // cluster split-K: every CTA parks its fp32 partials column-major in its own
+        // shared memory (reusing the A buffers), the leader sums them over DSMEM
+        float *red = reinterpret_cast<float *>(smem);
+        const int ncols = (swiglu ? 2 : 1) * mt;
+        if (ok) {
+            tc_fence_after();
+            for (int c = 0; c < ncols; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(lane_addr + static_cast<uint32_t>(c), v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) red[(c + j) * kRowsT + tid] = __uint_as_float(v[j]);
+            }
+        } else {
+            for (int c = 0; c < ncols; ++c) red[c * kRowsT + tid] = 0.0f;
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        if (kpart == 0) {
+            uint32_t base[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                base[r] = 0;
+                if (r < p.ksplit)
+                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                                 : "=r"(base[r])
+                                 : "r"(smem_u32(red) + static_cast<uint32_t>(tid * 4)), "r"(r));
+            }
+            for (int c = 0; c < mt; ++c) {
+                float gv[8], uv[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    gv[r] = 0.0f;
+                    uv[r] = 0.0f;
+                    if (r < p.ksplit) {
+                        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                                     : "=f"(gv[r])
+                                     : "r"(base[r] + static_cast<uint32_t>(c * kRowsT * 4)));
+                        if (swiglu)
+                            asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                                         : "=f"(uv[r])
+                                         : "r"(base[r] + static_cast<uint32_t>((mt + c) * kRowsT * 4)));
+                    }
+                }
+                float g = 0.0f, u = 0.0f;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    g += gv[r];
+                    u += uv[r];
+                }
+                const int64_t m = m0 + c;
+                if (ok && m < p.M && n < p.N) {
+                    const int64_t o = m * p.N + n;
+                    float v = g;
+                    if (swiglu) {
+                        v = v / (1.0f + __expf(-v)) * u;
+                    } else if (p.res != nullptr) {
+                        v += __half2float(p.res[o]);
+                    }
+                    p.y[o] = __float2half_rn(v);
+                }
+            }
+        }
+        // partners keep their shared memory until the leader has read it
+        asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    } else if (ok) {
         tc_fence_after();
-        // epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane
-        const int64_t n = n0 + 32 * warp + lane;
-        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * warp) << 16);
         for (int c = 0; c < mt; c += 16) {
             uint32_t g[16], u[16];
             tmem_ld16(lane_addr + static_cast<uint32_t>(c), g);
@@ -338,6 +410,16 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     if (!encode_x(&p.xmap, a.x, a.M, a.K, p.mt)) return T2C_EUNSUPPORTED;
     p.y = a.y;
     p.res = a.res;
+    // split K over a cluster when there are too few (row tile, token tile) pairs to fill the GPU
+    const int64_t tiles = (a.N + kRowsT - 1) / kRowsT * ((a.M + p.mt - 1) / p.mt);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    p.ksplit = 1;
+    const int nsb_all = static_cast<int>(a.K / 256);
+    if (p.mt <= (p.swiglu ? 32 : 64)) {
+        while (p.ksplit < 8 && tiles * p.ksplit < sms && nsb_all % (p.ksplit * 2) == 0 && nsb_all / (p.ksplit * 2) >= 2)
+            p.ksplit *= 2;
+    }
     p.N = a.N;
     p.M = a.M;
     p.K = static_cast<int>(a.K);
@@ -360,15 +442,20 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
         configured[slot] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((a.N + kRowsT - 1) / kRowsT), static_cast<unsigned>((a.M + p.mt - 1) / p.mt));
+    cfg.gridDim = dim3(static_cast<unsigned>((a.N + kRowsT - 1) / kRowsT * p.ksplit),
+                       static_cast<unsigned>((a.M + p.mt - 1) / p.mt));
     cfg.blockDim = dim3(kThreadsG);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(p.ksplit);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t err = cudaLaunchKernelEx(&cfg, qgemm_q4k_kernel, p);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "qgemm launch: %s", cudaGetErrorString(err));
     return T2C_OK;
