@@ -124,7 +124,7 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
@@ -343,18 +343,38 @@ def main() -> None:
 
     cfg = Qwen3Config.qwen3_8b()
     dev = torch.device("cuda", local)
-    weights = random_weights(cfg, seed=rank, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
+    # N > 1: tensor parallelism over the N ranks (same seeded weights everywhere, each rank keeps its shard)
+    full_weights = random_weights(cfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
     torch.cuda.synchronize()
-    wb = weight_bytes(weights)
     steps, warm = args.steps, args.warmup
     stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        from torch2vk_b200.tp import local_config, make_tp_runner, shard_weights
+
+        warm_t = torch.ones(1, device=dev)
+        dist.all_reduce(warm_t)  # NCCL communicator up before any graph capture
+        kcfg = local_config(cfg, world)
+        weights = shard_weights(full_weights, cfg, rank, world)
+
+        def new_runner(batch: int):
+            return make_tp_runner(cfg, full_weights, rank=rank, tp=world, batch=batch,
+                                  max_seq=PROMPT + steps + warm + 64, max_new_tokens=steps + warm + 8)
+    else:
+        kcfg, weights = cfg, full_weights
+
+        def new_runner(batch: int):
+            return Qwen3Runner(cfg, weights, batch=batch, max_seq=PROMPT + steps + warm + 64,
+                               max_new_tokens=steps + warm + 8)
+    wb = weight_bytes(weights)
 
     # ---- prefill (1024-token prompt), timed with events
-    runner = Qwen3Runner(cfg, weights, batch=1, max_seq=PROMPT + steps + warm + 64, max_new_tokens=steps + warm + 8)
+    runner = new_runner(1)
     gen = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (1, PROMPT), generator=gen).to(dev)
     runner.prefill(prompt)  # warm-up of every prefill launch path
-    t_prefill = events_time(lambda: runner.prefill(prompt), 1, stream)
+    t_prefill = max_over_ranks(events_time(lambda: runner.prefill(prompt), 1, stream), world)
     runner.capture()
 
     # ---- bs1 decode: W warm-up replays, then K timed replays
@@ -389,12 +409,12 @@ def main() -> None:
     t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_reps, world)
 
     # ---- dominant kernel: gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096), all 36 layers' weights in turn
-    x = torch.randn(1, cfg.hidden, device=dev, dtype=torch.float16)
-    act = torch.empty(1, cfg.intermediate, device=dev, dtype=torch.float16)
+    x = torch.randn(1, kcfg.hidden, device=dev, dtype=torch.float16)
+    act = torch.empty(1, kcfg.intermediate, device=dev, dtype=torch.float16)
 
     def swiglu_all() -> None:
         for lw in weights.layers:
-            kernels.linear_swiglu(x, lw.gate.data, lw.up.data, "q4_k", cfg.hidden, norm_weight=lw.post_norm,
+            kernels.linear_swiglu(x, lw.gate.data, lw.up.data, "q4_k", kcfg.hidden, norm_weight=lw.post_norm,
                                   out=act)
 
     swiglu_all()
@@ -404,14 +424,14 @@ def main() -> None:
     for _ in range(3):
         g.replay()
     t_kernel = events_time(g.replay, 10, stream) / cfg.layers
-    kbytes = (weights.layers[0].gate.data.numel() * 4 * 2) + 2 * cfg.hidden + 2 * cfg.intermediate
+    kbytes = (weights.layers[0].gate.data.numel() * 4 * 2) + 2 * kcfg.hidden + 2 * kcfg.intermediate
     pk, pk_kind = peaks()
 
     # ---- bs32 decode on a synthetic 1024-position KV cache (same kernels, M = 32)
+    runner._graph = None
     del runner
     torch.cuda.empty_cache()
-    big = Qwen3Runner(cfg, weights, batch=BATCH_LARGE, max_seq=PROMPT + steps + warm + 64,
-                      max_new_tokens=steps + warm + 8)
+    big = new_runner(BATCH_LARGE)
     for kc, vc in zip(big.k_cache, big.v_cache):
         kc.normal_(0, 0.5)
         vc.normal_(0, 0.5)
@@ -427,21 +447,22 @@ def main() -> None:
     clk = clocks.summary()
     line = {
         "metric": "qwen3_8b_int4_decode_tok_s_bs1",
-        "value": world / t_step,
+        "value": 1.0 / t_step,
         "unit": "tok/s",
         "n_gpus": world,
         "steps": steps,
         "warmup": warm,
         "ms_per_step": t_step * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "int4 x int8 dp4a, f32 accumulate",
         "data": "synthetic (seeded random weights, random prompt ids)",
         "config": {"workload": "Qwen3-8B decode, batch 1, 1024-token prompt, Q4_K linears + Q6_K head",
-                   "model": "qwen3-8b-arch", "global_batch": world, "seq_len": PROMPT,
-                   "parallelism": f"{world} replica(s)", "l2": "weights (4.3 GB) larger than L2 every step"},
-        "e2e": {"value": world / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+                   "model": "qwen3-8b-arch", "global_batch": 1, "seq_len": PROMPT,
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "l2": "weights (4.3 GB / tp per GPU) larger than L2 every step"},
+        "e2e": {"value": 1.0 / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "gpu_launches": per_step_launches * steps,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
         "roofline": {
@@ -460,8 +481,8 @@ def main() -> None:
             "achieved_gbs": (wb["linears"] + wb["lm_head"]) / t_step / 1e9,
             "frac": (wb["linears"] + wb["lm_head"]) / t_step / 1e9 / pk["hbm_gbs"],
         },
-        "decode_bs32_tok_s": world * BATCH_LARGE / t_step32,
-        "prefill_tok_s": world * PROMPT / t_prefill,
+        "decode_bs32_tok_s": BATCH_LARGE / t_step32,
+        "prefill_tok_s": PROMPT / t_prefill,
         "device_status_bits": status,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -471,6 +492,10 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
 
+        big._graph = None  # graphs holding NCCL work go before the process group
+        del big
+        torch.cuda.synchronize()
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -142,7 +142,12 @@ class Qwen3Runner:
         self.stopped = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self.eos = torch.tensor(list(self.eos_ids) or [-1], dtype=torch.int64, device=dev)
         if self.decode_splits <= 0:
-            self.decode_splits = max(1, min(32 if self.fused_attention else 64, self.max_seq // (64 if self.fused_attention else 128)))
+            if self.fused_attention:
+                # about 4 CTAs per SM over (batch, KV head, split), at most one split per 64 cache rows
+                want = max(1, 592 // max(1, self.batch * cfg.kv_heads))
+                self.decode_splits = max(1, min(32, want, self.max_seq // 64))
+            else:
+                self.decode_splits = max(1, min(64, self.max_seq // 128))
         ws = kernels.attn_decode_workspace_floats(self.batch, cfg.heads, cfg.head_dim, self.decode_splits)
         self.attn_workspace = torch.empty(max(ws, 1), dtype=torch.float32, device=dev)
         self.fused_workspace = kernels.attn_decode_fused_workspace(self.batch, cfg.heads, cfg.kv_heads, cfg.head_dim,
@@ -174,29 +179,37 @@ class Qwen3Runner:
         h = b.h
         kernels.linear_multi(h, [(lw.q.data, lw.q.kind), (lw.k.data, lw.k.kind), (lw.v.data, lw.v.kind)], cfg.hidden,
                              norm_weight=lw.input_norm, eps=cfg.eps, outs=[b.q, b.k, b.v])
+        self._attention(i, b, tokens_per_seq, decode)
+        kernels.linear(b.attn, lw.o.data, lw.o.kind, cfg.heads * cfg.head_dim, residual=h, out=h)
+        kernels.linear_swiglu(h, lw.gate.data, lw.up.data, lw.gate.kind, cfg.hidden, norm_weight=lw.post_norm,
+                              eps=cfg.eps, out=b.act)
+        kernels.linear(b.act, lw.down.data, lw.down.kind, cfg.intermediate, residual=h, out=h)
+
+    def _attention(self, i: int, b: _Buffers, tokens_per_seq: int, decode: bool) -> None:
+        """q/k norm + RoPE, KV-cache write and attention of layer i: b.q/b.k/b.v -> b.attn."""
+        cfg, lw = self.cfg, self.weights.layers[i]
         if decode and self.fused_attention:
             kernels.attn_decode_fused(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.inv_freq, self.k_cache[i],
                                       self.v_cache[i], self.positions, batch=self.batch, n_heads=cfg.heads,
                                       n_kv=cfg.kv_heads, head_dim=cfg.head_dim, splits=self.decode_splits,
                                       workspace=self.fused_workspace, eps=cfg.eps, out=b.attn)
+            return
+        kernels.qk_norm_rope_cache(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.k_cache[i], self.v_cache[i],
+                                   self.positions, self.inv_freq, batch=self.batch, tokens=tokens_per_seq,
+                                   n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, eps=cfg.eps,
+                                   q_out=b.qr)
+        if decode:
+            kernels.attn_decode(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
+                                n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, max_len=self.max_seq,
+                                splits=self.decode_splits, workspace=self.attn_workspace, out=b.attn)
         else:
-            kernels.qk_norm_rope_cache(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.k_cache[i], self.v_cache[i],
-                                       self.positions, self.inv_freq, batch=self.batch, tokens=tokens_per_seq,
-                                       n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim, eps=cfg.eps,
-                                       q_out=b.qr)
-            if decode:
-                kernels.attn_decode(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
-                                    n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim,
-                                    max_len=self.max_seq, splits=self.decode_splits, workspace=self.attn_workspace,
-                                    out=b.attn)
-            else:
-                kernels.attn_prefill(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
-                                     tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=cfg.kv_heads,
-                                     head_dim=cfg.head_dim, out=b.attn)
-        kernels.linear(b.attn, lw.o.data, lw.o.kind, cfg.heads * cfg.head_dim, residual=h, out=h)
-        kernels.linear_swiglu(h, lw.gate.data, lw.up.data, lw.gate.kind, cfg.hidden, norm_weight=lw.post_norm,
-                              eps=cfg.eps, out=b.act)
-        kernels.linear(b.act, lw.down.data, lw.down.kind, cfg.intermediate, residual=h, out=h)
+            kernels.attn_prefill(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
+                                 tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim,
+                                 out=b.attn)
+
+    def _embed(self, ids: torch.Tensor, out: torch.Tensor) -> None:
+        cfg = self.cfg
+        kernels.embedding(self.weights.embed, self.weights.embed_kind, ids, cfg.hidden, cfg.vocab, out=out)
 
     def _head(self, x_last: torch.Tensor, b: _Buffers) -> None:
         cfg, w = self.cfg, self.weights
@@ -220,8 +233,7 @@ class Qwen3Runner:
         self.generated_length.zero_()
         self.stopped.zero_()
         b = self._alloc(self.batch * tokens)
-        kernels.embedding(self.weights.embed, self.weights.embed_kind, ids.reshape(-1).contiguous(), cfg.hidden,
-                          cfg.vocab, out=b.h)
+        self._embed(ids.reshape(-1).contiguous(), b.h)
         for i in range(cfg.layers):
             self._layer(i, b, tokens, decode=False)
             if layer_outputs is not None:
@@ -234,7 +246,7 @@ class Qwen3Runner:
     def decode_step(self, *, layer_outputs: list[torch.Tensor] | None = None) -> None:
         """One greedy token for every sequence: embeds next_token, appends the new one."""
         cfg, b = self.cfg, self.decode
-        kernels.embedding(self.weights.embed, self.weights.embed_kind, self.next_token, cfg.hidden, cfg.vocab, out=b.h)
+        self._embed(self.next_token, b.h)
         for i in range(cfg.layers):
             self._layer(i, b, 1, decode=True)
             if layer_outputs is not None:
