@@ -124,6 +124,7 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():

@@ -315,6 +315,25 @@ int t2c_quantize(int wtype, const float *x, void *out, int64_t R, int64_t K, voi
 /* packed blocks -> fp32 [R, K] (decoders of the same shader files). */
 int t2c_dequantize(int wtype, const void *w, float *out, int64_t R, int64_t K, void *stream);
 
+/* ------------------------------------------------------------------ tensor parallelism
+ * One-shot all-reduce of fp16 tensors over NVLink peer memory (the two
+ * per-layer reductions of the row-split o_proj / down_proj partial sums in the
+ * tensor-parallel decode step; replaces the NCCL all-reduce a Megatron split
+ * would use).  Every rank holds one buffer of t2c_allreduce_buffer_bytes(n_max)
+ * bytes (zeroed, 256-byte aligned) mapped into every peer with the IPC helpers;
+ * `bufs` lists the tp buffer addresses as seen by this rank (host array),
+ * `counter` is this rank's two zeroed device words.  n (a multiple of 8, <= n_max)
+ * halves of x are summed in place.  A peer that never arrives: after 1 s the
+ * kernel leaves x unreduced and sets T2C_ETIMEOUT in t2c_device_status.
+ * The reference runs single-GPU only; there is no counterpart there.
+ */
+int64_t t2c_allreduce_buffer_bytes(int64_t n_max);
+int t2c_ipc_get_handle(const void *ptr, void *handle64, int64_t *offset);
+int t2c_ipc_open_handle(const void *handle64, void **ptr);
+int t2c_ipc_close_handle(void *ptr);
+int t2c_allreduce_sum_f16(void *x, int64_t n, void *const *bufs, int rank, int tp, uint32_t *counter, int64_t n_max,
+                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

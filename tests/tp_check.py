@@ -28,7 +28,9 @@ def main() -> None:
     weights = random_weights(cfg, seed=3, device=f"cuda:{local}", lm_head_kind="q6_k", topology="q4_k", std=0.05)
     prompt = torch.randint(0, cfg.vocab, (1, 24), generator=torch.Generator().manual_seed(5)).cuda()
     steps = 16
-    tp_runner = make_tp_runner(cfg, weights, rank=rank, tp=world, batch=1, max_seq=128, max_new_tokens=steps + 2)
+    peer = os.environ.get("TP_PEER", "1") == "1"
+    tp_runner = make_tp_runner(cfg, weights, rank=rank, tp=world, batch=1, max_seq=128, max_new_tokens=steps + 2,
+                               peer_allreduce=peer)
     warm = torch.ones(1, device="cuda")
     dist.all_reduce(warm)  # communicator up before any graph capture
     got = tp_runner.generate(prompt, steps).clone()
@@ -41,10 +43,16 @@ def main() -> None:
         same_across = all(torch.equal(e, got) for e in everyone)
         agree = int((ref == got).sum())
         first = int((ref[0] != got[0]).nonzero()[0]) if agree < steps else steps
-        print(f"TP OK {agree}/{steps} first_diff={first} ranks_identical={same_across}", flush=True)
+        from torch2vk_b200 import kernels
+
+        status = kernels.device_status()
+        print(f"TP OK {agree}/{steps} first_diff={first} ranks_identical={same_across} status={status}", flush=True)
         if not same_across or first < 8:
             print("TP MISMATCH", ref.tolist(), got.tolist(), flush=True)
     dist.barrier()
+    if tp_runner._peer is not None:
+        tp_runner._graph = None
+        tp_runner._peer.close()
     del tp_runner
     dist.destroy_process_group()
 

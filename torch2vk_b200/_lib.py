@@ -54,6 +54,11 @@ _SIGNATURES: dict[str, list] = {
     "t2c_attn_decode_fused": [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _c.c_float, _vp, _vp, _i64, _i64,
                               _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp],
     "t2c_attn_decode_fused_workspace": [_i64, _i64, _i64, _i64, _i64],
+    "t2c_allreduce_buffer_bytes": [_i64],
+    "t2c_ipc_get_handle": [_vp, _vp, _vp],
+    "t2c_ipc_open_handle": [_vp, _vp],
+    "t2c_ipc_close_handle": [_vp],
+    "t2c_allreduce_sum_f16": [_vp, _i64, _vp, _c.c_int, _c.c_int, _vp, _i64, _vp],
     "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i64, _vp],
     "t2c_copy4d": [_i32, _vp, _vp, _vp, _vp, _vp, _vp],
@@ -69,7 +74,8 @@ _SIGNATURES: dict[str, list] = {
     "t2c_advance_positions": [_vp, _i64, _vp, _vp],
     "t2c_attn_decode_static": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
 }
-_RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64}
+_RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64,
+             "t2c_allreduce_buffer_bytes": _c.c_int64}
 
 
 class T2CError(RuntimeError):

@@ -14,8 +14,11 @@ survey for Qwen3-8B):
     identical everywhere;
   * embedding, norms: replicated.
 Two all-reduces per layer ([tokens, hidden] fp16) and one all-gather per step.
-Every collective is issued on the runner's stream, so a decode step with its
-collectives is captured in one CUDA graph.
+Decode-sized all-reduces run as one kernel over NVLink peer memory
+(torch2vk_b200.comm, CUDA IPC buffers, bounded flag waits); larger ones
+(prefill) and the all-gather use NCCL.  Every collective is issued on the
+runner's stream, so a decode step with its collectives is captured in one
+CUDA graph.
 """
 
 from __future__ import annotations
@@ -81,6 +84,7 @@ class TPQwen3Runner(Qwen3Runner):
     rank: int = 0
     tp: int = 1
     group: object | None = None
+    peer_allreduce: bool = True  # decode-sized reductions over NVLink peer memory instead of NCCL
 
     def __post_init__(self) -> None:
         super().__post_init__()
@@ -92,9 +96,17 @@ class TPQwen3Runner(Qwen3Runner):
         g = (self.cfg.vocab + 3) // 4
         self._gather_ps = torch.empty(self.tp, self.batch, g, dtype=torch.float32, device=self.device)
         self._gather_pt = torch.empty(self.tp, self.batch, g, dtype=torch.int32, device=self.device)
+        self._peer = None
+        if self.peer_allreduce and self.tp > 1:
+            from torch2vk_b200.comm import PeerAllReduce
+
+            self._peer = PeerAllReduce(self.group, max_elems=self.batch * self.full_cfg.hidden, device=self.device)
 
     def _all_reduce(self, t: torch.Tensor) -> None:
-        self._dist.all_reduce(t, group=self.group)
+        if self._peer is not None:
+            self._peer(t)  # NCCL for tensors beyond its buffer (prefill)
+        else:
+            self._dist.all_reduce(t, group=self.group)
 
     def _layer(self, i: int, b, tokens_per_seq: int, decode: bool) -> None:
         cfg, lw = self.cfg, self.weights.layers[i]
