@@ -457,7 +457,7 @@ def main() -> None:
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
-        "dtype": "int4 x int8 dp4a, f32 accumulate",
+        "dtype": "q4_k weights x int8 activation planes (tensor-core mma), int32 / f32 accumulate",
         "data": "synthetic (seeded random weights, random prompt ids)",
         "config": {"workload": "Qwen3-8B decode, batch 1, 1024-token prompt, Q4_K linears + Q6_K head",
                    "model": "qwen3-8b-arch", "global_batch": 1, "seq_len": PROMPT,
@@ -468,7 +468,7 @@ def main() -> None:
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
         "roofline": {
             "bound": "hbm",
-            "kernel": "qmv_tma_kernel (gate/up + SwiGLU, Q4_K 2x12288x4096)",
+            "kernel": "qmv_m1_kernel (gate/up + SwiGLU, Q4_K 2 x 12288 x 4096 per GPU / tp)",
             "achieved": kbytes / t_kernel / 1e9,
             "peak": pk["hbm_gbs"],
             "unit": "GB/s",
