@@ -1180,35 +1180,6 @@ __device__ __forceinline__ void mma_q4k_block(uint32_t rowg, uint32_t row_stride
     }
 }
 
-// M = 1 variant: the 8 columns are 4 sub-blocks x 2 x planes.  A group of 4
-// sub-blocks (quarters 2G, 2G+1 of the block: low nibbles -> sub-blocks 4G,
-// 4G+2, high nibbles -> 4G+1, 4G+3) takes 4 accumulating mma: in mma i, lane
-// (g, t) feeds k-slots 4t..4t+3 from sub-block 4G + t/2 and k-slots 16+4t..
-// from sub-block 4G + 2 + t/2, values 16*(t%2) + 4i .. +3 of the sub-block, so a
-// lane's four A words of one (row, quarter) are one 16-byte load.  High
-// nibbles enter unshifted (16 q, unsigned A operand); 1/16 is folded into the
-// scale of the odd (high-nibble) sub-blocks.  B column s*2 + plane carries x
-// of sub-block 4G + s only (zero rows elsewhere), so D column pair t of lane
-// (g, t) is sub-block 4G + t, and each lane applies the scales of its own two
-// sub-blocks (t and 4 + t); the four lanes of a quad are summed per row block.
-__device__ __forceinline__ void mma_u8s8_16832_acc(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Scales of sub-blocks t and t + 4 of one Q4_K header: d*sc, dmin*m.
-__device__ __forceinline__ void q4k_lane_scales(const uint4 h, int t, float ds[2], float dm[2]) {
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t y = (h.y >> (8 * t)) & 0xffu, z = (h.z >> (8 * t)) & 0xffu, w = (h.w >> (8 * t)) & 0xffu;
-    ds[0] = d * small_u2f(y & 63u);
-    dm[0] = dmin * small_u2f(z & 63u);
-    ds[1] = d * small_u2f((w & 15u) | ((y >> 6) << 4));
-    dm[1] = dmin * small_u2f((w >> 4) | ((z >> 6) << 4));
-}
-
 // Item cursor of one warp: CTA iteration `it`, j-th item of the warp in that
 // iteration.  Items of a row block are its segments seg0, seg0 + wpb, ...;
 // with SwiGLU every segment is two items (gate rows, then up rows).
@@ -1461,8 +1432,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
 // the x values of its own K-segments (after, when there is a fused RMSNorm,
 // a warp-local sum of squares over the whole row), so the prologue has no
 // CTA barrier and x costs ~1.2 KB of shared memory per segment: two CTAs fit
-// on an SM.  Per segment: xh[512], 32-byte gap, xl[512], then (sx, xs) per
-// 32-value sub-block.
+// on an SM.  Per segment: xh[512], 32-byte gap, xl[512], then (sx', xs) per
+// 32-value sub-block, where sx' = sx / 16 for the odd (high-nibble) sub-blocks.
 constexpr int kM1SegX = 512 + 32 + 512 + 32;      // plane bytes (+ gaps)
 constexpr int kM1SegBytes = kM1SegX + 16 * 8;    // + meta
 constexpr int kM1MaxSegs = 16;                   // per warp (K <= 65536)
@@ -1504,48 +1475,105 @@ __device__ __forceinline__ void m1_prepare_segment(const QParams &p, int k0, flo
     *reinterpret_cast<uint4 *>(area + 512 + 32 + 16 * lane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     if ((lane & 1) == 0) {
         const float sx = amax / 16383.0f;
-        *reinterpret_cast<float2 *>(area + kM1SegX + 8 * (lane >> 1)) = make_float2(sx, sx * static_cast<float>(sum));
+        // sub-block lane / 2: the odd ones are high nibbles, which enter the mma as 16 q
+        const float f_sx = (lane & 2) ? sx * 0.0625f : sx;
+        *reinterpret_cast<float2 *>(area + kM1SegX + 8 * (lane >> 1)) = make_float2(f_sx, sx * static_cast<float>(sum));
     }
 }
 
-// One 144-byte block (values voff .. voff+255 of the segment) of a 16-row group.
-__device__ __forceinline__ void m1_block(uint32_t rowg, uint32_t row_stride, uint32_t seg_area, int voff, int lane,
+// Fragment mapping of the M = 1 kernel (m16n8k32, A = 16 weight rows, B = x).
+// In a group G of two quarters (sub-blocks 4G .. 4G+3), lane (g, t) loads 16
+// bytes of rows g and g+8: quarter 2G + (t & 1), bytes 16 (t >> 1) .. +15.
+// mma i takes word i of each: its low nibbles fill k-slots 4t .. 4t+3 and its
+// high nibbles (unshifted, i.e. 16 q) k-slots 16+4t .. 16+4t+3.  So k-slots
+// {0-3, 8-11} hold the low-nibble sub-block of quarter 2G (sub-block 4G),
+// {4-7, 12-15} that of quarter 2G+1 (4G+2), {16-19, 24-27} sub-block 4G+1 and
+// {20-23, 28-31} sub-block 4G+3.  B column pair c carries the two x planes of
+// one of them (c = 0: 4G, 1: 4G+2, 2: 4G+1, 3: 4G+3), zero in the other
+// k-slots, so D columns 2t, 2t+1 of lane (g, t) are sub-block 4G + cc(t),
+// cc = {0, 2, 1, 3}[t]: every lane applies the scales of one sub-block per
+// group, and the four lanes of a quad are summed per row block at the end.
+struct M1Lane {
+    uint32_t aoff;   // A words in a 144-byte block
+    uint32_t xoff;   // x plane words of G = 0 in a segment area
+    uint32_t moff;   // (sx', xs) of sub-block cc of G = 0 in a segment area
+    uint32_t m0, m1; // B masks: k-slots < 16 / >= 16 carry this lane's x column
+    uint32_t sel;    // byte_perm selector of header byte cc
+};
+
+__device__ __forceinline__ M1Lane m1_lane(int lane) {
+    const int g = lane >> 2, t = lane & 3, c = g >> 1, plane = g & 1;
+    const int cc = ((t & 1) << 1) | (t >> 1);
+    const bool mine = (c & 1) == (t & 1);
+    M1Lane L;
+    L.aoff = static_cast<uint32_t>(16 + 32 * (t & 1) + 16 * (t >> 1));
+    L.xoff = static_cast<uint32_t>((plane ? 512 + 32 : 0) + 32 * (2 * (t & 1) + (c >> 1)) + 16 * (t >> 1));
+    L.moff = static_cast<uint32_t>(kM1SegX + 8 * cc);
+    L.m0 = (mine && c < 2) ? 0xffffffffu : 0u;
+    L.m1 = (mine && c >= 2) ? 0xffffffffu : 0u;
+    L.sel = 0x4440u + static_cast<uint32_t>(cc);
+    return L;
+}
+
+__device__ __forceinline__ void mma_u8s8_16832(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d * sc and dmin * m of sub-blocks cc and cc + 4 of one Q4_K header.
+__device__ __forceinline__ void q4k_scales_sel(const uint4 h, uint32_t sel, float ds[2], float dm[2]) {
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const uint32_t y = __byte_perm(h.y, 0u, sel), z = __byte_perm(h.z, 0u, sel), w = __byte_perm(h.w, 0u, sel);
+    ds[0] = d * small_u2f(y & 63u);
+    dm[0] = dmin * small_u2f(z & 63u);
+    ds[1] = d * small_u2f((w & 15u) | ((y >> 6) << 4));
+    dm[1] = dmin * small_u2f((w >> 4) | ((z >> 6) << 4));
+}
+
+// One 144-byte block (values voff .. voff+255 of the segment) of a 16-row
+// group whose rows are kMmaSegBytes apart; acc = rows g, g + 8.
+__device__ __forceinline__ void m1_block(const uint8_t *rowg, const uint8_t *xseg, int voff, const M1Lane &L,
                                          float acc[2]) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t rowg8 = rowg + 8u * row_stride;
-    const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
+    const uint8_t *rowg8 = rowg + 8 * kMmaSegBytes;
+    const uint4 hg = *reinterpret_cast<const uint4 *>(rowg), hg8 = *reinterpret_cast<const uint4 *>(rowg8);
     float dsg[2], dmg[2], dsh[2], dmh[2];
-    q4k_lane_scales(hg, t, dsg, dmg);
-    q4k_lane_scales(hg8, t, dsh, dmh);
-    const uint32_t nib = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-    const float hi_scale = (t & 1) ? 0.0625f : 1.0f;
-    // B fragments: column s*2 + plane carries plane (g & 1) of sub-block 4G + s, values
-    // 16 (t & 1) .. +15, in the lanes whose k-slots belong to that sub-block (else zero)
-    const int s = g >> 1;
-    const bool active = (t >> 1) == (s & 1);
-    const uint32_t m0 = (active && s < 2) ? 0xffffffffu : 0u, m1 = (active && s >= 2) ? 0xffffffffu : 0u;
-    const uint32_t plane = seg_area + ((g & 1) ? 512u + 32u : 0u) + static_cast<uint32_t>(voff + 16 * (t & 1));
-    const uint32_t meta = seg_area + kM1SegX + 8u * static_cast<uint32_t>((voff >> 5) + t);
-    const uint32_t off = 16u + 16u * static_cast<uint32_t>(t & 1);
+    q4k_scales_sel(hg, L.sel, dsg, dmg);
+    q4k_scales_sel(hg8, L.sel, dsh, dmh);
 #pragma unroll
     for (int G = 0; G < 2; ++G) {
-        const uint4 X = active ? lds128(plane + 32u * static_cast<uint32_t>(4 * G + s)) : make_uint4(0u, 0u, 0u, 0u);
-        const uint2 mt = lds64(meta + 32u * G);  // (sx, xs) of sub-block 4G + t
-        const uint4 qa = lds128(rowg + off + 64 * G), qb = lds128(rowg + off + 64 * G + 32);
-        const uint4 ra = lds128(rowg8 + off + 64 * G), rb = lds128(rowg8 + off + 64 * G + 32);
-        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wb[4] = {qb.x, qb.y, qb.z, qb.w};
-        const uint32_t va[4] = {ra.x, ra.y, ra.z, ra.w}, vb[4] = {rb.x, rb.y, rb.z, rb.w};
+        const uint4 X = *reinterpret_cast<const uint4 *>(xseg + L.xoff + voff + 128 * G);
+        const float2 mt = *reinterpret_cast<const float2 *>(xseg + L.moff + (voff >> 2) + 32 * G);
+        const uint4 qa = *reinterpret_cast<const uint4 *>(rowg + L.aoff + 64 * G);
+        const uint4 ra = *reinterpret_cast<const uint4 *>(rowg8 + L.aoff + 64 * G);
+        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, va[4] = {ra.x, ra.y, ra.z, ra.w};
         const uint32_t xw[4] = {X.x, X.y, X.z, X.w};
         int d[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t a[4] = {wa[i] & nib, va[i] & nib, wb[i] & nib, vb[i] & nib};
-            mma_u8s8_16832_acc(d, a, xw[i] & m0, xw[i] & m1);
+            const uint32_t a[4] = {wa[i] & 0x0F0F0F0Fu, va[i] & 0x0F0F0F0Fu, wa[i] & 0xF0F0F0F0u, va[i] & 0xF0F0F0F0u};
+            mma_u8s8_16832(d, a, xw[i] & L.m0, xw[i] & L.m1);
         }
-        const float f = __uint_as_float(mt.x) * hi_scale, xs = __uint_as_float(mt.y);
-        acc[0] = fmaf(dsg[G] * f, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], xs, acc[0]));
-        acc[1] = fmaf(dsh[G] * f, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], xs, acc[1]));
+        acc[0] = fmaf(dsg[G] * mt.x, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], mt.y, acc[0]));
+        acc[1] = fmaf(dsh[G] * mt.x, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], mt.y, acc[1]));
     }
+}
+
+// Item j of row block `blk` (segment seg0 + j * wpb; SwiGLU: gate / up
+// alternate) as one 16-row x 288-byte TMA box.
+__device__ __forceinline__ void m1_issue(const QParams &p, int blk, int j, int seg0, uint8_t *stage, uint64_t *bar) {
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    int si = 0, jj = j;
+    if (swiglu) {
+        si = j & 1;
+        jj = j >> 1;
+    } else if (p.nstreams > 1) {
+        si = stream_of(p, blk);
+    }
+    const int row0 = (blk - static_cast<int>(p.s[swiglu ? 0 : si].rs_begin)) * kMmaRows;
+    // rows past N are zero-filled by the TMA unit and still count toward the transaction bytes
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kMmaRows * kMmaSegBytes));
+    tma_load_2d(stage, &p.tmap[si], (seg0 + jj * p.wpb) * (kMmaSegBytes / 4), row0, bar);
 }
 
 __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_constant__ QParams p) {
@@ -1553,30 +1581,36 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.stages;
     const bool swiglu = p.mode == MODE_SWIGLU;
-    const int nsegw = (p.nseg - warp % p.wpb + p.wpb - 1) / p.wpb;
+    // per-warp constants: row-block group, first segment, items per row block
+    const int group = warp / p.wpb, seg0 = warp % p.wpb;
+    const int nsegw = (p.nseg - seg0 + p.wpb - 1) / p.wpb;
+    const int items = swiglu ? 2 * nsegw : nsegw;
+    const int total = static_cast<int>(p.total_rowsets);
+    const int step = static_cast<int>(gridDim.x) * p.bpc;
+    const int first = static_cast<int>(blockIdx.x) * p.bpc + group;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
     uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
     uint8_t *xarea = smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
                      static_cast<size_t>(warp) * p.xseg_per_warp * kM1SegBytes;
     MmaSlot *slots = reinterpret_cast<MmaSlot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
                                                  static_cast<size_t>(kMmaWarps) * p.xseg_per_warp * kM1SegBytes);
-    const int64_t iters = (p.total_rowsets + static_cast<int64_t>(gridDim.x) * p.bpc - 1) /
-                          (static_cast<int64_t>(gridDim.x) * p.bpc);
-    const int group = warp / p.wpb;
 
-    MmaCursor ahead{0, 0};
+    // producer cursor (warp-uniform; lane 0 issues)
+    int pblk = first, pj = 0;
     if (lane == 0) {
         for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
         fence_mbar_init();
-        for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) {
-            mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j, stages + static_cast<size_t>(i) * p.stage_bytes,
-                      &full[i]);
-            mma_advance(p, ahead, warp);
+    }
+    for (int i = 0; i < S && pblk < total; ++i) {
+        if (lane == 0) m1_issue(p, pblk, pj, seg0, stages + static_cast<size_t>(i) * p.stage_bytes, &full[i]);
+        if (++pj == items) {
+            pj = 0;
+            pblk += step;
         }
     }
     for (int i = threadIdx.x; i < kMmaSlots * p.bpc * static_cast<int>(sizeof(MmaSlot) / 4); i += kMmaThreads)
         reinterpret_cast<int *>(slots)[i] = 0;
-    __syncthreads();  // mbarrier init and slot zeroing visible to every warp
+    __syncthreads();  // slot zeroing visible to every warp
     pdl_wait();
     pdl_trigger();
     // this warp's x segments; with a fused RMSNorm the wpb warps of a group
@@ -1586,7 +1620,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     if (p.norm_w != nullptr) {
         float ss = 0.0f;
         for (int j = 0; j < nsegw; ++j) {
-            const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + (warp % p.wpb + j * p.wpb) * (kMmaSegBlocks * 256));
+            const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + (seg0 + j * p.wpb) * (kMmaSegBlocks * 256));
             float f[16];
             unpack8(xv[2 * lane], f);
             unpack8(xv[2 * lane + 1], f + 8);
@@ -1602,21 +1636,15 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
         inv_rms = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
     }
     for (int j = 0; j < nsegw; ++j)
-        m1_prepare_segment(p, (warp % p.wpb + j * p.wpb) * (kMmaSegBlocks * 256), inv_rms, xarea + j * kM1SegBytes,
-                           lane);
+        m1_prepare_segment(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), inv_rms, xarea + j * kM1SegBytes, lane);
     __syncwarp();
-    ahead = MmaCursor{0, 0};
-    for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) mma_advance(p, ahead, warp);
 
-    const uint32_t stages_addr = smem_u32(stages), x_addr = smem_u32(xarea);
-    const int items = mma_items(p, warp);
+    const M1Lane L = m1_lane(lane);
     const int g = lane >> 2, t = lane & 3;
-    int s = 0;
+    int s = 0, it = 0;
     uint32_t phase = 0;
     bool failed = false;
-    for (int64_t it = 0; it < iters; ++it) {
-        const int64_t block = mma_block(p, it, warp);
-        if (block >= p.total_rowsets) break;  // later iterations have no block either
+    for (int blk = first; blk < total; blk += step, ++it) {
         float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         for (int j = 0; j < items; ++j) {
             if (!failed && !mbar_wait(&full[s], phase)) {
@@ -1624,25 +1652,29 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 failed = true;
             }
             if (!failed) {
-                const uint32_t stage = stages_addr + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_bytes);
-                const bool up = swiglu && (j & 1);
-                const int jl = swiglu ? (j >> 1) : j;
+                const uint8_t *stage = stages + static_cast<size_t>(s) * p.stage_bytes + g * kMmaSegBytes;
+                const uint8_t *xseg = xarea + (swiglu ? (j >> 1) : j) * kM1SegBytes;
                 float part[2] = {0.0f, 0.0f};
 #pragma unroll
-                for (int sb = 0; sb < kMmaSegBlocks; ++sb)
-                    m1_block(stage + static_cast<uint32_t>(g * kMmaSegBytes + sb * 144), kMmaSegBytes,
-                             x_addr + static_cast<uint32_t>(jl * kM1SegBytes), sb * 256, lane, part);
-                acc[0][0] += up ? 0.0f : part[0];
-                acc[0][1] += up ? 0.0f : part[1];
-                acc[1][0] += up ? part[0] : 0.0f;
-                acc[1][1] += up ? part[1] : 0.0f;
-                __syncwarp();
-                if (lane == 0 && mma_valid(p, ahead, warp, iters)) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mma_issue(p, warp, mma_block(p, ahead.it, warp), ahead.j,
-                              stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
+                for (int sb = 0; sb < kMmaSegBlocks; ++sb) m1_block(stage + sb * 144, xseg, sb * 256, L, part);
+                if (swiglu && (j & 1)) {
+                    acc[1][0] += part[0];
+                    acc[1][1] += part[1];
+                } else {
+                    acc[0][0] += part[0];
+                    acc[0][1] += part[1];
                 }
-                if (mma_valid(p, ahead, warp, iters)) mma_advance(p, ahead, warp);
+                __syncwarp();
+                if (pblk < total) {
+                    if (lane == 0) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        m1_issue(p, pblk, pj, seg0, stages + static_cast<size_t>(s) * p.stage_bytes, &full[s]);
+                    }
+                    if (++pj == items) {
+                        pj = 0;
+                        pblk += step;
+                    }
+                }
             }
             if (++s == S) {
                 s = 0;
@@ -1657,11 +1689,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
             }
         if (p.wpb == 1) {
-            mma_finish_block<1>(p, block, acc, lane);
+            mma_finish_block<1>(p, blk, acc, lane);
             continue;
         }
         MmaSlot *slot = slots + (it % kMmaSlots) * p.bpc + group;
-        if (!slot_wait_gen(&slot->gen, static_cast<int>(it / kMmaSlots))) {
+        if (!slot_wait_gen(&slot->gen, it / kMmaSlots)) {
             report_device_error(T2C_ETIMEOUT);
             failed = true;
             continue;
@@ -1688,7 +1720,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
             v[r][0] = *reinterpret_cast<volatile float *>(&slot->v[r][g][0]);
             v[r][1] = *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][0]);
         }
-        mma_finish_block<1>(p, block, v, lane);
+        mma_finish_block<1>(p, blk, v, lane);
         __syncwarp();
         if (t == 0) {
 #pragma unroll
