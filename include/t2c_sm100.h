@@ -184,9 +184,14 @@ int t2c_attn_decode(const void *q, const void *k_cache, const void *v_cache, voi
  * batch strides q_sb / k_sb / v_sb (elements); out [B, NH*D] with o_sb.  D = 128.
  * max_len: cache rows per sequence; a position outside [0, max_len) makes the
  * kernel touch nothing and set T2C_EINVAL in t2c_device_status.
- * splits > 1 needs t2c_attn_decode_fused_workspace(...) words of workspace whose
+ * splits <= 8: the splits CTAs of one (b, kv head) form a thread-block
+ * cluster and combine through distributed shared memory (no workspace).
+ * splits > 8 needs t2c_attn_decode_fused_workspace(...) words of workspace whose
  * last B*NH words (arrival counters) are zero before the first call; every
- * call leaves them zero.
+ * call leaves them zero.  positions, q_w, k_w, inv_freq and the cache rows of
+ * earlier positions are read before the wait on the preceding kernel of the
+ * stream, so they must not be written by that kernel (positions advanced one
+ * launch earlier or by a copy are fine).
  */
 int t2c_attn_decode_fused(const void *q_in, const void *k_in, const void *v_in, int64_t q_sb, int64_t k_sb,
                           int64_t v_sb, const float *q_w, const float *k_w, const float *inv_freq, float eps,

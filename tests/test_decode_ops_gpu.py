@@ -220,9 +220,13 @@ def test_elementwise_add_swiglu():
 
 
 @pytest.mark.parametrize("layout", ["token_major", "head_major"])
-@pytest.mark.parametrize("NH,NK,splits", [(32, 8, 1), (32, 8, 5), (32, 8, 23), (16, 8, 7), (8, 8, 3), (64, 8, 9)])
+@pytest.mark.parametrize("NH,NK,splits", [(32, 8, 1), (32, 8, 5), (32, 8, 8), (32, 8, 23), (16, 8, 7), (8, 8, 3),
+                                          (64, 8, 8), (64, 8, 9)])
 def test_attn_decode_fused_matches_unfused_chain(NH, NK, splits, layout):
-    """One-launch decode attention == qk_norm_rope_cache + attn_decode (same caches after, outputs close)."""
+    """One-launch decode attention == qk_norm_rope_cache + attn_decode (same caches after, outputs close).
+
+    splits <= 8: one thread-block cluster per (sequence, KV head), combined through distributed shared
+    memory; more splits: partials in a global workspace, combined by the last arriving warp."""
     from torch2vk_b200 import kernels
     from torch2vk_b200.qwen3 import Qwen3Config, inv_freq
 
@@ -268,7 +272,7 @@ def test_attn_decode_fused_rejects_bad_arguments():
     pos = torch.zeros(B, device="cuda", dtype=torch.int32)
     with pytest.raises(T2CError, match="workspace"):
         kernels.attn_decode_fused(t, kv, kv, w, w, w[:64], c, c, pos, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
-                                  splits=4, workspace=None)
+                                  splits=12, workspace=None)
     with pytest.raises(T2CError, match="D=64"):
         kernels.attn_decode_fused(t, kv, kv, w, w, w[:64], c, c, pos, batch=B, n_heads=NH * 2, n_kv=NK * 2,
                                   head_dim=64, splits=1, workspace=None)

@@ -542,6 +542,251 @@ __global__ void __launch_bounds__(G * 32) attn_decode_fused_kernel(
     if (lane == 0) counters[b * NH + h] = 0;
 }
 
+// ------------------------------------------ cluster decode attention (T = 1)
+// The same work as attn_decode_fused_kernel for splits <= 8: the `splits`
+// CTAs of one (batch b, kv head kh) form a thread-block cluster.  Each CTA
+// streams its cache positions through a ring of shared-memory tiles
+// (cp.async; tiles of earlier positions, the RoPE angles and the norm weights
+// are requested before griddepcontrol.wait), patches the new position's k / v
+// into its tile, and leaves per-head partials (max, sum, acc) in its own
+// shared memory.  After a cluster barrier, CTA r combines heads r, r + splits,
+// ... by reading every CTA's partials through distributed shared memory; a
+// second cluster barrier keeps the partials alive until those reads are done.
+// No workspace, no atomics, no global round trip for the combine.
+constexpr int kCaTile = 32;
+constexpr int kCaStages = 4;
+constexpr int kCaMaxSplits = 8;
+constexpr int kCaKStride = 136;  // halves per K row in shared memory: 272-byte rows, conflict-free 16-byte reads
+constexpr int kCaStageBytes = kCaTile * kCaKStride * 2 + kCaTile * 128 * 2;
+constexpr int kCaSmem = kCaStages * kCaStageBytes;
+
+__device__ __forceinline__ void ca_cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void ca_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void ca_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ca_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t ca_cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float ca_ld_remote(const void *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// RMSNorm (weights w) + RoPE (cos / sin of this lane's 4 dims) of one 128-value head row.
+__device__ __forceinline__ void norm_rope_pre(const uint2 raw, const float w[4], const float c[4], const float sn[4],
+                                              float eps, int lane, float r[4]) {
+    const float4 f = h4_to_f4(raw);
+    float v[4] = {f.x, f.y, f.z, f.w};
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float inv = rsqrtf(ss / 128.0f + eps);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = v[e] * inv * w[e];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        r[e] = lane < 16 ? v[e] * c[e] - partner * sn[e] : v[e] * c[e] + partner * sn[e];
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(G * 32) attn_decode_cluster_kernel(
+    const __half *__restrict__ q_in, const __half *__restrict__ k_in, const __half *__restrict__ v_in, int64_t q_sb,
+    int64_t k_sb, int64_t v_sb, const float *__restrict__ q_w, const float *__restrict__ k_w,
+    const float *__restrict__ inv_freq, float eps, __half *kc, __half *vc, int64_t cb, int64_t cs, int64_t ch,
+    __half *__restrict__ out, int64_t o_sb, const int32_t *__restrict__ positions, int NK, int max_len, int splits,
+    float qscale) {
+    constexpr int D = 128, E = 4, NT = G * 32;
+    extern __shared__ __align__(128) uint8_t ca_smem[];
+    __shared__ __align__(16) float qs[G][D];
+    __shared__ __align__(16) float ps[G][kCaTile];
+    __shared__ __align__(16) float part_acc[G][D];
+    __shared__ float part_ml[G][2];
+    const int sp = static_cast<int>(ca_cluster_rank());
+    const int kh = (blockIdx.x / splits) % NK;
+    const int b = blockIdx.x / (splits * NK);
+    const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = kh * G + g;
+    const int pos = positions[b];
+    if (pos < 0 || pos >= max_len) {  // no cache row to write: report, touch nothing (uniform over the cluster)
+        pdl_wait();
+        pdl_trigger();
+        if (threadIdx.x == 0) report_device_error(T2C_EINVAL);
+        return;
+    }
+    const int len = pos + 1;
+    const int chunk = (len + splits - 1) / splits;
+    const int p0 = min(len, sp * chunk), p1 = min(len, p0 + chunk);
+    const int ntiles = (p1 - p0 + kCaTile - 1) / kCaTile;
+    const bool owner = p0 <= pos && pos < p1;
+    const __half *kbase = kc + b * cb + kh * ch;
+    const __half *vbase = vc + b * cb + kh * ch;
+    // tile `tile` of this CTA's range into ring stage tile % kCaStages: one commit group per call
+    auto issue = [&](int tile) {
+        if (tile < ntiles) {
+            uint8_t *st = ca_smem + (tile % kCaStages) * kCaStageBytes;
+            __half *ks = reinterpret_cast<__half *>(st);
+            __half *vs = reinterpret_cast<__half *>(st + kCaTile * kCaKStride * 2);
+            const int t0 = p0 + tile * kCaTile;
+            const int rows = min(kCaTile, p1 - t0);
+            for (int i = threadIdx.x; i < rows * 16; i += NT) {
+                const int r = i >> 4, c = i & 15;
+                const int64_t src = static_cast<int64_t>(t0 + r) * cs + c * 8;
+                ca_cp16(ks + r * kCaKStride + c * 8, kbase + src);
+                ca_cp16(vs + r * D + c * 8, vbase + src);
+            }
+        }
+        ca_commit();
+    };
+#pragma unroll
+    for (int i = 0; i < kCaStages; ++i) issue(i);
+    float cw[E], sw[E], qw[E], kw[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        sincosf(static_cast<float>(pos) * inv_freq[(lane * E + e) & (D / 2 - 1)], &sw[e], &cw[e]);
+        qw[e] = q_w[lane * E + e];
+        kw[e] = k_w[lane * E + e];
+    }
+
+    pdl_wait();
+    pdl_trigger();
+    {
+        float r[4];
+        norm_rope_pre(*reinterpret_cast<const uint2 *>(q_in + b * q_sb + static_cast<int64_t>(h) * D + lane * E), qw, cw,
+                      sw, eps, lane, r);
+#pragma unroll
+        for (int e = 0; e < E; ++e) qs[g][lane * E + e] = __half2float(__float2half_rn(r[e])) * qscale;
+    }
+    uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
+    if (owner) {
+        float r[4];
+        norm_rope_pre(*reinterpret_cast<const uint2 *>(k_in + b * k_sb + static_cast<int64_t>(kh) * D + lane * E), kw, cw,
+                      sw, eps, lane, r);
+        knew = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
+        vnew = *reinterpret_cast<const uint2 *>(v_in + b * v_sb + static_cast<int64_t>(kh) * D + lane * E);
+        if (g == 0) {
+            *reinterpret_cast<uint2 *>(kc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = knew;
+            *reinterpret_cast<uint2 *>(vc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = vnew;
+        }
+    }
+    __syncwarp();
+
+    float m_run = -FLT_MAX, l_run = 0.0f;
+    float acc[E] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int tile = 0; tile < ntiles; ++tile) {
+        ca_wait<kCaStages - 1>();
+        __syncthreads();  // every thread's copies of this tile have landed
+        uint8_t *st = ca_smem + (tile % kCaStages) * kCaStageBytes;
+        __half *ks = reinterpret_cast<__half *>(st);
+        __half *vs = reinterpret_cast<__half *>(st + kCaTile * kCaKStride * 2);
+        const int t0 = p0 + tile * kCaTile;
+        const int n_valid = min(kCaTile, p1 - t0);
+        if (owner && pos >= t0 && pos < t0 + n_valid) {
+            // the tile holds the new position: its rows were read before this kernel wrote them
+            if (g == 0) {
+                *reinterpret_cast<uint2 *>(ks + (pos - t0) * kCaKStride + lane * E) = knew;
+                *reinterpret_cast<uint2 *>(vs + (pos - t0) * D + lane * E) = vnew;
+            }
+            __syncthreads();
+        }
+        const bool valid = lane < n_valid;
+        float s0 = 0.0f, s1 = 0.0f;
+        if (valid) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(ks + lane * kCaKStride);
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) {
+                const uint4 k8 = kr[c];
+                const float4 lo = h4_to_f4(make_uint2(k8.x, k8.y));
+                const float4 hi = h4_to_f4(make_uint2(k8.z, k8.w));
+                const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][c * 8]);
+                const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][c * 8 + 4]);
+                s0 = fmaf(lo.x, qa.x, s0);
+                s1 = fmaf(lo.y, qa.y, s1);
+                s0 = fmaf(lo.z, qa.z, s0);
+                s1 = fmaf(lo.w, qa.w, s1);
+                s0 = fmaf(hi.x, qb.x, s0);
+                s1 = fmaf(hi.y, qb.y, s1);
+                s0 = fmaf(hi.z, qb.z, s0);
+                s1 = fmaf(hi.w, qb.w, s1);
+            }
+        }
+        const float sv = valid ? s0 + s1 : -FLT_MAX;
+        const float m_new = fmaxf(m_run, warp_max(sv));
+        const float corr = exp2f(m_run - m_new);
+        const float p = valid ? exp2f(sv - m_new) : 0.0f;
+        l_run = l_run * corr + p;  // per-lane partial sums, reduced once at the end
+        m_run = m_new;
+        ps[g][lane] = p;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] *= corr;
+        __syncwarp();
+        for (int j = 0; j < n_valid; ++j) {
+            const float pj = ps[g][j];
+            const float4 vf = h4_to_f4(*reinterpret_cast<const uint2 *>(vs + j * D + lane * E));
+            acc[0] = fmaf(pj, vf.x, acc[0]);
+            acc[1] = fmaf(pj, vf.y, acc[1]);
+            acc[2] = fmaf(pj, vf.z, acc[2]);
+            acc[3] = fmaf(pj, vf.w, acc[3]);
+        }
+        __syncthreads();  // the stage is consumed by every warp before it is refilled
+        issue(tile + kCaStages);
+    }
+    ca_wait<0>();
+    const float l_tot = warp_sum(l_run);
+    if (splits == 1) {
+        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+        *reinterpret_cast<uint2 *>(out + b * o_sb + static_cast<int64_t>(h) * D + lane * E) =
+            f4_to_h4(make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv));
+        return;
+    }
+    *reinterpret_cast<float4 *>(&part_acc[g][lane * E]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (lane == 0) {
+        part_ml[g][0] = m_run;
+        part_ml[g][1] = l_tot;
+    }
+    ca_cluster_sync();
+    for (int hh = sp; hh < G; hh += splits) {
+        float mq[kCaMaxSplits], lq[kCaMaxSplits];
+        float mx = -FLT_MAX;
+#pragma unroll
+        for (int q = 0; q < kCaMaxSplits; ++q) {
+            if (q < splits) {
+                mq[q] = ca_ld_remote(&part_ml[hh][0], q);
+                lq[q] = ca_ld_remote(&part_ml[hh][1], q);
+                mx = fmaxf(mx, mq[q]);
+            }
+        }
+        float lsum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kCaMaxSplits; ++q) {
+            if (q < splits) {
+                mq[q] = mq[q] == -FLT_MAX ? 0.0f : exp2f(mq[q] - mx);
+                lsum = fmaf(mq[q], lq[q], lsum);
+            }
+        }
+        const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+        for (int d = threadIdx.x; d < D; d += NT) {
+            float a = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kCaMaxSplits; ++q)
+                if (q < splits) a = fmaf(mq[q], ca_ld_remote(&part_acc[hh][d], q), a);
+            out[b * o_sb + static_cast<int64_t>(kh * G + hh) * D + d] = __float2half_rn(a * inv);
+        }
+    }
+    ca_cluster_sync();  // partials stay in place until every CTA of the cluster has read them
+}
+
 // ------------------------------------------------------ prefill attention
 // CTA = 4 warps on (b, head h, 16-query tile).  Keys are processed in tiles
 // of 32: warp w owns queries 4w..4w+3 of the tile; lane j scores key j of the
@@ -819,13 +1064,49 @@ int launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t strea
     return T2C_OK;
 }
 
+// Launch with a (cluster, 1, 1) thread-block cluster and programmatic stream
+// serialization; the dynamic shared-memory limit is raised once per device.
+template <typename Kernel, typename... Args>
+int launch_cluster(Kernel kernel, bool &configured, dim3 grid, dim3 block, size_t smem, unsigned cluster,
+                   cudaStream_t stream, Args... args) {
+    if (!configured) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+            cudaSuccess)
+            return set_error(T2C_ECUDA, "cluster launch: cudaFuncSetAttribute failed");
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args...);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "cluster launch: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+int current_device_slot() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    return dev;
+}
+
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // Split partials (max, sum, 2 pad words, acc[D]) for every (b, head, split),
 // then one arrival counter per (b, head) in the last B * NH words.
 int64_t attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits) {
     (void)NK;
-    return splits > 1 ? B * NH * splits * (D + 4) + B * NH : 0;
+    return splits > kCaMaxSplits ? B * NH * splits * (D + 4) + B * NH : 0;
 }
 
 }  // namespace
@@ -948,15 +1229,36 @@ extern "C" int t2c_attn_decode_fused(const void *q_in, const void *k_in, const v
     if (!aligned(q_in, 8) || !aligned(k_in, 8) || !aligned(v_in, 8) || q_sb % 4 || k_sb % 4 || v_sb % 4 || !aligned(q_w, 16) ||
         !aligned(k_w, 16))
         return set_error(T2C_EINVAL, "attn_decode_fused: q/k/v rows must be 8-byte aligned");
+    const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+    const cudaStream_t s = as_stream(stream);
+    if (splits <= kCaMaxSplits) {
+        static bool configured[4][64] = {};  // [group 1 / 2 / 4 / 8][device]
+        const int dev_slot = current_device_slot();
+        const dim3 grid(static_cast<unsigned>(B * NK * splits));
+#define T2C_CLUSTER(GG)                                                                                                \
+    return launch_cluster(attn_decode_cluster_kernel<GG>, configured[GG == 1 ? 0 : GG == 2 ? 1 : GG == 4 ? 2 : 3][dev_slot], \
+                          grid, dim3(GG * 32), kCaSmem,                                                                  \
+                          static_cast<unsigned>(splits), s, static_cast<const __half *>(q_in),                           \
+                          static_cast<const __half *>(k_in), static_cast<const __half *>(v_in), q_sb, k_sb, v_sb, q_w,   \
+                          k_w, inv_freq, eps, static_cast<__half *>(k_cache), static_cast<__half *>(v_cache), cb, cs, ch, \
+                          static_cast<__half *>(out), o_sb, positions, static_cast<int>(NK), static_cast<int>(max_len),  \
+                          static_cast<int>(splits), qscale)
+        switch (G) {
+            case 1: T2C_CLUSTER(1);
+            case 2: T2C_CLUSTER(2);
+            case 4: T2C_CLUSTER(4);
+            case 8: T2C_CLUSTER(8);
+            default: return set_error(T2C_EUNSUPPORTED, "attn_decode_fused: group %d", G);
+        }
+#undef T2C_CLUSTER
+    }
     int *counters = nullptr;
-    if (splits > 1) {
+    {
         const int64_t need = attn_decode_fused_workspace(B, NH, NK, D, splits);
         if (!workspace || workspace_floats < need)
             return set_error(T2C_ESCRATCH, "attn_decode_fused: workspace needs %lld words", (long long)need);
         counters = reinterpret_cast<int *>(workspace + (need - B * NH));
     }
-    const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-    const cudaStream_t s = as_stream(stream);
     const dim3 grid(static_cast<unsigned>(B * NK * splits));
 #define T2C_FUSED(GG)                                                                                              \
     return launch(attn_decode_fused_kernel<GG>, grid, dim3(GG * 32), 0, s, static_cast<const __half *>(q_in),               \

@@ -1242,7 +1242,8 @@ __device__ __forceinline__ bool slot_wait_gen(volatile int *gen, int want) {
 }
 
 template <int MT>
-__device__ __forceinline__ void mma_finish_block(const QParams &p, int64_t block, const float v[2][2], int lane) {
+__device__ __forceinline__ void mma_finish_block(const QParams &p, int64_t block, const float v[2][2], int lane,
+                                                 const float *res_pre = nullptr) {
     const bool swiglu = p.mode == MODE_SWIGLU;
     const int g = lane >> 2, t = lane & 3;
     const int si = swiglu ? 0 : stream_of(p, block);
@@ -1288,7 +1289,11 @@ __device__ __forceinline__ void mma_finish_block(const QParams &p, int64_t block
             val = silu(v[0][h]) * v[1][h];
         } else {
             val = v[0][h];
-            if (st.res) val += __half2float(st.res[o]);
+            if (res_pre) {
+                val += res_pre[h];
+            } else if (st.res) {
+                val += __half2float(st.res[o]);
+            }
         }
         st.y[o] = __float2half_rn(val);
     }
@@ -1438,23 +1443,27 @@ constexpr int kM1SegX = 512 + 32 + 512 + 32;      // plane bytes (+ gaps)
 constexpr int kM1SegBytes = kM1SegX + 16 * 8;    // + meta
 constexpr int kM1MaxSegs = 16;                   // per warp (K <= 65536)
 
-// Quantizes values [k0, k0 + 512) of x into one segment area.
-__device__ __forceinline__ void m1_prepare_segment(const QParams &p, int k0, float inv_rms, uint8_t *area, int lane) {
+// x values [k0, k0 + 512) of a segment: lane l holds values 16 l .. 16 l + 15.
+__device__ __forceinline__ void m1_load_x(const QParams &p, int k0, int lane, float f[16]) {
     const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + k0 + 16 * lane);
-    float f[16];
     unpack8(xv[0], f);
     unpack8(xv[1], f + 8);
-    if (p.norm_w != nullptr) {
-        const float4 *wv = reinterpret_cast<const float4 *>(p.norm_w + k0 + 16 * lane);
+}
+__device__ __forceinline__ void m1_load_norm(const QParams &p, int k0, int lane, float w[16]) {
+    const float4 *wv = reinterpret_cast<const float4 *>(p.norm_w + k0 + 16 * lane);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 w4 = wv[i];
-            f[4 * i] *= inv_rms * w4.x;
-            f[4 * i + 1] *= inv_rms * w4.y;
-            f[4 * i + 2] *= inv_rms * w4.z;
-            f[4 * i + 3] *= inv_rms * w4.w;
-        }
+    for (int i = 0; i < 4; ++i) {
+        const float4 w4 = wv[i];
+        w[4 * i] = w4.x;
+        w[4 * i + 1] = w4.y;
+        w[4 * i + 2] = w4.z;
+        w[4 * i + 3] = w4.w;
     }
+}
+
+// Quantizes one segment of x (f, already scaled by the RMSNorm when there is
+// one) into a segment area.
+__device__ __forceinline__ void m1_prepare_segment(const float f[16], uint8_t *area, int lane) {
     float amax = 0.0f;
 #pragma unroll
     for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(f[e]));
@@ -1479,6 +1488,18 @@ __device__ __forceinline__ void m1_prepare_segment(const QParams &p, int k0, flo
         const float f_sx = (lane & 2) ? sx * 0.0625f : sx;
         *reinterpret_cast<float2 *>(area + kM1SegX + 8 * (lane >> 1)) = make_float2(f_sx, sx * static_cast<float>(sum));
     }
+}
+
+// Residual values of rows g, g + 8 of row block `blk` (lane t == 0), read
+// well before the epilogue that adds them.
+__device__ __forceinline__ void m1_load_res(const QParams &p, int blk, int lane, float rv[2]) {
+    rv[0] = rv[1] = 0.0f;
+    if (p.mode != MODE_ROWS || (lane & 3) != 0) return;
+    const QStream &st = p.s[p.nstreams > 1 ? stream_of(p, blk) : 0];
+    if (st.res == nullptr) return;
+    const int64_t row = (blk - st.rs_begin) * kMmaRows + (lane >> 2);
+    if (row < st.n) rv[0] = __half2float(st.res[row]);
+    if (row + 8 < st.n) rv[1] = __half2float(st.res[row + 8]);
 }
 
 // Fragment mapping of the M = 1 kernel (m16n8k32, A = 16 weight rows, B = x).
@@ -1559,6 +1580,15 @@ __device__ __forceinline__ void m1_block(const uint8_t *rowg, const uint8_t *xse
     }
 }
 
+// Split-K slot of the M = 1 kernel: each warp of a row block's group stores
+// its partial sums in its own column; the last warp to arrive adds the
+// columns in warp order (the result does not depend on arrival order).
+struct M1Slot {
+    float v[2][kMmaRows][kMmaWarps];  // [gate/up or value][row][warp of the group]
+    int arrived;
+    int gen;
+};
+
 // Item j of row block `blk` (segment seg0 + j * wpb; SwiGLU: gate / up
 // alternate) as one 16-row x 288-byte TMA box.
 __device__ __forceinline__ void m1_issue(const QParams &p, int blk, int j, int seg0, uint8_t *stage, uint64_t *bar) {
@@ -1592,7 +1622,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
     uint8_t *xarea = smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
                      static_cast<size_t>(warp) * p.xseg_per_warp * kM1SegBytes;
-    MmaSlot *slots = reinterpret_cast<MmaSlot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
+    M1Slot *slots = reinterpret_cast<M1Slot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes +
                                                  static_cast<size_t>(kMmaWarps) * p.xseg_per_warp * kM1SegBytes);
 
     // producer cursor (warp-uniform; lane 0 issues)
@@ -1608,22 +1638,34 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
             pblk += step;
         }
     }
-    for (int i = threadIdx.x; i < kMmaSlots * p.bpc * static_cast<int>(sizeof(MmaSlot) / 4); i += kMmaThreads)
+    for (int i = threadIdx.x; i < kMmaSlots * p.bpc * static_cast<int>(sizeof(M1Slot) / 4); i += kMmaThreads)
         reinterpret_cast<int *>(slots)[i] = 0;
+    // RMSNorm weights of the first segment: weights, like the matrix rows, are
+    // never written by the preceding kernel, so they load before the wait
+    float nw[16];
+    const bool norm = p.norm_w != nullptr;
+    if (norm && nsegw > 0) m1_load_norm(p, seg0 * (kMmaSegBlocks * 256), lane, nw);
     __syncthreads();  // slot zeroing visible to every warp
     pdl_wait();
     pdl_trigger();
-    // this warp's x segments; with a fused RMSNorm the wpb warps of a group
-    // (which together hold every segment of the row) add their sums of squares
-    // through shared memory (one CTA barrier)
+    float rv[2];
+    if (first < total) m1_load_res(p, first, lane, rv);
+    // this warp's x segments (the first one stays in registers); with a fused
+    // RMSNorm the wpb warps of a group (which together hold every segment of
+    // the row) add their sums of squares through shared memory (one CTA barrier)
+    float xf[16];
+    if (nsegw > 0) m1_load_x(p, seg0 * (kMmaSegBlocks * 256), lane, xf);
     float inv_rms = 1.0f;
-    if (p.norm_w != nullptr) {
+    if (norm) {
         float ss = 0.0f;
         for (int j = 0; j < nsegw; ++j) {
-            const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + (seg0 + j * p.wpb) * (kMmaSegBlocks * 256));
             float f[16];
-            unpack8(xv[2 * lane], f);
-            unpack8(xv[2 * lane + 1], f + 8);
+            if (j == 0) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) f[e] = xf[e];
+            } else {
+                m1_load_x(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), lane, f);
+            }
 #pragma unroll
             for (int e = 0; e < 16; ++e) ss = fmaf(f[e], f[e], ss);
         }
@@ -1635,8 +1677,30 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
         for (int w = group * p.wpb; w < (group + 1) * p.wpb; ++w) tot += sq[w];
         inv_rms = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
     }
-    for (int j = 0; j < nsegw; ++j)
-        m1_prepare_segment(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), inv_rms, xarea + j * kM1SegBytes, lane);
+    for (int j = 0; j < nsegw; ++j) {
+        const int k0 = (seg0 + j * p.wpb) * (kMmaSegBlocks * 256);
+        float f[16], w[16];
+        if (j == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                f[e] = xf[e];
+                w[e] = norm ? nw[e] : 1.0f;
+            }
+        } else {
+            m1_load_x(p, k0, lane, f);
+            if (norm) {
+                m1_load_norm(p, k0, lane, w);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) w[e] = 1.0f;
+            }
+        }
+        if (norm) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) f[e] *= inv_rms * w[e];
+        }
+        m1_prepare_segment(f, xarea + j * kM1SegBytes, lane);
+    }
     __syncwarp();
 
     const M1Lane L = m1_lane(lane);
@@ -1645,6 +1709,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     uint32_t phase = 0;
     bool failed = false;
     for (int blk = first; blk < total; blk += step, ++it) {
+        if (it > 0) m1_load_res(p, blk, lane, rv);
         float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         for (int j = 0; j < items; ++j) {
             if (!failed && !mbar_wait(&full[s], phase)) {
@@ -1689,10 +1754,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
             }
         if (p.wpb == 1) {
-            mma_finish_block<1>(p, blk, acc, lane);
+            mma_finish_block<1>(p, blk, acc, lane, rv);
             continue;
         }
-        MmaSlot *slot = slots + (it % kMmaSlots) * p.bpc + group;
+        M1Slot *slot = slots + (it % kMmaSlots) * p.bpc + group;
         if (!slot_wait_gen(&slot->gen, it / kMmaSlots)) {
             report_device_error(T2C_ETIMEOUT);
             failed = true;
@@ -1701,8 +1766,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
         if (t == 0) {
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                atomicAdd(&slot->v[r][g][0], acc[r][0]);
-                atomicAdd(&slot->v[r][g + 8][0], acc[r][1]);
+                slot->v[r][g][seg0] = acc[r][0];
+                slot->v[r][g + 8][seg0] = acc[r][1];
             }
         }
         __syncwarp();
@@ -1714,21 +1779,15 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence_block();
-        float v[2][2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            v[r][0] = *reinterpret_cast<volatile float *>(&slot->v[r][g][0]);
-            v[r][1] = *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][0]);
-        }
-        mma_finish_block<1>(p, blk, v, lane);
-        __syncwarp();
-        if (t == 0) {
+        float v[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        for (int w = 0; w < p.wpb; ++w) {
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                slot->v[r][g][0] = 0.0f;
-                slot->v[r][g + 8][0] = 0.0f;
+                v[r][0] += *reinterpret_cast<volatile float *>(&slot->v[r][g][w]);
+                v[r][1] += *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][w]);
             }
         }
+        mma_finish_block<1>(p, blk, v, lane, rv);
         __syncwarp();
         if (lane == 0) {
             slot->arrived = 0;
@@ -2019,7 +2078,7 @@ int launch_m1(QParams p, cudaStream_t stream) {
     p.xseg_per_warp = (p.nseg + p.wpb - 1) / p.wpb;
     if (p.xseg_per_warp > kM1MaxSegs) return set_error(T2C_EUNSUPPORTED, "qmv_m1: K too large");
     const size_t fixed = kStageHead + static_cast<size_t>(kMmaWarps) * p.xseg_per_warp * kM1SegBytes +
-                         static_cast<size_t>(kMmaSlots) * p.bpc * sizeof(MmaSlot) + kMmaWarps * sizeof(float);
+                         static_cast<size_t>(kMmaSlots) * p.bpc * sizeof(M1Slot) + kMmaWarps * sizeof(float);
     const size_t per_stage = static_cast<size_t>(kMmaWarps) * p.stage_bytes;
     // two CTAs per SM when two stages per warp fit in half of the shared memory, else one CTA with more stages
     const size_t half = 113 * 1024;

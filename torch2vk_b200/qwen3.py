@@ -142,8 +142,12 @@ class Qwen3Runner:
         self.stopped = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self.eos = torch.tensor(list(self.eos_ids) or [-1], dtype=torch.int64, device=dev)
         if self.decode_splits <= 0:
-            if self.fused_attention:
-                # about 4 CTAs per SM over (batch, KV head, split), at most one split per 64 cache rows
+            if self.fused_attention and self.max_seq <= 16384:
+                # one cluster of up to 8 CTAs per (sequence, KV head), about two CTAs per SM
+                want = max(1, 296 // max(1, self.batch * cfg.kv_heads))
+                self.decode_splits = max(1, min(8, want, self.max_seq // 64))
+            elif self.fused_attention:
+                # long caches: more splits, combined through a global workspace
                 want = max(1, 592 // max(1, self.batch * cfg.kv_heads))
                 self.decode_splits = max(1, min(32, want, self.max_seq // 64))
             else:
