@@ -543,45 +543,67 @@ __global__ void __launch_bounds__(G * 32) attn_decode_fused_kernel(
 }
 
 // ------------------------------------------ cluster decode attention (T = 1)
-// The same work as attn_decode_fused_kernel for splits <= 8: the `splits`
-// CTAs of one (batch b, kv head kh) form a thread-block cluster.  Each CTA
-// streams its cache positions through a ring of shared-memory tiles
-// (cp.async; tiles of earlier positions, the RoPE angles and the norm weights
-// are requested before griddepcontrol.wait), patches the new position's k / v
-// into its tile, and leaves per-head partials (max, sum, acc) in its own
-// shared memory.  After a cluster barrier, CTA r combines heads r, r + splits,
-// ... by reading every CTA's partials through distributed shared memory; a
-// second cluster barrier keeps the partials alive until those reads are done.
+// The same work as attn_decode_fused_kernel for splits <= 8, on tensor cores:
+// the `splits` CTAs of one (batch b, kv head kh) form a thread-block cluster.
+// A CTA owns the cache positions [p0, p1) of its split and streams them as
+// 32-position tiles through a ring of shared-memory stages (cp.async; the
+// first kCaStages tiles, the RoPE angles and the norm weights are requested
+// before griddepcontrol.wait).  Its 4 warps take 4 tiles at a time; for its
+// tile a warp computes the scores of all G query heads of the KV head with
+// mma.m16n8k16 (positions as rows, heads as the 8 columns: S^T = K Q^T), runs
+// an online softmax per head, and accumulates O^T += V^T P^T (dims as rows;
+// P split into fp16 high and low parts so the product keeps fp32 accuracy).
+// The warps' states merge through shared memory into the CTA's partial
+// (max, sum, acc) per head, which goes by distributed-shared-memory stores to
+// the CTA that combines that head (head hh -> cluster rank hh % splits); one
+// cluster barrier (release / acquire) then lets the combining CTAs finish.
 // No workspace, no atomics, no global round trip for the combine.
 constexpr int kCaTile = 32;
-constexpr int kCaStages = 4;
+constexpr int kCaStages = 8;
+constexpr int kCaWarps = 4;
 constexpr int kCaMaxSplits = 8;
-constexpr int kCaKStride = 136;  // halves per K row in shared memory: 272-byte rows, conflict-free 16-byte reads
-constexpr int kCaStageBytes = kCaTile * kCaKStride * 2 + kCaTile * 128 * 2;
+constexpr int kCaRow = 136;  // halves per K / V row in shared memory (272 B: conflict-free ldmatrix rows)
+constexpr int kCaStageBytes = 2 * kCaTile * kCaRow * 2;
 constexpr int kCaSmem = kCaStages * kCaStageBytes;
+constexpr int kCaRecv = 132;  // floats per received partial: acc[128], max, sum
 
-__device__ __forceinline__ void ca_cp16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void ca_cp16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
 }
 __device__ __forceinline__ void ca_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void ca_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-__device__ __forceinline__ void ca_cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ uint32_t ca_cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
-__device__ __forceinline__ float ca_ld_remote(const void *local, uint32_t rank) {
+__device__ __forceinline__ void ca_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void ca_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void ca_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void ca_st_remote(float *local, uint32_t rank, float v) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t r[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_f16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // RMSNorm (weights w) + RoPE (cos / sin of this lane's 4 dims) of one 128-value head row.
@@ -601,23 +623,25 @@ __device__ __forceinline__ void norm_rope_pre(const uint2 raw, const float w[4],
 }
 
 template <int G>
-__global__ void __launch_bounds__(G * 32) attn_decode_cluster_kernel(
+__global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
     const __half *__restrict__ q_in, const __half *__restrict__ k_in, const __half *__restrict__ v_in, int64_t q_sb,
     int64_t k_sb, int64_t v_sb, const float *__restrict__ q_w, const float *__restrict__ k_w,
     const float *__restrict__ inv_freq, float eps, __half *kc, __half *vc, int64_t cb, int64_t cs, int64_t ch,
     __half *__restrict__ out, int64_t o_sb, const int32_t *__restrict__ positions, int NK, int max_len, int splits,
     float qscale) {
-    constexpr int D = 128, E = 4, NT = G * 32;
+    static_assert(G <= 8, "at most 8 query heads per KV head (the mma N dimension)");
+    constexpr int D = 128, E = 4, NT = kCaWarps * 32;
     extern __shared__ __align__(128) uint8_t ca_smem[];
-    __shared__ __align__(16) float qs[G][D];
-    __shared__ __align__(16) float ps[G][kCaTile];
-    __shared__ __align__(16) float part_acc[G][D];
-    __shared__ float part_ml[G][2];
+    __shared__ __align__(16) __half qs[8][D];                 // fp16 q rows (heads >= G stay zero)
+    __shared__ __align__(16) __half pst[kCaWarps][2][8][40];  // P^T (hi, lo) per warp: [head][position], padded rows
+    __shared__ __align__(16) float wo[kCaWarps][8][D];        // per-warp acc
+    __shared__ float wml[kCaWarps][8][2];                     // per-warp (max, sum)
+    __shared__ __align__(16) float recv[16][kCaRecv];         // partials received for the heads this CTA combines
     const int sp = static_cast<int>(ca_cluster_rank());
     const int kh = (blockIdx.x / splits) % NK;
     const int b = blockIdx.x / (splits * NK);
-    const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = kh * G + g;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
     const int pos = positions[b];
     if (pos < 0 || pos >= max_len) {  // no cache row to write: report, touch nothing (uniform over the cluster)
         pdl_wait();
@@ -625,6 +649,7 @@ __global__ void __launch_bounds__(G * 32) attn_decode_cluster_kernel(
         if (threadIdx.x == 0) report_device_error(T2C_EINVAL);
         return;
     }
+    if (splits > 1) ca_arrive_relaxed();  // every CTA of the cluster has started before any remote store
     const int len = pos + 1;
     const int chunk = (len + splits - 1) / splits;
     const int p0 = min(len, sp * chunk), p1 = min(len, p0 + chunk);
@@ -632,24 +657,23 @@ __global__ void __launch_bounds__(G * 32) attn_decode_cluster_kernel(
     const bool owner = p0 <= pos && pos < p1;
     const __half *kbase = kc + b * cb + kh * ch;
     const __half *vbase = vc + b * cb + kh * ch;
-    // tile `tile` of this CTA's range into ring stage tile % kCaStages: one commit group per call
+    // tile `tile` of the range into stage tile % kCaStages (rows past p1 zero-filled); one commit group per call
     auto issue = [&](int tile) {
         if (tile < ntiles) {
-            uint8_t *st = ca_smem + (tile % kCaStages) * kCaStageBytes;
-            __half *ks = reinterpret_cast<__half *>(st);
-            __half *vs = reinterpret_cast<__half *>(st + kCaTile * kCaKStride * 2);
+            __half *ks = reinterpret_cast<__half *>(ca_smem + (tile % kCaStages) * kCaStageBytes);
+            __half *vs = ks + kCaTile * kCaRow;
             const int t0 = p0 + tile * kCaTile;
-            const int rows = min(kCaTile, p1 - t0);
-            for (int i = threadIdx.x; i < rows * 16; i += NT) {
+            for (int i = threadIdx.x; i < kCaTile * 16; i += NT) {
                 const int r = i >> 4, c = i & 15;
-                const int64_t src = static_cast<int64_t>(t0 + r) * cs + c * 8;
-                ca_cp16(ks + r * kCaKStride + c * 8, kbase + src);
-                ca_cp16(vs + r * D + c * 8, vbase + src);
+                const bool in = t0 + r < p1;
+                const int64_t src = (in ? static_cast<int64_t>(t0 + r) * cs : 0) + c * 8;
+                ca_cp16(ks + r * kCaRow + c * 8, kbase + src, in ? 16u : 0u);
+                ca_cp16(vs + r * kCaRow + c * 8, vbase + src, in ? 16u : 0u);
             }
         }
         ca_commit();
     };
-#pragma unroll
+#pragma unroll 1
     for (int i = 0; i < kCaStages; ++i) issue(i);
     float cw[E], sw[E], qw[E], kw[E];
 #pragma unroll
@@ -658,133 +682,203 @@ __global__ void __launch_bounds__(G * 32) attn_decode_cluster_kernel(
         qw[e] = q_w[lane * E + e];
         kw[e] = k_w[lane * E + e];
     }
+    for (int i = threadIdx.x; i < 8 * D / 2; i += NT) reinterpret_cast<uint32_t *>(qs)[i] = 0u;
+    __syncthreads();
 
     pdl_wait();
     pdl_trigger();
-    {
+    for (int hh = w; hh < G; hh += kCaWarps) {
         float r[4];
-        norm_rope_pre(*reinterpret_cast<const uint2 *>(q_in + b * q_sb + static_cast<int64_t>(h) * D + lane * E), qw, cw,
-                      sw, eps, lane, r);
-#pragma unroll
-        for (int e = 0; e < E; ++e) qs[g][lane * E + e] = __half2float(__float2half_rn(r[e])) * qscale;
+        norm_rope_pre(*reinterpret_cast<const uint2 *>(q_in + b * q_sb + static_cast<int64_t>(kh * G + hh) * D + lane * E),
+                      qw, cw, sw, eps, lane, r);
+        *reinterpret_cast<uint2 *>(&qs[hh][lane * E]) = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
     }
     uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
-    if (owner) {
+    if (owner && w == 0) {
         float r[4];
         norm_rope_pre(*reinterpret_cast<const uint2 *>(k_in + b * k_sb + static_cast<int64_t>(kh) * D + lane * E), kw, cw,
                       sw, eps, lane, r);
         knew = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
         vnew = *reinterpret_cast<const uint2 *>(v_in + b * v_sb + static_cast<int64_t>(kh) * D + lane * E);
-        if (g == 0) {
-            *reinterpret_cast<uint2 *>(kc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = knew;
-            *reinterpret_cast<uint2 *>(vc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = vnew;
-        }
+        *reinterpret_cast<uint2 *>(kc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = knew;
+        *reinterpret_cast<uint2 *>(vc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = vnew;
     }
-    __syncwarp();
+    __syncthreads();  // q rows complete
+    // B fragments of Q^T (k = dim, n = head) for the 8 k-steps of 16 dims
+    uint32_t qb[8][2];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+        qb[ks][0] = *reinterpret_cast<const uint32_t *>(&qs[g][16 * ks + 2 * t]);
+        qb[ks][1] = *reinterpret_cast<const uint32_t *>(&qs[g][16 * ks + 2 * t + 8]);
+    }
 
-    float m_run = -FLT_MAX, l_run = 0.0f;
-    float acc[E] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int tile = 0; tile < ntiles; ++tile) {
-        ca_wait<kCaStages - 1>();
-        __syncthreads();  // every thread's copies of this tile have landed
-        uint8_t *st = ca_smem + (tile % kCaStages) * kCaStageBytes;
-        __half *ks = reinterpret_cast<__half *>(st);
-        __half *vs = reinterpret_cast<__half *>(st + kCaTile * kCaKStride * 2);
-        const int t0 = p0 + tile * kCaTile;
-        const int n_valid = min(kCaTile, p1 - t0);
-        if (owner && pos >= t0 && pos < t0 + n_valid) {
-            // the tile holds the new position: its rows were read before this kernel wrote them
-            if (g == 0) {
-                *reinterpret_cast<uint2 *>(ks + (pos - t0) * kCaKStride + lane * E) = knew;
-                *reinterpret_cast<uint2 *>(vs + (pos - t0) * D + lane * E) = vnew;
+    // per lane: heads 2t, 2t+1; acc rows dims 16m + g, 16m + g + 8
+    float m_run[2] = {-FLT_MAX, -FLT_MAX}, l_run[2] = {0.0f, 0.0f};
+    float o[8][4];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
+    const int new_tile = owner ? (pos - p0) / kCaTile : -1;
+    for (int round = 0; round * kCaWarps < ntiles; ++round) {
+        ca_wait<kCaStages - kCaWarps>();
+        __syncthreads();  // every thread's copies of this round's tiles have landed
+        if (new_tile >= round * kCaWarps && new_tile < (round + 1) * kCaWarps) {
+            // the tile of the new position was read before this kernel wrote that row
+            __half *ks = reinterpret_cast<__half *>(ca_smem + (new_tile % kCaStages) * kCaStageBytes);
+            const int r = pos - p0 - new_tile * kCaTile;
+            if (w == 0) {
+                *reinterpret_cast<uint2 *>(ks + r * kCaRow + lane * E) = knew;
+                *reinterpret_cast<uint2 *>(ks + kCaTile * kCaRow + r * kCaRow + lane * E) = vnew;
             }
             __syncthreads();
         }
-        const bool valid = lane < n_valid;
-        float s0 = 0.0f, s1 = 0.0f;
-        if (valid) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(ks + lane * kCaKStride);
+        const int tile = round * kCaWarps + w;
+        if (tile < ntiles) {
+            const __half *ks = reinterpret_cast<const __half *>(ca_smem + (tile % kCaStages) * kCaStageBytes);
+            const __half *vs = ks + kCaTile * kCaRow;
+            const int t0 = p0 + tile * kCaTile;
+            // S^T = K Q^T: rows = 32 positions (2 m-tiles), columns = 8 heads
+            float s[2][4];
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
-                const uint4 k8 = kr[c];
-                const float4 lo = h4_to_f4(make_uint2(k8.x, k8.y));
-                const float4 hi = h4_to_f4(make_uint2(k8.z, k8.w));
-                const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][c * 8]);
-                const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][c * 8 + 4]);
-                s0 = fmaf(lo.x, qa.x, s0);
-                s1 = fmaf(lo.y, qa.y, s1);
-                s0 = fmaf(lo.z, qa.z, s0);
-                s1 = fmaf(lo.w, qa.w, s1);
-                s0 = fmaf(hi.x, qb.x, s0);
-                s1 = fmaf(hi.y, qb.y, s1);
-                s0 = fmaf(hi.z, qb.z, s0);
-                s1 = fmaf(hi.w, qb.w, s1);
+            for (int mt = 0; mt < 2; ++mt) {
+                s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.0f;
+#pragma unroll
+                for (int ks8 = 0; ks8 < 8; ++ks8) {
+                    uint32_t a[4];
+                    ldsm_x4(a, ks + (16 * mt + (lane & 15)) * kCaRow + 16 * ks8 + 8 * (lane >> 4));
+                    mma_f16_16816(s[mt], a, qb[ks8][0], qb[ks8][1]);
+                }
             }
-        }
-        const float sv = valid ? s0 + s1 : -FLT_MAX;
-        const float m_new = fmaxf(m_run, warp_max(sv));
-        const float corr = exp2f(m_run - m_new);
-        const float p = valid ? exp2f(sv - m_new) : 0.0f;
-        l_run = l_run * corr + p;  // per-lane partial sums, reduced once at the end
-        m_run = m_new;
-        ps[g][lane] = p;
+            // online softmax per head (columns 2t, 2t+1); rows g, g+8 of each m-tile
+            float mx[2] = {-FLT_MAX, -FLT_MAX};
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] *= corr;
-        __syncwarp();
-        for (int j = 0; j < n_valid; ++j) {
-            const float pj = ps[g][j];
-            const float4 vf = h4_to_f4(*reinterpret_cast<const uint2 *>(vs + j * D + lane * E));
-            acc[0] = fmaf(pj, vf.x, acc[0]);
-            acc[1] = fmaf(pj, vf.y, acc[1]);
-            acc[2] = fmaf(pj, vf.z, acc[2]);
-            acc[3] = fmaf(pj, vf.w, acc[3]);
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int p = t0 + 16 * mt + g + 8 * (e >> 1);
+                    s[mt][e] = p < p1 ? s[mt][e] * qscale : -FLT_MAX;
+                    mx[e & 1] = fmaxf(mx[e & 1], s[mt][e]);
+                }
+            float corr[2];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 4));
+                mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 8));
+                mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 16));
+                const float m_new = fmaxf(m_run[c], mx[c]);
+                corr[c] = exp2f(m_run[c] - m_new);
+                m_run[c] = m_new;
+                l_run[c] *= corr[c];
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int c = e & 1;
+                    const float p = s[mt][e] == -FLT_MAX ? 0.0f : exp2f(s[mt][e] - m_run[c]);
+                    l_run[c] += p;
+                    const __half ph = __float2half_rn(p);
+                    const __half pl = __float2half_rn(p - __half2float(ph));
+                    const int col = 16 * mt + g + 8 * (e >> 1);
+                    pst[w][0][2 * t + c][col] = ph;
+                    pst[w][1][2 * t + c][col] = pl;
+                }
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                o[m][0] *= corr[0];
+                o[m][1] *= corr[1];
+                o[m][2] *= corr[0];
+                o[m][3] *= corr[1];
+            }
+            __syncwarp();
+            // O^T += V^T P^T: rows = 128 dims (8 m-tiles), k = 32 positions (2 k-steps), columns = heads
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&pst[w][0][g][16 * kk + 2 * t]);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&pst[w][0][g][16 * kk + 2 * t + 8]);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&pst[w][1][g][16 * kk + 2 * t]);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(&pst[w][1][g][16 * kk + 2 * t + 8]);
+                const __half *vrow = vs + (16 * kk + (lane & 7) + 8 * (lane >> 4)) * kCaRow + 8 * ((lane >> 3) & 1);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    uint32_t a[4];
+                    ldsm_x4_t(a, vrow + 16 * m);
+                    mma_f16_16816(o[m], a, bh0, bh1);
+                    mma_f16_16816(o[m], a, bl0, bl1);
+                }
+            }
+            __syncwarp();
         }
-        __syncthreads();  // the stage is consumed by every warp before it is refilled
-        issue(tile + kCaStages);
+        __syncthreads();  // this round's stages are consumed before they are refilled
+#pragma unroll 1
+        for (int i = 0; i < kCaWarps; ++i) issue(round * kCaWarps + kCaStages + i);
     }
     ca_wait<0>();
-    const float l_tot = warp_sum(l_run);
-    if (splits == 1) {
-        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
-        *reinterpret_cast<uint2 *>(out + b * o_sb + static_cast<int64_t>(h) * D + lane * E) =
-            f4_to_h4(make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv));
-        return;
+    // merge the warps' states per head: (max, sum, acc)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        l_run[c] += __shfl_xor_sync(0xffffffffu, l_run[c], 4);
+        l_run[c] += __shfl_xor_sync(0xffffffffu, l_run[c], 8);
+        l_run[c] += __shfl_xor_sync(0xffffffffu, l_run[c], 16);
     }
-    *reinterpret_cast<float4 *>(&part_acc[g][lane * E]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    if (lane == 0) {
-        part_ml[g][0] = m_run;
-        part_ml[g][1] = l_tot;
+    if (g == 0) {
+        wml[w][2 * t][0] = m_run[0];
+        wml[w][2 * t][1] = l_run[0];
+        wml[w][2 * t + 1][0] = m_run[1];
+        wml[w][2 * t + 1][1] = l_run[1];
     }
-    ca_cluster_sync();
-    for (int hh = sp; hh < G; hh += splits) {
-        float mq[kCaMaxSplits], lq[kCaMaxSplits];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        wo[w][2 * t][16 * m + g] = o[m][0];
+        wo[w][2 * t + 1][16 * m + g] = o[m][1];
+        wo[w][2 * t][16 * m + g + 8] = o[m][2];
+        wo[w][2 * t + 1][16 * m + g + 8] = o[m][3];
+    }
+    __syncthreads();
+    if (splits > 1) ca_wait_acquire();  // (start barrier) every CTA of the cluster runs
+    const int d = threadIdx.x;  // NT == D: one dim per thread
+#pragma unroll 1
+    for (int hh = 0; hh < G; ++hh) {
         float mx = -FLT_MAX;
 #pragma unroll
-        for (int q = 0; q < kCaMaxSplits; ++q) {
-            if (q < splits) {
-                mq[q] = ca_ld_remote(&part_ml[hh][0], q);
-                lq[q] = ca_ld_remote(&part_ml[hh][1], q);
-                mx = fmaxf(mx, mq[q]);
-            }
-        }
-        float lsum = 0.0f;
+        for (int v = 0; v < kCaWarps; ++v) mx = fmaxf(mx, wml[v][hh][0]);
+        float lsum = 0.0f, a = 0.0f;
 #pragma unroll
-        for (int q = 0; q < kCaMaxSplits; ++q) {
-            if (q < splits) {
-                mq[q] = mq[q] == -FLT_MAX ? 0.0f : exp2f(mq[q] - mx);
-                lsum = fmaf(mq[q], lq[q], lsum);
-            }
+        for (int v = 0; v < kCaWarps; ++v) {
+            const float f = wml[v][hh][0] == -FLT_MAX ? 0.0f : exp2f(wml[v][hh][0] - mx);
+            lsum = fmaf(f, wml[v][hh][1], lsum);
+            a = fmaf(f, wo[v][hh][d], a);
         }
-        const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
-        for (int d = threadIdx.x; d < D; d += NT) {
-            float a = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kCaMaxSplits; ++q)
-                if (q < splits) a = fmaf(mq[q], ca_ld_remote(&part_acc[hh][d], q), a);
+        if (splits == 1) {
+            const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
             out[b * o_sb + static_cast<int64_t>(kh * G + hh) * D + d] = __float2half_rn(a * inv);
+        } else {
+            // partial of head hh -> CTA hh % splits, slot (hh / splits) * splits + sp
+            float *dst = &recv[(hh / splits) * splits + sp][0];
+            const uint32_t rank = static_cast<uint32_t>(hh % splits);
+            ca_st_remote(dst + d, rank, a);
+            if (d == 0) {
+                ca_st_remote(dst + 128, rank, mx);
+                ca_st_remote(dst + 129, rank, lsum);
+            }
         }
     }
-    ca_cluster_sync();  // partials stay in place until every CTA of the cluster has read them
+    if (splits == 1) return;
+    ca_arrive_release();
+    ca_wait_acquire();  // every partial has arrived
+    for (int hh = sp; hh < G; hh += splits) {
+        const float *src = &recv[(hh / splits) * splits][0];
+        float mx = -FLT_MAX;
+        for (int q = 0; q < splits; ++q) mx = fmaxf(mx, src[q * kCaRecv + 128]);
+        float lsum = 0.0f, a = 0.0f;
+        for (int q = 0; q < splits; ++q) {
+            const float m = src[q * kCaRecv + 128];
+            const float f = m == -FLT_MAX ? 0.0f : exp2f(m - mx);
+            lsum = fmaf(f, src[q * kCaRecv + 129], lsum);
+            a = fmaf(f, src[q * kCaRecv + d], a);
+        }
+        const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+        out[b * o_sb + static_cast<int64_t>(kh * G + hh) * D + d] = __float2half_rn(a * inv);
+    }
 }
 
 // ------------------------------------------------------ prefill attention
@@ -1237,7 +1331,7 @@ extern "C" int t2c_attn_decode_fused(const void *q_in, const void *k_in, const v
         const dim3 grid(static_cast<unsigned>(B * NK * splits));
 #define T2C_CLUSTER(GG)                                                                                                \
     return launch_cluster(attn_decode_cluster_kernel<GG>, configured[GG == 1 ? 0 : GG == 2 ? 1 : GG == 4 ? 2 : 3][dev_slot], \
-                          grid, dim3(GG * 32), kCaSmem,                                                                  \
+                          grid, dim3(kCaWarps * 32), kCaSmem,                                                            \
                           static_cast<unsigned>(splits), s, static_cast<const __half *>(q_in),                           \
                           static_cast<const __half *>(k_in), static_cast<const __half *>(v_in), q_sb, k_sb, v_sb, q_w,   \
                           k_w, inv_freq, eps, static_cast<__half *>(k_cache), static_cast<__half *>(v_cache), cb, cs, ch, \
