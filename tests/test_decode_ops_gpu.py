@@ -112,12 +112,14 @@ def test_attn_decode(NH, NK, splits):
     _close(out.view(B, NH, D), ref)
 
 
-def test_attn_prefill():
+@pytest.mark.parametrize("B,T,NH,NK,S,base", [(2, 37, 16, 8, 96, [0, 20]), (2, 150, 32, 8, 900, [0, 700]),
+                                                (1, 129, 64, 8, 200, [64])])
+def test_attn_prefill(B, T, NH, NK, S, base):
+    """Causal GQA prefill (64-query tiles on tensor cores, ragged last tile, cache prefix) vs an fp32 reference."""
     from torch2vk_b200 import kernels
 
     torch.manual_seed(3)
-    B, T, NH, NK, D, S = 2, 37, 16, 8, 128, 96
-    base = [0, 20]
+    D = 128
     q = torch.randn(B * T, NH * D, device="cuda", dtype=torch.float16)
     kc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
     vc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)

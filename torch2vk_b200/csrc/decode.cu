@@ -986,6 +986,191 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *__restr
     }
 }
 
+// ------------------------------------------- prefill attention, tensor cores
+// Flash attention for a chunk of T queries (absolute positions positions[b] +
+// t) against the cache rows 0 .. positions[b] + t, D = 128.  CTA = 4 warps on
+// (b, head h, 64-query tile); warp w owns queries 16 w .. 16 w + 15 of the
+// tile as the 16 rows of mma.m16n8k16.  Key / value tiles of 64 rows stream
+// through a 3-stage shared-memory ring (cp.async, rows padded to 272 bytes so
+// ldmatrix reads are conflict-free).  Per key tile a warp computes S = Q K^T
+// (8 n-tiles x 8 k-steps), an online softmax per row in the log2 domain, and
+// O += P V with P taken straight from the S accumulators as A fragments, split
+// into fp16 high and low parts so the product keeps fp32 accuracy.  Query
+// tiles are visited heaviest first (most keys under the causal mask).
+constexpr int kPtQ = 64;
+constexpr int kPtK = 64;
+constexpr int kPtStages = 2;
+constexpr int kPtRow = 136;  // halves per shared-memory row (272 B)
+constexpr int kPtStageBytes = 2 * kPtK * kPtRow * 2;
+constexpr int kPtSmem = kPtQ * kPtRow * 2 + kPtStages * kPtStageBytes;
+
+__global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
+    const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
+    __half *__restrict__ out, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
+    int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh, float scale_log2) {
+    extern __shared__ __align__(128) uint8_t pt_smem[];
+    __half *qs = reinterpret_cast<__half *>(pt_smem);
+    const int qtiles = (T + kPtQ - 1) / kPtQ;
+    const int qt = qtiles - 1 - static_cast<int>(blockIdx.x % qtiles);
+    const int h = (blockIdx.x / qtiles) % NH;
+    const int b = blockIdx.x / (qtiles * NH);
+    const int kh = h / (NH / NK);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    pdl_wait();
+    pdl_trigger();
+    const int base = positions[b];
+    const int q0 = qt * kPtQ;
+    const int last_key = base + min(T - 1, q0 + kPtQ - 1);
+    const int nkt = last_key / kPtK + 1;
+    const __half *kbase = kc + b * cb + kh * ch;
+    const __half *vbase = vc + b * cb + kh * ch;
+    auto issue = [&](int kt) {
+        if (kt < nkt) {
+            __half *ks = reinterpret_cast<__half *>(pt_smem + kPtQ * kPtRow * 2 + (kt % kPtStages) * kPtStageBytes);
+            __half *vs = ks + kPtK * kPtRow;
+            for (int i = threadIdx.x; i < kPtK * 16; i += 128) {
+                const int r = i >> 4, c = i & 15;
+                const int key = kt * kPtK + r;
+                const bool in = key <= last_key;
+                const int64_t src = (in ? static_cast<int64_t>(key) * cs : 0) + c * 8;
+                ca_cp16(ks + r * kPtRow + c * 8, kbase + src, in ? 16u : 0u);
+                ca_cp16(vs + r * kPtRow + c * 8, vbase + src, in ? 16u : 0u);
+            }
+        }
+        ca_commit();
+    };
+    issue(0);
+    issue(1);
+    // q tile -> shared memory (rows past T zero)
+    for (int i = threadIdx.x; i < kPtQ * 16; i += 128) {
+        const int r = i >> 4, c = i & 15;
+        const int tq = q0 + r;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (tq < T) v = *reinterpret_cast<const uint4 *>(q + b * q_sb + tq * q_st + h * q_sh + c * 8);
+        *reinterpret_cast<uint4 *>(qs + r * kPtRow + c * 8) = v;
+    }
+    __syncthreads();
+    uint32_t qa[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) ldsm_x4(qa[ks], qs + (16 * w + (lane & 15)) * kPtRow + 16 * ks + 8 * (lane >> 4));
+
+    // rows g and g + 8 of this warp: chunk-local query indices
+    const int tq0 = q0 + 16 * w + g, tq1 = tq0 + 8;
+    const int qp0 = base + tq0, qp1 = base + tq1;  // absolute positions (keys <= qp visible)
+    const int warp_first = base + q0 + 16 * w;      // smallest query position of the warp
+    float m_run[2] = {-FLT_MAX, -FLT_MAX}, l_run[2] = {0.0f, 0.0f};
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    for (int kt = 0; kt < nkt; ++kt) {
+        ca_wait<1>();
+        __syncthreads();
+        const __half *ks = reinterpret_cast<const __half *>(pt_smem + kPtQ * kPtRow * 2 + (kt % kPtStages) * kPtStageBytes);
+        const __half *vs = ks + kPtK * kPtRow;
+        const int k0 = kt * kPtK;
+        if (k0 <= base + q0 + 16 * w + 15) {  // some key of the tile is visible to some row of the warp
+            float s[8][4];
+#pragma unroll
+            for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
+#pragma unroll
+            for (int ks8 = 0; ks8 < 8; ++ks8) {
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    uint32_t kb[4];
+                    ldsm_x4(kb, ks + (16 * np + (lane & 7) + 8 * (lane >> 4)) * kPtRow + 16 * ks8 + 8 * ((lane >> 3) & 1));
+                    mma_f16_16816(s[2 * np], qa[ks8], kb[0], kb[1]);
+                    mma_f16_16816(s[2 * np + 1], qa[ks8], kb[2], kb[3]);
+                }
+            }
+            const bool masked = k0 + kPtK - 1 > warp_first;
+            float mx[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+            for (int n = 0; n < 8; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = k0 + 8 * n + 2 * t4 + (e & 1);
+                    const int r = e >> 1;
+                    float v = s[n][e] * scale_log2;
+                    if (masked && key > (r ? qp1 : qp0)) v = -FLT_MAX;
+                    s[n][e] = v;
+                    mx[r] = fmaxf(mx[r], v);
+                }
+            float corr[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                const float m_new = fmaxf(m_run[r], mx[r]);
+                corr[r] = exp2f(m_run[r] - m_new);
+                m_run[r] = m_new;
+                l_run[r] *= corr[r];
+            }
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+                o[n][0] *= corr[0];
+                o[n][1] *= corr[0];
+                o[n][2] *= corr[1];
+                o[n][3] *= corr[1];
+            }
+            // P as A fragments: k-step j covers keys 16 j .. 16 j + 15 = n-tiles 2 j, 2 j + 1
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float p[2][4];
+#pragma unroll
+                for (int hn = 0; hn < 2; ++hn)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float v = s[2 * j + hn][e];
+                        const float pv = v == -FLT_MAX ? 0.0f : exp2f(v - m_run[e >> 1]);
+                        l_run[e >> 1] += pv;
+                        p[hn][e] = pv;
+                    }
+                uint32_t ah[4], al[4];
+#pragma unroll
+                for (int hn = 0; hn < 2; ++hn)
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const __half2 hi = __floats2half2_rn(p[hn][2 * r], p[hn][2 * r + 1]);
+                        const float2 hf = __half22float2(hi);
+                        const __half2 lo = __floats2half2_rn(p[hn][2 * r] - hf.x, p[hn][2 * r + 1] - hf.y);
+                        ah[2 * hn + r] = *reinterpret_cast<const uint32_t *>(&hi);
+                        al[2 * hn + r] = *reinterpret_cast<const uint32_t *>(&lo);
+                    }
+#pragma unroll
+                for (int dp = 0; dp < 8; ++dp) {
+                    uint32_t vb[4];
+                    ldsm_x4_t(vb, vs + (16 * j + (lane & 7) + 8 * ((lane >> 3) & 1)) * kPtRow + 16 * dp + 8 * (lane >> 4));
+                    mma_f16_16816(o[2 * dp], ah, vb[0], vb[1]);
+                    mma_f16_16816(o[2 * dp], al, vb[0], vb[1]);
+                    mma_f16_16816(o[2 * dp + 1], ah, vb[2], vb[3]);
+                    mma_f16_16816(o[2 * dp + 1], al, vb[2], vb[3]);
+                }
+            }
+        }
+        __syncthreads();  // the stage is consumed before it is refilled
+        issue(kt + 2);
+    }
+    ca_wait<0>();
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+        l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+    }
+    const float inv0 = l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f;
+    const float inv1 = l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        const int d = 8 * n + 2 * t4;
+        if (tq0 < T)
+            *reinterpret_cast<__half2 *>(out + b * o_sb + tq0 * o_st + h * o_sh + d) =
+                __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+        if (tq1 < T)
+            *reinterpret_cast<__half2 *>(out + b * o_sb + tq1 * o_st + h * o_sh + d) =
+                __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+    }
+}
+
 // ---------------------------------------------------------------- misc
 __global__ void embedding_f16_kernel(const __half *__restrict__ w, const int64_t *__restrict__ ids,
                                      __half *__restrict__ out, int64_t n_ids, int64_t vocab, int H) {
@@ -1383,6 +1568,23 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
     if (!aligned(k_cache, 16) || cs % 8 || cb % 8 || ch % 8)
         return set_error(T2C_EINVAL, "attn_prefill: cache rows must be 16-byte aligned");
     const float scale = 1.0f / sqrtf(static_cast<float>(D));
+    if (D == 128 && aligned(q, 16) && qb % 8 == 0 && qt % 8 == 0 && qh % 8 == 0 && aligned(out, 4) && ob % 2 == 0 &&
+        ot % 2 == 0 && oh % 2 == 0) {
+        static bool configured[64] = {};
+        const int dev_slot = current_device_slot();
+        if (!configured[dev_slot]) {
+            if (cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem) !=
+                cudaSuccess)
+                return set_error(T2C_ECUDA, "attn_prefill: cudaFuncSetAttribute failed");
+            configured[dev_slot] = true;
+        }
+        const int64_t tiles = (T + kPtQ - 1) / kPtQ;
+        return launch(attn_prefill_tc_kernel, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128), kPtSmem,
+                      as_stream(stream), static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
+                      static_cast<const __half *>(v_cache), static_cast<__half *>(out), positions, static_cast<int>(T),
+                      static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh,
+                      1.4426950408889634f * scale);
+    }
     const int64_t qtiles = (T + kPfQ - 1) / kPfQ;
     const dim3 grid(static_cast<unsigned>(B * NH * qtiles)), block(128);
     const cudaStream_t s = as_stream(stream);
