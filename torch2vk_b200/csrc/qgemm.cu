@@ -9,10 +9,12 @@
 //    rows, two stages; requested before griddepcontrol.wait: weights are static);
 //  * x[mt, 64] fp16 arrives by 2-D TMA with 128-byte swizzle (three buffers,
 //    two chunks ahead);
-//  * the 128 threads dequantize one row each, d*sc*q - dmin*m in fp32 rounded
-//    to fp16, straight into the swizzled K-major A layout (three buffers);
-//  * one thread issues 4 x tcgen05.mma kind::f16 (K = 16 each) and commits
-//    them to the buffer's mbarrier, which also tells when A / x may be reused.
+//  * 8 warps dequantize (two threads per row, one 32-value sub-block each),
+//    d*sc*q - dmin*m in fp32 rounded to fp16, straight into the swizzled
+//    K-major A layout (three buffers);
+//  * one thread of the issue warp issues 4 x tcgen05.mma kind::f16 (K = 16
+//    each) and commits them to the buffer's mbarrier, which also tells when
+//    A / x may be reused; one thread of the producer warp issues the TMA copies.
 // Descriptors (PTX ISA "shared memory descriptor" / "instruction descriptor"):
 // K-major SWIZZLE_128B: start >> 4, LBO 1, SBO 1024 >> 4, version 1, layout 2;
 // a K step of 16 fp16 advances the start address by 32 bytes.
@@ -36,7 +38,10 @@ constexpr int kKC = 64;                     // values per K chunk
 constexpr int kNB = 3;                      // A / x buffers
 constexpr int kRawBytes = kRowsT * 144;     // one super-block of 128 rows
 constexpr int kABytes = kRowsT * kKC * 2;   // 16 KB of fp16
-constexpr int kThreadsG = 128;
+constexpr int kDeqWarps = 8;                // dequantization warps (2 threads per weight row)
+constexpr int kIssuer = 8;                  // warp that issues the tcgen05 MMAs
+constexpr int kProducer = 9;                // warp that issues the TMA copies
+constexpr int kThreadsG = 32 * (kDeqWarps + 2);
 
 struct GemmParams {
     alignas(64) CUtensorMap wmap;  // raw Q4_K words [N, row_bytes / 4], box 36 x 128
@@ -82,50 +87,49 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
 
 __device__ __forceinline__ float small_u2f_g(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
 
-// Row r of one 64-value quarter q of a 144-byte Q4_K block -> 8 swizzled 16-byte chunks of fp16.
-__device__ __forceinline__ void dequant_quarter(uint32_t raw_row, int q, uint32_t a_row, int r) {
-    uint4 h;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(h.x), "=r"(h.y), "=r"(h.z), "=r"(h.w) : "r"(raw_row));
-    uint4 n0, n1;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(n0.x), "=r"(n0.y), "=r"(n0.z), "=r"(n0.w)
-                 : "r"(raw_row + 16 + 32 * q));
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(n1.x), "=r"(n1.y), "=r"(n1.z), "=r"(n1.w)
-                 : "r"(raw_row + 32 + 32 * q));
-    // 6-bit codes of sub-blocks 2q (low nibbles) and 2q+1 (high nibbles), packing of quantize/vulkan.py:331-342
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const int i0 = (2 * q) & 3;
-    const bool low = q < 2;
-    const uint32_t y = h.y >> (8 * i0), z = h.z >> (8 * i0), w = h.w >> (8 * i0);
-    const uint32_t hs = ((y >> 6) & 0x3u) | (((y >> 14) & 0x3u) << 8);
-    const uint32_t hm = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
-    const uint32_t scp = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hs << 4));
-    const uint32_t mnp = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hm << 4));
-    const float ds[2] = {d * small_u2f_g(scp & 0xffu), d * small_u2f_g(scp >> 8)};
-    const float dm[2] = {dmin * small_u2f_g(mnp & 0xffu), dmin * small_u2f_g(mnp >> 8)};
+// One sub-block half of a 64-value chunk: row r of quarter q of a 144-byte
+// Q4_K block, nibble half hf (0: low nibbles = values 0..31 of the chunk,
+// sub-block 2q; 1: high nibbles = values 32..63, sub-block 2q + 1) -> four
+// swizzled 16-byte chunks (4 hf .. 4 hf + 3) of fp16 d*sc*q - dmin*m.
+__device__ __forceinline__ void dequant_half(const uint8_t *raw_row, int q, int hf, uint32_t a_row, int r) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(raw_row);
+    const uint4 n0 = *reinterpret_cast<const uint4 *>(raw_row + 16 + 32 * q);
+    const uint4 n1 = *reinterpret_cast<const uint4 *>(raw_row + 32 + 32 * q);
+    // 6-bit codes of sub-block j = 2q + hf (packing of quantize/vulkan.py:331-342)
+    const int j = 2 * q + hf, jb = j & 3;
+    const uint32_t y = (h.y >> (8 * jb)) & 0xffu, z = (h.z >> (8 * jb)) & 0xffu, w = (h.w >> (8 * jb)) & 0xffu;
+    const uint32_t sc = j < 4 ? (y & 63u) : ((w & 15u) | ((y >> 6) << 4));
+    const uint32_t mn = j < 4 ? (z & 63u) : ((w >> 4) | ((z >> 6) << 4));
+    const float ds = half_bits_to_float(h.x) * small_u2f_g(sc);
+    const float dm = half_bits_to_float(h.x >> 16) * small_u2f_g(mn);
     const uint32_t wq[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    const int sh = 4 * hf;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const int half_sel = c >> 2;  // 0: low nibbles (values 0..31), 1: high nibbles (32..63)
-        const uint32_t w0 = wq[2 * (c & 3)], w1 = wq[2 * (c & 3) + 1];
+    for (int c = 0; c < 4; ++c) {
+        // values 8c .. 8c+7 of the sub-block = nibble hf of bytes 8c .. 8c+7 of the quarter
+        const uint32_t lo = (wq[2 * c] >> sh) & 0x0F0F0F0Fu, hi = (wq[2 * c + 1] >> sh) & 0x0F0F0F0Fu;
         uint32_t packed[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const uint32_t src = e < 2 ? w0 : w1;
-            const int sh = 16 * (e & 1) + 4 * half_sel;
-            const float v0 = fmaf(ds[half_sel], small_u2f_g((src >> sh) & 0xFu), -dm[half_sel]);
-            const float v1 = fmaf(ds[half_sel], small_u2f_g((src >> (sh + 8)) & 0xFu), -dm[half_sel]);
+            const uint32_t src = e < 2 ? lo : hi;
+            const int k0 = 2 * (e & 1);
+            const float v0 = fmaf(ds, __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7440u + k0)) - 8388608.0f, -dm);
+            const float v1 = fmaf(ds, __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7441u + k0)) - 8388608.0f, -dm);
             const __half2 hv = __floats2half2_rn(v0, v1);
             packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
         }
-        const uint32_t dst = a_row + static_cast<uint32_t>(((c ^ (r & 7)) << 4));
+        const uint32_t dst = a_row + static_cast<uint32_t>((((4 * hf + c) ^ (r & 7)) << 4));
         asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
                      "r"(packed[2]), "r"(packed[3])
                      : "memory");
     }
 }
 
+// Warp roles: warps 0..7 dequantize (thread = weight row tid % 128, nibble
+// half tid / 128), warp 8 issues the MMAs, warp 9 issues the TMA copies.
+// They meet only at mbarriers: raw_full / raw_empty (raw weight stages),
+// x_full (x chunks), a_full (dequantized A buffers, one arrival per dequant
+// warp) and mma_done (tcgen05.commit: A / x buffer free again).
 __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_constant__ GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles
@@ -136,7 +140,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     const int kpart = blockIdx.x % p.ksplit;  // rank in the cluster
     const int64_t n0 = static_cast<int64_t>(blockIdx.x / p.ksplit) * kRowsT;
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * mt;
-    const int nsb = p.K / 256 / p.ksplit;     // super-blocks of this CTA's K range
+    const int nsb = p.K / 256 / p.ksplit;  // super-blocks of this CTA's K range
     const int sb0 = kpart * nsb;
     const int nch = nsb * 4, kc0 = sb0 * 4;
     const int xbytes = mt * 128;
@@ -146,6 +150,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     ptr += kNB * kABytes;
     const uint32_t aup_base = smem_u32(ptr);
     if (swiglu) ptr += kNB * kABytes;
+    uint8_t *x_ptr = ptr;
     const uint32_t x_base = smem_u32(ptr);
     ptr += kNB * xbytes;
     uint8_t *raw_ptr = ptr;
@@ -153,23 +158,30 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     uint8_t *rawup_ptr = ptr;
     if (swiglu) ptr += 2 * kRawBytes;
     uint64_t *raw_full = reinterpret_cast<uint64_t *>(ptr);
-    uint64_t *x_full = raw_full + 2;
-    uint64_t *mma_done = x_full + kNB;
+    uint64_t *raw_empty = raw_full + 2;
+    uint64_t *x_full = raw_empty + 2;
+    uint64_t *a_full = x_full + kNB;
+    uint64_t *mma_done = a_full + kNB;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + kNB);
-    __shared__ int failed;
+    __shared__ int failed_s;
+    volatile int &failed = failed_s;
+    const uint32_t raw_bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
 
-    if (tid == 0) {
+    if (tid == kProducer * 32) {
         failed = 0;
-        for (int i = 0; i < 2; ++i) mbar_init(&raw_full[i], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kDeqWarps);
+        }
         for (int i = 0; i < kNB; ++i) {
             mbar_init(&x_full[i], 1);
+            mbar_init(&a_full[i], kDeqWarps);
             mbar_init(&mma_done[i], 1);
         }
         fence_mbar_init();
         // static weights: first two super-blocks before the dependency on the previous kernel
         for (int s = 0; s < 2 && s < nsb; ++s) {
-            const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
-            mbar_arrive_expect_tx(&raw_full[s], bytes);
+            mbar_arrive_expect_tx(&raw_full[s], raw_bytes);
             tma_load_2d(raw_ptr + s * kRawBytes, &p.wmap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
             if (swiglu)
                 tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
@@ -185,50 +197,56 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
-
     pdl_wait();
     pdl_trigger();
-    if (tid == 0) {
-        for (int c = 0; c < kNB - 1 && c < nch; ++c) {
-            mbar_arrive_expect_tx(&x_full[c], static_cast<uint32_t>(xbytes));
-            tma_load_2d(smem + (x_base - a_base) + c * xbytes, &p.xmap, (kc0 + c) * kKC, static_cast<int>(m0),
-                        &x_full[c]);
-        }
-    }
-    const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(mt >> 3) << 17) | (static_cast<uint32_t>(kRowsT >> 4) << 24);
 
-    for (int kc = 0; kc < nch; ++kc) {
-        const int sb = kc >> 2, q = kc & 3, b = kc % kNB;
-        if (q == 0 && !failed) {
-            if (!mbar_wait(&raw_full[sb & 1], static_cast<uint32_t>((sb >> 1) & 1))) failed = 1;
-        }
-        if (kc >= kNB && !failed) {
-            if (!mbar_wait(&mma_done[b], static_cast<uint32_t>(((kc - kNB) / kNB) & 1))) failed = 1;
-        }
-        __syncthreads();
-        if (failed) break;
-        const uint32_t raw_row = smem_u32(raw_ptr) + static_cast<uint32_t>((sb & 1) * kRawBytes + tid * 144);
-        dequant_quarter(raw_row, q, a_base + static_cast<uint32_t>(b * kABytes + tid * 128), tid);
-        if (swiglu) {
-            const uint32_t up_row = smem_u32(rawup_ptr) + static_cast<uint32_t>((sb & 1) * kRawBytes + tid * 144);
-            dequant_quarter(up_row, q, aup_base + static_cast<uint32_t>(b * kABytes + tid * 128), tid);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            if (q == 3 && sb + 2 < nsb) {
-                // every thread has read this raw stage: refill it with super-block sb + 2
-                const uint32_t bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
-                mbar_arrive_expect_tx(&raw_full[sb & 1], bytes);
-                tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
-                            &raw_full[sb & 1]);
-                if (swiglu)
-                    tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
-                                &raw_full[sb & 1]);
+    if (warp == kProducer) {
+        if (lane == 0) {
+            for (int c = 0; c < kNB - 1 && c < nch; ++c) {
+                mbar_arrive_expect_tx(&x_full[c], static_cast<uint32_t>(xbytes));
+                tma_load_2d(x_ptr + c * xbytes, &p.xmap, (kc0 + c) * kKC, static_cast<int>(m0), &x_full[c]);
             }
-            if (!mbar_wait(&x_full[b], static_cast<uint32_t>((kc / kNB) & 1))) {
-                failed = 1;
-            } else {
+            for (int kc = 0; kc < nch && !failed; ++kc) {
+                // x of chunk kc + kNB - 1 goes into the buffer of chunk kc - 1 once its MMAs are done
+                const int nx = kc + kNB - 1;
+                if (nx < nch) {
+                    const int bx = nx % kNB;
+                    if (kc >= 1 && !mbar_wait(&mma_done[bx], static_cast<uint32_t>(((kc - 1) / kNB) & 1))) {
+                        failed = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&x_full[bx], static_cast<uint32_t>(xbytes));
+                    tma_load_2d(x_ptr + bx * xbytes, &p.xmap, (kc0 + nx) * kKC, static_cast<int>(m0), &x_full[bx]);
+                }
+                // raw stage of super-block sb is free after its last quarter: load sb + 2
+                if ((kc & 3) == 3) {
+                    const int sb = kc >> 2;
+                    if (sb + 2 < nsb) {
+                        if (!mbar_wait(&raw_empty[sb & 1], static_cast<uint32_t>((sb >> 1) & 1))) {
+                            failed = 1;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&raw_full[sb & 1], raw_bytes);
+                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
+                                    &raw_full[sb & 1]);
+                        if (swiglu)
+                            tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36,
+                                        static_cast<int>(n0), &raw_full[sb & 1]);
+                    }
+                }
+            }
+        }
+    } else if (warp == kIssuer) {
+        if (lane == 0) {
+            const uint32_t idesc =
+                (1u << 4) | (static_cast<uint32_t>(mt >> 3) << 17) | (static_cast<uint32_t>(kRowsT >> 4) << 24);
+            for (int kc = 0; kc < nch && !failed; ++kc) {
+                const int b = kc % kNB;
+                const uint32_t ph = static_cast<uint32_t>((kc / kNB) & 1);
+                if (!mbar_wait(&a_full[b], ph) || !mbar_wait(&x_full[b], ph)) {
+                    failed = 1;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t xa = x_base + static_cast<uint32_t>(b * xbytes);
                 const uint32_t aa = a_base + static_cast<uint32_t>(b * kABytes);
@@ -243,75 +261,129 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                                  idesc, kc > 0 || s > 0);
                 }
                 umma_commit(&mma_done[b]);
-                // x for chunk kc + 2 goes into the buffer of chunk kc - 1 once its MMAs are done
-                const int nx = kc + kNB - 1;
-                if (nx < nch) {
-                    const int bx = nx % kNB;
-                    if (kc >= 1 && !mbar_wait(&mma_done[bx], static_cast<uint32_t>(((kc - 1) / kNB) & 1))) {
-                        failed = 1;
-                    } else {
-                        mbar_arrive_expect_tx(&x_full[bx], static_cast<uint32_t>(xbytes));
-                        tma_load_2d(smem + (x_base - a_base) + bx * xbytes, &p.xmap, (kc0 + nx) * kKC,
-                                    static_cast<int>(m0), &x_full[bx]);
-                    }
-                }
+            }
+        }
+    } else {
+        // dequantization warps
+        const int r = tid & (kRowsT - 1), hf = tid >> 7;
+        for (int kc = 0; kc < nch; ++kc) {
+            const int sb = kc >> 2, q = kc & 3, b = kc % kNB;
+            bool ok = true;
+            if (q == 0) ok = mbar_wait(&raw_full[sb & 1], static_cast<uint32_t>((sb >> 1) & 1));
+            if (ok && kc >= kNB) ok = mbar_wait(&mma_done[b], static_cast<uint32_t>(((kc - kNB) / kNB) & 1));
+            if (!ok || failed) {
+                failed = 1;
+                break;
+            }
+            dequant_half(raw_ptr + (sb & 1) * kRawBytes + r * 144, q, hf,
+                         a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
+            if (swiglu)
+                dequant_half(rawup_ptr + (sb & 1) * kRawBytes + r * 144, q, hf,
+                             aup_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[b]);
+                if (q == 3) mbar_arrive(&raw_empty[sb & 1]);
             }
         }
     }
     __syncthreads();
     bool ok = !failed;
-    if (ok) ok = mbar_wait(&mma_done[(nch - 1) % kNB], static_cast<uint32_t>(((nch - 1) / kNB) & 1));
+    if (ok && nch > 0) ok = mbar_wait(&mma_done[(nch - 1) % kNB], static_cast<uint32_t>(((nch - 1) / kNB) & 1));
     if (!ok && tid == 0) report_device_error(T2C_ETIMEOUT);
-    const int64_t n = n0 + 32 * warp + lane;  // TMEM lane quadrant of warp w: weight rows 32w..32w+31
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-    if (p.ksplit > 1) {
-        // cluster split-K: every CTA parks its fp32 partials column-major in its own
-        // shared memory (reusing the A buffers), the leader sums them over DSMEM
-        float *red = reinterpret_cast<float *>(smem);
-        const int ncols = (swiglu ? 2 : 1) * mt;
-        if (ok) {
-            tc_fence_after();
-            for (int c = 0; c < ncols; c += 16) {
-                uint32_t v[16];
-                tmem_ld16(lane_addr + static_cast<uint32_t>(c), v);
+    if (warp < kDeqWarps) {
+        // TMEM lane quadrant of warp w: weight rows 32 (w % 4) ..; warps 0..3 / 4..7 split the columns
+        const int quad = warp & 3;
+        const int64_t n = n0 + 32 * quad + lane;
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+        const bool split_cols = (mt % 32) == 0;
+        const int c_begin = split_cols ? (warp >> 2) * (mt / 2) : 0;
+        const int c_end = split_cols ? c_begin + mt / 2 : (warp < 4 ? mt : 0);
+        if (p.ksplit > 1) {
+            // cluster split-K: every CTA parks its fp32 partials column-major in its own
+            // shared memory (reusing the A buffers), the leader sums them over DSMEM
+            float *red = reinterpret_cast<float *>(smem);
+            const int row = 32 * quad + lane;
+            if (ok) {
+                tc_fence_after();
+                for (int c = c_begin; c < c_end; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(lane_addr + static_cast<uint32_t>(c), v);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) red[(c + j) * kRowsT + tid] = __uint_as_float(v[j]);
+                    for (int j = 0; j < 16; ++j) red[(c + j) * kRowsT + row] = __uint_as_float(v[j]);
+                    if (swiglu) {
+                        tmem_ld16(lane_addr + static_cast<uint32_t>(mt + c), v);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) red[(mt + c + j) * kRowsT + row] = __uint_as_float(v[j]);
+                    }
+                }
+            } else {
+                for (int c = c_begin; c < c_end; ++c) {
+                    red[c * kRowsT + row] = 0.0f;
+                    if (swiglu) red[(mt + c) * kRowsT + row] = 0.0f;
+                }
             }
-        } else {
-            for (int c = 0; c < ncols; ++c) red[c * kRowsT + tid] = 0.0f;
+        } else if (ok) {
+            tc_fence_after();
+            for (int c = c_begin; c < c_end; c += 16) {
+                uint32_t g[16], u[16];
+                tmem_ld16(lane_addr + static_cast<uint32_t>(c), g);
+                if (swiglu) tmem_ld16(lane_addr + static_cast<uint32_t>(mt + c), u);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t m = m0 + c + j;
+                    if (m < p.M && n < p.N) {
+                        const int64_t o = m * p.N + n;
+                        float v = __uint_as_float(g[j]);
+                        if (swiglu) {
+                            v = v / (1.0f + __expf(-v)) * __uint_as_float(u[j]);
+                        } else if (p.res != nullptr) {
+                            v += __half2float(p.res[o]);
+                        }
+                        p.y[o] = __float2half_rn(v);
+                    }
+                }
+            }
         }
+    }
+    if (p.ksplit > 1) {
         asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-        if (kpart == 0) {
+        if (kpart == 0 && warp < kDeqWarps) {
+            const int row = tid & (kRowsT - 1);
+            const int64_t n = n0 + row;
+            float *red = reinterpret_cast<float *>(smem);
             uint32_t base[8];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                base[r] = 0;
-                if (r < p.ksplit)
+            for (int rk = 0; rk < 8; ++rk) {
+                base[rk] = 0;
+                if (rk < p.ksplit)
                     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                                 : "=r"(base[r])
-                                 : "r"(smem_u32(red) + static_cast<uint32_t>(tid * 4)), "r"(r));
+                                 : "=r"(base[rk])
+                                 : "r"(smem_u32(red) + static_cast<uint32_t>(row * 4)), "r"(rk));
             }
-            for (int c = 0; c < mt; ++c) {
+            // threads 0..127 and 128..255 take alternate columns
+            for (int c = tid >> 7; c < mt; c += 2) {
                 float gv[8], uv[8];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    gv[r] = 0.0f;
-                    uv[r] = 0.0f;
-                    if (r < p.ksplit) {
+                for (int rk = 0; rk < 8; ++rk) {
+                    gv[rk] = 0.0f;
+                    uv[rk] = 0.0f;
+                    if (rk < p.ksplit) {
                         asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                                     : "=f"(gv[r])
-                                     : "r"(base[r] + static_cast<uint32_t>(c * kRowsT * 4)));
+                                     : "=f"(gv[rk])
+                                     : "r"(base[rk] + static_cast<uint32_t>(c * kRowsT * 4)));
                         if (swiglu)
                             asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                                         : "=f"(uv[r])
-                                         : "r"(base[r] + static_cast<uint32_t>((mt + c) * kRowsT * 4)));
+                                         : "=f"(uv[rk])
+                                         : "r"(base[rk] + static_cast<uint32_t>((mt + c) * kRowsT * 4)));
                     }
                 }
                 float g = 0.0f, u = 0.0f;
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    g += gv[r];
-                    u += uv[r];
+                for (int rk = 0; rk < 8; ++rk) {
+                    g += gv[rk];
+                    u += uv[rk];
                 }
                 const int64_t m = m0 + c;
                 if (ok && m < p.M && n < p.N) {
@@ -328,27 +400,6 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
         }
         // partners keep their shared memory until the leader has read it
         asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    } else if (ok) {
-        tc_fence_after();
-        for (int c = 0; c < mt; c += 16) {
-            uint32_t g[16], u[16];
-            tmem_ld16(lane_addr + static_cast<uint32_t>(c), g);
-            if (swiglu) tmem_ld16(lane_addr + static_cast<uint32_t>(mt + c), u);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int64_t m = m0 + c + j;
-                if (m < p.M && n < p.N) {
-                    const int64_t o = m * p.N + n;
-                    float v = __uint_as_float(g[j]);
-                    if (swiglu) {
-                        v = v / (1.0f + __expf(-v)) * __uint_as_float(u[j]);
-                    } else if (p.res != nullptr) {
-                        v += __half2float(p.res[o]);
-                    }
-                    p.y[o] = __float2half_rn(v);
-                }
-            }
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -428,7 +479,7 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     p.tmem_cols = cols;
     const size_t smem = 1024 + static_cast<size_t>(kNB) * kABytes * (p.swiglu ? 2 : 1) +
                         static_cast<size_t>(kNB) * p.mt * 128 + 2 * static_cast<size_t>(kRawBytes) * (p.swiglu ? 2 : 1) +
-                        (2 + 2 * kNB) * 8 + 16;
+                        (4 + 3 * kNB) * 8 + 16;
     constexpr size_t kLimit = 226 * 1024;  // dynamic bytes; the kernel's static words sit beside them
     if (smem > kLimit) return T2C_EUNSUPPORTED;
     static bool configured[64] = {false};
