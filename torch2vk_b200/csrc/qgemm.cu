@@ -44,12 +44,15 @@ constexpr int kProducer = 9;                // warp that issues the TMA copies
 constexpr int kThreadsG = 32 * (kDeqWarps + 2);
 
 struct GemmParams {
-    alignas(64) CUtensorMap wmap;  // raw Q4_K words [N, row_bytes / 4], box 36 x 128
-    alignas(64) CUtensorMap umap;  // up weight (SwiGLU)
-    alignas(64) CUtensorMap xmap;  // x fp16 [M, K], box 64 x mt, 128-byte swizzle
-    __half *y;
-    const __half *res;
-    int64_t N, M;
+    alignas(64) CUtensorMap wmap[3];  // raw Q4_K words [N, row_bytes / 4], box 36 x 128, per weight
+    alignas(64) CUtensorMap umap;     // up weight (SwiGLU)
+    alignas(64) CUtensorMap xmap;     // x fp16 [M, K], box 64 x mt, 128-byte swizzle
+    __half *y[3];
+    const __half *res[3];
+    int64_t Nw[3];
+    int tile0[4];                     // first row tile of each weight (tile0[nw] = all row tiles)
+    int nw;
+    int64_t M;
     int K, mt, swiglu, tmem_cols;
     int ksplit;  // CTAs of a cluster splitting K (1: no split)
 };
@@ -90,7 +93,19 @@ __device__ __forceinline__ float small_u2f_g(uint32_t v) { return __uint_as_floa
 // One sub-block half of a 64-value chunk: row r of quarter q of a 144-byte
 // Q4_K block, nibble half hf (0: low nibbles = values 0..31 of the chunk,
 // sub-block 2q; 1: high nibbles = values 32..63, sub-block 2q + 1) -> four
-// swizzled 16-byte chunks (4 hf .. 4 hf + 3) of fp16 d*sc*q - dmin*m.
+// swizzled 16-byte chunks (4 hf .. 4 hf + 3) of fp16 d * (sc q) - dmin m.
+// Two nibbles at a time become the fp16 pair 1024 + q (byte_perm into
+// 0x64xx); one paired fma gives sc q exactly (an integer <= 945), a second
+// one d * (sc q) - dmin m with the fp16 super-block scale d, so the only
+// roundings are that of dmin m (formed in fp32) and the final one.
+__device__ __forceinline__ uint32_t nib_pair(uint32_t src, uint32_t sel, __half2 sc2, __half2 nb2, __half2 d2,
+                                             __half2 ndm2) {
+    const uint32_t u = __byte_perm(src, 0x64646464u, sel);
+    const __half2 qs = __hfma2(*reinterpret_cast<const __half2 *>(&u), sc2, nb2);
+    const __half2 v = __hfma2(d2, qs, ndm2);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
 __device__ __forceinline__ void dequant_half(const uint8_t *raw_row, int q, int hf, uint32_t a_row, int r) {
     const uint4 h = *reinterpret_cast<const uint4 *>(raw_row);
     const uint4 n0 = *reinterpret_cast<const uint4 *>(raw_row + 16 + 32 * q);
@@ -100,28 +115,21 @@ __device__ __forceinline__ void dequant_half(const uint8_t *raw_row, int q, int 
     const uint32_t y = (h.y >> (8 * jb)) & 0xffu, z = (h.z >> (8 * jb)) & 0xffu, w = (h.w >> (8 * jb)) & 0xffu;
     const uint32_t sc = j < 4 ? (y & 63u) : ((w & 15u) | ((y >> 6) << 4));
     const uint32_t mn = j < 4 ? (z & 63u) : ((w >> 4) | ((z >> 6) << 4));
-    const float ds = half_bits_to_float(h.x) * small_u2f_g(sc);
-    const float dm = half_bits_to_float(h.x >> 16) * small_u2f_g(mn);
+    const float scf = small_u2f_g(sc);
+    const __half2 sc2 = __float2half2_rn(scf), nb2 = __float2half2_rn(-1024.0f * scf);
+    const uint32_t dbits = (h.x & 0xffffu) * 0x10001u;
+    const __half2 d2 = *reinterpret_cast<const __half2 *>(&dbits);
+    const __half2 ndm2 = __float2half2_rn(-(half_bits_to_float(h.x >> 16) * small_u2f_g(mn)));
     const uint32_t wq[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
     const int sh = 4 * hf;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         // values 8c .. 8c+7 of the sub-block = nibble hf of bytes 8c .. 8c+7 of the quarter
         const uint32_t lo = (wq[2 * c] >> sh) & 0x0F0F0F0Fu, hi = (wq[2 * c + 1] >> sh) & 0x0F0F0F0Fu;
-        uint32_t packed[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const uint32_t src = e < 2 ? lo : hi;
-            const int k0 = 2 * (e & 1);
-            const float v0 = fmaf(ds, __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7440u + k0)) - 8388608.0f, -dm);
-            const float v1 = fmaf(ds, __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7441u + k0)) - 8388608.0f, -dm);
-            const __half2 hv = __floats2half2_rn(v0, v1);
-            packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
-        }
+        const uint32_t p0 = nib_pair(lo, 0x4140u, sc2, nb2, d2, ndm2), p1 = nib_pair(lo, 0x4342u, sc2, nb2, d2, ndm2);
+        const uint32_t p2 = nib_pair(hi, 0x4140u, sc2, nb2, d2, ndm2), p3 = nib_pair(hi, 0x4342u, sc2, nb2, d2, ndm2);
         const uint32_t dst = a_row + static_cast<uint32_t>((((4 * hf + c) ^ (r & 7)) << 4));
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
-                     "r"(packed[2]), "r"(packed[3])
-                     : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(p0), "r"(p1), "r"(p2), "r"(p3) : "memory");
     }
 }
 
@@ -138,7 +146,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
     const int mt = p.mt;
     const bool swiglu = p.swiglu != 0;
     const int kpart = blockIdx.x % p.ksplit;  // rank in the cluster
-    const int64_t n0 = static_cast<int64_t>(blockIdx.x / p.ksplit) * kRowsT;
+    // row tile -> weight (fused QKV: consecutive tile ranges of the three weights)
+    const int tile = static_cast<int>(blockIdx.x / p.ksplit);
+    int wi = 0;
+    if (p.nw > 1 && tile >= p.tile0[1]) wi = (p.nw > 2 && tile >= p.tile0[2]) ? 2 : 1;
+    const int64_t n0 = static_cast<int64_t>(tile - p.tile0[wi]) * kRowsT;
+    const CUtensorMap *wmap = &p.wmap[wi];
+    __half *const yout = p.y[wi];
+    const __half *const res = p.res[wi];
+    const int64_t N = p.Nw[wi];
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * mt;
     const int nsb = p.K / 256 / p.ksplit;  // super-blocks of this CTA's K range
     const int sb0 = kpart * nsb;
@@ -182,7 +198,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
         // static weights: first two super-blocks before the dependency on the previous kernel
         for (int s = 0; s < 2 && s < nsb; ++s) {
             mbar_arrive_expect_tx(&raw_full[s], raw_bytes);
-            tma_load_2d(raw_ptr + s * kRawBytes, &p.wmap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
+            tma_load_2d(raw_ptr + s * kRawBytes, wmap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
             if (swiglu)
                 tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
         }
@@ -227,7 +243,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                             break;
                         }
                         mbar_arrive_expect_tx(&raw_full[sb & 1], raw_bytes);
-                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, &p.wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
+                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
                                     &raw_full[sb & 1]);
                         if (swiglu)
                             tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36,
@@ -333,15 +349,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int64_t m = m0 + c + j;
-                    if (m < p.M && n < p.N) {
-                        const int64_t o = m * p.N + n;
+                    if (m < p.M && n < N) {
+                        const int64_t o = m * N + n;
                         float v = __uint_as_float(g[j]);
                         if (swiglu) {
                             v = v / (1.0f + __expf(-v)) * __uint_as_float(u[j]);
-                        } else if (p.res != nullptr) {
-                            v += __half2float(p.res[o]);
+                        } else if (res != nullptr) {
+                            v += __half2float(res[o]);
                         }
-                        p.y[o] = __float2half_rn(v);
+                        yout[o] = __float2half_rn(v);
                     }
                 }
             }
@@ -386,15 +402,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                     u += uv[rk];
                 }
                 const int64_t m = m0 + c;
-                if (ok && m < p.M && n < p.N) {
-                    const int64_t o = m * p.N + n;
+                if (ok && m < p.M && n < N) {
+                    const int64_t o = m * N + n;
                     float v = g;
                     if (swiglu) {
                         v = v / (1.0f + __expf(-v)) * u;
-                    } else if (p.res != nullptr) {
-                        v += __half2float(p.res[o]);
+                    } else if (res != nullptr) {
+                        v += __half2float(res[o]);
                     }
-                    p.y[o] = __float2half_rn(v);
+                    yout[o] = __float2half_rn(v);
                 }
             }
         }
@@ -448,7 +464,10 @@ bool encode_x(CUtensorMap *map, const __half *x, int64_t m, int64_t k, int mt) {
 }  // namespace
 
 int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
-    if (a.M <= 4 || a.K % 256 || a.K > 65536 || a.N <= 0 || a.N > INT32_MAX || a.M > INT32_MAX) return T2C_EUNSUPPORTED;
+    if (a.M <= 4 || a.K % 256 || a.K > 65536 || a.M > INT32_MAX || a.nw < 1 || a.nw > 3 || (a.w_up && a.nw != 1))
+        return T2C_EUNSUPPORTED;
+    for (int i = 0; i < a.nw; ++i)
+        if (a.N[i] <= 0 || a.N[i] > INT32_MAX) return T2C_EUNSUPPORTED;
     GemmParams p = {};
     p.swiglu = a.w_up != nullptr;
     const int cap = p.swiglu ? 128 : 256;
@@ -456,13 +475,21 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     if (mt > cap) mt = cap;
     p.mt = static_cast<int>(mt);
     const int64_t row_bytes = a.K / 256 * 144;
-    if (!encode_raw(&p.wmap, a.w, a.N, row_bytes)) return T2C_EUNSUPPORTED;
-    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N, row_bytes)) return T2C_EUNSUPPORTED;
+    p.nw = a.nw;
+    int64_t row_tiles = 0;
+    for (int i = 0; i < a.nw; ++i) {
+        if (!encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes)) return T2C_EUNSUPPORTED;
+        p.tile0[i] = static_cast<int>(row_tiles);
+        row_tiles += (a.N[i] + kRowsT - 1) / kRowsT;
+        p.Nw[i] = a.N[i];
+        p.y[i] = a.y[i];
+        p.res[i] = a.res[i];
+    }
+    p.tile0[a.nw] = static_cast<int>(row_tiles);
+    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N[0], row_bytes)) return T2C_EUNSUPPORTED;
     if (!encode_x(&p.xmap, a.x, a.M, a.K, p.mt)) return T2C_EUNSUPPORTED;
-    p.y = a.y;
-    p.res = a.res;
     // split K over a cluster when there are too few (row tile, token tile) pairs to fill the GPU
-    const int64_t tiles = (a.N + kRowsT - 1) / kRowsT * ((a.M + p.mt - 1) / p.mt);
+    const int64_t tiles = row_tiles * ((a.M + p.mt - 1) / p.mt);
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
     p.ksplit = 1;
@@ -471,7 +498,6 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
         while (p.ksplit < 8 && tiles * p.ksplit < sms && nsb_all % (p.ksplit * 2) == 0 && nsb_all / (p.ksplit * 2) >= 2)
             p.ksplit *= 2;
     }
-    p.N = a.N;
     p.M = a.M;
     p.K = static_cast<int>(a.K);
     int cols = 32;
@@ -493,7 +519,7 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
         configured[slot] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((a.N + kRowsT - 1) / kRowsT * p.ksplit),
+    cfg.gridDim = dim3(static_cast<unsigned>(row_tiles * p.ksplit),
                        static_cast<unsigned>((a.M + p.mt - 1) / p.mt));
     cfg.blockDim = dim3(kThreadsG);
     cfg.dynamicSmemBytes = smem;

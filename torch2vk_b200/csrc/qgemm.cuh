@@ -11,12 +11,13 @@
 namespace t2c {
 
 struct QGemmArgs {
-    const uint8_t *w;      // Q4_K rows (row_bytes = K / 256 * 144), 16-byte aligned
-    const uint8_t *w_up;   // SwiGLU: the up weight (same shape), else nullptr
-    int64_t N, K, M;
+    int nw;                // weights sharing x (1..3: fused QKV), 1 with SwiGLU
+    const uint8_t *w[3];   // Q4_K rows (row_bytes = K / 256 * 144), 16-byte aligned
+    const uint8_t *w_up;   // SwiGLU: the up weight (same shape as w[0]), else nullptr
+    int64_t N[3], K, M;
     const __half *x;       // [M, K], 16-byte aligned rows
-    __half *y;             // [M, N]
-    const __half *res;     // [M, N] or nullptr
+    __half *y[3];          // [M, N[i]]
+    const __half *res[3];  // [M, N[i]] or nullptr
 };
 
 // Returns T2C_OK, or T2C_EUNSUPPORTED when the shape is not served (caller falls back).

@@ -2153,27 +2153,25 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     a.M = M;
     a.x = p.x;
     if (p.mode == MODE_SWIGLU) {
-        a.w = p.s[0].w;
+        a.nw = 1;
+        a.w[0] = p.s[0].w;
         a.w_up = p.s[1].w;
-        a.N = p.s[0].n;
-        a.y = p.s[0].y;
-        const int rc = qgemm_q4k(a, stream);
-        if (rc == T2C_EUNSUPPORTED) return T2C_OK;
-        used = true;
-        return rc;
+        a.N[0] = p.s[0].n;
+        a.y[0] = p.s[0].y;
+    } else {
+        // all weights of a fused QKV in one launch
+        a.nw = p.nstreams;
+        for (int i = 0; i < p.nstreams; ++i) {
+            a.w[i] = p.s[i].w;
+            a.N[i] = p.s[i].n;
+            a.y[i] = p.s[i].y;
+            a.res[i] = p.s[i].res;
+        }
     }
-    for (int i = 0; i < p.nstreams; ++i) {
-        a.w = p.s[i].w;
-        a.w_up = nullptr;
-        a.N = p.s[i].n;
-        a.y = p.s[i].y;
-        a.res = p.s[i].res;
-        const int rc = qgemm_q4k(a, stream);
-        if (rc == T2C_EUNSUPPORTED && i == 0) return T2C_OK;  // nothing launched yet: fall back
-        if (rc != T2C_OK) return rc == T2C_EUNSUPPORTED ? set_error(T2C_EUNSUPPORTED, "qgemm: stream %d", i) : rc;
-    }
+    const int rc = qgemm_q4k(a, stream);
+    if (rc == T2C_EUNSUPPORTED) return T2C_OK;  // nothing launched: the matvec kernels serve this call
     used = true;
-    return T2C_OK;
+    return rc;
 }
 
 int run_linear(QParams p, int64_t M, cudaStream_t stream) {
