@@ -225,7 +225,10 @@ def run_profile(args, local: int) -> None:
     decode32: the same at batch 32 on a synthetic 1024-position KV cache.
     prefill: --steps prefills of the 1024-token prompt (batch 1).
     attn:   the fused decode attention of Qwen3-8B (32 Q / 8 KV heads, D 128) at position 1040 over
-            48 layers' KV caches in turn (288 MB, larger than L2), --steps launches.
+            48 layers' KV caches in turn (288 MB, larger than L2), 8 splits per KV head (one
+            thread-block cluster, as the decode runner uses), --steps launches.
+    gemm:   the prefill gate/up + SwiGLU GEMM (Q4_K 2 x 12288 x 4096, 1024 tokens) over 4 layers'
+            weights in turn (226 MB), --steps launches.
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
             in turn (226 MB, larger than L2), --steps launches.
     """
@@ -278,7 +281,7 @@ def run_profile(args, local: int) -> None:
 
         inv = inv_freq(cfg).to(dev)
         pos = torch.full((B,), 1040, device=dev, dtype=torch.int32)
-        splits = max(1, min(32, (PROMPT + 400 + 10 + 64) // 64))
+        splits = 8
         ws = kernels.attn_decode_fused_workspace(B, NH, NK, D, splits, dev)
         out = torch.empty(B, NH * D, device=dev, dtype=torch.float16)
 
@@ -293,6 +296,25 @@ def run_profile(args, local: int) -> None:
         cudart.cudaProfilerStart()
         for i in range(args.steps):
             one(i)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "gemm":
+        gen = torch.Generator(device=dev).manual_seed(0)
+        pairs = []
+        for _ in range(4):
+            g = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
+            u = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
+            pairs.append((g, u))
+        x = torch.randn(PROMPT, cfg.hidden, device=dev, dtype=torch.float16)
+        out = torch.empty(PROMPT, cfg.intermediate, device=dev, dtype=torch.float16)
+        for i in range(args.warmup):
+            g, u = pairs[i % 4]
+            kernels.linear_swiglu(x, g, u, "q4_k", cfg.hidden, out=out)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for i in range(args.steps):
+            g, u = pairs[i % 4]
+            kernels.linear_swiglu(x, g, u, "q4_k", cfg.hidden, out=out)
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
     else:
@@ -326,7 +348,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn"], default=None,
+    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "gemm"], default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     args = ap.parse_args()
     if args.warmup < 3:
