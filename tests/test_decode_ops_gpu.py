@@ -179,6 +179,39 @@ def test_lm_head_argmax_and_select(oracle, kind, K, N):
     assert int(nxt[0]) == int(nxt[1]) and int(done[0]) == 1 and int(done[1]) == 1
 
 
+@pytest.mark.parametrize("kind,K,N,M", [("q6_k", 4096, 4099, 8), ("q6_k", 4096, 8192, 32), ("q4_k", 4096, 4099, 20),
+                                        ("q6_k", 2048, 1000, 5)])
+def test_lm_head_argmax_tensor_core(oracle, kind, K, N, M):
+    """M > 4: the LM head runs on the tcgen05 GEMM (fp16 operands) with the argmax epilogue.
+
+    Scores are fp16-operand dot products: each partial may differ from the double-precision oracle by
+    4e-3 relative (the tensor-core GEMM bound), and a group's reported row must be the oracle's argmax
+    unless the two best rows of the group are that close."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(6)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    w[777 % N] = w[123]
+    packed = oracle.quantize(w, kind)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    nw = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    xf = x.astype(np.float64)
+    xn = (xf / np.sqrt(np.mean(xf * xf, axis=1, keepdims=True) + 1e-6) * nw).astype(np.float16)
+    logits = oracle.matvec(packed, kind, xn)
+    ps, pt = kernels.lm_head_argmax(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), kind, K,
+                                    norm_weight=torch.from_numpy(nw).cuda())
+    ps_c, pt_c = ps.cpu().numpy(), pt.cpu().numpy()
+    scale = float(np.sqrt(np.mean(logits.astype(np.float64) ** 2)))
+    for m in range(M):
+        for g in range(ps_c.shape[1]):
+            rows = logits[m, 4 * g:4 * g + 4]
+            tol = 4e-3 * (abs(float(rows.max())) + scale)
+            assert abs(float(ps_c[m, g]) - float(rows.max())) <= tol
+            best = int(np.argmax(rows))
+            assert pt_c[m, g] == 4 * g + best or float(rows.max()) - float(rows[pt_c[m, g] - 4 * g]) <= 2 * tol
+    assert kernels.device_status() == 0
+
+
 def test_token_select_tie_breaks_to_lower_id():
     from torch2vk_b200 import kernels
 

@@ -1,4 +1,4 @@
-// Q4_K GEMM on tcgen05 tensor cores with TMEM accumulators (M > 4 tokens:
+// Q4_K / Q6_K GEMM on tcgen05 tensor cores with TMEM accumulators (M > 4 tokens:
 // prefill, batched decode).  The weights are the A operand: a CTA owns 128
 // weight rows (UMMA M = 128) and mt tokens (UMMA N = mt, <= 256), so
 //   D[n, m] = sum_k deq(W)[n, k] * x[m, k]     (fp32 in TMEM, 128 lanes x mt columns)
@@ -36,7 +36,25 @@ namespace {
 constexpr int kRowsT = 128;                 // weight rows per CTA (UMMA M)
 constexpr int kKC = 64;                     // values per K chunk
 constexpr int kNB = 3;                      // A / x buffers
-constexpr int kRawBytes = kRowsT * 144;     // one super-block of 128 rows
+// Raw weight stage = one 256-value block of 128 rows.  Q4_K: 144-byte blocks,
+// box 36 u32.  Q6_K: 210-byte blocks start at even, not 16-byte aligned,
+// offsets, so the box is the 224-byte window from the 16-byte boundary at or
+// below the block start (the block sits at offset (210 b) % 16 in it).
+template <int FMT>
+struct RawFmt;
+template <>
+struct RawFmt<T2C_Q4_K> {
+    static constexpr int kRow = 144, kBox = 36;
+    __device__ static int x_of(int b) { return b * 36; }
+    __device__ static int off_of(int) { return 0; }
+};
+template <>
+struct RawFmt<T2C_Q6_K> {
+    static constexpr int kRow = 224, kBox = 56;
+    __device__ static int x_of(int b) { return ((210 * b) >> 4) * 4; }
+    __device__ static int off_of(int b) { return (210 * b) & 15; }
+};
+constexpr int kRawBytesMax = kRowsT * 224;
 constexpr int kABytes = kRowsT * kKC * 2;   // 16 KB of fp16
 constexpr int kDeqWarps = 8;                // dequantization warps (2 threads per weight row)
 constexpr int kIssuer = 8;                  // warp that issues the tcgen05 MMAs
@@ -55,6 +73,9 @@ struct GemmParams {
     int64_t M;
     int K, mt, swiglu, tmem_cols;
     int ksplit;  // CTAs of a cluster splitting K (1: no split)
+    float *ps;   // argmax mode: best (score, row) per group of 4 rows, [M, G]
+    uint32_t *pt;
+    int64_t G;
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -133,12 +154,86 @@ __device__ __forceinline__ void dequant_half(const uint8_t *raw_row, int q, int 
     }
 }
 
+// 4 bytes at a 2-byte aligned shared address a, as aligned words w[i] = bytes a + 4 i .. (i < n).
+template <int N>
+__device__ __forceinline__ void lds_words_a2(uint32_t a, uint32_t w[N]) {
+    const uint32_t base = a & ~3u, sh = (a & 3u) * 8u;
+    uint32_t r[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; ++i) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r[i]) : "r"(base + 4 * i));
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
+}
+
+// Q6_K: chunk ch (values 64 ch .. 64 ch + 63) of the 210-byte block at shared
+// address blk (2-byte aligned), half hf -> four swizzled 16-byte chunks of
+// fp16 (d * sc) * (q - 32), formed in fp32 as the reference decoder does
+// (linear_nobias_q6_k_matvec_f32.py:116-156): value l of group c = 2 (ch & 1)
+// + hf of half-block s = ch >> 1 has its low 4 bits in nibble (ch & 1) of
+// ql[64 s + 32 hf + l], its high 2 bits at bit 2c of qh[32 s + l], and scale
+// sc[8 s + 2 c + l / 16].
+__device__ __forceinline__ void dequant_q6k_half(uint32_t blk, int ch, int hf, uint32_t a_row, int r) {
+    const int s = ch >> 1, c = 2 * (ch & 1) + hf;
+    uint32_t ql[8], qh[8], sw[1], dw[1];
+    lds_words_a2<8>(blk + 64 * s + 32 * hf, ql);
+    lds_words_a2<8>(blk + 128 + 32 * s, qh);
+    lds_words_a2<1>(blk + 192 + 8 * s + 2 * c, sw);
+    lds_words_a2<1>(blk + 208, dw);
+    const float d = half_bits_to_float(dw[0]);
+    const float ds0 = d * static_cast<float>(static_cast<int8_t>(sw[0] & 0xffu));
+    const float ds1 = d * static_cast<float>(static_cast<int8_t>((sw[0] >> 8) & 0xffu));
+    const int nsh = 4 * (ch & 1), hsh = 2 * c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float ds = j < 2 ? ds0 : ds1;
+        uint32_t packed[4];
+#pragma unroll
+        for (int wi = 0; wi < 2; ++wi) {
+            const uint32_t qv = ((ql[2 * j + wi] >> nsh) & 0x0F0F0F0Fu) | (((qh[2 * j + wi] >> hsh) & 0x03030303u) << 4);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float v0 = ds * (__uint_as_float(__byte_perm(qv, 0x4B000000u, 0x7440u + 2 * e)) - 8388640.0f);
+                const float v1 = ds * (__uint_as_float(__byte_perm(qv, 0x4B000000u, 0x7441u + 2 * e)) - 8388640.0f);
+                const __half2 hv = __floats2half2_rn(v0, v1);
+                packed[2 * wi + e] = *reinterpret_cast<const uint32_t *>(&hv);
+            }
+        }
+        const uint32_t dst = a_row + static_cast<uint32_t>((((4 * hf + j) ^ (r & 7)) << 4));
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
+                     "r"(packed[2]), "r"(packed[3])
+                     : "memory");
+    }
+}
+
+// Argmax epilogue: for token m, the best (value, row) of each group of 4 rows
+// (four consecutive lanes; ties keep the lower row) -> ps / pt[m, n / 4].
+__device__ __forceinline__ void argmax4_store(const GemmParams &p, int64_t m, int64_t n, int64_t N, float v, bool ok) {
+    float best = (n < N && ok) ? v : -INFINITY;
+    uint32_t tok = static_cast<uint32_t>(n);
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t ot = __shfl_xor_sync(0xffffffffu, tok, o);
+        if (ob > best || (ob == best && ot < tok)) {
+            best = ob;
+            tok = ot;
+        }
+    }
+    if ((n & 3) == 0 && n < N && m < p.M) {
+        p.ps[m * p.G + (n >> 2)] = best;
+        p.pt[m * p.G + (n >> 2)] = tok;
+    }
+}
+
 // Warp roles: warps 0..7 dequantize (thread = weight row tid % 128, nibble
 // half tid / 128), warp 8 issues the MMAs, warp 9 issues the TMA copies.
 // They meet only at mbarriers: raw_full / raw_empty (raw weight stages),
 // x_full (x chunks), a_full (dequantized A buffers, one arrival per dequant
 // warp) and mma_done (tcgen05.commit: A / x buffer free again).
-__global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_constant__ GemmParams p) {
+template <int FMT>
+__global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
+    using RF = RawFmt<FMT>;
+    constexpr int kRawBytes = kRowsT * RF::kRow;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -198,7 +293,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
         // static weights: first two super-blocks before the dependency on the previous kernel
         for (int s = 0; s < 2 && s < nsb; ++s) {
             mbar_arrive_expect_tx(&raw_full[s], raw_bytes);
-            tma_load_2d(raw_ptr + s * kRawBytes, wmap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
+            tma_load_2d(raw_ptr + s * kRawBytes, wmap, RF::x_of(sb0 + s), static_cast<int>(n0), &raw_full[s]);
             if (swiglu)
                 tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
         }
@@ -243,7 +338,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                             break;
                         }
                         mbar_arrive_expect_tx(&raw_full[sb & 1], raw_bytes);
-                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, wmap, (sb0 + sb + 2) * 36, static_cast<int>(n0),
+                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, wmap, RF::x_of(sb0 + sb + 2), static_cast<int>(n0),
                                     &raw_full[sb & 1]);
                         if (swiglu)
                             tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36,
@@ -291,9 +386,14 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                 failed = 1;
                 break;
             }
+            if (FMT == T2C_Q6_K) {
+                dequant_q6k_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + r * RF::kRow) + RF::off_of(sb0 + sb), q, hf,
+                                 a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
+            } else {
             dequant_half(raw_ptr + (sb & 1) * kRawBytes + r * 144, q, hf,
                          a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
-            if (swiglu)
+            }
+            if (FMT == T2C_Q4_K && swiglu)
                 dequant_half(rawup_ptr + (sb & 1) * kRawBytes + r * 144, q, hf,
                              aup_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -346,6 +446,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                 uint32_t g[16], u[16];
                 tmem_ld16(lane_addr + static_cast<uint32_t>(c), g);
                 if (swiglu) tmem_ld16(lane_addr + static_cast<uint32_t>(mt + c), u);
+                if (p.ps != nullptr) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) argmax4_store(p, m0 + c + j, n, N, __uint_as_float(g[j]), true);
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int64_t m = m0 + c + j;
@@ -402,6 +507,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_q4k_kernel(const __grid_co
                     u += uv[rk];
                 }
                 const int64_t m = m0 + c;
+                if (p.ps != nullptr) {
+                    argmax4_store(p, m, n, N, g, ok);
+                    continue;
+                }
                 if (ok && m < p.M && n < N) {
                     const int64_t o = m * N + n;
                     float v = g;
@@ -437,12 +546,12 @@ PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
     return encode;
 }
 
-bool encode_raw(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes) {
+bool encode_raw(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes, int box_words) {
     const auto enc = tensor_map_encoder();
     if (!enc || row_bytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(n)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-    const cuuint32_t box[2] = {36, kRowsT};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_words), kRowsT};
     const cuuint32_t es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -463,9 +572,12 @@ bool encode_x(CUtensorMap *map, const __half *x, int64_t m, int64_t k, int mt) {
 
 }  // namespace
 
-int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
+int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     if (a.M <= 4 || a.K % 256 || a.K > 65536 || a.M > INT32_MAX || a.nw < 1 || a.nw > 3 || (a.w_up && a.nw != 1))
         return T2C_EUNSUPPORTED;
+    if (a.fmt != T2C_Q4_K && a.fmt != T2C_Q6_K) return T2C_EUNSUPPORTED;
+    if (a.fmt == T2C_Q6_K && a.w_up) return T2C_EUNSUPPORTED;
+    if (a.ps && (a.nw != 1 || a.w_up || !a.pt)) return T2C_EUNSUPPORTED;
     for (int i = 0; i < a.nw; ++i)
         if (a.N[i] <= 0 || a.N[i] > INT32_MAX) return T2C_EUNSUPPORTED;
     GemmParams p = {};
@@ -474,11 +586,13 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     int64_t mt = (a.M + 15) / 16 * 16;
     if (mt > cap) mt = cap;
     p.mt = static_cast<int>(mt);
-    const int64_t row_bytes = a.K / 256 * 144;
+    const int64_t row_bytes = a.K / 256 * (a.fmt == T2C_Q6_K ? 210 : 144);
+    const int box = a.fmt == T2C_Q6_K ? 56 : 36;
+    const size_t raw_bytes = static_cast<size_t>(kRowsT) * (a.fmt == T2C_Q6_K ? 224 : 144);
     p.nw = a.nw;
     int64_t row_tiles = 0;
     for (int i = 0; i < a.nw; ++i) {
-        if (!encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes)) return T2C_EUNSUPPORTED;
+        if (!encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes, box)) return T2C_EUNSUPPORTED;
         p.tile0[i] = static_cast<int>(row_tiles);
         row_tiles += (a.N[i] + kRowsT - 1) / kRowsT;
         p.Nw[i] = a.N[i];
@@ -486,7 +600,10 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
         p.res[i] = a.res[i];
     }
     p.tile0[a.nw] = static_cast<int>(row_tiles);
-    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N[0], row_bytes)) return T2C_EUNSUPPORTED;
+    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N[0], row_bytes, box)) return T2C_EUNSUPPORTED;
+    p.ps = a.ps;
+    p.pt = a.pt;
+    p.G = a.G;
     if (!encode_x(&p.xmap, a.x, a.M, a.K, p.mt)) return T2C_EUNSUPPORTED;
     // split K over a cluster when there are too few (row tile, token tile) pairs to fill the GPU
     const int64_t tiles = row_tiles * ((a.M + p.mt - 1) / p.mt);
@@ -504,19 +621,22 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     while (cols < (p.swiglu ? 2 : 1) * p.mt) cols *= 2;
     p.tmem_cols = cols;
     const size_t smem = 1024 + static_cast<size_t>(kNB) * kABytes * (p.swiglu ? 2 : 1) +
-                        static_cast<size_t>(kNB) * p.mt * 128 + 2 * static_cast<size_t>(kRawBytes) * (p.swiglu ? 2 : 1) +
+                        static_cast<size_t>(kNB) * p.mt * 128 + 2 * raw_bytes * (p.swiglu ? 2 : 1) +
                         (4 + 3 * kNB) * 8 + 16;
     constexpr size_t kLimit = 226 * 1024;  // dynamic bytes; the kernel's static words sit beside them
     if (smem > kLimit) return T2C_EUNSUPPORTED;
-    static bool configured[64] = {false};
+    static bool configured[2][64] = {};
     int device = 0;
     cudaGetDevice(&device);
     const int slot = device < 0 ? 0 : (device > 63 ? 63 : device);
-    if (!configured[slot]) {
-        if (cudaFuncSetAttribute(qgemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kLimit)) !=
-            cudaSuccess)
-            return set_error(T2C_ECUDA, "qgemm: cudaFuncSetAttribute failed");
-        configured[slot] = true;
+    const int fi = a.fmt == T2C_Q6_K ? 1 : 0;
+    if (!configured[fi][slot]) {
+        const cudaError_t e = fi ? cudaFuncSetAttribute(qgemm_kernel<T2C_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        static_cast<int>(kLimit))
+                                 : cudaFuncSetAttribute(qgemm_kernel<T2C_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        static_cast<int>(kLimit));
+        if (e != cudaSuccess) return set_error(T2C_ECUDA, "qgemm: cudaFuncSetAttribute failed");
+        configured[fi][slot] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(row_tiles * p.ksplit),
@@ -533,7 +653,8 @@ int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, qgemm_q4k_kernel, p);
+    const cudaError_t err = fi ? cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q6_K>, p)
+                               : cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q4_K>, p);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "qgemm launch: %s", cudaGetErrorString(err));
     return T2C_OK;
 }

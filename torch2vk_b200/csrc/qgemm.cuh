@@ -11,6 +11,7 @@
 namespace t2c {
 
 struct QGemmArgs {
+    int fmt;               // T2C_Q4_K or T2C_Q6_K (Q6_K: K a multiple of 2048, no SwiGLU)
     int nw;                // weights sharing x (1..3: fused QKV), 1 with SwiGLU
     const uint8_t *w[3];   // Q4_K rows (row_bytes = K / 256 * 144), 16-byte aligned
     const uint8_t *w_up;   // SwiGLU: the up weight (same shape as w[0]), else nullptr
@@ -18,10 +19,13 @@ struct QGemmArgs {
     const __half *x;       // [M, K], 16-byte aligned rows
     __half *y[3];          // [M, N[i]]
     const __half *res[3];  // [M, N[i]] or nullptr
+    float *ps;             // argmax mode (LM head): best (score, row) per 4 rows [M, G], else nullptr
+    uint32_t *pt;
+    int64_t G;
 };
 
 // Returns T2C_OK, or T2C_EUNSUPPORTED when the shape is not served (caller falls back).
-int qgemm_q4k(const QGemmArgs &a, cudaStream_t stream);
+int qgemm(const QGemmArgs &a, cudaStream_t stream);
 cudaError_t status_qgemm(unsigned int *bits, int clear, cudaStream_t s);
 
 }  // namespace t2c

@@ -2145,20 +2145,31 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
 // M > 4, every stream Q4_K, no fused RMSNorm, not argmax: tcgen05 GEMM per stream.
 int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     used = false;
-    if (mma_disabled() || M <= 4 || p.mode == MODE_ARGMAX || p.norm_w != nullptr) return T2C_OK;
-    for (int i = 0; i < p.nstreams; ++i)
-        if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
+    if (mma_disabled() || M <= 4 || p.norm_w != nullptr) return T2C_OK;
+    const int fmt = p.s[0].fmt;
+    if (fmt != T2C_Q4_K && fmt != T2C_Q6_K) return T2C_OK;
+    bool same = true;
+    for (int i = 1; i < (p.mode == MODE_SWIGLU ? 2 : p.nstreams); ++i) same = same && p.s[i].fmt == fmt;
     QGemmArgs a = {};
+    a.fmt = fmt;
     a.K = p.K;
     a.M = M;
     a.x = p.x;
     if (p.mode == MODE_SWIGLU) {
+        if (!same) return T2C_OK;
         a.nw = 1;
         a.w[0] = p.s[0].w;
         a.w_up = p.s[1].w;
         a.N[0] = p.s[0].n;
         a.y[0] = p.s[0].y;
-    } else {
+    } else if (p.mode == MODE_ARGMAX) {
+        a.nw = 1;
+        a.w[0] = p.s[0].w;
+        a.N[0] = p.s[0].n;
+        a.ps = p.ps;
+        a.pt = p.pt;
+        a.G = p.G;
+    } else if (same) {
         // all weights of a fused QKV in one launch
         a.nw = p.nstreams;
         for (int i = 0; i < p.nstreams; ++i) {
@@ -2167,8 +2178,29 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
             a.y[i] = p.s[i].y;
             a.res[i] = p.s[i].res;
         }
+    } else {
+        // mixed formats (Q4_K_M: Q6_K v): one launch per weight, all or nothing
+        for (int i = 0; i < p.nstreams; ++i) {
+            const int fi = p.s[i].fmt;
+            const bool ok_fmt = fi == T2C_Q4_K || (fi == T2C_Q6_K && p.K % 2048 == 0);
+            if (!ok_fmt || reinterpret_cast<uintptr_t>(p.s[i].w) % 16) return T2C_OK;
+        }
+        for (int i = 0; i < p.nstreams; ++i) {
+            QGemmArgs one = a;
+            one.fmt = p.s[i].fmt;
+            one.nw = 1;
+            one.w[0] = p.s[i].w;
+            one.N[0] = p.s[i].n;
+            one.y[0] = p.s[i].y;
+            one.res[0] = p.s[i].res;
+            const int rc = qgemm(one, stream);
+            if (rc == T2C_EUNSUPPORTED && i == 0) return T2C_OK;
+            if (rc != T2C_OK) return rc == T2C_EUNSUPPORTED ? set_error(T2C_EUNSUPPORTED, "qgemm: weight %d", i) : rc;
+        }
+        used = true;
+        return T2C_OK;
     }
-    const int rc = qgemm_q4k(a, stream);
+    const int rc = qgemm(a, stream);
     if (rc == T2C_EUNSUPPORTED) return T2C_OK;  // nothing launched: the matvec kernels serve this call
     used = true;
     return rc;

@@ -284,6 +284,9 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, kind: str | int, k: int, *,
     n = _check_weight(w, wtype, k)
     m = _check_x(x, k)
     g = (n + 3) // 4
+    if norm_weight is not None and m > 4:
+        # the tensor-core GEMM for M > 4 reads x as it is: normalize first (torch-allocated temporary)
+        x, norm_weight = rms_norm(x, norm_weight, eps), None
     if partial_scores is None:
         partial_scores = torch.empty(m, g, dtype=torch.float32, device=x.device)
         partial_tokens = torch.empty(m, g, dtype=torch.int32, device=x.device)
