@@ -24,12 +24,14 @@ def _close(got: torch.Tensor, ref: torch.Tensor, rel: float = 4e-3, abs_: float 
     assert not bool(bad.any()), f"max err {float(err.max())} (bound at worst {float(bound.flatten()[err.argmax()])})"
 
 
-def test_rms_norm():
+@pytest.mark.parametrize("rows,cols", [(37, 1024), (1, 4096), (32, 4096), (5, 12288), (3, 1028)])
+def test_rms_norm(rows, cols):
+    """One CTA per row for rows of up to 8192 values (multiples of 8), one warp per row otherwise."""
     from torch2vk_b200 import kernels
 
     torch.manual_seed(0)
-    x = torch.randn(37, 1024, device="cuda", dtype=torch.float16) * 3
-    w = torch.rand(1024, device="cuda") + 0.5
+    x = torch.randn(rows, cols, device="cuda", dtype=torch.float16) * 3
+    w = torch.rand(cols, device="cuda") + 0.5
     y = kernels.rms_norm(x, w, 1e-6)
     xf = x.float()
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w

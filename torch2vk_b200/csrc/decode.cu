@@ -48,6 +48,53 @@ __global__ void rms_norm_kernel(const __half *__restrict__ x, const float *__res
     }
 }
 
+// One CTA per row (rows of up to 32 x 256 values): every thread issues its
+// 16-byte loads at once, so a row costs one load latency instead of a chain of
+// them; the sum of squares meets in shared memory.
+constexpr int kRnThreads = 256;
+constexpr int kRnVec = 4;  // 16-byte vectors per thread
+__global__ void __launch_bounds__(kRnThreads) rms_norm_row_kernel(const __half *__restrict__ x, const float *__restrict__ w,
+                                                                  __half *__restrict__ y, int cols, float eps) {
+    __shared__ float part[kRnThreads / 32];
+    const int64_t row = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int nv = cols / 8;
+    pdl_wait();
+    pdl_trigger();
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * cols);
+    uint4 v[kRnVec];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRnVec; ++i) {
+        const int c = tid + i * kRnThreads;
+        v[i] = c < nv ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kRnVec; ++i) {
+        const float4 a = h4_to_f4(make_uint2(v[i].x, v[i].y)), b = h4_to_f4(make_uint2(v[i].z, v[i].w));
+        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) part[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRnThreads / 32; ++i) tot += part[i];
+    const float inv = rsqrtf(tot / static_cast<float>(cols) + eps);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + row * cols);
+#pragma unroll
+    for (int i = 0; i < kRnVec; ++i) {
+        const int c = tid + i * kRnThreads;
+        if (c >= nv) continue;
+        const float4 g0 = *reinterpret_cast<const float4 *>(w + 8 * c), g1 = *reinterpret_cast<const float4 *>(w + 8 * c + 4);
+        float4 a = h4_to_f4(make_uint2(v[i].x, v[i].y)), b = h4_to_f4(make_uint2(v[i].z, v[i].w));
+        a = make_float4(a.x * inv * g0.x, a.y * inv * g0.y, a.z * inv * g0.z, a.w * inv * g0.w);
+        b = make_float4(b.x * inv * g1.x, b.y * inv * g1.y, b.z * inv * g1.z, b.w * inv * g1.w);
+        const uint2 ha = f4_to_h4(a), hb = f4_to_h4(b);
+        yr[c] = make_uint4(ha.x, ha.y, hb.x, hb.y);
+    }
+}
+
 // ------------------------------------------------ q/k norm + RoPE + cache
 // One warp per (token, head) vector of D values (D/32 per lane, D <= 256).
 // Heads [0, NH): q; [NH, NH+NK): k (norm + rope -> k cache); [NH+NK, NH+2NK): v copy.
@@ -1400,6 +1447,9 @@ extern "C" int t2c_rms_norm(const void *x, const float *w, void *y, int64_t rows
     if (!x || !w || !y) return set_error(T2C_EINVAL, "rms_norm: NULL pointer");
     if (rows <= 0 || cols <= 0 || cols % 4) return set_error(T2C_EINVAL, "rms_norm: cols must be a positive multiple of 4");
     if (!aligned(x, 8) || !aligned(y, 8) || !aligned(w, 16)) return set_error(T2C_EINVAL, "rms_norm: misaligned operand");
+    if (cols % 8 == 0 && cols <= 8 * kRnThreads * kRnVec && aligned(x, 16) && aligned(y, 16))
+        return launch(rms_norm_row_kernel, dim3(static_cast<unsigned>(rows)), dim3(kRnThreads), 0, as_stream(stream),
+                      static_cast<const __half *>(x), w, static_cast<__half *>(y), static_cast<int>(cols), eps);
     const int warps = 8;
     return launch(rms_norm_kernel, dim3(static_cast<unsigned>((rows + warps - 1) / warps)), dim3(warps * 32), 0,
                   as_stream(stream), static_cast<const __half *>(x), w, static_cast<__half *>(y), rows,
