@@ -320,6 +320,44 @@ int t2c_quantize(int wtype, const float *x, void *out, int64_t R, int64_t K, voi
 /* packed blocks -> fp32 [R, K] (decoders of the same shader files). */
 int t2c_dequantize(int wtype, const void *w, float *out, int64_t R, int64_t K, void *stream);
 
+/* ------------------------------------------------------------------ ASR audio encoder
+ * Qwen3-ASR audio tower (models/quantized_qwen3_asr/dispatch/audio_encoder.py): Q8_0 weights,
+ * fp16 activations, fp32 biases.
+ *
+ * y[M, N] = x[M, K] @ deq(W)^T + bias (bias may be NULL; act 1 applies GELU (erf) after the
+ * bias).  W: Q8_0 rows of ceil(K/32) blocks.  x 16-byte aligned, K a multiple of 8.
+ * Replaces ExportLinearBiasQ8_0WeightF32BiasProgram
+ *   src/models/quantized_qwen3_asr/shaders/linear_bias_q8_0w_f32b_f32.py:38-92
+ * and (bias NULL) ExportLinearNobiasQ8_0Program (linear_nobias_q8_0_f32.py).
+ */
+int t2c_linear_q8_0_bias(const void *x, const void *w, const float *bias, void *y, int64_t M, int64_t N, int64_t K,
+                         int act, void *stream);
+/* NCHW fp16 conv2d with Q8_0 weights [Co, ceil(Ci*kh*kw / 32) blocks] (k = (ic, fh, fw)), fp32
+ * bias, zero padding; out [B, Co, Ho, Wo]; act 1 applies GELU after the bias.
+ * Replaces ExportConv2dQ8_0WeightF32BiasProgram
+ *   src/models/quantized_qwen3_asr/shaders/conv2d_q8_0w_f32b_f16.py:36-98 */
+int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci, int64_t Hi,
+                    int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                    int64_t ph, int64_t pw, int act, void *stream);
+/* Row LayerNorm, fp16 x / y [rows, cols], fp32 w / b [cols] (cols a multiple of 8, <= 4096).
+ * Replaces ExportLayerNormF32WeightF32BiasProgram (layer_norm_f32w_f32b_f32.py). */
+int t2c_layer_norm(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t cols, float eps,
+                   void *stream);
+/* y = x * 0.5 * (1 + erf(x / sqrt 2)), fp16.  Replaces ExportGeluF32Program (gelu_f32.py). */
+int t2c_gelu(const void *x, void *y, int64_t n, void *stream);
+/* out[o, :] = x[index[o], :] (fp16 rows of H; int64 index; an index outside [0, rows) writes a
+ * zero row and sets T2C_EINVAL).  Replaces ExportIndexSelectF32Program (index_select_f32_*.py). */
+int t2c_index_rows(const void *x, const int64_t *index, void *out, int64_t O, int64_t H, int64_t rows, void *stream);
+/* Non-causal attention with an additive fp16 mask (the encoder's block-diagonal windows):
+ * out[b,h,t,:] = softmax(q[b,h,t,:] . k[b,h,s,:] * scale + mask[b,h,t,s]) v[b,h,s,:], D = 64.
+ * Strides (elements) are {batch, head, row} for q, k, v, out and {batch, head, query row} for the
+ * mask (0 broadcasts; the key stride is 1).  Replaces ExportSdpaProgram
+ *   src/models/quantized_qwen3_asr/shaders/sdpa_masked_f32.py:33-90 */
+int t2c_attn_masked(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B, int64_t H,
+                    int64_t T, int64_t S, int64_t D, const int64_t *q_strides, const int64_t *k_strides,
+                    const int64_t *v_strides, const int64_t *m_strides, const int64_t *o_strides, float scale,
+                    void *stream);
+
 /* ------------------------------------------------------------------ tensor parallelism
  * One-shot all-reduce of fp16 tensors over NVLink peer memory (the two
  * per-layer reductions of the row-split o_proj / down_proj partial sums in the

@@ -68,6 +68,12 @@ _SIGNATURES: dict[str, list] = {
     "t2c_kv_cache_write": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                            _vp],
     "t2c_token_select_chunks": [_vp, _vp, _i64, _vp, _vp, _vp],
+    "t2c_linear_q8_0_bias": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp],
+    "t2c_conv2d_q8_0": [_vp, _vp, _vp, _vp] + [_i64] * 13 + [_i32, _vp],
+    "t2c_layer_norm": [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
+    "t2c_gelu": [_vp, _vp, _i64, _vp],
+    "t2c_index_rows": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "t2c_attn_masked": [_vp] * 5 + [_i64] * 5 + [_vp] * 5 + [_f32, _vp],
     "t2c_embedding": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "t2c_add": [_vp, _vp, _vp, _i64, _vp],
     "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],

@@ -1,0 +1,600 @@
+// Kernels of the Qwen3-ASR audio encoder (quantized_qwen3_asr, config 5):
+// Q8_0-weight linears and 3x3 stride-2 convolutions as one tensor-core GEMM
+// (mma.m16n8k16, fp16 operands, fp32 accumulation, fp32 bias and optional
+// GELU in the epilogue), LayerNorm, GELU, row gather and windowed
+// (additive-mask) attention.  Activations are fp16 throughout, as in the
+// reference's exported encoder (models/quantized_qwen3_asr/dispatch/audio_encoder.py).
+#include <float.h>
+
+#include "common.cuh"
+
+namespace t2c {
+namespace {
+
+__device__ __forceinline__ void ldsm4(uint32_t r[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm4_t(uint32_t r[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ float4 h4_to_f4_c(uint2 v) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+// ------------------------------------------------------- Q8_0 GEMM / conv
+// y[m, n] = sum_k A[m, k] * d[n, k/32] * q[n, k] + bias[n]  (optional GELU).
+// LINEAR: A = x [M, K] row-major.  CONV: A is the implicit im2col of an NCHW
+// input, m = (b, oh, ow), k = (ic, fh, fw), with zero padding; the output is
+// written NCHW (n = output channel).  CTA = 4 warps on a 64 x 64 (m, n) tile;
+// K advances one Q8_0 block (32 values) at a time through two shared-memory
+// buffers (the next block is loaded into registers while the current one is
+// multiplied).  Weights are dequantized to fp16 (d * q rounded once).
+struct Q8Gemm {
+    const __half *x;
+    const uint8_t *w;
+    const float *bias;
+    __half *y;
+    int M, N, K, nblk;
+    int64_t row_bytes;
+    int act;
+    int Ci, Hi, Wi, Ho, Wo, kh, kw, sh, sw, ph, pw;
+};
+constexpr int kQT = 64;
+constexpr int kQRow = 40;  // halves per shared row (80 B: conflict-free ldmatrix rows)
+
+template <bool CONV>
+__global__ void __launch_bounds__(128) q8_gemm_kernel(const Q8Gemm p) {
+    __shared__ __align__(16) __half As[2][kQT][kQRow];
+    __shared__ __align__(16) __half Bs[2][kQT][kQRow];
+    __shared__ int pix[kQT][3];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int m0 = blockIdx.x * kQT, n0 = blockIdx.y * kQT;
+    const int wm = (warp & 1) * 32, wn = (warp >> 1) * 32;
+    pdl_wait();
+    pdl_trigger();
+    if (CONV) {
+        if (tid < kQT) {
+            const int m = m0 + tid;
+            if (m < p.M) {
+                const int hw = p.Ho * p.Wo;
+                const int b = m / hw, r = m - b * hw, oh = r / p.Wo, ow = r - oh * p.Wo;
+                pix[tid][0] = b * p.Ci * p.Hi * p.Wi;
+                pix[tid][1] = oh * p.sh - p.ph;
+                pix[tid][2] = ow * p.sw - p.pw;
+            } else {
+                pix[tid][0] = -1;
+            }
+        }
+        __syncthreads();
+    }
+    // per-thread register stage of one K block
+    uint4 av[2];
+    __half ac[16];
+    uint32_t bq[8];
+    float bd = 0.0f;
+    const int brow = tid >> 1, bhf = tid & 1;
+    auto load = [&](int kb) {
+        const int k0 = kb * 32;
+        if (CONV) {
+            const int kk = tid & 31, k = k0 + kk;
+            const bool kin = k < p.K;
+            int ic = 0, fh = 0, fw = 0;
+            if (kin) {
+                const int khw = p.kh * p.kw;
+                ic = k / khw;
+                const int rem = k - ic * khw;
+                fh = rem / p.kw;
+                fw = rem - fh * p.kw;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int row = (tid >> 5) + 4 * j;
+                __half v = __float2half(0.0f);
+                const int pb = pix[row][0];
+                if (kin && pb >= 0) {
+                    const int ih = pix[row][1] + fh, iw = pix[row][2] + fw;
+                    if (ih >= 0 && ih < p.Hi && iw >= 0 && iw < p.Wi) v = p.x[pb + (ic * p.Hi + ih) * p.Wi + iw];
+                }
+                ac[j] = v;
+            }
+        } else {
+            const int m = m0 + brow;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int k = k0 + 16 * bhf + 8 * j;
+                av[j] = (m < p.M && k + 8 <= p.K)
+                            ? *reinterpret_cast<const uint4 *>(p.x + static_cast<int64_t>(m) * p.K + k)
+                            : make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        const int n = n0 + brow;
+        if (n < p.N) {
+            const uint8_t *blk = p.w + static_cast<int64_t>(n) * p.row_bytes + static_cast<int64_t>(kb) * 34;
+            bd = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
+            const unsigned short *qs = reinterpret_cast<const unsigned short *>(blk + 2 + 16 * bhf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bq[j] = qs[j];
+        } else {
+            bd = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bq[j] = 0u;
+        }
+    };
+    auto store = [&](int buf) {
+        if (CONV) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) As[buf][(tid >> 5) + 4 * j][tid & 31] = ac[j];
+        } else {
+            *reinterpret_cast<uint4 *>(&As[buf][brow][16 * bhf]) = av[0];
+            *reinterpret_cast<uint4 *>(&As[buf][brow][16 * bhf + 8]) = av[1];
+        }
+        uint32_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float lo = bd * static_cast<float>(static_cast<int8_t>(bq[j] & 0xffu));
+            const float hi = bd * static_cast<float>(static_cast<int8_t>(bq[j] >> 8));
+            const __half2 hv = __floats2half2_rn(lo, hi);
+            h[j] = *reinterpret_cast<const uint32_t *>(&hv);
+        }
+        *reinterpret_cast<uint4 *>(&Bs[buf][brow][16 * bhf]) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(&Bs[buf][brow][16 * bhf + 8]) = make_uint4(h[4], h[5], h[6], h[7]);
+    };
+    float acc[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+    load(0);
+    store(0);
+    __syncthreads();
+    int buf = 0;
+    for (int kb = 0; kb < p.nblk; ++kb) {
+        if (kb + 1 < p.nblk) load(kb + 1);
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t a[2][4], b[2][4];
+#pragma unroll
+            for (int mi = 0; mi < 2; ++mi) ldsm4(a[mi], &As[buf][wm + 16 * mi + (lane & 15)][16 * ks + 8 * (lane >> 4)]);
+#pragma unroll
+            for (int np = 0; np < 2; ++np)
+                ldsm4(b[np], &Bs[buf][wn + 16 * np + (lane & 7) + 8 * (lane >> 4)][16 * ks + 8 * ((lane >> 3) & 1)]);
+#pragma unroll
+            for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    mma16816(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+                    mma16816(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+                }
+        }
+        if (kb + 1 < p.nblk) store(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int m = m0 + wm + 16 * mi + g + 8 * (e >> 1);
+                const int n = n0 + wn + 8 * ni + 2 * t4 + (e & 1);
+                if (m >= p.M || n >= p.N) continue;
+                float v = acc[mi][ni][e] + (p.bias ? p.bias[n] : 0.0f);
+                if (p.act) v = gelu_erf(v);
+                if (CONV) {
+                    const int hw = p.Ho * p.Wo;
+                    const int b = m / hw, r = m - b * hw;
+                    p.y[(static_cast<int64_t>(b) * p.N + n) * hw + r] = __float2half_rn(v);
+                } else {
+                    p.y[static_cast<int64_t>(m) * p.N + n] = __float2half_rn(v);
+                }
+            }
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One CTA per row (cols <= 4096, a multiple of 8): y = (x - mean) / sqrt(var + eps) * w + b,
+// mean and variance of the fp32 values (two passes over registers).
+constexpr int kLnThreads = 256;
+__global__ void __launch_bounds__(kLnThreads) layer_norm_kernel(const __half *__restrict__ x, const float *__restrict__ w,
+                                                                const float *__restrict__ bias, __half *__restrict__ y,
+                                                                int cols, float eps) {
+    __shared__ float part[kLnThreads / 32];
+    __shared__ float stat;
+    const int64_t row = blockIdx.x;
+    const int tid = threadIdx.x, nv = cols / 8;
+    pdl_wait();
+    pdl_trigger();
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * cols);
+    float f[2][8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = tid + i * kLnThreads;
+        const uint4 v = c < nv ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+        const float4 a = h4_to_f4_c(make_uint2(v.x, v.y)), b = h4_to_f4_c(make_uint2(v.z, v.w));
+        f[i][0] = a.x; f[i][1] = a.y; f[i][2] = a.z; f[i][3] = a.w;
+        f[i][4] = b.x; f[i][5] = b.y; f[i][6] = b.z; f[i][7] = b.w;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += f[i][e];
+    }
+    s = warp_sum(s);
+    if ((tid & 31) == 0) part[tid >> 5] = s;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < kLnThreads / 32; ++i) t += part[i];
+        stat = t / static_cast<float>(cols);
+    }
+    __syncthreads();
+    const float mean = stat;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = tid + i * kLnThreads;
+        if (c < nv) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q += (f[i][e] - mean) * (f[i][e] - mean);
+        }
+    }
+    q = warp_sum(q);
+    __syncthreads();
+    if ((tid & 31) == 0) part[tid >> 5] = q;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < kLnThreads / 32; ++i) t += part[i];
+        stat = rsqrtf(t / static_cast<float>(cols) + eps);
+    }
+    __syncthreads();
+    const float inv = stat;
+    uint4 *yr = reinterpret_cast<uint4 *>(y + row * cols);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = tid + i * kLnThreads;
+        if (c >= nv) continue;
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int k = 8 * c + 2 * e;
+            const __half2 hv = __floats2half2_rn((f[i][2 * e] - mean) * inv * w[k] + bias[k],
+                                                 (f[i][2 * e + 1] - mean) * inv * w[k + 1] + bias[k + 1]);
+            h[e] = *reinterpret_cast<const uint32_t *>(&hv);
+        }
+        yr[c] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+// -------------------------------------------------------------- elementwise
+__global__ void gelu_kernel(const __half *__restrict__ x, __half *__restrict__ y, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = __float2half_rn(gelu_erf(__half2float(x[i])));
+}
+
+// out[o, :] = x[index[o], :]; an index outside [0, rows) writes zeros and sets T2C_EINVAL.
+__global__ void index_rows_kernel(const __half *__restrict__ x, const int64_t *__restrict__ index,
+                                  __half *__restrict__ out, int64_t O, int64_t H, int64_t rows) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < O * H;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t o = i / H, c = i - o * H;
+        const int64_t r = index[o];
+        if (r < 0 || r >= rows) {
+            if (c == 0) report_device_error(T2C_EINVAL);
+            out[i] = __float2half(0.0f);
+        } else {
+            out[i] = x[r * H + c];
+        }
+    }
+}
+
+// ---------------------------------------------------- masked attention
+// out[b, h, t, :] = softmax(q k^T * scale + mask[t, s]) v over all S keys
+// (non-causal; the additive fp16 mask carries the encoder's block-diagonal
+// windows, -inf outside).  CTA = 4 warps on (b, h, 64-query tile); key / value
+// tiles of 64 rows in shared memory; mma.m16n8k16 for S = Q K^T and O += P V
+// (P split into fp16 high / low parts), online softmax in the log2 domain.
+template <int D>
+__global__ void __launch_bounds__(128) attn_masked_kernel(
+    const __half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
+    const __half *__restrict__ mask, __half *__restrict__ out, int H, int T, int S, int64_t q_sb, int64_t q_sh,
+    int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_ss, int64_t v_sb, int64_t v_sh, int64_t v_ss, int64_t m_sb,
+    int64_t m_sh, int64_t m_st, int64_t o_sb, int64_t o_sh, int64_t o_st, float scale_log2) {
+    constexpr int R = D + 8;  // halves per shared row
+    constexpr int KS = D / 16, NT = D / 8;
+    __shared__ __align__(16) __half qs[64][R];
+    __shared__ __align__(16) __half ks[64][R];
+    __shared__ __align__(16) __half vs[64][R];
+    const int qtiles = (T + 63) / 64;
+    const int qt = blockIdx.x % qtiles;
+    const int h = (blockIdx.x / qtiles) % H;
+    const int b = blockIdx.x / (qtiles * H);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    pdl_wait();
+    pdl_trigger();
+    const int q0 = qt * 64;
+    for (int i = threadIdx.x; i < 64 * (D / 8); i += 128) {
+        const int r = i / (D / 8), c = i - r * (D / 8);
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (q0 + r < T) val = *reinterpret_cast<const uint4 *>(q + b * q_sb + h * q_sh + (q0 + r) * q_st + 8 * c);
+        *reinterpret_cast<uint4 *>(&qs[r][8 * c]) = val;
+    }
+    __syncthreads();
+    uint32_t qa[KS][4];
+#pragma unroll
+    for (int s = 0; s < KS; ++s) ldsm4(qa[s], &qs[16 * w + (lane & 15)][16 * s + 8 * (lane >> 4)]);
+    const int t0 = q0 + 16 * w + g, t1 = t0 + 8;
+    const __half *mrow0 = mask + b * m_sb + h * m_sh + static_cast<int64_t>(min(t0, T - 1)) * m_st;
+    const __half *mrow1 = mask + b * m_sb + h * m_sh + static_cast<int64_t>(min(t1, T - 1)) * m_st;
+    float m_run[2] = {-FLT_MAX, -FLT_MAX}, l_run[2] = {0.0f, 0.0f};
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 64) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 64 * (D / 8); i += 128) {
+            const int r = i / (D / 8), c = i - r * (D / 8);
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+            if (s0 + r < S) {
+                kv = *reinterpret_cast<const uint4 *>(k + b * k_sb + h * k_sh + (s0 + r) * k_ss + 8 * c);
+                vv = *reinterpret_cast<const uint4 *>(v + b * v_sb + h * v_sh + (s0 + r) * v_ss + 8 * c);
+            }
+            *reinterpret_cast<uint4 *>(&ks[r][8 * c]) = kv;
+            *reinterpret_cast<uint4 *>(&vs[r][8 * c]) = vv;
+        }
+        __syncthreads();
+        float sc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+#pragma unroll
+        for (int s = 0; s < KS; ++s)
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t kb[4];
+                ldsm4(kb, &ks[16 * np + (lane & 7) + 8 * (lane >> 4)][16 * s + 8 * ((lane >> 3) & 1)]);
+                mma16816(sc[2 * np], qa[s], kb[0], kb[1]);
+                mma16816(sc[2 * np + 1], qa[s], kb[2], kb[3]);
+            }
+        float mx[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = s0 + 8 * n + 2 * t4 + (e & 1);
+                const int r = e >> 1;
+                float val = -INFINITY;
+                if (key < S) {
+                    const float mk = __half2float((r ? mrow1 : mrow0)[key]);
+                    val = (sc[n][e] * scale_log2) + mk * 1.4426950408889634f;
+                }
+                sc[n][e] = val;
+                mx[r] = fmaxf(mx[r], val);
+            }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float m_new = fmaxf(m_run[r], mx[r]);
+            corr[r] = exp2f(m_run[r] - m_new);
+            m_run[r] = m_new;
+            l_run[r] *= corr[r];
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            o[n][0] *= corr[0];
+            o[n][1] *= corr[0];
+            o[n][2] *= corr[1];
+            o[n][3] *= corr[1];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float pv[2][4];
+#pragma unroll
+            for (int hn = 0; hn < 2; ++hn)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float p = exp2f(sc[2 * j + hn][e] - m_run[e >> 1]);
+                    l_run[e >> 1] += p;
+                    pv[hn][e] = p;
+                }
+            uint32_t ah[4], al[4];
+#pragma unroll
+            for (int hn = 0; hn < 2; ++hn)
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const __half2 hi = __floats2half2_rn(pv[hn][2 * r], pv[hn][2 * r + 1]);
+                    const float2 hf = __half22float2(hi);
+                    const __half2 lo = __floats2half2_rn(pv[hn][2 * r] - hf.x, pv[hn][2 * r + 1] - hf.y);
+                    ah[2 * hn + r] = *reinterpret_cast<const uint32_t *>(&hi);
+                    al[2 * hn + r] = *reinterpret_cast<const uint32_t *>(&lo);
+                }
+#pragma unroll
+            for (int dp = 0; dp < D / 16; ++dp) {
+                uint32_t vb[4];
+                ldsm4_t(vb, &vs[16 * j + (lane & 7) + 8 * ((lane >> 3) & 1)][16 * dp + 8 * (lane >> 4)]);
+                mma16816(o[2 * dp], ah, vb[0], vb[1]);
+                mma16816(o[2 * dp], al, vb[0], vb[1]);
+                mma16816(o[2 * dp + 1], ah, vb[2], vb[3]);
+                mma16816(o[2 * dp + 1], al, vb[2], vb[3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+        l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+    }
+    const float inv0 = l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f, inv1 = l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        const int d = 8 * n + 2 * t4;
+        if (t0 < T)
+            *reinterpret_cast<__half2 *>(out + b * o_sb + h * o_sh + static_cast<int64_t>(t0) * o_st + d) =
+                __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+        if (t1 < T)
+            *reinterpret_cast<__half2 *>(out + b * o_sb + h * o_sh + static_cast<int64_t>(t1) * o_st + d) =
+                __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+    }
+}
+
+template <typename Kernel, typename... Args>
+int launch_asr(Kernel kernel, dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args...);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "asr launch: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+bool al(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int q8_gemm(Q8Gemm p, bool conv, cudaStream_t s) {
+    const dim3 grid(static_cast<unsigned>((p.M + kQT - 1) / kQT), static_cast<unsigned>((p.N + kQT - 1) / kQT));
+    return conv ? launch_asr(q8_gemm_kernel<true>, grid, dim3(128), s, p) : launch_asr(q8_gemm_kernel<false>, grid, dim3(128), s, p);
+}
+
+}  // namespace
+
+cudaError_t status_asr(unsigned int *bits, int clear, cudaStream_t s) { return read_tu_status(bits, clear, s); }
+
+}  // namespace t2c
+
+using namespace t2c;
+
+extern "C" int t2c_linear_q8_0_bias(const void *x, const void *w, const float *bias, void *y, int64_t M, int64_t N,
+                                    int64_t K, int act, void *stream) {
+    if (!x || !w || !y) return set_error(T2C_EINVAL, "linear_q8_0_bias: NULL pointer");
+    if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+        return set_error(T2C_EINVAL, "linear_q8_0_bias: bad shape");
+    if (K % 8 || !al(x, 16) || !al(w, 2)) return set_error(T2C_EINVAL, "linear_q8_0_bias: x rows must be 16-byte aligned (K %% 8 == 0)");
+    Q8Gemm p = {};
+    p.x = static_cast<const __half *>(x);
+    p.w = static_cast<const uint8_t *>(w);
+    p.bias = bias;
+    p.y = static_cast<__half *>(y);
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.nblk = static_cast<int>((K + 31) / 32);
+    p.row_bytes = static_cast<int64_t>(p.nblk) * 34;
+    p.act = act;
+    return q8_gemm(p, false, as_stream(stream));
+}
+
+extern "C" int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci,
+                               int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw,
+                               int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act, void *stream) {
+    if (!x || !w || !out) return set_error(T2C_EINVAL, "conv2d_q8_0: NULL pointer");
+    if (B <= 0 || Ci <= 0 || Hi <= 0 || Wi <= 0 || Co <= 0 || Ho <= 0 || Wo <= 0 || kh <= 0 || kw <= 0 || sh <= 0 ||
+        sw <= 0 || ph < 0 || pw < 0)
+        return set_error(T2C_EINVAL, "conv2d_q8_0: bad shape");
+    if (B * Ci * Hi * Wi > INT32_MAX || B * Ho * Wo > INT32_MAX || Ci * kh * kw > INT32_MAX)
+        return set_error(T2C_EUNSUPPORTED, "conv2d_q8_0: sizes beyond 2^31 elements");
+    if ((Ho - 1) * sh - ph + kh - 1 >= Hi + ph || (Wo - 1) * sw - pw + kw - 1 >= Wi + pw)
+        return set_error(T2C_EINVAL, "conv2d_q8_0: output extent does not match input, stride and padding");
+    if (!al(w, 2)) return set_error(T2C_EINVAL, "conv2d_q8_0: weight must be 2-byte aligned");
+    Q8Gemm p = {};
+    p.x = static_cast<const __half *>(x);
+    p.w = static_cast<const uint8_t *>(w);
+    p.bias = bias;
+    p.y = static_cast<__half *>(out);
+    p.M = static_cast<int>(B * Ho * Wo);
+    p.N = static_cast<int>(Co);
+    p.K = static_cast<int>(Ci * kh * kw);
+    p.nblk = (p.K + 31) / 32;
+    p.row_bytes = static_cast<int64_t>(p.nblk) * 34;
+    p.act = act;
+    p.Ci = static_cast<int>(Ci);
+    p.Hi = static_cast<int>(Hi);
+    p.Wi = static_cast<int>(Wi);
+    p.Ho = static_cast<int>(Ho);
+    p.Wo = static_cast<int>(Wo);
+    p.kh = static_cast<int>(kh);
+    p.kw = static_cast<int>(kw);
+    p.sh = static_cast<int>(sh);
+    p.sw = static_cast<int>(sw);
+    p.ph = static_cast<int>(ph);
+    p.pw = static_cast<int>(pw);
+    return q8_gemm(p, true, as_stream(stream));
+}
+
+extern "C" int t2c_layer_norm(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t cols,
+                              float eps, void *stream) {
+    if (!x || !w || !b || !y) return set_error(T2C_EINVAL, "layer_norm: NULL pointer");
+    if (rows <= 0 || cols <= 0 || cols % 8 || cols > 8 * 2 * kLnThreads)
+        return set_error(T2C_EINVAL, "layer_norm: cols must be a multiple of 8 up to %d", 16 * kLnThreads);
+    if (!al(x, 16) || !al(y, 16)) return set_error(T2C_EINVAL, "layer_norm: rows must be 16-byte aligned");
+    return launch_asr(layer_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kLnThreads), as_stream(stream),
+                      static_cast<const __half *>(x), w, b, static_cast<__half *>(y), static_cast<int>(cols), eps);
+}
+
+extern "C" int t2c_gelu(const void *x, void *y, int64_t n, void *stream) {
+    if (!x || !y || n <= 0) return set_error(T2C_EINVAL, "gelu: bad argument");
+    int64_t grid = (n + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    return launch_asr(gelu_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
+                      static_cast<const __half *>(x), static_cast<__half *>(y), n);
+}
+
+extern "C" int t2c_index_rows(const void *x, const int64_t *index, void *out, int64_t O, int64_t H, int64_t rows,
+                              void *stream) {
+    if (!x || !index || !out || O <= 0 || H <= 0 || rows <= 0) return set_error(T2C_EINVAL, "index_rows: bad argument");
+    int64_t grid = (O * H + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    return launch_asr(index_rows_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
+                      static_cast<const __half *>(x), index, static_cast<__half *>(out), O, H, rows);
+}
+
+extern "C" int t2c_attn_masked(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B,
+                               int64_t H, int64_t T, int64_t S, int64_t D, const int64_t *q_strides,
+                               const int64_t *k_strides, const int64_t *v_strides, const int64_t *m_strides,
+                               const int64_t *o_strides, float scale, void *stream) {
+    if (!q || !k || !v || !mask || !out || !q_strides || !k_strides || !v_strides || !m_strides || !o_strides)
+        return set_error(T2C_EINVAL, "attn_masked: NULL pointer");
+    if (B <= 0 || H <= 0 || T <= 0 || S <= 0) return set_error(T2C_EINVAL, "attn_masked: bad shape");
+    if (D != 64) return set_error(T2C_EUNSUPPORTED, "attn_masked: D=%lld (64 only)", (long long)D);
+    const int64_t *st[3] = {q_strides, k_strides, v_strides};
+    const void *ptrs[3] = {q, k, v};
+    for (int i = 0; i < 3; ++i) {
+        if (!al(ptrs[i], 16) || st[i][0] % 8 || st[i][1] % 8 || st[i][2] % 8)
+            return set_error(T2C_EINVAL, "attn_masked: q / k / v rows must be 16-byte aligned");
+    }
+    if (!al(out, 4) || o_strides[0] % 2 || o_strides[1] % 2 || o_strides[2] % 2)
+        return set_error(T2C_EINVAL, "attn_masked: out rows must be 4-byte aligned");
+    const int64_t qtiles = (T + 63) / 64;
+    const dim3 grid(static_cast<unsigned>(B * H * qtiles));
+    const float sl2 = 1.4426950408889634f * scale;
+#define T2C_AM(DD)                                                                                                    \
+    return launch_asr(attn_masked_kernel<DD>, grid, dim3(128), as_stream(stream), static_cast<const __half *>(q),      \
+                      static_cast<const __half *>(k), static_cast<const __half *>(v), static_cast<const __half *>(mask), \
+                      static_cast<__half *>(out), static_cast<int>(H), static_cast<int>(T), static_cast<int>(S),        \
+                      q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2], v_strides[0],  \
+                      v_strides[1], v_strides[2], m_strides[0], m_strides[1], m_strides[2], o_strides[0], o_strides[1], \
+                      o_strides[2], sl2)
+    T2C_AM(64);
+#undef T2C_AM
+}

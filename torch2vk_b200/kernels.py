@@ -391,3 +391,86 @@ def token_select_chunks(scores: torch.Tensor, tokens: torch.Tensor, chunk_scores
                         chunk_tokens: torch.Tensor) -> None:
     _lib.lib().call("t2c_token_select_chunks", _lib.ptr(scores), _lib.ptr(tokens), scores.numel(),
                     _lib.ptr(chunk_scores), _lib.ptr(chunk_tokens), _lib.stream_ptr())
+
+
+# ------------------------------------------------------------------ ASR audio encoder
+def _q8_rows(w: torch.Tensor, n: int, k: int) -> None:
+    nbytes = (k + 31) // 32 * 34
+    if w.numel() * w.element_size() != n * nbytes or not w.is_cuda:
+        raise ValueError(f"Q8_0 weight must hold {n} rows of {nbytes} bytes on the GPU")
+
+
+def linear_q8_0_bias(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, n: int, *, gelu: bool = False,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ deq(W)^T + bias (optional GELU): Q8_0 weights, fp16 x [..., K], fp32 bias [N]."""
+    k = x.shape[-1]
+    if x.dtype != torch.float16 or not x.is_contiguous():
+        raise ValueError("x must be contiguous float16")
+    _q8_rows(w, n, k)
+    if bias is not None:
+        _check(bias, torch.float32, "bias")
+    m = x.numel() // k
+    out = torch.empty(*x.shape[:-1], n, dtype=torch.float16, device=x.device) if out is None else out
+    _lib.lib().call("t2c_linear_q8_0_bias", _lib.ptr(x), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(out), m, n, k,
+                    1 if gelu else 0, _lib.stream_ptr())
+    return out
+
+
+def conv2d_q8_0(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, co: int, *, kernel: int = 3,
+                stride: int = 2, padding: int = 1, gelu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """NCHW fp16 conv2d with Q8_0 weights [Co, ceil(Ci*kernel^2/32) blocks] and fp32 bias (optional GELU)."""
+    if x.dtype != torch.float16 or x.dim() != 4 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous float16 [B, Ci, H, W] tensor")
+    b, ci, hi, wi = x.shape
+    _q8_rows(w, co, ci * kernel * kernel)
+    ho = (hi + 2 * padding - kernel) // stride + 1
+    wo = (wi + 2 * padding - kernel) // stride + 1
+    out = torch.empty(b, co, ho, wo, dtype=torch.float16, device=x.device) if out is None else out
+    _lib.lib().call("t2c_conv2d_q8_0", _lib.ptr(x), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(out), b, ci, hi, wi, co,
+                    ho, wo, kernel, kernel, stride, stride, padding, padding, 1 if gelu else 0, _lib.stream_ptr())
+    return out
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    cols = x.shape[-1]
+    _check(w, torch.float32, "w")
+    _check(b, torch.float32, "b")
+    out = torch.empty_like(x) if out is None else out
+    _lib.lib().call("t2c_layer_norm", _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), _lib.ptr(out), x.numel() // cols, cols,
+                    float(eps), _lib.stream_ptr())
+    return out
+
+
+def gelu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty_like(x) if out is None else out
+    _lib.lib().call("t2c_gelu", _lib.ptr(x), _lib.ptr(out), x.numel(), _lib.stream_ptr())
+    return out
+
+
+def index_rows(x: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    h = x.shape[-1]
+    rows = x.numel() // h
+    _check(index, torch.int64, "index")
+    out = torch.empty(index.numel(), h, dtype=x.dtype, device=x.device) if out is None else out
+    _lib.lib().call("t2c_index_rows", _lib.ptr(x), _lib.ptr(index), _lib.ptr(out), index.numel(), h, rows,
+                    _lib.stream_ptr())
+    return out
+
+
+def attn_masked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor, *, scale: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """q [B, H, T, D], k / v [B, H, S, D], additive fp16 mask broadcastable to [B, H, T, S] (unit key stride)."""
+    B, H, T, D = q.shape
+    S = k.shape[2]
+    out = torch.empty(B, H, T, D, dtype=torch.float16, device=q.device) if out is None else out
+    m = mask.expand(B, H, T, S)
+    if m.stride(3) != 1:
+        raise ValueError("mask must have unit stride along keys")
+
+    def st(t):
+        return _lib.i64_array([t.stride(0), t.stride(1), t.stride(2)])
+
+    _lib.lib().call("t2c_attn_masked", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(mask), _lib.ptr(out), B, H, T,
+                    S, D, st(q), st(k), st(v), st(m), st(out), float(scale), _lib.stream_ptr())
+    return out
