@@ -26,6 +26,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 REPO = Path(__file__).resolve().parent
@@ -467,6 +468,24 @@ def main() -> None:
     t_step32 = max_over_ranks(events_time(big.step, reps32, stream), world)
 
     per_step_launches = cfg.layers * (5 if big.fused_attention else 6 + (1 if big.decode_splits > 1 else 0)) + 5
+    big._graph = None
+    del big
+    torch.cuda.empty_cache()
+
+    # ---- ASR audio encoder (configuration 5: the Qwen3-ASR-0.6B audio tower, Q8_0 weights, 3000 seeded
+    # synthetic mel frames -> 30 chunks -> 390 tokens); replicas only: every rank runs its own
+    from torch2vk_b200.asr import AsrEncoderConfig, AsrEncoderRunner, prepare_inputs, random_params
+
+    acfg = AsrEncoderConfig.qwen3_asr_0_6b()
+    ainp = prepare_inputs(np.random.default_rng(4).standard_normal((acfg.num_mel_bins, 3000)).astype(np.float32), acfg)
+    arun = AsrEncoderRunner(acfg, random_params(acfg, seed=0), device=dev)
+    atens = arun.upload(ainp)
+    for _ in range(3):
+        arun.forward(atens)
+    t_asr = max_over_ranks(events_time(lambda: arun.forward(atens), 5, stream), world)
+    asr = {"workload": "Qwen3-ASR-0.6B audio encoder, 3000 mel frames (30 chunks, 390 tokens), Q8_0 weights",
+           "ms": t_asr * 1e3, "tflops": arun.flops(ainp) / t_asr / 1e12}
+    del arun, atens
     clk = clocks.summary()
     line = {
         "metric": "qwen3_8b_int4_decode_tok_s_bs1",
@@ -506,6 +525,7 @@ def main() -> None:
         },
         "decode_bs32_tok_s": BATCH_LARGE / t_step32,
         "prefill_tok_s": PROMPT / t_prefill,
+        "asr_encoder": asr,
         "device_status_bits": status,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -263,3 +263,40 @@ def test_declaration_rules():
         a.validate_declaration()
     with pytest.raises(RuntimeError, match="runtime state"):
         a.buffer = object()
+
+
+@needs_ref
+def test_reference_asr_audio_encoder_dispatch_through_session(ref_modules):
+    """The reference's generated Qwen3-ASR audio tower (models/quantized_qwen3_asr/dispatch/audio_encoder.py)
+    for 3000 mel frames (30 chunks, 390 tokens) through RuntimeSession's validation: every contract class
+    it dispatches (Q8_0 conv2d / linear with bias, GELU, LayerNorm, masked SDPA, transposes, gather) has
+    a CUDA op, and the transposes have known permutations."""
+    from models.quantized_qwen3_asr.dispatch.audio_encoder import run_audio_encoder
+    from models.quantized_qwen3_asr.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+    from torch2vk_b200.runtime.variants import TRANSPOSE_PERMUTATIONS
+
+    frames, chunks, tokens, prompt = 3000, 30, 390, 400
+    mt = create_model_tensors(input_ids_shape=(1, prompt), attention_mask_shape=(1, prompt),
+                              input_features_shape=(1, 128, frames), feature_attention_mask_shape=(1, frames),
+                              prompt_length=prompt, audio_chunk_count=chunks, audio_sequence_length=tokens,
+                              max_sequence_length=prompt + 16, num_hidden_layers=28, num_key_value_heads=8,
+                              head_dim=128, max_new_tokens=4, eos_token_count=2, vocab_size=151936)
+    ae = mt.audio_encoder
+    rt = DrySession(mt)
+    inputs = {ae.x.name: np.zeros(ae.x.spec.shape, np.float16),
+              ae.position_embedding.name: np.zeros(ae.position_embedding.spec.shape, np.float16),
+              ae.compact_index.name: np.arange(tokens, dtype=np.int64),
+              ae.attention_mask.name: np.zeros(ae.attention_mask.spec.shape, np.float16)}
+    with rt.request(inputs=inputs):
+        with rt.frame("spike.audio"):
+            run_audio_encoder(rt)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    assert {"ExportConv2dQ8_0WeightF32BiasProgram", "ExportLinearBiasQ8_0WeightF32BiasProgram",
+            "ExportSdpaProgram", "ExportLayerNormF32WeightF32BiasProgram"} <= classes
+    for name, cls, _, _ in rt.calls:
+        if cls == "ExportTransposeProgram":
+            assert name in TRANSPOSE_PERMUTATIONS, name
+    sdpa = [c for c in rt.calls if c[1] == "ExportSdpaProgram"]
+    assert len(sdpa) == 18 and all(c[3]["D"] == 64 and c[3]["T"] == tokens for c in sdpa)

@@ -48,7 +48,14 @@ def _kind_of(weight: torch.Tensor, class_name: str) -> str:
     "ExportLinearNobiasQ8_0MatvecProgram", "ExportLinearNobiasQ8_0Program")
 def _linear(rt, variant, b, s, pc):
     """y = x @ deq(W)^T (linear_nobias_{q4_k,q6_k,q8_0}[_matvec]_f32.py)."""
-    kernels.linear(b["x"], b["weight"], _kind_of(b["weight"], variant.contract.class_name), s["K"], out=b["output"])
+    kind = _kind_of(b["weight"], variant.contract.class_name)
+    k = int(s["K"])
+    if kind == "q8_0" and b["x"].numel() // k > 8 and k % 8 == 0:
+        # many rows (the ASR conv_out projection): the Q8_0 tensor-core GEMM
+        n = b["output"].shape[-1]
+        kernels.linear_q8_0_bias(b["x"], b["weight"], None, n, out=b["output"])
+        return
+    kernels.linear(b["x"], b["weight"], kind, k, out=b["output"])
 
 
 @op("OptimizedLinearNobiasQ4KMatvecAddProgram", "OptimizedLinearNobiasQ6KMatvecAddProgram")
@@ -163,9 +170,13 @@ def _transpose(rt, variant, b, s, pc):
         perm = (0, 2, 1, 3)
     if perm is None:
         raise NotImplementedError(f"{variant.name}: unknown transpose permutation")
+    if len(perm) != x.dim():
+        raise ValueError(f"{variant.name}: rank-{len(perm)} permutation of a rank-{x.dim()} tensor")
     src = x.permute(*perm)
     if tuple(src.shape) != tuple(out.shape):
         raise ValueError(f"{variant.name}: permuted {tuple(src.shape)} != output {tuple(out.shape)}")
+    while src.dim() < 4:
+        src, out = src.unsqueeze(0), out.unsqueeze(0)
     kernels.copy4d(src, out)
 
 
@@ -206,10 +217,18 @@ def _kv_write_token_major(rt, variant, b, s, pc):
 
 
 @op("ExportSdpaProgram")
+def _sdpa(rt, variant, b, s, pc):
+    """ExportSdpaProgram: the masked variant (a `mask` field: the ASR encoder's windows) or the causal one."""
+    if "mask" in b:
+        _sdpa_masked(rt, variant, b, s, pc)
+    else:
+        _sdpa_causal(rt, variant, b, s, pc)
+
+
 def _sdpa_causal(rt, variant, b, s, pc):
     """Causal GQA attention, q [B,NH,T,D] over k/v [B,NK,S,D] from position 0 (sdpa_causal_f32.py:22-142)."""
     if "causal" not in variant.name:
-        raise NotImplementedError(f"{variant.name}: only causal ExportSdpaProgram variants are served")
+        raise NotImplementedError(f"{variant.name}: only causal or masked ExportSdpaProgram variants are served")
     q, k, v, out = b["q"], b["k"], b["v"], b["output"]
     B, NH, T, D = q.shape
     NK, S = k.shape[1], k.shape[2]
@@ -301,3 +320,48 @@ def _store(rt, variant, b, s, pc):
 
 def served_class_names() -> tuple[str, ...]:
     return tuple(sorted(OPS))
+
+
+# ------------------------------------------------------------ ASR audio encoder
+@op("ExportLinearBiasQ8_0WeightF32BiasProgram")
+def _linear_bias_q8(rt, variant, b, s, pc):
+    """y = x @ deq(W)^T + bias, Q8_0 weights (quantized_qwen3_asr linear_bias_q8_0w_f32b_f32.py:38-92)."""
+    kernels.linear_q8_0_bias(b["x"], b["weight"], b["bias"], int(s["N"]), out=b["output"])
+
+
+@op("ExportConv2dQ8_0WeightF32BiasProgram")
+def _conv2d_q8(rt, variant, b, s, pc):
+    """NCHW conv2d with Q8_0 weights and fp32 bias (conv2d_q8_0w_f32b_f16.py:36-98)."""
+    if pc["kh"] != pc["kw"] or pc["stride_h"] != pc["stride_w"] or pc["pad_h"] != pc["pad_w"]:
+        raise NotImplementedError(f"{variant.name}: non-square kernel, stride or padding")
+    out = b["output"]
+    y = kernels.conv2d_q8_0(b["x"], b["weight"], b["bias"], out.shape[1], kernel=int(pc["kh"]),
+                            stride=int(pc["stride_h"]), padding=int(pc["pad_h"]), out=out)
+    if tuple(y.shape) != tuple(out.shape):
+        raise ValueError(f"{variant.name}: output {tuple(out.shape)} does not match the convolution")
+
+
+@op("ExportGeluF32Program")
+def _gelu(rt, variant, b, s, pc):
+    """x * 0.5 * (1 + erf(x / sqrt 2)) (gelu_f32.py; its erf is a 1.5e-7 approximation of the same function)."""
+    kernels.gelu(b["x"], out=b["output"])
+
+
+@op("ExportLayerNormF32WeightF32BiasProgram")
+def _layer_norm(rt, variant, b, s, pc):
+    """Row LayerNorm, fp32 weight and bias (layer_norm_f32w_f32b_f32.py)."""
+    kernels.layer_norm(b["x"], b["weight"], b["bias"], float(pc["eps"]), out=b["output"])
+
+
+@op("ExportIndexSelectF32Program")
+def _index_select(rt, variant, b, s, pc):
+    """out[o, :] = x[index[o], :] (index_select_f32_*.py)."""
+    kernels.index_rows(b["x"], b["index"], out=b["output"])
+
+
+def _sdpa_masked(rt, variant, b, s, pc):
+    """softmax(q k^T / sqrt(D) + mask) v, non-causal, additive fp16 mask (sdpa_masked_f32.py:33-90)."""
+    q, k, v, mask, out = b["q"], b["k"], b["v"], b["mask"], b["output"]
+    if k.shape[1] != q.shape[1]:
+        raise NotImplementedError(f"{variant.name}: {q.shape[1]} query heads over {k.shape[1]} key heads")
+    kernels.attn_masked(q, k, v, mask, scale=float(q.shape[-1]) ** -0.5, out=out)

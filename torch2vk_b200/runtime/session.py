@@ -435,6 +435,27 @@ class RuntimeSession:
             self._drop(t)
         self._frame_tensors = []
 
+    def release_layer_workspace(self, layer_tensors: object, *, layer: str,
+                                keep: Sequence[LogicalTensor] = ()) -> None:
+        """Frees the frame-workspace activations of one layer before frame exit, except `keep` and the
+        tensors they alias (src/torch2vk/runtime/materialization.py:423-448)."""
+        self._require_open()
+        if not layer:
+            raise ValueError("release_layer_workspace requires a non-empty layer")
+        keep_ids = set()
+        for t in keep:
+            while t is not None:
+                keep_ids.add(id(t))
+                t = t.alias_source
+        for tensor in collect_named_logical_tensors(layer_tensors).values():
+            if id(tensor) in keep_ids or tensor.layer != layer or tensor.buffer is None:
+                continue
+            if tensor.role is not TensorRole.ACTIVATION or tensor.memory is not MemoryClass.FRAME_WORKSPACE:
+                continue
+            if tensor.lifetime is not TensorLifetime.FRAME:
+                continue
+            self._drop(tensor)
+
     def release_frame_workspace(self, tensor: LogicalTensor) -> None:
         """Frees a frame / op-scratch tensor (through its alias chain) before frame exit; other
         tensors are left alone (src/torch2vk/runtime/materialization.py:451-461)."""

@@ -328,7 +328,13 @@ QWEN3_TOKEN_STORE_EOS = _v(
 # Permutation (output dim i reads input dim PERM[i]) of each ExportTransposeProgram
 # variant; every transpose of the Qwen3 export swaps dims 1 and 2
 # (quantized_qwen3/shaders/transpose_f32_*.py index in the order c0, c2, c1, c3).
-TRANSPOSE_PERMUTATIONS: dict[str, tuple[int, int, int, int]] = {"transpose_f32": (0, 2, 1, 3)}
+TRANSPOSE_PERMUTATIONS: dict[str, tuple[int, ...]] = {
+    "transpose_f32": (0, 2, 1, 3),
+    # the Qwen3-ASR audio encoder's transposes (quantized_qwen3_asr/shaders/transpose_f32_*.py)
+    "transpose_f32_d95ce920ac": (0, 2, 1),
+    "transpose_f32_6a3397f037": (1, 0, 2),
+    "transpose_f32_48d16b9b88": (0, 2, 1, 3),
+}
 
 
 def all_variants() -> dict[str, ShaderVariant]:
