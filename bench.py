@@ -535,8 +535,7 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
 
-        big._graph = None  # graphs holding NCCL work go before the process group
-        del big
+        # the decode graphs (which hold NCCL work) were released before the ASR section
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
