@@ -1442,6 +1442,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
 constexpr int kM1SegX = 512 + 32 + 512 + 32;      // plane bytes (+ gaps)
 constexpr int kM1SegBytes = kM1SegX + 16 * 8;    // + meta
 constexpr int kM1MaxSegs = 16;                   // per warp (K <= 65536)
+constexpr int kM1XReg = 4;                       // segments whose x loads are issued together
 
 // x values [k0, k0 + 512) of a segment: lane l holds values 16 l .. 16 l + 15.
 __device__ __forceinline__ void m1_load_x(const QParams &p, int k0, int lane, float f[16]) {
@@ -1653,19 +1654,33 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     // this warp's x segments (the first one stays in registers); with a fused
     // RMSNorm the wpb warps of a group (which together hold every segment of
     // the row) add their sums of squares through shared memory (one CTA barrier)
-    float xf[16];
-    if (nsegw > 0) m1_load_x(p, seg0 * (kMmaSegBlocks * 256), lane, xf);
+    // every x load of this warp's first kM1XReg segments is issued before any is used: one
+    // round trip to L2 instead of one per segment (x was just written by the preceding kernel)
+    uint4 xr[kM1XReg][2];
+#pragma unroll
+    for (int j = 0; j < kM1XReg; ++j) {
+        if (j < nsegw) {
+            const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + (seg0 + j * p.wpb) * (kMmaSegBlocks * 256) + 16 * lane);
+            xr[j][0] = xv[0];
+            xr[j][1] = xv[1];
+        }
+    }
     float inv_rms = 1.0f;
     if (norm) {
         float ss = 0.0f;
-        for (int j = 0; j < nsegw; ++j) {
-            float f[16];
-            if (j == 0) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) f[e] = xf[e];
-            } else {
-                m1_load_x(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), lane, f);
+        for (int j = 0; j < kM1XReg; ++j) {
+            if (j < nsegw) {
+                float f[16];
+                unpack8(xr[j][0], f);
+                unpack8(xr[j][1], f + 8);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) ss = fmaf(f[e], f[e], ss);
             }
+        }
+        for (int j = kM1XReg; j < nsegw; ++j) {
+            float f[16];
+            m1_load_x(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), lane, f);
 #pragma unroll
             for (int e = 0; e < 16; ++e) ss = fmaf(f[e], f[e], ss);
         }
@@ -1677,29 +1692,34 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
         for (int w = group * p.wpb; w < (group + 1) * p.wpb; ++w) tot += sq[w];
         inv_rms = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
     }
-    for (int j = 0; j < nsegw; ++j) {
+    auto prep = [&](int j, float f[16]) {
         const int k0 = (seg0 + j * p.wpb) * (kMmaSegBlocks * 256);
-        float f[16], w[16];
-        if (j == 0) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                f[e] = xf[e];
-                w[e] = norm ? nw[e] : 1.0f;
-            }
-        } else {
-            m1_load_x(p, k0, lane, f);
-            if (norm) {
-                m1_load_norm(p, k0, lane, w);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) w[e] = 1.0f;
-            }
-        }
+        float w[16];
         if (norm) {
+            if (j == 0) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) w[e] = nw[e];
+            } else {
+                m1_load_norm(p, k0, lane, w);
+            }
 #pragma unroll
             for (int e = 0; e < 16; ++e) f[e] *= inv_rms * w[e];
         }
         m1_prepare_segment(f, xarea + j * kM1SegBytes, lane);
+    };
+#pragma unroll
+    for (int j = 0; j < kM1XReg; ++j) {
+        if (j < nsegw) {
+            float f[16];
+            unpack8(xr[j][0], f);
+            unpack8(xr[j][1], f + 8);
+            prep(j, f);
+        }
+    }
+    for (int j = kM1XReg; j < nsegw; ++j) {
+        float f[16];
+        m1_load_x(p, (seg0 + j * p.wpb) * (kMmaSegBlocks * 256), lane, f);
+        prep(j, f);
     }
     __syncwarp();
 
