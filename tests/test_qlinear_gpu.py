@@ -257,3 +257,37 @@ def test_q4k_gemm_cluster_split_k(oracle, m, n, k, swiglu):
         y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(), "q4_k", k)
     _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
     assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("n,k,mode", [(4096, 4096, "residual"), (2048, 4096, "swiglu"), (4096, 12288, "plain"),
+                                      (6144, 4096, "qkv"), (4000, 4096, "plain")])
+def test_m1_qwen3_8b_shapes(oracle, n, k, mode):
+    """M = 1 at Qwen3-8B sizes (8 warps split K of a 16-row block; K = 12288: three segments per warp;
+    a ragged last row block).  Bound as for every matvec: 2e-3 against the double-precision oracle."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(n + k)
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    xg = torch.from_numpy(x).cuda()
+    if mode == "swiglu":
+        pg = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+        pu = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+        g = oracle.matvec(pg, "q4_k", x).astype(np.float64)
+        u = oracle.matvec(pu, "q4_k", x).astype(np.float64)
+        ref = g / (1.0 + np.exp(-g)) * u
+        y = kernels.linear_swiglu(xg, torch.from_numpy(pg).cuda(), torch.from_numpy(pu).cuda(), "q4_k", k)
+        _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
+    elif mode == "qkv":
+        specs = [4096, 1024, 1024]
+        packed = [oracle.quantize(_weights(rng, r, k, special=False), "q4_k") for r in specs]
+        outs = kernels.linear_multi(xg, [(torch.from_numpy(p).cuda(), "q4_k") for p in packed], k)
+        for out, p in zip(outs, packed):
+            _tol_check(out.float().cpu().numpy(), oracle.matvec(p, "q4_k", x))
+    else:
+        packed = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+        res = rng.standard_normal((1, n)).astype(np.float16) if mode == "residual" else None
+        ref = oracle.matvec(packed, "q4_k", x) + (res.astype(np.float32) if res is not None else 0.0)
+        y = kernels.linear(xg, torch.from_numpy(packed).cuda(), "q4_k", k,
+                           residual=torch.from_numpy(res).cuda() if res is not None else None)
+        _tol_check(y.float().cpu().numpy(), ref)
+    assert kernels.device_status() == 0
