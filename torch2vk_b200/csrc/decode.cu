@@ -593,10 +593,11 @@ __global__ void __launch_bounds__(G * 32) attn_decode_fused_kernel(
 // The same work as attn_decode_fused_kernel for splits <= 8, on tensor cores:
 // the `splits` CTAs of one (batch b, kv head kh) form a thread-block cluster.
 // A CTA owns the cache positions [p0, p1) of its split and streams them as
-// 32-position tiles through a ring of shared-memory stages (cp.async; the
-// first kCaStages tiles, the RoPE angles and the norm weights are requested
-// before griddepcontrol.wait).  Its 4 warps take 4 tiles at a time; for its
-// tile a warp computes the scores of all G query heads of the KV head with
+// 32-position tiles, one shared-memory stage per warp: warp w takes tiles
+// w, w + 8, ... and loads them itself (cp.async; its first tile, the RoPE
+// angles and the norm weights are requested before griddepcontrol.wait), so
+// the tile loop has no CTA barrier and up to 256 positions per CTA (2048 per
+// cluster) take one pass.  For its tile a warp computes the scores of all G query heads of the KV head with
 // mma.m16n8k16 (positions as rows, heads as the 8 columns: S^T = K Q^T), runs
 // an online softmax per head, and accumulates O^T += V^T P^T (dims as rows;
 // P split into fp16 high and low parts so the product keeps fp32 accuracy).
@@ -606,11 +607,12 @@ __global__ void __launch_bounds__(G * 32) attn_decode_fused_kernel(
 // cluster barrier (release / acquire) then lets the combining CTAs finish.
 // No workspace, no atomics, no global round trip for the combine.
 constexpr int kCaTile = 32;
-constexpr int kCaStages = 8;
-constexpr int kCaWarps = 4;
+constexpr int kCaWarps = 8;
+constexpr int kCaStages = kCaWarps;  // one stage per warp
 constexpr int kCaMaxSplits = 8;
 constexpr int kCaRow = 136;  // halves per K / V row in shared memory (272 B: conflict-free ldmatrix rows)
 constexpr int kCaStageBytes = 2 * kCaTile * kCaRow * 2;
+static_assert(kCaStageBytes % 16 == 0 && kCaStageBytes >= 8 * 128 * 4, "a stage holds a warp's [8 heads][128] fp32 partial");
 constexpr int kCaSmem = kCaStages * kCaStageBytes;
 constexpr int kCaRecv = 132;  // floats per received partial: acc[128], max, sum
 
@@ -646,8 +648,9 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t r[4], const void *p) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(smem_u32(p)));
 }
+// not volatile: a pure register operation, so the compiler may interleave independent accumulator chains
 __device__ __forceinline__ void mma_f16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                  "{%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -681,8 +684,8 @@ __global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
     extern __shared__ __align__(128) uint8_t ca_smem[];
     __shared__ __align__(16) __half qs[8][D];                 // fp16 q rows (heads >= G stay zero)
     __shared__ __align__(16) __half pst[kCaWarps][2][8][40];  // P^T (hi, lo) per warp: [head][position], padded rows
-    __shared__ __align__(16) float wo[kCaWarps][8][D];        // per-warp acc
     __shared__ float wml[kCaWarps][8][2];                     // per-warp (max, sum)
+    __shared__ __align__(16) __half kvnew[2][D];              // the new position's k / v row (owner CTA)
     __shared__ __align__(16) float recv[16][kCaRecv];         // partials received for the heads this CTA combines
     const int sp = static_cast<int>(ca_cluster_rank());
     const int kh = (blockIdx.x / splits) % NK;
@@ -704,53 +707,57 @@ __global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
     const bool owner = p0 <= pos && pos < p1;
     const __half *kbase = kc + b * cb + kh * ch;
     const __half *vbase = vc + b * cb + kh * ch;
-    // tile `tile` of the range into stage tile % kCaStages (rows past p1 zero-filled); one commit group per call
+    // this warp's tile `tile` into its own stage (rows past p1 zero-filled), by its own 32 lanes
+    __half *const kst = reinterpret_cast<__half *>(ca_smem + w * kCaStageBytes);
+    __half *const vst = kst + kCaTile * kCaRow;
     auto issue = [&](int tile) {
-        if (tile < ntiles) {
-            __half *ks = reinterpret_cast<__half *>(ca_smem + (tile % kCaStages) * kCaStageBytes);
-            __half *vs = ks + kCaTile * kCaRow;
-            const int t0 = p0 + tile * kCaTile;
-            for (int i = threadIdx.x; i < kCaTile * 16; i += NT) {
-                const int r = i >> 4, c = i & 15;
-                const bool in = t0 + r < p1;
-                const int64_t src = (in ? static_cast<int64_t>(t0 + r) * cs : 0) + c * 8;
-                ca_cp16(ks + r * kCaRow + c * 8, kbase + src, in ? 16u : 0u);
-                ca_cp16(vs + r * kCaRow + c * 8, vbase + src, in ? 16u : 0u);
-            }
+        const int t0 = p0 + tile * kCaTile;
+#pragma unroll 4
+        for (int i = lane; i < kCaTile * 16; i += 32) {
+            const int r = i >> 4, c = i & 15;
+            const bool in = t0 + r < p1;
+            const int64_t src = (in ? static_cast<int64_t>(t0 + r) * cs : 0) + c * 8;
+            ca_cp16(kst + r * kCaRow + c * 8, kbase + src, in ? 16u : 0u);
+            ca_cp16(vst + r * kCaRow + c * 8, vbase + src, in ? 16u : 0u);
         }
         ca_commit();
     };
-#pragma unroll 1
-    for (int i = 0; i < kCaStages; ++i) issue(i);
-    float cw[E], sw[E], qw[E], kw[E];
+    // norm weights and RoPE frequencies are requested first but used only after the wait: the
+    // (possibly long, HBM-queued) latency of these loads does not delay reaching the wait
+    float fr[E], qw[E], kw[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        sincosf(static_cast<float>(pos) * inv_freq[(lane * E + e) & (D / 2 - 1)], &sw[e], &cw[e]);
+        fr[e] = inv_freq[(lane * E + e) & (D / 2 - 1)];
         qw[e] = q_w[lane * E + e];
         kw[e] = k_w[lane * E + e];
     }
+    if (w < ntiles) issue(w);
     for (int i = threadIdx.x; i < 8 * D / 2; i += NT) reinterpret_cast<uint32_t *>(qs)[i] = 0u;
     __syncthreads();
 
     pdl_wait();
     pdl_trigger();
+    float cw[E], sw[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) sincosf(static_cast<float>(pos) * fr[e], &sw[e], &cw[e]);
     for (int hh = w; hh < G; hh += kCaWarps) {
         float r[4];
         norm_rope_pre(*reinterpret_cast<const uint2 *>(q_in + b * q_sb + static_cast<int64_t>(kh * G + hh) * D + lane * E),
                       qw, cw, sw, eps, lane, r);
         *reinterpret_cast<uint2 *>(&qs[hh][lane * E]) = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
     }
-    uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
-    if (owner && w == 0) {
+    if (owner && w == kCaWarps - 1) {  // the last warp: G <= 4 leaves it free of query rows
         float r[4];
         norm_rope_pre(*reinterpret_cast<const uint2 *>(k_in + b * k_sb + static_cast<int64_t>(kh) * D + lane * E), kw, cw,
                       sw, eps, lane, r);
-        knew = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
-        vnew = *reinterpret_cast<const uint2 *>(v_in + b * v_sb + static_cast<int64_t>(kh) * D + lane * E);
+        const uint2 knew = f4_to_h4(make_float4(r[0], r[1], r[2], r[3]));
+        const uint2 vnew = *reinterpret_cast<const uint2 *>(v_in + b * v_sb + static_cast<int64_t>(kh) * D + lane * E);
         *reinterpret_cast<uint2 *>(kc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = knew;
         *reinterpret_cast<uint2 *>(vc + b * cb + static_cast<int64_t>(pos) * cs + kh * ch + lane * E) = vnew;
+        *reinterpret_cast<uint2 *>(&kvnew[0][lane * E]) = knew;
+        *reinterpret_cast<uint2 *>(&kvnew[1][lane * E]) = vnew;
     }
-    __syncthreads();  // q rows complete
+    __syncthreads();  // q rows (and the new k / v row) complete
     // B fragments of Q^T (k = dim, n = head) for the 8 k-steps of 16 dims
     uint32_t qb[8][2];
 #pragma unroll
@@ -765,36 +772,41 @@ __global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
 #pragma unroll
     for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
     const int new_tile = owner ? (pos - p0) / kCaTile : -1;
-    for (int round = 0; round * kCaWarps < ntiles; ++round) {
-        ca_wait<kCaStages - kCaWarps>();
-        __syncthreads();  // every thread's copies of this round's tiles have landed
-        if (new_tile >= round * kCaWarps && new_tile < (round + 1) * kCaWarps) {
-            // the tile of the new position was read before this kernel wrote that row
-            __half *ks = reinterpret_cast<__half *>(ca_smem + (new_tile % kCaStages) * kCaStageBytes);
+#pragma unroll 1
+    for (int tile = w; tile < ntiles; tile += kCaWarps) {
+        ca_wait<0>();
+        __syncwarp();  // every lane's copies of this tile have landed
+        if (tile == new_tile) {
+            // the new position's row may have been read before this kernel wrote it
             const int r = pos - p0 - new_tile * kCaTile;
-            if (w == 0) {
-                *reinterpret_cast<uint2 *>(ks + r * kCaRow + lane * E) = knew;
-                *reinterpret_cast<uint2 *>(ks + kCaTile * kCaRow + r * kCaRow + lane * E) = vnew;
-            }
-            __syncthreads();
+            *reinterpret_cast<uint2 *>(kst + r * kCaRow + lane * E) = *reinterpret_cast<const uint2 *>(&kvnew[0][lane * E]);
+            *reinterpret_cast<uint2 *>(vst + r * kCaRow + lane * E) = *reinterpret_cast<const uint2 *>(&kvnew[1][lane * E]);
+            __syncwarp();
         }
-        const int tile = round * kCaWarps + w;
-        if (tile < ntiles) {
-            const __half *ks = reinterpret_cast<const __half *>(ca_smem + (tile % kCaStages) * kCaStageBytes);
-            const __half *vs = ks + kCaTile * kCaRow;
+        {
+            const __half *ks = kst;
+            const __half *vs = vst;
             const int t0 = p0 + tile * kCaTile;
-            // S^T = K Q^T: rows = 32 positions (2 m-tiles), columns = 8 heads
-            float s[2][4];
+            // S^T = K Q^T: rows = 32 positions (2 m-tiles), columns = 8 heads; four independent
+            // accumulator chains (m-tile x even / odd k-step), summed at the end
+            float s[2][4], s2[2][4];
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.0f;
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int ks8 = 0; ks8 < 8; ++ks8) {
-                    uint32_t a[4];
-                    ldsm_x4(a, ks + (16 * mt + (lane & 15)) * kCaRow + 16 * ks8 + 8 * (lane >> 4));
-                    mma_f16_16816(s[mt], a, qb[ks8][0], qb[ks8][1]);
-                }
+                for (int e = 0; e < 4; ++e) s[mt][e] = s2[mt][e] = 0.0f;
+#pragma unroll
+            for (int ks8 = 0; ks8 < 8; ++ks8) {
+                uint32_t a[2][4];
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+                    ldsm_x4(a[mt], ks + (16 * mt + (lane & 15)) * kCaRow + 16 * ks8 + 8 * (lane >> 4));
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) mma_f16_16816((ks8 & 1) ? s2[mt] : s[mt], a[mt], qb[ks8][0], qb[ks8][1]);
             }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[mt][e] += s2[mt][e];
             // online softmax per head (columns 2t, 2t+1); rows g, g+8 of each m-tile
             float mx[2] = {-FLT_MAX, -FLT_MAX};
 #pragma unroll
@@ -845,21 +857,20 @@ __global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
                 const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&pst[w][1][g][16 * kk + 2 * t]);
                 const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(&pst[w][1][g][16 * kk + 2 * t + 8]);
                 const __half *vrow = vs + (16 * kk + (lane & 7) + 8 * (lane >> 4)) * kCaRow + 8 * ((lane >> 3) & 1);
+                // high parts over the 8 m-tiles, then the low parts: no back-to-back dependent pair
+                uint32_t a[8][4];
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
-                    uint32_t a[4];
-                    ldsm_x4_t(a, vrow + 16 * m);
-                    mma_f16_16816(o[m], a, bh0, bh1);
-                    mma_f16_16816(o[m], a, bl0, bl1);
+                    ldsm_x4_t(a[m], vrow + 16 * m);
+                    mma_f16_16816(o[m], a[m], bh0, bh1);
                 }
+#pragma unroll
+                for (int m = 0; m < 8; ++m) mma_f16_16816(o[m], a[m], bl0, bl1);
             }
-            __syncwarp();
+            __syncwarp();  // the stage is consumed before it is refilled
         }
-        __syncthreads();  // this round's stages are consumed before they are refilled
-#pragma unroll 1
-        for (int i = 0; i < kCaWarps; ++i) issue(round * kCaWarps + kCaStages + i);
+        if (tile + kCaWarps < ntiles) issue(tile + kCaWarps);
     }
-    ca_wait<0>();
     // merge the warps' states per head: (max, sum, acc)
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -873,46 +884,73 @@ __global__ void __launch_bounds__(kCaWarps * 32) attn_decode_cluster_kernel(
         wml[w][2 * t + 1][0] = m_run[1];
         wml[w][2 * t + 1][1] = l_run[1];
     }
+    // per-warp acc [8 heads][D] in the warp's own (consumed) stage
+    auto wo = [&](int v) { return reinterpret_cast<float(*)[D]>(ca_smem + v * kCaStageBytes); };
+    float(*const mine)[D] = wo(w);
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-        wo[w][2 * t][16 * m + g] = o[m][0];
-        wo[w][2 * t + 1][16 * m + g] = o[m][1];
-        wo[w][2 * t][16 * m + g + 8] = o[m][2];
-        wo[w][2 * t + 1][16 * m + g + 8] = o[m][3];
+        mine[2 * t][16 * m + g] = o[m][0];
+        mine[2 * t + 1][16 * m + g] = o[m][1];
+        mine[2 * t][16 * m + g + 8] = o[m][2];
+        mine[2 * t + 1][16 * m + g + 8] = o[m][3];
     }
     __syncthreads();
     if (splits > 1) ca_wait_acquire();  // (start barrier) every CTA of the cluster runs
-    const int d = threadIdx.x;  // NT == D: one dim per thread
-#pragma unroll 1
-    for (int hh = 0; hh < G; ++hh) {
-        float mx = -FLT_MAX;
+    static_assert(NT == 2 * D, "two threads per dim: the halves take alternate heads");
+    const int d = threadIdx.x & (D - 1), half = threadIdx.x >> 7;
+    constexpr int GH = (G + 1) / 2;  // heads per half
+    // every head's CTA partial from local shared memory first, then the remote stores in one burst
+    // (no local load waits behind a remote store)
+    float hmx[GH], hls[GH], ha[GH];
 #pragma unroll
-        for (int v = 0; v < kCaWarps; ++v) mx = fmaxf(mx, wml[v][hh][0]);
-        float lsum = 0.0f, a = 0.0f;
+    for (int j = 0; j < GH; ++j) {
+        const int hh = 2 * j + half;
+        hmx[j] = -FLT_MAX;
+        hls[j] = ha[j] = 0.0f;
+        if (hh < G) {
+            float mx = -FLT_MAX;
 #pragma unroll
-        for (int v = 0; v < kCaWarps; ++v) {
-            const float f = wml[v][hh][0] == -FLT_MAX ? 0.0f : exp2f(wml[v][hh][0] - mx);
-            lsum = fmaf(f, wml[v][hh][1], lsum);
-            a = fmaf(f, wo[v][hh][d], a);
+            for (int v = 0; v < kCaWarps; ++v) mx = fmaxf(mx, wml[v][hh][0]);
+            float lsum = 0.0f, a = 0.0f;
+#pragma unroll
+            for (int v = 0; v < kCaWarps; ++v) {
+                const float f = wml[v][hh][0] == -FLT_MAX ? 0.0f : exp2f(wml[v][hh][0] - mx);
+                lsum = fmaf(f, wml[v][hh][1], lsum);
+                a = fmaf(f, wo(v)[hh][d], a);
+            }
+            hmx[j] = mx;
+            hls[j] = lsum;
+            ha[j] = a;
         }
-        if (splits == 1) {
-            const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
-            out[b * o_sb + static_cast<int64_t>(kh * G + hh) * D + d] = __float2half_rn(a * inv);
-        } else {
+    }
+    if (splits == 1) {
+#pragma unroll
+        for (int j = 0; j < GH; ++j) {
+            const int hh = 2 * j + half;
+            if (hh < G) {
+                const float inv = hls[j] > 0.0f ? 1.0f / hls[j] : 0.0f;
+                out[b * o_sb + static_cast<int64_t>(kh * G + hh) * D + d] = __float2half_rn(ha[j] * inv);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < GH; ++j) {
+        const int hh = 2 * j + half;
+        if (hh < G) {
             // partial of head hh -> CTA hh % splits, slot (hh / splits) * splits + sp
             float *dst = &recv[(hh / splits) * splits + sp][0];
             const uint32_t rank = static_cast<uint32_t>(hh % splits);
-            ca_st_remote(dst + d, rank, a);
+            ca_st_remote(dst + d, rank, ha[j]);
             if (d == 0) {
-                ca_st_remote(dst + 128, rank, mx);
-                ca_st_remote(dst + 129, rank, lsum);
+                ca_st_remote(dst + 128, rank, hmx[j]);
+                ca_st_remote(dst + 129, rank, hls[j]);
             }
         }
     }
-    if (splits == 1) return;
     ca_arrive_release();
     ca_wait_acquire();  // every partial has arrived
-    for (int hh = sp; hh < G; hh += splits) {
+    for (int hh = sp + half * splits; hh < G; hh += 2 * splits) {
         const float *src = &recv[(hh / splits) * splits][0];
         float mx = -FLT_MAX;
         for (int q = 0; q < splits; ++q) mx = fmaxf(mx, src[q * kCaRecv + 128]);
