@@ -38,7 +38,7 @@ enum {
 };
 
 /* Weight block formats (GGUF ggml type ids). */
-enum { T2C_Q8_0 = 8, T2C_Q4_K = 12, T2C_Q6_K = 14, T2C_F16 = 1 };
+enum { T2C_Q8_0 = 8, T2C_Q4_K = 12, T2C_Q6_K = 14, T2C_F16 = 1, T2C_F32 = 0 };
 
 const char *t2c_last_error(void);
 int t2c_abi_version(void);
@@ -357,6 +357,65 @@ int t2c_attn_masked(const void *q, const void *k, const void *v, const void *mas
                     int64_t T, int64_t S, int64_t D, const int64_t *q_strides, const int64_t *k_strides,
                     const int64_t *v_strides, const int64_t *m_strides, const int64_t *o_strides, float scale,
                     void *stream);
+
+/* ------------------------------------------------------------------ fp32-activation prefill
+ * The optimized Qwen3 model's llama.cpp-style prefill chain keeps activations in
+ * fp32 between programs (src/models/optimized_qwen3/dispatch/text_layer.py:131-199).
+ */
+/* y fp32 [M, N] = x fp32 [M, K] @ deq(W)^T.  x is rounded to fp16 into the caller's
+ * scratch (t2c_linear_f32_scratch_bytes, 256-byte aligned) and multiplied on the
+ * tensor cores with fp32 accumulation; the reference multiplies fp16 operands
+ * with fp16 accumulation.  Replaces LlamaMatmulQ4KF32Program / LlamaMatmulQ6KF32Program
+ *   src/models/optimized_qwen3/shaders/llama_matmul_q4_k_f32.py:31-141
+ *   src/models/optimized_qwen3/shaders/llama_matmul_q6_k_f32.py */
+int64_t t2c_linear_f32_scratch_bytes(int64_t M, int64_t N, int64_t K);
+int t2c_linear_f32(int wtype, const float *x, const void *w, float *y, int64_t M, int64_t N, int64_t K, void *scratch,
+                   int64_t scratch_bytes, void *stream);
+/* y = x * rsqrt(mean(x^2) + eps) * w per row, fp32 (x, y [rows, H]; w [H]).  Replaces
+ * OptimizedQwen3RmsNormMulF32Program  src/models/optimized_qwen3/shaders/rms_norm_mul_f32.py */
+int t2c_rms_norm_f32(const float *x, const float *w, float *y, int64_t rows, int64_t H, float eps, void *stream);
+/* RMSNorm (w [D]) + rotate-half RoPE from fp16 cos / sin tables [B, T, D] of fp32
+ * x [B, T, G, D]; out [B, T, G, D] fp32 (out_f32 != 0) or fp16.  D = 64 or 128.
+ * Replaces OptimizedQwen3RmsNormRopeTokenF32Program / ...F32ToF16Program
+ *   src/models/optimized_qwen3/shaders/rms_norm_rope_token_f32.py:22
+ *   src/models/optimized_qwen3/shaders/rms_norm_rope_token_f32_to_f16.py */
+int t2c_rms_norm_rope_f32(const float *x, const float *w, const void *cos_t, const void *sin_t, void *out, int out_f32,
+                          int64_t B, int64_t T, int64_t G, int64_t D, float eps, void *stream);
+/* out = a + b (op 0) or silu(a) * b (op 1), fp32, n elements, 16-byte aligned.
+ * Replaces AddF32PrefillProgram (add_f32_prefill.py) and SwigluF32Program (swiglu_f32.py). */
+int t2c_binary_f32(int op, const float *a, const float *b, float *out, int64_t n, void *stream);
+/* y = x converted between T2C_F32 and T2C_F16 (n elements). */
+int t2c_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, void *stream);
+/* out[b, 0, :] = fp16(x[b, S - 1, :]).  Replaces SliceLastTokenF32ToF16Program
+ *   src/models/optimized_qwen3/shaders/slice_last_token_f32_to_f16.py */
+int t2c_slice_last_f32_to_f16(const float *x, void *out, int64_t B, int64_t S, int64_t H, void *stream);
+/* Token-major fp16 caches[i] [B, cache_lens[i], H, D] (1..3 of them) receive
+ * fp16(src[b, t, h, :]) at row positions[t] (int64); a cache too short for the row
+ * is skipped, as in the reference.  Replaces
+ * OptimizedQwen3TokenMajorValueCacheWriteF32ToF16{Pair,Triple}Program
+ *   src/models/optimized_qwen3/shaders/token_major_value_cache_write_f32_to_f16_pair.py */
+int t2c_value_cache_write_f32(const float *src, const int64_t *positions, int ncaches, void *const *caches,
+                              const int64_t *cache_lens, int64_t B, int64_t T, int64_t H, int64_t D, void *stream);
+/* Flash-attention mask classifier: out [row_blocks, words] uint32, 2 bits per
+ * (16-row, 64-column) block of the fp16 mask [T, S]: 1 = every value <= -FLT_MAX/2
+ * (or outside the mask), 2 = every value 0.  Replaces OptimizedQwen3FaMaskOptF16Program
+ *   src/models/optimized_qwen3/shaders/fa_mask_opt_f16.py */
+int t2c_fa_mask_opt(const void *mask, uint32_t *out, int64_t T, int64_t S, int64_t words, int64_t row_blocks,
+                    void *stream);
+/* softmax(q k^T * scale + mask) v over keys [0, S) of token-major fp16 caches
+ * [B, S, NK, D]; q and out fp32 token-major [B, T, NH, D]; mask fp16 [T, S]
+ * (row stride mask_row_stride); mask_opt (optional, from t2c_fa_mask_opt) lets a
+ * warp skip fully masked 64-key tiles.  D = 128, on the tensor cores.  Replaces
+ * LlamaFlashAttnF32F16F16Program
+ *   src/models/optimized_qwen3/shaders/llama_flash_attn_f32_f16_f16.py:35-158 */
+int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, const void *v_cache, const void *mask,
+                                const uint32_t *mask_opt, float *out, int64_t B, int64_t T, int64_t S, int64_t NH,
+                                int64_t NK, int64_t D, int64_t mask_row_stride, int64_t mask_opt_row_stride,
+                                float scale, void *stream);
+/* out fp32 [n_ids, H] = rows of a Q4_K embedding.  Replaces
+ * OptimizedQwen3EmbeddingQ4KActF32Program  src/models/optimized_qwen3/shaders/embedding_q4_k_act_f32.py */
+int t2c_embedding_f32(int wtype, const void *weight, const int64_t *ids, float *out, int64_t n_ids, int64_t vocab,
+                      int64_t H, void *stream);
 
 /* ------------------------------------------------------------------ tensor parallelism
  * One-shot all-reduce of fp16 tensors over NVLink peer memory (the two

@@ -170,3 +170,27 @@ def test_q4_k_m_rules_match_reference_source():
 
     for n in range(1, 65):
         assert ns["q4_k_m_more_bits_layer_indices"](n) == q4_k_m_more_bits_layer_indices(n)
+
+
+def test_fa_mask_opt_restatement_known_codes():
+    """Hand-built masks with known 2-bit codes (fa_mask_opt_f16.py: 1 = all <= -FLT_MAX/2 or outside
+    the mask, 2 = all zero, 0 = mixed), words stored [row_block][word]."""
+    from oracle import prefill32_ref as ref
+
+    m = np.zeros((20, 1100), np.float16)
+    m[:, 64:128] = -np.inf          # block 1: all masked
+    m[3, 200] = 1.0                 # block 3 of row block 0: mixed
+    m[16:, 256:320] = -np.inf       # block 4 of row block 1 only
+    codes = ref.fa_mask_opt(m)
+    assert codes.shape == (2, 2)
+
+    def code(rb, blk):
+        return (int(codes[rb, blk // 16]) >> (2 * (blk % 16))) & 3
+
+    assert [code(0, b) for b in range(6)] == [2, 1, 2, 0, 2, 2]
+    assert [code(1, b) for b in range(6)] == [2, 1, 2, 2, 1, 2]
+    assert code(0, 17) == 2 and code(0, 18) == 1            # 1100 columns: block 17 partial, 18 outside
+    assert all(code(1, b) == 1 for b in range(18, 32))
+    causal = ref.causal_mask(0, 32, 128)
+    c = ref.fa_mask_opt(causal)
+    assert (int(c[0, 0]) & 3) == 0 and ((int(c[0, 0]) >> 2) & 3) == 1   # diagonal block mixed, next masked

@@ -187,6 +187,92 @@ def test_reference_optimized_qwen3_decode_through_session(ref_modules):
         "LinearNobiasQ4QKQ6VMatvecProgram" in classes
 
 
+@needs_ref
+def test_reference_optimized_qwen3_prefill_through_session(ref_modules):
+    """The fp32-activation prefill chain (models/optimized_qwen3/run.py:394-445): full 512-token
+    chunk + tail chunk, embedding, mask classifier, every layer, the last layer's decode-shaped tail,
+    norm, LM head select and token store."""
+    from models.optimized_qwen3.dispatch.embed_tokens import run_prefill_full_embed, run_prefill_tail_embed
+    from models.optimized_qwen3.dispatch.text_layer import (
+        run_prefill_full_layer,
+        run_prefill_full_mask_opt,
+        run_prefill_tail_last_layer_tail,
+        run_prefill_tail_layer,
+        run_prefill_tail_mask_opt,
+    )
+    from models.optimized_qwen3.dispatch.text_norm import run_text_norm
+    from models.optimized_qwen3.shaders.lm_head_q6_k_argmax_partial_f16 import LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16
+    from models.optimized_qwen3.shaders.qwen3_token_select_reduce_chunks_f32 import (
+        QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32,
+    )
+    from models.optimized_qwen3.shaders.qwen3_token_select_reduce_f32 import QWEN3_TOKEN_SELECT_REDUCE_F32
+    from models.optimized_qwen3.shaders.qwen3_token_store_eos_f32 import QWEN3_TOKEN_STORE_EOS_F32
+    from models.optimized_qwen3.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+    from torch2vk.runtime.rope_table import ROPE_TABLE_F32
+
+    prompt, chunk = 520, 512
+    tail, attn_len, max_seq = prompt - chunk, 576, 704
+    mt = create_model_tensors(prompt_length=prompt, prefill_chunk_length=chunk, prefill_tail_length=tail,
+                              prefill_attention_length=attn_len, max_sequence_length=max_seq, num_hidden_layers=28,
+                              num_key_value_heads=8, head_dim=128, max_new_tokens=4, eos_token_count=1,
+                              vocab_size=151936)
+    rt = DrySession(mt)
+    rt.initialize_session_tensors({mt.eos_token_ids: np.array([151645], np.int64)})
+    caches = (mt.prefill_full_key_caches + mt.prefill_full_value_caches + mt.prefill_key_caches +
+              mt.prefill_value_caches + mt.decode_key_caches + mt.decode_value_caches)
+    state = {c: np.zeros(c.concrete_shape, np.float16) for c in caches}
+    state.update({mt.generated_tokens: np.zeros((1, 4), np.int64), mt.generated_length: np.zeros(1, np.uint32),
+                  mt.stopped: np.zeros(1, np.uint32)})
+    inputs = {
+        mt.prefill_full_input_ids.name: np.zeros((1, chunk), np.int64),
+        mt.prefill_full_causal_mask.name: np.zeros((chunk, chunk), np.float16),
+        mt.prefill_full_layers[0].cache_position.name: np.arange(chunk, dtype=np.int64),
+        mt.prefill_tail_input_ids.name: np.zeros((1, tail), np.int64),
+        mt.prefill_tail_causal_mask.name: np.zeros((tail, attn_len), np.float16),
+        mt.prefill_tail_layers[0].cache_position.name: np.arange(chunk, prompt, dtype=np.int64),
+    }
+    with rt.request(inputs=inputs, state=state):
+        with rt.frame("qwen3.prefill.full512"):
+            ROPE_TABLE_F32(rt, start_position=0, theta=1e6, cos=mt.prefill_full_rope.cos, sin=mt.prefill_full_rope.sin)
+            run_prefill_full_embed(rt)
+            run_prefill_full_mask_opt(rt)
+            for i in range(len(mt.prefill_full_layers)):
+                run_prefill_full_layer(rt, i)
+        with rt.frame("qwen3.prefill.tail"):
+            ROPE_TABLE_F32(rt, start_position=chunk, theta=1e6, cos=mt.prefill_tail_rope.cos,
+                           sin=mt.prefill_tail_rope.sin)
+            run_prefill_tail_embed(rt)
+            run_prefill_tail_mask_opt(rt)
+            for i in range(len(mt.prefill_tail_layers) - 1):
+                run_prefill_tail_layer(rt, i)
+            run_prefill_tail_last_layer_tail(rt)
+            run_text_norm(rt)
+            # models/optimized_qwen3/run.py:116-139 (_run_lm_head_select)
+            LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16(rt, x=mt.text_norm.mul_1, weight=mt.lm_head.p_weight,
+                                            partial_scores=mt.lm_head_partial_scores,
+                                            partial_tokens=mt.lm_head_partial_tokens)
+            QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32(rt, scores=mt.lm_head_partial_scores,
+                                                 tokens=mt.lm_head_partial_tokens,
+                                                 chunk_scores=mt.lm_head_chunk_scores,
+                                                 chunk_tokens=mt.lm_head_chunk_tokens)
+            QWEN3_TOKEN_SELECT_REDUCE_F32(rt, partial_scores=mt.lm_head_chunk_scores,
+                                          partial_tokens=mt.lm_head_chunk_tokens, eos_token_ids=mt.eos_token_ids,
+                                          next_token=mt.next_token, done=mt.done)
+            QWEN3_TOKEN_STORE_EOS_F32(rt, next_token=mt.next_token, token_index=0, done=mt.done,
+                                      generated_tokens=mt.generated_tokens, generated_length=mt.generated_length,
+                                      stopped=mt.stopped)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    for needed in ("LlamaMatmulQ4KF32Program", "LlamaFlashAttnF32F16F16Program", "OptimizedQwen3FaMaskOptF16Program",
+                   "OptimizedQwen3RmsNormRopeTokenF32Program", "OptimizedQwen3TokenMajorValueCacheWriteF32ToF16PairProgram",
+                   "SwigluF32Program", "AddF32PrefillProgram", "SliceLastTokenF32ToF16Program",
+                   "OptimizedQwen3EmbeddingQ4KActF32Program"):
+        assert needed in classes, needed
+    fa = [c for c in rt.calls if c[1] == "LlamaFlashAttnF32F16F16Program"]
+    assert len(fa) == 56 and {c[2]["T"] for c in fa} == {chunk, tail}
+
+
 # ---------------------------------------------------------------- validation errors
 def _tensors():
     from torch2vk_b200.runtime.logical import LogicalTensor, MemoryClass, TensorLifetime, TensorRole

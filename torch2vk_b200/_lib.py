@@ -25,6 +25,7 @@ Q8_0 = 8
 Q4_K = 12
 Q6_K = 14
 F16 = 1
+F32 = 0
 WTYPE_BY_NAME = {"q8_0": Q8_0, "q4_k": Q4_K, "q6_k": Q6_K, "f16": F16}
 
 _c = ctypes
@@ -79,9 +80,20 @@ _SIGNATURES: dict[str, list] = {
     "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],
     "t2c_advance_positions": [_vp, _i64, _vp, _vp],
     "t2c_attn_decode_static": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "t2c_linear_f32_scratch_bytes": [_i64, _i64, _i64],
+    "t2c_linear_f32": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp],
+    "t2c_rms_norm_f32": [_vp, _vp, _vp, _i64, _i64, _f32, _vp],
+    "t2c_rms_norm_rope_f32": [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _f32, _vp],
+    "t2c_binary_f32": [_i32, _vp, _vp, _vp, _i64, _vp],
+    "t2c_cast": [_vp, _i32, _vp, _i32, _i64, _vp],
+    "t2c_slice_last_f32_to_f16": [_vp, _vp, _i64, _i64, _i64, _vp],
+    "t2c_value_cache_write_f32": [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "t2c_fa_mask_opt": [_vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "t2c_attn_prefill_masked_f32": [_vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 8 + [_f32, _vp],
+    "t2c_embedding_f32": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
 }
 _RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64,
-             "t2c_allreduce_buffer_bytes": _c.c_int64}
+             "t2c_allreduce_buffer_bytes": _c.c_int64, "t2c_linear_f32_scratch_bytes": _c.c_int64}
 
 
 class T2CError(RuntimeError):

@@ -1089,11 +1089,18 @@ constexpr int kPtRow = 136;  // halves per shared-memory row (272 B)
 constexpr int kPtStageBytes = 2 * kPtK * kPtRow * 2;
 constexpr int kPtSmem = kPtQ * kPtRow * 2 + kPtStages * kPtStageBytes;
 
+// EXT = the llama.cpp-style program (llama_flash_attn_f32_f16_f16): fp32 q and output, keys
+// [0, S) of the cache with an explicit additive fp16 mask [T, S] instead of the causal rule, and
+// the mask classifier's 2-bit codes per (16-row block, 64-key tile): 1 = all masked (the warp
+// skips the tile), 2 = all zero (no mask values read).
+template <bool EXT>
 __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
-    const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
-    __half *__restrict__ out, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
-    int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh, float scale_log2) {
+    const void *__restrict__ qv, const __half *__restrict__ kc, const __half *__restrict__ vc,
+    void *__restrict__ outv, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
+    int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh, float scale_log2,
+    const __half *__restrict__ mask, int64_t m_st, const uint32_t *__restrict__ mopt, int64_t mo_st, int S) {
     extern __shared__ __align__(128) uint8_t pt_smem[];
+    __shared__ int s_nkt;
     __half *qs = reinterpret_cast<__half *>(pt_smem);
     const int qtiles = (T + kPtQ - 1) / kPtQ;
     const int qt = qtiles - 1 - static_cast<int>(blockIdx.x % qtiles);
@@ -1104,10 +1111,28 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
     const int g = lane >> 2, t4 = lane & 3;
     pdl_wait();
     pdl_trigger();
-    const int base = positions[b];
+    const int base = EXT ? 0 : positions[b];
     const int q0 = qt * kPtQ;
-    const int last_key = base + min(T - 1, q0 + kPtQ - 1);
-    const int nkt = last_key / kPtK + 1;
+    const int last_key = EXT ? S - 1 : base + min(T - 1, q0 + kPtQ - 1);
+    const int rb = (q0 >> 4) + w;  // this warp's 16-row block (mask classifier rows)
+    auto code_of = [&](int kt) -> uint32_t {
+        return (mopt[rb * mo_st + (kt >> 4)] >> (2 * (kt & 15))) & 3u;
+    };
+    int nkt = last_key / kPtK + 1;
+    if (EXT && mopt != nullptr) {
+        // the CTA stops after the last key tile that some warp's rows do not mask entirely
+        if (threadIdx.x == 0) s_nkt = 0;
+        __syncthreads();
+        int last = -1;
+        if (rb * 16 < T)
+            for (int kt = lane; kt < nkt; kt += 32)
+                if (code_of(kt) != 1u) last = kt;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+        if (lane == 0) atomicMax(&s_nkt, last + 1);
+        __syncthreads();
+        nkt = s_nkt;
+    }
     const __half *kbase = kc + b * cb + kh * ch;
     const __half *vbase = vc + b * cb + kh * ch;
     auto issue = [&](int kt) {
@@ -1127,12 +1152,24 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
     };
     issue(0);
     issue(1);
-    // q tile -> shared memory (rows past T zero)
+    // q tile -> shared memory (rows past T zero; fp32 q rounded to fp16)
     for (int i = threadIdx.x; i < kPtQ * 16; i += 128) {
         const int r = i >> 4, c = i & 15;
         const int tq = q0 + r;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (tq < T) v = *reinterpret_cast<const uint4 *>(q + b * q_sb + tq * q_st + h * q_sh + c * 8);
+        if (tq < T) {
+            const int64_t off = b * q_sb + tq * q_st + h * q_sh + c * 8;
+            if (EXT) {
+                const float4 a = *reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + off);
+                const float4 c4 = *reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + off + 4);
+                const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+                const __half2 h2 = __floats2half2_rn(c4.x, c4.y), h3 = __floats2half2_rn(c4.z, c4.w);
+                v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                               *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            } else {
+                v = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(qv) + off);
+            }
+        }
         *reinterpret_cast<uint4 *>(qs + r * kPtRow + c * 8) = v;
     }
     __syncthreads();
@@ -1154,7 +1191,9 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
         const __half *ks = reinterpret_cast<const __half *>(pt_smem + kPtQ * kPtRow * 2 + (kt % kPtStages) * kPtStageBytes);
         const __half *vs = ks + kPtK * kPtRow;
         const int k0 = kt * kPtK;
-        if (k0 <= base + q0 + 16 * w + 15) {  // some key of the tile is visible to some row of the warp
+        const uint32_t code = (EXT && mopt != nullptr && rb * 16 < T) ? code_of(kt) : 0u;
+        // some key of the tile is visible to some row of the warp
+        if (EXT ? (code != 1u && rb * 16 < T) : (k0 <= base + q0 + 16 * w + 15)) {
             float s[8][4];
 #pragma unroll
             for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
@@ -1177,7 +1216,17 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
                     const int key = k0 + 8 * n + 2 * t4 + (e & 1);
                     const int r = e >> 1;
                     float v = s[n][e] * scale_log2;
-                    if (masked && key > (r ? qp1 : qp0)) v = -FLT_MAX;
+                    if (EXT) {
+                        if (key >= S) {
+                            v = -FLT_MAX;
+                        } else if (code != 2u) {
+                            const int tq = min(r ? tq1 : tq0, T - 1);
+                            const float mv = __half2float(mask[tq * m_st + key]);
+                            v = mv <= -1.7014117e38f ? -FLT_MAX : fmaf(mv, 1.4426950408889634f, v);
+                        }
+                    } else if (masked && key > (r ? qp1 : qp0)) {
+                        v = -FLT_MAX;
+                    }
                     s[n][e] = v;
                     mx[r] = fmaxf(mx[r], v);
                 }
@@ -1247,12 +1296,16 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
         const int d = 8 * n + 2 * t4;
-        if (tq0 < T)
-            *reinterpret_cast<__half2 *>(out + b * o_sb + tq0 * o_st + h * o_sh + d) =
-                __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
-        if (tq1 < T)
-            *reinterpret_cast<__half2 *>(out + b * o_sb + tq1 * o_st + h * o_sh + d) =
-                __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+        const int64_t o0 = b * o_sb + tq0 * o_st + h * o_sh + d, o1 = b * o_sb + tq1 * o_st + h * o_sh + d;
+        if (EXT) {
+            float *out = static_cast<float *>(outv);
+            if (tq0 < T) *reinterpret_cast<float2 *>(out + o0) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+            if (tq1 < T) *reinterpret_cast<float2 *>(out + o1) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
+        } else {
+            __half *out = static_cast<__half *>(outv);
+            if (tq0 < T) *reinterpret_cast<__half2 *>(out + o0) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+            if (tq1 < T) *reinterpret_cast<__half2 *>(out + o1) = __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+        }
     }
 }
 
@@ -1274,8 +1327,9 @@ __global__ void embedding_f16_kernel(const __half *__restrict__ w, const int64_t
 }
 
 // Q4_K row decode (embedding_q4_k_f32.py:96-110): w = (d * sc) * q - dmin * m.
+template <typename OT>
 __global__ void embedding_q4k_kernel(const uint8_t *__restrict__ w, const int64_t *__restrict__ ids,
-                                     __half *__restrict__ out, int64_t n_ids, int64_t vocab, int H) {
+                                     OT *__restrict__ out, int64_t n_ids, int64_t vocab, int H) {
     const int64_t row = blockIdx.x;
     if (row >= n_ids) return;
     pdl_wait();
@@ -1301,7 +1355,7 @@ __global__ void embedding_q4k_kernel(const uint8_t *__restrict__ w, const int64_
         }
         const uint8_t byte = blk[16 + (i >> 6) * 32 + (i & 31)];
         const uint32_t qv = (i & 32) ? (byte >> 4) : (byte & 15u);
-        out[row * H + k] = __float2half_rn((d * static_cast<float>(sc)) * static_cast<float>(qv) - dmin * static_cast<float>(m));
+        out[row * H + k] = static_cast<OT>((d * static_cast<float>(sc)) * static_cast<float>(qv) - dmin * static_cast<float>(m));
     }
 }
 
@@ -1661,17 +1715,18 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
         static bool configured[64] = {};
         const int dev_slot = current_device_slot();
         if (!configured[dev_slot]) {
-            if (cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem) !=
+            if (cudaFuncSetAttribute(attn_prefill_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem) !=
                 cudaSuccess)
                 return set_error(T2C_ECUDA, "attn_prefill: cudaFuncSetAttribute failed");
             configured[dev_slot] = true;
         }
         const int64_t tiles = (T + kPtQ - 1) / kPtQ;
-        return launch(attn_prefill_tc_kernel, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128), kPtSmem,
-                      as_stream(stream), static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
-                      static_cast<const __half *>(v_cache), static_cast<__half *>(out), positions, static_cast<int>(T),
+        return launch(attn_prefill_tc_kernel<false>, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128), kPtSmem,
+                      as_stream(stream), q, static_cast<const __half *>(k_cache),
+                      static_cast<const __half *>(v_cache), out, positions, static_cast<int>(T),
                       static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh,
-                      1.4426950408889634f * scale);
+                      1.4426950408889634f * scale, static_cast<const __half *>(nullptr), int64_t{0},
+                      static_cast<const uint32_t *>(nullptr), int64_t{0}, 0);
     }
     const int64_t qtiles = (T + kPfQ - 1) / kPfQ;
     const dim3 grid(static_cast<unsigned>(B * NH * qtiles)), block(128);
@@ -1689,6 +1744,38 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
     return set_error(T2C_EUNSUPPORTED, "attn_prefill: D=%lld", (long long)D);
 }
 
+extern "C" int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, const void *v_cache, const void *mask,
+                                           const uint32_t *mask_opt, float *out, int64_t B, int64_t T, int64_t S,
+                                           int64_t NH, int64_t NK, int64_t D, int64_t mask_row_stride,
+                                           int64_t mask_opt_row_stride, float scale, void *stream) {
+    if (!q || !k_cache || !v_cache || !mask || !out) return set_error(T2C_EINVAL, "attn_prefill_masked_f32: NULL pointer");
+    if (B <= 0 || T <= 0 || S <= 0 || NH <= 0 || NK <= 0 || NH % NK || T > INT32_MAX || S > INT32_MAX ||
+        mask_row_stride < S)
+        return set_error(T2C_EINVAL, "attn_prefill_masked_f32: bad shape");
+    if (D != 128) return set_error(T2C_EUNSUPPORTED, "attn_prefill_masked_f32: D=%lld (128 only)", (long long)D);
+    if (!aligned(q, 16) || !aligned(out, 8) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
+        return set_error(T2C_EINVAL, "attn_prefill_masked_f32: alignment");
+    if (mask_opt != nullptr && mask_opt_row_stride < (S + 1023) / 1024)
+        return set_error(T2C_EINVAL, "attn_prefill_masked_f32: mask_opt rows need %lld words", (long long)((S + 1023) / 1024));
+    static bool configured[64] = {};
+    const int dev_slot = current_device_slot();
+    if (!configured[dev_slot]) {
+        if (cudaFuncSetAttribute(attn_prefill_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem) !=
+            cudaSuccess)
+            return set_error(T2C_ECUDA, "attn_prefill_masked_f32: cudaFuncSetAttribute failed");
+        configured[dev_slot] = true;
+    }
+    // token-major q / out [B, T, NH, D] and caches [B, S, NK, D]
+    const int64_t tiles = (T + kPtQ - 1) / kPtQ;
+    return launch(attn_prefill_tc_kernel<true>, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128), kPtSmem,
+                  as_stream(stream), static_cast<const void *>(q), static_cast<const __half *>(k_cache),
+                  static_cast<const __half *>(v_cache), static_cast<void *>(out),
+                  static_cast<const int32_t *>(nullptr), static_cast<int>(T), static_cast<int>(NH),
+                  static_cast<int>(NK), S * NK * D, NK * D, D, T * NH * D, NH * D, D, T * NH * D, NH * D, D,
+                  1.4426950408889634f * scale, static_cast<const __half *>(mask), mask_row_stride, mask_opt,
+                  mask_opt_row_stride, static_cast<int>(S));
+}
+
 extern "C" int t2c_embedding(int wtype, const void *weight, const int64_t *ids, void *out, int64_t n_ids,
                              int64_t vocab, int64_t H, void *stream) {
     if (!weight || !ids || !out) return set_error(T2C_EINVAL, "embedding: NULL pointer");
@@ -1702,11 +1789,21 @@ extern "C" int t2c_embedding(int wtype, const void *weight, const int64_t *ids, 
     }
     if (wtype == T2C_Q4_K) {
         if (H % 256) return set_error(T2C_EINVAL, "embedding: Q4_K needs H %% 256 == 0");
-        return launch(embedding_q4k_kernel, dim3(static_cast<unsigned>(n_ids)), dim3(256), 0, s,
+        return launch(embedding_q4k_kernel<__half>, dim3(static_cast<unsigned>(n_ids)), dim3(256), 0, s,
                       static_cast<const uint8_t *>(weight), ids, static_cast<__half *>(out), n_ids, vocab,
                       static_cast<int>(H));
     }
     return set_error(T2C_EUNSUPPORTED, "embedding: weight type %d", wtype);
+}
+
+extern "C" int t2c_embedding_f32(int wtype, const void *weight, const int64_t *ids, float *out, int64_t n_ids,
+                                 int64_t vocab, int64_t H, void *stream) {
+    if (!weight || !ids || !out) return set_error(T2C_EINVAL, "embedding_f32: NULL pointer");
+    if (n_ids <= 0 || vocab <= 0 || H <= 0 || H > INT32_MAX) return set_error(T2C_EINVAL, "embedding_f32: bad shape");
+    if (wtype != T2C_Q4_K) return set_error(T2C_EUNSUPPORTED, "embedding_f32: weight type %d", wtype);
+    if (H % 256) return set_error(T2C_EINVAL, "embedding_f32: Q4_K needs H %% 256 == 0");
+    return launch(embedding_q4k_kernel<float>, dim3(static_cast<unsigned>(n_ids)), dim3(256), 0, as_stream(stream),
+                  static_cast<const uint8_t *>(weight), ids, out, n_ids, vocab, static_cast<int>(H));
 }
 
 extern "C" int t2c_add(const void *x, const void *r, void *y, int64_t n, void *stream) {

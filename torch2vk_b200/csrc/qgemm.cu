@@ -66,6 +66,7 @@ struct GemmParams {
     alignas(64) CUtensorMap umap;     // up weight (SwiGLU)
     alignas(64) CUtensorMap xmap;     // x fp16 [M, K], box 64 x mt, 128-byte swizzle
     __half *y[3];
+    float *yf[3];                     // fp32 outputs instead of y (non-null), plain linear only
     const __half *res[3];
     int64_t Nw[3];
     int tile0[4];                     // first row tile of each weight (tile0[nw] = all row tiles)
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
     const int64_t n0 = static_cast<int64_t>(tile - p.tile0[wi]) * kRowsT;
     const CUtensorMap *wmap = &p.wmap[wi];
     __half *const yout = p.y[wi];
+    float *const youtf = p.yf[wi];
     const __half *const res = p.res[wi];
     const int64_t N = p.Nw[wi];
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * mt;
@@ -462,7 +464,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                         } else if (res != nullptr) {
                             v += __half2float(res[o]);
                         }
-                        yout[o] = __float2half_rn(v);
+                        if (youtf != nullptr)
+                            youtf[o] = v;
+                        else
+                            yout[o] = __float2half_rn(v);
                     }
                 }
             }
@@ -519,7 +524,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                     } else if (res != nullptr) {
                         v += __half2float(res[o]);
                     }
-                    yout[o] = __float2half_rn(v);
+                    if (youtf != nullptr)
+                        youtf[o] = v;
+                    else
+                        yout[o] = __float2half_rn(v);
                 }
             }
         }
@@ -597,6 +605,7 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
         row_tiles += (a.N[i] + kRowsT - 1) / kRowsT;
         p.Nw[i] = a.N[i];
         p.y[i] = a.y[i];
+        p.yf[i] = a.yf[i];
         p.res[i] = a.res[i];
     }
     p.tile0[a.nw] = static_cast<int>(row_tiles);

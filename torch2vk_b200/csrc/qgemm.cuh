@@ -18,6 +18,7 @@ struct QGemmArgs {
     int64_t N[3], K, M;
     const __half *x;       // [M, K], 16-byte aligned rows
     __half *y[3];          // [M, N[i]]
+    float *yf[3];          // fp32 [M, N[i]] written instead of y[i] when non-null (no residual / SwiGLU)
     const __half *res[3];  // [M, N[i]] or nullptr
     float *ps;             // argmax mode (LM head): best (score, row) per 4 rows [M, G], else nullptr
     uint32_t *pt;

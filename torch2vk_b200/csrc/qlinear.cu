@@ -2370,3 +2370,41 @@ extern "C" int t2c_lm_head_argmax(int wtype, const void *x, const void *w, float
     p.G = (N + 3) / 4;
     return run_linear(p, M, as_stream(stream));
 }
+
+extern "C" int64_t t2c_linear_f32_scratch_bytes(int64_t M, int64_t N, int64_t K) {
+    return (M * K * 2 + 255) / 256 * 256 + M * N * 2;
+}
+
+extern "C" int t2c_linear_f32(int wtype, const float *x, const void *w, float *y, int64_t M, int64_t N, int64_t K,
+                              void *scratch, int64_t scratch_bytes, void *stream) {
+    int rc = validate_common(M, K, x);
+    if (rc) return rc;
+    if ((rc = validate_weight(wtype, w, K))) return rc;
+    if (y == nullptr || N <= 0) return set_error(T2C_EINVAL, "linear_f32: bad output or N");
+    if (scratch == nullptr || reinterpret_cast<uintptr_t>(scratch) % 256 ||
+        scratch_bytes < t2c_linear_f32_scratch_bytes(M, N, K))
+        return set_error(T2C_ESCRATCH, "linear_f32: scratch needs %lld bytes (256-byte aligned)",
+                         (long long)t2c_linear_f32_scratch_bytes(M, N, K));
+    // x rounded to fp16 (the reference's cooperative-matrix operands are fp16 as well)
+    __half *x16 = static_cast<__half *>(scratch);
+    __half *y16 = reinterpret_cast<__half *>(static_cast<uint8_t *>(scratch) + (M * K * 2 + 255) / 256 * 256);
+    if ((rc = t2c_cast(x, T2C_F32, x16, T2C_F16, M * K, stream))) return rc;
+    const cudaStream_t s = as_stream(stream);
+    if (!mma_disabled() && M > 4 && (wtype == T2C_Q4_K || (wtype == T2C_Q6_K && K % 2048 == 0))) {
+        // tensor-core GEMM writing fp32 directly from the TMEM accumulators
+        QGemmArgs a = {};
+        a.fmt = wtype;
+        a.nw = 1;
+        a.w[0] = static_cast<const uint8_t *>(w);
+        a.N[0] = N;
+        a.K = K;
+        a.M = M;
+        a.x = x16;
+        a.yf[0] = y;
+        rc = qgemm(a, s);
+        if (rc != T2C_EUNSUPPORTED) return rc;
+    }
+    // other shapes: the fp16 kernels, then widen
+    if ((rc = t2c_linear(wtype, x16, w, nullptr, y16, M, N, K, stream))) return rc;
+    return t2c_cast(y16, T2C_F16, y, T2C_F32, M * N, stream);
+}

@@ -99,10 +99,10 @@ __global__ void rope_table_kernel(__half *__restrict__ cos_out, __half *__restri
 // One warp per (b, t, g) row of D values: RMSNorm with fp32 weight, then
 // rotate-half RoPE with fp16 cos/sin tables [B, T, D]; output addressed by
 // strides (b, g, t) so head-major [B, G, T, D] or token-major layouts work.
-template <int E>
-__global__ void rms_norm_rope_kernel(const __half *__restrict__ x, const float *__restrict__ w,
+template <int E, typename XT = __half, typename OT = __half>
+__global__ void rms_norm_rope_kernel(const XT *__restrict__ x, const float *__restrict__ w,
                                      const __half *__restrict__ cos_t, const __half *__restrict__ sin_t,
-                                     __half *__restrict__ out, int B, int T, int G, int64_t ob, int64_t og,
+                                     OT *__restrict__ out, int B, int T, int G, int64_t ob, int64_t og,
                                      int64_t ot, float eps) {
     constexpr int D = E * 32;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -118,7 +118,7 @@ __global__ void rms_norm_rope_kernel(const __half *__restrict__ x, const float *
     float ss = 0.0f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        v[e] = __half2float(x[row * D + d0 + e]);
+        v[e] = static_cast<float>(x[row * D + d0 + e]);
         ss += v[e] * v[e];
     }
     ss = warp_sum(ss);
@@ -126,13 +126,174 @@ __global__ void rms_norm_rope_kernel(const __half *__restrict__ x, const float *
 #pragma unroll
     for (int e = 0; e < E; ++e) v[e] = v[e] * inv * w[d0 + e];
     const int64_t trow = (static_cast<int64_t>(b) * T + t) * D;
-    __half *o = out + b * ob + g * og + t * ot;
+    OT *o = out + b * ob + g * og + t * ot;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
         const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
         const float c = __half2float(cos_t[trow + d0 + e]), s = __half2float(sin_t[trow + d0 + e]);
-        o[d0 + e] = __float2half_rn(lane < 16 ? v[e] * c - partner * s : v[e] * c + partner * s);
+        o[d0 + e] = static_cast<OT>(lane < 16 ? v[e] * c - partner * s : v[e] * c + partner * s);
     }
+}
+
+// ------------------------------------------- fp32-activation prefill programs
+// y = x * rsqrt(mean(x^2) + eps) * w, fp32 in and out, one CTA of 256 threads per row
+// (rms_norm_mul_f32.py: fp32 sum of squares, fp32 output).
+__global__ void rms_norm_f32_kernel(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ y,
+                                    int H, float eps) {
+    __shared__ float part[8];
+    pdl_wait();
+    pdl_trigger();
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
+    const bool vec = (H % 4) == 0;
+    float ss = 0.0f;
+    if (vec) {
+        for (int h = threadIdx.x * 4; h < H; h += 1024) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + base + h);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+    } else {
+        for (int h = threadIdx.x; h < H; h += 256) ss = fmaf(x[base + h], x[base + h], ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) total += part[i];
+    const float inv = rsqrtf(total / static_cast<float>(H) + eps);
+    if (vec) {
+        for (int h = threadIdx.x * 4; h < H; h += 1024) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + base + h);
+            const float4 g = *reinterpret_cast<const float4 *>(w + h);
+            *reinterpret_cast<float4 *>(y + base + h) = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+        }
+    } else {
+        for (int h = threadIdx.x; h < H; h += 256) y[base + h] = x[base + h] * inv * w[h];
+    }
+}
+
+enum { BIN_ADD = 0, BIN_SWIGLU = 1 };
+
+// out = a + b, or silu(a) * b (= a / (1 + exp(-a)) * b), fp32, 4 values per thread
+__global__ void binary_f32_kernel(int op, const float *__restrict__ a, const float *__restrict__ b,
+                                  float *__restrict__ out, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
+    for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
+        if (i + 4 <= n) {
+            const float4 x = *reinterpret_cast<const float4 *>(a + i);
+            const float4 y = *reinterpret_cast<const float4 *>(b + i);
+            float4 r;
+            if (op == BIN_ADD) {
+                r = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+            } else {
+                r = make_float4(x.x / (1.0f + expf(-x.x)) * y.x, x.y / (1.0f + expf(-x.y)) * y.y,
+                                x.z / (1.0f + expf(-x.z)) * y.z, x.w / (1.0f + expf(-x.w)) * y.w);
+            }
+            *reinterpret_cast<float4 *>(out + i) = r;
+        } else {
+            for (int64_t j = i; j < n; ++j)
+                out[j] = op == BIN_ADD ? a[j] + b[j] : a[j] / (1.0f + expf(-a[j])) * b[j];
+        }
+    }
+}
+
+template <typename S, typename D>
+__global__ void cast_kernel(const S *__restrict__ x, D *__restrict__ y, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = static_cast<D>(static_cast<float>(x[i]));
+}
+
+// out[b, 0, h] = fp16(x[b, S - 1, h])
+__global__ void slice_last_f32_kernel(const float *__restrict__ x, __half *__restrict__ out, int B, int64_t S, int H) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t total = static_cast<int64_t>(B) * H;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / H, h = i % H;
+        out[i] = __float2half_rn(x[(b * S + (S - 1)) * H + h]);
+    }
+}
+
+// Token-major value caches [B, S_c, H, D] (up to 3) receive fp16(src[b, t, h, d]) at row
+// positions[t]; a cache whose extent S_c does not reach that row is skipped (as the reference).
+struct CacheSet {
+    __half *c[3];
+    int64_t S[3];
+    int n;
+};
+__global__ void value_cache_write_f32_kernel(const float *__restrict__ src, const int64_t *__restrict__ positions,
+                                             CacheSet cs, int B, int T, int H, int D) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t total = static_cast<int64_t>(B) * T * H * D;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t r = i;
+        const int d = static_cast<int>(r % D);
+        r /= D;
+        const int h = static_cast<int>(r % H);
+        r /= H;
+        const int t = static_cast<int>(r % T);
+        const int64_t b = r / T;
+        const int64_t pos = positions[t];
+        const __half v = __float2half_rn(src[i]);
+        for (int k = 0; k < cs.n; ++k)
+            if (pos >= 0 && pos < cs.S[k]) cs.c[k][((b * cs.S[k] + pos) * H + h) * D + d] = v;
+    }
+}
+
+// Flash-attention mask classifier (fa_mask_opt_f16.py): for the 16 blocks of 16 rows x 64
+// columns that output word (row block r, word w) covers, 2 bits each: 1 = every value
+// <= -FLT_MAX / 2 (or the block lies outside the mask), 2 = every value == 0.
+__global__ void fa_mask_opt_kernel(const __half *__restrict__ mask, uint32_t *__restrict__ out, int T, int64_t S,
+                                   int64_t row_stride, int64_t out_row_stride) {
+    pdl_wait();
+    pdl_trigger();
+    const int word = blockIdx.x, rb = blockIdx.y;
+    const float big = 1.7014117e38f;
+    __shared__ float smin[4], smax[4];
+    uint32_t result = 0;
+    for (int bx = 0; bx < 16; ++bx) {
+        float mn = big, mx = -big;
+        for (int idx = threadIdx.x; idx < 16 * 64; idx += blockDim.x) {
+            const int64_t col = (idx & 63) + (static_cast<int64_t>(word) * 16 + bx) * 64;
+            const int row = (idx >> 6) + rb * 16;
+            if (col < S && row < T) {
+                const float v = __half2float(mask[row * row_stride + col]);
+                mn = fminf(mn, v);
+                mx = fmaxf(mx, v);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        if ((threadIdx.x & 31) == 0) {
+            smin[threadIdx.x >> 5] = mn;
+            smax[threadIdx.x >> 5] = mx;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) {
+                mn = fminf(mn, smin[i]);
+                mx = fmaxf(mx, smax[i]);
+            }
+            if (mx <= -big) result |= 1u << (2 * bx);
+            if (mn == 0.0f && mx == 0.0f) result |= 2u << (2 * bx);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[static_cast<int64_t>(rb) * out_row_stride + word] = result;
 }
 
 // cache[b, pos_t, h, :] = src[b, t, h, :] with pos_t = positions[t] (int64) or `position` + t.
@@ -347,5 +508,126 @@ extern "C" int t2c_token_select_chunks(const float *scores, const uint32_t *toke
     cfg.numAttrs = 1;
     cudaError_t err = cudaLaunchKernelEx(&cfg, select_chunks_kernel, scores, tokens, G, chunk_scores, chunk_tokens);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "token_select_chunks: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+extern "C" int t2c_rms_norm_f32(const float *x, const float *w, float *y, int64_t rows, int64_t H, float eps,
+                                void *stream) {
+    if (!x || !w || !y) return set_error(T2C_EINVAL, "rms_norm_f32: NULL pointer");
+    if (rows <= 0 || H <= 0 || H > INT32_MAX) return set_error(T2C_EINVAL, "rms_norm_f32: bad shape");
+    if (H % 4 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
+                       reinterpret_cast<uintptr_t>(w) % 16))
+        return set_error(T2C_EINVAL, "rms_norm_f32: rows must be 16-byte aligned");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(rows));
+    cfg.blockDim = dim3(256);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, rms_norm_f32_kernel, x, w, y, static_cast<int>(H), eps);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "rms_norm_f32: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+extern "C" int t2c_rms_norm_rope_f32(const float *x, const float *w, const void *cos_t, const void *sin_t, void *out,
+                                     int out_f32, int64_t B, int64_t T, int64_t G, int64_t D, float eps, void *stream) {
+    if (!x || !w || !cos_t || !sin_t || !out) return set_error(T2C_EINVAL, "rms_norm_rope_f32: NULL pointer");
+    if (B <= 0 || T <= 0 || G <= 0) return set_error(T2C_EINVAL, "rms_norm_rope_f32: bad shape");
+    if (D != 128 && D != 64) return set_error(T2C_EUNSUPPORTED, "rms_norm_rope_f32: D=%lld", (long long)D);
+    const int64_t rows = B * T * G;
+    const int warps = 8;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + warps - 1) / warps));
+    cfg.blockDim = dim3(warps * 32);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // token-major output [B, T, G, D]
+    const int64_t ob = T * G * D, og = D, ot = G * D;
+    const __half *cp = static_cast<const __half *>(cos_t);
+    const __half *sp = static_cast<const __half *>(sin_t);
+    const int b = static_cast<int>(B), t = static_cast<int>(T), g = static_cast<int>(G);
+    cudaError_t err;
+    if (D == 128) {
+        err = out_f32 ? cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<4, float, float>, x, w, cp, sp,
+                                           static_cast<float *>(out), b, t, g, ob, og, ot, eps)
+                      : cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<4, float, __half>, x, w, cp, sp,
+                                           static_cast<__half *>(out), b, t, g, ob, og, ot, eps);
+    } else {
+        err = out_f32 ? cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<2, float, float>, x, w, cp, sp,
+                                           static_cast<float *>(out), b, t, g, ob, og, ot, eps)
+                      : cudaLaunchKernelEx(&cfg, rms_norm_rope_kernel<2, float, __half>, x, w, cp, sp,
+                                           static_cast<__half *>(out), b, t, g, ob, og, ot, eps);
+    }
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "rms_norm_rope_f32: %s", cudaGetErrorString(err));
+    return T2C_OK;
+}
+
+extern "C" int t2c_binary_f32(int op, const float *a, const float *b, float *out, int64_t n, void *stream) {
+    if (!a || !b || !out || n < 0) return set_error(T2C_EINVAL, "binary_f32: bad arguments");
+    if (op != BIN_ADD && op != BIN_SWIGLU) return set_error(T2C_EINVAL, "binary_f32: op %d", op);
+    if (reinterpret_cast<uintptr_t>(a) % 16 || reinterpret_cast<uintptr_t>(b) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return set_error(T2C_EINVAL, "binary_f32: operands must be 16-byte aligned");
+    if (n == 0) return T2C_OK;
+    return launch(binary_f32_kernel, (n + 3) / 4, 256, as_stream(stream), op, a, b, out, n);
+}
+
+extern "C" int t2c_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, void *stream) {
+    if (!x || !y || n < 0) return set_error(T2C_EINVAL, "cast: bad arguments");
+    if (n == 0) return T2C_OK;
+    const cudaStream_t s = as_stream(stream);
+    if (x_dtype == T2C_F32 && y_dtype == T2C_F16)
+        return launch(cast_kernel<float, __half>, n, 256, s, static_cast<const float *>(x), static_cast<__half *>(y), n);
+    if (x_dtype == T2C_F16 && y_dtype == T2C_F32)
+        return launch(cast_kernel<__half, float>, n, 256, s, static_cast<const __half *>(x), static_cast<float *>(y), n);
+    return set_error(T2C_EUNSUPPORTED, "cast: dtypes %d -> %d", x_dtype, y_dtype);
+}
+
+extern "C" int t2c_slice_last_f32_to_f16(const float *x, void *out, int64_t B, int64_t S, int64_t H, void *stream) {
+    if (!x || !out || B <= 0 || S <= 0 || H <= 0 || H > INT32_MAX) return set_error(T2C_EINVAL, "slice_last: bad arguments");
+    return launch(slice_last_f32_kernel, B * H, 256, as_stream(stream), x, static_cast<__half *>(out),
+                  static_cast<int>(B), S, static_cast<int>(H));
+}
+
+extern "C" int t2c_value_cache_write_f32(const float *src, const int64_t *positions, int ncaches, void *const *caches,
+                                         const int64_t *cache_lens, int64_t B, int64_t T, int64_t H, int64_t D,
+                                         void *stream) {
+    if (!src || !positions || !caches || !cache_lens || ncaches < 1 || ncaches > 3)
+        return set_error(T2C_EINVAL, "value_cache_write_f32: bad arguments");
+    if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return set_error(T2C_EINVAL, "value_cache_write_f32: bad shape");
+    CacheSet cs = {};
+    cs.n = ncaches;
+    for (int i = 0; i < ncaches; ++i) {
+        if (!caches[i] || cache_lens[i] <= 0) return set_error(T2C_EINVAL, "value_cache_write_f32: cache %d", i);
+        cs.c[i] = static_cast<__half *>(caches[i]);
+        cs.S[i] = cache_lens[i];
+    }
+    return launch(value_cache_write_f32_kernel, B * T * H * D, 256, as_stream(stream), src, positions, cs,
+                  static_cast<int>(B), static_cast<int>(T), static_cast<int>(H), static_cast<int>(D));
+}
+
+extern "C" int t2c_fa_mask_opt(const void *mask, uint32_t *out, int64_t T, int64_t S, int64_t words, int64_t row_blocks,
+                               void *stream) {
+    if (!mask || !out || T <= 0 || S <= 0 || words <= 0 || row_blocks <= 0)
+        return set_error(T2C_EINVAL, "fa_mask_opt: bad arguments");
+    if (words > 65535 || row_blocks > 65535) return set_error(T2C_EINVAL, "fa_mask_opt: grid too large");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(words), static_cast<unsigned>(row_blocks));
+    cfg.blockDim = dim3(128);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, fa_mask_opt_kernel, static_cast<const __half *>(mask), out,
+                                               static_cast<int>(T), S, S, words);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "fa_mask_opt: %s", cudaGetErrorString(err));
     return T2C_OK;
 }

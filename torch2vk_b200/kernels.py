@@ -474,3 +474,149 @@ def attn_masked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.T
     _lib.lib().call("t2c_attn_masked", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(mask), _lib.ptr(out), B, H, T,
                     S, D, st(q), st(k), st(v), st(m), st(out), float(scale), _lib.stream_ptr())
     return out
+
+
+# ------------------------------------------------ fp32-activation prefill programs
+def _check_f32(t: torch.Tensor, name: str) -> None:
+    _check(t, torch.float32, name)
+
+
+def linear_f32(x: torch.Tensor, w: torch.Tensor, kind: str | int, k: int, *,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """y fp32 [..., N] = x fp32 [..., K] @ deq(W)^T (x rounded to fp16 for the tensor cores)."""
+    _check_f32(x, "x")
+    if x.shape[-1] != k:
+        raise ValueError(f"x last dim {x.shape[-1]} != K {k}")
+    wtype = wtype_of(kind)
+    n = _check_weight(w, wtype, k)
+    m = x.numel() // k
+    out = torch.empty(*x.shape[:-1], n, dtype=torch.float32, device=x.device) if out is None else out
+    _check_f32(out, "out")
+    nbytes = _lib.lib().raw("t2c_linear_f32_scratch_bytes")(m, n, k)
+    scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=x.device)
+    base = (-scratch.data_ptr()) % 256
+    _lib.lib().call("t2c_linear_f32", wtype, _lib.ptr(x), _lib.ptr(w), _lib.ptr(out), m, n, k,
+                    scratch.data_ptr() + base, nbytes, _lib.stream_ptr())
+    return out
+
+
+def rms_norm_f32(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 RMSNorm over the last dim (fp32 weight)."""
+    _check_f32(x, "x")
+    _check_f32(w, "w")
+    h = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _check_f32(out, "out")
+    _lib.lib().call("t2c_rms_norm_f32", _lib.ptr(x), _lib.ptr(w), _lib.ptr(out), x.numel() // h, h, float(eps),
+                    _lib.stream_ptr())
+    return out
+
+
+def rms_norm_rope_f32(x: torch.Tensor, w: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor,
+                      out: torch.Tensor, *, eps: float = 1e-6) -> torch.Tensor:
+    """x fp32 [B, T, G, D] -> rope(rmsnorm(x) * w) [B, T, G, D] in out's dtype (fp32 or fp16)."""
+    _check_f32(x, "x")
+    _check_f32(w, "w")
+    _check(cos_t, torch.float16, "cos")
+    _check(sin_t, torch.float16, "sin")
+    if out.dtype not in (torch.float32, torch.float16) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 or float16 tensor")
+    B, T, G, D = x.shape
+    _lib.lib().call("t2c_rms_norm_rope_f32", _lib.ptr(x), _lib.ptr(w), _lib.ptr(cos_t), _lib.ptr(sin_t), _lib.ptr(out),
+                    int(out.dtype == torch.float32), B, T, G, D, float(eps), _lib.stream_ptr())
+    return out
+
+
+def add_f32(x: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    for t, n in ((x, "x"), (y, "y")):
+        _check_f32(t, n)
+    out = torch.empty_like(x) if out is None else out
+    _lib.lib().call("t2c_binary_f32", 0, _lib.ptr(x), _lib.ptr(y), _lib.ptr(out), x.numel(), _lib.stream_ptr())
+    return out
+
+
+def swiglu_f32(g: torch.Tensor, u: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(g) * u in fp32."""
+    for t, n in ((g, "gate"), (u, "up")):
+        _check_f32(t, n)
+    out = torch.empty_like(g) if out is None else out
+    _lib.lib().call("t2c_binary_f32", 1, _lib.ptr(g), _lib.ptr(u), _lib.ptr(out), g.numel(), _lib.stream_ptr())
+    return out
+
+
+_DTYPE_CODE = {torch.float32: _lib.F32, torch.float16: _lib.F16}
+
+
+def cast(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = x converted between float32 and float16 (same number of elements)."""
+    if x.numel() != out.numel() or not x.is_contiguous() or not out.is_contiguous():
+        raise ValueError("cast needs contiguous tensors of equal size")
+    _lib.lib().call("t2c_cast", _lib.ptr(x), _DTYPE_CODE[x.dtype], _lib.ptr(out), _DTYPE_CODE[out.dtype], x.numel(),
+                    _lib.stream_ptr())
+    return out
+
+
+def slice_last_f32_to_f16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out [B, 1, H] fp16 = x [B, S, H] fp32 at the last position."""
+    _check_f32(x, "x")
+    _check(out, torch.float16, "out")
+    B, S, H = x.shape
+    _lib.lib().call("t2c_slice_last_f32_to_f16", _lib.ptr(x), _lib.ptr(out), B, S, H, _lib.stream_ptr())
+    return out
+
+
+def value_cache_write_f32(src: torch.Tensor, positions: torch.Tensor, caches: list[torch.Tensor]) -> None:
+    """fp16 token-major caches [B, S_c, H, D] get src [B, T, H, D] (fp32) at rows positions[t]."""
+    _check_f32(src, "src")
+    _check(positions, torch.int64, "cache_position")
+    B, T, H, D = src.shape
+    for c in caches:
+        _check(c, torch.float16, "cache")
+        if c.shape[0] != B or c.shape[2] != H or c.shape[3] != D:
+            raise ValueError(f"cache shape {tuple(c.shape)} does not match src {tuple(src.shape)}")
+    _lib.lib().call("t2c_value_cache_write_f32", _lib.ptr(src), _lib.ptr(positions), len(caches),
+                    _lib.ptr_array([_lib.ptr(c) for c in caches]), _lib.i64_array([c.shape[1] for c in caches]),
+                    B, T, H, D, _lib.stream_ptr())
+
+
+def fa_mask_opt(mask: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """2-bit codes per (16-row, 64-column) block of the fp16 mask [T, S], written [row_blocks][words]."""
+    _check(mask, torch.float16, "mask")
+    if out.dtype not in (torch.uint32, torch.int32) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous 32-bit tensor")
+    T, S = mask.shape
+    words, row_blocks = (S + 1023) // 1024, (T + 15) // 16
+    if out.numel() < words * row_blocks:
+        raise ValueError(f"out holds {out.numel()} words, needs {words * row_blocks}")
+    _lib.lib().call("t2c_fa_mask_opt", _lib.ptr(mask), _lib.ptr(out), T, S, words, row_blocks, _lib.stream_ptr())
+    return out
+
+
+def attn_prefill_masked_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor,
+                            mask_opt: torch.Tensor | None, out: torch.Tensor, *, scale: float) -> torch.Tensor:
+    """softmax(q k^T * scale + mask) v; q / out fp32 [B, T, NH, D], k / v fp16 [B, S, NK, D], mask fp16 [T, S]."""
+    _check_f32(q, "q")
+    _check_f32(out, "out")
+    _check(k, torch.float16, "k")
+    _check(v, torch.float16, "v")
+    _check(mask, torch.float16, "mask")
+    B, T, NH, D = q.shape
+    S, NK = k.shape[1], k.shape[2]
+    words = (S + 1023) // 1024
+    if mask_opt is not None and mask_opt.numel() < words * ((T + 15) // 16):
+        raise ValueError("mask_opt is smaller than the mask's block grid")
+    _lib.lib().call("t2c_attn_prefill_masked_f32", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(mask),
+                    _lib.ptr(mask_opt), _lib.ptr(out), B, T, S, NH, NK, D, mask.shape[1], words, float(scale),
+                    _lib.stream_ptr())
+    return out
+
+
+def embedding_f32(weight: torch.Tensor, kind: str | int, ids: torch.Tensor, hidden: int, vocab: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """out fp32 [..., hidden] = dequantized rows ids of a Q4_K embedding."""
+    _check(ids, torch.int64, "ids")
+    out = torch.empty(*ids.shape, hidden, dtype=torch.float32, device=ids.device) if out is None else out
+    _check_f32(out, "out")
+    _lib.lib().call("t2c_embedding_f32", wtype_of(kind), _lib.ptr(weight), _lib.ptr(ids), _lib.ptr(out), ids.numel(),
+                    vocab, hidden, _lib.stream_ptr())
+    return out

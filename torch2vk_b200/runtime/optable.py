@@ -365,3 +365,81 @@ def _sdpa_masked(rt, variant, b, s, pc):
     if k.shape[1] != q.shape[1]:
         raise NotImplementedError(f"{variant.name}: {q.shape[1]} query heads over {k.shape[1]} key heads")
     kernels.attn_masked(q, k, v, mask, scale=float(q.shape[-1]) ** -0.5, out=out)
+
+# ------------------------------------- fp32-activation prefill (optimized Qwen3, llama.cpp-style)
+@op("LlamaMatmulQ4KF32Program", "LlamaMatmulQ6KF32Program")
+def _llama_matmul(rt, variant, b, s, pc):
+    """output fp32 [X0,X1,N] = x fp32 [X0,X1,K] @ deq(W)^T (llama_matmul_q{4,6}_k_f32.py; the reference
+    multiplies fp16 operands with fp16 accumulation, the tensor-core GEMM here accumulates in fp32)."""
+    kind = "q6_k" if "Q6K" in variant.contract.class_name else "q4_k"
+    kernels.linear_f32(b["x"], b["weight"], kind, s["K"], out=b["output"])
+
+
+@op("OptimizedQwen3RmsNormMulF32Program")
+def _rms_norm_f32(rt, variant, b, s, pc):
+    """x * rsqrt(mean(x^2) + 1e-6) * w, fp32 (rms_norm_mul_f32.py)."""
+    kernels.rms_norm_f32(b["x"], b["weight"], 1e-6, out=b["output"])
+
+
+@op("OptimizedQwen3RmsNormRopeTokenF32Program", "OptimizedQwen3RmsNormRopeTokenF32ToF16Program")
+def _rms_norm_rope_token(rt, variant, b, s, pc):
+    """Per (b, t, head) row: RMSNorm (1e-6) * w then rotate-half RoPE from the fp16 cos / sin tables
+    (rms_norm_rope_token_f32.py:22; the _to_f16 variant stores fp16)."""
+    kernels.rms_norm_rope_f32(b["x"], b["weight"], b["cos"], b["sin"], b["output"], eps=1e-6)
+
+
+@op("AddF32PrefillProgram")
+def _add_f32(rt, variant, b, s, pc):
+    """x + y in fp32 (add_f32_prefill.py)."""
+    kernels.add_f32(b["x"], b["y"], out=b["output"])
+
+
+@op("SwigluF32Program")
+def _swiglu_f32(rt, variant, b, s, pc):
+    """gate / (1 + exp(-gate)) * up in fp32 (swiglu_f32.py)."""
+    kernels.swiglu_f32(b["gate"], b["up"], out=b["output"])
+
+
+@op("SliceLastTokenF32ToF16Program")
+def _slice_last_f32(rt, variant, b, s, pc):
+    """output[b,0,:] = fp16(x[b,S-1,:]) (slice_last_token_f32_to_f16.py)."""
+    kernels.slice_last_f32_to_f16(b["x"], b["output"])
+
+
+@op("OptimizedQwen3TokenMajorValueCacheWriteF32ToF16PairProgram",
+    "OptimizedQwen3TokenMajorValueCacheWriteF32ToF16TripleProgram")
+def _value_cache_write_f32(rt, variant, b, s, pc):
+    """fp16(src [B,T,H,D]) into each token-major cache at cache_position[t]; a cache too short for
+    the row is skipped (token_major_value_cache_write_f32_to_f16_{pair,triple}.py)."""
+    caches = [b[f"cache_{c}"] for c in ("a", "b", "c") if f"cache_{c}" in b]
+    kernels.value_cache_write_f32(b["src"], b["cache_position"], caches)
+
+
+@op("OptimizedQwen3FaMaskOptF16Program")
+def _fa_mask_opt(rt, variant, b, s, pc):
+    """2-bit all-masked / all-zero codes per 16 x 64 block of the mask (fa_mask_opt_f16.py), stored as
+    the shader does: word w of row block r at r * W + w."""
+    W, R = s["W"], s["R"]
+    if W != (s["S"] + 1023) // 1024 or R != (s["T"] + 15) // 16:
+        raise ValueError(f"{variant.name}: output ({W}, {R}) does not cover mask ({s['T']}, {s['S']})")
+    kernels.fa_mask_opt(b["mask"], b["output"])
+
+
+@op("LlamaFlashAttnF32F16F16Program")
+def _llama_flash_attn(rt, variant, b, s, pc):
+    """softmax(q k^T * scale + mask) v with fp32 q / output [B,T,NH,D] and fp16 token-major caches
+    [B,S,NK,D] (llama_flash_attn_f32_f16_f16.py:35-158; no attention sinks: bit 24 of
+    mask_n_head_log2 is clear in every reference call)."""
+    if int(pc.get("mask_n_head_log2", 0)) & (1 << 24):
+        raise NotImplementedError(f"{variant.name}: attention sinks are not served")
+    if float(pc.get("logit_softcap", 0.0)) != 0.0 or float(pc.get("max_bias", 0.0)) != 0.0:
+        raise NotImplementedError(f"{variant.name}: logit softcap / ALiBi bias are not served")
+    kernels.attn_prefill_masked_f32(b["q"], b["k"], b["v"], b["mask"], b.get("mask_opt"), b["output"],
+                                    scale=float(pc["scale"]))
+
+
+@op("OptimizedQwen3EmbeddingQ4KActF32Program")
+def _embedding_q4k_f32(rt, variant, b, s, pc):
+    """output fp32 [I0,I1,H] = dequantized Q4_K rows (embedding_q4_k_act_f32.py)."""
+    w = b["weight"]
+    kernels.embedding_f32(w, "q4_k", b["indices"], s["H"], w.shape[0], out=b["output"])
