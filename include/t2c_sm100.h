@@ -263,6 +263,10 @@ int t2c_elementwise4d(int op, int is_f32, const void *a, const int64_t *a_stride
 /* RoPE cos/sin tables [B, T, D] fp16 (src/torch2vk/runtime/rope_table.py:31-121). */
 int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
                    int64_t start_position, float attention_scaling, void *stream);
+/* The same table in fp32.  Replaces RopeTableOutputF32Program
+ *   src/torch2vk/runtime/rope_table.py:124-160 */
+int t2c_rope_table_f32(float *cos_out, float *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                       int64_t start_position, float attention_scaling, void *stream);
 /*
  * Per-row RMSNorm + rotate-half RoPE from fp16 cos/sin tables [B, T, D]; x
  * [B, T, G, D] fp16, out addressed by strides (b, g, t).  Replaces
@@ -348,6 +352,16 @@ int t2c_gelu(const void *x, void *y, int64_t n, void *stream);
 /* out[o, :] = x[index[o], :] (fp16 rows of H; int64 index; an index outside [0, rows) writes a
  * zero row and sets T2C_EINVAL).  Replaces ExportIndexSelectF32Program (index_select_f32_*.py). */
 int t2c_index_rows(const void *x, const int64_t *index, void *out, int64_t O, int64_t H, int64_t rows, void *stream);
+/* cache[b, index[s], :] = src[b, s, :] (fp16; cache [B, T, H], src [B, S, H]); a row index
+ * outside [0, T) is skipped and sets T2C_EINVAL.  Replaces ExportIndexCopyF32Program
+ *   src/models/quantized_qwen3_asr/shaders/index_copy_f32_7ba4f1ff13.py (audio-feature injection) */
+int t2c_index_copy_rows(void *cache, const int64_t *index, const void *src, int64_t B, int64_t T, int64_t S, int64_t H,
+                        void *stream);
+/* out fp16 [n_ids, H] = d * q of Q8_0 rows (an id outside [0, vocab) reads row 0 and sets
+ * T2C_EINVAL).  Replaces ExportEmbeddingQ8_0Program
+ *   src/models/quantized_qwen3_asr/shaders/embedding_q8_0_f32.py */
+int t2c_embedding_q8_0(const void *weight, const int64_t *ids, void *out, int64_t n_ids, int64_t vocab, int64_t H,
+                       void *stream);
 /* Non-causal attention with an additive fp16 mask (the encoder's block-diagonal windows):
  * out[b,h,t,:] = softmax(q[b,h,t,:] . k[b,h,s,:] * scale + mask[b,h,t,s]) v[b,h,s,:], D = 64.
  * Strides (elements) are {batch, head, row} for q, k, v, out and {batch, head, query row} for the

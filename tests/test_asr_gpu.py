@@ -128,3 +128,68 @@ def test_asr_encoder_matches_oracle(oracle):
     assert float((out * golden).sum() / (np.linalg.norm(out) * np.linalg.norm(golden))) >= 0.99
     from torch2vk_b200 import kernels
     assert kernels.device_status() == 0
+
+
+def test_text_decoder_embedding_and_audio_inject(oracle):
+    """ExportEmbeddingQ8_0Program (fp16 of d * q, exact against the oracle decoder) and
+    ExportIndexCopyF32Program (row scatter, exact; an out-of-range row is skipped and reported)."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(4)
+    vocab, h = 500, 1024
+    packed = oracle.quantize((rng.standard_normal((vocab, h)) * 0.05).astype(np.float32), "q8_0")
+    table = oracle.dequantize(packed, "q8_0", h).astype(np.float16)
+    ids = np.array([[3, 499, 0, 3, 250, 17]], np.int64)
+    out = kernels.embedding_q8_0(torch.from_numpy(packed).cuda(), torch.from_numpy(ids).cuda(), h, vocab)
+    assert np.array_equal(out.cpu().numpy(), table[ids])
+
+    B, T, S = 1, 40, 12
+    cache = rng.standard_normal((B, T, h)).astype(np.float16)
+    src = rng.standard_normal((B, S, h)).astype(np.float16)
+    index = np.arange(5, 5 + S, dtype=np.int64)
+    dev = torch.from_numpy(cache.copy()).cuda()
+    kernels.device_status(clear=True)
+    kernels.index_copy_rows(dev, torch.from_numpy(index).cuda(), torch.from_numpy(src).cuda())
+    want = cache.copy()
+    want[:, index] = src
+    assert np.array_equal(dev.cpu().numpy(), want)
+    assert kernels.device_status(clear=True) == 0
+    bad = index.copy()
+    bad[3] = T + 2
+    dev = torch.from_numpy(cache.copy()).cuda()
+    kernels.index_copy_rows(dev, torch.from_numpy(bad).cuda(), torch.from_numpy(src).cuda())
+    want = cache.copy()
+    keep = np.arange(S) != 3
+    want[:, bad[keep]] = src[:, keep]
+    assert np.array_equal(dev.cpu().numpy(), want)
+    assert kernels.device_status(clear=True) & (1 << 1)
+
+
+def test_rope_table_f32_and_quantize_ops(oracle):
+    """RopeTableOutputF32Program (fp32 table; its fp16 rounding equals the fp16 table) and the GGUF
+    quantizer programs through the op table (bit-exact with the oracle)."""
+    from types import SimpleNamespace
+
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.runtime import optable
+
+    c32, s32 = torch.empty(2, 33, 128, device="cuda"), torch.empty(2, 33, 128, device="cuda")
+    c16, s16 = (torch.empty(2, 33, 128, dtype=torch.float16, device="cuda") for _ in range(2))
+    v = SimpleNamespace(name="rope_table_output_f32", contract=SimpleNamespace(class_name="RopeTableOutputF32Program"))
+    optable.OPS["RopeTableOutputF32Program"](None, v, {"cos": c32, "sin": s32}, {},
+                                             {"theta": 1e6, "start_position": 1000, "attention_scaling": 1.0})
+    kernels.rope_table(c16, s16, theta=1e6, start_position=1000)
+    assert torch.equal(c32.half(), c16) and torch.equal(s32.half(), s16)
+    pos = 1000 + np.arange(33, dtype=np.float64)
+    inv = 1e6 ** (-(2 * (np.arange(128) % 64)) / 128)
+    assert np.abs(c32[0].cpu().numpy() - np.cos(pos[:, None] * inv[None, :])).max() < 2e-3
+
+    rng = np.random.default_rng(9)
+    for cls, kind, dtype, words in (("GGUFQuantizeQ4KF32Program", "q4_k", torch.int32, 36),
+                                    ("GGUFQuantizeQ6KF32Program", "q6_k", torch.int16, 105),
+                                    ("GGUFQuantizeQ8_0F32Program", "q8_0", torch.int16, 17 * 8)):
+        x = (rng.standard_normal((24, 256)) * 0.1).astype(np.float32)
+        out = torch.empty(24, words, dtype=dtype, device="cuda")
+        v = SimpleNamespace(name=cls, contract=SimpleNamespace(class_name=cls))
+        optable.OPS[cls](None, v, {"x": torch.from_numpy(x).cuda(), "output": out}, {"R": 24, "K": 256}, {})
+        assert np.array_equal(out.cpu().numpy().view(np.uint8).reshape(24, -1), oracle.quantize(x, kind)), cls

@@ -304,6 +304,45 @@ __global__ void index_rows_kernel(const __half *__restrict__ x, const int64_t *_
     }
 }
 
+// cache[b, index[s], :] = src[b, s, :] (fp16 rows of H; the audio-feature injection into the
+// text embeddings).  A destination row outside [0, T) is skipped and sets T2C_EINVAL.
+__global__ void index_copy_rows_kernel(__half *__restrict__ cache, const int64_t *__restrict__ index,
+                                       const __half *__restrict__ src, int64_t B, int64_t T, int64_t S, int64_t H) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < B * S * H;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t h = i % H, bs = i / H;
+        const int64_t s = bs % S, b = bs / S;
+        const int64_t t = index[s];
+        if (t < 0 || t >= T) {
+            if (h == 0) report_device_error(T2C_EINVAL);
+            continue;
+        }
+        cache[(b * T + t) * H + h] = src[i];
+    }
+}
+
+// out[i, :] = fp16(d * q) of Q8_0 rows ids[i] (embedding_q8_0_f32.py: d fp16, 32 int8 per block)
+__global__ void embedding_q8_0_kernel(const uint8_t *__restrict__ w, const int64_t *__restrict__ ids,
+                                      __half *__restrict__ out, int64_t n_ids, int64_t vocab, int64_t H) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t row_bytes = H / 32 * 34;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_ids * H;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / H, c = i - r * H;
+        int64_t id = ids[r];
+        if (id < 0 || id >= vocab) {
+            if (c == 0) report_device_error(T2C_EINVAL);
+            id = 0;
+        }
+        const uint8_t *blk = w + id * row_bytes + (c >> 5) * 34;
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+        out[i] = __float2half_rn(d * static_cast<float>(static_cast<int8_t>(blk[2 + (c & 31)])));
+    }
+}
+
 // ---------------------------------------------------- masked attention
 // out[b, h, t, :] = softmax(q k^T * scale + mask[t, s]) v over all S keys
 // (non-causal; the additive fp16 mask carries the encoder's block-diagonal
@@ -567,6 +606,26 @@ extern "C" int t2c_index_rows(const void *x, const int64_t *index, void *out, in
     if (grid > 148 * 32) grid = 148 * 32;
     return launch_asr(index_rows_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
                       static_cast<const __half *>(x), index, static_cast<__half *>(out), O, H, rows);
+}
+
+extern "C" int t2c_index_copy_rows(void *cache, const int64_t *index, const void *src, int64_t B, int64_t T, int64_t S,
+                                   int64_t H, void *stream) {
+    if (!cache || !index || !src || B <= 0 || T <= 0 || S <= 0 || H <= 0)
+        return set_error(T2C_EINVAL, "index_copy_rows: bad arguments");
+    int64_t grid = (B * S * H + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    return launch_asr(index_copy_rows_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
+                      static_cast<__half *>(cache), index, static_cast<const __half *>(src), B, T, S, H);
+}
+
+extern "C" int t2c_embedding_q8_0(const void *weight, const int64_t *ids, void *out, int64_t n_ids, int64_t vocab,
+                                  int64_t H, void *stream) {
+    if (!weight || !ids || !out || n_ids <= 0 || vocab <= 0 || H <= 0 || H % 32)
+        return set_error(T2C_EINVAL, "embedding_q8_0: bad arguments (H a multiple of 32)");
+    int64_t grid = (n_ids * H + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    return launch_asr(embedding_q8_0_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
+                      static_cast<const uint8_t *>(weight), ids, static_cast<__half *>(out), n_ids, vocab, H);
 }
 
 extern "C" int t2c_attn_masked(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B,

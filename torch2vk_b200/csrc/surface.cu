@@ -77,7 +77,8 @@ __global__ void elementwise4d_kernel(int op, int f32, const void *__restrict__ a
 
 // cos/sin [B, T, D] fp16: angle = (start + t) * theta^(-2 (d mod D/2) / D), times attention_scaling
 // (src/torch2vk/runtime/rope_table.py:31-121 arithmetic).
-__global__ void rope_table_kernel(__half *__restrict__ cos_out, __half *__restrict__ sin_out, int64_t B, int T, int D,
+template <typename OT>
+__global__ void rope_table_kernel(OT *__restrict__ cos_out, OT *__restrict__ sin_out, int64_t B, int T, int D,
                                   float theta, int64_t start, float scaling) {
     pdl_wait();
     pdl_trigger();
@@ -92,8 +93,8 @@ __global__ void rope_table_kernel(__half *__restrict__ cos_out, __half *__restri
     const float angle = static_cast<float>(start + t) * inv_freq;
     float sn, cs;
     sincosf(angle, &sn, &cs);
-    cos_out[i] = __float2half_rn(cs * scaling);
-    sin_out[i] = __float2half_rn(sn * scaling);
+    cos_out[i] = static_cast<OT>(cs * scaling);
+    sin_out[i] = static_cast<OT>(sn * scaling);
 }
 
 // One warp per (b, t, g) row of D values: RMSNorm with fp32 weight, then
@@ -438,7 +439,7 @@ extern "C" int t2c_elementwise4d(int op, int is_f32, const void *a, const int64_
 extern "C" int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
                               int64_t start_position, float attention_scaling, void *stream) {
     if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table: bad arguments");
-    return launch(rope_table_kernel, B * T * D, 256, as_stream(stream), static_cast<__half *>(cos_out),
+    return launch(rope_table_kernel<__half>, B * T * D, 256, as_stream(stream), static_cast<__half *>(cos_out),
                   static_cast<__half *>(sin_out), B, static_cast<int>(T), static_cast<int>(D), theta, start_position,
                   attention_scaling);
 }
@@ -630,4 +631,11 @@ extern "C" int t2c_fa_mask_opt(const void *mask, uint32_t *out, int64_t T, int64
                                                static_cast<int>(T), S, S, words);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "fa_mask_opt: %s", cudaGetErrorString(err));
     return T2C_OK;
+}
+
+extern "C" int t2c_rope_table_f32(float *cos_out, float *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                                  int64_t start_position, float attention_scaling, void *stream) {
+    if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table_f32: bad arguments");
+    return launch(rope_table_kernel<float>, B * T * D, 256, as_stream(stream), cos_out, sin_out, B, static_cast<int>(T),
+                  static_cast<int>(D), theta, start_position, attention_scaling);
 }

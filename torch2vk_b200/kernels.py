@@ -109,13 +109,18 @@ def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, kin
     return out
 
 
-def quantize(x: torch.Tensor, kind: str | int) -> torch.Tensor:
+def quantize(x: torch.Tensor, kind: str | int, out: torch.Tensor | None = None) -> torch.Tensor:
     """fp32 [R, K] -> packed GGUF blocks (physical dtype of the reference layout)."""
     wtype = wtype_of(kind)
     if x.dtype != torch.float32 or x.dim() != 2 or not x.is_cuda or not x.is_contiguous():
         raise ValueError("quantize expects a contiguous CUDA float32 [R, K] tensor")
     r, k = x.shape
     rb = row_bytes(wtype, k)
+    if out is not None:
+        if not out.is_contiguous() or out.numel() * out.element_size() != r * rb:
+            raise ValueError(f"out must be contiguous with {r * rb} bytes")
+        _lib.lib().call("t2c_quantize", wtype, _lib.ptr(x), _lib.ptr(out), r, k, _lib.stream_ptr())
+        return out
     out = torch.empty(r, rb, dtype=torch.uint8, device=x.device)
     _lib.lib().call("t2c_quantize", wtype, _lib.ptr(x), _lib.ptr(out), r, k, _lib.stream_ptr())
     return out.view(PHYSICAL_DTYPE[wtype])
@@ -366,8 +371,12 @@ def elementwise4d(op: str, a: torch.Tensor, b: torch.Tensor | None, out: torch.T
 
 def rope_table(cos_out: torch.Tensor, sin_out: torch.Tensor, *, theta: float, start_position: int,
                attention_scaling: float = 1.0) -> None:
+    """cos / sin [B, T, D] (fp16, or fp32 for the output-f32 variant) at positions start_position + t."""
     b, t, d = cos_out.shape
-    _lib.lib().call("t2c_rope_table", _lib.ptr(cos_out), _lib.ptr(sin_out), b, t, d, float(theta), int(start_position),
+    if cos_out.dtype != sin_out.dtype or cos_out.dtype not in (torch.float16, torch.float32):
+        raise ValueError("cos / sin must both be float16 or both float32")
+    name = "t2c_rope_table_f32" if cos_out.dtype == torch.float32 else "t2c_rope_table"
+    _lib.lib().call(name, _lib.ptr(cos_out), _lib.ptr(sin_out), b, t, d, float(theta), int(start_position),
                     float(attention_scaling), _lib.stream_ptr())
 
 
@@ -619,4 +628,30 @@ def embedding_f32(weight: torch.Tensor, kind: str | int, ids: torch.Tensor, hidd
     _check_f32(out, "out")
     _lib.lib().call("t2c_embedding_f32", wtype_of(kind), _lib.ptr(weight), _lib.ptr(ids), _lib.ptr(out), ids.numel(),
                     vocab, hidden, _lib.stream_ptr())
+    return out
+
+
+def index_copy_rows(cache: torch.Tensor, index: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """cache [B, T, H][b, index[s]] = src [B, S, H][b, s] (fp16, in place)."""
+    _check(cache, torch.float16, "cache")
+    _check(src, torch.float16, "src")
+    _check(index, torch.int64, "index")
+    B, T, H = cache.shape
+    S = src.shape[1]
+    if src.shape[0] != B or src.shape[2] != H or index.numel() != S:
+        raise ValueError(f"index_copy: cache {tuple(cache.shape)} src {tuple(src.shape)} index {index.numel()}")
+    _lib.lib().call("t2c_index_copy_rows", _lib.ptr(cache), _lib.ptr(index), _lib.ptr(src), B, T, S, H,
+                    _lib.stream_ptr())
+    return cache
+
+
+def embedding_q8_0(weight: torch.Tensor, ids: torch.Tensor, hidden: int, vocab: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """out fp16 [..., hidden] = dequantized Q8_0 rows ids."""
+    _check(ids, torch.int64, "ids")
+    _check_weight(weight, Q8_0, hidden)
+    out = torch.empty(*ids.shape, hidden, dtype=torch.float16, device=ids.device) if out is None else out
+    _check(out, torch.float16, "out")
+    _lib.lib().call("t2c_embedding_q8_0", _lib.ptr(weight), _lib.ptr(ids), _lib.ptr(out), ids.numel(), vocab, hidden,
+                    _lib.stream_ptr())
     return out

@@ -93,9 +93,10 @@ def _rms_norm_rope_transpose(rt, variant, b, s, pc):
                           out_strides=(G * T * D, T * D, D))
 
 
-@op("RopeTableF32Program")
+@op("RopeTableF32Program", "RopeTableOutputF32Program")
 def _rope_table(rt, variant, b, s, pc):
-    """cos/sin [B,T,D] fp16 at positions start_position + t (runtime/rope_table.py:31-121)."""
+    """cos/sin [B,T,D] at positions start_position + t, fp16 (runtime/rope_table.py:31-121) or fp32
+    (RopeTableOutputF32Program, :124-160)."""
     kernels.rope_table(b["cos"], b["sin"], theta=float(pc["theta"]), start_position=int(pc["start_position"]),
                        attention_scaling=float(pc.get("attention_scaling", 1.0)))
 
@@ -310,7 +311,8 @@ def _select(rt, variant, b, s, pc):
                          done=b["done"].view(torch.int32).view(1))
 
 
-@op("Qwen3TokenStoreEosProgram", "Qwen3TokenStoreEosF32Program")
+@op("Qwen3TokenStoreEosProgram", "Qwen3TokenStoreEosF32Program", "Qwen3TokenStoreProgram",
+    "Qwen3AsrTokenStoreEosProgram", "Qwen3AsrTokenStoreProgram")
 def _store(rt, variant, b, s, pc):
     """generated_tokens[token_index] = next_token unless stopped; EOS stops (qwen3_token_store.py)."""
     kernels.token_store(b["next_token"].view(1), b["done"].view(torch.int32).view(1), b["generated_tokens"],
@@ -443,3 +445,26 @@ def _embedding_q4k_f32(rt, variant, b, s, pc):
     """output fp32 [I0,I1,H] = dequantized Q4_K rows (embedding_q4_k_act_f32.py)."""
     w = b["weight"]
     kernels.embedding_f32(w, "q4_k", b["indices"], s["H"], w.shape[0], out=b["output"])
+
+
+# ------------------------------------------------------------- GGUF quantizers
+@op("GGUFQuantizeQ4KF32Program", "GGUFQuantizeQ6KF32Program", "GGUFQuantizeQ8_0F32Program")
+def _gguf_quantize(rt, variant, b, s, pc):
+    """fp32 [R, K] -> packed blocks, bit-exact with the reference quantizers (quantize/vulkan.py:91-637)."""
+    name = variant.contract.class_name
+    kind = "q4_k" if "Q4K" in name else "q6_k" if "Q6K" in name else "q8_0"
+    kernels.quantize(b["x"], kind, out=b["output"])
+
+
+# ------------------------------------------------------ ASR text decoder
+@op("ExportEmbeddingQ8_0Program")
+def _embedding_q8_0(rt, variant, b, s, pc):
+    """output fp16 [I0,I1,H] = d * q of Q8_0 rows (quantized_qwen3_asr embedding_q8_0_f32.py)."""
+    w = b["weight"]
+    kernels.embedding_q8_0(w, b["indices"], s["H"], w.shape[0], out=b["output"])
+
+
+@op("ExportIndexCopyF32Program")
+def _index_copy(rt, variant, b, s, pc):
+    """cache[b, index[s], :] = src[b, s, :] (index_copy_f32_*.py: the audio-token injection)."""
+    kernels.index_copy_rows(b["cache"], b["index"], b["src"])
