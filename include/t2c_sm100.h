@@ -431,6 +431,18 @@ int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, const void 
 int t2c_embedding_f32(int wtype, const void *weight, const int64_t *ids, float *out, int64_t n_ids, int64_t vocab,
                       int64_t H, void *stream);
 
+/* Elementwise steps of the exported (unfused) RMSNorm chain, fp32 arithmetic; a_f16 / b_f16 /
+ * out_f16 select fp16 (1) or fp32 (0) storage.  op 0: a*a (ExportPowScalarF32Program, exponent 2),
+ * 1: 1/sqrt(a) (ExportRsqrtF32Program), 2: a + scalar (ExportAddScalarProgram), 3: a[i] * b[i / H]
+ * (ExportMulBroadcastLastProgram), 4: a[i] * b[i % H] (ExportMulLeftBroadcastF32XProgram)
+ *   src/models/optimized_qwen3_asr/shaders/{pow_scalar_f32,rsqrt_f32,add_scalar,mul_broadcast_last,
+ *   mul_left_broadcast_f32x_f32}.py */
+int t2c_ew_misc(int op, const void *a, int a_f16, const void *b, int b_f16, void *out, int out_f16, int64_t n, int64_t H,
+                float scalar, void *stream);
+/* out[r] = mean(x[r, :]) for fp32 x [rows, cols].  Replaces ExportMeanDimProgram
+ *   src/models/optimized_qwen3_asr/shaders/mean_dim_f32.py */
+int t2c_row_mean_f32(const float *x, float *out, int64_t rows, int64_t cols, void *stream);
+
 /* ------------------------------------------------------------------ tensor parallelism
  * One-shot all-reduce of fp16 tensors over NVLink peer memory (the two
  * per-layer reductions of the row-split o_proj / down_proj partial sums in the

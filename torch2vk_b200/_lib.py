@@ -94,6 +94,8 @@ _SIGNATURES: dict[str, list] = {
     "t2c_rope_table_f32": [_vp, _vp, _i64, _i64, _i64, _f32, _i64, _f32, _vp],
     "t2c_index_copy_rows": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "t2c_embedding_q8_0": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "t2c_ew_misc": [_i32, _vp, _i32, _vp, _i32, _vp, _i32, _i64, _i64, _f32, _vp],
+    "t2c_row_mean_f32": [_vp, _vp, _i64, _i64, _vp],
 }
 _RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64,
              "t2c_allreduce_buffer_bytes": _c.c_int64, "t2c_linear_f32_scratch_bytes": _c.c_int64}

@@ -136,6 +136,42 @@ __global__ void rms_norm_rope_kernel(const XT *__restrict__ x, const float *__re
     }
 }
 
+// Mixed-precision elementwise steps of an unfused RMSNorm chain (the exported ASR text norm):
+// POW2 a*a, RSQRT 1/sqrt(a), ADD_SCALAR a + scalar, MUL_ROW a[i] * b[i / H], MUL_COL a[i] * b[i % H].
+// Operand / output dtypes by flag (1 = fp16, 0 = fp32); arithmetic in fp32.
+enum { EM_POW2 = 0, EM_RSQRT = 1, EM_ADD_SCALAR = 2, EM_MUL_ROW = 3, EM_MUL_COL = 4 };
+__global__ void ew_misc_kernel(int op, const void *__restrict__ a, int a16, const void *__restrict__ b, int b16,
+                               void *__restrict__ out, int o16, int64_t n, int64_t H, float scalar) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float x = ld_f(a, i, !a16);
+        float r;
+        switch (op) {
+            case EM_POW2: r = x * x; break;
+            case EM_RSQRT: r = rsqrtf(x); break;
+            case EM_ADD_SCALAR: r = x + scalar; break;
+            case EM_MUL_ROW: r = x * ld_f(b, i / H, !b16); break;
+            default: r = x * ld_f(b, i % H, !b16); break;
+        }
+        st_f(out, i, r, !o16);
+    }
+}
+
+// out[r] = mean of row r of x [rows, cols] (fp32), one warp per row
+__global__ void row_mean_f32_kernel(const float *__restrict__ x, float *__restrict__ out, int64_t rows, int64_t cols) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float sum = 0.0f;
+    for (int64_t c = lane; c < cols; c += 32) sum += x[r * cols + c];
+    sum = warp_sum(sum);
+    if (lane == 0) out[r] = sum / static_cast<float>(cols);
+}
+
 // ------------------------------------------- fp32-activation prefill programs
 // y = x * rsqrt(mean(x^2) + eps) * w, fp32 in and out, one CTA of 256 threads per row
 // (rms_norm_mul_f32.py: fp32 sum of squares, fp32 output).
@@ -638,4 +674,28 @@ extern "C" int t2c_rope_table_f32(float *cos_out, float *sin_out, int64_t B, int
     if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table_f32: bad arguments");
     return launch(rope_table_kernel<float>, B * T * D, 256, as_stream(stream), cos_out, sin_out, B, static_cast<int>(T),
                   static_cast<int>(D), theta, start_position, attention_scaling);
+}
+
+extern "C" int t2c_ew_misc(int op, const void *a, int a_f16, const void *b, int b_f16, void *out, int out_f16, int64_t n,
+                           int64_t H, float scalar, void *stream) {
+    if (!a || !out || n < 0 || op < EM_POW2 || op > EM_MUL_COL) return set_error(T2C_EINVAL, "ew_misc: bad arguments");
+    if ((op == EM_MUL_ROW || op == EM_MUL_COL) && (!b || H <= 0)) return set_error(T2C_EINVAL, "ew_misc: b / H");
+    if (n == 0) return T2C_OK;
+    return launch(ew_misc_kernel, n, 256, as_stream(stream), op, a, a_f16, b, b_f16, out, out_f16, n, H, scalar);
+}
+
+extern "C" int t2c_row_mean_f32(const float *x, float *out, int64_t rows, int64_t cols, void *stream) {
+    if (!x || !out || rows <= 0 || cols <= 0) return set_error(T2C_EINVAL, "row_mean_f32: bad arguments");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, row_mean_f32_kernel, x, out, rows, cols);
+    if (err != cudaSuccess) return set_error(T2C_ECUDA, "row_mean_f32: %s", cudaGetErrorString(err));
+    return T2C_OK;
 }

@@ -655,3 +655,32 @@ def embedding_q8_0(weight: torch.Tensor, ids: torch.Tensor, hidden: int, vocab: 
     _lib.lib().call("t2c_embedding_q8_0", _lib.ptr(weight), _lib.ptr(ids), _lib.ptr(out), ids.numel(), vocab, hidden,
                     _lib.stream_ptr())
     return out
+
+
+EM_OPS = {"pow2": 0, "rsqrt": 1, "add_scalar": 2, "mul_row": 3, "mul_col": 4}
+
+
+def ew_misc(op: str, a: torch.Tensor, out: torch.Tensor, b: torch.Tensor | None = None, *, H: int = 0,
+            scalar: float = 0.0) -> torch.Tensor:
+    """Mixed fp16 / fp32 elementwise step (fp32 arithmetic): pow2, rsqrt, add_scalar, mul_row
+    (a[i] * b[i // H]) or mul_col (a[i] * b[i % H])."""
+    for t in (a, out) + ((b,) if b is not None else ()):
+        if t.dtype not in (torch.float16, torch.float32) or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError("ew_misc operands must be contiguous CUDA float16 / float32 tensors")
+    if out.numel() != a.numel():
+        raise ValueError("ew_misc: out and a differ in size")
+    f16 = lambda t: int(t is not None and t.dtype == torch.float16)  # noqa: E731
+    _lib.lib().call("t2c_ew_misc", EM_OPS[op], _lib.ptr(a), f16(a), _lib.ptr(b), f16(b), _lib.ptr(out), f16(out),
+                    a.numel(), int(H), float(scalar), _lib.stream_ptr())
+    return out
+
+
+def row_mean_f32(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[r] = mean over the last dim of fp32 x."""
+    _check_f32(x, "x")
+    _check_f32(out, "out")
+    cols = x.shape[-1]
+    if out.numel() != x.numel() // cols:
+        raise ValueError("row_mean_f32: out must hold one value per row")
+    _lib.lib().call("t2c_row_mean_f32", _lib.ptr(x), _lib.ptr(out), x.numel() // cols, cols, _lib.stream_ptr())
+    return out

@@ -468,3 +468,95 @@ def _embedding_q8_0(rt, variant, b, s, pc):
 def _index_copy(rt, variant, b, s, pc):
     """cache[b, index[s], :] = src[b, s, :] (index_copy_f32_*.py: the audio-token injection)."""
     kernels.index_copy_rows(b["cache"], b["index"], b["src"])
+
+
+# ------------------------------------------------ optimized Qwen3-ASR text decoder
+@op("LinearNobiasQ4KPairProgram", "LinearNobiasQ4KTripleProgram")
+def _linear_pair_triple(rt, variant, b, s, pc):
+    """Two / three Q4_K weights sharing x, one fused launch (optimized_qwen3_asr
+    linear_nobias_q4_k_{pair,triple}_f32.py; the reference accumulates in fp16, here fp32)."""
+    parts = [i for i in range(3) if f"weight{i}" in b]
+    kernels.linear_multi(b["x"], [(b[f"weight{i}"], "q4_k") for i in parts], s["K"],
+                         outs=[b[f"output{i}"] for i in parts])
+
+
+@op("OptimizedQwen3SdpaCausalCacheWriteProgram")
+def _sdpa_causal_cache_write(rt, variant, b, s, pc):
+    """Writes k (head-major) / v (token-major) rows into head-major caches at cache_position[t]
+    (a row past S skipped), then causal attention of the chunk's queries over the chunk's own keys
+    (optimized_qwen3_asr sdpa_causal_cache_write_f16.py)."""
+    q, k, v, out = b["q"], b["k"], b["v"], b["output"]
+    B, NH, NK, T, S, D = (s[x] for x in ("B", "NH", "NK", "T", "S", "D"))
+    if T > S:
+        raise NotImplementedError(f"{variant.name}: T={T} above the cache length S={S}")
+    pos = b["cache_position"]
+    cs = (NK * S * D, D, S * D)
+    kernels.kv_cache_write(b["k_cache"], k, cache_strides_bsh=cs, seq_len=S, src_strides_bth=(NK * T * D, D, T * D),
+                           batch=B, heads=NK, tokens=T, head_dim=D, positions=pos)
+    kernels.kv_cache_write(b["v_cache"], v, cache_strides_bsh=cs, seq_len=S, src_strides_bth=(T * NK * D, NK * D, D),
+                           batch=B, heads=NK, tokens=T, head_dim=D, positions=pos)
+    vh = torch.empty(B, NK, T, D, dtype=torch.float16, device=v.device)
+    kernels.copy4d(v.permute(0, 2, 1, 3), vh)
+    kernels.attn_prefill(q, k, vh, torch.zeros(B, dtype=torch.int32, device=q.device), batch=B, tokens=T, n_heads=NH, n_kv=NK, head_dim=D, layout="head_major",
+                         q_layout="head_major", out=out)
+
+
+@op("SdpaDecodeCacheWriteF16Program")
+def _sdpa_decode_write_f16(rt, variant, b, s, pc):
+    """Writes new k (head-major) / v (token-major) at cache_position into head-major caches, then one
+    query per head over 0..min(cache_position, S - 1) (optimized_qwen3_asr sdpa_decode_cache_write_f16.py)."""
+    q, out = b["q"], b["output"]
+    B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
+    if s["T"] != 1:
+        raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
+    pos = int(pc["cache_position"])
+    cs = (NK * S * D, D, S * D)
+    if pos < S:
+        kernels.kv_cache_write(b["k_cache"], b["new_k"], cache_strides_bsh=cs, seq_len=S,
+                               src_strides_bth=(NK * D, D, D), batch=B, heads=NK, tokens=1, head_dim=D, position=pos)
+        kernels.kv_cache_write(b["v_cache"], b["new_v"], cache_strides_bsh=cs, seq_len=S,
+                               src_strides_bth=(NK * D, NK * D, D), batch=B, heads=NK, tokens=1, head_dim=D,
+                               position=pos)
+    last = min(pos, S - 1)
+    positions = torch.full((B,), last, dtype=torch.int32, device=q.device)
+    kernels.attn_decode(q, b["k_cache"], b["v_cache"], positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
+                        max_len=S, splits=_decode_splits(last + 1), layout="head_major", out=out)
+
+
+# unfused RMSNorm chain of the exported text norm (optimized_qwen3_asr shaders)
+@op("ExportPowScalarF32Program")
+def _pow_scalar(rt, variant, b, s, pc):
+    """x * x (pow_scalar_f32.py: exponent 2, fp16 in, fp32 out)."""
+    if variant.source not in ("cuda", "") and "v * v" not in variant.source:
+        raise NotImplementedError(f"{variant.name}: only the exponent-2 program is served")
+    kernels.ew_misc("pow2", b["x"], b["output"])
+
+
+@op("ExportRsqrtF32Program")
+def _rsqrt(rt, variant, b, s, pc):
+    """1 / sqrt(x) in fp32 (rsqrt_f32.py)."""
+    kernels.ew_misc("rsqrt", b["x"], b["output"])
+
+
+@op("ExportAddScalarProgram")
+def _add_scalar(rt, variant, b, s, pc):
+    """x + scalar (add_scalar.py; the scalar is a push constant, 1e-6 for the norm's eps)."""
+    kernels.ew_misc("add_scalar", b["x"], b["output"], scalar=float(pc["scalar"]))
+
+
+@op("ExportMeanDimProgram")
+def _mean_dim(rt, variant, b, s, pc):
+    """Mean over the last dim, fp32 (mean_dim_f32.py)."""
+    kernels.row_mean_f32(b["x"], b["output"])
+
+
+@op("ExportMulBroadcastLastProgram")
+def _mul_broadcast_last(rt, variant, b, s, pc):
+    """fp16(x[t, h] * y[t]) (mul_broadcast_last.py: y [1, T, 1] fp32)."""
+    kernels.ew_misc("mul_row", b["x"], b["output"], b["y"], H=int(pc["H"]))
+
+
+@op("ExportMulLeftBroadcastF32XProgram")
+def _mul_left_broadcast(rt, variant, b, s, pc):
+    """fp16(y[t, h] * x[h]) (mul_left_broadcast_f32x_f32.py: x [H] fp32 weight, y fp16)."""
+    kernels.ew_misc("mul_col", b["y"], b["output"], b["x"], H=int(pc["H"]))
