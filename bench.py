@@ -11,8 +11,10 @@ Q6_K (the Q4_K_M head type), embeddings F16, norms F32.  A 1024-token random
 prompt is prefilled, then one "step" = one greedy decode token per sequence,
 replayed from a CUDA graph.  `value` = decode tokens/s over all ranks.
 
-N > 1: one independent replica per GPU (weak scaling, no collective); the
-tensor-parallel path is not part of this run.
+N > 1 (torchrun, one rank per GPU): tensor parallelism over the N ranks (heads,
+rows and the vocabulary sharded; the row-parallel partial sums meet in a
+peer-memory all-reduce), the same model and batch as N = 1, so `scaling` is
+"strong".
 """
 
 from __future__ import annotations
@@ -64,7 +66,12 @@ class ClockSampler:
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
-            time.sleep(0.15)
+            # nvidia-smi's own start-up (driver / NVML initialisation) must be over before the
+            # timed region begins: wait for its first sample (at most 5 s)
+            deadline = time.monotonic() + 5.0
+            while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.02)
+            time.sleep(0.05)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -371,6 +378,10 @@ def main() -> None:
     full_weights = random_weights(cfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
     torch.cuda.synchronize()
     steps, warm = args.steps, args.warmup
+    # every decode step a runner takes (warm-up, timed, e2e warm-up and e2e) gets its own
+    # cache row and token slot: a step past the cache would be rejected by the kernels
+    e2e_reps = min(steps, 200)
+    decode_steps = warm + steps + 3 + e2e_reps
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         import torch.distributed as dist
@@ -384,13 +395,13 @@ def main() -> None:
 
         def new_runner(batch: int):
             return make_tp_runner(cfg, full_weights, rank=rank, tp=world, batch=batch,
-                                  max_seq=PROMPT + steps + warm + 64, max_new_tokens=steps + warm + 8)
+                                  max_seq=PROMPT + decode_steps + 64, max_new_tokens=decode_steps + 8)
     else:
         kcfg, weights = cfg, full_weights
 
         def new_runner(batch: int):
-            return Qwen3Runner(cfg, weights, batch=batch, max_seq=PROMPT + steps + warm + 64,
-                               max_new_tokens=steps + warm + 8)
+            return Qwen3Runner(cfg, weights, batch=batch, max_seq=PROMPT + decode_steps + 64,
+                               max_new_tokens=decode_steps + 8)
     wb = weight_bytes(weights)
 
     # ---- prefill (1024-token prompt), timed with events
@@ -427,10 +438,10 @@ def main() -> None:
     for _ in range(3):
         e2e_step()
     t0 = time.perf_counter()
-    e2e_reps = min(steps, 200)
     for _ in range(e2e_reps):
         e2e_step()
     t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_reps, world)
+    status |= kernels.device_status()
 
     # ---- dominant kernel: gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096), all 36 layers' weights in turn
     x = torch.randn(1, kcfg.hidden, device=dev, dtype=torch.float16)
