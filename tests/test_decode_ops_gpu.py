@@ -135,6 +135,30 @@ def test_attn_prefill(B, T, NH, NK, S, base):
     _close(out.view(B, T, NH, D), ref)
 
 
+@pytest.mark.parametrize("T", [2048, 8192])
+def test_attn_prefill_long(T):
+    """Causal GQA prefill at the attention sweep's long prompts (2k / 8k, batch 1, 32 Q / 8 KV heads) vs a
+    plain PyTorch fp32 reference computed on the GPU."""
+    from torch2vk_b200 import kernels
+
+    torch.manual_seed(T)
+    B, NH, NK, D = 1, 32, 8, 128
+    q = torch.randn(B * T, NH * D, device="cuda", dtype=torch.float16)
+    kc = torch.randn(B, T, NK, D, device="cuda", dtype=torch.float16)
+    vc = torch.randn(B, T, NK, D, device="cuda", dtype=torch.float16)
+    positions = torch.zeros(B, device="cuda", dtype=torch.int32)
+    out = kernels.attn_prefill(q, kc, vc, positions, batch=B, tokens=T, n_heads=NH, n_kv=NK, head_dim=D)
+    qq = q.view(T, NH, D).float().transpose(0, 1)                      # [NH, T, D]
+    kk = kc[0].float().transpose(0, 1).repeat_interleave(NH // NK, 0)  # [NH, T, D]
+    vv = vc[0].float().transpose(0, 1).repeat_interleave(NH // NK, 0)
+    causal = torch.full((T, T), float("-inf"), device="cuda").triu(1)
+    ref = torch.empty(NH, T, D, device="cuda")
+    for h in range(NH):
+        p = torch.softmax(qq[h] @ kk[h].T / math.sqrt(D) + causal, dim=-1)
+        ref[h] = p @ vv[h]
+    _close(out.view(T, NH, D), ref.transpose(0, 1))
+
+
 def test_embedding_f16_and_q4k(oracle):
     from torch2vk_b200 import kernels
 
@@ -294,6 +318,39 @@ def test_attn_decode_fused_matches_unfused_chain(NH, NK, splits, layout):
         _close(out, ref.float(), rel=2e-3, abs_=2e-3)
         if ws is not None:
             assert int(ws[-B * NH:].view(torch.int32).abs().sum()) == 0
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("S,pos,splits", [(16384, 16383, 8), (32768, 32767, 8), (32768, 30001, 16), (4096, 2500, 3)])
+def test_attn_decode_fused_long_context(S, pos, splits):
+    """Decode against 4k-32k caches (the attention sweep's decode mode): with 8 splits each CTA walks
+    up to 4096 positions, i.e. 16 passes of its 8 warps over 32-position tiles; 16 splits take the
+    workspace combine.  Compared with the unfused chain on the same caches."""
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, inv_freq
+
+    torch.manual_seed(S + splits)
+    B, NH, NK, D = 1, 32, 8, 128
+    inv = inv_freq(Qwen3Config.qwen3_8b()).cuda()
+    q = torch.randn(B, NH * D, device="cuda", dtype=torch.float16)
+    k = torch.randn(B, NK * D, device="cuda", dtype=torch.float16)
+    v = torch.randn(B, NK * D, device="cuda", dtype=torch.float16)
+    qw = 1 + 0.1 * torch.randn(D, device="cuda")
+    kw = 1 + 0.1 * torch.randn(D, device="cuda")
+    kc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    vc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    positions = torch.tensor([pos], device="cuda", dtype=torch.int32)
+    kc2, vc2 = kc.clone(), vc.clone()
+    qr = kernels.qk_norm_rope_cache(q, k, v, qw, kw, kc2, vc2, positions, inv, batch=B, tokens=1, n_heads=NH,
+                                    n_kv=NK, head_dim=D)
+    ref = kernels.attn_decode(qr, kc2, vc2, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                              splits=1)
+    ws = kernels.attn_decode_fused_workspace(B, NH, NK, D, splits)
+    out = kernels.attn_decode_fused(q, k, v, qw, kw, inv, kc, vc, positions, batch=B, n_heads=NH, n_kv=NK,
+                                    head_dim=D, splits=splits, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    _close(out, ref.float(), rel=2e-3, abs_=2e-3)
     assert kernels.device_status() == 0
 
 
