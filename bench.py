@@ -349,6 +349,60 @@ def run_profile(args, local: int) -> None:
         raise SystemExit("device status bit set")
 
 
+def run_sweep(args, local: int) -> None:
+    """The isolated quantized-linear sweep: N x K in {4096 x 4096, 12288 x 4096,
+    4096 x 12288, 151936 x 4096}, M in {1, 4, 16, 64, 256, 2048}, Q4_K (int4, 32-value sub-blocks) and
+    Q8_0 (int8, blocks of 32); weights N(0, 0.02) quantized by this repo's GPU quantizer, x N(0, 1) fp16.
+
+    Each point: enough weight copies that one pass over them exceeds L2 (the copies are used in turn);
+    `--steps` launches captured in one CUDA graph (no host launch cost in the figure), `--warmup`
+    replays, then 5 replays timed with CUDA events on the launching stream.
+    Prints one JSON line per point: us per launch, weight GB/s, % of the measured HBM copy
+    bandwidth and TFLOP/s (the roofline that binds: HBM at small M, tensor at large M)."""
+    from torch2vk_b200 import kernels
+
+    pk, src = peaks()
+    hbm = float(pk["hbm_gbs"])
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    torch.manual_seed(0)
+    for kind in ("q4_k", "q8_0"):
+        for n, k in ((4096, 4096), (12288, 4096), (4096, 12288), (151936, 4096)):
+            one = kernels.quantize(torch.randn(n, k, device=dev) * 0.02, kind)
+            wbytes = one.numel() * one.element_size()
+            copies = max(1, -(-256 * 2**20 // wbytes))  # > 2 x L2 per pass
+            ws = [one] + [one.clone() for _ in range(copies - 1)]
+            for m in (1, 4, 16, 64, 256, 2048):
+                x = torch.randn(m, k, device=dev, dtype=torch.float16)
+                out = torch.empty(m, n, device=dev, dtype=torch.float16)
+                i = [0]
+
+                def launch() -> None:
+                    w = ws[i[0] % copies]
+                    i[0] += 1
+                    kernels.linear(x, w, kind, k, out=out)
+
+                launch()  # first call outside the capture (one-time kernel attribute set-up)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(args.steps):
+                        launch()
+                for _ in range(args.warmup):
+                    graph.replay()
+                t = events_time(graph.replay, 5, stream) / args.steps
+                del graph
+                flops = 2.0 * m * n * k
+                print(json.dumps({"kind": kind, "N": n, "K": k, "M": m, "us": round(t * 1e6, 2),
+                                  "weight_GBps": round(wbytes / t / 1e9, 1),
+                                  "hbm_frac": round(wbytes / t / 1e9 / hbm, 3), "TFLOPs": round(flops / t / 1e12, 1),
+                                  "copies": copies, "peak_source": src}), flush=True)
+            del ws, one
+            torch.cuda.empty_cache()
+    if kernels.device_status() != 0:
+        raise SystemExit("device status bit set")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -358,6 +412,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "gemm"], default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the quantized-linear sweep (one JSON line per shape, M and type) instead of the step")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -367,6 +423,9 @@ def main() -> None:
         return
     if args.profile:
         run_profile(args, local)
+        return
+    if args.sweep:
+        run_sweep(args, local)
         return
 
     from torch2vk_b200 import kernels

@@ -81,9 +81,9 @@ def test_linear_parity(oracle, kind, m, nk):
     ref = oracle.matvec(packed, kind, x)
     y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), kind, k)
     # Q4_K, and Q6_K with K a multiple of 2048, run on the tensor-core GEMM for M > 4, whose operands are
-    # fp16 (dequantized weights rounded to fp16, relative 2^-11 each): its bound against the exact
+    # fp16 (dequantized weights rounded to fp16, relative 2^-11 each; Q8_0 as well): its bound against the exact
     # double-precision matvec is 4e-3.
-    tensor_core = m > 4 and (kind == "q4_k" or (kind == "q6_k" and k % 2048 == 0))
+    tensor_core = m > 4 and (kind in ("q4_k", "q8_0") or (kind == "q6_k" and k % 2048 == 0))
     _tol_check(y.float().cpu().numpy(), ref, rel=4e-3 if tensor_core else 2e-3)
 
 
@@ -290,4 +290,25 @@ def test_m1_qwen3_8b_shapes(oracle, n, k, mode):
         y = kernels.linear(xg, torch.from_numpy(packed).cuda(), "q4_k", k,
                            residual=torch.from_numpy(res).cuda() if res is not None else None)
         _tol_check(y.float().cpu().numpy(), ref)
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("m", [16, 64, 300])
+@pytest.mark.parametrize("nk,res", [((4096, 4096), False), ((1030, 12288), True), ((520, 7680), False)])
+def test_linear_q8_0_tensor_core(oracle, m, nk, res):
+    """Q8_0 on the tcgen05 GEMM (272-byte windows of eight 34-byte blocks, d * q rounded to fp16): more
+    tokens, a ragged row count, the residual epilogue and K = 7680 (the ASR conv_out projection)."""
+    from torch2vk_b200 import kernels
+
+    n, k = nk
+    rng = np.random.default_rng(n + k + m)
+    packed = oracle.quantize(_weights(rng, n, k), "q8_0")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    ref = oracle.matvec(packed, "q8_0", x)
+    r = rng.standard_normal((m, n)).astype(np.float16) if res else None
+    if res:
+        ref = ref + r.astype(np.float32)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q8_0", k,
+                       residual=torch.from_numpy(r).cuda() if res else None)
+    _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
     assert kernels.device_status() == 0

@@ -1,4 +1,4 @@
-// Q4_K / Q6_K GEMM on tcgen05 tensor cores with TMEM accumulators (M > 4 tokens:
+// Q4_K / Q6_K / Q8_0 GEMM on tcgen05 tensor cores with TMEM accumulators (M > 4 tokens:
 // prefill, batched decode).  The weights are the A operand: a CTA owns 128
 // weight rows (UMMA M = 128) and mt tokens (UMMA N = mt, <= 256), so
 //   D[n, m] = sum_k deq(W)[n, k] * x[m, k]     (fp32 in TMEM, 128 lanes x mt columns)
@@ -54,7 +54,15 @@ struct RawFmt<T2C_Q6_K> {
     __device__ static int x_of(int b) { return ((210 * b) >> 4) * 4; }
     __device__ static int off_of(int b) { return (210 * b) & 15; }
 };
-constexpr int kRawBytesMax = kRowsT * 224;
+// Q8_0: 34-byte blocks of 32 values; eight of them (272 bytes, a multiple of 16) make the
+// 256-value group of a raw stage, so the TMA window starts on a 16-byte boundary.
+template <>
+struct RawFmt<T2C_Q8_0> {
+    static constexpr int kRow = 272, kBox = 68;
+    __device__ static int x_of(int b) { return b * 68; }
+    __device__ static int off_of(int) { return 0; }
+};
+constexpr int kRawBytesMax = kRowsT * 272;
 constexpr int kABytes = kRowsT * kKC * 2;   // 16 KB of fp16
 constexpr int kDeqWarps = 8;                // dequantization warps (2 threads per weight row)
 constexpr int kIssuer = 8;                  // warp that issues the tcgen05 MMAs
@@ -200,6 +208,40 @@ __device__ __forceinline__ void dequant_q6k_half(uint32_t blk, int ch, int hf, u
             }
         }
         const uint32_t dst = a_row + static_cast<uint32_t>((((4 * hf + j) ^ (r & 7)) << 4));
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
+                     "r"(packed[2]), "r"(packed[3])
+                     : "memory");
+    }
+}
+
+// Q8_0: chunk q (values 64 q .. 64 q + 63) of the 272-byte group of 8 blocks at shared address
+// grp, half hf = block 2 q + hf -> four swizzled 16-byte chunks of fp16 d * q.  Each int8 becomes
+// the exact fp16 integer q ((1024 + (q + 128)) - 1152, byte_perm into 0x64xx), and one paired
+// multiply by the fp16 block scale d gives the only rounding (the reference forms d * q in fp32:
+// linear_nobias_q8_0_matvec_f32.py:84-95).
+__device__ __forceinline__ void dequant_q8_half(uint32_t grp, int q, int hf, uint32_t a_row, int r) {
+    const uint32_t blk = grp + 34u * static_cast<uint32_t>(2 * q + hf);
+    uint32_t w[8], dw[1];
+    lds_words_a2<8>(blk + 2, w);
+    lds_words_a2<1>(blk, dw);
+    const uint32_t dbits = (dw[0] & 0xffffu) * 0x10001u;
+    const __half2 d2 = *reinterpret_cast<const __half2 *>(&dbits);
+    const __half2 off = __float2half2_rn(1152.0f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t packed[4];
+#pragma unroll
+        for (int wi = 0; wi < 2; ++wi) {
+            const uint32_t u = w[2 * c + wi] ^ 0x80808080u;  // q + 128 per byte
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const uint32_t hv = __byte_perm(u, 0x64646464u, e ? 0x4342u : 0x4140u);
+                const __half2 qv = __hsub2(*reinterpret_cast<const __half2 *>(&hv), off);
+                const __half2 v = __hmul2(qv, d2);
+                packed[2 * wi + e] = *reinterpret_cast<const uint32_t *>(&v);
+            }
+        }
+        const uint32_t dst = a_row + static_cast<uint32_t>((((4 * hf + c) ^ (r & 7)) << 4));
         asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
                      "r"(packed[2]), "r"(packed[3])
                      : "memory");
@@ -388,7 +430,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                 failed = 1;
                 break;
             }
-            if (FMT == T2C_Q6_K) {
+            if (FMT == T2C_Q8_0) {
+                dequant_q8_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + r * RF::kRow), q, hf,
+                                a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
+            } else if (FMT == T2C_Q6_K) {
                 dequant_q6k_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + r * RF::kRow) + RF::off_of(sb0 + sb), q, hf,
                                  a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
             } else {
@@ -583,8 +628,8 @@ bool encode_x(CUtensorMap *map, const __half *x, int64_t m, int64_t k, int mt) {
 int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     if (a.M <= 4 || a.K % 256 || a.K > 65536 || a.M > INT32_MAX || a.nw < 1 || a.nw > 3 || (a.w_up && a.nw != 1))
         return T2C_EUNSUPPORTED;
-    if (a.fmt != T2C_Q4_K && a.fmt != T2C_Q6_K) return T2C_EUNSUPPORTED;
-    if (a.fmt == T2C_Q6_K && a.w_up) return T2C_EUNSUPPORTED;
+    if (a.fmt != T2C_Q4_K && a.fmt != T2C_Q6_K && a.fmt != T2C_Q8_0) return T2C_EUNSUPPORTED;
+    if (a.fmt != T2C_Q4_K && a.w_up) return T2C_EUNSUPPORTED;
     if (a.ps && (a.nw != 1 || a.w_up || !a.pt)) return T2C_EUNSUPPORTED;
     for (int i = 0; i < a.nw; ++i)
         if (a.N[i] <= 0 || a.N[i] > INT32_MAX) return T2C_EUNSUPPORTED;
@@ -594,9 +639,9 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     int64_t mt = (a.M + 15) / 16 * 16;
     if (mt > cap) mt = cap;
     p.mt = static_cast<int>(mt);
-    const int64_t row_bytes = a.K / 256 * (a.fmt == T2C_Q6_K ? 210 : 144);
-    const int box = a.fmt == T2C_Q6_K ? 56 : 36;
-    const size_t raw_bytes = static_cast<size_t>(kRowsT) * (a.fmt == T2C_Q6_K ? 224 : 144);
+    const int64_t row_bytes = a.K / 256 * (a.fmt == T2C_Q6_K ? 210 : a.fmt == T2C_Q8_0 ? 272 : 144);
+    const int box = a.fmt == T2C_Q6_K ? 56 : a.fmt == T2C_Q8_0 ? 68 : 36;
+    const size_t raw_bytes = static_cast<size_t>(kRowsT) * (a.fmt == T2C_Q6_K ? 224 : a.fmt == T2C_Q8_0 ? 272 : 144);
     p.nw = a.nw;
     int64_t row_tiles = 0;
     for (int i = 0; i < a.nw; ++i) {
@@ -634,16 +679,19 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
                         (4 + 3 * kNB) * 8 + 16;
     constexpr size_t kLimit = 226 * 1024;  // dynamic bytes; the kernel's static words sit beside them
     if (smem > kLimit) return T2C_EUNSUPPORTED;
-    static bool configured[2][64] = {};
+    static bool configured[3][64] = {};
     int device = 0;
     cudaGetDevice(&device);
     const int slot = device < 0 ? 0 : (device > 63 ? 63 : device);
-    const int fi = a.fmt == T2C_Q6_K ? 1 : 0;
+    const int fi = a.fmt == T2C_Q6_K ? 1 : a.fmt == T2C_Q8_0 ? 2 : 0;
     if (!configured[fi][slot]) {
-        const cudaError_t e = fi ? cudaFuncSetAttribute(qgemm_kernel<T2C_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        static_cast<int>(kLimit))
-                                 : cudaFuncSetAttribute(qgemm_kernel<T2C_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        static_cast<int>(kLimit));
+        const cudaError_t e =
+            fi == 1 ? cudaFuncSetAttribute(qgemm_kernel<T2C_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kLimit))
+            : fi == 2 ? cudaFuncSetAttribute(qgemm_kernel<T2C_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kLimit))
+                      : cudaFuncSetAttribute(qgemm_kernel<T2C_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kLimit));
         if (e != cudaSuccess) return set_error(T2C_ECUDA, "qgemm: cudaFuncSetAttribute failed");
         configured[fi][slot] = true;
     }
@@ -662,8 +710,9 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t err = fi ? cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q6_K>, p)
-                               : cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q4_K>, p);
+    const cudaError_t err = fi == 1   ? cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q6_K>, p)
+                            : fi == 2 ? cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q8_0>, p)
+                                      : cudaLaunchKernelEx(&cfg, qgemm_kernel<T2C_Q4_K>, p);
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "qgemm launch: %s", cudaGetErrorString(err));
     return T2C_OK;
 }

@@ -11,7 +11,7 @@
 namespace t2c {
 
 struct QGemmArgs {
-    int fmt;               // T2C_Q4_K or T2C_Q6_K (Q6_K: K a multiple of 2048, no SwiGLU)
+    int fmt;               // T2C_Q4_K, T2C_Q6_K (K a multiple of 2048) or T2C_Q8_0 (K a multiple of 256); SwiGLU Q4_K only
     int nw;                // weights sharing x (1..3: fused QKV), 1 with SwiGLU
     const uint8_t *w[3];   // Q4_K rows (row_bytes = K / 256 * 144), 16-byte aligned
     const uint8_t *w_up;   // SwiGLU: the up weight (same shape as w[0]), else nullptr

@@ -2134,7 +2134,10 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     for (int i = 0; i < p.nstreams; ++i)
         if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
     const bool swiglu = p.mode == MODE_SWIGLU;
-    const int MT = M <= 1 ? 1 : (M <= 2 ? 2 : 4);
+    // K above 8192: the 2..4-token kernel's x planes over all of K leave too little shared memory
+    // for weight stages, so each token takes its own pass of the M = 1 kernel instead
+    const bool per_token = M > 1 && p.K > 8192;
+    const int MT = (M <= 1 || per_token) ? 1 : (M <= 2 ? 2 : 4);
     p.stage_bytes = kMmaRows * kMmaSegBytes;
     if (mma_fixed_smem(MT, p.K) + 2 * static_cast<size_t>(kMmaWarps) * p.stage_bytes > kSmemLimit) return T2C_OK;
     p.nseg = p.K / (kMmaSegBlocks * 256);
@@ -2155,6 +2158,20 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
             return T2C_OK;  // no map: the dp4a kernels serve this call
     }
     used = true;
+    if (per_token) {
+        for (int64_t t = 0; t < M; ++t) {
+            QParams q = p;
+            q.M = 1;
+            q.x = p.x + t * p.K;
+            for (int i = 0; i < kMaxStreams; ++i) {
+                if (q.s[i].y != nullptr) q.s[i].y += t * q.s[i].n;
+                if (q.s[i].res != nullptr) q.s[i].res += t * q.s[i].n;
+            }
+            const int rc = launch_m1(q, stream);
+            if (rc) return rc;
+        }
+        return T2C_OK;
+    }
     switch (MT) {
         case 1: return launch_m1(p, stream);
         case 2: return launch_mma<2>(p, stream);
@@ -2162,12 +2179,13 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     }
 }
 
-// M > 4, every stream Q4_K, no fused RMSNorm, not argmax: tcgen05 GEMM per stream.
+// M > 4, Q4_K / Q6_K / Q8_0 streams, no fused RMSNorm: tcgen05 GEMM (fused QKV in one launch when the
+// formats agree, else one launch per weight).
 int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     used = false;
     if (mma_disabled() || M <= 4 || p.norm_w != nullptr) return T2C_OK;
     const int fmt = p.s[0].fmt;
-    if (fmt != T2C_Q4_K && fmt != T2C_Q6_K) return T2C_OK;
+    if (fmt != T2C_Q4_K && fmt != T2C_Q6_K && fmt != T2C_Q8_0) return T2C_OK;
     bool same = true;
     for (int i = 1; i < (p.mode == MODE_SWIGLU ? 2 : p.nstreams); ++i) same = same && p.s[i].fmt == fmt;
     QGemmArgs a = {};
@@ -2202,7 +2220,7 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
         // mixed formats (Q4_K_M: Q6_K v): one launch per weight, all or nothing
         for (int i = 0; i < p.nstreams; ++i) {
             const int fi = p.s[i].fmt;
-            const bool ok_fmt = fi == T2C_Q4_K || (fi == T2C_Q6_K && p.K % 2048 == 0);
+            const bool ok_fmt = fi == T2C_Q4_K || fi == T2C_Q8_0 || (fi == T2C_Q6_K && p.K % 2048 == 0);
             if (!ok_fmt || reinterpret_cast<uintptr_t>(p.s[i].w) % 16) return T2C_OK;
         }
         for (int i = 0; i < p.nstreams; ++i) {
@@ -2390,7 +2408,7 @@ extern "C" int t2c_linear_f32(int wtype, const float *x, const void *w, float *y
     __half *y16 = reinterpret_cast<__half *>(static_cast<uint8_t *>(scratch) + (M * K * 2 + 255) / 256 * 256);
     if ((rc = t2c_cast(x, T2C_F32, x16, T2C_F16, M * K, stream))) return rc;
     const cudaStream_t s = as_stream(stream);
-    if (!mma_disabled() && M > 4 && (wtype == T2C_Q4_K || (wtype == T2C_Q6_K && K % 2048 == 0))) {
+    if (!mma_disabled() && M > 4 && (wtype == T2C_Q4_K || wtype == T2C_Q8_0 || (wtype == T2C_Q6_K && K % 2048 == 0))) {
         // tensor-core GEMM writing fp32 directly from the TMEM accumulators
         QGemmArgs a = {};
         a.fmt = wtype;

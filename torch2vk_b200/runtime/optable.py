@@ -50,8 +50,8 @@ def _linear(rt, variant, b, s, pc):
     """y = x @ deq(W)^T (linear_nobias_{q4_k,q6_k,q8_0}[_matvec]_f32.py)."""
     kind = _kind_of(b["weight"], variant.contract.class_name)
     k = int(s["K"])
-    if kind == "q8_0" and b["x"].numel() // k > 8 and k % 8 == 0:
-        # many rows (the ASR conv_out projection): the Q8_0 tensor-core GEMM
+    if kind == "q8_0" and b["x"].numel() // k > 8 and k % 256 != 0 and k % 8 == 0:
+        # many rows and K not a whole number of 256-value groups: the mma.sync Q8_0 GEMM
         n = b["output"].shape[-1]
         kernels.linear_q8_0_bias(b["x"], b["weight"], None, n, out=b["output"])
         return
