@@ -31,8 +31,11 @@ def _q8(oracle, w: np.ndarray):
 
 @pytest.mark.parametrize("m,n,k,bias,gelu", [(1, 96, 128, True, False), (33, 896, 896, True, False),
                                             (130, 3584, 896, True, True), (70, 100, 7680, False, False),
-                                            (5, 64, 40, True, True)])
+                                            (5, 64, 40, True, True), (390, 5120, 1280, True, True),
+                                            (390, 1280, 5120, True, False), (33, 1300, 1280, True, False)])
 def test_linear_q8_0_bias(oracle, m, n, k, bias, gelu):
+    """K a multiple of 256 and more than 4 rows: the tcgen05 GEMM with the bias / GELU epilogue
+    (the encoder's d_model 1280 and FFN 5120 shapes); otherwise the mma.sync Q8_0 GEMM."""
     from torch2vk_b200 import kernels
 
     rng = np.random.default_rng(m + n + k)

@@ -7,6 +7,7 @@
 #include <float.h>
 
 #include "common.cuh"
+#include "qgemm.cuh"
 
 namespace t2c {
 namespace {
@@ -541,6 +542,22 @@ extern "C" int t2c_linear_q8_0_bias(const void *x, const void *w, const float *b
     p.nblk = static_cast<int>((K + 31) / 32);
     p.row_bytes = static_cast<int64_t>(p.nblk) * 34;
     p.act = act;
+    if (M > 4 && K % 256 == 0 && al(w, 16)) {
+        // whole 256-value groups: the tcgen05 GEMM with the bias / GELU epilogue
+        QGemmArgs a = {};
+        a.fmt = T2C_Q8_0;
+        a.nw = 1;
+        a.w[0] = p.w;
+        a.N[0] = N;
+        a.K = K;
+        a.M = M;
+        a.x = p.x;
+        a.y[0] = p.y;
+        a.bias = bias;
+        a.act = act;
+        const int rc = qgemm(a, as_stream(stream));
+        if (rc != T2C_EUNSUPPORTED) return rc;
+    }
     return q8_gemm(p, false, as_stream(stream));
 }
 

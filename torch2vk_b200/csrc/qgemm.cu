@@ -85,6 +85,8 @@ struct GemmParams {
     float *ps;   // argmax mode: best (score, row) per group of 4 rows, [M, G]
     uint32_t *pt;
     int64_t G;
+    const float *bias;  // plain single-weight mode: fp32 [N] added before the activation
+    int act;            // 1: erf GELU
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -117,6 +119,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ float gelu_erf_g(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
 __device__ __forceinline__ float small_u2f_g(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
 
@@ -506,8 +510,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                         float v = __uint_as_float(g[j]);
                         if (swiglu) {
                             v = v / (1.0f + __expf(-v)) * __uint_as_float(u[j]);
-                        } else if (res != nullptr) {
-                            v += __half2float(res[o]);
+                        } else {
+                            if (p.bias != nullptr) v += p.bias[n];
+                            if (p.act) v = gelu_erf_g(v);
+                            if (res != nullptr) v += __half2float(res[o]);
                         }
                         if (youtf != nullptr)
                             youtf[o] = v;
@@ -566,8 +572,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                     float v = g;
                     if (swiglu) {
                         v = v / (1.0f + __expf(-v)) * u;
-                    } else if (res != nullptr) {
-                        v += __half2float(res[o]);
+                    } else {
+                        if (p.bias != nullptr) v += p.bias[n];
+                        if (p.act) v = gelu_erf_g(v);
+                        if (res != nullptr) v += __half2float(res[o]);
                     }
                     if (youtf != nullptr)
                         youtf[o] = v;
@@ -631,6 +639,7 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     if (a.fmt != T2C_Q4_K && a.fmt != T2C_Q6_K && a.fmt != T2C_Q8_0) return T2C_EUNSUPPORTED;
     if (a.fmt != T2C_Q4_K && a.w_up) return T2C_EUNSUPPORTED;
     if (a.ps && (a.nw != 1 || a.w_up || !a.pt)) return T2C_EUNSUPPORTED;
+    if ((a.bias || a.act) && (a.nw != 1 || a.w_up || a.ps)) return T2C_EUNSUPPORTED;
     for (int i = 0; i < a.nw; ++i)
         if (a.N[i] <= 0 || a.N[i] > INT32_MAX) return T2C_EUNSUPPORTED;
     GemmParams p = {};
@@ -658,6 +667,8 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     p.ps = a.ps;
     p.pt = a.pt;
     p.G = a.G;
+    p.bias = a.bias;
+    p.act = a.act;
     if (!encode_x(&p.xmap, a.x, a.M, a.K, p.mt)) return T2C_EUNSUPPORTED;
     // split K over a cluster when there are too few (row tile, token tile) pairs to fill the GPU
     const int64_t tiles = row_tiles * ((a.M + p.mt - 1) / p.mt);

@@ -23,6 +23,8 @@ struct QGemmArgs {
     float *ps;             // argmax mode (LM head): best (score, row) per 4 rows [M, G], else nullptr
     uint32_t *pt;
     int64_t G;
+    const float *bias;     // fp32 [N] added before the activation (one plain weight), or nullptr
+    int act;               // 1: erf GELU after the bias (one plain weight)
 };
 
 // Returns T2C_OK, or T2C_EUNSUPPORTED when the shape is not served (caller falls back).
