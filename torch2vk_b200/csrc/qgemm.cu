@@ -469,7 +469,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
         const int c_end = split_cols ? c_begin + mt / 2 : (warp < 4 ? mt : 0);
         if (p.ksplit > 1) {
             // cluster split-K: every CTA parks its fp32 partials column-major in its own
-            // shared memory (reusing the A buffers), the leader sums them over DSMEM
+            // shared memory (reusing the operand buffers and raw stages: every copy has landed
+            // and every MMA has completed), the leader sums them over DSMEM
             float *red = reinterpret_cast<float *>(smem);
             const int row = 32 * quad + lane;
             if (ok) {
@@ -678,6 +679,18 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     const int nsb_all = static_cast<int>(a.K / 256);
     if (p.mt <= (p.swiglu ? 32 : 64)) {
         while (p.ksplit < 8 && tiles * p.ksplit < sms && nsb_all % (p.ksplit * 2) == 0 && nsb_all / (p.ksplit * 2) >= 2)
+            p.ksplit *= 2;
+    } else {
+        // larger token tiles: split only while the doubled grid still fits on the SMs, and only where
+        // the parked fp32 partials (mt columns x 128 rows, x 2 with SwiGLU) fit in the operand buffers
+        // and raw stages they reuse once the main loop is over
+        const size_t red = static_cast<size_t>(p.swiglu ? 2 : 1) * p.mt * kRowsT * 4;
+        const size_t reusable = static_cast<size_t>(kNB) * kABytes * (p.swiglu ? 2 : 1) +
+                                static_cast<size_t>(kNB) * p.mt * 128 + 2 * raw_bytes * (p.swiglu ? 2 : 1);
+        // (each CTA keeps at least 12 super-blocks: with fewer the DSMEM sum of 128 x mt partials
+        // costs more than the split gains; measured at K = 4096 vs 12288, M = 256)
+        while (red <= reusable && p.ksplit < 8 && tiles * p.ksplit * 2 <= sms && nsb_all % (p.ksplit * 2) == 0 &&
+               nsb_all / (p.ksplit * 2) >= 12)
             p.ksplit *= 2;
     }
     p.M = a.M;
