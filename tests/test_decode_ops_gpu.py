@@ -282,7 +282,7 @@ def test_elementwise_add_swiglu():
 
 @pytest.mark.parametrize("layout", ["token_major", "head_major"])
 @pytest.mark.parametrize("NH,NK,splits", [(32, 8, 1), (32, 8, 5), (32, 8, 8), (32, 8, 23), (16, 8, 7), (8, 8, 3),
-                                          (64, 8, 8), (64, 8, 9)])
+                                          (64, 8, 8), (64, 8, 9), (4, 1, 8), (8, 2, 8)])
 def test_attn_decode_fused_matches_unfused_chain(NH, NK, splits, layout):
     """One-launch decode attention == qk_norm_rope_cache + attn_decode (same caches after, outputs close).
 

@@ -260,7 +260,12 @@ def test_q4k_gemm_cluster_split_k(oracle, m, n, k, swiglu):
 
 
 @pytest.mark.parametrize("n,k,mode", [(4096, 4096, "residual"), (2048, 4096, "swiglu"), (4096, 12288, "plain"),
-                                      (6144, 4096, "qkv"), (4000, 4096, "plain")])
+                                      (6144, 4096, "qkv"), (4000, 4096, "plain"),
+                                      # rank-local shapes of tensor parallelism over 4 / 8 GPUs: row-parallel
+                                      # o_proj / down_proj with K = 1024 / 512 and 3072 / 1536, column-parallel
+                                      # gate / up with 3072 / 1536 rows, QKV of 8 + 2 + 2 / 4 + 1 + 1 heads
+                                      (4096, 512, "residual"), (4096, 1536, "residual"), (4096, 1024, "residual"),
+                                      (1536, 4096, "swiglu"), (768, 4096, "qkv")])
 def test_m1_qwen3_8b_shapes(oracle, n, k, mode):
     """M = 1 at Qwen3-8B sizes (8 warps split K of a 16-row block; K = 12288: three segments per warp;
     a ragged last row block).  Bound as for every matvec: 2e-3 against the double-precision oracle."""
@@ -278,7 +283,7 @@ def test_m1_qwen3_8b_shapes(oracle, n, k, mode):
         y = kernels.linear_swiglu(xg, torch.from_numpy(pg).cuda(), torch.from_numpy(pu).cuda(), "q4_k", k)
         _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
     elif mode == "qkv":
-        specs = [4096, 1024, 1024]
+        specs = [n * 2 // 3, n // 6, n // 6]  # q / k / v rows (6144: 4096 / 1024 / 1024)
         packed = [oracle.quantize(_weights(rng, r, k, special=False), "q4_k") for r in specs]
         outs = kernels.linear_multi(xg, [(torch.from_numpy(p).cuda(), "q4_k") for p in packed], k)
         for out, p in zip(outs, packed):
