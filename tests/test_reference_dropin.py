@@ -158,6 +158,49 @@ def test_reference_quantized_qwen3_dispatch_through_session(ref_modules):
 
 
 @needs_ref
+def test_replay_plan_of_reference_decode_frame(ref_modules):
+    """rt.build_replay_plan over the reference's generated decode frame, then execute_replay with a new
+    cache_position (models/quantized_qwen3/run.py replays its decode step this way): the plan re-issues
+    the frame's dispatches in order, with the dynamic push constant substituted and nothing else changed."""
+    from models.quantized_qwen3.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+    from torch2vk.runtime.replay import execute_replay, stage_replay_step_inputs
+
+    P = 8
+    mt = create_model_tensors(prompt_length=P, max_sequence_length=64, num_hidden_layers=28, num_key_value_heads=8,
+                              head_dim=128, max_new_tokens=4, eos_token_count=2, vocab_size=151936)
+    rt = DrySession(mt)
+    rt.initialize_session_tensors({mt.eos_token_ids: np.array([151643, 151645], np.int64)})
+    zero = np.zeros((1, 8, 64, 128), np.float16)
+    state = {c: zero for c in mt.key_caches + mt.value_caches}
+    state.update({mt.generated_tokens: np.zeros((1, 4), np.int64), mt.generated_length: np.zeros(1, np.uint32),
+                  mt.stopped: np.zeros(1, np.uint32)})
+    with rt.request(inputs={mt.input_ids.name: np.zeros((1, P), np.int64),
+                            mt.text_layers[0].cache_position.name: np.arange(P, dtype=np.int64)}, state=state):
+        _drive_quantized_qwen3(rt, mt, cache_position=P)
+        ctx = rt._frame_history["qwen3.decode.0000"]
+        frame_calls = rt.calls[ctx.start_dispatch_index:ctx.end_dispatch_index]
+        plan = rt.build_replay_plan(name="decode", frame="qwen3.decode.0000")
+        assert plan.num_dispatches == len(frame_calls) > 300
+        assert set(plan.dynamic_push_constant_names) == {"cache_position", "start_position", "theta", "token_index"}
+        with pytest.raises(ValueError, match="unexpected dynamic push constants"):
+            execute_replay(plan, dynamic_push_constants={"nope": 1})
+        stage_replay_step_inputs(rt, plan=plan, inputs={})
+        before = len(rt.calls)
+        execute_replay(plan, dynamic_push_constants={"cache_position": P + 1, "token_index": 2})
+        replayed = rt.calls[before:]
+    assert [c[0] for c in replayed] == [c[0] for c in frame_calls]
+    for old, new in zip(frame_calls, replayed):
+        assert new[2] == old[2]  # shape symbols
+        want = dict(old[3])
+        if "cache_position" in want and old[0].startswith(("sdpa_decode", "kv_cache_write_decode")):
+            want["cache_position"] = P + 1
+        if "token_index" in want:
+            want["token_index"] = 2
+        assert new[3] == want, old[0]
+
+
+@needs_ref
 def test_reference_optimized_qwen3_decode_through_session(ref_modules):
     from models.optimized_qwen3.dispatch.decode_embed import run_decode_embed
     from models.optimized_qwen3.dispatch.decode_layer import run_decode_layer

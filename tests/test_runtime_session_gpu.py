@@ -343,3 +343,65 @@ def test_dispatch_outside_frame_and_missing_weight_key(model):
         with rt.frame("bad"):
             with pytest.raises(ValueError, match="expects dtype"):
                 V.LINEAR_NOBIAS_Q6_K_MATVEC_F32(rt, x=x_in, weight=ws.q, output=y)
+
+
+def test_replay_plans(model, oracle):
+    """rt.build_replay_plan / execute_replay (src/torch2vk/runtime/replay.py:226-364): a frame without
+    push-constant inputs replays from a CUDA graph (first execution captures it) and picks up new step
+    inputs staged with stage_replay_step_inputs; a decode frame replays with a new cache_position."""
+    from torch2vk_b200.runtime import variants as V
+    from torch2vk_b200.runtime.replay import execute_replay, stage_replay_step_inputs
+    from torch2vk_b200.runtime.session import RuntimeSession
+
+    model_dir, packed, norm, _ = model
+    ws = _declare(model_dir)
+    rng = np.random.default_rng(12)
+    x_in = _t("xr", "float16", (1, 3, K), "input")
+    rms, yq = _t("rmsr", "float16", (1, 3, K)), _t("yqr", "float16", (1, 3, 256))
+    xs = [rng.standard_normal((1, 3, K)).astype(np.float16) for _ in range(3)]
+    NH, NK, D, S, T = 4, 2, 128, 64, 5
+    q1 = _t("q1r", "float16", (1, NH, 1, D), "input")
+    k1, v1 = _t("k1r", "float16", (1, NK, 1, D), "input"), _t("v1r", "float16", (1, NK, 1, D), "input")
+    kc, vc = _t("kcr", "float16", (1, NK, S, D), "state"), _t("vcr", "float16", (1, NK, S, D), "state")
+    dec = _t("decr", "float16", (1, NH, 1, D))
+    kbase = (rng.standard_normal((1, NK, S, D)) / 4).astype(np.float16)
+    vbase = rng.standard_normal((1, NK, S, D)).astype(np.float16)
+    qd = (rng.standard_normal((1, NH, 1, D)) / 4).astype(np.float16)
+    kd = (rng.standard_normal((1, NK, 1, D)) / 4).astype(np.float16)
+    vd = rng.standard_normal((1, NK, 1, D)).astype(np.float16)
+    with RuntimeSession.open(model_dir=model_dir, model_tensors=ws) as rt:
+        rt.materialize_model_weights()
+        with rt.request(state={kc: kbase, vc: vbase}):
+            with rt.frame("lin"):
+                rt.register_host_inputs({x_in: xs[0]})
+                V.RMS_NORM_F32W_F32(rt, x=x_in, weight=ws.norm, output=rms)
+                V.LINEAR_NOBIAS_Q4_K_MATVEC_F32(rt, x=rms, weight=ws.q, output=yq)
+                first = rt.readback(yq)
+            plan = rt.build_replay_plan(name="lin", frame="lin", readback_tensors={"y": yq})
+            assert plan.dynamic_push_constant_names == ()
+            outs = []
+            for x in xs:  # execution 1 captures the graph, 2 and 3 replay it
+                stage_replay_step_inputs(rt, plan=plan, inputs={x_in: x})
+                outs.append(np.frombuffer(execute_replay(plan)["y"], np.float16).reshape(1, 3, 256))
+            assert plan.graph is not None
+            with rt.frame("dec"):
+                rt.register_host_inputs({q1: qd, k1: kd, v1: vd})
+                V.KV_CACHE_WRITE_DECODE_F16(rt, cache=kc, src=k1, cache_position=T)
+                V.KV_CACHE_WRITE_DECODE_F16(rt, cache=vc, src=v1, cache_position=T)
+                V.SDPA_DECODE_CACHE_F16(rt, q=q1, k=kc, v=vc, output=dec, cache_position=T)
+            dplan = rt.build_replay_plan(name="dec", frame="dec", readback_tensors={"dec": dec})
+            assert dplan.dynamic_push_constant_names == ("cache_position",)
+            got = np.frombuffer(execute_replay(dplan, dynamic_push_constants={"cache_position": T + 3})["dec"],
+                                np.float16).reshape(1, NH, 1, D)
+            got_kc = rt.readback(kc)
+    assert np.array_equal(outs[0], first)
+    for x, out in zip(xs, outs):
+        xf = x.astype(np.float32).reshape(3, K)
+        r16 = (xf / np.sqrt(np.mean(xf.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * norm).astype(np.float16)
+        _tol(out.reshape(3, -1), oracle.matvec(packed["q.weight"][0], "q4_k", r16), rel=4e-3)
+    assert np.array_equal(got_kc[0, :, T], kd[0, :, 0]) and np.array_equal(got_kc[0, :, T + 3], kd[0, :, 0])
+    kfull, vfull = kbase[0].astype(np.float64).copy(), vbase[0].astype(np.float64).copy()
+    for p in (T, T + 3):
+        kfull[:, p], vfull[:, p] = kd[0, :, 0], vd[0, :, 0]
+    np.testing.assert_allclose(got[0, :, 0].astype(np.float64),
+                               _attn_ref(qd[0, :, 0].astype(np.float64), kfull, vfull, T + 4), atol=2e-3)

@@ -40,6 +40,14 @@ from torch2vk_b200.runtime.shader import (
     TensorFieldSpec,
     eval_expr,
 )
+from torch2vk_b200.runtime.replay import (
+    ReplayDispatch,
+    ReplayPlan,
+    build_replay_plan_impl,
+    push_inputs_of,
+    rebind_replay_plan_impl,
+    replay_plan_compatible_impl,
+)
 from torch2vk_b200.runtime.types import bind_tensor_layout_symbols, concrete_shape, tensor_nbytes
 
 TORCH_DTYPES = {
@@ -289,6 +297,11 @@ class RuntimeSession:
             raise NotImplementedError(f"{variant.name}: no CUDA op for contract class {contract.class_name}")
         buffers = {name: t.buffer for name, t in tensors.items()}
         self._launch(op, variant, buffers, symbols, push_values)
+        log = getattr(self, "_replay_log", None)
+        if log is None:
+            self._replay_log = log = []
+        log.append(ReplayDispatch(op=op, variant=variant, tensors=dict(tensors), symbols=dict(symbols),
+                                  push_values=dict(push_values), push_inputs=push_inputs_of(contract)))
         index = len(self._dispatch_records)
         self._dispatch_records.append(DispatchRecord(
             index=index, frame=frame.frame, shader=variant.name,
@@ -469,6 +482,28 @@ class RuntimeSession:
         self._drop(tensor)
 
     # -------------------------------------------------------------- readback
+    # ------------------------------------------------------------- replay plans
+    def build_replay_plan(self, *, name: str, frame: str,
+                          readback_tensors: Mapping[str, LogicalTensor] | None = None) -> ReplayPlan:
+        """A replayable copy of a finished frame's dispatches (src/torch2vk/runtime/session.py:381-393)."""
+        self._require_open()
+        return build_replay_plan_impl(self, name=name, frame=frame, readback_tensors=readback_tensors)
+
+    def rebind_replay_plan(self, plan: ReplayPlan) -> None:
+        rebind_replay_plan_impl(self, plan)
+
+    def replay_plan_compatible(self, plan: ReplayPlan) -> bool:
+        return replay_plan_compatible_impl(self, plan)
+
+    def cached_replay_plans(self, namespace: str) -> tuple[ReplayPlan, ...]:
+        return tuple(getattr(self, "_replay_cache", {}).get(namespace, ()))
+
+    def cache_replay_plan(self, namespace: str, plan: ReplayPlan) -> None:
+        cache = getattr(self, "_replay_cache", None)
+        if cache is None:
+            self._replay_cache = cache = {}
+        cache.setdefault(namespace, []).append(plan)
+
     def synchronize(self) -> None:
         self.stream.synchronize()
 
