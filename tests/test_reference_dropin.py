@@ -190,6 +190,20 @@ def test_replay_plan_of_reference_decode_frame(ref_modules):
         execute_replay(plan, dynamic_push_constants={"cache_position": P + 1, "token_index": 2})
         replayed = rt.calls[before:]
     assert [c[0] for c in replayed] == [c[0] for c in frame_calls]
+    # the run scripts' cache helpers (models/quantized_qwen3/run.py imports them)
+    from torch2vk.runtime.replay_cache_key import (
+        build_cached_replay_plan,
+        cached_replay_plan,
+        replay_cache_namespace,
+        source_tree_digest,
+    )
+
+    digest = source_tree_digest(REF_SRC / "models" / "quantized_qwen3" / "run.py")
+    assert len(digest) == 16
+    ns = replay_cache_namespace(name="decode", source_digest=digest, model_dir="/tmp", shape_key="p8")
+    assert cached_replay_plan(rt, namespace=ns) is None
+    built = build_cached_replay_plan(rt, namespace=ns, name="decode", frame="qwen3.decode.0000", readback_error="x")
+    assert cached_replay_plan(rt, namespace=ns) is built
     for old, new in zip(frame_calls, replayed):
         assert new[2] == old[2]  # shape symbols
         want = dict(old[3])

@@ -8,6 +8,7 @@ install() registers, in sys.modules,
   torch2vk.runtime.quantized_dispatch -> torch2vk_b200.runtime.quantized_dispatch
   torch2vk.runtime.rope_table      -> torch2vk_b200.runtime.rope_table
   torch2vk.runtime.replay          -> torch2vk_b200.runtime.replay
+  torch2vk.runtime.replay_cache_key -> torch2vk_b200.runtime.replay_cache_key
   torch2vk.vulkan.types            -> torch2vk_b200.runtime.types
   torch2vk.vulkan.shader_execution_requirements -> torch2vk_b200.runtime.execution_requirements
   torch2vk.quantize                -> torch2vk_b200.quantize
@@ -31,6 +32,7 @@ ALIASES = {
     "torch2vk.runtime.quantized_dispatch": "torch2vk_b200.runtime.quantized_dispatch",
     "torch2vk.runtime.rope_table": "torch2vk_b200.runtime.rope_table",
     "torch2vk.runtime.replay": "torch2vk_b200.runtime.replay",
+    "torch2vk.runtime.replay_cache_key": "torch2vk_b200.runtime.replay_cache_key",
     "torch2vk.vulkan.types": "torch2vk_b200.runtime.types",
     "torch2vk.vulkan.shader_execution_requirements": "torch2vk_b200.runtime.execution_requirements",
     "torch2vk.quantize": "torch2vk_b200.quantize",

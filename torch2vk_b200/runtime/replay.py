@@ -65,6 +65,10 @@ class ReplayPlan:
     def num_dispatches(self) -> int:
         return len(self.dispatches)
 
+    @property
+    def readback_slots(self) -> dict[str, LogicalTensor]:
+        return self.readback_tensors
+
     def close(self) -> None:
         if self._closed:
             return
