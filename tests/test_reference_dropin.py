@@ -536,3 +536,101 @@ def test_reference_asr_text_decoder_through_session(ref_modules):
     assert classes <= set(rt._ops), classes - set(rt._ops)
     assert {"ExportEmbeddingQ8_0Program", "ExportIndexCopyF32Program", "Qwen3AsrTokenStoreEosProgram",
             "ExportSdpaDecodeCacheF16Program"} <= classes
+
+
+@needs_ref
+def test_reference_optimized_asr_text_decoder_through_session(ref_modules):
+    """models/optimized_qwen3_asr (run.py:369-420 and its decode step :140-161): audio tower, prefill with
+    the fused Q4_K pair / triple linears, cache-writing attention, the last layer's tail, norm, LM head
+    select and ASR token store, then one decode step with the cache-writing decode attention.  The
+    package's __init__ pulls the forced aligner's audio dependencies (absent here), so the package
+    module is registered without it; its generated tensors / dispatch / shaders modules import as is."""
+    import types
+
+    pkg = types.ModuleType("models.optimized_qwen3_asr")
+    pkg.__path__ = [str(REF_SRC / "models" / "optimized_qwen3_asr")]
+    import models
+
+    sys.modules["models.optimized_qwen3_asr"] = pkg
+    from models.optimized_qwen3_asr.dispatch.audio_encoder import run_audio_encoder
+    from models.optimized_qwen3_asr.dispatch.audio_inject import run_audio_inject
+    from models.optimized_qwen3_asr.dispatch.decode_embed import run_decode_embed
+    from models.optimized_qwen3_asr.dispatch.decode_layer import run_decode_layer
+    from models.optimized_qwen3_asr.dispatch.decode_norm import run_decode_norm
+    from models.optimized_qwen3_asr.dispatch.embed_tokens import run_embed_tokens
+    from models.optimized_qwen3_asr.dispatch.text_layer import run_text_last_layer_tail, run_text_layer
+    from models.optimized_qwen3_asr.dispatch.text_norm import run_text_norm
+    from models.optimized_qwen3_asr.shaders.lm_head_q6_k_argmax_partial_f16 import LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16
+    from models.optimized_qwen3_asr.shaders.qwen3_asr_token_store_eos import QWEN3_ASR_TOKEN_STORE_EOS
+    from models.optimized_qwen3_asr.shaders.qwen3_token_select_reduce_chunks_f32 import (
+        QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32,
+    )
+    from models.optimized_qwen3_asr.shaders.qwen3_token_select_reduce_f32 import QWEN3_TOKEN_SELECT_REDUCE_F32
+    from models.optimized_qwen3_asr.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+    from torch2vk.runtime.rope_table import ROPE_TABLE_F32, run_rope_table_f32
+
+    assert models is not None
+    frames, chunks, tokens, prompt = 3000, 30, 390, 400
+    mt = create_model_tensors(input_ids_shape=(1, prompt), attention_mask_shape=(1, prompt),
+                              input_features_shape=(1, 128, frames), feature_attention_mask_shape=(1, frames),
+                              prompt_length=prompt, audio_chunk_count=chunks, audio_sequence_length=tokens,
+                              max_sequence_length=prompt + 16, num_hidden_layers=28, num_key_value_heads=8,
+                              head_dim=128, max_new_tokens=4, eos_token_count=2, vocab_size=151936)
+
+    def head(x):  # run.py:104-127
+        LM_HEAD_Q6_K_ARGMAX_PARTIAL_F16(rt, x=x, weight=mt.lm_head.p_weight, partial_scores=mt.lm_head_partial_scores,
+                                        partial_tokens=mt.lm_head_partial_tokens)
+        QWEN3_TOKEN_SELECT_REDUCE_CHUNKS_F32(rt, scores=mt.lm_head_partial_scores, tokens=mt.lm_head_partial_tokens,
+                                             chunk_scores=mt.lm_head_chunk_scores,
+                                             chunk_tokens=mt.lm_head_chunk_tokens)
+        QWEN3_TOKEN_SELECT_REDUCE_F32(rt, partial_scores=mt.lm_head_chunk_scores,
+                                      partial_tokens=mt.lm_head_chunk_tokens, eos_token_ids=mt.eos_token_ids,
+                                      next_token=mt.next_token, done=mt.done)
+
+    def store(i):
+        QWEN3_ASR_TOKEN_STORE_EOS(rt, next_token=mt.next_token, token_index=i, done=mt.done,
+                                  generated_tokens=mt.generated_tokens, generated_length=mt.generated_length,
+                                  stopped=mt.stopped)
+
+    ae = mt.audio_encoder
+    rt = DrySession(mt)
+    rt.initialize_session_tensors({mt.eos_token_ids: np.array([151643, 151645], np.int64)})
+    inputs = {ae.x.name: np.zeros(ae.x.spec.shape, np.float16),
+              ae.position_embedding.name: np.zeros(ae.position_embedding.spec.shape, np.float16),
+              ae.compact_index.name: np.arange(tokens, dtype=np.int64),
+              ae.attention_mask.name: np.zeros(ae.attention_mask.spec.shape, np.float16),
+              "input_ids": np.zeros((1, prompt), np.int64),
+              mt.position_ids.name: np.zeros((3, 1, prompt), np.int64),
+              mt.audio_inject.audio_positions.name: np.arange(5, 5 + tokens, dtype=np.int64),
+              mt.text_layers[0].cache_position.name: np.arange(prompt, dtype=np.int64)}
+    zero = np.zeros((1, 8, prompt + 16, 128), np.float16)
+    state = {c: zero for c in mt.key_caches + mt.value_caches}
+    state.update({mt.generated_tokens: np.zeros((1, 4), np.int64), mt.generated_length: np.zeros(1, np.uint32),
+                  mt.stopped: np.zeros(1, np.uint32)})
+    with rt.request(inputs=inputs, state=state):
+        with rt.frame("spike.audio"):
+            run_audio_encoder(rt)
+        run_rope_table_f32(rt, start_position=0, theta=1e6, cos=mt.prefill_rope.cos, sin=mt.prefill_rope.sin,
+                           frame_name="spike.text.prefill_rope")
+        with rt.frame("spike.text.prefill"):
+            run_embed_tokens(rt)
+            run_audio_inject(rt)
+            for i in range(len(mt.text_layers) - 1):
+                run_text_layer(rt, i)
+            run_text_last_layer_tail(rt)
+            run_text_norm(rt)
+            head(mt.text_norm.mul_1)
+            store(0)
+        with rt.frame("spike.decode.0000"):
+            ROPE_TABLE_F32(rt, start_position=prompt, theta=1e6, cos=mt.decode_rope.cos, sin=mt.decode_rope.sin)
+            run_decode_embed(rt)
+            for i in range(len(mt.decode_layers)):
+                run_decode_layer(rt, i, cache_position=prompt)
+            run_decode_norm(rt)
+            head(mt.decode_norm.mul_1)
+            store(1)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    assert {"LinearNobiasQ4KPairProgram", "LinearNobiasQ4KTripleProgram", "OptimizedQwen3SdpaCausalCacheWriteProgram",
+            "SdpaDecodeCacheWriteF16Program", "Qwen3AsrTokenStoreEosProgram"} <= classes, classes

@@ -482,6 +482,13 @@ class RuntimeSession:
         self._drop(tensor)
 
     # -------------------------------------------------------------- readback
+    def bind_model_tensors(self, model_tensors: object) -> None:
+        """Binds (or replaces) the declared model tensors of this session
+        (src/torch2vk/runtime/session.py:269-278)."""
+        self._require_open()
+        collect_named_logical_tensors(model_tensors)
+        self._model_tensors = model_tensors
+
     # ------------------------------------------------------------- replay plans
     def build_replay_plan(self, *, name: str, frame: str,
                           readback_tensors: Mapping[str, LogicalTensor] | None = None) -> ReplayPlan:
