@@ -267,6 +267,12 @@ int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D
  *   src/torch2vk/runtime/rope_table.py:124-160 */
 int t2c_rope_table_f32(float *cos_out, float *sin_out, int64_t B, int64_t T, int64_t D, float theta,
                        int64_t start_position, float attention_scaling, void *stream);
+/* The same tables (fp16, or fp32 when out_f32) with the start position read from device
+ * memory (int64), so a captured CUDA graph replays them at each step's position.  Replaces the
+ * push-constant input start_position of RopeTableF32Program / RopeTableOutputF32Program under
+ * replay (src/torch2vk/runtime/rope_table.py:31-160, src/torch2vk/runtime/replay.py:163-364). */
+int t2c_rope_table_dev(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                       const int64_t *start_position_dev, float attention_scaling, int out_f32, void *stream);
 /*
  * Per-row RMSNorm + rotate-half RoPE from fp16 cos/sin tables [B, T, D]; x
  * [B, T, G, D] fp16, out addressed by strides (b, g, t).  Replaces

@@ -196,3 +196,34 @@ def test_rope_table_f32_and_quantize_ops(oracle):
         v = SimpleNamespace(name=cls, contract=SimpleNamespace(class_name=cls))
         optable.OPS[cls](None, v, {"x": torch.from_numpy(x).cuda(), "output": out}, {"R": 24, "K": 256}, {})
         assert np.array_equal(out.cpu().numpy().view(np.uint8).reshape(24, -1), oracle.quantize(x, kind)), cls
+
+
+def test_large_cache_write_and_rope_table():
+    """Launches above the surface helper's grid cap (148 x 64 blocks of 256 threads): a 4096-token
+    head-major cache write (8 heads x 128, 4.2M elements, kv_cache_write_f16.py:22-92) and a rope table
+    of 2 x 10000 x 128 entries write every element; the table with its start read from device memory
+    equals the host-start one."""
+    from torch2vk_b200 import kernels
+
+    B, H, T, D, S = 1, 8, 4096, 128, 4160
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    src = torch.randn(B, H, T, D, device="cuda", generator=gen).half()
+    cache = torch.zeros(B, H, S, D, dtype=torch.float16, device="cuda")
+    pos = torch.arange(40, 40 + T, dtype=torch.int64, device="cuda")
+    kernels.kv_cache_write(cache, src, cache_strides_bsh=(H * S * D, D, S * D), seq_len=S,
+                           src_strides_bth=(H * T * D, D, T * D), batch=B, heads=H, tokens=T, head_dim=D, positions=pos)
+    assert torch.equal(cache[:, :, 40:40 + T], src) and not cache[:, :, :40].any() and not cache[:, :, 40 + T:].any()
+    cache.zero_()
+    kernels.kv_cache_write(cache, src, cache_strides_bsh=(H * S * D, D, S * D), seq_len=S,
+                           src_strides_bth=(H * T * D, D, T * D), batch=B, heads=H, tokens=T, head_dim=D, position=64)
+    assert torch.equal(cache[:, :, 64:64 + T], src)
+
+    c16, s16 = (torch.empty(2, 10000, 128, dtype=torch.float16, device="cuda") for _ in range(2))
+    kernels.rope_table(c16, s16, theta=1e6, start_position=7)
+    ref = np.cos((7 + np.arange(10000, dtype=np.float64))[:, None] * (1e6 ** (-(2 * (np.arange(128) % 64)) / 128)))
+    assert np.abs(c16[1].double().cpu().numpy() - ref).max() < 2e-3
+    for dt in (torch.float16, torch.float32):
+        cd, sd = (torch.empty(2, 10000, 128, dtype=dt, device="cuda") for _ in range(2))
+        kernels.rope_table(cd, sd, theta=1e6, start_position=0,
+                           start_position_dev=torch.tensor([7], dtype=torch.int64, device="cuda"))
+        assert torch.equal(cd.half(), c16) and torch.equal(sd.half(), s16)

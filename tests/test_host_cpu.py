@@ -72,3 +72,33 @@ def test_session_requires_cuda():
         pytest.skip("a GPU is present")
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         RuntimeSession.open()
+
+
+def test_replay_push_slots_and_guards():
+    """Captured replay plans: a DynamicPush hands ops device slots that are rewritten from each step's
+    value, records guards, and bakes any host use of the value behind an equality guard."""
+    import numpy as np
+
+    from torch2vk_b200.runtime.replay import DynamicPush, PushSlots
+
+    slots = PushSlots(torch.device("cpu"))
+    pos = DynamicPush(slots, "cache_position", 300)
+    a = pos.device(torch.int64, 3, ramp=True)
+    b = pos.device(torch.int32, 4, clamp_max=301)
+    assert pos.device(torch.int64, 3, ramp=True).data_ptr() == a.data_ptr()  # shared slot
+    assert a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0
+    pos.guard(0, 640)
+    theta = DynamicPush(slots, "theta", 1e6)
+    assert float(theta) == 1e6 and theta == 1e6
+    slots.names = frozenset({"cache_position", "theta"})
+    img = slots.host_image({"cache_position": 305, "theta": 1e6})
+    off_a, _ = slots.slots[("cache_position", torch.int64, 3, True, None)]
+    off_b, _ = slots.slots[("cache_position", torch.int32, 4, False, 301)]
+    assert np.frombuffer(img[off_a:off_a + 24].tobytes(), np.int64).tolist() == [305, 306, 307]
+    assert np.frombuffer(img[off_b:off_b + 16].tobytes(), np.int32).tolist() == [301] * 4
+    assert slots.admits({"cache_position": 639, "theta": 1e6})
+    assert not slots.admits({"cache_position": 640, "theta": 1e6})  # outside the range guard
+    assert not slots.admits({"cache_position": 5, "theta": 1e4})  # baked value changed
+    assert not slots.admits({"cache_position": 5})  # another set of names than the capture's
+    assert int(DynamicPush(slots, "token_index", 7)) + 1 == 8
+    assert ("token_index", "eq", 7, None) in slots.guards

@@ -405,3 +405,91 @@ def test_replay_plans(model, oracle):
         kfull[:, p], vfull[:, p] = kd[0, :, 0], vd[0, :, 0]
     np.testing.assert_allclose(got[0, :, 0].astype(np.float64),
                                _attn_ref(qd[0, :, 0].astype(np.float64), kfull, vfull, T + 4), atol=2e-3)
+
+
+def test_replay_plan_dynamic_graph(model):
+    """A decode frame whose ops take dynamic push constants (rope start_position / theta, cache_position,
+    token_index) is captured into a CUDA graph after its first execution; later steps replay the graph
+    with the values written to device slots (src/torch2vk/runtime/replay.py:226-364), and a step that
+    changes a baked value (theta) runs the dispatches directly."""
+    from torch2vk_b200.runtime import variants as V
+    from torch2vk_b200.runtime.replay import execute_replay, stage_replay_step_inputs
+    from torch2vk_b200.runtime.session import RuntimeSession
+
+    model_dir = model[0]
+    ws = _declare(model_dir)
+    NH, NK, D, S, P, G = 4, 2, 128, 640, 300, 8
+    rng = np.random.default_rng(21)
+    q1 = _t("q1g", "float16", (1, NH, 1, D), "input")
+    k1, v1 = _t("k1g", "float16", (1, NK, 1, D), "input"), _t("v1g", "float16", (1, NK, 1, D), "input")
+    v1t = _t("v1tg", "float16", (1, 1, NK, D), "input")
+    nt, dn = _t("ntg", "int64", (1, 1), "input"), _t("dng", "uint32", (1,), "input")
+    kc, vc = _t("kcg", "float16", (1, NK, S, D), "state"), _t("vcg", "float16", (1, NK, S, D), "state")
+    kt, vt = _t("ktg", "float16", (1, S, NK, D), "state"), _t("vtg", "float16", (1, S, NK, D), "state")
+    gen = _t("geng", "int64", (1, G), "state")
+    glen, stp = _t("glg", "uint32", (1,), "state"), _t("stg", "uint32", (1,), "state")
+    dec, dec2 = _t("decg", "float16", (1, NH, 1, D)), _t("dec2g", "float16", (1, NH, 1, D))
+    cos, sin = _t("cosg", "float16", (1, 1, D)), _t("sing", "float16", (1, 1, D))
+    kbase = (rng.standard_normal((1, NK, S, D)) / 4).astype(np.float16)
+    vbase = rng.standard_normal((1, NK, S, D)).astype(np.float16)
+    qd = (rng.standard_normal((1, NH, 1, D)) / 4).astype(np.float16)
+    steps = [((rng.standard_normal((1, NK, 1, D)) / 4).astype(np.float16),
+              rng.standard_normal((1, NK, 1, D)).astype(np.float16)) for _ in range(5)]
+
+    def step_inputs(j):
+        kd, vd = steps[j]
+        return {q1: qd, k1: kd, v1: vd, v1t: vd.transpose(0, 2, 1, 3).copy(),
+                nt: np.array([[1000 + j]], np.int64), dn: np.zeros(1, np.uint32)}
+
+    def cos_ref(p, theta):
+        inv = theta ** (-2.0 * (np.arange(D) % (D // 2)) / D)
+        return np.cos(p * inv)
+
+    zeros = {gen: np.zeros((1, G), np.int64), glen: np.zeros(1, np.uint32), stp: np.zeros(1, np.uint32)}
+    with RuntimeSession.open(model_dir=model_dir, model_tensors=ws) as rt:
+        rt.materialize_model_weights()
+        state = {kc: kbase, vc: vbase, kt: kbase.transpose(0, 2, 1, 3).copy(),
+                 vt: vbase.transpose(0, 2, 1, 3).copy(), **zeros}
+        with rt.request(state=state):
+            with rt.frame("step"):
+                rt.register_host_inputs(step_inputs(0))
+                V.ROPE_TABLE_F32(rt, cos=cos, sin=sin, start_position=P, theta=1e6)
+                V.KV_CACHE_WRITE_DECODE_F16(rt, cache=kc, src=k1, cache_position=P)
+                V.KV_CACHE_WRITE_DECODE_F16(rt, cache=vc, src=v1, cache_position=P)
+                V.SDPA_DECODE_CACHE_F16(rt, q=q1, k=kc, v=vc, output=dec, cache_position=P)
+                V.SDPA_DECODE_CACHE_WRITE_F32(rt, q=q1, new_k=k1, new_v=v1t, k_cache=kt, v_cache=vt, output=dec2,
+                                              cache_position=P)
+                V.QWEN3_TOKEN_STORE_EOS(rt, next_token=nt, done=dn, generated_tokens=gen, generated_length=glen,
+                                        stopped=stp, token_index=0)
+            plan = rt.build_replay_plan(name="step", frame="step",
+                                        readback_tensors={"dec": dec, "dec2": dec2, "cos": cos})
+            assert set(plan.dynamic_push_constant_names) == {"cache_position", "start_position", "theta",
+                                                             "token_index"}
+            outs = []
+            for j in range(1, 5):  # step 1 runs directly and captures; steps 2-4 replay the graph
+                stage_replay_step_inputs(rt, plan=plan, inputs=step_inputs(j))
+                r = execute_replay(plan, dynamic_push_constants={"cache_position": P + j, "start_position": P + j,
+                                                                 "theta": 1e6, "token_index": j})
+                outs.append({n: np.frombuffer(v, np.float16) for n, v in r.items()})
+            assert plan.graph is not None and plan.push_slots is not None
+            assert (plan.direct_executions, plan.graph_replays) == (1, 3)
+            r = execute_replay(plan, dynamic_push_constants={"cache_position": P + 4, "start_position": P + 4,
+                                                             "theta": 1e4, "token_index": 4})
+            assert (plan.direct_executions, plan.graph_replays) == (2, 3)
+            cos_1e4 = np.frombuffer(r["cos"], np.float16)
+            got_kc, got_kt, got_gen = rt.readback(kc), rt.readback(kt), rt.readback(gen)
+    kfull, vfull = kbase[0].astype(np.float64).copy(), vbase[0].astype(np.float64).copy()
+    kfull[:, P], vfull[:, P] = steps[0][0][0, :, 0], steps[0][1][0, :, 0]
+    for j, o in enumerate(outs, start=1):
+        p = P + j
+        kfull[:, p], vfull[:, p] = steps[j][0][0, :, 0], steps[j][1][0, :, 0]
+        ref = _attn_ref(qd[0, :, 0].astype(np.float64), kfull, vfull, p + 1)
+        np.testing.assert_allclose(o["dec"].reshape(NH, D), ref, atol=2e-3)
+        np.testing.assert_allclose(o["dec2"].reshape(NH, D), ref, atol=2e-3)
+        np.testing.assert_allclose(o["cos"].astype(np.float64), cos_ref(p, 1e6), atol=2e-3)
+    np.testing.assert_allclose(cos_1e4.astype(np.float64), cos_ref(P + 4, 1e4), atol=2e-3)
+    for j in range(5):
+        assert np.array_equal(got_kc[0, :, P + j], steps[j][0][0, :, 0])
+        assert np.array_equal(got_kt[0, P + j], steps[j][0][0, :, 0])
+    assert np.array_equal(got_kc[0, :, :P], kbase[0, :, :P]) and np.array_equal(got_kc[0, :, P + 5:], kbase[0, :, P + 5:])
+    assert got_gen[0, :5].tolist() == [1000, 1001, 1002, 1003, 1004]

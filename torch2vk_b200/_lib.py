@@ -92,6 +92,7 @@ _SIGNATURES: dict[str, list] = {
     "t2c_attn_prefill_masked_f32": [_vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 8 + [_f32, _vp],
     "t2c_embedding_f32": [_i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "t2c_rope_table_f32": [_vp, _vp, _i64, _i64, _i64, _f32, _i64, _f32, _vp],
+    "t2c_rope_table_dev": [_vp, _vp, _i64, _i64, _i64, _f32, _vp, _f32, _i32, _vp],
     "t2c_index_copy_rows": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "t2c_embedding_q8_0": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "t2c_ew_misc": [_i32, _vp, _i32, _vp, _i32, _vp, _i32, _i64, _i64, _f32, _vp],

@@ -76,25 +76,28 @@ __global__ void elementwise4d_kernel(int op, int f32, const void *__restrict__ a
 }
 
 // cos/sin [B, T, D] fp16: angle = (start + t) * theta^(-2 (d mod D/2) / D), times attention_scaling
-// (src/torch2vk/runtime/rope_table.py:31-121 arithmetic).
+// (src/torch2vk/runtime/rope_table.py:31-121 arithmetic); start read from start_dev when non-NULL.
 template <typename OT>
 __global__ void rope_table_kernel(OT *__restrict__ cos_out, OT *__restrict__ sin_out, int64_t B, int T, int D,
-                                  float theta, int64_t start, float scaling) {
+                                  float theta, int64_t start, const int64_t *__restrict__ start_dev, float scaling) {
     pdl_wait();
     pdl_trigger();
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= B * T * D) return;
-    const int64_t td = i % (static_cast<int64_t>(T) * D);
-    const int t = static_cast<int>(td / D);
-    const int d = static_cast<int>(td - static_cast<int64_t>(t) * D);
-    const int f = d % (D / 2);
-    const float exponent = (2.0f * static_cast<float>(f)) / static_cast<float>(D);
-    const float inv_freq = powf(theta, -exponent);
-    const float angle = static_cast<float>(start + t) * inv_freq;
-    float sn, cs;
-    sincosf(angle, &sn, &cs);
-    cos_out[i] = static_cast<OT>(cs * scaling);
-    sin_out[i] = static_cast<OT>(sn * scaling);
+    if (start_dev) start = *start_dev;
+    // grid-stride: the launch helper caps the grid
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < B * T * D;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t td = i % (static_cast<int64_t>(T) * D);
+        const int t = static_cast<int>(td / D);
+        const int d = static_cast<int>(td - static_cast<int64_t>(t) * D);
+        const int f = d % (D / 2);
+        const float exponent = (2.0f * static_cast<float>(f)) / static_cast<float>(D);
+        const float inv_freq = powf(theta, -exponent);
+        const float angle = static_cast<float>(start + t) * inv_freq;
+        float sn, cs;
+        sincosf(angle, &sn, &cs);
+        cos_out[i] = static_cast<OT>(cs * scaling);
+        sin_out[i] = static_cast<OT>(sn * scaling);
+    }
 }
 
 // One warp per (b, t, g) row of D values: RMSNorm with fp32 weight, then
@@ -339,20 +342,22 @@ __global__ void kv_write_kernel(__half *__restrict__ cache, const __half *__rest
                                 int64_t cb, int64_t cs, int64_t ch, int64_t sb, int64_t st, int64_t sh, int64_t S) {
     pdl_wait();
     pdl_trigger();
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<int64_t>(B) * H * T * D) return;
-    const int d = static_cast<int>(i % D);
-    int64_t r = i / D;
-    const int t = static_cast<int>(r % T);
-    r /= T;
-    const int h = static_cast<int>(r % H);
-    const int b = static_cast<int>(r / H);
-    const int64_t pos = positions ? positions[t] : position + t;
-    if (pos < 0 || pos >= S) {
-        report_device_error(T2C_EINVAL);
-        return;
+    // grid-stride: the launch helper caps the grid
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<int64_t>(B) * H * T * D;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int d = static_cast<int>(i % D);
+        int64_t r = i / D;
+        const int t = static_cast<int>(r % T);
+        r /= T;
+        const int h = static_cast<int>(r % H);
+        const int b = static_cast<int>(r / H);
+        const int64_t pos = positions ? positions[t] : position + t;
+        if (pos < 0 || pos >= S) {
+            report_device_error(T2C_EINVAL);
+            continue;
+        }
+        cache[b * cb + pos * cs + h * ch + d] = src[b * sb + t * st + h * sh + d];
     }
-    cache[b * cb + pos * cs + h * ch + d] = src[b * sb + t * st + h * sh + d];
 }
 
 __device__ __forceinline__ bool better(float s, uint32_t t, float bs, uint32_t bt) {
@@ -477,7 +482,7 @@ extern "C" int t2c_rope_table(void *cos_out, void *sin_out, int64_t B, int64_t T
     if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table: bad arguments");
     return launch(rope_table_kernel<__half>, B * T * D, 256, as_stream(stream), static_cast<__half *>(cos_out),
                   static_cast<__half *>(sin_out), B, static_cast<int>(T), static_cast<int>(D), theta, start_position,
-                  attention_scaling);
+                  static_cast<const int64_t *>(nullptr), attention_scaling);
 }
 
 extern "C" int t2c_rms_norm_rope(const void *x, const float *w, const void *cos_t, const void *sin_t, void *out,
@@ -673,7 +678,21 @@ extern "C" int t2c_rope_table_f32(float *cos_out, float *sin_out, int64_t B, int
                                   int64_t start_position, float attention_scaling, void *stream) {
     if (!cos_out || !sin_out || B <= 0 || T <= 0 || D <= 0 || D % 2) return set_error(T2C_EINVAL, "rope_table_f32: bad arguments");
     return launch(rope_table_kernel<float>, B * T * D, 256, as_stream(stream), cos_out, sin_out, B, static_cast<int>(T),
-                  static_cast<int>(D), theta, start_position, attention_scaling);
+                  static_cast<int>(D), theta, start_position, static_cast<const int64_t *>(nullptr), attention_scaling);
+}
+
+extern "C" int t2c_rope_table_dev(void *cos_out, void *sin_out, int64_t B, int64_t T, int64_t D, float theta,
+                                  const int64_t *start_position_dev, float attention_scaling, int out_f32,
+                                  void *stream) {
+    if (!cos_out || !sin_out || !start_position_dev || B <= 0 || T <= 0 || D <= 0 || D % 2)
+        return set_error(T2C_EINVAL, "rope_table_dev: bad arguments");
+    if (out_f32)
+        return launch(rope_table_kernel<float>, B * T * D, 256, as_stream(stream), static_cast<float *>(cos_out),
+                      static_cast<float *>(sin_out), B, static_cast<int>(T), static_cast<int>(D), theta, int64_t{0},
+                      start_position_dev, attention_scaling);
+    return launch(rope_table_kernel<__half>, B * T * D, 256, as_stream(stream), static_cast<__half *>(cos_out),
+                  static_cast<__half *>(sin_out), B, static_cast<int>(T), static_cast<int>(D), theta, int64_t{0},
+                  start_position_dev, attention_scaling);
 }
 
 extern "C" int t2c_ew_misc(int op, const void *a, int a_f16, const void *b, int b_f16, void *out, int out_f16, int64_t n,

@@ -370,11 +370,18 @@ def elementwise4d(op: str, a: torch.Tensor, b: torch.Tensor | None, out: torch.T
 
 
 def rope_table(cos_out: torch.Tensor, sin_out: torch.Tensor, *, theta: float, start_position: int,
-               attention_scaling: float = 1.0) -> None:
-    """cos / sin [B, T, D] (fp16, or fp32 for the output-f32 variant) at positions start_position + t."""
+               attention_scaling: float = 1.0, start_position_dev: torch.Tensor | None = None) -> None:
+    """cos / sin [B, T, D] (fp16, or fp32 for the output-f32 variant) at positions start_position + t;
+    with start_position_dev (int64 [1] on the GPU) the start is read from device memory instead."""
     b, t, d = cos_out.shape
     if cos_out.dtype != sin_out.dtype or cos_out.dtype not in (torch.float16, torch.float32):
         raise ValueError("cos / sin must both be float16 or both float32")
+    if start_position_dev is not None:
+        _check(start_position_dev, torch.int64, "start_position_dev")
+        _lib.lib().call("t2c_rope_table_dev", _lib.ptr(cos_out), _lib.ptr(sin_out), b, t, d, float(theta),
+                        _lib.ptr(start_position_dev), float(attention_scaling),
+                        1 if cos_out.dtype == torch.float32 else 0, _lib.stream_ptr())
+        return
     name = "t2c_rope_table_f32" if cos_out.dtype == torch.float32 else "t2c_rope_table"
     _lib.lib().call(name, _lib.ptr(cos_out), _lib.ptr(sin_out), b, t, d, float(theta), int(start_position),
                     float(attention_scaling), _lib.stream_ptr())

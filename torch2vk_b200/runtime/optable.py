@@ -17,6 +17,7 @@ from collections.abc import Callable
 import torch
 
 from torch2vk_b200 import kernels
+from torch2vk_b200.runtime.replay import DynamicPush
 
 OpFn = Callable[..., None]
 OPS: dict[str, OpFn] = {}
@@ -97,8 +98,10 @@ def _rms_norm_rope_transpose(rt, variant, b, s, pc):
 def _rope_table(rt, variant, b, s, pc):
     """cos/sin [B,T,D] at positions start_position + t, fp16 (runtime/rope_table.py:31-121) or fp32
     (RopeTableOutputF32Program, :124-160)."""
-    kernels.rope_table(b["cos"], b["sin"], theta=float(pc["theta"]), start_position=int(pc["start_position"]),
-                       attention_scaling=float(pc.get("attention_scaling", 1.0)))
+    start = pc["start_position"]
+    dev = start.device(torch.int64) if isinstance(start, DynamicPush) else None
+    kernels.rope_table(b["cos"], b["sin"], theta=float(pc["theta"]), start_position=0 if dev is not None else int(start),
+                       attention_scaling=float(pc.get("attention_scaling", 1.0)), start_position_dev=dev)
 
 
 # ---------------------------------------------------------------- elementwise
@@ -195,10 +198,13 @@ def _kv_write(rt, variant, b, s, pc):
     (kv_cache_write_f16.py:22-92, kv_cache_write_decode_f16.py:23-85)."""
     cache, src = b["cache"], b["src"]
     B, H, S, D, T = (s[k] for k in ("B", "H", "S", "D", "T"))
-    pos_t = b.get("cache_position")
+    pos_t, pos = b.get("cache_position"), pc.get("cache_position", 0)
+    if pos_t is None and isinstance(pos, DynamicPush):  # captured replay plan: rows start + t from device memory
+        pos.guard(0, S - T + 1)
+        pos_t, pos = pos.device(torch.int64, T, ramp=True), 0
     kernels.kv_cache_write(cache, src, cache_strides_bsh=(H * S * D, D, S * D), seq_len=S,
                            src_strides_bth=(H * T * D, D, T * D), batch=B, heads=H, tokens=T, head_dim=D,
-                           positions=pos_t, position=int(pc.get("cache_position", 0)))
+                           positions=pos_t, position=int(pos))
 
 
 @op("OptimizedQwen3TokenMajorKvCacheWriteF16PairProgram", "OptimizedQwen3TokenMajorKvCacheWriteF16TripleProgram")
@@ -243,6 +249,30 @@ def _decode_splits(max_len: int) -> int:
     return max(1, min(64, max_len // 256))
 
 
+def _decode_at(rt, pc, B: int, S: int):
+    """(write position, attention positions int32 [B], splits) of a decode step at push constant
+    cache_position.  The write position is an int, or None past the cache's end (the step writes
+    nothing); while a replay plan is captured it is an int64 [1] device slot and the graph serves
+    only steps with 0 <= cache_position < S."""
+    p = pc["cache_position"]
+    if isinstance(p, DynamicPush):
+        p.guard(0, S)
+        return p.device(torch.int64, 1), p.device(torch.int32, B, clamp_max=S - 1), _decode_splits(S)
+    pos = int(p)
+    last = min(pos, S - 1)
+    return (pos if pos < S else None), _positions(rt, B, last), _decode_splits(last + 1)
+
+
+def _write_decode_kv(b, wpos, cache_strides, NK: int, D: int, S: int, B: int) -> None:
+    if wpos is None:
+        return
+    dev = isinstance(wpos, torch.Tensor)
+    for cache, src, sb in ((b["k_cache"], b["new_k"], D), (b["v_cache"], b["new_v"], NK * D)):
+        kernels.kv_cache_write(cache, src, cache_strides_bsh=cache_strides, seq_len=S, src_strides_bth=(NK * D, sb, D),
+                               batch=B, heads=NK, tokens=1, head_dim=D, positions=wpos if dev else None,
+                               position=0 if dev else wpos)
+
+
 @op("ExportSdpaDecodeCacheF16Program")
 def _sdpa_decode(rt, variant, b, s, pc):
     """One query per head over head-major cache[0..cache_position] (sdpa_decode_cache_f16.py:22-136)."""
@@ -250,9 +280,15 @@ def _sdpa_decode(rt, variant, b, s, pc):
     B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
     if s["T"] != 1:
         raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
-    pos = min(int(pc["cache_position"]), S - 1)
-    kernels.attn_decode(q, k, v, _positions(rt, B, pos), batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
-                        splits=_decode_splits(pos + 1), layout="head_major", out=out)
+    p = pc["cache_position"]
+    if isinstance(p, DynamicPush):  # captured replay plan: lengths from device memory
+        p.guard(0, None)
+        positions, splits = p.device(torch.int32, B, clamp_max=S - 1), _decode_splits(S)
+    else:
+        pos = min(int(p), S - 1)
+        positions, splits = _positions(rt, B, pos), _decode_splits(pos + 1)
+    kernels.attn_decode(q, k, v, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                        splits=splits, layout="head_major", out=out)
 
 
 @op("SdpaDecodeCacheWriteF32Program")
@@ -263,17 +299,10 @@ def _sdpa_decode_write(rt, variant, b, s, pc):
     B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
     if s["T"] != 1:
         raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
-    pos = int(pc["cache_position"])
-    if pos < S:
-        cs = (S * NK * D, NK * D, D)
-        kernels.kv_cache_write(b["k_cache"], b["new_k"], cache_strides_bsh=cs, seq_len=S,
-                               src_strides_bth=(NK * D, D, D), batch=B, heads=NK, tokens=1, head_dim=D, position=pos)
-        kernels.kv_cache_write(b["v_cache"], b["new_v"], cache_strides_bsh=cs, seq_len=S,
-                               src_strides_bth=(NK * D, NK * D, D), batch=B, heads=NK, tokens=1, head_dim=D,
-                               position=pos)
-    last = min(pos, S - 1)
-    kernels.attn_decode(q, b["k_cache"], b["v_cache"], _positions(rt, B, last), batch=B, n_heads=NH, n_kv=NK,
-                        head_dim=D, max_len=S, splits=_decode_splits(last + 1), layout="token_major", out=out)
+    wpos, positions, splits = _decode_at(rt, pc, B, S)
+    _write_decode_kv(b, wpos, (S * NK * D, NK * D, D), NK, D, S, B)
+    kernels.attn_decode(q, b["k_cache"], b["v_cache"], positions, batch=B, n_heads=NH, n_kv=NK,
+                        head_dim=D, max_len=S, splits=splits, layout="token_major", out=out)
 
 
 # -------------------------------------------------------- embedding / LM head / tokens
@@ -315,9 +344,13 @@ def _select(rt, variant, b, s, pc):
     "Qwen3AsrTokenStoreEosProgram", "Qwen3AsrTokenStoreProgram")
 def _store(rt, variant, b, s, pc):
     """generated_tokens[token_index] = next_token unless stopped; EOS stops (qwen3_token_store.py)."""
+    index, dev = pc["token_index"], None
+    if isinstance(index, DynamicPush):  # captured replay plan: the index from device memory
+        index.guard(-(1 << 31), 1 << 31)
+        index, dev = 0, index.device(torch.int32)
     kernels.token_store(b["next_token"].view(1), b["done"].view(torch.int32).view(1), b["generated_tokens"],
                         b["generated_length"].view(torch.int32).view(1), b["stopped"].view(torch.int32).view(1),
-                        token_index=int(pc["token_index"]), stop_on_eos=bool(pc.get("stop_on_eos", 1)))
+                        token_index=int(index), token_index_dev=dev, stop_on_eos=bool(pc.get("stop_on_eos", 1)))
 
 
 def served_class_names() -> tuple[str, ...]:
@@ -509,18 +542,10 @@ def _sdpa_decode_write_f16(rt, variant, b, s, pc):
     B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
     if s["T"] != 1:
         raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
-    pos = int(pc["cache_position"])
-    cs = (NK * S * D, D, S * D)
-    if pos < S:
-        kernels.kv_cache_write(b["k_cache"], b["new_k"], cache_strides_bsh=cs, seq_len=S,
-                               src_strides_bth=(NK * D, D, D), batch=B, heads=NK, tokens=1, head_dim=D, position=pos)
-        kernels.kv_cache_write(b["v_cache"], b["new_v"], cache_strides_bsh=cs, seq_len=S,
-                               src_strides_bth=(NK * D, NK * D, D), batch=B, heads=NK, tokens=1, head_dim=D,
-                               position=pos)
-    last = min(pos, S - 1)
-    positions = torch.full((B,), last, dtype=torch.int32, device=q.device)
+    wpos, positions, splits = _decode_at(rt, pc, B, S)
+    _write_decode_kv(b, wpos, (NK * S * D, D, S * D), NK, D, S, B)
     kernels.attn_decode(q, b["k_cache"], b["v_cache"], positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
-                        max_len=S, splits=_decode_splits(last + 1), layout="head_major", out=out)
+                        max_len=S, splits=splits, layout="head_major", out=out)
 
 
 # unfused RMSNorm chain of the exported text norm (optimized_qwen3_asr shaders)

@@ -12,12 +12,20 @@ came from push-constant inputs (those are the plan's dynamic push constants,
 e.g. `cache_position`, `start_position`, `token_index`).  The frame released
 its workspace at exit, so the plan owns device buffers for every frame-lifetime
 tensor it touches; request state, session tensors and weights are bound from
-their LogicalTensors.  `execute_replay` re-launches the ops on the session
-stream with the dynamic values substituted.  A plan without push-constant
-inputs is captured into a CUDA graph on its first execution and replayed from
-the graph afterwards (if a capture fails the plan stays on direct launches);
-`rebind_replay_plan` drops that graph so the next execution binds the current
-buffers.
+their LogicalTensors.  `execute_replay` launches the ops on the session
+stream with the dynamic values substituted.  Every plan is captured into a
+CUDA graph after its first (direct) execution and replayed from the graph
+afterwards.  Dynamic push constants reach a captured graph through device
+memory: an op that reads such a value on the GPU asks the `DynamicPush`
+wrapper it is handed during capture for a slot of the plan's push buffer, and
+the plan rewrites the slots from the step's values (one host-to-device copy)
+before each replay; an op may attach guards (e.g. `cache_position < S`, where
+its direct form takes another branch), and any host use of the value (int(),
+float(), comparisons) bakes the captured value in behind an equality guard.
+An execution whose values fail a guard, or that names a different set of
+dynamic push constants than the capture did, launches the ops directly.  If a
+capture fails the plan stays on direct launches; `rebind_replay_plan` drops
+the graph so the next execution binds the current buffers.
 """
 
 from __future__ import annotations
@@ -32,6 +40,164 @@ import torch
 from torch2vk_b200.runtime.logical import LogicalTensor, TensorLifetime, TensorRole
 from torch2vk_b200.runtime.shader import PushConstantInput
 from torch2vk_b200.runtime.types import concrete_shape, tensor_nbytes
+
+
+_PUSH_BUFFER_BYTES = 1 << 16
+_SLOT_ALIGN = 16
+
+
+class DynamicPush:
+    """A dynamic push-constant value as an op sees it while its plan is captured into a CUDA graph."""
+
+    __slots__ = ("_slots", "name", "value")
+
+    def __init__(self, slots: "PushSlots", name: str, value: int | float):
+        self._slots, self.name, self.value = slots, name, value
+
+    def device(self, dtype: torch.dtype, count: int = 1, *, ramp: bool = False,
+               clamp_max: int | None = None) -> torch.Tensor:
+        """A device tensor of `count` elements holding value (+ i when ramp), capped at clamp_max,
+        rewritten from each step's value before every replay."""
+        return self._slots.slot(self.name, dtype, count, ramp, clamp_max)
+
+    def guard(self, lo: int | float | None = None, hi: int | float | None = None) -> int | float:
+        """The graph serves only steps with lo <= value < hi; returns the captured value."""
+        self._slots.guards.add((self.name, "range", lo, hi))
+        return self.value
+
+    def _bake(self) -> int | float:
+        self._slots.guards.add((self.name, "eq", self.value, None))
+        return self.value
+
+    def __int__(self) -> int:
+        return int(self._bake())
+
+    def __index__(self) -> int:
+        return int(self._bake())
+
+    def __float__(self) -> float:
+        return float(self._bake())
+
+    def __bool__(self) -> bool:
+        return bool(self._bake())
+
+    def __eq__(self, other) -> bool:
+        return self._bake() == (other._bake() if isinstance(other, DynamicPush) else other)
+
+    def __ne__(self, other) -> bool:
+        return not self.__eq__(other)
+
+    def __lt__(self, other) -> bool:
+        return self._bake() < other
+
+    def __le__(self, other) -> bool:
+        return self._bake() <= other
+
+    def __gt__(self, other) -> bool:
+        return self._bake() > other
+
+    def __ge__(self, other) -> bool:
+        return self._bake() >= other
+
+    def __hash__(self) -> int:
+        return hash(self._bake())
+
+    def __add__(self, other):
+        return self._bake() + other
+
+    __radd__ = __add__
+
+    def __sub__(self, other):
+        return self._bake() - other
+
+    def __rsub__(self, other):
+        return other - self._bake()
+
+    def __mul__(self, other):
+        return self._bake() * other
+
+    __rmul__ = __mul__
+
+    def __floordiv__(self, other):
+        return self._bake() // other
+
+    def __mod__(self, other):
+        return self._bake() % other
+
+    def __neg__(self):
+        return -self._bake()
+
+    def __repr__(self) -> str:
+        return f"DynamicPush({self.name}={self.value!r})"
+
+
+_NP = {torch.int32: np.int32, torch.int64: np.int64, torch.float32: np.float32}
+
+
+class PushSlots:
+    """Device slots of a captured plan's dynamic push constants and the guards of the capture."""
+
+    def __init__(self, device: torch.device):
+        self.buffer = torch.zeros(_PUSH_BUFFER_BYTES, dtype=torch.uint8, device=device)
+        self.used = 0
+        self.slots: dict[tuple, tuple[int, int]] = {}  # (name, dtype, count, ramp, clamp_max) -> (offset, nbytes)
+        self.guards: set[tuple] = set()
+        self.names: frozenset[str] = frozenset()
+        self._staging: list[torch.Tensor] | None = None
+        self._events: list[torch.cuda.Event | None] = [None, None]
+        self._turn = 0
+
+    def slot(self, name: str, dtype: torch.dtype, count: int, ramp: bool, clamp_max: int | None) -> torch.Tensor:
+        if dtype not in _NP:
+            raise TypeError(f"push slot dtype {dtype} is not supported")
+        key = (name, dtype, int(count), bool(ramp), clamp_max)
+        if key not in self.slots:
+            nbytes = int(count) * torch.empty((), dtype=dtype).element_size()
+            if self.used + nbytes > _PUSH_BUFFER_BYTES:
+                raise RuntimeError("replay push buffer is full")
+            self.slots[key] = (self.used, nbytes)
+            self.used += (nbytes + _SLOT_ALIGN - 1) // _SLOT_ALIGN * _SLOT_ALIGN
+        off, nbytes = self.slots[key]
+        return self.buffer[off:off + nbytes].view(dtype)
+
+    def admits(self, push: Mapping[str, int | float]) -> bool:
+        if frozenset(push) != self.names:
+            return False
+        for name, kind, a, b in self.guards:
+            v = push[name]
+            if kind == "eq" and v != a:
+                return False
+            if kind == "range" and ((a is not None and v < a) or (b is not None and v >= b)):
+                return False
+        return True
+
+    def host_image(self, push: Mapping[str, int | float]) -> np.ndarray:
+        img = np.zeros(max(self.used, _SLOT_ALIGN), np.uint8)
+        for (name, dtype, count, ramp, clamp_max), (off, nbytes) in self.slots.items():
+            vals = np.full(count, push[name], dtype=np.float64 if dtype == torch.float32 else np.int64)
+            if ramp:
+                vals = vals + np.arange(count)
+            if clamp_max is not None:
+                vals = np.minimum(vals, clamp_max)
+            img[off:off + nbytes] = np.frombuffer(vals.astype(_NP[dtype]).tobytes(), np.uint8)
+        return img
+
+    def upload(self, push: Mapping[str, int | float], stream: torch.cuda.Stream) -> None:
+        """Writes the slots for this step on `stream` from one of two pinned staging images (an image
+        is rewritten only after its previous copy has finished)."""
+        img = self.host_image(push)
+        if self._staging is None:
+            self._staging = [torch.empty(img.size, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        i = self._turn
+        self._turn ^= 1
+        if self._events[i] is not None:
+            self._events[i].synchronize()
+        self._staging[i].numpy()[:] = img
+        with torch.cuda.stream(stream):
+            self.buffer[:img.size].copy_(self._staging[i], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        self._events[i] = ev
 
 
 @dataclass
@@ -59,6 +225,9 @@ class ReplayPlan:
     owned: dict[int, LogicalTensor] = field(default_factory=dict)
     graph: torch.cuda.CUDAGraph | None = None
     graph_failed: bool = False
+    push_slots: PushSlots | None = None
+    graph_replays: int = 0
+    direct_executions: int = 0
     _closed: bool = False
 
     @property
@@ -74,6 +243,7 @@ class ReplayPlan:
             return
         self._closed = True
         self.graph = None
+        self.push_slots = None
         self.workspace.clear()
         self.owned.clear()
 
@@ -140,14 +310,32 @@ def _refresh_inputs(rt, plan: ReplayPlan) -> None:
                 dst.copy_(arr.reshape(dst.shape), non_blocking=False)
 
 
-def _launch_all(rt, plan: ReplayPlan, push: Mapping[str, int | float]) -> None:
+def _launch_all(rt, plan: ReplayPlan, push: Mapping[str, int | float], slots: PushSlots | None = None) -> None:
     for d in plan.dispatches:
         values = dict(d.push_values)
         for field_name, input_name in d.push_inputs.items():
             if input_name in push:
-                values[field_name] = push[input_name]
+                values[field_name] = DynamicPush(slots, input_name, push[input_name]) if slots is not None \
+                    else push[input_name]
         buffers = {n: _buffer(rt, plan, t) for n, t in d.tensors.items()}
         rt._launch(d.op, d.variant, buffers, d.symbols, values)
+
+
+def _capture(rt, plan: ReplayPlan, push: Mapping[str, int | float]) -> None:
+    """Captures the plan's dispatches into a CUDA graph (nothing runs); dynamic values go through slots."""
+    rt.stream.synchronize()
+    slots = PushSlots(rt.device) if push else None
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph, stream=rt.stream):
+            _launch_all(rt, plan, push, slots)
+    except Exception:
+        plan.graph_failed = True
+        torch.cuda.synchronize(rt.device)
+        return
+    if slots is not None:
+        slots.names = frozenset(push)
+    plan.graph, plan.push_slots = graph, slots
 
 
 def execute_replay(plan: ReplayPlan, dynamic_symbols: Mapping[str, int] | None = None,
@@ -163,23 +351,19 @@ def execute_replay(plan: ReplayPlan, dynamic_symbols: Mapping[str, int] | None =
         raise ValueError(f"ReplayPlan {plan.name!r} got unexpected dynamic push constants: {sorted(unexpected)}")
     rt = plan.session
     _refresh_inputs(rt, plan)
-    static = not plan.dynamic_push_constant_names and isinstance(getattr(rt, "stream", None), torch.cuda.Stream)
-    if static and plan.graph is not None:
+    on_cuda = isinstance(getattr(rt, "stream", None), torch.cuda.Stream)
+    slots = plan.push_slots
+    if on_cuda and plan.graph is not None and (slots.admits(push) if slots is not None else not push):
+        if slots is not None:
+            slots.upload(push, rt.stream)
         with torch.cuda.stream(rt.stream):
             plan.graph.replay()
-    elif static and not plan.graph_failed:
-        _launch_all(rt, plan, push)  # the first run doubles as the warm-up of every op
-        rt.stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        try:
-            with torch.cuda.graph(graph, stream=rt.stream):
-                _launch_all(rt, plan, push)
-            plan.graph = graph
-        except Exception:
-            plan.graph_failed = True
-            torch.cuda.synchronize(rt.device)
+        plan.graph_replays += 1
     else:
-        _launch_all(rt, plan, push)
+        _launch_all(rt, plan, push)  # the first run doubles as the warm-up of every op
+        plan.direct_executions += 1
+        if on_cuda and plan.graph is None and not plan.graph_failed:
+            _capture(rt, plan, push)
     results: dict[str, bytes] = {}
     if plan.readback_tensors:
         rt.synchronize()
@@ -209,6 +393,7 @@ def stage_replay_step_inputs(rt, *, plan: ReplayPlan, inputs: Mapping[LogicalTen
 def rebind_replay_plan_impl(rt, plan: ReplayPlan) -> None:
     """External buffers may have moved (a new request): the next execution binds them afresh."""
     plan.graph = None
+    plan.push_slots = None
 
 
 def replay_plan_compatible_impl(rt, plan: ReplayPlan) -> bool:
