@@ -403,6 +403,72 @@ def run_sweep(args, local: int) -> None:
         raise SystemExit("device status bit set")
 
 
+def run_session(args, local: int) -> None:
+    """The bs1 decode step of a Qwen3-0.6B-shaped model dispatched through RuntimeSession, the
+    reference-facing path (286 dispatches a step): `--warmup` direct frames, then a replay plan of the
+    last one, captured into a CUDA graph on its first execution and stepped `--steps` times with the
+    step's input staged from the host and the next token read back every step.  One JSON line."""
+    import tempfile
+
+    from torch2vk_b200.qwen3_session import SessionDecodeModel
+    from torch2vk_b200.runtime.replay import execute_replay, stage_replay_step_inputs
+    from torch2vk_b200.runtime.session import RuntimeSession
+
+    torch.cuda.set_device(local)
+    m = SessionDecodeModel()
+    d = Path(tempfile.mkdtemp())
+    m.write_gguf(d)
+    x = (np.random.default_rng(0).standard_normal((1, 1, m.hidden)) * 0.5).astype(np.float16)
+    eos = np.array([151643, 151645], np.int64)
+    start = 128
+    with RuntimeSession.open(model_dir=d, model_tensors=m.weights) as rt:
+        rt.materialize_model_weights()
+        with rt.request(state=m.request_state()):
+            direct = []
+            for j in range(args.warmup):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                with rt.frame(f"decode.{j}"):
+                    rt.register_host_inputs({m.x_in: x, m.eos: eos})
+                    m.step(rt, start + j, j)
+                    rt.readback(m.next_token)
+                direct.append((time.perf_counter() - t0) * 1e3)
+            plan = rt.build_replay_plan(name="decode", frame=f"decode.{args.warmup - 1}",
+                                        readback_tensors={"next": m.next_token})
+
+            def run(j: int) -> None:
+                stage_replay_step_inputs(rt, plan=plan, inputs={m.x_in: x, m.eos: eos})
+                execute_replay(plan, dynamic_push_constants={"cache_position": start + j, "start_position": start + j,
+                                                             "theta": 1e6, "token_index": j})
+
+            j = args.warmup
+            for _ in range(3):  # direct execution + capture, then two replays
+                run(j)
+                j += 1
+            steps = max(1, min(args.steps, 511 - j))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                run(j)
+                j += 1
+            step_ms = (time.perf_counter() - t0) * 1e3 / steps
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(rt.stream):
+                e0.record()
+                for _ in range(50):
+                    plan.graph.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            graph_ms = e0.elapsed_time(e1) / 50
+    print(json.dumps({"metric": "session_decode_tok_s", "value": round(1e3 / step_ms, 1), "unit": "tok/s",
+                      "steps": steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+                      "graph_device_ms": round(graph_ms, 4), "direct_frame_ms": round(float(np.median(direct)), 3),
+                      "dispatches": plan.num_dispatches, "graph_replays": plan.graph_replays,
+                      "direct_executions": plan.direct_executions, "dtype": "fp16 x Q4_K / Q6_K", "data": "synthetic",
+                      "config": {"workload": "Qwen3-0.6B-shaped bs1 decode through RuntimeSession "
+                                             "(optimized variants, replay plan with device push constants)"}}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -414,6 +480,8 @@ def main() -> None:
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",
                     help="the quantized-linear sweep (one JSON line per shape, M and type) instead of the step")
+    ap.add_argument("--session", action="store_true",
+                    help="the decode step through RuntimeSession and a replay plan (one JSON line) instead")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -426,6 +494,9 @@ def main() -> None:
         return
     if args.sweep:
         run_sweep(args, local)
+        return
+    if args.session:
+        run_session(args, local)
         return
 
     from torch2vk_b200 import kernels
