@@ -249,7 +249,7 @@ def _decode_splits(max_len: int) -> int:
     return max(1, min(64, max_len // 256))
 
 
-def _decode_at(rt, pc, B: int, S: int):
+def _decode_at(pc, B: int, S: int, device: torch.device):
     """(write position, attention positions int32 [B], splits) of a decode step at push constant
     cache_position.  The write position is an int, or None past the cache's end (the step writes
     nothing); while a replay plan is captured it is an int64 [1] device slot and the graph serves
@@ -260,7 +260,8 @@ def _decode_at(rt, pc, B: int, S: int):
         return p.device(torch.int64, 1), p.device(torch.int32, B, clamp_max=S - 1), _decode_splits(S)
     pos = int(p)
     last = min(pos, S - 1)
-    return (pos if pos < S else None), _positions(rt, B, last), _decode_splits(last + 1)
+    positions = torch.full((B,), last, dtype=torch.int32, device=device)
+    return (pos if pos < S else None), positions, _decode_splits(last + 1)
 
 
 def _write_decode_kv(b, wpos, cache_strides, NK: int, D: int, S: int, B: int) -> None:
@@ -299,7 +300,7 @@ def _sdpa_decode_write(rt, variant, b, s, pc):
     B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
     if s["T"] != 1:
         raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
-    wpos, positions, splits = _decode_at(rt, pc, B, S)
+    wpos, positions, splits = _decode_at(pc, B, S, q.device)
     _write_decode_kv(b, wpos, (S * NK * D, NK * D, D), NK, D, S, B)
     kernels.attn_decode(q, b["k_cache"], b["v_cache"], positions, batch=B, n_heads=NH, n_kv=NK,
                         head_dim=D, max_len=S, splits=splits, layout="token_major", out=out)
@@ -542,7 +543,7 @@ def _sdpa_decode_write_f16(rt, variant, b, s, pc):
     B, NH, NK, S, D = s["B"], s["NH"], s["NK"], s["S"], s["D"]
     if s["T"] != 1:
         raise ValueError(f"{variant.name}: decode attention takes T=1, got {s['T']}")
-    wpos, positions, splits = _decode_at(rt, pc, B, S)
+    wpos, positions, splits = _decode_at(pc, B, S, q.device)
     _write_decode_kv(b, wpos, (NK * S * D, D, S * D), NK, D, S, B)
     kernels.attn_decode(q, b["k_cache"], b["v_cache"], positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D,
                         max_len=S, splits=splits, layout="head_major", out=out)
