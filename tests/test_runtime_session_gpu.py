@@ -493,3 +493,48 @@ def test_replay_plan_dynamic_graph(model):
         assert np.array_equal(got_kt[0, P + j], steps[j][0][0, :, 0])
     assert np.array_equal(got_kc[0, :, :P], kbase[0, :, :P]) and np.array_equal(got_kc[0, :, P + 5:], kbase[0, :, P + 5:])
     assert got_gen[0, :5].tolist() == [1000, 1001, 1002, 1003, 1004]
+
+
+def test_session_decode_plan_matches_direct_frames(tmp_path):
+    """A Qwen3-shaped decode step through the session (torch2vk_b200.qwen3_session: the optimized
+    variants of src/models/optimized_qwen3/dispatch/decode_layer.py:36-128 and the greedy head) gives
+    bit-identical next-token scores and tokens whether each step is dispatched as a frame or replayed
+    from the captured graph of a replay plan."""
+    from torch2vk_b200.qwen3_session import SessionDecodeModel
+    from torch2vk_b200.runtime.replay import execute_replay, stage_replay_step_inputs
+    from torch2vk_b200.runtime.session import RuntimeSession
+
+    m = SessionDecodeModel(layers=2, vocab=4096, max_seq=256, seed=3)
+    m.write_gguf(tmp_path)
+    rng = np.random.default_rng(4)
+    xs = [(rng.standard_normal((1, 1, m.hidden)) * 0.5).astype(np.float16) for _ in range(6)]
+    eos = np.array([4094, 4095], np.int64)
+    start = 40
+    with RuntimeSession.open(model_dir=tmp_path, model_tensors=m.weights) as rt:
+        rt.materialize_model_weights()
+        with rt.request(state=m.request_state()):
+            direct = []
+            for j in range(6):
+                with rt.frame(f"d{j}"):
+                    rt.register_host_inputs({m.x_in: xs[j], m.eos: eos})
+                    m.step(rt, start + j, j)
+                    direct.append((rt.readback(m.cs), rt.readback(m.next_token)))
+            gen_direct = rt.readback(m.generated)
+        with rt.request(state=m.request_state()):
+            with rt.frame("f0"):
+                rt.register_host_inputs({m.x_in: xs[0], m.eos: eos})
+                m.step(rt, start, 0)
+            plan = rt.build_replay_plan(name="decode", frame="f0",
+                                        readback_tensors={"cs": m.cs, "next": m.next_token})
+            replayed = []
+            for j in range(1, 6):
+                stage_replay_step_inputs(rt, plan=plan, inputs={m.x_in: xs[j], m.eos: eos})
+                r = execute_replay(plan, dynamic_push_constants={"cache_position": start + j,
+                                                                 "start_position": start + j, "theta": 1e6,
+                                                                 "token_index": j})
+                replayed.append((np.frombuffer(r["cs"], np.float32), np.frombuffer(r["next"], np.int64)))
+            gen_replay = rt.readback(m.generated)
+    assert (plan.direct_executions, plan.graph_replays) == (1, 4)
+    for (cs_d, nt_d), (cs_r, nt_r) in zip(direct[1:], replayed):
+        assert np.array_equal(cs_d.reshape(-1), cs_r) and np.array_equal(nt_d.reshape(-1), nt_r)
+    assert np.array_equal(gen_direct[0, :6], gen_replay[0, :6])
