@@ -9,6 +9,7 @@ import ctypes
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -102,3 +103,45 @@ def test_replay_push_slots_and_guards():
     assert not slots.admits({"cache_position": 5})  # another set of names than the capture's
     assert int(DynamicPush(slots, "token_index", 7)) + 1 == 8
     assert ("token_index", "eq", 7, None) in slots.guards
+
+
+def test_decode_ops_read_dynamic_push_constants_from_slots(monkeypatch):
+    """While a replay plan is captured, the decode ops hand the kernels device slots instead of host
+    values: attention lengths (cache_position clamped to S - 1), the cache-write row, the rope-table
+    start and the token index; their guards bound the steps the graph serves."""
+    from types import SimpleNamespace
+
+    from torch2vk_b200.runtime import optable
+    from torch2vk_b200.runtime.replay import DynamicPush, PushSlots
+
+    calls = []
+    for name in ("attn_decode", "kv_cache_write", "rope_table", "token_store"):
+        monkeypatch.setattr(optable.kernels, name, lambda *a, _n=name, **k: calls.append((_n, a, k)))
+    slots = PushSlots(torch.device("cpu"))
+    B, NH, NK, S, D = 2, 4, 2, 64, 128
+    v = SimpleNamespace(name="v")
+    f16 = lambda *shape: torch.zeros(*shape, dtype=torch.float16)  # noqa: E731
+    b = {"q": f16(B, NH, 1, D), "new_k": f16(B, NK, 1, D), "new_v": f16(B, 1, NK, D), "k_cache": f16(B, S, NK, D),
+         "v_cache": f16(B, S, NK, D), "output": f16(B, NH, 1, D)}
+    s = {"B": B, "NH": NH, "NK": NK, "S": S, "D": D, "T": 1}
+    optable.OPS["SdpaDecodeCacheWriteF32Program"](None, v, b, s, {"cache_position": DynamicPush(slots, "cache_position", 9)})
+    optable.OPS["RopeTableF32Program"](None, v, {"cos": f16(1, 1, D), "sin": f16(1, 1, D)}, {},
+                                       {"theta": DynamicPush(slots, "theta", 1e6),
+                                        "start_position": DynamicPush(slots, "start_position", 9)})
+    optable.OPS["Qwen3TokenStoreEosProgram"](None, v, {"next_token": torch.zeros(1, 1, dtype=torch.int64),
+                                                      "done": torch.zeros(1, dtype=torch.int32),
+                                                      "generated_tokens": torch.zeros(1, 8, dtype=torch.int64),
+                                                      "generated_length": torch.zeros(1, dtype=torch.int32),
+                                                      "stopped": torch.zeros(1, dtype=torch.int32)}, {},
+                                             {"token_index": DynamicPush(slots, "token_index", 3)})
+    names = [c[0] for c in calls]
+    assert names == ["kv_cache_write", "kv_cache_write", "attn_decode", "rope_table", "token_store"]
+    push = {"cache_position": 70, "start_position": 70, "theta": 1e6, "token_index": 5}
+    slots.names = frozenset(push)
+    slots.buffer.copy_(torch.from_numpy(np.pad(slots.host_image(push), (0, slots.buffer.numel() - max(slots.used, 16)))))
+    assert calls[0][2]["positions"].tolist() == [70] and calls[0][2]["position"] == 0
+    assert calls[2][1][3].tolist() == [S - 1] * B and calls[2][2]["splits"] == optable._decode_splits(S)
+    assert calls[3][2]["start_position_dev"].tolist() == [70]
+    assert calls[4][2]["token_index_dev"].tolist() == [5]
+    assert not slots.admits(push)  # the cache write's guard: 0 <= cache_position < S
+    assert slots.admits({**push, "cache_position": 63}) and not slots.admits({**push, "theta": 1e4})
