@@ -639,7 +639,7 @@ def main() -> None:
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
-        "dtype": "q4_k weights x int8 activation planes (tensor-core mma), int32 / f32 accumulate",
+        "dtype": "fp16 activations x Q4_K / Q6_K codes as exact fp16 (mma.sync f16, f32 accumulate)",
         "data": "synthetic (seeded random weights, random prompt ids)",
         "config": {"workload": "Qwen3-8B decode, batch 1, 1024-token prompt, Q4_K linears + Q6_K head",
                    "model": "qwen3-8b-arch", "global_batch": 1, "seq_len": PROMPT,

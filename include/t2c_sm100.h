@@ -163,6 +163,8 @@ int t2c_qk_norm_rope_cache(const void *q_in, const void *k_in, const void *v_in,
  * positions in `splits` parts (max_len / splits positions each); the partial
  * (max, sum, acc) go to `workspace` (fp32, B * NH * splits * (D + 2) floats,
  * caller-provided; unused when splits == 1) and a combine pass writes out.
+ * A position outside [0, max_len) sets T2C_EINVAL in the device status word
+ * (t2c_device_status) and its rows attend to nothing (zero output).
  * Replaces ExportSdpaDecodeCacheF16Program / SdpaDecodeCacheWriteF32Program
  *   src/models/quantized_qwen3/shaders/sdpa_decode_cache_f16.py:22-136
  *   src/models/optimized_qwen3/shaders/sdpa_decode_cache_write_f32.py:22-171
@@ -216,7 +218,10 @@ int64_t t2c_attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64
  *     The array exists on every GPU that loads the library, until exit.
  *   - The first call on a device resolves the array's device address on the
  *     current device (cudaGetSymbolAddress); make that first call before any
- *     stream capture.
+ *     stream capture.  The address is kept for the device's primary context:
+ *     do not call again on a device after cudaDeviceReset.
+ *   - Shape checks come first (T2C_EINVAL / T2C_EUNSUPPORTED for splits > 64
+ *     or head_dim other than 64 / 128), then the scratch limit.
  *   - All calls share the one array, which keeps the last call's contents;
  *     every split record is fully rewritten before it is read, so nothing
  *     needs clearing, but calls that overlap on the GPU (other streams or

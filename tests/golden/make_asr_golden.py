@@ -21,6 +21,7 @@ the script checks that oracle/asr_ref.py reproduces the HF output.
 from __future__ import annotations
 
 import importlib.util
+import os
 import sys
 import types
 from pathlib import Path
@@ -59,7 +60,7 @@ def load_hf(reference_root: Path):
 
 
 def main() -> None:
-    reference_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    reference_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(os.environ["T2C_REFERENCE_ROOT"])
     conf_mod, model_mod = load_hf(reference_root)
     c = TINY
     hf_cfg = conf_mod.Qwen3ASRAudioEncoderConfig(

@@ -354,6 +354,34 @@ def test_attn_decode_fused_long_context(S, pos, splits):
     assert kernels.device_status() == 0
 
 
+@pytest.mark.parametrize("static", [False, True])
+def test_attn_decode_position_outside_cache(static):
+    """A position >= max_len with an uneven split count (max_len not a multiple of splits): the kernel sets
+    T2C_EINVAL in the device status, that row attends to nothing, the other rows are unaffected."""
+    from torch2vk_b200 import _lib, kernels
+
+    torch.manual_seed(4)
+    B, NH, NK, D, S, splits = 3, 32, 8, 128, 700, 3
+    q = torch.randn(B, NH * D, device="cuda", dtype=torch.float16)
+    kc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    vc = torch.randn(B, S, NK, D, device="cuda", dtype=torch.float16)
+    positions = torch.tensor([100, S, S + 40], device="cuda", dtype=torch.int32)
+    kernels.device_status(clear=True)
+    if static:
+        out = torch.full_like(q, 7.0)
+        cb, cs, ch = kernels.cache_strides(kc, "token_major")
+        _lib.lib().call("t2c_attn_decode_static", _lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(out),
+                        _lib.ptr(positions), B, NH, NK, D, S, cb, cs, ch, splits, _lib.stream_ptr())
+    else:
+        out = kernels.attn_decode(q, kc, vc, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
+                                  splits=splits, out=torch.full_like(q, 7.0))
+    torch.cuda.synchronize()
+    assert kernels.device_status(clear=True) & (1 << 1)
+    o = out.view(B, NH, D)
+    _close(o[:1], _attn_ref(q.view(B, NH, D)[:1], kc[:1], vc[:1], [101], NH, NK))
+    assert torch.count_nonzero(o[1:]).item() == 0
+
+
 def test_attn_decode_fused_rejects_bad_arguments():
     from torch2vk_b200 import kernels
     from torch2vk_b200._lib import T2CError

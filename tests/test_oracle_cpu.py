@@ -12,6 +12,7 @@
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -19,7 +20,8 @@ import numpy as np
 import pytest
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-REF_SRC = Path("/root/reference/src")
+# the reference checkout (read only); tests that need it skip when T2C_REFERENCE_ROOT is unset
+REF_SRC = Path(os.environ.get("T2C_REFERENCE_ROOT", "/nonexistent")) / "src"
 KINDS = ["q8_0", "q4_k", "q6_k"]
 
 

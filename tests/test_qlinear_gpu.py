@@ -3,10 +3,11 @@
 Tier 1 (bit-exact): GPU quantizer bytes == CPU oracle bytes; GPU decoder
 floats == oracle decoder floats.  Tier 2 (tolerance): the quantized linear
 against the oracle's direct block matvec (double accumulation over the same
-fp16 x and the same packed weights).  The tolerance is written below: the only
-approximation in the matvec kernels (M <= 4) is the 15-bit fixed-point x per 32
-values plus the fp16 store, so the bound is |err| <= 2e-3 * (|ref| + rms(ref));
-the tensor-core GEMM (Q4_K, M > 4) computes on fp16 operands and gets 4e-3.
+fp16 x and the same packed weights).  The tolerance is written below: the
+matvec kernels (M <= 4) take the fp16 x as it is (fp32 accumulation, fp16
+store), so |err| <= 2e-3 * (|ref| + rms(ref)) is loose for them (the tight
+per-output bound is in test_activation_outliers_gpu.py); the tensor-core GEMM
+(M > 4) computes on fp16-rounded weights and gets 4e-3.
 """
 
 from __future__ import annotations
@@ -173,29 +174,17 @@ def test_linear_multi_q4k_tensor_core_path(oracle, m):
         _tol_check(out.float().cpu().numpy(), ref)
 
 
-def test_q4k_dp4a_kernel_still_matches(tmp_path):
-    """The dp4a streamed kernel (forced with T2C_QMV_DP4A=1) on the shapes the tensor-core kernel now serves."""
-    import os
-    import subprocess
-    import sys
+@pytest.mark.parametrize("m,n,k", [(1, 1030, 768), (3, 96, 1280), (2, 200, 2304)])
+def test_q4k_exact_kernel_odd_superblock_counts(oracle, m, n, k):
+    """Q4_K with K / 256 odd (no 512-value segments): the exact fp16-x kernel, one pass per token."""
+    from torch2vk_b200 import kernels
 
-    script = tmp_path / "dp4a.py"
-    script.write_text(
-        "import numpy as np, torch\n"
-        "from oracle import oracle\n"
-        "from torch2vk_b200 import kernels\n"
-        "rng = np.random.default_rng(2)\n"
-        "for m, n, k in ((1, 1030, 2048), (4, 96, 3072)):\n"
-        "    p = oracle.quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32), 'q4_k')\n"
-        "    x = rng.standard_normal((m, k)).astype(np.float16)\n"
-        "    ref = oracle.matvec(p, 'q4_k', x)\n"
-        "    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(p).cuda(), 'q4_k', k).float().cpu().numpy()\n"
-        "    rms = np.sqrt(np.mean(ref ** 2))\n"
-        "    assert np.all(np.abs(y - ref) <= 2e-3 * (np.abs(ref) + rms)), float(np.abs(y - ref).max())\n"
-        "print('ok')\n")
-    env = dict(os.environ, T2C_QMV_DP4A="1", PYTHONPATH=str(Path(__file__).resolve().parents[1]))
-    r = subprocess.run([sys.executable, str(script)], env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+    rng = np.random.default_rng(m * 13 + n + k)
+    packed = oracle.quantize(_weights(rng, n, k), "q4_k")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    ref = oracle.matvec(packed, "q4_k", x)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q4_k", k)
+    _tol_check(y.float().cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("m,n,k", [(5, 128, 256), (16, 1030, 1024), (64, 384, 4096), (300, 200, 2048),

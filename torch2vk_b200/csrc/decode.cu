@@ -180,7 +180,7 @@ template <int E, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     __half *__restrict__ out, const int32_t *__restrict__ positions, int NH, int NK, int64_t cb, int64_t cs,
-    int64_t ch, int chunk, int splits, float *__restrict__ ws, float scale) {
+    int64_t ch, int max_len, int chunk, int splits, float *__restrict__ ws, float scale) {
     constexpr int D = E * 32;
     __shared__ float qs[G][D];
     __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
@@ -191,7 +191,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
-    const int len = positions[b] + 1;
+    // A position outside the cache has no rows to attend to: report it and
+    // attend to nothing (every split still writes its record, so the combine
+    // never reads stale workspace).
+    const int pos_b = positions[b];
+    const bool bad_pos = pos_b < 0 || pos_b >= max_len;
+    if (bad_pos && sp == 0 && kh == 0 && threadIdx.x == 0) report_device_error(T2C_EINVAL);
+    const int len = bad_pos ? 0 : pos_b + 1;
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
         const int g = i / D, d = i - g * D;
         qs[g][d] = __half2float(q[(static_cast<int64_t>(b) * NH + kh * G + g) * D + d]) * scale;
@@ -1580,7 +1586,7 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
                                int64_t cb, int64_t cs, int64_t ch, int64_t splits, float *workspace,
                                int64_t workspace_floats, void *stream) {
     if (!q || !k_cache || !v_cache || !out || !positions) return set_error(T2C_EINVAL, "attn_decode: NULL pointer");
-    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || max_len <= 0 || splits <= 0)
+    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || max_len <= 0 || max_len > INT32_MAX || splits <= 0)
         return set_error(T2C_EINVAL, "attn_decode: bad shape");
     const int G = static_cast<int>(NH / NK);
     if (G > kMaxGroup) return set_error(T2C_EUNSUPPORTED, "attn_decode: group %d > %d", G, kMaxGroup);
@@ -1600,7 +1606,8 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
 #define T2C_ATT(E, GG)                                                                                           \
     rc = launch(attn_decode_kernel<E, GG>, grid, block, 0, s, static_cast<const __half *>(q),                      \
                 static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache), static_cast<__half *>(out), \
-                positions, static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, chunk, static_cast<int>(splits),  \
+                positions, static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, static_cast<int>(max_len), chunk, \
+                static_cast<int>(splits),                                                                        \
                 workspace, scale)
     if (D == 128) {
         switch (G) {
@@ -1856,6 +1863,10 @@ extern "C" int t2c_advance_positions(int32_t *positions, int64_t B, int32_t *tok
 static constexpr int64_t kStaticAttnScratchFloats = 4 * 1024 * 1024;  // 16 MiB
 static __device__ __align__(256) float g_static_attn_scratch[kStaticAttnScratchFloats];
 
+// Device address of the array per device ordinal, resolved once.  It belongs
+// to the device's primary context (the one the runtime API uses); after that
+// context is destroyed (cudaDeviceReset) a process must not call
+// t2c_attn_decode_static on that device again.
 namespace {
 std::mutex g_static_scratch_mutex;
 float *g_static_scratch_ptr[64] = {nullptr};
@@ -1865,6 +1876,16 @@ extern "C" int t2c_attn_decode_static(const void *q, const void *k_cache, const 
                                       const int32_t *positions, int64_t B, int64_t NH, int64_t NK, int64_t D,
                                       int64_t max_len, int64_t cb, int64_t cs, int64_t ch, int64_t splits,
                                       void *stream) {
+    // Shape checks first, so that an unsupported split count is reported as
+    // such and the scratch product below cannot overflow.
+    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || max_len <= 0 || splits <= 0)
+        return set_error(T2C_EINVAL, "attn_decode_static: bad shape");
+    if (D != 64 && D != 128) return set_error(T2C_EUNSUPPORTED, "attn_decode_static: head_dim %lld", (long long)D);
+    if (splits > kMaxSplits)
+        return set_error(T2C_EUNSUPPORTED, "attn_decode_static: splits %lld > %d", (long long)splits, kMaxSplits);
+    if (B > kStaticAttnScratchFloats || NH > kStaticAttnScratchFloats || B * NH > kStaticAttnScratchFloats)
+        return set_error(T2C_ESCRATCH, "attn_decode_static: B*NH = %lld*%lld exceeds the fixed scratch", (long long)B,
+                         (long long)NH);
     const int64_t need = splits > 1 ? B * NH * splits * (D + 2) : 0;
     if (need > kStaticAttnScratchFloats) {
         return set_error(T2C_ESCRATCH,

@@ -1,32 +1,31 @@
 // Quantized linear for decode-sized batches (M <= 8 per launch chunk):
 // y[m, n] = sum_k x[m, k] * deq(W)[n, k] over GGUF Q4_K / Q6_K / Q8_0 rows.
 //
-// B200 design (HBM-bound):
-//  * x prologue: each CTA turns its x rows into 15-bit fixed point per
-//    32-value sub-block (x ~= sx * (128 * xh + xl), xh int8, xl in [0,127])
-//    in shared memory, optionally applying RMSNorm on the way.
-//  * Streamed kernel (qmv_tma_kernel): persistent CTAs; a producer warp
-//    streams row blocks of the packed weight matrix HBM -> shared memory with
-//    1-D bulk async copies (cp.async.bulk, completion on mbarriers) through a
-//    ring of stages, while four consumer warps decode the staged blocks.  The
-//    copies need no registers, so the bytes in flight per SM are set by the
-//    ring depth, not by occupancy.
-//  * Decode: integer nibble / 6-bit / int8 codes meet the int8 x planes in
-//    dp4a (exact integer sub-block sums); the block scales d*sc and dmin*m
-//    are applied once per sub-block in fp32.  Each lane keeps four rows'
-//    partial sums so one x fragment serves four rows; partial sums are
-//    reduced with warp shuffles.
-//  * Epilogues: + residual (matvec_add), silu(gate) * up (SwiGLU pair), fp16
-//    store.
-//  * Direct kernel (qmv_direct_kernel): the same decode reading weights
-//    straight from global memory; used when a layout cannot be bulk-copied
-//    (16-byte alignment).
-// Semantics follow the reference matvec shaders
+// Arithmetic (M <= 4) follows the reference matvec shaders
 // (src/models/quantized_qwen3/shaders/linear_nobias_q4_k_matvec_f32.py:107-197,
 //  linear_nobias_q6_k_matvec_f32.py:116-193, linear_nobias_q8_0_matvec_f32.py:84-119):
-// fp32 accumulation of x * (d*sc*q - dmin*m); only the rounding of x to
-// 15 bits per 32-value sub-block differs (relative error <= 2^-15 of the
-// sub-block maximum).
+// the fp16 x (with a fused RMSNorm: the normalized values rounded to fp16
+// once, as the reference's fp16 activation tensor) times the decoded weight,
+// accumulated in fp32.  The products run on fp16 tensor cores (mma.sync
+// m16n8k16, fp32 accumulators) with every weight code entering as an exactly
+// representable fp16 value (Q4_K nibbles as subnormals q * 2^-24, Q6_K levels
+// L - 32 and Q8_0 codes as small integers) and the block scales applied in
+// fp32; only the summation order differs from the reference's fp32 loop.
+//
+// B200 design (HBM-bound):
+//  * qmv_m1_kernel (Q4_K, M = 1): per-warp rings of 16-row x 288-byte 2-D TMA
+//    boxes (bounded mbarrier waits, weights requested before
+//    griddepcontrol.wait), K split over the warps of a CTA, mma columns = the
+//    sub-blocks of a block so each lane scales its own partial sums.
+//  * qmv_mma_kernel (Q4_K, M = 2..4): the same streaming, mma columns =
+//    tokens, sub-block scales folded into the fp16 A operand exactly.
+//  * qmv_x16_kernel (any type, one token per pass): direct global loads,
+//    16-row tiles, the sparse-column mapping of the M = 1 kernel.
+//  * qmv_tma_kernel / qmv_direct_kernel: dp4a on 15-bit fixed-point x planes;
+//    kept only for M > 4 shapes the tensor-core GEMM does not take (Q6_K with
+//    K % 2048 != 0, Q8_0 with K % 256 != 0).
+//  * Epilogues: + residual (matvec_add), silu(gate) * up (SwiGLU pair),
+//    per-4-row argmax partials (LM head), fp16 store.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
@@ -295,6 +294,113 @@ __device__ void prepare_x(const QParams &p, int8_t *xh, int8_t *xl, float *sx, i
         const float x0 = s0 * static_cast<float>(xq16[4 * u] + xq16[4 * u + 1]);
         const float x1 = s1 * static_cast<float>(xq16[4 * u + 2] + xq16[4 * u + 3]);
         meta[u] = make_float4(s0, s1, x0, x1);
+    }
+    sync_threads_nt<MT, NT>();
+}
+
+__device__ __forceinline__ uint32_t pack_half2_bits(__half lo, __half hi) {
+    return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+
+// fp16 x of the 2..4-token tensor-core kernel.  Per batch row, the K values
+// rounded to fp16 once (as the reference's fp16 activations) in
+// pair-interleaved 4-value chunks (x0, x2, x1, x3), with 16 bytes of padding
+// after every 16 chunks (the B fragments of the four lanes of a quad then
+// fall in distinct banks): row stride xf_row_bytes(K).  Then per row and
+// super-block the 8 sub-block sums as fp16 pairs (hi[8], lo[8]) with
+// hi = fp16(sum), lo = fp16(sum - hi), the B operand of the min-term mma.
+__host__ __device__ __forceinline__ int xf_row_bytes(int K) { return 2 * K + (K >> 6) * 16; }
+__host__ __device__ __forceinline__ int xf_chunk_off(int c) { return 8 * c + 16 * (c >> 4); }
+
+template <int MT, int NT>
+__device__ void prepare_x_f16(const QParams &p, uint8_t *xperm, uint8_t *xsum, float *red) {
+    const int K = p.K;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    constexpr int kW = NT / 32;
+    const int chunks_per_row = K >> 3;
+    const int total = MT * chunks_per_row;
+    const uint4 *xv = reinterpret_cast<const uint4 *>(p.x);
+    const int rb = xf_row_bytes(K), sb_per_row = K >> 8;
+    float inv_rms[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) inv_rms[m] = 1.0f;
+    if (p.norm_w != nullptr) {
+        float ss[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) ss[m] = 0.0f;
+        for (int c = tid; c < total; c += NT) {
+            const int m = c / chunks_per_row;
+            if (m >= p.M) continue;
+            float f[8];
+            unpack8(xv[c], f);
+            float part = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part = fmaf(f[e], f[e], part);
+#pragma unroll
+            for (int mm = 0; mm < MT; ++mm)
+                if (mm == m) ss[mm] += part;
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) red[warp * MT + m] = t;
+        }
+        sync_threads_nt<MT, NT>();
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float t = 0.0f;
+            for (int w = 0; w < kW; ++w) t += red[w * MT + m];
+            inv_rms[m] = rsqrtf(t / static_cast<float>(K) + p.eps);
+        }
+    }
+    // NT and chunks_per_row are multiples of 4, so lanes 4i .. 4i + 3 always
+    // hold the four 8-value chunks of one 32-value sub-block
+    for (int base = 0; base < total; base += NT) {
+        const int c = base + tid;
+        const int m = c / chunks_per_row;
+        const int k = (c - m * chunks_per_row) * 8;
+        float f[8];
+        if (c < total && m < p.M) {
+            unpack8(xv[c], f);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = 0.0f;
+        }
+        if (p.norm_w != nullptr && c < total) {
+            float r = 1.0f;
+#pragma unroll
+            for (int mm = 0; mm < MT; ++mm)
+                if (mm == m) r = inv_rms[mm];
+            const float4 w0 = *reinterpret_cast<const float4 *>(p.norm_w + k);
+            const float4 w1 = *reinterpret_cast<const float4 *>(p.norm_w + k + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = f[e] * r * wv[e];
+        }
+        __half h[8];
+        float sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            h[e] = __float2half_rn(f[e]);
+            sum += __half2float(h[e]);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (c < total) {
+            const int cc = k >> 2;  // first 4-value chunk
+            *reinterpret_cast<uint4 *>(xperm + m * rb + xf_chunk_off(cc)) =
+                make_uint4(pack_half2_bits(h[0], h[2]), pack_half2_bits(h[1], h[3]), pack_half2_bits(h[4], h[6]),
+                           pack_half2_bits(h[5], h[7]));
+            if ((lane & 3) == 0) {
+                const int j = k >> 5;  // sub-block of the row
+                const __half hi = __float2half_rn(sum);
+                const __half lo = __float2half_rn(sum - __half2float(hi));
+                uint8_t *dst = xsum + (m * sb_per_row + (j >> 3)) * 32 + 2 * (j & 7);
+                st_u16(dst, __half_as_ushort(hi));
+                st_u16(dst + 16, __half_as_ushort(lo));
+            }
+        }
     }
     sync_threads_nt<MT, NT>();
 }
@@ -1103,23 +1209,50 @@ constexpr int kMmaSegBlocks = 2;
 constexpr int kMmaSegBytes = kMmaSegBlocks * 144;
 constexpr int kMmaRows = 16;
 
-__device__ __forceinline__ void mma_s8_16832(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+
+
+
+__device__ __forceinline__ void mma_f16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
+// fp16 x of the 2..4-token kernel (prepare_x_f16): shared addresses.
+struct XF {
+    uint32_t perm, sum;
+    int row_bytes, sum_row;  // xf_row_bytes(K), (K / 256) * 32
+};
+
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
-// Scales of sub-blocks 2t, 2t+1 of one Q4_K block header (d*sc, dmin*m).
-__device__ __forceinline__ void q4k_pair_scales(const uint4 h, int t, float &ds0, float &ds1, float &dm0, float &dm1) {
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+// Small non-negative integer v (< 2048) times 2^-e as fp16 bits, duplicated in both halves.
+__device__ __forceinline__ uint32_t half2_dup(float v) {
+    const uint32_t b = __half_as_ushort(__float2half_rn(v));
+    return b | (b << 16);
+}
+
+// One 144-byte super-block of a 16-row group for up to 4 batch rows:
+// acc[0] row g, acc[1] row g+8, batch row t (mma m16n8k16, f16 inputs, fp32
+// accumulators).  Lane (g, t) reads group t of rows g, g + 8 (low nibbles:
+// sub-block 2t, high nibbles: sub-block 2t + 1).  Each nibble becomes an fp16
+// subnormal by masking (q * 2^-24 or 16 q * 2^-24) and is multiplied by its
+// sub-block scale code (sc, or sc / 16 for the high nibbles) in one f16x2
+// multiply: sc * q * 2^-24 exactly (sc * q < 1024), so one accumulator holds
+// the whole super-block.  B column n carries batch row n / 2 (clamped to
+// M - 1): D column 2t of lane (g, t) is batch row t.  The min term
+// sum_j m_j * xsum_j comes from one more mma (A = m codes, B = the hi / lo
+// fp16 parts of the sub-block sums).  The k order inside an mma follows the
+// pair-interleaved x chunks: word j, byte parity p of group t fill k-slots
+// {2t, 2t + 1} with bytes 4j + p, 4j + p + 2 (low nibbles) and
+// {2t + 8, 2t + 9} with their high nibbles.
+__device__ __forceinline__ void q4k_codes(const uint4 h, int t, uint32_t &sc0, uint32_t &sc1, uint32_t &m0,
+                                          uint32_t &m1) {
     const int i0 = (2 * t) & 3;
     const bool low = t < 2;
     const uint32_t y = h.y >> (8 * i0), z = h.z >> (8 * i0), w = h.w >> (8 * i0);
@@ -1127,57 +1260,69 @@ __device__ __forceinline__ void q4k_pair_scales(const uint4 h, int t, float &ds0
     const uint32_t hm = ((z >> 6) & 0x3u) | (((z >> 14) & 0x3u) << 8);
     const uint32_t scp = low ? (y & 0x3F3Fu) : ((w & 0x0F0Fu) | (hs << 4));
     const uint32_t mnp = low ? (z & 0x3F3Fu) : (((w >> 4) & 0x0F0Fu) | (hm << 4));
-    ds0 = d * small_u2f(scp & 0xffu);
-    ds1 = d * small_u2f(scp >> 8);
-    dm0 = dmin * small_u2f(mnp & 0xffu);
-    dm1 = dmin * small_u2f(mnp >> 8);
+    sc0 = scp & 0xffu;
+    sc1 = scp >> 8;
+    m0 = mnp & 0xffu;
+    m1 = mnp >> 8;
 }
 
-// One 144-byte super-block of a 16-row group: acc[0] row g, acc[1] row g+8 (batch row t).
-// rowg: shared address of the block in row g; xk: x offset (values) of the block.
-__device__ __forceinline__ void mma_q4k_block(uint32_t rowg, uint32_t row_stride, int kabs, const XS &x, int lane,
+__device__ __forceinline__ void mma_q4k_block(uint32_t rowg, uint32_t row_stride, int kabs, const XF &x, int lane,
                                               int M, float acc[2]) {
     const int g = lane >> 2, t = lane & 3;
     const uint32_t rowg8 = rowg + 8u * row_stride;
     const uint4 hg = lds128(rowg), hg8 = lds128(rowg8);
-    float ds[2][2], dm[2][2];
-    q4k_pair_scales(hg, t, ds[0][0], ds[0][1], dm[0][0], dm[0][1]);
-    q4k_pair_scales(hg8, t, ds[1][0], ds[1][1], dm[1][0], dm[1][1]);
-    // B column g: batch row g/2, plane g%2 (zero for absent batch rows)
-    const bool bcol = (g >> 1) < M;
-    const uint32_t xplane = (g & 1) ? x.xl : x.xh;
-    const int bm = bcol ? (g >> 1) : 0;
-    const bool dcol = t < M;
-    const int dmrow = dcol ? t : 0;
+    uint32_t scl[2], sch[2], mm[2];
+    float d[2], dmin[2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint2 wg = lds64(rowg + 16 + 32 * q + 8 * t);
-        const uint2 wg8 = lds64(rowg8 + 16 + 32 * q + 8 * t);
-        const int k0 = kabs + 64 * q + 8 * t;
-        const uint2 b_lo = bcol ? lds64(xplane + x.off(bm, k0)) : make_uint2(0u, 0u);
-        const uint2 b_hi = bcol ? lds64(xplane + x.off(bm, k0 + 32)) : make_uint2(0u, 0u);
-        const uint4 mt = lds128(x.meta + 16u * static_cast<uint32_t>(dmrow * x.u64 + ((kabs >> 6) + q)));
-        const uint32_t a_lo[4] = {wg.x & 0x0F0F0F0Fu, wg8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu, wg8.y & 0x0F0F0F0Fu};
-        const uint32_t a_hi[4] = {(wg.x >> 4) & 0x0F0F0F0Fu, (wg8.x >> 4) & 0x0F0F0F0Fu, (wg.y >> 4) & 0x0F0F0F0Fu,
-                                  (wg8.y >> 4) & 0x0F0F0F0Fu};
-        int d_lo[4], d_hi[4];
-        mma_s8_16832(d_lo, a_lo, b_lo.x, b_lo.y);
-        mma_s8_16832(d_hi, a_hi, b_hi.x, b_hi.y);
-        // scales of sub-blocks 2q, 2q+1 live in lane (g, q)
-        const int src = (lane & ~3) | q;
-        const float s0g = __shfl_sync(0xffffffffu, ds[0][0], src), s1g = __shfl_sync(0xffffffffu, ds[0][1], src);
-        const float m0g = __shfl_sync(0xffffffffu, dm[0][0], src), m1g = __shfl_sync(0xffffffffu, dm[0][1], src);
-        const float s0h = __shfl_sync(0xffffffffu, ds[1][0], src), s1h = __shfl_sync(0xffffffffu, ds[1][1], src);
-        const float m0h = __shfl_sync(0xffffffffu, dm[1][0], src), m1h = __shfl_sync(0xffffffffu, dm[1][1], src);
-        const float sx0 = dcol ? __uint_as_float(mt.x) : 0.0f, sx1 = dcol ? __uint_as_float(mt.y) : 0.0f;
-        const float xs0 = dcol ? __uint_as_float(mt.z) : 0.0f, xs1 = dcol ? __uint_as_float(mt.w) : 0.0f;
-        acc[0] = fmaf(s0g * sx0, static_cast<float>(d_lo[0] * 128 + d_lo[1]), acc[0]);
-        acc[1] = fmaf(s0h * sx0, static_cast<float>(d_lo[2] * 128 + d_lo[3]), acc[1]);
-        acc[0] = fmaf(s1g * sx1, static_cast<float>(d_hi[0] * 128 + d_hi[1]), acc[0]);
-        acc[1] = fmaf(s1h * sx1, static_cast<float>(d_hi[2] * 128 + d_hi[3]), acc[1]);
-        acc[0] = fmaf(-m0g, xs0, fmaf(-m1g, xs1, acc[0]));
-        acc[1] = fmaf(-m0h, xs0, fmaf(-m1h, xs1, acc[1]));
+    for (int r = 0; r < 2; ++r) {
+        const uint4 h = r ? hg8 : hg;
+        uint32_t c0, c1, n0, n1;
+        q4k_codes(h, t, c0, c1, n0, n1);
+        scl[r] = half2_dup(static_cast<float>(c0));
+        sch[r] = half2_dup(static_cast<float>(c1) * 0.0625f);
+        mm[r] = pack_half2_bits(__float2half_rn(static_cast<float>(n0)), __float2half_rn(static_cast<float>(n1)));
+        d[r] = half_bits_to_float(h.x) * 16777216.0f;
+        dmin[r] = half_bits_to_float(h.x >> 16);
     }
+    const uint4 w0 = lds128(rowg + 16 + 32 * t), w1 = lds128(rowg + 32 + 32 * t);
+    const uint4 v0 = lds128(rowg8 + 16 + 32 * t), v1 = lds128(rowg8 + 32 + 32 * t);
+    const int bm = min(g >> 1, M - 1);
+    const int sb = kabs >> 8;
+    const uint32_t xb = x.perm + static_cast<uint32_t>(bm * x.row_bytes + 576 * sb + 144 * t);
+    uint32_t bl[16], bh[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 a = lds128(xb + 16 * i), b = lds128(xb + 64 + 16 * i);
+        bl[4 * i] = a.x;
+        bl[4 * i + 1] = a.y;
+        bl[4 * i + 2] = a.z;
+        bl[4 * i + 3] = a.w;
+        bh[4 * i] = b.x;
+        bh[4 * i + 1] = b.y;
+        bh[4 * i + 2] = b.z;
+        bh[4 * i + 3] = b.w;
+    }
+    const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const uint32_t V[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float D[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint32_t w = W[j], v = V[j];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const uint32_t a[4] = {hmul2_bits(w & 0x000F000Fu, scl[0]), hmul2_bits(v & 0x000F000Fu, scl[1]),
+                                   hmul2_bits(w & 0x00F000F0u, sch[0]), hmul2_bits(v & 0x00F000F0u, sch[1])};
+            mma_f16_16816(D, a, bl[2 * j + p], bh[2 * j + p]);
+            w >>= 8;
+            v >>= 8;
+        }
+    }
+    const uint32_t xs = x.sum + static_cast<uint32_t>(bm * x.sum_row + 32 * sb + 4 * t);
+    const uint32_t am[4] = {mm[0], mm[1], mm[0], mm[1]};
+    float E[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    mma_f16_16816(E, am, lds32(xs), lds32(xs + 16));
+    acc[0] += fmaf(d[0], D[0], -dmin[0] * E[0]);
+    acc[1] += fmaf(d[1], D[2], -dmin[1] * E[2]);
 }
 
 // Item cursor of one warp: CTA iteration `it`, j-th item of the warp in that
@@ -1309,12 +1454,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
     uint64_t *full = reinterpret_cast<uint64_t *>(smem) + warp * kMaxStages;
     uint8_t *stages = smem + kStageHead + static_cast<size_t>(warp) * S * p.stage_bytes;
     MmaSlot *slots = reinterpret_cast<MmaSlot *>(smem + kStageHead + static_cast<size_t>(kMmaWarps) * S * p.stage_bytes);
-    float4 *meta = reinterpret_cast<float4 *>(slots + kMmaSlots * kMmaWarps);
-    int8_t *xh = reinterpret_cast<int8_t *>(meta + MT * (K >> 6));
-    int8_t *xl = xh + MT * padded_k(K) + 32;  // +32: xh / xl fragments of one k on different banks
-    float *sx = reinterpret_cast<float *>(xl + MT * padded_k(K));
-    int *xq16 = reinterpret_cast<int *>(sx + MT * (K >> 5));
-    float *pred = reinterpret_cast<float *>(xq16 + MT * (K >> 4));
+    uint8_t *xperm = reinterpret_cast<uint8_t *>(slots + kMmaSlots * kMmaWarps);
+    uint8_t *xsum = xperm + MT * xf_row_bytes(K);
+    float *pred = reinterpret_cast<float *>(xsum + MT * (K >> 8) * 32);
     const int64_t iters = (p.total_rowsets + static_cast<int64_t>(gridDim.x) * p.bpc - 1) /
                           (static_cast<int64_t>(gridDim.x) * p.bpc);
     const int group = warp / p.wpb;
@@ -1333,9 +1475,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
         reinterpret_cast<int *>(slots)[i] = 0;
     pdl_wait();
     pdl_trigger();
-    prepare_x<MT, kMmaThreads>(p, xh, xl, sx, xq16, meta, pred);  // ends with a CTA barrier
-    const XS x{smem_u32(xh), smem_u32(xl), smem_u32(meta), smem_u32(sx), smem_u32(xq16), padded_k(K), K >> 6,
-               K >> 5};
+    prepare_x_f16<MT, kMmaThreads>(p, xperm, xsum, pred);  // ends with a CTA barrier
+    const XF x{smem_u32(xperm), smem_u32(xsum), xf_row_bytes(K), (K >> 8) * 32};
     ahead = MmaCursor{0, 0};
     for (int i = 0; i < S && mma_valid(p, ahead, warp, iters); ++i) mma_advance(p, ahead, warp);
 
@@ -1433,14 +1574,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
 }
 
 // ------------------------------------------------ M = 1 kernel, per-warp x
-// Same streaming and split-K as qmv_mma_kernel, but each warp quantizes only
+// Same streaming and split-K as qmv_mma_kernel, but each warp prepares only
 // the x values of its own K-segments (after, when there is a fused RMSNorm,
 // a warp-local sum of squares over the whole row), so the prologue has no
-// CTA barrier and x costs ~1.2 KB of shared memory per segment: two CTAs fit
-// on an SM.  Per segment: xh[512], 32-byte gap, xl[512], then (sx', xs) per
-// 32-value sub-block, where sx' = sx / 16 for the odd (high-nibble) sub-blocks.
-constexpr int kM1SegX = 512 + 32 + 512 + 32;      // plane bytes (+ gaps)
-constexpr int kM1SegBytes = kM1SegX + 16 * 8;    // + meta
+// CTA barrier and x costs ~1.1 KB of shared memory per segment: two CTAs fit
+// on an SM.  x keeps the reference's arithmetic: the (normalized) values are
+// rounded to fp16 once, like the reference's fp16 activation tensor, and enter
+// the fp16 tensor-core products unchanged.  Per 512-value segment:
+//   [0, 1024)     fp16 x in pair-interleaved 4-value chunks (x0, x2, x1, x3),
+//                 so that every 32-bit word is one mma B pair (k, k + 2);
+//   [1024, 1088)  fp32 sums of the segment's 16 sub-blocks (32 values each);
+//   [1088, 1152)  zeros: the B source of lanes whose mma column is unused.
+constexpr int kM1SegSum = 1024;
+constexpr int kM1SegZero = 1088;
+constexpr int kM1SegBytes = 1152;
 constexpr int kM1MaxSegs = 16;                   // per warp (K <= 65536)
 constexpr int kM1XReg = 4;                       // segments whose x loads are issued together
 
@@ -1462,33 +1609,27 @@ __device__ __forceinline__ void m1_load_norm(const QParams &p, int k0, int lane,
     }
 }
 
-// Quantizes one segment of x (f, already scaled by the RMSNorm when there is
-// one) into a segment area.
+// Rounds one segment of x (f, already scaled by the RMSNorm when there is
+// one) to fp16 and writes it, its sub-block sums and the zero area.
 __device__ __forceinline__ void m1_prepare_segment(const float f[16], uint8_t *area, int lane) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(f[e]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));  // lanes 2i, 2i+1 = sub-block i
-    const float inv = amax > 0.0f ? 16383.0f / amax : 0.0f;
-    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
-    int sum = 0;
+    __half h[16];
+    float sum = 0.0f;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-        int q = __float2int_rn(f[e] * inv);
-        q = max(-16383, min(16383, q));
-        sum += q;
-        hw[e >> 2] |= (static_cast<uint32_t>(q >> 7) & 0xffu) << (8 * (e & 3));
-        lw[e >> 2] |= static_cast<uint32_t>(q & 127) << (8 * (e & 3));
+        h[e] = __float2half_rn(f[e]);
+        sum += __half2float(h[e]);
     }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    *reinterpret_cast<uint4 *>(area + 16 * lane) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4 *>(area + 512 + 32 + 16 * lane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    if ((lane & 1) == 0) {
-        const float sx = amax / 16383.0f;
-        // sub-block lane / 2: the odd ones are high nibbles, which enter the mma as 16 q
-        const float f_sx = (lane & 2) ? sx * 0.0625f : sx;
-        *reinterpret_cast<float2 *>(area + kM1SegX + 8 * (lane >> 1)) = make_float2(f_sx, sx * static_cast<float>(sum));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // lanes 2i, 2i+1 = sub-block i
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w[2 * i] = pack_half2_bits(h[4 * i], h[4 * i + 2]);
+        w[2 * i + 1] = pack_half2_bits(h[4 * i + 1], h[4 * i + 3]);
     }
+    *reinterpret_cast<uint4 *>(area + 32 * lane) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4 *>(area + 32 * lane + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+    if ((lane & 1) == 0) *reinterpret_cast<float *>(area + kM1SegSum + 4 * (lane >> 1)) = sum;
+    if (lane < 4) *reinterpret_cast<uint4 *>(area + kM1SegZero + 16 * lane) = make_uint4(0u, 0u, 0u, 0u);
 }
 
 // Residual values of rows g, g + 8 of row block `blk` (lane t == 0), read
@@ -1503,82 +1644,110 @@ __device__ __forceinline__ void m1_load_res(const QParams &p, int blk, int lane,
     if (row + 8 < st.n) rv[1] = __half2float(st.res[row + 8]);
 }
 
-// Fragment mapping of the M = 1 kernel (m16n8k32, A = 16 weight rows, B = x).
-// In a group G of two quarters (sub-blocks 4G .. 4G+3), lane (g, t) loads 16
-// bytes of rows g and g+8: quarter 2G + (t & 1), bytes 16 (t >> 1) .. +15.
-// mma i takes word i of each: its low nibbles fill k-slots 4t .. 4t+3 and its
-// high nibbles (unshifted, i.e. 16 q) k-slots 16+4t .. 16+4t+3.  So k-slots
-// {0-3, 8-11} hold the low-nibble sub-block of quarter 2G (sub-block 4G),
-// {4-7, 12-15} that of quarter 2G+1 (4G+2), {16-19, 24-27} sub-block 4G+1 and
-// {20-23, 28-31} sub-block 4G+3.  B column pair c carries the two x planes of
-// one of them (c = 0: 4G, 1: 4G+2, 2: 4G+1, 3: 4G+3), zero in the other
-// k-slots, so D columns 2t, 2t+1 of lane (g, t) are sub-block 4G + cc(t),
-// cc = {0, 2, 1, 3}[t]: every lane applies the scales of one sub-block per
-// group, and the four lanes of a quad are summed per row block at the end.
+// Fragment mapping of the M = 1 kernel (mma m16n8k16, f16 inputs, fp32
+// accumulators; A = 16 weight rows, B = x).  Lane (g, t) reads group t (bytes
+// 32 t .. 32 t + 31 of the 128 nibble bytes) of rows g and g + 8 of a Q4_K
+// block: the low nibbles are sub-block 2t, the high nibbles sub-block 2t + 1.
+// The nibbles enter the mma as fp16 subnormals by masking alone: q * 2^-24
+// (low) and 16 q * 2^-24 (high), exact.  mma (j, p) (word j, byte parity p)
+// gives lane t's k-slots {2t, 2t + 1} the low nibbles of bytes 4j + p and
+// 4j + p + 2, and k-slots {2t + 8, 2t + 9} their high nibbles.  B column 2t
+// carries the x values of the low slots of lane t, column 2t + 1 those of its
+// high slots, zero elsewhere, so D columns 2t, 2t + 1 of lane (g, t) are
+// exactly the sums q * x over sub-blocks 2t and 2t + 1 of rows g, g + 8: every
+// lane applies the scales of its own two sub-blocks, and the four lanes of a
+// quad are summed per row block at the end.
 struct M1Lane {
-    uint32_t aoff;   // A words in a 144-byte block
-    uint32_t xoff;   // x plane words of G = 0 in a segment area
-    uint32_t moff;   // (sx', xs) of sub-block cc of G = 0 in a segment area
-    uint32_t m0, m1; // B masks: k-slots < 16 / >= 16 carry this lane's x column
-    uint32_t sel;    // byte_perm selector of header byte cc
+    uint32_t aoff;           // group t's bytes in a 144-byte block
+    uint32_t b0off, b0step;  // B source of the low slots (segment-relative; step per super-block)
+    uint32_t b1off, b1step;  // B source of the high slots
+    uint32_t soff;           // sums of sub-blocks 2t, 2t + 1 of super-block 0
+    // scale decode of sub-blocks 2t, 2t + 1: header bytes (2t, 2t + 1) mod 4 by byte_perm `sel`, then
+    // codes = (W & mw) | ((Y >> sy) & my) (t < 2: the 6-bit bytes of Y; t >= 2: low / high nibbles of W
+    // with the top two bits of Y / Z)
+    uint32_t sel, mw, my, sy;
 };
 
 __device__ __forceinline__ M1Lane m1_lane(int lane) {
-    const int g = lane >> 2, t = lane & 3, c = g >> 1, plane = g & 1;
-    const int cc = ((t & 1) << 1) | (t >> 1);
-    const bool mine = (c & 1) == (t & 1);
+    const int g = lane >> 2, t = lane & 3, h = g - 2 * t;
     M1Lane L;
-    L.aoff = static_cast<uint32_t>(16 + 32 * (t & 1) + 16 * (t >> 1));
-    L.xoff = static_cast<uint32_t>((plane ? 512 + 32 : 0) + 32 * (2 * (t & 1) + (c >> 1)) + 16 * (t >> 1));
-    L.moff = static_cast<uint32_t>(kM1SegX + 8 * cc);
-    L.m0 = (mine && c < 2) ? 0xffffffffu : 0u;
-    L.m1 = (mine && c >= 2) ? 0xffffffffu : 0u;
-    L.sel = 0x4440u + static_cast<uint32_t>(cc);
+    L.aoff = static_cast<uint32_t>(16 + 32 * t);
+    L.b0off = h == 0 ? static_cast<uint32_t>(128 * t) : static_cast<uint32_t>(kM1SegZero);
+    L.b0step = h == 0 ? 512u : 0u;
+    L.b1off = h == 1 ? static_cast<uint32_t>(128 * t + 64) : static_cast<uint32_t>(kM1SegZero);
+    L.b1step = h == 1 ? 512u : 0u;
+    L.soff = static_cast<uint32_t>(kM1SegSum + 8 * t);
+    const uint32_t b = static_cast<uint32_t>((2 * t) & 3);
+    L.sel = 0x4400u | ((b + 1) << 4) | b;
+    L.mw = t < 2 ? 0u : 0x0F0Fu;
+    L.my = t < 2 ? 0x3F3Fu : 0x3030u;
+    L.sy = t < 2 ? 0u : 2u;
     return L;
 }
 
-__device__ __forceinline__ void mma_u8s8_16832(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// d * sc and dmin * m of sub-blocks cc and cc + 4 of one Q4_K header.
-__device__ __forceinline__ void q4k_scales_sel(const uint4 h, uint32_t sel, float ds[2], float dm[2]) {
+// d * sc * 2^24, d * sc * 2^20 (the high nibbles enter as 16 q) and dmin * m
+// of sub-blocks 2t, 2t + 1 of one Q4_K header.  Codes become floats through
+// the 2^23 mantissa trick folded into one exact fma: s * (2^23 + c) - s * 2^23.
+__device__ __forceinline__ void m1_scales(const uint4 h, const M1Lane &L, float ds[2], float dm[2]) {
+    const uint32_t Y = __byte_perm(h.y, 0u, L.sel), Z = __byte_perm(h.z, 0u, L.sel), W = __byte_perm(h.w, 0u, L.sel);
+    const uint32_t scp = (W & L.mw) | ((Y >> L.sy) & L.my);
+    const uint32_t mnp = ((W >> 4) & L.mw) | ((Z >> L.sy) & L.my);
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const uint32_t y = __byte_perm(h.y, 0u, sel), z = __byte_perm(h.z, 0u, sel), w = __byte_perm(h.w, 0u, sel);
-    ds[0] = d * small_u2f(y & 63u);
-    dm[0] = dmin * small_u2f(z & 63u);
-    ds[1] = d * small_u2f((w & 15u) | ((y >> 6) << 4));
-    dm[1] = dmin * small_u2f((w >> 4) | ((z >> 6) << 4));
+    const float d24 = d * 16777216.0f, d20 = d * 1048576.0f;
+    ds[0] = fmaf(d24, __uint_as_float(__byte_perm(scp, 0x4B000000u, 0x7540u)), -d24 * 8388608.0f);
+    ds[1] = fmaf(d20, __uint_as_float(__byte_perm(scp, 0x4B000000u, 0x7541u)), -d20 * 8388608.0f);
+    dm[0] = fmaf(dmin, __uint_as_float(__byte_perm(mnp, 0x4B000000u, 0x7540u)), -dmin * 8388608.0f);
+    dm[1] = fmaf(dmin, __uint_as_float(__byte_perm(mnp, 0x4B000000u, 0x7541u)), -dmin * 8388608.0f);
 }
 
-// One 144-byte block (values voff .. voff+255 of the segment) of a 16-row
-// group whose rows are kMmaSegBytes apart; acc = rows g, g + 8.
-__device__ __forceinline__ void m1_block(const uint8_t *rowg, const uint8_t *xseg, int voff, const M1Lane &L,
+// One 144-byte block (super-block sb of the segment) of a 16-row group whose
+// rows are kMmaSegBytes apart; acc = rows g, g + 8.
+__device__ __forceinline__ void m1_block(const uint8_t *rowg, const uint8_t *xseg, int sb, const M1Lane &L,
                                          float acc[2]) {
     const uint8_t *rowg8 = rowg + 8 * kMmaSegBytes;
     const uint4 hg = *reinterpret_cast<const uint4 *>(rowg), hg8 = *reinterpret_cast<const uint4 *>(rowg8);
-    float dsg[2], dmg[2], dsh[2], dmh[2];
-    q4k_scales_sel(hg, L.sel, dsg, dmg);
-    q4k_scales_sel(hg8, L.sel, dsh, dmh);
+    float ds[2][2], dm[2][2];
+    m1_scales(hg, L, ds[0], dm[0]);
+    m1_scales(hg8, L, ds[1], dm[1]);
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(rowg + L.aoff);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(rowg + L.aoff + 16);
+    const uint4 v0 = *reinterpret_cast<const uint4 *>(rowg8 + L.aoff);
+    const uint4 v1 = *reinterpret_cast<const uint4 *>(rowg8 + L.aoff + 16);
+    const uint8_t *b0p = xseg + L.b0off + sb * L.b0step;
+    const uint8_t *b1p = xseg + L.b1off + sb * L.b1step;
+    uint32_t bl[16], bh[16];
 #pragma unroll
-    for (int G = 0; G < 2; ++G) {
-        const uint4 X = *reinterpret_cast<const uint4 *>(xseg + L.xoff + voff + 128 * G);
-        const float2 mt = *reinterpret_cast<const float2 *>(xseg + L.moff + (voff >> 2) + 32 * G);
-        const uint4 qa = *reinterpret_cast<const uint4 *>(rowg + L.aoff + 64 * G);
-        const uint4 ra = *reinterpret_cast<const uint4 *>(rowg8 + L.aoff + 64 * G);
-        const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, va[4] = {ra.x, ra.y, ra.z, ra.w};
-        const uint32_t xw[4] = {X.x, X.y, X.z, X.w};
-        int d[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t a[4] = {wa[i] & 0x0F0F0F0Fu, va[i] & 0x0F0F0F0Fu, wa[i] & 0xF0F0F0F0u, va[i] & 0xF0F0F0F0u};
-            mma_u8s8_16832(d, a, xw[i] & L.m0, xw[i] & L.m1);
-        }
-        acc[0] = fmaf(dsg[G] * mt.x, static_cast<float>(d[0] * 128 + d[1]), fmaf(-dmg[G], mt.y, acc[0]));
-        acc[1] = fmaf(dsh[G] * mt.x, static_cast<float>(d[2] * 128 + d[3]), fmaf(-dmh[G], mt.y, acc[1]));
+    for (int i = 0; i < 4; ++i) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(b0p + 16 * i);
+        const uint4 b = *reinterpret_cast<const uint4 *>(b1p + 16 * i);
+        bl[4 * i] = a.x;
+        bl[4 * i + 1] = a.y;
+        bl[4 * i + 2] = a.z;
+        bl[4 * i + 3] = a.w;
+        bh[4 * i] = b.x;
+        bh[4 * i + 1] = b.y;
+        bh[4 * i + 2] = b.z;
+        bh[4 * i + 3] = b.w;
     }
+    const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const uint32_t V[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    // two accumulator chains (even / odd byte parity) halve the dependent mma latency
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        // byte shifts on the multiply pipe (high half of w * 2^24), the masks on the logic pipe
+        const uint32_t w = W[j], v = V[j], w8 = __umulhi(w, 1u << 24), v8 = __umulhi(v, 1u << 24);
+        const uint32_t a0[4] = {w & 0x000F000Fu, v & 0x000F000Fu, w & 0x00F000F0u, v & 0x00F000F0u};
+        const uint32_t a1[4] = {w8 & 0x000F000Fu, v8 & 0x000F000Fu, w8 & 0x00F000F0u, v8 & 0x00F000F0u};
+        mma_f16_16816(d, a0, bl[2 * j], bh[2 * j]);
+        mma_f16_16816(e, a1, bl[2 * j + 1], bh[2 * j + 1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] += e[i];
+    const float2 xs = *reinterpret_cast<const float2 *>(xseg + L.soff + 32 * sb);
+    // ds carries the 2^24 (low) and 2^20 (high) of the subnormal weights
+    acc[0] += fmaf(ds[0][0], d[0], fmaf(ds[0][1], d[1], -fmaf(dm[0][0], xs.x, dm[0][1] * xs.y)));
+    acc[1] += fmaf(ds[1][0], d[2], fmaf(ds[1][1], d[3], -fmaf(dm[1][0], xs.x, dm[1][1] * xs.y)));
 }
 
 // Split-K slot of the M = 1 kernel: each warp of a row block's group stores
@@ -1741,7 +1910,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 const uint8_t *xseg = xarea + (swiglu ? (j >> 1) : j) * kM1SegBytes;
                 float part[2] = {0.0f, 0.0f};
 #pragma unroll
-                for (int sb = 0; sb < kMmaSegBlocks; ++sb) m1_block(stage + sb * 144, xseg, sb * 256, L, part);
+                for (int sb = 0; sb < kMmaSegBlocks; ++sb) m1_block(stage + sb * 144, xseg, sb, L, part);
                 if (swiglu && (j & 1)) {
                     acc[1][0] += part[0];
                     acc[1][1] += part[1];
@@ -1814,6 +1983,419 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
             __threadfence_block();
             *reinterpret_cast<volatile int *>(&slot->gen) = slot->gen + 1;
         }
+    }
+}
+
+// ======================================================= exact fp16-x kernel
+// qmv_x16_kernel: one token per launch (M = 1; larger M runs one pass per
+// token), weight streams of any GGUF type (Q4_K, Q6_K, Q8_0, mixed in one
+// fused QKV), modes ROWS (+ residual), SWIGLU and ARGMAX.  x keeps the
+// reference's arithmetic: the (normalized) values are rounded to fp16 once
+// and enter fp16 tensor-core products unchanged; every weight code enters as
+// an exactly representable fp16 value and the block scales are applied in
+// fp32, so the only differences from the reference's fp32 loop are fp32
+// summation order and the fp16 store.
+//   * Tiles of 16 rows (mma m16n8k16 A); the 8 warps of a CTA take bpc tiles
+//     at a time with wpb warps per tile splitting K into 256-value units
+//     (partial sums meet in shared memory in warp order: deterministic).
+//   * Weights come straight from global memory (ld.global.nc), each lane
+//     loading the bytes of its own two rows; x (fp16, natural order) and the
+//     fp32 sums of its 32-value blocks are staged in shared memory.
+//   * Columns of the mma carry scale groups, not tokens: lane t's k-slots
+//     {2t, 2t + 1} belong to one group and {2t + 8, 2t + 9} to another, and
+//     B column 2t (2t + 1) holds x only in the first (second) pair of slots,
+//     so D columns 2t, 2t + 1 of lane (g, t) are group sums that lane t
+//     scales itself; the four lanes of a quad are added at the end.
+//       Q4_K: group t of each block (low nibbles: sub-block 2t, high: 2t + 1),
+//             nibbles as fp16 subnormals (q * 2^-24, 16 q * 2^-24) by masking;
+//             d * sc and dmin * m * xsum per sub-block in fp32.
+//       Q6_K: per (half s, 16-value half lh, quarter pair cp): quarters cp and
+//             cp + 2 at positions 16 lh + 4t .. + 3; the 6-bit levels L become
+//             fp16 1024 + L by byte permutes and L - 32 by one f16x2 subtract
+//             (exact); d * sc of the two 16-value groups in fp32.
+//       Q8_0: blocks 2t and 2t + 1 of each 8-block unit; q + 128 as fp16
+//             subnormals, d * (D - 128 * xsum) in fp32.
+constexpr int kXWarps = 8;
+constexpr int kXThreads = kXWarps * 32;
+
+__device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return ldg_nc_u32(p); }
+
+// 32-bit word at a 2-byte aligned address.
+__device__ __forceinline__ uint32_t ldg32_a2(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    if ((a & 3u) == 0) return ldg32(p);
+    return __funnelshift_r(ldg32(p - 2), ldg32(p + 2), 16);
+}
+
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ void mma_f16_16816_zc(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// x of one token: fp16 [K] in natural order, fp32 sums of 32-value blocks [K / 32].
+__device__ void x16_prepare(const QParams &p, uint8_t *xs, float *xsum, float *red) {
+    const int K = p.K;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunks = K >> 3;
+    const uint4 *xv = reinterpret_cast<const uint4 *>(p.x);
+    float inv_rms = 1.0f;
+    if (p.norm_w != nullptr) {
+        float ss = 0.0f;
+        for (int c = tid; c < chunks; c += kXThreads) {
+            float f[8];
+            unpack8(xv[c], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int w = 0; w < kXWarps; ++w) tot += red[w];
+        inv_rms = rsqrtf(tot / static_cast<float>(K) + p.eps);
+    }
+    // kXThreads and chunks are multiples of 4: lanes 4i .. 4i + 3 hold the chunks of one 32-value block
+    for (int base = 0; base < chunks; base += kXThreads) {
+        const int c = base + tid;
+        float f[8];
+        if (c < chunks) {
+            unpack8(xv[c], f);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = 0.0f;
+        }
+        if (p.norm_w != nullptr && c < chunks) {
+            const float4 w0 = *reinterpret_cast<const float4 *>(p.norm_w + 8 * c);
+            const float4 w1 = *reinterpret_cast<const float4 *>(p.norm_w + 8 * c + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = f[e] * inv_rms * wv[e];
+        }
+        __half h[8];
+        float sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            h[e] = __float2half_rn(f[e]);
+            sum += __half2float(h[e]);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (c < chunks) {
+            *reinterpret_cast<uint4 *>(xs + 16 * c) =
+                make_uint4(pack_half2_bits(h[0], h[1]), pack_half2_bits(h[2], h[3]), pack_half2_bits(h[4], h[5]),
+                           pack_half2_bits(h[6], h[7]));
+            if ((lane & 3) == 0) xsum[c >> 2] = sum;
+        }
+    }
+    __syncthreads();
+}
+
+// Per-lane constants of the sparse-column mapping.
+struct XLane {
+    int g, t;
+    uint32_t b0on, b1on;  // all-ones when this lane's B column takes the first / second slot pair
+    uint32_t sel, mw, my, sy;  // Q4_K scale decode of sub-blocks 2t, 2t + 1 (as M1Lane)
+};
+
+__device__ __forceinline__ XLane x_lane(int lane) {
+    XLane L;
+    L.g = lane >> 2;
+    L.t = lane & 3;
+    const int h = L.g - 2 * L.t;
+    L.b0on = h == 0 ? 0xffffffffu : 0u;
+    L.b1on = h == 1 ? 0xffffffffu : 0u;
+    const uint32_t b = static_cast<uint32_t>((2 * L.t) & 3);
+    L.sel = 0x4400u | ((b + 1) << 4) | b;
+    L.mw = L.t < 2 ? 0u : 0x0F0Fu;
+    L.my = L.t < 2 ? 0x3F3Fu : 0x3030u;
+    L.sy = L.t < 2 ? 0u : 2u;
+    return L;
+}
+
+// d * sc * 2^24, d * sc * 2^20 and dmin * m of sub-blocks 2t, 2t + 1 (see m1_scales).
+__device__ __forceinline__ void x_q4k_scales(const uint4 h, const XLane &L, float ds[2], float dm[2]) {
+    const uint32_t Y = __byte_perm(h.y, 0u, L.sel), Z = __byte_perm(h.z, 0u, L.sel), W = __byte_perm(h.w, 0u, L.sel);
+    const uint32_t scp = (W & L.mw) | ((Y >> L.sy) & L.my);
+    const uint32_t mnp = ((W >> 4) & L.mw) | ((Z >> L.sy) & L.my);
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const float d24 = d * 16777216.0f, d20 = d * 1048576.0f;
+    ds[0] = fmaf(d24, __uint_as_float(__byte_perm(scp, 0x4B000000u, 0x7540u)), -d24 * 8388608.0f);
+    ds[1] = fmaf(d20, __uint_as_float(__byte_perm(scp, 0x4B000000u, 0x7541u)), -d20 * 8388608.0f);
+    dm[0] = fmaf(dmin, __uint_as_float(__byte_perm(mnp, 0x4B000000u, 0x7540u)), -dmin * 8388608.0f);
+    dm[1] = fmaf(dmin, __uint_as_float(__byte_perm(mnp, 0x4B000000u, 0x7541u)), -dmin * 8388608.0f);
+}
+
+// Unit u (256 values) of two rows (ra, rb: row starts, nullptr when past N) for Q4_K.
+__device__ __forceinline__ void x16_q4k(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
+                                        const float *xsum, const XLane &L, float acc[2]) {
+    const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+    const uint8_t *ba = ra ? ra + 144 * u : nullptr, *bb = rb ? rb + 144 * u : nullptr;
+    const uint4 ha = ba ? ldg_nc_v4(ba) : z4, hb = bb ? ldg_nc_v4(bb) : z4;
+    const uint4 wa0 = ba ? ldg_nc_v4(ba + 16 + 32 * L.t) : z4, wa1 = ba ? ldg_nc_v4(ba + 32 + 32 * L.t) : z4;
+    const uint4 wb0 = bb ? ldg_nc_v4(bb + 16 + 32 * L.t) : z4, wb1 = bb ? ldg_nc_v4(bb + 32 + 32 * L.t) : z4;
+    // B: lo (hi) values of group t' = this lane's t for the lanes whose column takes them
+    const uint8_t *xb = xs + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
+    uint32_t bx[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(xb + 16 * i);
+        bx[4 * i] = v.x;
+        bx[4 * i + 1] = v.y;
+        bx[4 * i + 2] = v.z;
+        bx[4 * i + 3] = v.w;
+    }
+    float ds[2][2], dm[2][2];
+    x_q4k_scales(ha, L, ds[0], dm[0]);
+    x_q4k_scales(hb, L, ds[1], dm[1]);
+    const uint32_t A[8] = {wa0.x, wa0.y, wa0.z, wa0.w, wa1.x, wa1.y, wa1.z, wa1.w};
+    const uint32_t B[8] = {wb0.x, wb0.y, wb0.z, wb0.w, wb1.x, wb1.y, wb1.z, wb1.w};
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        // bytes (4j, 4j + 1) then (4j + 2, 4j + 3): x pairs in natural order
+        const uint32_t a01 = __byte_perm(A[j], 0u, 0x4140u), a23 = __byte_perm(A[j], 0u, 0x4342u);
+        const uint32_t b01 = __byte_perm(B[j], 0u, 0x4140u), b23 = __byte_perm(B[j], 0u, 0x4342u);
+        const uint32_t f0[4] = {a01 & 0x000F000Fu, b01 & 0x000F000Fu, a01 & 0x00F000F0u, b01 & 0x00F000F0u};
+        const uint32_t f1[4] = {a23 & 0x000F000Fu, b23 & 0x000F000Fu, a23 & 0x00F000F0u, b23 & 0x00F000F0u};
+        mma_f16_16816(d, f0, bx[2 * j] & L.b0on, bx[2 * j] & L.b1on);
+        mma_f16_16816(e, f1, bx[2 * j + 1] & L.b0on, bx[2 * j + 1] & L.b1on);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] += e[i];
+    const float2 xs2 = *reinterpret_cast<const float2 *>(xsum + 8 * u + 2 * L.t);
+    acc[0] += fmaf(ds[0][0], d[0], fmaf(ds[0][1], d[1], -fmaf(dm[0][0], xs2.x, dm[0][1] * xs2.y)));
+    acc[1] += fmaf(ds[1][0], d[2], fmaf(ds[1][1], d[3], -fmaf(dm[1][0], xs2.x, dm[1][1] * xs2.y)));
+}
+
+// All 32-bit words one lane needs from a Q6_K block (at a 2-byte aligned
+// address).  Lane t owns quarter c = t >> 1 and 16-value half lh = t & 1 of
+// both 128-value halves s: ql words [s][j] at 64 s + 32 c + 16 lh + 4j (low
+// nibbles: quarter c, high nibbles: quarter c + 2), qh words [s][j] at
+// 128 + 32 s + 16 lh + 4j, the 16 int8 scales (sign-flipped) and d.
+struct Q6Words {
+    uint32_t ql[8], qh[8], sc[4];
+    float d;
+};
+
+__device__ __forceinline__ void q6_load(const uint8_t *b, int t, Q6Words &q) {
+    if (b == nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q.ql[i] = 0u;
+            q.qh[i] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q.sc[i] = 0x80808080u;
+        q.d = 0.0f;
+        return;
+    }
+    // every load is issued before any is used; a block at an address = 2 (mod 4) takes each word from
+    // its two aligned neighbours
+    const bool odd = (reinterpret_cast<uintptr_t>(b) & 3u) != 0;
+    const uint8_t *a = odd ? b - 2 : b;
+    const int lo_off = 32 * (t >> 1) + 16 * (t & 1), hi_off = 128 + 16 * (t & 1);
+    uint32_t w0[20], w1[20];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int o = lo_off + 64 * (i >> 2) + 4 * (i & 3);
+        w0[i] = ldg32(a + o);
+        w1[i] = odd ? ldg32(a + o + 4) : 0u;
+        const int h = hi_off + 32 * (i >> 2) + 4 * (i & 3);
+        w0[8 + i] = ldg32(a + h);
+        w1[8 + i] = odd ? ldg32(a + h + 4) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w0[16 + i] = ldg32(a + 192 + 4 * i);
+        w1[16 + i] = odd ? ldg32(a + 196 + 4 * i) : 0u;
+    }
+    const uint32_t dw = ldg_nc_u16(b + 208);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        q.ql[i] = odd ? __funnelshift_r(w0[i], w1[i], 16) : w0[i];
+        q.qh[i] = odd ? __funnelshift_r(w0[8 + i], w1[8 + i], 16) : w0[8 + i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q.sc[i] = (odd ? __funnelshift_r(w0[16 + i], w1[16 + i], 16) : w0[16 + i]) ^ 0x80808080u;
+    q.d = half_bits_to_float(dw);
+}
+
+// Byte t of a sign-flipped scale word times d, exact: (2^23 + 128 + sc) - (2^23 + 128) is exact in fp32,
+// and so is d * sc.
+__device__ __forceinline__ float q6_ds(uint32_t scx, uint32_t sel, float d) {
+    return d * (__uint_as_float(__byte_perm(scx, 0x4B000000u, sel)) - 8388736.0f);
+}
+
+// Unit u (one 210-byte super-block) of two rows for Q6_K.  Per half s, lane t
+// accumulates its two 16-value groups (quarter c = t >> 1 and c + 2, half
+// lh = t & 1) over 8 mma and scales them once: groups 8s + t and 8s + t + 4.
+__device__ __forceinline__ void x16_q6k(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
+                                        const XLane &L, float acc[2]) {
+    Q6Words A, B;
+    q6_load(ra ? ra + 210 * u : nullptr, L.t, A);
+    q6_load(rb ? rb + 210 * u : nullptr, L.t, B);
+    const uint32_t k1056 = 0x64206420u;  // fp16 1056 = 1024 + 32 in both halves
+    const int c = L.t >> 1;
+    const uint32_t shl = static_cast<uint32_t>(4 - 2 * c), shr = static_cast<uint32_t>(2 * c);
+    const uint32_t sel = 0x7540u + static_cast<uint32_t>(L.t);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        // x of this lane's group (quarter c) or of quarter c + 2 (64 values on) for the high-slot lanes
+        const uint8_t *xb = xs + 2 * (256 * u + 128 * s + 32 * c + 16 * (L.t & 1)) + (L.b1on ? 128 : 0);
+        const uint4 x0 = *reinterpret_cast<const uint4 *>(xb), x1 = *reinterpret_cast<const uint4 *>(xb + 16);
+        const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float D[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t qla = A.ql[4 * s + j], qha = A.qh[4 * s + j];
+            const uint32_t qlb = B.ql[4 * s + j], qhb = B.qh[4 * s + j];
+            const uint32_t la = (qla & 0x0F0F0F0Fu) | ((qha << shl) & 0x30303030u);
+            const uint32_t lb = (qlb & 0x0F0F0F0Fu) | ((qhb << shl) & 0x30303030u);
+            const uint32_t ha = ((qla >> 4) & 0x0F0F0F0Fu) | ((qha >> shr) & 0x30303030u);
+            const uint32_t hb = ((qlb >> 4) & 0x0F0F0F0Fu) | ((qhb >> shr) & 0x30303030u);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                const uint32_t ps = h2 ? 0x4342u : 0x4140u;
+                const uint32_t a[4] = {hsub2_bits(__byte_perm(la, 0x64646464u, ps), k1056),
+                                       hsub2_bits(__byte_perm(lb, 0x64646464u, ps), k1056),
+                                       hsub2_bits(__byte_perm(ha, 0x64646464u, ps), k1056),
+                                       hsub2_bits(__byte_perm(hb, 0x64646464u, ps), k1056)};
+                const uint32_t b = bx[2 * j + h2];
+                mma_f16_16816(D, a, b & L.b0on, b & L.b1on);
+            }
+        }
+        acc[0] += fmaf(q6_ds(A.sc[2 * s], sel, A.d), D[0], q6_ds(A.sc[2 * s + 1], sel, A.d) * D[1]);
+        acc[1] += fmaf(q6_ds(B.sc[2 * s], sel, B.d), D[2], q6_ds(B.sc[2 * s + 1], sel, B.d) * D[3]);
+    }
+}
+
+// Unit u (8 blocks = 272 bytes, 256 values) of two rows for Q8_0: lane t takes blocks 2t and 2t + 1.
+// int8 codes as exact fp16: 1024 + 128 + q by byte permutes, minus 1152 by one f16x2 subtract.
+__device__ __forceinline__ void x16_q80(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
+                                        const XLane &L, float acc[2]) {
+    const uint8_t *ba = ra ? ra + 272 * u + 68 * L.t : nullptr, *bb = rb ? rb + 272 * u + 68 * L.t : nullptr;
+    uint32_t wa[17], wb[17];
+#pragma unroll
+    for (int i = 0; i < 17; ++i) {
+        wa[i] = ba ? ldg32(ba + 4 * i) : 0u;
+        wb[i] = bb ? ldg32(bb + 4 * i) : 0u;
+    }
+    // block 2t: d = bytes 0-1, q = bytes 2..33; block 2t + 1: d = bytes 34-35, q = bytes 36..67
+    const float da0 = half_bits_to_float(wa[0]), da1 = half_bits_to_float(wa[8] >> 16);
+    const float db0 = half_bits_to_float(wb[0]), db1 = half_bits_to_float(wb[8] >> 16);
+    const uint8_t *xb = xs + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
+    const uint32_t k1152 = 0x64806480u;  // fp16 1152 = 1024 + 128
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t qa0 = __funnelshift_r(wa[j], wa[j + 1], 16) ^ 0x80808080u;  // block 2t, values 4j..4j+3
+        const uint32_t qb0 = __funnelshift_r(wb[j], wb[j + 1], 16) ^ 0x80808080u;
+        const uint32_t qa1 = wa[9 + j] ^ 0x80808080u;  // block 2t + 1
+        const uint32_t qb1 = wb[9 + j] ^ 0x80808080u;
+        const uint2 xv = *reinterpret_cast<const uint2 *>(xb + 8 * j);
+        const uint32_t f0[4] = {hsub2_bits(__byte_perm(qa0, 0x64646464u, 0x4140u), k1152),
+                                hsub2_bits(__byte_perm(qb0, 0x64646464u, 0x4140u), k1152),
+                                hsub2_bits(__byte_perm(qa1, 0x64646464u, 0x4140u), k1152),
+                                hsub2_bits(__byte_perm(qb1, 0x64646464u, 0x4140u), k1152)};
+        const uint32_t f1[4] = {hsub2_bits(__byte_perm(qa0, 0x64646464u, 0x4342u), k1152),
+                                hsub2_bits(__byte_perm(qb0, 0x64646464u, 0x4342u), k1152),
+                                hsub2_bits(__byte_perm(qa1, 0x64646464u, 0x4342u), k1152),
+                                hsub2_bits(__byte_perm(qb1, 0x64646464u, 0x4342u), k1152)};
+        mma_f16_16816(d, f0, xv.x & L.b0on, xv.x & L.b1on);
+        mma_f16_16816(e, f1, xv.y & L.b0on, xv.y & L.b1on);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] += e[i];
+    acc[0] += fmaf(da0, d[0], da1 * d[1]);
+    acc[1] += fmaf(db0, d[2], db1 * d[3]);
+}
+
+__device__ __forceinline__ void x16_unit(int fmt, const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
+                                         const float *xsum, const XLane &L, float acc[2]) {
+    if (fmt == T2C_Q4_K) {
+        x16_q4k(ra, rb, u, xs, xsum, L, acc);
+    } else if (fmt == T2C_Q6_K) {
+        x16_q6k(ra, rb, u, xs, L, acc);
+    } else {
+        x16_q80(ra, rb, u, xs, L, acc);
+    }
+}
+
+__global__ void __launch_bounds__(kXThreads, 2) qmv_x16_kernel(const __grid_constant__ QParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int K = p.K;
+    uint8_t *xs = smem;
+    float *xsum = reinterpret_cast<float *>(smem + 2 * K);
+    float *red = xsum + (K >> 5);
+    float *part = red + kXWarps;  // [warp][gate/up][16 rows]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const XLane L = x_lane(lane);
+    pdl_wait();
+    pdl_trigger();
+    x16_prepare(p, xs, xsum, red);
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    const int wpb = p.wpb, bpc = kXWarps / wpb;
+    const int grp = warp / wpb, wig = warp - grp * wpb;
+    const int units = K >> 8;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * bpc; base < p.total_rowsets;
+         base += static_cast<int64_t>(gridDim.x) * bpc) {
+        const int64_t tile = base + grp;
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        if (tile < p.total_rowsets) {
+            const int si = swiglu ? 0 : stream_of(p, tile);
+            const int64_t row0 = (tile - p.s[si].rs_begin) * kMmaRows;
+#pragma unroll 1
+            for (int wi = 0; wi < (swiglu ? 2 : 1); ++wi) {
+                const QStream &st = p.s[swiglu ? wi : si];
+                const int64_t na = row0 + L.g, nb = row0 + L.g + 8;
+                const uint8_t *ra = na < st.n ? st.w + na * st.row_bytes : nullptr;
+                const uint8_t *rb = nb < st.n ? st.w + nb * st.row_bytes : nullptr;
+                float a2[2] = {0.0f, 0.0f};
+#pragma unroll 1
+                for (int u = wig; u < units; u += wpb) x16_unit(st.fmt, ra, rb, u, xs, xsum, L, a2);
+                acc[wi][0] = a2[0];
+                acc[wi][1] = a2[1];
+            }
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 1);
+                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
+                }
+        }
+        if (wpb > 1) {
+            if (L.t == 0) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    part[(warp * 2 + r) * 16 + L.g] = acc[r][0];
+                    part[(warp * 2 + r) * 16 + L.g + 8] = acc[r][1];
+                }
+            }
+            __syncthreads();
+            if (wig == 0) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    float v0 = 0.0f, v1 = 0.0f;
+                    for (int w = warp; w < warp + wpb; ++w) {
+                        v0 += part[(w * 2 + r) * 16 + L.g];
+                        v1 += part[(w * 2 + r) * 16 + L.g + 8];
+                    }
+                    acc[r][0] = v0;
+                    acc[r][1] = v1;
+                }
+            }
+            __syncthreads();
+        }
+        if (wig == 0 && tile < p.total_rowsets) mma_finish_block<1>(p, tile, acc, lane);
     }
 }
 
@@ -2070,9 +2652,8 @@ int encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row
 }
 
 size_t mma_fixed_smem(int MT, int K) {
-    return kStageHead + kMmaSlots * kMmaWarps * sizeof(MmaSlot) + static_cast<size_t>(MT) * (K / 64) * 16 +
-           2 * static_cast<size_t>(MT) * padded_k(K) + 32 + static_cast<size_t>(MT) * (K / 32) * 4 +
-           static_cast<size_t>(MT) * (K / 16) * 4 + static_cast<size_t>(kMmaWarps) * MT * 4;
+    return kStageHead + kMmaSlots * kMmaWarps * sizeof(MmaSlot) + static_cast<size_t>(MT) * xf_row_bytes(K) +
+           static_cast<size_t>(MT) * (K / 256) * 32 + static_cast<size_t>(kMmaWarps) * MT * 4;
 }
 
 template <int MT>
@@ -2119,18 +2700,11 @@ int launch_m1(QParams p, cudaStream_t stream) {
     return launch_pdl(qmv_m1_kernel, static_cast<int>(blocks), kMmaThreads, smem, stream, p);
 }
 
-bool mma_disabled() {
-    static const bool off = [] {
-        const char *v = getenv("T2C_QMV_DP4A");
-        return v != nullptr && v[0] == '1';
-    }();
-    return off;
-}
 
 // Tensor-core path when every stream is Q4_K, M <= 4 and K splits into 512-value segments.
 int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     used = false;
-    if (mma_disabled() || M > 4 || p.K % (kMmaSegBlocks * 256) != 0) return T2C_OK;
+    if (M > 4 || p.K % (kMmaSegBlocks * 256) != 0) return T2C_OK;
     for (int i = 0; i < p.nstreams; ++i)
         if (p.s[i].fmt != T2C_Q4_K) return T2C_OK;
     const bool swiglu = p.mode == MODE_SWIGLU;
@@ -2183,7 +2757,7 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
 // formats agree, else one launch per weight).
 int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     used = false;
-    if (mma_disabled() || M <= 4 || p.norm_w != nullptr) return T2C_OK;
+    if (M <= 4 || p.norm_w != nullptr) return T2C_OK;
     const int fmt = p.s[0].fmt;
     if (fmt != T2C_Q4_K && fmt != T2C_Q6_K && fmt != T2C_Q8_0) return T2C_OK;
     bool same = true;
@@ -2244,12 +2818,61 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     return rc;
 }
 
+// Exact fp16-x kernel, one launch per token (any GGUF type, K % 256 == 0).
+int launch_x16(QParams p, int64_t M, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    const bool swiglu = p.mode == MODE_SWIGLU;
+    int64_t tiles = 0;
+    for (int i = 0; i < p.nstreams; ++i) {
+        p.s[i].rs_begin = tiles;
+        tiles += (p.s[i].n + kMmaRows - 1) / kMmaRows;
+        if (swiglu) break;  // gate and up rows form one set of tiles
+    }
+    if (swiglu) p.s[1].rs_begin = tiles;  // never selected
+    p.total_rowsets = tiles;
+    const int units = p.K / 256;
+    // warps per tile (split K): enough warps in flight for the whole GPU, at most one unit each
+    const int64_t want = static_cast<int64_t>(sm_count()) * 2 * kXWarps;
+    int wpb = 1;
+    while (wpb < kXWarps && tiles * wpb < want && wpb * 2 <= units) wpb *= 2;
+    p.wpb = wpb;
+    const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4 + kXWarps * 4 +
+                        static_cast<size_t>(kXWarps) * 2 * 16 * 4;
+    int rc = ensure_smem_attr(qmv_x16_kernel, configured[device_slot()]);
+    if (rc) return rc;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmv_x16_kernel, kXThreads, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    const int bpc = kXWarps / wpb;
+    int64_t blocks = (tiles + bpc - 1) / bpc;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+    if (blocks > cap) blocks = cap;
+    for (int64_t t = 0; t < M; ++t) {
+        QParams q = p;
+        q.M = 1;
+        q.x = p.x + t * p.K;
+        for (int i = 0; i < kMaxStreams; ++i) {
+            if (q.s[i].y != nullptr) q.s[i].y += t * q.s[i].n;
+            if (q.s[i].res != nullptr) q.s[i].res += t * q.s[i].n;
+        }
+        if (p.mode == MODE_ARGMAX) {
+            q.ps = p.ps + t * p.G;
+            q.pt = p.pt + t * p.G;
+        }
+        rc = launch_pdl(qmv_x16_kernel, static_cast<int>(blocks), kXThreads, smem, stream, q);
+        if (rc) return rc;
+    }
+    return T2C_OK;
+}
+
 int run_linear(QParams p, int64_t M, cudaStream_t stream) {
     bool used = false;
     const int rc_gemm = try_gemm(p, M, stream, used);
     if (used) return rc_gemm;
     const int rc_mma = try_mma(p, M, stream, used);
     if (used) return rc_mma;
+    if (M <= 4 && p.K % 256 == 0) return launch_x16(p, M, stream);
     bool tma = true;
     const bool swiglu = p.mode == MODE_SWIGLU;
     int stage_bytes = 0;
@@ -2408,7 +3031,7 @@ extern "C" int t2c_linear_f32(int wtype, const float *x, const void *w, float *y
     __half *y16 = reinterpret_cast<__half *>(static_cast<uint8_t *>(scratch) + (M * K * 2 + 255) / 256 * 256);
     if ((rc = t2c_cast(x, T2C_F32, x16, T2C_F16, M * K, stream))) return rc;
     const cudaStream_t s = as_stream(stream);
-    if (!mma_disabled() && M > 4 && (wtype == T2C_Q4_K || wtype == T2C_Q8_0 || (wtype == T2C_Q6_K && K % 2048 == 0))) {
+    if (M > 4 && (wtype == T2C_Q4_K || wtype == T2C_Q8_0 || (wtype == T2C_Q6_K && K % 2048 == 0))) {
         // tensor-core GEMM writing fp32 directly from the TMEM accumulators
         QGemmArgs a = {};
         a.fmt = wtype;
