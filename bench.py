@@ -168,6 +168,49 @@ def traffic_from_profile() -> float | None:
     return None
 
 
+# -------------------------------------------------------------- TP parity
+def tp_parity(world: int, rank: int, local: int, steps: int = 32) -> dict:
+    """Greedy tokens of the tensor-parallel runner against the single-GPU runner (rank 0 compares).
+
+    A seeded 4-layer model with the 8B head layout (32 Q / 8 KV heads, 4096-wide projections, which
+    split over 2, 4 and 8 ranks at super-block boundaries), Q4_K linears and a Q6_K head, 24-token prompt,
+    `steps` graph-replayed decode steps on every rank.  The comparison against the CPU oracle runs in
+    tests/test_tp_gpu.py; this line shows that the measured configuration decodes the same tokens.
+    """
+    import torch.distributed as dist
+
+    from torch2vk_b200 import kernels
+    from torch2vk_b200.qwen3 import Qwen3Config, Qwen3Runner, random_weights
+    from torch2vk_b200.tp import make_tp_runner
+
+    dev = torch.device("cuda", local)
+    small = Qwen3Config(hidden=1024, layers=4, heads=32, kv_heads=8, head_dim=128, intermediate=4096, vocab=8192)
+    w = random_weights(small, seed=1, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
+    ids = torch.randint(0, small.vocab, (1, 24), generator=torch.Generator().manual_seed(0)).to(dev)
+    tp_runner = make_tp_runner(small, w, rank=rank, tp=world, batch=1, max_seq=96, max_new_tokens=steps + 2)
+    got = tp_runner.generate(ids, steps).clone()
+    torch.cuda.synchronize()
+    everyone = [torch.empty_like(got) for _ in range(world)]
+    dist.all_gather(everyone, got)
+    result = {"steps": steps, "first_diff": None, "ranks_identical": all(torch.equal(e, got) for e in everyone),
+              "reference": "single-GPU runner on the same weights"}
+    if rank == 0:
+        single = Qwen3Runner(small, w, batch=1, max_seq=96, max_new_tokens=steps + 2)
+        ref = single.generate(ids, steps)
+        ne = (ref.cpu() != got.cpu()).nonzero()
+        result["first_diff"] = int(ne[0, -1]) if ne.numel() else steps
+        single._graph = None
+        del single
+    result["device_status_bits"] = kernels.device_status()
+    dist.barrier()
+    tp_runner._graph = None
+    if tp_runner._peer is not None:
+        tp_runner._peer.close()
+    del tp_runner
+    torch.cuda.synchronize()
+    return result
+
+
 # ------------------------------------------------------------ CPU baseline
 def cpu_baseline(sample_layers: int = 3, steps: int = 6) -> dict:
     """The reference PyTorch CPU path (HF fp32 Qwen3, dequantized-weight math) timed on the host cores.
@@ -533,6 +576,7 @@ def main() -> None:
             return Qwen3Runner(cfg, weights, batch=batch, max_seq=PROMPT + decode_steps + 64,
                                max_new_tokens=decode_steps + 8)
     wb = weight_bytes(weights)
+    parity = tp_parity(world, rank, local) if world > 1 else None
 
     # ---- prefill (1024-token prompt), timed with events
     runner = new_runner(1)
@@ -542,12 +586,14 @@ def main() -> None:
     t_prefill = max_over_ranks(events_time(lambda: runner.prefill(prompt), 1, stream), world)
     runner.capture()
 
-    # ---- bs1 decode: W warm-up replays, then K timed replays
+    # ---- bs1 decode: W warm-up replays, then K timed replays.  Every rank starts its clock sampler
+    # first (its start-up takes up to seconds), then all ranks meet, so that the timed replays begin
+    # together and no rank's first peer all-reduce waits on another rank's sampler start-up.
     for _ in range(warm):
         runner.step()
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
         t_step = events_time(runner.step, steps, stream)
     barrier(world)
     t_step = max_over_ranks(t_step, world)
@@ -669,6 +715,8 @@ def main() -> None:
         "asr_encoder": asr,
         "device_status_bits": status,
     }
+    if parity is not None:
+        line["tp_parity"] = parity
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

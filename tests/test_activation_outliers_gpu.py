@@ -186,3 +186,52 @@ def test_lm_head_argmax_outliers(oracle, case, kind):
         assert abs(scores[g] - ref[row]) <= bound[row], f"group {g}: score {scores[g]} vs {ref[row]}"
         best = 4 * g + int(np.argmax(ref[4 * g:4 * g + 4]))
         assert ref[best] - ref[row] <= bound[best] + bound[row], f"group {g}: row {row} instead of {best}"
+
+
+@pytest.mark.parametrize("case", ["a", "b", "c"])
+@pytest.mark.parametrize("m", [5, 8, 16])
+def test_batched_q4k_outliers(oracle, case, m):
+    """5..16 tokens of Q4_K (the batched kernel: K split over a thread-block cluster, tokens as mma columns)."""
+    from torch2vk_b200 import kernels
+
+    n, k = 300, 4096
+    rng = np.random.default_rng(hash(("bt", case, m)) % 2**32)
+    x, mask = _activations(rng, case, m, k)
+    packed = oracle.quantize(_weights(rng, n, k, case, mask), "q4_k")
+    ref, absdot = _ref(oracle, packed, "q4_k", k, x)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q4_k", k,
+                       residual=torch.from_numpy(res).cuda())
+    ref = ref + res.astype(np.float64)
+    _check(y.float().cpu().numpy(), ref, absdot + np.abs(res), f"batched q4_k M={m} case {case}")
+
+
+@pytest.mark.parametrize("m,k", [(8, 12288), (9, 1024), (16, 3072)])
+def test_batched_fused_norm_swiglu_and_qkv(oracle, m, k):
+    """Batched kernel with the fused RMSNorm (the sum of squares shared across the cluster): gate/up + SwiGLU
+    and a fused three-weight QKV, at the K of the 8B down projection and of the 0.6B shapes."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m * 7 + k)
+    x, mask = _activations(rng, "b", m, k)
+    nw = _norm_weight(rng, k, mask)
+    xn = _normed(x, nw)
+    n = 200
+    pg = oracle.quantize(_weights(rng, n, k, "b", mask), "q4_k")
+    pu = oracle.quantize(_weights(rng, n, k, "b", mask), "q4_k")
+    y = kernels.linear_swiglu(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(), torch.from_numpy(pu).cuda(),
+                              "q4_k", k, norm_weight=torch.from_numpy(nw).cuda())
+    g, gabs = _ref(oracle, pg, "q4_k", k, xn)
+    u, uabs = _ref(oracle, pu, "q4_k", k, xn)
+    sig = 1.0 / (1.0 + np.exp(-g))
+    dsilu = sig * (1.0 + g * (1.0 - sig))
+    absdot = np.abs(dsilu * u) * (gabs + np.abs(g)) + np.abs(g * sig) * (uabs + np.abs(u))
+    _check(y.float().cpu().numpy(), g * sig * u, absdot, f"batched swiglu M={m} K={k}")
+    specs = [(96, "q4_k"), (40, "q4_k"), (72, "q4_k")]
+    packed = [oracle.quantize(_weights(rng, nn, k, "b", mask), kind) for nn, kind in specs]
+    outs = kernels.linear_multi(torch.from_numpy(x).cuda(), [(torch.from_numpy(pk).cuda(), kd) for pk, (_, kd) in
+                                                               zip(packed, specs)], k,
+                                norm_weight=torch.from_numpy(nw).cuda())
+    for (nn, kd), pk, o in zip(specs, packed, outs):
+        ref, absdot = _ref(oracle, pk, kd, k, xn)
+        _check(o.float().cpu().numpy(), ref, absdot, f"batched qkv M={m} K={k} n={nn}")

@@ -1,8 +1,10 @@
-"""Tensor parallelism on real GPUs (needs >= 2): TP=2 greedy tokens vs the single-GPU runner.
+"""Tensor parallelism on real GPUs (needs >= 2): TP greedy tokens vs the oracle and the single-GPU runner.
 
-The bound: fp16 all-reduces sum the row-parallel partials in a different
-order than one GPU does, so tokens may flip only at near-ties; the first 8
-tokens must agree and every rank must hold the same tokens.
+The gate: 32 greedy decode tokens of a seeded 32-Q / 8-KV-head model equal the
+oracle's (HF fp32 on the dequantized blocks) and the single-GPU runner's, and
+every rank holds the same tokens.  The row-parallel partial sums meet in a
+different order than on one GPU, which could flip a token only at a near-tie
+of the top two logits; the check prints the smallest top-two gap it saw.
 """
 
 from __future__ import annotations
@@ -21,7 +23,7 @@ REPO = Path(__file__).resolve().parents[1]
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("peer", ["1", "0"])
-def test_tp2_matches_single_gpu(peer):
+def test_tp2_matches_oracle_and_single_gpu(peer):
     """peer=1: decode all-reduces over NVLink peer memory; peer=0: NCCL all-reduce."""
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(peer)}",
@@ -32,5 +34,4 @@ def test_tp2_matches_single_gpu(peer):
     assert r.returncode == 0, out[-3000:]
     line = next(ln for ln in out.splitlines() if ln.startswith("TP OK"))
     assert "ranks_identical=True" in line and "status=0" in line, line
-    first = int(line.split("first_diff=")[1].split()[0])
-    assert first >= 8, out[-2000:]
+    assert "first_diff_oracle=32 " in line and "first_diff_single=32 " in line, line

@@ -29,6 +29,9 @@ struct QGemmArgs {
 
 // Returns T2C_OK, or T2C_EUNSUPPORTED when the shape is not served (caller falls back).
 int qgemm(const QGemmArgs &a, cudaStream_t stream);
+// 5.. tokens of Q4_K weights, 16 per launch (qbatch.cu): exact fp16-x batched matvec, optional fused RMSNorm.
+int qbatch(const QGemmArgs &a, const float *norm_w, float eps, cudaStream_t stream);
+cudaError_t status_qbatch(unsigned int *bits, int clear, cudaStream_t s);
 cudaError_t status_qgemm(unsigned int *bits, int clear, cudaStream_t s);
 
 }  // namespace t2c

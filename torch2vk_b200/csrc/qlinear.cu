@@ -2753,12 +2753,50 @@ int try_mma(QParams p, int64_t M, cudaStream_t stream, bool &used) {
     }
 }
 
+bool batched_kernel_serves(int64_t M, int64_t K) { return M > 4 && M <= 16 && (K <= 8192 || M <= 8); }
+
 // M > 4, Q4_K / Q6_K / Q8_0 streams, no fused RMSNorm: tcgen05 GEMM (fused QKV in one launch when the
 // formats agree, else one launch per weight).
 int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
     used = false;
-    if (M <= 4 || p.norm_w != nullptr) return T2C_OK;
+    if (M <= 4) return T2C_OK;
     const int fmt = p.s[0].fmt;
+    // Q4_K at 5..16 tokens with K <= 8192, or 5..8 tokens at any K: the batched exact kernel (fused
+    // RMSNorm allowed).  Beyond that the tcgen05 GEMM measured faster (per launch from 16 tokens at
+    // K = 12288, where the x slices leave room for only two weight stages per warp; over a whole
+    // batch-32 decode step at 32 tokens).
+    if (batched_kernel_serves(M, p.K) && p.mode != MODE_ARGMAX) {
+        bool all_q4k = true;
+        for (int i = 0; i < (p.mode == MODE_SWIGLU ? 2 : p.nstreams); ++i) all_q4k = all_q4k && p.s[i].fmt == T2C_Q4_K;
+        if (all_q4k) {
+            QGemmArgs b = {};
+            b.fmt = T2C_Q4_K;
+            b.K = p.K;
+            b.M = M;
+            b.x = p.x;
+            if (p.mode == MODE_SWIGLU) {
+                b.nw = 1;
+                b.w[0] = p.s[0].w;
+                b.w_up = p.s[1].w;
+                b.N[0] = p.s[0].n;
+                b.y[0] = p.s[0].y;
+            } else {
+                b.nw = p.nstreams;
+                for (int i = 0; i < p.nstreams; ++i) {
+                    b.w[i] = p.s[i].w;
+                    b.N[i] = p.s[i].n;
+                    b.y[i] = p.s[i].y;
+                    b.res[i] = p.s[i].res;
+                }
+            }
+            const int rc = qbatch(b, p.norm_w, p.eps, stream);
+            if (rc != T2C_EUNSUPPORTED) {
+                used = true;
+                return rc;
+            }
+        }
+    }
+    if (p.norm_w != nullptr) return T2C_OK;
     if (fmt != T2C_Q4_K && fmt != T2C_Q6_K && fmt != T2C_Q8_0) return T2C_OK;
     bool same = true;
     for (int i = 1; i < (p.mode == MODE_SWIGLU ? 2 : p.nstreams); ++i) same = same && p.s[i].fmt == fmt;

@@ -64,14 +64,22 @@ def linear(x: torch.Tensor, w: torch.Tensor, kind: str | int, k: int, *, residua
     return out
 
 
+def _fused_norm_ok(m: int, k: int, kinds) -> bool:
+    """Whether the kernels that serve M tokens fuse the RMSNorm prologue: the decode matvecs (M <= 4)
+    and the batched Q4_K kernel do, the tcgen05 GEMM does not.  The batched kernel serves Q4_K at
+    5..16 tokens when K <= 8192, and at 5..8 tokens for any K (qlinear.cu, batched_kernel_serves)."""
+    batched = 4 < m <= 16 and (k <= 8192 or m <= 8)
+    return m <= 4 or (batched and all(wtype_of(kd) == wtype_of("q4_k") for kd in kinds))
+
+
 def linear_multi(x: torch.Tensor, weights: list[tuple[torch.Tensor, str | int]], k: int, *,
                  norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
                  residuals: list[torch.Tensor | None] | None = None,
                  outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
     """One x, up to three weights (fused QKV / gate-up); optional fused RMSNorm prologue."""
     m = _check_x(x, k)
-    if norm_weight is not None and m > 4:
-        # the tensor-core GEMM for M > 4 reads x as it is: normalize first (torch-allocated temporary)
+    if norm_weight is not None and not _fused_norm_ok(m, k, [kind for _, kind in weights]):
+        # the tensor-core GEMM reads x as it is: normalize first (torch-allocated temporary)
         x, norm_weight = rms_norm(x, norm_weight, eps), None
     wtypes, wptrs, ns = [], [], []
     for w, kind in weights:
@@ -102,7 +110,7 @@ def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, kin
     m = _check_x(x, k)
     if out is None:
         out = torch.empty(*x.shape[:-1], n, dtype=torch.float16, device=x.device)
-    if norm_weight is not None and m > 4:
+    if norm_weight is not None and not _fused_norm_ok(m, k, [kind]):
         x, norm_weight = rms_norm(x, norm_weight, eps), None
     _lib.lib().call("t2c_linear_swiglu", wtype, _lib.ptr(x), _lib.ptr(w_gate), _lib.ptr(w_up), _lib.ptr(out),
                     _lib.ptr(norm_weight), float(eps), m, n, k, _lib.stream_ptr())
