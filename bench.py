@@ -446,6 +446,145 @@ def run_sweep(args, local: int) -> None:
         raise SystemExit("device status bit set")
 
 
+def run_attention(args, local: int) -> None:
+    """Attention alone: fp16 GQA with 32 Q / 8 KV heads, head_dim 128, Q/K/V
+    N(0, 1) / sqrt(128).  (a) causal prefill of S in {512, 2048, 8192} tokens at batch 1 and 8
+    (attn_prefill_tc_kernel), roofline = tensor (4 B NH D S (S + 1) / 2 flop); (b) decode of one query
+    token against KV caches of {1k, 4k, 16k, 32k} positions at batch 1, 16 and 64, the decode path of
+    the runner (attn_decode_fused: q / k norm + RoPE + the new position's cache write + split attention,
+    the split count chosen as Qwen3Runner chooses it), roofline = HBM (K + V bytes read).  Each point:
+    `--warmup` untimed launches, then `--steps` launches in one CUDA graph timed with events (decode:
+    the caches of every point exceed L2 from 1k positions at batch 16; smaller points are L2-resident and
+    marked).  One JSON line per point."""
+    from torch2vk_b200 import kernels
+
+    pk, src = peaks()
+    hbm, tc = float(pk["hbm_gbs"]), float(pk["bf16_tflops"])
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    NH, NK, D = 32, 8, 128
+    g = torch.Generator(device=dev).manual_seed(3)
+    scale = 1.0 / np.sqrt(D)
+
+    def timed(launch) -> float:
+        launch()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                launch()
+        for _ in range(args.warmup):
+            graph.replay()
+        t = events_time(graph.replay, 3, stream) / args.steps
+        del graph
+        return t
+
+    for B in (1, 8):
+        for S in (512, 2048, 8192):
+            q = torch.randn(B, S, NH, D, device=dev, generator=g).mul_(scale).half()
+            kc = torch.randn(B, S, NK, D, device=dev, generator=g).mul_(scale).half()
+            vc = torch.randn(B, S, NK, D, device=dev, generator=g).mul_(scale).half()
+            pos = torch.zeros(B, dtype=torch.int32, device=dev)
+            out = torch.empty_like(q)
+            t = timed(lambda: kernels.attn_prefill(q, kc, vc, pos, batch=B, tokens=S, n_heads=NH, n_kv=NK,
+                                                   head_dim=D, out=out))
+            flops = 4.0 * B * NH * D * S * (S + 1) / 2
+            print(json.dumps({"mode": "prefill", "B": B, "S": S, "us": round(t * 1e6, 1),
+                              "TFLOPs": round(flops / t / 1e12, 1), "tensor_frac": round(flops / t / 1e12 / tc, 3),
+                              "peak_source": src}), flush=True)
+            del q, kc, vc, out
+    torch.cuda.empty_cache()
+    qw = torch.ones(D, device=dev)
+    kw = torch.ones(D, device=dev)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    for B in (1, 16, 64):
+        for L in (1024, 4096, 16384, 32768):
+            max_seq = L + 64
+            kc = torch.randn(B, max_seq, NK, D, device=dev, generator=g).mul_(scale).half()
+            vc = torch.randn(B, max_seq, NK, D, device=dev, generator=g).mul_(scale).half()
+            qkv = torch.randn(B, (NH + 2 * NK) * D, device=dev, generator=g).half()
+            qi, ki, vi = qkv[:, :NH * D], qkv[:, NH * D:(NH + NK) * D], qkv[:, (NH + NK) * D:]
+            pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+            if max_seq <= 16384:
+                splits = max(1, min(8, max(1, 296 // (B * NK)), max_seq // 64))
+            else:
+                splits = max(1, min(32, max(1, 592 // (B * NK)), max_seq // 64))
+            ws = kernels.attn_decode_fused_workspace(B, NH, NK, D, splits, dev)
+            out = torch.empty(B, NH * D, dtype=torch.float16, device=dev)
+            t = timed(lambda: kernels.attn_decode_fused(qi, ki, vi, qw, kw, inv, kc, vc, pos, batch=B, n_heads=NH,
+                                                        n_kv=NK, head_dim=D, splits=splits, workspace=ws, out=out))
+            kv_bytes = 2.0 * B * NK * L * D * 2
+            print(json.dumps({"mode": "decode", "B": B, "L": L, "splits": splits, "us": round(t * 1e6, 1),
+                              "GBps": round(kv_bytes / t / 1e9, 1), "hbm_frac": round(kv_bytes / t / 1e9 / hbm, 3),
+                              "l2_resident": kv_bytes < 2 * 126e6, "peak_source": src}), flush=True)
+            del kc, vc, qkv, ws, out
+            torch.cuda.empty_cache()
+    if kernels.device_status() != 0:
+        raise SystemExit("device status bit set")
+
+
+def asr_e2e_figures(dev: torch.device) -> dict:
+    """BASELINE config 5 end to end: B clips of 3000 seeded N(0, 1) log-mel frames -> the Qwen3-ASR-0.6B
+    audio tower (Q8_0) -> 390 audio rows injected into a 405-token prompt -> Qwen3-0.6B-shaped text
+    decoder (Q4_K_M linears, Q6_K head) -> 64 greedy tokens per clip, at B = 1, 4, 16.  Seeded random
+    weights (no checkpoint here).  Each B: one untimed run (graph capture), then one run timed per phase
+    with CUDA events; inputs uploaded before the timed region."""
+    from torch2vk_b200.asr import AsrEncoderConfig, random_params
+    from torch2vk_b200.asr_pipeline import AsrPipeline
+    from torch2vk_b200.qwen3 import Qwen3Config, random_weights
+
+    acfg = AsrEncoderConfig.qwen3_asr_0_6b()
+    aparams = random_params(acfg, seed=0)
+    tcfg = Qwen3Config.qwen3_0_6b()
+    tw = random_weights(tcfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k_m")
+    rng = np.random.default_rng(4)
+    gen = torch.Generator().manual_seed(1)
+    prefix = torch.randint(0, tcfg.vocab, (1, 9), generator=gen)
+    suffix = torch.randint(0, tcfg.vocab, (1, 6), generator=gen)
+    points = []
+    for batch in (1, 4, 16):
+        pipe = AsrPipeline(acfg, aparams, tcfg, tw, batch=batch, frames=3000, prefix=9, suffix=6, max_new_tokens=64,
+                           device=dev)
+        clips = pipe.upload([rng.standard_normal((acfg.num_mel_bins, 3000)).astype(np.float32) for _ in range(batch)])
+        ids = pipe.prompt(prefix, suffix, placeholder=151646)
+        pipe.transcribe(clips, ids)
+        t = pipe.timed_transcribe(clips, ids)
+        total = t.encoder_s + t.prefill_s + t.decode_s
+        points.append({"batch": batch, "tok_s": batch * 64 / total, "encoder_ms": t.encoder_s * 1e3,
+                       "prefill_ms": t.prefill_s * 1e3, "decode_ms": t.decode_s * 1e3,
+                       "prompt_tokens": pipe.prompt_len})
+        pipe.runner._graph = None
+        del pipe, clips
+        torch.cuda.empty_cache()
+    del tw
+    return {"workload": "Qwen3-ASR-0.6B-shaped: 3000-frame clips, audio tower + 28-layer text decoder, 64 greedy "
+                        "tokens per clip (seeded weights)", "points": points}
+
+
+def qwen3_0_6b_figures(dev: torch.device, stream: torch.cuda.Stream) -> dict:
+    """BASELINE config 1 on the fused runner: Qwen3-0.6B architecture (28 layers, hidden 1024, 16 Q / 8 KV
+    heads, FFN 3072, vocab 151936, tied-embedding shapes), seeded weights quantized on the GPU (Q4_K
+    linears, Q6_K head, F16 embedding), batch 1: a 128-token random prompt prefilled, then 128 greedy decode
+    steps replayed from the CUDA graph."""
+    from torch2vk_b200.qwen3 import Qwen3Config, Qwen3Runner, random_weights
+
+    cfg = Qwen3Config.qwen3_0_6b()
+    w = random_weights(cfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k")
+    runner = Qwen3Runner(cfg, w, batch=1, max_seq=128 + 128 + 16, max_new_tokens=128 + 8)
+    prompt = torch.randint(0, cfg.vocab, (1, 128), generator=torch.Generator().manual_seed(0)).to(dev)
+    runner.prefill(prompt)
+    t_pre = events_time(lambda: runner.prefill(prompt), 3, stream)
+    runner.prefill(prompt)
+    runner.capture()
+    runner.step()  # the captured step's first replay
+    t_dec = events_time(runner.step, 127, stream)
+    runner._graph = None
+    del runner, w
+    torch.cuda.empty_cache()
+    return {"workload": "Qwen3-0.6B, batch 1, 128-token prompt then 128 greedy decode steps (CUDA-graph replay)",
+            "prefill_tok_s": 128 / t_pre, "decode_tok_s": 1.0 / t_dec}
+
+
 def run_session(args, local: int) -> None:
     """The bs1 decode step of a Qwen3-0.6B-shaped model dispatched through RuntimeSession, the
     reference-facing path (286 dispatches a step): `--warmup` direct frames, then a replay plan of the
@@ -523,6 +662,8 @@ def main() -> None:
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",
                     help="the quantized-linear sweep (one JSON line per shape, M and type) instead of the step")
+    ap.add_argument("--attention", action="store_true",
+                    help="time attention alone (BASELINE config 3 grid); one JSON line per point")
     ap.add_argument("--session", action="store_true",
                     help="the decode step through RuntimeSession and a replay plan (one JSON line) instead")
     args = ap.parse_args()
@@ -540,6 +681,9 @@ def main() -> None:
         return
     if args.session:
         run_session(args, local)
+        return
+    if args.attention:
+        run_attention(args, local)
         return
 
     from torch2vk_b200 import kernels
@@ -673,6 +817,8 @@ def main() -> None:
     asr = {"workload": "Qwen3-ASR-0.6B audio encoder, 3000 mel frames (30 chunks, 390 tokens), Q8_0 weights",
            "ms": t_asr * 1e3, "tflops": arun.flops(ainp) / t_asr / 1e12}
     del arun, atens
+    small = qwen3_0_6b_figures(dev, stream) if world == 1 else None
+    asr_e2e = asr_e2e_figures(dev) if world == 1 else None
     clk = clocks.summary()
     line = {
         "metric": "qwen3_8b_int4_decode_tok_s_bs1",
@@ -717,6 +863,10 @@ def main() -> None:
     }
     if parity is not None:
         line["tp_parity"] = parity
+    if small is not None:
+        line["qwen3_0_6b"] = small
+    if asr_e2e is not None:
+        line["asr_e2e"] = asr_e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

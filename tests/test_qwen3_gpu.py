@@ -46,7 +46,10 @@ def _check_layer(got: torch.Tensor, ref: torch.Tensor, what: str) -> None:
     g, r = got.float().cpu().flatten(), ref.float().flatten()
     max_abs = float((g - r).abs().max())
     cos = float(torch.nn.functional.cosine_similarity(g, r, dim=0))
-    assert max_abs <= MAX_ABS and cos >= MIN_COS, f"{what}: max_abs {max_abs:.4g} cos {cos:.6f}"
+    assert max_abs <= MAX_ABS and cos >= MIN_COS, (
+        f"{what}: max_abs {max_abs:.4g} cos {cos:.6f} (max |ref| {float(r.abs().max()):.4g}, "
+        f"|ref| at the worst element {float(r[(g - r).abs().argmax()].abs()):.4g}, "
+        f"99.9th percentile error {float((g - r).abs().quantile(0.999)) if g.numel() < 2**24 else float('nan'):.4g})")
 
 
 def _run(oracle_cfg: dict, prompt_len: int, steps: int, batch: int = 1, topology: str = "q4_k_m"):

@@ -6,13 +6,12 @@ F16 names / prefixes, forced Q8_0 / Q6_K names / prefixes, rank != 2 -> F32,
 cols % 256 -> Q4_K, cols % 32 -> Q8_0, else F32).  export_q4_k_m_gguf streams
 safetensors tensors through the GPU quantizer kernels (bit-exact with the CPU
 oracle restatement of the reference quantizers) into a GGUF v3 file with the
-reference's metadata keys, tensor order and 32-byte alignment.
+reference's metadata keys and 32-byte alignment, header first (payload sizes
+come from the checkpoint headers).
 """
 
 from __future__ import annotations
 
-import shutil
-from collections.abc import Iterator
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -157,17 +156,43 @@ def quantize_q8_0_vulkan(rt, array: np.ndarray, *, name: str = "") -> np.ndarray
 
 
 # ------------------------------------------------------------------ export
-def _iter_safetensors(model_dir: Path, subdirs: tuple[str, ...]) -> Iterator[tuple[str, torch.Tensor]]:
-    from safetensors import safe_open
-
+def _safetensor_files(model_dir: Path, subdirs: tuple[str, ...]) -> list[Path]:
+    files: list[Path] = []
     for source in (model_dir, *(model_dir / s for s in subdirs)):
-        paths = sorted(source.glob("*.safetensors"))
-        if not paths:
+        found = sorted(source.glob("*.safetensors"))
+        if not found:
             raise FileNotFoundError(f"No safetensors files found in {source}")
-        for p in paths:
-            with safe_open(p, framework="pt", device="cpu") as ck:
-                for name in ck.keys():
-                    yield name, ck.get_tensor(name)
+        files += found
+    return files
+
+
+@dataclass(frozen=True, slots=True)
+class _PlannedTensor:
+    """One checkpoint tensor as it will sit in the GGUF file: where it comes from, its type, its logical
+    shape there and the size of its payload (known from the checkpoint header alone)."""
+    name: str
+    source: Path
+    ggml_type: GGUFTensorType
+    logical_shape: tuple[int, ...]
+    nbytes: int
+
+
+def _payload_plan(name: str, shape: tuple[int, ...], dtype: str,
+                  config: "Q4KMQuantizationConfig") -> tuple[GGUFTensorType, tuple[int, ...], int]:
+    """GGUF type, logical shape and payload bytes of a checkpoint tensor, from its shape and dtype."""
+    t = config.gguf_type(checkpoint_key=name, dtype=dtype, shape=shape)
+    count = int(np.prod(shape)) if shape else 1
+    if t is GGUFTensorType.F16:
+        return t, shape, 2 * count
+    if t is GGUFTensorType.F32:
+        return t, shape, 4 * count
+    rows, cols = _matrix_shape(shape)
+    if t is GGUFTensorType.Q8_0:
+        padded = _round_up(cols, 32)
+        return t, (rows, padded), rows * (padded // 32) * 34
+    if t is GGUFTensorType.Q6_K:
+        return t, (rows, cols), rows * (cols // 256) * 210
+    return t, shape, rows * (cols // 256) * 144
 
 
 def tensor_to_gguf(name: str, tensor: torch.Tensor, config: Q4KMQuantizationConfig,
@@ -211,37 +236,64 @@ def gguf_matches_quantization(path: Path, config: Q4KMQuantizationConfig) -> boo
 
 def export_q4_k_m_gguf(*, model_dir: str | Path, output: str | Path, config: Q4KMQuantizationConfig,
                        overwrite: bool = False, device: int = 0) -> Path:
-    """safetensors checkpoint -> Q4_K_M GGUF (quantize/gguf.py:191-247); an existing file with
-    the same type plan is kept unless overwrite."""
+    """safetensors checkpoint -> Q4_K_M GGUF v3 file (the reference's export entry point,
+    src/torch2vk/quantize/gguf.py:191-247: same arguments, type plan and metadata keys; an existing file
+    whose tensor types already follow `config` is kept unless `overwrite`).
+
+    The file is produced header first: every tensor's GGUF type and payload size follow from the
+    checkpoint's own headers (names, shapes, dtypes), so the header with all tensor offsets is written
+    before any weight is read; then each tensor is loaded, quantized on the GPU and written at its offset
+    (payloads 32-byte aligned).  The file is assembled under a temporary name beside `output` and renamed
+    into place only when complete.
+    """
+    from safetensors import safe_open
+
     out = Path(output).expanduser().resolve()
     if out.exists() and not overwrite and gguf_matches_quantization(out, config):
         return out
+    plan: list[_PlannedTensor] = []
+    names: set[str] = set()
+    for path in _safetensor_files(Path(model_dir).expanduser().resolve(), config.safetensor_subdirs):
+        with safe_open(path, framework="pt", device="cpu") as ck:
+            for name in ck.keys():
+                if name in names:
+                    raise ValueError(f"tensor {name} appears twice in the checkpoint ({path})")
+                names.add(name)
+                sl = ck.get_slice(name)
+                shape = tuple(int(d) for d in sl.get_shape())
+                dtype = {"F32": "float32", "F16": "float16", "BF16": "bfloat16"}.get(sl.get_dtype(),
+                                                                                  sl.get_dtype().lower())
+                t, logical, nbytes = _payload_plan(name, shape, dtype, config)
+                plan.append(_PlannedTensor(name, path, t, logical, nbytes))
     out.parent.mkdir(parents=True, exist_ok=True)
-    if out.exists():
-        out.unlink()
-    data_path = out.with_name(f"{out.name}.data.tmp")
-    final_path = out.with_name(f"{out.name}.tmp")
-    infos: list[gguf.WriteTensor] = []
-    seen: set[str] = set()
+    partial = out.parent / f".{out.name}.partial"
     try:
-        with data_path.open("wb") as data:
-            for name, tensor in _iter_safetensors(Path(model_dir).expanduser().resolve(), config.safetensor_subdirs):
-                if name in seen:
-                    raise ValueError(f"Duplicate safetensor tensor name while writing GGUF: {name}")
-                seen.add(name)
-                wt = tensor_to_gguf(name, tensor, config, device)
-                data.write(np.ascontiguousarray(wt.data).tobytes())
-                gguf.pad_to_alignment(data)
-                infos.append(gguf.WriteTensor(wt.name, np.empty(wt.data.nbytes, np.uint8), wt.ggml_type,
-                                              wt.logical_shape))
-        with final_path.open("wb") as h:
-            gguf.write_header(h, infos, arch=config.gguf_arch, name=config.model_name,
-                              extra_u32=config.extra_uint32_metadata)
-            with data_path.open("rb") as data:
-                shutil.copyfileobj(data, h, length=16 << 20)
-        final_path.replace(out)
+        with partial.open("wb") as h:
+            # the header only needs each payload's size: stand-in arrays of that many bytes
+            gguf.write_header(h, [gguf.WriteTensor(p.name, np.empty(p.nbytes, np.uint8), p.ggml_type,
+                                                   p.logical_shape) for p in plan],
+                              arch=config.gguf_arch, name=config.model_name, extra_u32=config.extra_uint32_metadata)
+            open_file, handle = None, None
+            try:
+                for p in plan:
+                    if p.source != open_file:
+                        if handle is not None:
+                            handle.__exit__(None, None, None)
+                        handle = safe_open(p.source, framework="pt", device="cpu")
+                        handle.__enter__()
+                        open_file = p.source
+                    wt = tensor_to_gguf(p.name, handle.get_tensor(p.name), config, device)
+                    payload = np.ascontiguousarray(wt.data)
+                    if payload.nbytes != p.nbytes or wt.ggml_type is not p.ggml_type:
+                        raise RuntimeError(f"{p.name}: planned {p.ggml_type.name} {p.nbytes} bytes, "
+                                           f"produced {wt.ggml_type.name} {payload.nbytes}")
+                    h.write(payload.tobytes())
+                    gguf.pad_to_alignment(h)
+            finally:
+                if handle is not None:
+                    handle.__exit__(None, None, None)
+        partial.replace(out)
     finally:
-        for p in (data_path, final_path):
-            if p.exists():
-                p.unlink()
+        if partial.exists():
+            partial.unlink()
     return out

@@ -224,8 +224,13 @@ class Qwen3Runner:
                             token_index_dev=self.token_index, stop_on_eos=bool(self.eos_ids))
 
     # ------------------------------------------------------------- forward
-    def prefill(self, ids: torch.Tensor, *, layer_outputs: list[torch.Tensor] | None = None) -> None:
-        """Runs the prompt ids [batch, T] through all layers and selects the first new token."""
+    def prefill(self, ids: torch.Tensor, *, layer_outputs: list[torch.Tensor] | None = None,
+                inject: tuple[torch.Tensor, torch.Tensor] | None = None) -> None:
+        """Runs the prompt ids [batch, T] through all layers and selects the first new token.
+
+        inject = (positions int64 [S], rows fp16 [batch, S, hidden]): after the token embedding, the
+        rows at those prompt positions are replaced (Qwen3-ASR's audio features at the audio placeholder
+        positions: the reference's audio_inject program, optimized_qwen3_asr/dispatch)."""
         cfg = self.cfg
         if ids.shape[0] != self.batch:
             raise ValueError(f"prefill ids batch {ids.shape[0]} != runner batch {self.batch}")
@@ -238,6 +243,8 @@ class Qwen3Runner:
         self.stopped.zero_()
         b = self._alloc(self.batch * tokens)
         self._embed(ids.reshape(-1).contiguous(), b.h)
+        if inject is not None:
+            kernels.index_copy_rows(b.h.view(self.batch, tokens, cfg.hidden), inject[0], inject[1])
         for i in range(cfg.layers):
             self._layer(i, b, tokens, decode=False)
             if layer_outputs is not None:
