@@ -204,6 +204,33 @@ int t2c_attn_decode_fused(const void *q_in, const void *k_in, const void *v_in, 
 int64_t t2c_attn_decode_fused_workspace(int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits);
 
 /*
+ * Paged KV cache (split-K decode attention and the cache write).  The cache is
+ * a pool of pages, each page_size (a power of two) positions of NK heads x D
+ * fp16: element (page, row, head, d) at page * page_stride + row * row_stride
+ * + head * head_stride + d.  block_table[b * bt_stride + i] is the physical
+ * page holding positions [i * page_size, (i + 1) * page_size) of sequence b,
+ * so a sequence holds at most bt_stride * page_size positions.  Attention is
+ * t2c_attn_decode's (same workspace rule, output layout and out-of-range
+ * position report) with the row address taken from the table; the write
+ * stores T new rows per sequence (src [B, T, NK * D] by element strides) at
+ * positions[b] .. positions[b] + T - 1.  A table entry outside
+ * [0, num_pages) is reported through t2c_device_status (the write skips that
+ * row; attention reads page 0 in its place).
+ * The reference keeps one contiguous cache per layer (kv_cache_write_f16.py:22-92,
+ * sdpa_decode_cache_f16.py:22-136); the paged layout serves the same attention
+ * contract for many sequences sharing one pool.
+ */
+int t2c_attn_decode_paged(const void *q, const void *k_pages, const void *v_pages, void *out,
+                          const int32_t *positions, const int32_t *block_table, int64_t bt_stride, int64_t num_pages,
+                          int64_t page_size, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                          int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits, float *workspace,
+                          int64_t workspace_floats, void *stream);
+int t2c_kv_cache_write_paged(void *pages, const void *src, int64_t src_b_stride, int64_t src_t_stride,
+                             const int32_t *positions, const int32_t *block_table, int64_t bt_stride,
+                             int64_t num_pages, int64_t page_size, int64_t page_stride, int64_t row_stride,
+                             int64_t head_stride, int64_t B, int64_t T, int64_t NK, int64_t D, void *stream);
+
+/*
  * t2c_attn_decode for callers that cannot allocate device memory: the same
  * split-K decode attention, with its split partials kept in a fixed 16 MiB
  * device array inside the library instead of a caller workspace.  Meant for

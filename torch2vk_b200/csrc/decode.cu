@@ -176,11 +176,17 @@ constexpr int kAttnWarps = 4;
 constexpr int kMaxGroup = 8;
 constexpr int kMaxSplits = 64;
 
-template <int E, int G>
+// Paged caches (PAGED): position p of sequence b lives in physical page
+// bt[b * bt_stride + (p >> page_log2)], row (p & (page size - 1)) of it; cb is
+// then the page stride (elements) and cs the row stride inside a page.  A
+// block-table entry outside [0, num_pages) is reported and read as page 0, so
+// every access stays inside the pool.
+template <int E, int G, bool PAGED>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     __half *__restrict__ out, const int32_t *__restrict__ positions, int NH, int NK, int64_t cb, int64_t cs,
-    int64_t ch, int max_len, int chunk, int splits, float *__restrict__ ws, float scale) {
+    int64_t ch, int max_len, int chunk, int splits, float *__restrict__ ws, float scale,
+    const int32_t *__restrict__ bt, int64_t bt_stride, int page_log2, int num_pages) {
     constexpr int D = E * 32;
     __shared__ float qs[G][D];
     __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
@@ -213,17 +219,29 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
 #pragma unroll
         for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
     }
-    const __half *kbase = kc + b * cb + kh * ch;
-    const __half *vbase = vc + b * cb + kh * ch;
     for (int t0 = p0 + warp * 32; t0 < p1; t0 += kAttnWarps * 32) {
         const int pos = t0 + lane;
         const bool valid = pos < p1;
+        // element offset of this lane's position row (K and V share it)
+        int64_t roff = kh * ch;
+        if constexpr (PAGED) {
+            if (valid) {
+                int page = bt[b * bt_stride + (pos >> page_log2)];
+                if (page < 0 || page >= num_pages) {
+                    report_device_error(T2C_EINVAL);
+                    page = 0;
+                }
+                roff += static_cast<int64_t>(page) * cb + static_cast<int64_t>(pos & ((1 << page_log2) - 1)) * cs;
+            }
+        } else {
+            roff += b * cb + static_cast<int64_t>(pos) * cs;
+        }
         // scores: lane = position; the whole K row is requested at once
         float s[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.0f;
         if (valid) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kbase + static_cast<int64_t>(pos) * cs);
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kc + roff);
             uint4 kraw[D / 8];
 #pragma unroll
             for (int c = 0; c < D / 8; ++c) kraw[c] = kr[c];
@@ -245,8 +263,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
         float vf[32][E];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
+            const int64_t rj = __shfl_sync(0xffffffffu, roff, j);
             if (j < n_valid) {
-                const __half *vr = vbase + static_cast<int64_t>(t0 + j) * cs + lane * E;
+                const __half *vr = vc + rj + lane * E;
                 if constexpr (E == 4) {
                     const float4 f = h4_to_f4(*reinterpret_cast<const uint2 *>(vr));
                     vf[j][0] = f.x;
@@ -366,6 +385,41 @@ __global__ void attn_combine_kernel(const float *__restrict__ ws, __half *__rest
         }
         for (; sp < splits; ++sp) a0 = fmaf(wts[sp], rec[sp * (D + 2) + 2 + d], a0);
         out[bh * D + d] = __float2half_rn((a0 + a1 + a2 + a3) * inv);
+    }
+}
+
+// Paged KV write: rows src[b * src_sb + t * src_st + h * D ..] (T new tokens per
+// sequence, NK heads) go to position positions[b] + t of sequence b: page
+// bt[b * bt_stride + (pos >> page_log2)], row pos & (P - 1).  One thread per
+// 16-byte piece of a row.
+__global__ void kv_write_paged_kernel(__half *__restrict__ pages, const __half *__restrict__ src, int64_t src_sb,
+                                      int64_t src_st, const int32_t *__restrict__ positions,
+                                      const int32_t *__restrict__ bt, int64_t bt_stride, int page_log2,
+                                      int64_t pstride, int64_t rstride, int64_t hstride, int B, int T, int NK, int D,
+                                      int max_len, int num_pages) {
+    pdl_wait();
+    pdl_trigger();
+    const int pieces = D / 8;
+    const int64_t total = static_cast<int64_t>(B) * T * NK * pieces;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int piece = static_cast<int>(i % pieces);
+        const int h = static_cast<int>((i / pieces) % NK);
+        const int t = static_cast<int>((i / (static_cast<int64_t>(pieces) * NK)) % T);
+        const int b = static_cast<int>(i / (static_cast<int64_t>(pieces) * NK * T));
+        const int pos = positions[b] + t;
+        if (pos < 0 || pos >= max_len) {  // no page row for it: report, write nothing
+            if (piece == 0 && h == 0) report_device_error(T2C_EINVAL);
+            continue;
+        }
+        const int64_t page = bt[b * bt_stride + (pos >> page_log2)];
+        if (page < 0 || page >= num_pages) {  // not a page of the pool: report, write nothing
+            report_device_error(T2C_EINVAL);
+            continue;
+        }
+        const uint4 v = *reinterpret_cast<const uint4 *>(src + b * src_sb + t * src_st + h * D + 8 * piece);
+        *reinterpret_cast<uint4 *>(pages + page * pstride + static_cast<int64_t>(pos & ((1 << page_log2) - 1)) * rstride +
+                                   h * hstride + 8 * piece) = v;
     }
 }
 
@@ -1604,11 +1658,10 @@ extern "C" int t2c_attn_decode(const void *q, const void *k_cache, const void *v
     const dim3 grid(static_cast<unsigned>(B * NK * splits)), block(kAttnWarps * 32);
     int rc = T2C_OK;
 #define T2C_ATT(E, GG)                                                                                           \
-    rc = launch(attn_decode_kernel<E, GG>, grid, block, 0, s, static_cast<const __half *>(q),                      \
+    rc = launch(attn_decode_kernel<E, GG, false>, grid, block, 0, s, static_cast<const __half *>(q),               \
                 static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache), static_cast<__half *>(out), \
                 positions, static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, static_cast<int>(max_len), chunk, \
-                static_cast<int>(splits),                                                                        \
-                workspace, scale)
+                static_cast<int>(splits), workspace, scale, static_cast<const int32_t *>(nullptr), int64_t(0), 0, 0)
     if (D == 128) {
         switch (G) {
             case 1: T2C_ATT(4, 1); break;
@@ -1855,6 +1908,93 @@ extern "C" int t2c_advance_positions(int32_t *positions, int64_t B, int32_t *tok
     if (!positions || B <= 0) return set_error(T2C_EINVAL, "advance_positions: bad argument");
     return launch(advance_kernel, dim3(static_cast<unsigned>((B + 127) / 128)), dim3(128), 0, as_stream(stream),
                   positions, B, token_index);
+}
+
+static int page_log2_of(int64_t page_size) {
+    if (page_size <= 0 || page_size > (1 << 20) || (page_size & (page_size - 1))) return -1;
+    int l = 0;
+    while ((int64_t(1) << l) < page_size) ++l;
+    return l;
+}
+
+extern "C" int t2c_attn_decode_paged(const void *q, const void *k_pages, const void *v_pages, void *out,
+                                     const int32_t *positions, const int32_t *block_table, int64_t bt_stride,
+                                     int64_t num_pages, int64_t page_size, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                     int64_t B, int64_t NH, int64_t NK, int64_t D, int64_t splits, float *workspace,
+                                     int64_t workspace_floats, void *stream) {
+    if (!q || !k_pages || !v_pages || !out || !positions || !block_table)
+        return set_error(T2C_EINVAL, "attn_decode_paged: NULL pointer");
+    const int pl = page_log2_of(page_size);
+    if (pl < 0) return set_error(T2C_EINVAL, "attn_decode_paged: page_size %lld is not a power of two", (long long)page_size);
+    if (B <= 0 || NH <= 0 || NK <= 0 || NH % NK || bt_stride <= 0 || splits <= 0 || bt_stride * page_size > INT32_MAX ||
+        num_pages <= 0 || num_pages > INT32_MAX)
+        return set_error(T2C_EINVAL, "attn_decode_paged: bad shape");
+    const int G = static_cast<int>(NH / NK);
+    if (G > kMaxGroup || (G & (G - 1))) return set_error(T2C_EUNSUPPORTED, "attn_decode_paged: group %d", G);
+    if (D != 128 && D != 64) return set_error(T2C_EUNSUPPORTED, "attn_decode_paged: D=%lld", (long long)D);
+    if (splits > kMaxSplits)
+        return set_error(T2C_EUNSUPPORTED, "attn_decode_paged: splits %lld > %d", (long long)splits, kMaxSplits);
+    if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || page_stride % 8 || row_stride % 8 || head_stride % 8)
+        return set_error(T2C_EINVAL, "attn_decode_paged: page rows must be 16-byte aligned");
+    if (splits > 1) {
+        const int64_t need = B * NH * splits * (D + 2);
+        if (!workspace || workspace_floats < need)
+            return set_error(T2C_ESCRATCH, "attn_decode_paged: workspace needs %lld floats", (long long)need);
+    }
+    const int64_t max_len = bt_stride * page_size;
+    const int chunk = static_cast<int>((max_len + splits - 1) / splits);
+    const float scale = 1.0f / sqrtf(static_cast<float>(D));
+    const cudaStream_t s = as_stream(stream);
+    const dim3 grid(static_cast<unsigned>(B * NK * splits)), block(kAttnWarps * 32);
+    int rc = T2C_OK;
+#define T2C_ATTP(E, GG)                                                                                          \
+    rc = launch(attn_decode_kernel<E, GG, true>, grid, block, 0, s, static_cast<const __half *>(q),                \
+                static_cast<const __half *>(k_pages), static_cast<const __half *>(v_pages), static_cast<__half *>(out), \
+                positions, static_cast<int>(NH), static_cast<int>(NK), page_stride, row_stride, head_stride,         \
+                static_cast<int>(max_len), chunk, static_cast<int>(splits), workspace, scale, block_table, bt_stride, pl,     \
+                static_cast<int>(num_pages))
+    switch (G * 1000 + static_cast<int>(D)) {
+        case 1128: T2C_ATTP(4, 1); break;
+        case 2128: T2C_ATTP(4, 2); break;
+        case 4128: T2C_ATTP(4, 4); break;
+        case 8128: T2C_ATTP(4, 8); break;
+        case 1064: T2C_ATTP(2, 1); break;
+        case 2064: T2C_ATTP(2, 2); break;
+        case 4064: T2C_ATTP(2, 4); break;
+        default: T2C_ATTP(2, 8); break;
+    }
+#undef T2C_ATTP
+    if (rc != T2C_OK || splits == 1) return rc;
+    if (D == 128)
+        return launch(attn_combine_kernel<4>, dim3(static_cast<unsigned>(B * NH)), dim3(128), 0, s,
+                      static_cast<const float *>(workspace), static_cast<__half *>(out), static_cast<int>(B),
+                      static_cast<int>(NH), static_cast<int>(splits));
+    return launch(attn_combine_kernel<2>, dim3(static_cast<unsigned>(B * NH)), dim3(64), 0, s,
+                  static_cast<const float *>(workspace), static_cast<__half *>(out), static_cast<int>(B),
+                  static_cast<int>(NH), static_cast<int>(splits));
+}
+
+extern "C" int t2c_kv_cache_write_paged(void *pages, const void *src, int64_t src_b_stride, int64_t src_t_stride,
+                                        const int32_t *positions, const int32_t *block_table, int64_t bt_stride,
+                                        int64_t num_pages, int64_t page_size, int64_t page_stride, int64_t row_stride,
+                                        int64_t head_stride, int64_t B, int64_t T, int64_t NK, int64_t D, void *stream) {
+    if (!pages || !src || !positions || !block_table) return set_error(T2C_EINVAL, "kv_cache_write_paged: NULL pointer");
+    const int pl = page_log2_of(page_size);
+    if (pl < 0) return set_error(T2C_EINVAL, "kv_cache_write_paged: page_size %lld is not a power of two", (long long)page_size);
+    if (B <= 0 || T <= 0 || NK <= 0 || D <= 0 || D % 8 || bt_stride <= 0 || bt_stride * page_size > INT32_MAX ||
+        num_pages <= 0 || num_pages > INT32_MAX)
+        return set_error(T2C_EINVAL, "kv_cache_write_paged: bad shape");
+    if (!aligned(pages, 16) || !aligned(src, 16) || page_stride % 8 || row_stride % 8 || head_stride % 8 ||
+        src_b_stride % 8 || src_t_stride % 8)
+        return set_error(T2C_EINVAL, "kv_cache_write_paged: rows must be 16-byte aligned");
+    const int64_t total = B * T * NK * (D / 8);
+    const int64_t blocks_needed = (total + 255) / 256;
+    const int blocks = static_cast<int>(blocks_needed < 4096 ? blocks_needed : 4096);
+    return launch(kv_write_paged_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, as_stream(stream),
+                  static_cast<__half *>(pages), static_cast<const __half *>(src), src_b_stride, src_t_stride, positions,
+                  block_table, bt_stride, pl, page_stride, row_stride, head_stride, static_cast<int>(B),
+                  static_cast<int>(T), static_cast<int>(NK), static_cast<int>(D), static_cast<int>(bt_stride * page_size),
+                  static_cast<int>(num_pages));
 }
 
 // ------------------------------------------------ decode attention, no allocation

@@ -211,6 +211,44 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
     return out
 
 
+def attn_decode_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor, positions: torch.Tensor,
+                      block_table: torch.Tensor, *, batch: int, n_heads: int, n_kv: int, head_dim: int,
+                      splits: int = 1, workspace: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """attn_decode over a paged cache: pages [num_pages, page_size, n_kv, head_dim] fp16, block_table
+    [sequences, pages_per_seq] int32 (row b = sequence b's physical pages)."""
+    _check(q, torch.float16, "q")
+    _check(positions, torch.int32, "positions")
+    _check(block_table, torch.int32, "block_table")
+    if k_pages.shape != v_pages.shape or k_pages.dim() != 4 or k_pages.dtype != torch.float16:
+        raise ValueError("k_pages / v_pages must be float16 [num_pages, page_size, n_kv, head_dim]")
+    out = torch.empty_like(q) if out is None else out
+    need = attn_decode_workspace_floats(batch, n_heads, head_dim, splits)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.float32, device=q.device)
+    ps, rs, hs, _ = k_pages.stride()
+    _lib.lib().call("t2c_attn_decode_paged", _lib.ptr(q), _lib.ptr(k_pages), _lib.ptr(v_pages), _lib.ptr(out),
+                    _lib.ptr(positions), _lib.ptr(block_table), block_table.stride(0), k_pages.shape[0],
+                    k_pages.shape[1], ps, rs, hs, batch, n_heads, n_kv, head_dim, splits, _lib.ptr(workspace),
+                    workspace.numel() if workspace is not None else 0, _lib.stream_ptr())
+    return out
+
+
+def kv_cache_write_paged(pages: torch.Tensor, src: torch.Tensor, positions: torch.Tensor, block_table: torch.Tensor,
+                         *, batch: int, tokens: int, n_kv: int, head_dim: int) -> None:
+    """Writes src [batch, tokens, n_kv * head_dim] (row views fine) at positions[b] .. + tokens - 1 of each
+    sequence's pages."""
+    _check(positions, torch.int32, "positions")
+    _check(block_table, torch.int32, "block_table")
+    if src.dtype != torch.float16 or src.stride(-1) != 1:
+        raise ValueError("src must be float16 with unit last stride")
+    s3 = src.view(batch, tokens, -1) if src.dim() != 3 else src
+    ps, rs, hs, _ = pages.stride()
+    _lib.lib().call("t2c_kv_cache_write_paged", _lib.ptr(pages), _lib.ptr(s3), s3.stride(0), s3.stride(1),
+                    _lib.ptr(positions), _lib.ptr(block_table), block_table.stride(0), pages.shape[0], pages.shape[1],
+                    ps, rs, hs, batch, tokens, n_kv, head_dim, _lib.stream_ptr())
+
+
 def attn_decode_fused_workspace(batch: int, n_heads: int, n_kv: int, head_dim: int, splits: int,
                                 device: torch.device | str = "cuda") -> torch.Tensor | None:
     """Zeroed workspace (split partials + arrival counters) for attn_decode_fused, or None for one split."""

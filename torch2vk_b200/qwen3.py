@@ -28,6 +28,7 @@ from dataclasses import dataclass, field
 import torch
 
 from torch2vk_b200 import kernels
+from torch2vk_b200.paged_kv import PagedKVCache
 
 Q6_NAMES = ("v_proj", "down_proj")
 
@@ -123,15 +124,32 @@ class Qwen3Runner:
     eos_ids: tuple[int, ...] = ()
     decode_splits: int = 0
     fused_attention: bool = True
+    page_size: int = 0
+    kv_pages: int = 0
     k_cache: list[torch.Tensor] = field(init=False)
     v_cache: list[torch.Tensor] = field(init=False)
 
     def __post_init__(self) -> None:
+        """page_size > 0 keeps the KV cache in a paged pool (PagedKVCache) of kv_pages pages (default: enough
+        for every sequence at max_seq) instead of one contiguous [batch, max_seq] cache per layer."""
         cfg, dev = self.cfg, self.weights.final_norm.device
         self.device = dev
-        shape = (self.batch, self.max_seq, cfg.kv_heads, cfg.head_dim)
-        self.k_cache = [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(cfg.layers)]
-        self.v_cache = [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(cfg.layers)]
+        self.paged: PagedKVCache | None = None
+        if self.page_size > 0:
+            per_seq = -(-self.max_seq // self.page_size)
+            self.paged = PagedKVCache(layers=cfg.layers, num_pages=self.kv_pages or self.batch * per_seq,
+                                      page_size=self.page_size, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                                      max_seqs=self.batch, max_pages_per_seq=per_seq, device=dev)
+            self.k_cache, self.v_cache = self.paged.k, self.paged.v
+            # the decode step's new K/V rows, written here by the RoPE kernel (position stride 0) and then
+            # copied into their pages
+            stage = (self.batch, cfg.kv_heads * cfg.head_dim)
+            self.k_stage = torch.zeros(stage, dtype=torch.float16, device=dev)
+            self.v_stage = torch.zeros(stage, dtype=torch.float16, device=dev)
+        else:
+            shape = (self.batch, self.max_seq, cfg.kv_heads, cfg.head_dim)
+            self.k_cache = [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(cfg.layers)]
+            self.v_cache = [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(cfg.layers)]
         self.inv_freq = inv_freq(cfg).to(dev)
         self.positions = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self.token_index = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -142,7 +160,10 @@ class Qwen3Runner:
         self.stopped = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self.eos = torch.tensor(list(self.eos_ids) or [-1], dtype=torch.int64, device=dev)
         if self.decode_splits <= 0:
-            if self.fused_attention and self.max_seq <= 16384:
+            if self.paged is not None:
+                want = max(1, 592 // max(1, self.batch * cfg.kv_heads))
+                self.decode_splits = max(1, min(32, want, self.max_seq // 64))
+            elif self.fused_attention and self.max_seq <= 16384:
                 # one cluster of up to 8 CTAs per (sequence, KV head), about two CTAs per SM
                 want = max(1, 296 // max(1, self.batch * cfg.kv_heads))
                 self.decode_splits = max(1, min(8, want, self.max_seq // 64))
@@ -192,6 +213,9 @@ class Qwen3Runner:
     def _attention(self, i: int, b: _Buffers, tokens_per_seq: int, decode: bool) -> None:
         """q/k norm + RoPE, KV-cache write and attention of layer i: b.q/b.k/b.v -> b.attn."""
         cfg, lw = self.cfg, self.weights.layers[i]
+        if self.paged is not None:
+            self._attention_paged(i, b, tokens_per_seq, decode)
+            return
         if decode and self.fused_attention:
             kernels.attn_decode_fused(b.q, b.k, b.v, lw.q_norm, lw.k_norm, self.inv_freq, self.k_cache[i],
                                       self.v_cache[i], self.positions, batch=self.batch, n_heads=cfg.heads,
@@ -210,6 +234,44 @@ class Qwen3Runner:
             kernels.attn_prefill(b.qr, self.k_cache[i], self.v_cache[i], self.positions, batch=self.batch,
                                  tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=cfg.kv_heads, head_dim=cfg.head_dim,
                                  out=b.attn)
+
+    def _attention_paged(self, i: int, b: _Buffers, tokens_per_seq: int, decode: bool) -> None:
+        """_attention over the paged pool.  Decode: RoPE into the staging rows, paged write, paged split-K
+        attention.  Prefill (positions start at 0): RoPE into a contiguous prompt cache, causal attention
+        over it, then the prompt's rows are copied into their pages."""
+        cfg, lw, pool = self.cfg, self.weights.layers[i], self.paged
+        nk, d, bt = cfg.kv_heads, cfg.head_dim, pool.block_table
+        if decode:
+            ks = self.k_stage.as_strided((self.batch, self.max_seq, nk, d), (nk * d, 0, d, 1))
+            vs = self.v_stage.as_strided((self.batch, self.max_seq, nk, d), (nk * d, 0, d, 1))
+        else:
+            ks = torch.empty(self.batch, tokens_per_seq, nk, d, dtype=torch.float16, device=self.device)
+            vs = torch.empty_like(ks)
+        kernels.qk_norm_rope_cache(b.q, b.k, b.v, lw.q_norm, lw.k_norm, ks, vs, self.positions, self.inv_freq,
+                                   batch=self.batch, tokens=tokens_per_seq, n_heads=cfg.heads, n_kv=nk, head_dim=d,
+                                   eps=cfg.eps, q_out=b.qr)
+        src_k = self.k_stage if decode else ks.view(self.batch, tokens_per_seq, nk * d)
+        src_v = self.v_stage if decode else vs.view(self.batch, tokens_per_seq, nk * d)
+        for pages, src in ((pool.k[i], src_k), (pool.v[i], src_v)):
+            kernels.kv_cache_write_paged(pages, src, self.positions, bt, batch=self.batch, tokens=tokens_per_seq,
+                                         n_kv=nk, head_dim=d)
+        if decode:
+            kernels.attn_decode_paged(b.qr, pool.k[i], pool.v[i], self.positions, bt, batch=self.batch,
+                                      n_heads=cfg.heads, n_kv=nk, head_dim=d, splits=self.decode_splits,
+                                      workspace=self.attn_workspace, out=b.attn)
+        else:
+            kernels.attn_prefill(b.qr, ks, vs, self.positions, batch=self.batch, tokens=tokens_per_seq,
+                                 n_heads=cfg.heads, n_kv=nk, head_dim=d, out=b.attn)
+
+    def _reserve_pages(self, positions: int) -> None:
+        """Every sequence gets pages for `positions` positions, handed out round-robin (sequence b's pages
+        are then not adjacent in the pool); pages held from an earlier prompt are returned first."""
+        pool = self.paged
+        for s in range(self.batch):
+            pool.release(s)
+        for end in range(pool.page_size, positions + pool.page_size, pool.page_size):
+            for s in range(self.batch):
+                pool.reserve(s, min(end, positions))
 
     def _embed(self, ids: torch.Tensor, out: torch.Tensor) -> None:
         cfg = self.cfg
@@ -237,6 +299,8 @@ class Qwen3Runner:
         tokens = ids.shape[1]
         if tokens > self.max_seq:
             raise ValueError(f"prompt of {tokens} tokens exceeds max_seq {self.max_seq}")
+        if self.paged is not None:
+            self._reserve_pages(min(self.max_seq, tokens + self.max_new_tokens))
         self.positions.zero_()
         self.token_index.zero_()
         self.generated_length.zero_()
