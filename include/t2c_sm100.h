@@ -448,6 +448,23 @@ int t2c_slice_last_f32_to_f16(const float *x, void *out, int64_t B, int64_t S, i
  *   src/models/optimized_qwen3/shaders/token_major_value_cache_write_f32_to_f16_pair.py */
 int t2c_value_cache_write_f32(const float *src, const int64_t *positions, int ncaches, void *const *caches,
                               const int64_t *cache_lens, int64_t B, int64_t T, int64_t H, int64_t D, void *stream);
+/* Bidirectional GQA attention under an additive fp16 mask (OmniVoice's LLM):
+ * out[b,t,h,:] = softmax(q[b,t,h,:] . k[b,s,h/(NH/NK),:] * scale + mask[b,t,s]) v[b,s,h/(NH/NK),:]
+ * over all S keys; q / out fp16 token-major [B, T, NH, D], k / v fp16 [B, S, NK, D], mask element
+ * (b, t, s) at b * mask_b_stride + t * mask_row_stride + s (values <= -FLT_MAX/2, -inf included,
+ * mask the key).  D = 128, on the tensor cores.  Replaces ExportSdpaProgram
+ *   src/models/quantized_omnivoice/shaders/sdpa_masked_f32.py */
+int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B,
+                        int64_t T, int64_t S, int64_t NH, int64_t NK, int64_t D, int64_t mask_b_stride,
+                        int64_t mask_row_stride, float scale, void *stream);
+/* OmniVoice input embedding: out fp16 [B, S, H]; where audio_mask[b, s] != 0 the fp32 sum over the C
+ * codebooks of Q8_0 audio rows c * audio_vocab + ids[b, c, s], else Q8_0 text row ids[b, 0, s]
+ * (ids int64 [B, C, S], audio_mask uint32 [B, S]).  An id outside its table reads row 0 and sets
+ * T2C_EINVAL.  Replaces OmniVoiceInputEmbedQ8_0Program
+ *   src/models/quantized_omnivoice/custom_shaders.py:17-181 */
+int t2c_omnivoice_input_embed(const void *text_weight, const void *audio_weight, const int64_t *ids,
+                              const uint32_t *audio_mask, void *out, int64_t B, int64_t C, int64_t S, int64_t H,
+                              int64_t text_vocab, int64_t audio_vocab, void *stream);
 /* Flash-attention mask classifier: out [row_blocks, words] uint32, 2 bits per
  * (16-row, 64-column) block of the fp16 mask [T, S]: 1 = every value <= -FLT_MAX/2
  * (or outside the mask), 2 = every value 0.  Replaces OptimizedQwen3FaMaskOptF16Program

@@ -206,7 +206,7 @@ def test_lm_head_argmax_and_select(oracle, kind, K, N):
 
 
 @pytest.mark.parametrize("kind,K,N,M", [("q6_k", 4096, 4099, 8), ("q6_k", 4096, 8192, 32), ("q4_k", 4096, 4099, 20),
-                                        ("q6_k", 2048, 1000, 5)])
+                                        ("q6_k", 2048, 1000, 5), ("q6_k", 1024, 8192, 9), ("q6_k", 2560, 1000, 40)])
 def test_lm_head_argmax_tensor_core(oracle, kind, K, N, M):
     """M > 4: the LM head runs on the tcgen05 GEMM (fp16 operands) with the argmax epilogue.
 

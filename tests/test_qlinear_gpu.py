@@ -81,10 +81,10 @@ def test_linear_parity(oracle, kind, m, nk):
     x = rng.standard_normal((m, k)).astype(np.float16)
     ref = oracle.matvec(packed, kind, x)
     y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), kind, k)
-    # Q4_K, and Q6_K with K a multiple of 2048, run on the tensor-core GEMM for M > 4, whose operands are
-    # fp16 (dequantized weights rounded to fp16, relative 2^-11 each; Q8_0 as well): its bound against the exact
-    # double-precision matvec is 4e-3.
-    tensor_core = m > 4 and (kind in ("q4_k", "q8_0") or (kind == "q6_k" and k % 2048 == 0))
+    # Q4_K, Q8_0, and Q6_K with K a multiple of 2048 or N a multiple of 8, run on the tensor-core GEMM for M > 4,
+    # whose operands are fp16 (dequantized weights rounded to fp16, relative 2^-11 each): its bound against the
+    # exact double-precision matvec is 4e-3.
+    tensor_core = m > 4 and (kind in ("q4_k", "q8_0") or (kind == "q6_k" and (k % 2048 == 0 or n % 8 == 0)))
     _tol_check(y.float().cpu().numpy(), ref, rel=4e-3 if tensor_core else 2e-3)
 
 
@@ -204,6 +204,28 @@ def test_q4k_gemm_tensor_cores(oracle, m, n, k):
     _tol_check(y.float().cpu().numpy(), ref, rel=3e-3)
 
 
+@pytest.mark.parametrize("m,n,k", [(5, 1024, 3072), (64, 200, 1024), (300, 136, 256), (17, 3072, 1280),
+                                   (129, 1024, 3072), (40, 1030, 3072)])
+def test_q6k_gemm_any_k(oracle, m, n, k):
+    """Q6_K on the tcgen05 GEMM for every K % 256 == 0: K % 2048 != 0 rows (not 16-byte multiples) arrive
+    through eight-row group maps.  N % 8 != 0 with such K stays on the fp16-x matvec passes."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m * 5 + n + k)
+    packed = oracle.quantize(_weights(rng, n, k), "q6_k")
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    if n % 8 == 0:
+        w = oracle.dequantize(packed, "q6_k", k).astype(np.float16).astype(np.float64)  # fp16 operands
+        ref = x.astype(np.float64) @ w.T + res
+    else:
+        ref = oracle.matvec(packed, "q6_k", x).astype(np.float64) + res
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q6_k", k,
+                       residual=torch.from_numpy(res).cuda())
+    _tol_check(y.float().cpu().numpy(), ref, rel=3e-3)
+    assert kernels.device_status() == 0
+
+
 @pytest.mark.parametrize("m", [7, 130])
 def test_q4k_gemm_swiglu_and_norm(oracle, m):
     from torch2vk_b200 import kernels
@@ -306,3 +328,18 @@ def test_linear_q8_0_tensor_core(oracle, m, nk, res):
                        residual=torch.from_numpy(r).cuda() if res else None)
     _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
     assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 9])
+def test_matvec_is_deterministic(oracle, m):
+    """Split-K partial sums meet in a fixed order: repeated launches give identical bits (the decode step,
+    and so the greedy tokens, do not depend on warp scheduling)."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m)
+    n, k = 4096, 12288
+    packed = torch.from_numpy(oracle.quantize(_weights(rng, n, k), "q4_k")).cuda()
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float16)).cuda()
+    first = kernels.linear(x, packed, "q4_k", k)
+    for _ in range(20):
+        assert torch.equal(kernels.linear(x, packed, "q4_k", k), first)

@@ -344,6 +344,50 @@ __global__ void embedding_q8_0_kernel(const uint8_t *__restrict__ w, const int64
     }
 }
 
+// OmniVoice input embedding (omnivoice_input_embed_q8_0_f32, quantized_omnivoice/custom_shaders.py:17-181):
+// out[b, s, :] = fp16(sum over codebooks c of audio row c * V + ids[b, c, s]) where audio_mask[b, s]
+// is set (fp32 sum in codebook order), else fp16(text row ids[b, 0, s]).  Each value d * q of a
+// Q8_0 block is exact in fp32.  An id outside its table reads row 0 and reports T2C_EINVAL.
+__global__ void omnivoice_input_embed_kernel(const uint8_t *__restrict__ tw, const uint8_t *__restrict__ aw,
+                                             const int64_t *__restrict__ ids, const uint32_t *__restrict__ amask,
+                                             __half *__restrict__ out, int B, int C, int S, int H, int64_t TV,
+                                             int64_t V) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t row_bytes = H / 32 * 34;
+    auto q8 = [&](const uint8_t *w, int64_t row, int h) {
+        const uint8_t *blk = w + row * row_bytes + (h >> 5) * 34;
+        const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+        return d * static_cast<float>(static_cast<int8_t>(blk[2 + (h & 31)]));
+    };
+    const int64_t total = static_cast<int64_t>(B) * S * H;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int h = static_cast<int>(i % H);
+        const int64_t bs = i / H;
+        const int s = static_cast<int>(bs % S), b = static_cast<int>(bs / S);
+        if (amask[bs] != 0u) {
+            float value = 0.0f;
+            for (int c = 0; c < C; ++c) {
+                int64_t tok = ids[(static_cast<int64_t>(b) * C + c) * S + s];
+                if (tok < 0 || tok >= V) {
+                    if (h == 0) report_device_error(T2C_EINVAL);
+                    tok = 0;
+                }
+                value += q8(aw, c * V + tok, h);
+            }
+            out[i] = __float2half_rn(value);
+        } else {
+            int64_t tok = ids[static_cast<int64_t>(b) * C * S + s];
+            if (tok < 0 || tok >= TV) {
+                if (h == 0) report_device_error(T2C_EINVAL);
+                tok = 0;
+            }
+            out[i] = __float2half_rn(q8(tw, tok, h));
+        }
+    }
+}
+
 // ---------------------------------------------------- masked attention
 // out[b, h, t, :] = softmax(q k^T * scale + mask[t, s]) v over all S keys
 // (non-causal; the additive fp16 mask carries the encoder's block-diagonal
@@ -643,6 +687,22 @@ extern "C" int t2c_embedding_q8_0(const void *weight, const int64_t *ids, void *
     if (grid > 148 * 32) grid = 148 * 32;
     return launch_asr(embedding_q8_0_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
                       static_cast<const uint8_t *>(weight), ids, static_cast<__half *>(out), n_ids, vocab, H);
+}
+
+extern "C" int t2c_omnivoice_input_embed(const void *text_weight, const void *audio_weight, const int64_t *ids,
+                                         const uint32_t *audio_mask, void *out, int64_t B, int64_t C, int64_t S,
+                                         int64_t H, int64_t text_vocab, int64_t audio_vocab, void *stream) {
+    if (!text_weight || !audio_weight || !ids || !audio_mask || !out)
+        return set_error(T2C_EINVAL, "omnivoice_input_embed: NULL pointer");
+    if (B <= 0 || C <= 0 || S <= 0 || H <= 0 || H % 32 || text_vocab <= 0 || audio_vocab <= 0 || B * S > INT32_MAX ||
+        C > 64)
+        return set_error(T2C_EINVAL, "omnivoice_input_embed: bad shape (H a multiple of 32)");
+    int64_t grid = (B * S * H + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    return launch_asr(omnivoice_input_embed_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), as_stream(stream),
+                      static_cast<const uint8_t *>(text_weight), static_cast<const uint8_t *>(audio_weight), ids,
+                      audio_mask, static_cast<__half *>(out), static_cast<int>(B), static_cast<int>(C),
+                      static_cast<int>(S), static_cast<int>(H), text_vocab, audio_vocab);
 }
 
 extern "C" int t2c_attn_masked(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B,

@@ -1149,16 +1149,18 @@ constexpr int kPtRow = 136;  // halves per shared-memory row (272 B)
 constexpr int kPtStageBytes = 2 * kPtK * kPtRow * 2;
 constexpr int kPtSmem = kPtQ * kPtRow * 2 + kPtStages * kPtStageBytes;
 
-// EXT = the llama.cpp-style program (llama_flash_attn_f32_f16_f16): fp32 q and output, keys
-// [0, S) of the cache with an explicit additive fp16 mask [T, S] instead of the causal rule, and
-// the mask classifier's 2-bit codes per (16-row block, 64-key tile): 1 = all masked (the warp
-// skips the tile), 2 = all zero (no mask values read).
-template <bool EXT>
+// EXT = the llama.cpp-style program (llama_flash_attn_f32_f16_f16): keys [0, S) of the cache with
+// an explicit additive fp16 mask [T, S] (sequence b's at mask + b * m_sb) instead of the causal
+// rule, and the mask classifier's 2-bit codes per (16-row block, 64-key tile): 1 = all masked (the
+// warp skips the tile), 2 = all zero (no mask values read).  F32IO: fp32 q and output (that
+// program's), else fp16.
+template <bool EXT, bool F32IO = EXT>
 __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
     const void *__restrict__ qv, const __half *__restrict__ kc, const __half *__restrict__ vc,
     void *__restrict__ outv, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
     int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh, float scale_log2,
-    const __half *__restrict__ mask, int64_t m_st, const uint32_t *__restrict__ mopt, int64_t mo_st, int S) {
+    const __half *__restrict__ mask, int64_t m_st, const uint32_t *__restrict__ mopt, int64_t mo_st, int S,
+    int64_t m_sb) {
     extern __shared__ __align__(128) uint8_t pt_smem[];
     __shared__ int s_nkt;
     __half *qs = reinterpret_cast<__half *>(pt_smem);
@@ -1219,7 +1221,7 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (tq < T) {
             const int64_t off = b * q_sb + tq * q_st + h * q_sh + c * 8;
-            if (EXT) {
+            if (F32IO) {
                 const float4 a = *reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + off);
                 const float4 c4 = *reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + off + 4);
                 const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
@@ -1281,7 +1283,7 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
                             v = -FLT_MAX;
                         } else if (code != 2u) {
                             const int tq = min(r ? tq1 : tq0, T - 1);
-                            const float mv = __half2float(mask[tq * m_st + key]);
+                            const float mv = __half2float(mask[b * m_sb + tq * m_st + key]);
                             v = mv <= -1.7014117e38f ? -FLT_MAX : fmaf(mv, 1.4426950408889634f, v);
                         }
                     } else if (masked && key > (r ? qp1 : qp0)) {
@@ -1357,7 +1359,7 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(
     for (int n = 0; n < 16; ++n) {
         const int d = 8 * n + 2 * t4;
         const int64_t o0 = b * o_sb + tq0 * o_st + h * o_sh + d, o1 = b * o_sb + tq1 * o_st + h * o_sh + d;
-        if (EXT) {
+        if (F32IO) {
             float *out = static_cast<float *>(outv);
             if (tq0 < T) *reinterpret_cast<float2 *>(out + o0) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
             if (tq1 < T) *reinterpret_cast<float2 *>(out + o1) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
@@ -1786,7 +1788,7 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
                       static_cast<const __half *>(v_cache), out, positions, static_cast<int>(T),
                       static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh,
                       1.4426950408889634f * scale, static_cast<const __half *>(nullptr), int64_t{0},
-                      static_cast<const uint32_t *>(nullptr), int64_t{0}, 0);
+                      static_cast<const uint32_t *>(nullptr), int64_t{0}, 0, int64_t{0});
     }
     const int64_t qtiles = (T + kPfQ - 1) / kPfQ;
     const dim3 grid(static_cast<unsigned>(B * NH * qtiles)), block(128);
@@ -1833,7 +1835,34 @@ extern "C" int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, 
                   static_cast<const int32_t *>(nullptr), static_cast<int>(T), static_cast<int>(NH),
                   static_cast<int>(NK), S * NK * D, NK * D, D, T * NH * D, NH * D, D, T * NH * D, NH * D, D,
                   1.4426950408889634f * scale, static_cast<const __half *>(mask), mask_row_stride, mask_opt,
-                  mask_opt_row_stride, static_cast<int>(S));
+                  mask_opt_row_stride, static_cast<int>(S), int64_t(0));
+}
+
+extern "C" int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, const void *mask, void *out,
+                                   int64_t B, int64_t T, int64_t S, int64_t NH, int64_t NK, int64_t D,
+                                   int64_t mask_b_stride, int64_t mask_row_stride, float scale, void *stream) {
+    if (!q || !k || !v || !mask || !out) return set_error(T2C_EINVAL, "attn_masked_gqa: NULL pointer");
+    if (B <= 0 || T <= 0 || S <= 0 || NH <= 0 || NK <= 0 || NH % NK || T > INT32_MAX || S > INT32_MAX ||
+        mask_row_stride < S || mask_b_stride < 0)
+        return set_error(T2C_EINVAL, "attn_masked_gqa: bad shape");
+    if (D != 128) return set_error(T2C_EUNSUPPORTED, "attn_masked_gqa: D=%lld (128 only)", (long long)D);
+    if (!aligned(q, 16) || !aligned(out, 4) || !aligned(k, 16) || !aligned(v, 16))
+        return set_error(T2C_EINVAL, "attn_masked_gqa: alignment");
+    static bool configured[64] = {};
+    const int dev_slot = current_device_slot();
+    if (!configured[dev_slot]) {
+        if (cudaFuncSetAttribute(attn_prefill_tc_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kPtSmem) != cudaSuccess)
+            return set_error(T2C_ECUDA, "attn_masked_gqa: cudaFuncSetAttribute failed");
+        configured[dev_slot] = true;
+    }
+    const int64_t tiles = (T + kPtQ - 1) / kPtQ;
+    return launch(attn_prefill_tc_kernel<true, false>, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128),
+                  kPtSmem, as_stream(stream), q, static_cast<const __half *>(k), static_cast<const __half *>(v), out,
+                  static_cast<const int32_t *>(nullptr), static_cast<int>(T), static_cast<int>(NH),
+                  static_cast<int>(NK), S * NK * D, NK * D, D, T * NH * D, NH * D, D, T * NH * D, NH * D, D,
+                  1.4426950408889634f * scale, static_cast<const __half *>(mask), mask_row_stride,
+                  static_cast<const uint32_t *>(nullptr), int64_t{0}, static_cast<int>(S), mask_b_stride);
 }
 
 extern "C" int t2c_embedding(int wtype, const void *weight, const int64_t *ids, void *out, int64_t n_ids,

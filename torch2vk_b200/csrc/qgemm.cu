@@ -48,11 +48,19 @@ struct RawFmt<T2C_Q4_K> {
     __device__ static int x_of(int b) { return b * 36; }
     __device__ static int off_of(int) { return 0; }
 };
+// When K % 2048 != 0 a Q6_K row is not a multiple of 16 bytes, so no 2-D map
+// can step from row to row; eight rows always are (8 x 210 x K / 256 bytes).
+// Grouped mode then maps the weight as [N / 8 groups, 8 rows' bytes] and a
+// stage is eight boxes of 16 groups x 224 bytes, box j holding row j of every
+// group: weight row r = 8 g + j lands in stage slot 16 j + g, at offset
+// (j x row_bytes + 210 b) % 16 within its 224-byte window.
 template <>
 struct RawFmt<T2C_Q6_K> {
     static constexpr int kRow = 224, kBox = 56;
     __device__ static int x_of(int b) { return ((210 * b) >> 4) * 4; }
     __device__ static int off_of(int b) { return (210 * b) & 15; }
+    __device__ static int gx_of(int b, int j, int row_bytes) { return ((j * row_bytes + 210 * b) >> 4) * 4; }
+    __device__ static int goff_of(int b, int j, int row_bytes) { return (j * row_bytes + 210 * b) & 15; }
 };
 // Q8_0: 34-byte blocks of 32 values; eight of them (272 bytes, a multiple of 16) make the
 // 256-value group of a raw stage, so the TMA window starts on a 16-byte boundary.
@@ -87,6 +95,8 @@ struct GemmParams {
     int64_t G;
     const float *bias;  // plain single-weight mode: fp32 [N] added before the activation
     int act;            // 1: erf GELU
+    int q6_grouped;     // Q6_K rows of K % 2048 != 0: eight-row group maps (RawFmt<T2C_Q6_K>)
+    int row_bytes;
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -325,6 +335,20 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
     __shared__ int failed_s;
     volatile int &failed = failed_s;
     const uint32_t raw_bytes = swiglu ? 2u * kRawBytes : static_cast<uint32_t>(kRawBytes);
+    // raw weight stage s <- super-block sb (absolute); the caller has armed raw_full[s]
+    auto load_raw = [&](int s, int sb) {
+        if constexpr (FMT == T2C_Q6_K) {
+            if (p.q6_grouped) {
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j)
+                    tma_load_2d(raw_ptr + s * kRawBytes + j * 16 * RF::kRow, wmap, RF::gx_of(sb, j, p.row_bytes),
+                                static_cast<int>(n0 >> 3), &raw_full[s]);
+                return;
+            }
+        }
+        tma_load_2d(raw_ptr + s * kRawBytes, wmap, RF::x_of(sb), static_cast<int>(n0), &raw_full[s]);
+        if (swiglu) tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, sb * 36, static_cast<int>(n0), &raw_full[s]);
+    };
 
     if (tid == kProducer * 32) {
         failed = 0;
@@ -341,9 +365,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
         // static weights: first two super-blocks before the dependency on the previous kernel
         for (int s = 0; s < 2 && s < nsb; ++s) {
             mbar_arrive_expect_tx(&raw_full[s], raw_bytes);
-            tma_load_2d(raw_ptr + s * kRawBytes, wmap, RF::x_of(sb0 + s), static_cast<int>(n0), &raw_full[s]);
-            if (swiglu)
-                tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, (sb0 + s) * 36, static_cast<int>(n0), &raw_full[s]);
+            load_raw(s, sb0 + s);
         }
     }
     if (warp == 0) {
@@ -386,11 +408,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                             break;
                         }
                         mbar_arrive_expect_tx(&raw_full[sb & 1], raw_bytes);
-                        tma_load_2d(raw_ptr + (sb & 1) * kRawBytes, wmap, RF::x_of(sb0 + sb + 2), static_cast<int>(n0),
-                                    &raw_full[sb & 1]);
-                        if (swiglu)
-                            tma_load_2d(rawup_ptr + (sb & 1) * kRawBytes, &p.umap, (sb0 + sb + 2) * 36,
-                                        static_cast<int>(n0), &raw_full[sb & 1]);
+                        load_raw(sb & 1, sb0 + sb + 2);
                     }
                 }
             }
@@ -434,11 +452,13 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                 failed = 1;
                 break;
             }
-            if (FMT == T2C_Q8_0) {
+            if constexpr (FMT == T2C_Q8_0) {
                 dequant_q8_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + r * RF::kRow), q, hf,
                                 a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
-            } else if (FMT == T2C_Q6_K) {
-                dequant_q6k_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + r * RF::kRow) + RF::off_of(sb0 + sb), q, hf,
+            } else if constexpr (FMT == T2C_Q6_K) {
+                const int slot = p.q6_grouped ? (r & 7) * 16 + (r >> 3) : r;
+                const int off = p.q6_grouped ? RF::goff_of(sb0 + sb, r & 7, p.row_bytes) : RF::off_of(sb0 + sb);
+                dequant_q6k_half(smem_u32(raw_ptr + (sb & 1) * kRawBytes + slot * RF::kRow) + off, q, hf,
                                  a_base + static_cast<uint32_t>(b * kABytes + r * 128), r);
             } else {
             dequant_half(raw_ptr + (sb & 1) * kRawBytes + r * 144, q, hf,
@@ -608,12 +628,14 @@ PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
     return encode;
 }
 
-bool encode_raw(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes, int box_words) {
+// rows_per_box kRowsT: one TMA row per weight row; 16: rows are eight-row groups (grouped Q6_K)
+bool encode_raw(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes, int box_words,
+                int rows_per_box = kRowsT) {
     const auto enc = tensor_map_encoder();
     if (!enc || row_bytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(n)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_words), kRowsT};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_words), static_cast<cuuint32_t>(rows_per_box)};
     const cuuint32_t es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -653,9 +675,16 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     const int box = a.fmt == T2C_Q6_K ? 56 : a.fmt == T2C_Q8_0 ? 68 : 36;
     const size_t raw_bytes = static_cast<size_t>(kRowsT) * (a.fmt == T2C_Q6_K ? 224 : a.fmt == T2C_Q8_0 ? 272 : 144);
     p.nw = a.nw;
+    p.q6_grouped = a.fmt == T2C_Q6_K && row_bytes % 16 != 0;
+    p.row_bytes = static_cast<int>(row_bytes);
+    if (p.q6_grouped)
+        for (int i = 0; i < a.nw; ++i)
+            if (a.N[i] % 8) return T2C_EUNSUPPORTED;
     int64_t row_tiles = 0;
     for (int i = 0; i < a.nw; ++i) {
-        if (!encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes, box)) return T2C_EUNSUPPORTED;
+        const bool ok = p.q6_grouped ? encode_raw(&p.wmap[i], a.w[i], a.N[i] / 8, 8 * row_bytes, box, kRowsT / 8)
+                                     : encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes, box);
+        if (!ok) return T2C_EUNSUPPORTED;
         p.tile0[i] = static_cast<int>(row_tiles);
         row_tiles += (a.N[i] + kRowsT - 1) / kRowsT;
         p.Nw[i] = a.N[i];

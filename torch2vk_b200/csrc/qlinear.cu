@@ -23,7 +23,7 @@
 //    16-row tiles, the sparse-column mapping of the M = 1 kernel.
 //  * qmv_tma_kernel / qmv_direct_kernel: dp4a on 15-bit fixed-point x planes;
 //    kept only for M > 4 shapes the tensor-core GEMM does not take (Q6_K with
-//    K % 2048 != 0, Q8_0 with K % 256 != 0).
+//    K % 2048 != 0 and N % 8 != 0, Q8_0 with K % 256 != 0).
 //  * Epilogues: + residual (matvec_add), silu(gate) * up (SwiGLU pair),
 //    per-4-row argmax partials (LM head), fp16 store.
 #include <cuda.h>
@@ -1365,13 +1365,14 @@ __device__ __forceinline__ void mma_issue(const QParams &p, int warp, int64_t bl
     tma_load_2d(stage, &p.tmap[si], seg * (kMmaSegBytes / 4), row0, bar);
 }
 
-// Split-K partials of a row block meet in a shared-memory slot: each warp of the
-// block's group adds its rows, and the last to arrive applies the epilogue.
-// Slot (iteration % kMmaSlots, group) is reused once the previous use is done
+// Split-K partials of a row block meet in shared memory: each warp of the
+// block's group stores its rows in its own slot, and the last to arrive adds
+// the group's slots in warp order and applies the epilogue.  The slots of
+// (iteration % kMmaSlots, group) are reused once the previous use is done
 // (generation counter); the wait for that is bounded.
 constexpr int kMmaSlots = 4;
 struct MmaSlot {
-    float v[2][kMmaRows][4];  // [gate/up or value][row][batch row]
+    float v[2][kMmaRows][4];  // one warp's partial sums: [gate/up or value][row][batch row]
     int arrived;
     int gen;
 };
@@ -1526,8 +1527,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
             mma_finish_block<MT>(p, block, acc, lane);
             continue;
         }
-        MmaSlot *slot = slots + (it % kMmaSlots) * kMmaWarps + group;
-        if (!slot_wait_gen(&slot->gen, static_cast<int>(it / kMmaSlots))) {
+        // each warp parks its partial sums in its own slot; the group's last warp adds them in warp
+        // order (a fixed summation order: results do not depend on which warp finishes first).  The
+        // group's first slot carries the arrival count and the generation.
+        MmaSlot *const base = slots + (it % kMmaSlots) * kMmaWarps + group * p.wpb;
+        MmaSlot *const mine = slots + (it % kMmaSlots) * kMmaWarps + warp;
+        if (!slot_wait_gen(&base->gen, static_cast<int>(it / kMmaSlots))) {
             report_device_error(T2C_ETIMEOUT);
             failed = true;
             continue;
@@ -1535,40 +1540,34 @@ __global__ void __launch_bounds__(kMmaThreads, 1) qmv_mma_kernel(const __grid_co
         if (t < p.M) {  // lane (g, t) holds rows g, g+8 of batch row t
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                atomicAdd(&slot->v[r][g][t], acc[r][0]);
-                atomicAdd(&slot->v[r][g + 8][t], acc[r][1]);
+                mine->v[r][g][t] = acc[r][0];
+                mine->v[r][g + 8][t] = acc[r][1];
             }
         }
         __syncwarp();
         int last = 0;
         if (lane == 0) {
             __threadfence_block();
-            last = atomicAdd(&slot->arrived, 1) == p.wpb - 1;
+            last = atomicAdd(&base->arrived, 1) == p.wpb - 1;
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence_block();
-        float v[2][2];
+        float v[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         const int tm = t < p.M ? t : 0;
+        for (int w = 0; w < p.wpb; ++w) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            v[r][0] = *reinterpret_cast<volatile float *>(&slot->v[r][g][tm]);
-            v[r][1] = *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][tm]);
+            for (int r = 0; r < 2; ++r) {
+                v[r][0] += *reinterpret_cast<volatile float *>(&base[w].v[r][g][tm]);
+                v[r][1] += *reinterpret_cast<volatile float *>(&base[w].v[r][g + 8][tm]);
+            }
         }
         mma_finish_block<MT>(p, block, v, lane);
         __syncwarp();
-        if (t < p.M) {
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                slot->v[r][g][t] = 0.0f;
-                slot->v[r][g + 8][t] = 0.0f;
-            }
-        }
-        __syncwarp();
         if (lane == 0) {
-            slot->arrived = 0;
+            base->arrived = 0;
             __threadfence_block();
-            *reinterpret_cast<volatile int *>(&slot->gen) = slot->gen + 1;
+            *reinterpret_cast<volatile int *>(&base->gen) = base->gen + 1;
         }
     }
 }
@@ -2832,7 +2831,7 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
         // mixed formats (Q4_K_M: Q6_K v): one launch per weight, all or nothing
         for (int i = 0; i < p.nstreams; ++i) {
             const int fi = p.s[i].fmt;
-            const bool ok_fmt = fi == T2C_Q4_K || fi == T2C_Q8_0 || (fi == T2C_Q6_K && p.K % 2048 == 0);
+            const bool ok_fmt = fi == T2C_Q4_K || fi == T2C_Q8_0 || (fi == T2C_Q6_K && (p.K % 2048 == 0 || p.s[i].n % 8 == 0));
             if (!ok_fmt || reinterpret_cast<uintptr_t>(p.s[i].w) % 16) return T2C_OK;
         }
         for (int i = 0; i < p.nstreams; ++i) {
@@ -3069,7 +3068,7 @@ extern "C" int t2c_linear_f32(int wtype, const float *x, const void *w, float *y
     __half *y16 = reinterpret_cast<__half *>(static_cast<uint8_t *>(scratch) + (M * K * 2 + 255) / 256 * 256);
     if ((rc = t2c_cast(x, T2C_F32, x16, T2C_F16, M * K, stream))) return rc;
     const cudaStream_t s = as_stream(stream);
-    if (M > 4 && (wtype == T2C_Q4_K || wtype == T2C_Q8_0 || (wtype == T2C_Q6_K && K % 2048 == 0))) {
+    if (M > 4 && (wtype == T2C_Q4_K || wtype == T2C_Q8_0 || wtype == T2C_Q6_K)) {
         // tensor-core GEMM writing fp32 directly from the TMEM accumulators
         QGemmArgs a = {};
         a.fmt = wtype;

@@ -538,6 +538,27 @@ def attn_masked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.T
     return out
 
 
+def attn_masked_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor, *, batch: int,
+                    tokens: int, n_heads: int, n_kv: int, head_dim: int, scale: float | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Bidirectional GQA attention under an additive fp16 mask: q / out fp16 token-major [B, T, NH, D] (row
+    views fine), k / v fp16 [B, T, NK, D], mask [B, 1, T, T] (or [B, T, T]; unit key stride)."""
+    _check(q, torch.float16, "q")
+    _check(mask, torch.float16, "mask")
+    for t, n in ((k, "k"), (v, "v")):
+        _check(t, torch.float16, n)
+        if not t.is_contiguous():
+            raise ValueError(f"{n} must be contiguous [B, T, NK, D]")
+    if mask.stride(-1) != 1 or mask.shape[-1] != tokens or mask.shape[-2] != tokens:
+        raise ValueError("mask must be [B, (1,) T, T] with unit key stride")
+    out = torch.empty_like(q) if out is None else out
+    scale = head_dim ** -0.5 if scale is None else scale
+    _lib.lib().call("t2c_attn_masked_gqa", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(mask), _lib.ptr(out),
+                    batch, tokens, tokens, n_heads, n_kv, head_dim, mask.stride(0), mask.stride(-2), float(scale),
+                    _lib.stream_ptr())
+    return out
+
+
 # ------------------------------------------------ fp32-activation prefill programs
 def _check_f32(t: torch.Tensor, name: str) -> None:
     _check(t, torch.float32, name)
