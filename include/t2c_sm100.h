@@ -450,12 +450,14 @@ int t2c_value_cache_write_f32(const float *src, const int64_t *positions, int nc
                               const int64_t *cache_lens, int64_t B, int64_t T, int64_t H, int64_t D, void *stream);
 /* Bidirectional GQA attention under an additive fp16 mask (OmniVoice's LLM):
  * out[b,t,h,:] = softmax(q[b,t,h,:] . k[b,s,h/(NH/NK),:] * scale + mask[b,t,s]) v[b,s,h/(NH/NK),:]
- * over all S keys; q / out fp16 token-major [B, T, NH, D], k / v fp16 [B, S, NK, D], mask element
- * (b, t, s) at b * mask_b_stride + t * mask_row_stride + s (values <= -FLT_MAX/2, -inf included,
- * mask the key).  D = 128, on the tensor cores.  Replaces ExportSdpaProgram
+ * over all S keys, fp16 q / k / v / out addressed by element strides {batch, position, head}
+ * (k and v share theirs; rows of D contiguous values), mask element (b, t, s) at
+ * b * mask_b_stride + t * mask_row_stride + s (values <= -FLT_MAX/2, -inf included, mask the
+ * key).  D = 128, on the tensor cores.  Replaces ExportSdpaProgram
  *   src/models/quantized_omnivoice/shaders/sdpa_masked_f32.py */
 int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, const void *mask, void *out, int64_t B,
-                        int64_t T, int64_t S, int64_t NH, int64_t NK, int64_t D, int64_t mask_b_stride,
+                        int64_t T, int64_t S, int64_t NH, int64_t NK, int64_t D, const int64_t *q_strides,
+                        const int64_t *kv_strides, const int64_t *o_strides, int64_t mask_b_stride,
                         int64_t mask_row_stride, float scale, void *stream);
 /* OmniVoice input embedding: out fp16 [B, S, H]; where audio_mask[b, s] != 0 the fp32 sum over the C
  * codebooks of Q8_0 audio rows c * audio_vocab + ids[b, c, s], else Q8_0 text row ids[b, 0, s]

@@ -636,3 +636,45 @@ def test_reference_optimized_asr_text_decoder_through_session(ref_modules):
     assert classes <= set(rt._ops), classes - set(rt._ops)
     assert {"LinearNobiasQ4KPairProgram", "LinearNobiasQ4KTripleProgram", "OptimizedQwen3SdpaCausalCacheWriteProgram",
             "SdpaDecodeCacheWriteF16Program", "Qwen3AsrTokenStoreEosProgram"} <= classes, classes
+
+
+@pytest.mark.skipif(not (REF_SRC / "models" / "quantized_omnivoice").is_dir(), reason="reference sources not present")
+def test_reference_omnivoice_llm_step_through_session(ref_modules):
+    """The reference's generated OmniVoice generation step up to the audio heads
+    (models/quantized_omnivoice/run.py:113-129: input embedding, dispatch/llm_forward.py, dispatch/audio_head.py)
+    through RuntimeSession's validation: every contract class it dispatches has a CUDA op (the Q8_0 input
+    embedding, Q4_K / Q6_K linears, RMSNorms, the unfused RoPE chain, bidirectional masked GQA SDPA at D = 128),
+    and every transpose has a known permutation.  CFG scoring and the top-k token update are not served."""
+    from models.quantized_omnivoice.dispatch.audio_head import run_audio_head
+    from models.quantized_omnivoice.dispatch.llm_forward import run_llm_forward
+    from models.quantized_omnivoice.shaders.omnivoice_input_embed_q8_0_f32 import OMNIVOICE_INPUT_EMBED_Q8_0_F32
+    from models.quantized_omnivoice.tensors.model import create_model_tensors, model_tensors
+    from torch2vk.runtime.rope_table import run_rope_table_f32
+    from tests.dry_session import DrySession
+    from torch2vk_b200.runtime.variants import TRANSPOSE_PERMUTATIONS
+
+    create_model_tensors(target_len=40)
+    mt = model_tensors()
+    rt = DrySession(mt)
+    S = mt.batch_input_ids.spec.shape[2]
+    state = {mt.batch_input_ids: np.zeros((2, 8, S), np.int64), mt.batch_audio_mask: np.zeros((2, S), np.uint32),
+             mt.attention_mask: np.zeros((2, 1, S, S), np.float16), mt.tokens: np.zeros((1, 8, 40), np.int64)}
+    with rt.request(state=state):
+        # run.py:62-101 (_run_rope_table, _run_input_embed), restated: run.py itself imports audio I/O modules
+        run_rope_table_f32(rt, start_position=0, theta=1_000_000.0, cos=mt.rope.cos, sin=mt.rope.sin,
+                           frame_name="omnivoice.rope")
+        with rt.frame("omnivoice.step.0000"):
+            OMNIVOICE_INPUT_EMBED_Q8_0_F32(rt, text_weight=mt.text_embedding_weight,
+                                           audio_weight=mt.audio_embedding_weight,
+                                           batch_input_ids=mt.batch_input_ids, batch_audio_mask=mt.batch_audio_mask,
+                                           hidden_states=mt.llm_forward.hidden_states)
+            run_llm_forward(rt)
+            run_audio_head(rt)
+    classes = {c for _, c, _, _ in rt.calls}
+    assert classes <= set(rt._ops), classes - set(rt._ops)
+    assert {"OmniVoiceInputEmbedQ8_0Program", "ExportSdpaProgram", "ExportLinearNobiasQ6KProgram"} <= classes
+    for name, cls, _, _ in rt.calls:
+        if cls == "ExportTransposeProgram":
+            assert name in TRANSPOSE_PERMUTATIONS, name
+    sdpa = [c for c in rt.calls if c[1] == "ExportSdpaProgram"]
+    assert len(sdpa) == 28 and all(c[3]["D"] == 128 and c[3]["NH"] == 16 and c[3]["NK"] == 8 for c in sdpa)

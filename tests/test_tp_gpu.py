@@ -1,10 +1,11 @@
 """Tensor parallelism on real GPUs (needs >= 2): TP greedy tokens vs the oracle and the single-GPU runner.
 
 The gate: 32 greedy decode tokens of a seeded 32-Q / 8-KV-head model equal the
-oracle's (HF fp32 on the dequantized blocks) and the single-GPU runner's, and
-every rank holds the same tokens.  The row-parallel partial sums meet in a
-different order than on one GPU, which could flip a token only at a near-tie
-of the top two logits; the check prints the smallest top-two gap it saw.
+oracle's (HF fp32 on the dequantized blocks), every rank holds the same
+tokens, and they equal the single-GPU runner's except where that runner
+itself leaves the oracle at a near tie of the top two logits (the row-parallel
+partial sums meet in a different order than on one GPU; this seed has a tie of
+0.0002 at step 8).
 """
 
 from __future__ import annotations
@@ -34,4 +35,9 @@ def test_tp2_matches_oracle_and_single_gpu(peer):
     assert r.returncode == 0, out[-3000:]
     line = next(ln for ln in out.splitlines() if ln.startswith("TP OK"))
     assert "ranks_identical=True" in line and "status=0" in line, line
-    assert "first_diff_oracle=32 " in line and "first_diff_single=32 " in line, line
+    assert "first_diff_oracle=32 " in line, line
+    # against the single-GPU runner: identical, or apart only where the single-GPU runner itself leaves the
+    # oracle at a near tie of the top two logits (its partial sums meet in another order than TP's)
+    f = dict(kv.split("=") for kv in line.split()[2:])
+    if f["first_diff_single"] != "32":
+        assert f["single_vs_oracle"] == f["first_diff_single"] and float(f["gap_at_single_diff"]) < 0.02, line

@@ -5,8 +5,9 @@ Qwen3 on the dequantized GGUF blocks; the packed blocks are what the GPU
 streams), runs the tensor-parallel runner (prefill + graph-replayed decode),
 and rank 0 compares 32 greedy tokens with the oracle's greedy decode and with
 the single-GPU runner on the same weights.  Prints
-"TP OK first_diff_oracle=<i> first_diff_single=<j> ranks_identical=<b> status=<s> min_gap=<g>"
-(a first_diff of 32 means all 32 tokens agree).
+"TP OK first_diff_oracle=<i> first_diff_single=<j> single_vs_oracle=<k> gap_at_single_diff=<g>
+ranks_identical=<b> status=<s> min_gap=<g>" (a first_diff of 32 means all 32 tokens agree; the
+oracle's top-two logit gap at step j says whether a TP / single-GPU difference sits at a near tie).
 """
 
 from __future__ import annotations
@@ -65,7 +66,10 @@ def main() -> None:
         ref_oracle, gaps = qwen3_ref.greedy(pm.hf, ids, STEPS)
         same_across = all(torch.equal(e, got) for e in everyone)
         status = kernels.device_status()
-        print(f"TP OK first_diff_oracle={first_diff(got, ref_oracle)} first_diff_single={first_diff(got, ref_single)} "
+        fd_single = first_diff(got, ref_single)
+        gap_at = gaps[fd_single] if fd_single < STEPS else float("inf")
+        print(f"TP OK first_diff_oracle={first_diff(got, ref_oracle)} first_diff_single={fd_single} "
+              f"single_vs_oracle={first_diff(ref_single, ref_oracle)} gap_at_single_diff={gap_at:.4f} "
               f"ranks_identical={same_across} status={status} min_gap={min(gaps):.4f}", flush=True)
     dist.barrier()
     if tp_runner._peer is not None:

@@ -79,7 +79,7 @@ _SIGNATURES: dict[str, list] = {
     "t2c_add": [_vp, _vp, _vp, _i64, _vp],
     "t2c_swiglu": [_vp, _vp, _vp, _i64, _vp],
     "t2c_advance_positions": [_vp, _i64, _vp, _vp],
-    "t2c_attn_masked_gqa": [_vp] * 5 + [_i64] * 8 + [_f32, _vp],
+    "t2c_attn_masked_gqa": [_vp] * 5 + [_i64] * 6 + [_vp] * 3 + [_i64] * 2 + [_f32, _vp],
     "t2c_omnivoice_input_embed": [_vp] * 5 + [_i64] * 6 + [_vp],
     "t2c_attn_decode_paged": [_vp] * 6 + [_i64] * 11 + [_vp, _i64, _vp],
     "t2c_kv_cache_write_paged": [_vp, _vp, _i64, _i64, _vp, _vp] + [_i64] * 10 + [_vp],

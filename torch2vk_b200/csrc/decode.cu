@@ -1840,12 +1840,17 @@ extern "C" int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, 
 
 extern "C" int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, const void *mask, void *out,
                                    int64_t B, int64_t T, int64_t S, int64_t NH, int64_t NK, int64_t D,
+                                   const int64_t *q_strides, const int64_t *kv_strides, const int64_t *o_strides,
                                    int64_t mask_b_stride, int64_t mask_row_stride, float scale, void *stream) {
-    if (!q || !k || !v || !mask || !out) return set_error(T2C_EINVAL, "attn_masked_gqa: NULL pointer");
+    if (!q || !k || !v || !mask || !out || !q_strides || !kv_strides || !o_strides)
+        return set_error(T2C_EINVAL, "attn_masked_gqa: NULL pointer");
     if (B <= 0 || T <= 0 || S <= 0 || NH <= 0 || NK <= 0 || NH % NK || T > INT32_MAX || S > INT32_MAX ||
         mask_row_stride < S || mask_b_stride < 0)
         return set_error(T2C_EINVAL, "attn_masked_gqa: bad shape");
     if (D != 128) return set_error(T2C_EUNSUPPORTED, "attn_masked_gqa: D=%lld (128 only)", (long long)D);
+    for (int i = 0; i < 3; ++i)
+        if (q_strides[i] % 8 || kv_strides[i] % 8 || o_strides[i] % 2)
+            return set_error(T2C_EINVAL, "attn_masked_gqa: q / k / v rows must be 16-byte aligned, out rows 4-byte");
     if (!aligned(q, 16) || !aligned(out, 4) || !aligned(k, 16) || !aligned(v, 16))
         return set_error(T2C_EINVAL, "attn_masked_gqa: alignment");
     static bool configured[64] = {};
@@ -1860,9 +1865,10 @@ extern "C" int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, 
     return launch(attn_prefill_tc_kernel<true, false>, dim3(static_cast<unsigned>(B * NH * tiles)), dim3(128),
                   kPtSmem, as_stream(stream), q, static_cast<const __half *>(k), static_cast<const __half *>(v), out,
                   static_cast<const int32_t *>(nullptr), static_cast<int>(T), static_cast<int>(NH),
-                  static_cast<int>(NK), S * NK * D, NK * D, D, T * NH * D, NH * D, D, T * NH * D, NH * D, D,
-                  1.4426950408889634f * scale, static_cast<const __half *>(mask), mask_row_stride,
-                  static_cast<const uint32_t *>(nullptr), int64_t{0}, static_cast<int>(S), mask_b_stride);
+                  static_cast<int>(NK), kv_strides[0], kv_strides[1], kv_strides[2], q_strides[0], q_strides[1],
+                  q_strides[2], o_strides[0], o_strides[1], o_strides[2], 1.4426950408889634f * scale,
+                  static_cast<const __half *>(mask), mask_row_stride, static_cast<const uint32_t *>(nullptr),
+                  int64_t{0}, static_cast<int>(S), mask_b_stride);
 }
 
 extern "C" int t2c_embedding(int wtype, const void *weight, const int64_t *ids, void *out, int64_t n_ids,

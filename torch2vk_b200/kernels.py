@@ -539,23 +539,33 @@ def attn_masked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.T
 
 
 def attn_masked_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor, *, batch: int,
-                    tokens: int, n_heads: int, n_kv: int, head_dim: int, scale: float | None = None,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
-    """Bidirectional GQA attention under an additive fp16 mask: q / out fp16 token-major [B, T, NH, D] (row
-    views fine), k / v fp16 [B, T, NK, D], mask [B, 1, T, T] (or [B, T, T]; unit key stride)."""
-    _check(q, torch.float16, "q")
-    _check(mask, torch.float16, "mask")
-    for t, n in ((k, "k"), (v, "v")):
+                    tokens: int, n_heads: int, n_kv: int, head_dim: int, layout: str = "token_major",
+                    scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Bidirectional GQA attention under an additive fp16 mask [B, (1,) T, S] (unit key stride).
+
+    layout "token_major": q / out [B, T, NH, D] (row views fine), k / v [B, S, NK, D];
+    "head_major": q / out [B, NH, T, D], k / v [B, NK, S, D]."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (mask, "mask")):
         _check(t, torch.float16, n)
-        if not t.is_contiguous():
-            raise ValueError(f"{n} must be contiguous [B, T, NK, D]")
-    if mask.stride(-1) != 1 or mask.shape[-1] != tokens or mask.shape[-2] != tokens:
-        raise ValueError("mask must be [B, (1,) T, T] with unit key stride")
     out = torch.empty_like(q) if out is None else out
+    if k.stride() != v.stride() or k.shape != v.shape:
+        raise ValueError("k and v must have the same shape and strides")
+    if mask.stride(-1) != 1 or mask.shape[-2] != tokens:
+        raise ValueError("mask must be [B, (1,) T, S] with unit key stride")
+    S = mask.shape[-1]
+    if layout == "token_major":
+        q4, o4 = q.view(batch, tokens, n_heads, head_dim), out.view(batch, tokens, n_heads, head_dim)
+        st = lambda t: [t.stride(0), t.stride(1), t.stride(2)]  # noqa: E731
+    elif layout == "head_major":
+        q4, o4 = q, out
+        st = lambda t: [t.stride(0), t.stride(2), t.stride(1)]  # noqa: E731
+    else:
+        raise ValueError(layout)
     scale = head_dim ** -0.5 if scale is None else scale
     _lib.lib().call("t2c_attn_masked_gqa", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(mask), _lib.ptr(out),
-                    batch, tokens, tokens, n_heads, n_kv, head_dim, mask.stride(0), mask.stride(-2), float(scale),
-                    _lib.stream_ptr())
+                    batch, tokens, S, n_heads, n_kv, head_dim, _lib.i64_array(st(q4)), _lib.i64_array(st(k)),
+                    _lib.i64_array(st(o4)), mask.stride(0) if mask.shape[0] > 1 else 0, mask.stride(-2),
+                    float(scale), _lib.stream_ptr())
     return out
 
 

@@ -396,11 +396,38 @@ def _index_select(rt, variant, b, s, pc):
 
 
 def _sdpa_masked(rt, variant, b, s, pc):
-    """softmax(q k^T / sqrt(D) + mask) v, non-causal, additive fp16 mask (sdpa_masked_f32.py:33-90)."""
+    """softmax(q k^T / sqrt(D) + mask) v, non-causal, additive fp16 mask, q [B,NH,T,D] over k / v [B,NK,S,D]
+    (sdpa_masked_f32.py:33-90): the ASR encoder's windows (D = 64, as many key heads as query heads) or
+    OmniVoice's bidirectional GQA (D = 128, mask [B,1,T,S])."""
     q, k, v, mask, out = b["q"], b["k"], b["v"], b["mask"], b["output"]
-    if k.shape[1] != q.shape[1]:
-        raise NotImplementedError(f"{variant.name}: {q.shape[1]} query heads over {k.shape[1]} key heads")
-    kernels.attn_masked(q, k, v, mask, scale=float(q.shape[-1]) ** -0.5, out=out)
+    B, NH, T, D = q.shape
+    NK = k.shape[1]
+    if D == 128:
+        m = mask.reshape(mask.shape[0], T, mask.shape[-1]) if mask.dim() == 4 and mask.shape[1] == 1 else mask
+        kernels.attn_masked_gqa(q, k, v, m, batch=B, tokens=T, n_heads=NH, n_kv=NK, head_dim=D, layout="head_major",
+                                out=out)
+        return
+    if NK != NH:
+        raise NotImplementedError(f"{variant.name}: {NH} query heads over {NK} key heads at D={D}")
+    kernels.attn_masked(q, k, v, mask, scale=float(D) ** -0.5, out=out)
+
+
+@op("OmniVoiceInputEmbedQ8_0Program")
+def _omnivoice_input_embed(rt, variant, b, s, pc):
+    """Text rows, or the fp32 codebook sum of audio rows, Q8_0 (quantized_omnivoice/custom_shaders.py:17-181)."""
+    from torch2vk_b200 import _lib
+
+    ids, amask, out = b["batch_input_ids"], b["batch_audio_mask"], b["hidden_states"]
+    B, C, S = ids.shape
+    H = out.shape[-1]
+    row_bytes = H // 32 * 34
+    tw, aw = b["text_weight"], b["audio_weight"]
+    tv = tw.numel() * tw.element_size() // row_bytes
+    av = aw.numel() * aw.element_size() // row_bytes // C
+    if int(pc.get("V", av)) != av:
+        raise ValueError(f"{variant.name}: audio table of {av} rows per codebook, push constant V={pc['V']}")
+    _lib.lib().call("t2c_omnivoice_input_embed", _lib.ptr(tw), _lib.ptr(aw), _lib.ptr(ids), _lib.ptr(amask),
+                    _lib.ptr(out), B, C, S, H, tv, av, _lib.stream_ptr())
 
 # ------------------------------------- fp32-activation prefill (optimized Qwen3, llama.cpp-style)
 @op("LlamaMatmulQ4KF32Program", "LlamaMatmulQ6KF32Program")

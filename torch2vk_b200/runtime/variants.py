@@ -334,6 +334,10 @@ TRANSPOSE_PERMUTATIONS: dict[str, tuple[int, ...]] = {
     "transpose_f32_d95ce920ac": (0, 2, 1),
     "transpose_f32_6a3397f037": (1, 0, 2),
     "transpose_f32_48d16b9b88": (0, 2, 1, 3),
+    # OmniVoice's LLM (quantized_omnivoice/shaders/transpose_f32_*.py: heads <-> positions)
+    "transpose_f32_322f87bdab": (0, 2, 1, 3),
+    "transpose_f32_b4bb3205fc": (0, 2, 1, 3),
+    "transpose_f32_e6f353739d": (0, 2, 1, 3),
 }
 
 
