@@ -101,6 +101,11 @@ def test_replay_push_slots_and_guards():
     assert not slots.admits({"cache_position": 640, "theta": 1e6})  # outside the range guard
     assert not slots.admits({"cache_position": 5, "theta": 1e4})  # baked value changed
     assert not slots.admits({"cache_position": 5})  # another set of names than the capture's
+    # why a value set is not served: a range miss runs directly, an equality or name-set miss recaptures
+    assert slots.rejection({"cache_position": 640, "theta": 1e6}) == "range"
+    assert slots.rejection({"cache_position": 5, "theta": 1e4}) == "eq"
+    assert slots.rejection({"cache_position": 5}) == "names"
+    assert slots.rejection({"cache_position": 5, "theta": 1e6}) is None
     assert int(DynamicPush(slots, "token_index", 7)) + 1 == 8
     assert ("token_index", "eq", 7, None) in slots.guards
 

@@ -246,6 +246,9 @@ def _sdpa_causal(rt, variant, b, s, pc):
 
 
 def _decode_splits(max_len: int) -> int:
+    """Split count of a decode attention over a cache of max_len positions.  Direct frames and captured
+    replay plans both take it from the cache length (not the current position), so a replayed step
+    combines the same partials in the same order as the direct one: bit-identical results."""
     return max(1, min(64, max_len // 256))
 
 
@@ -261,7 +264,7 @@ def _decode_at(pc, B: int, S: int, device: torch.device):
     pos = int(p)
     last = min(pos, S - 1)
     positions = torch.full((B,), last, dtype=torch.int32, device=device)
-    return (pos if pos < S else None), positions, _decode_splits(last + 1)
+    return (pos if pos < S else None), positions, _decode_splits(S)
 
 
 def _write_decode_kv(b, wpos, cache_strides, NK: int, D: int, S: int, B: int) -> None:
@@ -287,7 +290,7 @@ def _sdpa_decode(rt, variant, b, s, pc):
         positions, splits = p.device(torch.int32, B, clamp_max=S - 1), _decode_splits(S)
     else:
         pos = min(int(p), S - 1)
-        positions, splits = _positions(rt, B, pos), _decode_splits(pos + 1)
+        positions, splits = _positions(rt, B, pos), _decode_splits(S)
     kernels.attn_decode(q, k, v, positions, batch=B, n_heads=NH, n_kv=NK, head_dim=D, max_len=S,
                         splits=splits, layout="head_major", out=out)
 

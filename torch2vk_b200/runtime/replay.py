@@ -23,14 +23,17 @@ before each replay; an op may attach guards (e.g. `cache_position < S`, where
 its direct form takes another branch), and any host use of the value (int(),
 float(), comparisons) bakes the captured value in behind an equality guard.
 An execution whose values fail a guard, or that names a different set of
-dynamic push constants than the capture did, launches the ops directly.  If a
-capture fails the plan stays on direct launches; `rebind_replay_plan` drops
-the graph so the next execution binds the current buffers.
+dynamic push constants than the capture did, launches the ops directly; after
+an equality-guard or name-set failure the plan captures again for the new
+values (at most four times, then it warns once and stays on direct launches).
+If a capture fails the plan stays on direct launches; `rebind_replay_plan`
+drops the graph so the next execution binds the current buffers.
 """
 
 from __future__ import annotations
 
 import contextlib
+import warnings
 from collections.abc import Mapping
 from dataclasses import dataclass, field
 
@@ -43,6 +46,7 @@ from torch2vk_b200.runtime.types import concrete_shape, tensor_nbytes
 
 
 _PUSH_BUFFER_BYTES = 1 << 16
+_MAX_RECAPTURES = 4
 _SLOT_ALIGN = 16
 
 
@@ -161,15 +165,21 @@ class PushSlots:
         return self.buffer[off:off + nbytes].view(dtype)
 
     def admits(self, push: Mapping[str, int | float]) -> bool:
+        return self.rejection(push) is None
+
+    def rejection(self, push: Mapping[str, int | float]) -> str | None:
+        """None when the captured graph serves these values, else why not: "names" (another set of
+        dynamic push constants), "eq" (a value baked in at capture changed) or "range" (a value outside
+        the range the captured ops serve, e.g. a cache position past the cache)."""
         if frozenset(push) != self.names:
-            return False
+            return "names"
         for name, kind, a, b in self.guards:
             v = push[name]
             if kind == "eq" and v != a:
-                return False
+                return "eq"
             if kind == "range" and ((a is not None and v < a) or (b is not None and v >= b)):
-                return False
-        return True
+                return "range"
+        return None
 
     def host_image(self, push: Mapping[str, int | float]) -> np.ndarray:
         img = np.zeros(max(self.used, _SLOT_ALIGN), np.uint8)
@@ -228,6 +238,7 @@ class ReplayPlan:
     push_slots: PushSlots | None = None
     graph_replays: int = 0
     direct_executions: int = 0
+    recaptures: int = 0
     _closed: bool = False
 
     @property
@@ -362,6 +373,20 @@ def execute_replay(plan: ReplayPlan, dynamic_symbols: Mapping[str, int] | None =
     else:
         _launch_all(rt, plan, push)  # the first run doubles as the warm-up of every op
         plan.direct_executions += 1
+        why = slots.rejection(push) if slots is not None else ("names" if push else None)
+        if on_cuda and plan.graph is not None and not plan.graph_failed and why in ("eq", "names"):
+            # the captured graph does not admit these values (an op baked one of them in behind an
+            # equality guard, or another set of names): capture again for the new values, a bounded
+            # number of times, then stay on direct launches and say so once.  Values outside a range
+            # guard (a step the captured ops do not serve) just run directly.
+            if plan.recaptures < _MAX_RECAPTURES:
+                plan.recaptures += 1
+                plan.graph, plan.push_slots = None, None
+            else:
+                plan.graph_failed = True
+                warnings.warn(f"ReplayPlan {plan.name!r}: dynamic push constants {sorted(push)} keep failing the "
+                              f"captured graph's guards after {_MAX_RECAPTURES} recaptures; further executions "
+                              "launch the dispatches directly", RuntimeWarning, stacklevel=2)
         if on_cuda and plan.graph is None and not plan.graph_failed:
             _capture(rt, plan, push)
     results: dict[str, bytes] = {}
