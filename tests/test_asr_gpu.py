@@ -227,3 +227,22 @@ def test_large_cache_write_and_rope_table():
         kernels.rope_table(cd, sd, theta=1e6, start_position=0,
                            start_position_dev=torch.tensor([7], dtype=torch.int64, device="cuda"))
         assert torch.equal(cd.half(), c16) and torch.equal(sd.half(), s16)
+
+
+def test_asr_encoder_batched_equals_single():
+    """forward_batch over three utterances (convolutions over all chunks, linears over all rows, windowed
+    attention per utterance) against one forward per utterance: the same rows up to GEMM summation order."""
+    import dataclasses
+
+    from torch2vk_b200.asr import AsrEncoderConfig, AsrEncoderRunner, prepare_inputs, random_params
+
+    cfg = dataclasses.replace(AsrEncoderConfig.qwen3_asr_0_6b(), layers=2)
+    runner = AsrEncoderRunner(cfg, random_params(cfg, seed=1))
+    rng = np.random.default_rng(9)
+    clips = [runner.upload(prepare_inputs(rng.standard_normal((cfg.num_mel_bins, 1000)).astype(np.float32), cfg))
+             for _ in range(3)]
+    batched = runner.forward_batch(clips).float().cpu()
+    for b, t in enumerate(clips):
+        single = runner.forward(t).float().cpu()
+        err = (batched[b] - single).abs().max().item()
+        assert err <= 2e-3 * single.abs().max().item(), (b, err)

@@ -217,18 +217,38 @@ class AsrEncoderRunner:
         }
 
     def forward(self, t: dict[str, torch.Tensor]) -> torch.Tensor:
+        """Encoder output rows [tokens, output_dim] fp16 of one uploaded utterance."""
+        return self.forward_batch([t])[0]
+
+    def forward_batch(self, clips: list[dict[str, torch.Tensor]]) -> torch.Tensor:
+        """Encoder output [B, tokens, output_dim] fp16 of B uploaded utterances of the same length in one
+        pass: the convolutions run over all B x chunks, the linears over all B x tokens rows, and the
+        windowed attention per utterance (batch B, the same window mask)."""
         cfg, w = self.cfg, self.w
         c, d = cfg.conv_channels, cfg.d_model
-        x = t["feature"]
+        B = len(clips)
+        if B == 0:
+            raise ValueError("forward_batch needs at least one utterance")
+        first = clips[0]
+        for t in clips[1:]:
+            if t["feature"].shape != first["feature"].shape or t["index"].shape != first["index"].shape:
+                raise ValueError("forward_batch: utterances must have the same number of frames")
+        cat = (lambda key: first[key]) if B == 1 else (lambda key: torch.cat([t[key] for t in clips], 0))
+        x = cat("feature")
         for i in (1, 2, 3):
             x = kernels.conv2d_q8_0(x, w[f"conv2d{i}.weight"], w[f"conv2d{i}.bias"], c, gelu=True)
-        b, _, f, td = x.shape
-        xt = torch.empty(b, td, c, f, dtype=torch.float16, device=x.device)
+        bc, _, f, td = x.shape
+        chunks = bc // B
+        xt = torch.empty(bc, td, c, f, dtype=torch.float16, device=x.device)
         kernels.copy4d(x.permute(0, 3, 1, 2), xt)
-        e = kernels.linear_q8_0_bias(xt.view(b, td, c * f), w["conv_out.weight"], None, d)
-        e = kernels.add(e, t["pos"])
-        h = kernels.index_rows(e.view(b * td, d), t["index"])
-        n = h.shape[0]
+        e = kernels.linear_q8_0_bias(xt.view(bc, td, c * f), w["conv_out.weight"], None, d)
+        e = kernels.add(e, cat("pos"))
+        if B == 1:
+            index = first["index"]
+        else:
+            index = torch.cat([t["index"] + b * chunks * td for b, t in enumerate(clips)], 0)
+        h = kernels.index_rows(e.view(bc * td, d), index)
+        n = first["index"].shape[0]
         hd = cfg.head_dim
         scale = 1.0 / math.sqrt(hd)
         for i in range(cfg.layers):
@@ -239,11 +259,11 @@ class AsrEncoderRunner:
             k = kernels.linear_q8_0_bias(a, w[p + "self_attn.k_proj.weight"], w[p + "self_attn.k_proj.bias"], d)
             v = kernels.linear_q8_0_bias(a, w[p + "self_attn.v_proj.weight"], w[p + "self_attn.v_proj.bias"], d)
 
-            def heads(z: torch.Tensor) -> torch.Tensor:  # [n, d] -> [1, H, n, hd] view
-                return z.view(n, cfg.heads, hd).permute(1, 0, 2).unsqueeze(0)
+            def heads(z: torch.Tensor) -> torch.Tensor:  # [B n, d] -> [B, H, n, hd] view
+                return z.view(B, n, cfg.heads, hd).permute(0, 2, 1, 3)
 
-            o = torch.empty(n, d, dtype=torch.float16, device=h.device)
-            kernels.attn_masked(heads(q), heads(k), heads(v), t["mask"], scale=scale, out=heads(o))
+            o = torch.empty(B * n, d, dtype=torch.float16, device=h.device)
+            kernels.attn_masked(heads(q), heads(k), heads(v), first["mask"], scale=scale, out=heads(o))
             o = kernels.linear_q8_0_bias(o, w[p + "self_attn.out_proj.weight"], w[p + "self_attn.out_proj.bias"], d)
             h = kernels.add(r, o)
             r = h
@@ -253,7 +273,7 @@ class AsrEncoderRunner:
             h = kernels.add(r, a)
         h = kernels.layer_norm(h, w["ln_post.weight"], w["ln_post.bias"], cfg.eps)
         h = kernels.linear_q8_0_bias(h, w["proj1.weight"], w["proj1.bias"], d, gelu=True)
-        return kernels.linear_q8_0_bias(h, w["proj2.weight"], w["proj2.bias"], cfg.output_dim)
+        return kernels.linear_q8_0_bias(h, w["proj2.weight"], w["proj2.bias"], cfg.output_dim).view(B, n, -1)
 
     def flops(self, inputs: AsrInputs) -> float:
         """Multiply-add flops of one forward (convolutions, linears, attention within windows)."""

@@ -67,8 +67,8 @@ class AsrPipeline:
         return out
 
     def encode(self, clips: list[dict[str, torch.Tensor]]) -> torch.Tensor:
-        for b, t in enumerate(clips):
-            self.features[b].copy_(self.encoder.forward(t))
+        """All clips through the audio tower in one batched pass (AsrEncoderRunner.forward_batch)."""
+        self.features.copy_(self.encoder.forward_batch(clips))
         return self.features
 
     def prompt(self, prefix_ids: torch.Tensor, suffix_ids: torch.Tensor, placeholder: int) -> torch.Tensor:

@@ -178,6 +178,7 @@ class Qwen3Runner:
         self.fused_workspace = kernels.attn_decode_fused_workspace(self.batch, cfg.heads, cfg.kv_heads, cfg.head_dim,
                                                                    self.decode_splits, dev)
         self.decode = self._alloc(self.batch)
+        self._prefill_buffers: tuple[int, _Buffers] | None = None
         self._graph: torch.cuda.CUDAGraph | None = None
 
     # ------------------------------------------------------------ buffers
@@ -305,7 +306,12 @@ class Qwen3Runner:
         self.token_index.zero_()
         self.generated_length.zero_()
         self.stopped.zero_()
-        b = self._alloc(self.batch * tokens)
+        # prompt-sized activations are kept for the next prefill of the same length (no allocator traffic
+        # on repeated prompts)
+        if self._prefill_buffers is None or self._prefill_buffers[0] != tokens:
+            self._prefill_buffers = None
+            self._prefill_buffers = (tokens, self._alloc(self.batch * tokens))
+        b = self._prefill_buffers[1]
         self._embed(ids.reshape(-1).contiguous(), b.h)
         if inject is not None:
             kernels.index_copy_rows(b.h.view(self.batch, tokens, cfg.hidden), inject[0], inject[1])
