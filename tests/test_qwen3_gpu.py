@@ -122,3 +122,28 @@ def test_qwen3_0_6b_greedy_32_steps(topology):
     got = runner.generate(ids.cuda(), 32).cpu()
     ref, gaps = qwen3_ref.greedy(pm.hf, ids, 32)
     assert torch.equal(got, ref), f"got {got.tolist()}\nref {ref.tolist()}\nmin top-2 gaps {np.round(gaps, 4)}"
+
+
+def test_greedy_32_steps_with_massive_activation_channels():
+    """Model-level check of the exact-x matvecs: RMSNorm weights with a few large channels (x 40 on 4 of
+    1024 hidden channels of every input / post-attention norm, as real checkpoints' massive activations),
+    32 greedy steps against the oracle on the same weights, identical up to the oracle's first near tie."""
+    from oracle import qwen3_ref
+    from torch2vk_b200.qwen3 import Qwen3Config, Qwen3Runner
+
+    cfg = Qwen3Config(**SMALL)
+    pm = qwen3_ref.build(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab,
+                         seed=3, topology="q4_k_m")
+    channels = [7, 300, 301, 901]
+    with torch.no_grad():
+        for name, p in pm.hf.named_parameters():
+            if name.endswith(("input_layernorm.weight", "post_attention_layernorm.weight")):
+                p[channels] *= 40.0
+                pm.norms[name] = p.detach().numpy().astype(np.float32).copy()
+    ids = qwen3_ref.prompt_ids(20, cfg.vocab, seed=3)
+    runner = Qwen3Runner(cfg, upload(pm, cfg), batch=1, max_seq=64, max_new_tokens=33)
+    got = runner.generate(ids.cuda(), 32).cpu()
+    ref, gaps = qwen3_ref.greedy(pm.hf, ids, 32)
+    n = next((i for i, gap in enumerate(gaps) if gap < 0.02), 32)
+    assert n >= 8, gaps
+    assert torch.equal(got[:, :n], ref[:, :n]), f"got {got.tolist()}\nref {ref.tolist()}\nmin top-2 gaps {gaps}"
