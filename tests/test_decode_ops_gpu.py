@@ -179,11 +179,12 @@ def test_embedding_f16_and_q4k(oracle):
 # 16, so they take the direct (non-bulk-copy) kernel; N = 4099 leaves a ragged group.
 @pytest.mark.parametrize("kind,K,N", [("q6_k", 1024, 4112), ("q6_k", 4096, 4112), ("q4_k", 1024, 4112),
                                       ("q6_k", 512, 4099), ("q8_0", 1088, 4099)])
-def test_lm_head_argmax_and_select(oracle, kind, K, N):
+@pytest.mark.parametrize("M", [2, 3, 4])
+def test_lm_head_argmax_and_select(oracle, kind, K, N, M):
+    """2..4 tokens in one pass of the weights (Q6_K / Q8_0: qmv_x16_kernel<2 or 4>)."""
     from torch2vk_b200 import kernels
 
     rng = np.random.default_rng(5)
-    M = 2
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     w[777] = w[123]          # an exact duplicate row: tie -> lower id
     packed = oracle.quantize(w, kind)

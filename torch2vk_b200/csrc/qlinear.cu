@@ -19,7 +19,7 @@
 //    sub-blocks of a block so each lane scales its own partial sums.
 //  * qmv_mma_kernel (Q4_K, M = 2..4): the same streaming, mma columns =
 //    tokens, sub-block scales folded into the fp16 A operand exactly.
-//  * qmv_x16_kernel (any type, one token per pass): direct global loads,
+//  * qmv_x16_kernel (any type, up to 4 tokens per pass): direct global loads,
 //    16-row tiles, the sparse-column mapping of the M = 1 kernel.
 //  * qmv_tma_kernel / qmv_direct_kernel: dp4a on 15-bit fixed-point x planes;
 //    kept only for M > 4 shapes the tensor-core GEMM does not take (Q6_K with
@@ -1986,9 +1986,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
 }
 
 // ======================================================= exact fp16-x kernel
-// qmv_x16_kernel: one token per launch (M = 1; larger M runs one pass per
-// token), weight streams of any GGUF type (Q4_K, Q6_K, Q8_0, mixed in one
-// fused QKV), modes ROWS (+ residual), SWIGLU and ARGMAX.  x keeps the
+// qmv_x16_kernel<MT>: up to MT = 4 tokens per pass (the weight words of a unit
+// are loaded once and serve every token; more tokens take further passes),
+// weight streams of any GGUF type (Q4_K, Q6_K, Q8_0, mixed in one fused QKV),
+// modes ROWS (+ residual), SWIGLU and ARGMAX.  x keeps the
 // reference's arithmetic: the (normalized) values are rounded to fp16 once
 // and enter fp16 tensor-core products unchanged; every weight code enters as
 // an exactly representable fp16 value and the block scales are applied in
@@ -2040,11 +2041,15 @@ __device__ __forceinline__ void mma_f16_16816_zc(float d[4], const uint32_t a[4]
 }
 
 // x of one token: fp16 [K] in natural order, fp32 sums of 32-value blocks [K / 32].
-__device__ void x16_prepare(const QParams &p, uint8_t *xs, float *xsum, float *red) {
+// Token m of the pass: x row m of p.x into xs + m * 2K (fp16) and xsum + m * K / 32.
+__device__ void x16_prepare_token(const QParams &p, int m, uint8_t *xs, float *xsum, float *red) {
     const int K = p.K;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int chunks = K >> 3;
-    const uint4 *xv = reinterpret_cast<const uint4 *>(p.x);
+    const uint4 *xv = reinterpret_cast<const uint4 *>(p.x + static_cast<int64_t>(m) * K);
+    xs += static_cast<size_t>(m) * 2 * K;
+    xsum += static_cast<size_t>(m) * (K >> 5);
+    red += m * kXWarps;
     float inv_rms = 1.0f;
     if (p.norm_w != nullptr) {
         float ss = 0.0f;
@@ -2094,6 +2099,17 @@ __device__ void x16_prepare(const QParams &p, uint8_t *xs, float *xsum, float *r
             if ((lane & 3) == 0) xsum[c >> 2] = sum;
         }
     }
+}
+
+// x of the pass's p.M tokens (rows past p.M of a MT-token pass are zero), then one CTA barrier.
+template <int MT>
+__device__ void x16_prepare(const QParams &p, uint8_t *xs, float *xsum, float *red) {
+#pragma unroll 1
+    for (int m = 0; m < p.M; ++m) x16_prepare_token(p, m, xs, xsum, red);
+    const int K = p.K;
+    for (int i = threadIdx.x + p.M * (2 * K / 16); i < MT * (2 * K / 16); i += kXThreads)
+        reinterpret_cast<uint4 *>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x + p.M * (K >> 5); i < MT * (K >> 5); i += kXThreads) xsum[i] = 0.0f;
     __syncthreads();
 }
 
@@ -2132,46 +2148,53 @@ __device__ __forceinline__ void x_q4k_scales(const uint4 h, const XLane &L, floa
     dm[1] = fmaf(dmin, __uint_as_float(__byte_perm(mnp, 0x4B000000u, 0x7541u)), -dmin * 8388608.0f);
 }
 
-// Unit u (256 values) of two rows (ra, rb: row starts, nullptr when past N) for Q4_K.
+// Unit u (256 values) of two rows (ra, rb: row starts, nullptr when past N) for Q4_K; the weight words are
+// loaded once and serve each of the MT tokens (x of token m at xs + m * xstride, its sums at
+// xsum + m * sstride).
+template <int MT>
 __device__ __forceinline__ void x16_q4k(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
-                                        const float *xsum, const XLane &L, float acc[2]) {
+                                        const float *xsum, int xstride, int sstride, const XLane &L,
+                                        float acc[MT][2]) {
     const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
     const uint8_t *ba = ra ? ra + 144 * u : nullptr, *bb = rb ? rb + 144 * u : nullptr;
     const uint4 ha = ba ? ldg_nc_v4(ba) : z4, hb = bb ? ldg_nc_v4(bb) : z4;
     const uint4 wa0 = ba ? ldg_nc_v4(ba + 16 + 32 * L.t) : z4, wa1 = ba ? ldg_nc_v4(ba + 32 + 32 * L.t) : z4;
     const uint4 wb0 = bb ? ldg_nc_v4(bb + 16 + 32 * L.t) : z4, wb1 = bb ? ldg_nc_v4(bb + 32 + 32 * L.t) : z4;
-    // B: lo (hi) values of group t' = this lane's t for the lanes whose column takes them
-    const uint8_t *xb = xs + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
-    uint32_t bx[16];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(xb + 16 * i);
-        bx[4 * i] = v.x;
-        bx[4 * i + 1] = v.y;
-        bx[4 * i + 2] = v.z;
-        bx[4 * i + 3] = v.w;
-    }
     float ds[2][2], dm[2][2];
     x_q4k_scales(ha, L, ds[0], dm[0]);
     x_q4k_scales(hb, L, ds[1], dm[1]);
     const uint32_t A[8] = {wa0.x, wa0.y, wa0.z, wa0.w, wa1.x, wa1.y, wa1.z, wa1.w};
     const uint32_t B[8] = {wb0.x, wb0.y, wb0.z, wb0.w, wb1.x, wb1.y, wb1.z, wb1.w};
-    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+    for (int m = 0; m < MT; ++m) {
+        // B: lo (hi) values of group t' = this lane's t for the lanes whose column takes them
+        const uint8_t *xb = xs + m * xstride + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
+        uint32_t bx[16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        // bytes (4j, 4j + 1) then (4j + 2, 4j + 3): x pairs in natural order
-        const uint32_t a01 = __byte_perm(A[j], 0u, 0x4140u), a23 = __byte_perm(A[j], 0u, 0x4342u);
-        const uint32_t b01 = __byte_perm(B[j], 0u, 0x4140u), b23 = __byte_perm(B[j], 0u, 0x4342u);
-        const uint32_t f0[4] = {a01 & 0x000F000Fu, b01 & 0x000F000Fu, a01 & 0x00F000F0u, b01 & 0x00F000F0u};
-        const uint32_t f1[4] = {a23 & 0x000F000Fu, b23 & 0x000F000Fu, a23 & 0x00F000F0u, b23 & 0x00F000F0u};
-        mma_f16_16816(d, f0, bx[2 * j] & L.b0on, bx[2 * j] & L.b1on);
-        mma_f16_16816(e, f1, bx[2 * j + 1] & L.b0on, bx[2 * j + 1] & L.b1on);
+        for (int i = 0; i < 4; ++i) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(xb + 16 * i);
+            bx[4 * i] = v.x;
+            bx[4 * i + 1] = v.y;
+            bx[4 * i + 2] = v.z;
+            bx[4 * i + 3] = v.w;
+        }
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            // bytes (4j, 4j + 1) then (4j + 2, 4j + 3): x pairs in natural order
+            const uint32_t a01 = __byte_perm(A[j], 0u, 0x4140u), a23 = __byte_perm(A[j], 0u, 0x4342u);
+            const uint32_t b01 = __byte_perm(B[j], 0u, 0x4140u), b23 = __byte_perm(B[j], 0u, 0x4342u);
+            const uint32_t f0[4] = {a01 & 0x000F000Fu, b01 & 0x000F000Fu, a01 & 0x00F000F0u, b01 & 0x00F000F0u};
+            const uint32_t f1[4] = {a23 & 0x000F000Fu, b23 & 0x000F000Fu, a23 & 0x00F000F0u, b23 & 0x00F000F0u};
+            mma_f16_16816(d, f0, bx[2 * j] & L.b0on, bx[2 * j] & L.b1on);
+            mma_f16_16816(e, f1, bx[2 * j + 1] & L.b0on, bx[2 * j + 1] & L.b1on);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] += e[i];
+        const float2 xs2 = *reinterpret_cast<const float2 *>(xsum + m * sstride + 8 * u + 2 * L.t);
+        acc[m][0] += fmaf(ds[0][0], d[0], fmaf(ds[0][1], d[1], -fmaf(dm[0][0], xs2.x, dm[0][1] * xs2.y)));
+        acc[m][1] += fmaf(ds[1][0], d[2], fmaf(ds[1][1], d[3], -fmaf(dm[1][0], xs2.x, dm[1][1] * xs2.y)));
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] += e[i];
-    const float2 xs2 = *reinterpret_cast<const float2 *>(xsum + 8 * u + 2 * L.t);
-    acc[0] += fmaf(ds[0][0], d[0], fmaf(ds[0][1], d[1], -fmaf(dm[0][0], xs2.x, dm[0][1] * xs2.y)));
-    acc[1] += fmaf(ds[1][0], d[2], fmaf(ds[1][1], d[3], -fmaf(dm[1][0], xs2.x, dm[1][1] * xs2.y)));
 }
 
 // All 32-bit words one lane needs from a Q6_K block (at a 2-byte aligned
@@ -2183,6 +2206,13 @@ struct Q6Words {
     uint32_t ql[8], qh[8], sc[4];
     float d;
 };
+
+// Words [4 Q + (half ? 2 : 0), + 16) bytes of the 32 bytes w[0..7] (Q, half compile-time in the caller's switch).
+template <int Q>
+__device__ __forceinline__ void q6_pick4(const uint32_t w[8], bool half, uint32_t *out) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = half ? __funnelshift_r(w[Q + i], w[Q + i + 1], 16) : w[Q + i];
+}
 
 __device__ __forceinline__ void q6_load(const uint8_t *b, int t, Q6Words &q) {
     if (b == nullptr) {
@@ -2196,34 +2226,52 @@ __device__ __forceinline__ void q6_load(const uint8_t *b, int t, Q6Words &q) {
         q.d = 0.0f;
         return;
     }
-    // every load is issued before any is used; a block at an address = 2 (mod 4) takes each word from
-    // its two aligned neighbours
-    const bool odd = (reinterpret_cast<uintptr_t>(b) & 3u) != 0;
-    const uint8_t *a = odd ? b - 2 : b;
+    // five 16-byte pieces (ql at lo_off and lo_off + 64, qh at hi_off and hi_off + 32, the scales at 192),
+    // all at the block's offset sh within their aligned 16-byte windows: every window is loaded before
+    // any word is taken apart.  A window holds at least one byte of the block, so it stays inside any
+    // allocation of 16-byte granularity.
     const int lo_off = 32 * (t >> 1) + 16 * (t & 1), hi_off = 128 + 16 * (t & 1);
-    uint32_t w0[20], w1[20];
+    const uintptr_t ab = reinterpret_cast<uintptr_t>(b);
+    const int sh = static_cast<int>(ab & 15u);
+    const uint8_t *base = reinterpret_cast<const uint8_t *>(ab - static_cast<uintptr_t>(sh));
+    const int offs[5] = {lo_off, lo_off + 64, hi_off, hi_off + 32, 192};
+    uint32_t w[5][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int o = lo_off + 64 * (i >> 2) + 4 * (i & 3);
-        w0[i] = ldg32(a + o);
-        w1[i] = odd ? ldg32(a + o + 4) : 0u;
-        const int h = hi_off + 32 * (i >> 2) + 4 * (i & 3);
-        w0[8 + i] = ldg32(a + h);
-        w1[8 + i] = odd ? ldg32(a + h + 4) : 0u;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        w0[16 + i] = ldg32(a + 192 + 4 * i);
-        w1[16 + i] = odd ? ldg32(a + 196 + 4 * i) : 0u;
+    for (int c = 0; c < 5; ++c) {
+        const uint4 v0 = ldg_nc_v4(base + offs[c]);
+        const uint4 v1 = sh ? ldg_nc_v4(base + offs[c] + 16) : make_uint4(0u, 0u, 0u, 0u);
+        w[c][0] = v0.x;
+        w[c][1] = v0.y;
+        w[c][2] = v0.z;
+        w[c][3] = v0.w;
+        w[c][4] = v1.x;
+        w[c][5] = v1.y;
+        w[c][6] = v1.z;
+        w[c][7] = v1.w;
     }
     const uint32_t dw = ldg_nc_u16(b + 208);
+    uint32_t *dst[5] = {q.ql, q.ql + 4, q.qh, q.qh + 4, q.sc};
+    const bool half = (sh & 2) != 0;
+    switch (sh >> 2) {
+        case 0:
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        q.ql[i] = odd ? __funnelshift_r(w0[i], w1[i], 16) : w0[i];
-        q.qh[i] = odd ? __funnelshift_r(w0[8 + i], w1[8 + i], 16) : w0[8 + i];
+            for (int c = 0; c < 5; ++c) q6_pick4<0>(w[c], half, dst[c]);
+            break;
+        case 1:
+#pragma unroll
+            for (int c = 0; c < 5; ++c) q6_pick4<1>(w[c], half, dst[c]);
+            break;
+        case 2:
+#pragma unroll
+            for (int c = 0; c < 5; ++c) q6_pick4<2>(w[c], half, dst[c]);
+            break;
+        default:
+#pragma unroll
+            for (int c = 0; c < 5; ++c) q6_pick4<3>(w[c], half, dst[c]);
+            break;
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) q.sc[i] = (odd ? __funnelshift_r(w0[16 + i], w1[16 + i], 16) : w0[16 + i]) ^ 0x80808080u;
+    for (int i = 0; i < 4; ++i) q.sc[i] ^= 0x80808080u;
     q.d = half_bits_to_float(dw);
 }
 
@@ -2236,8 +2284,9 @@ __device__ __forceinline__ float q6_ds(uint32_t scx, uint32_t sel, float d) {
 // Unit u (one 210-byte super-block) of two rows for Q6_K.  Per half s, lane t
 // accumulates its two 16-value groups (quarter c = t >> 1 and c + 2, half
 // lh = t & 1) over 8 mma and scales them once: groups 8s + t and 8s + t + 4.
-__device__ __forceinline__ void x16_q6k(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
-                                        const XLane &L, float acc[2]) {
+template <int MT>
+__device__ __forceinline__ void x16_q6k(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs, int xstride,
+                                        const XLane &L, float acc[MT][2]) {
     Q6Words A, B;
     q6_load(ra ? ra + 210 * u : nullptr, L.t, A);
     q6_load(rb ? rb + 210 * u : nullptr, L.t, B);
@@ -2245,10 +2294,12 @@ __device__ __forceinline__ void x16_q6k(const uint8_t *ra, const uint8_t *rb, in
     const int c = L.t >> 1;
     const uint32_t shl = static_cast<uint32_t>(4 - 2 * c), shr = static_cast<uint32_t>(2 * c);
     const uint32_t sel = 0x7540u + static_cast<uint32_t>(L.t);
+#pragma unroll 1
+    for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
         // x of this lane's group (quarter c) or of quarter c + 2 (64 values on) for the high-slot lanes
-        const uint8_t *xb = xs + 2 * (256 * u + 128 * s + 32 * c + 16 * (L.t & 1)) + (L.b1on ? 128 : 0);
+        const uint8_t *xb = xs + m * xstride + 2 * (256 * u + 128 * s + 32 * c + 16 * (L.t & 1)) + (L.b1on ? 128 : 0);
         const uint4 x0 = *reinterpret_cast<const uint4 *>(xb), x1 = *reinterpret_cast<const uint4 *>(xb + 16);
         const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
         float D[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -2271,15 +2322,16 @@ __device__ __forceinline__ void x16_q6k(const uint8_t *ra, const uint8_t *rb, in
                 mma_f16_16816(D, a, b & L.b0on, b & L.b1on);
             }
         }
-        acc[0] += fmaf(q6_ds(A.sc[2 * s], sel, A.d), D[0], q6_ds(A.sc[2 * s + 1], sel, A.d) * D[1]);
-        acc[1] += fmaf(q6_ds(B.sc[2 * s], sel, B.d), D[2], q6_ds(B.sc[2 * s + 1], sel, B.d) * D[3]);
+        acc[m][0] += fmaf(q6_ds(A.sc[2 * s], sel, A.d), D[0], q6_ds(A.sc[2 * s + 1], sel, A.d) * D[1]);
+        acc[m][1] += fmaf(q6_ds(B.sc[2 * s], sel, B.d), D[2], q6_ds(B.sc[2 * s + 1], sel, B.d) * D[3]);
     }
 }
 
 // Unit u (8 blocks = 272 bytes, 256 values) of two rows for Q8_0: lane t takes blocks 2t and 2t + 1.
 // int8 codes as exact fp16: 1024 + 128 + q by byte permutes, minus 1152 by one f16x2 subtract.
-__device__ __forceinline__ void x16_q80(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
-                                        const XLane &L, float acc[2]) {
+template <int MT>
+__device__ __forceinline__ void x16_q80(const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs, int xstride,
+                                        const XLane &L, float acc[MT][2]) {
     const uint8_t *ba = ra ? ra + 272 * u + 68 * L.t : nullptr, *bb = rb ? rb + 272 * u + 68 * L.t : nullptr;
     uint32_t wa[17], wb[17];
 #pragma unroll
@@ -2290,8 +2342,10 @@ __device__ __forceinline__ void x16_q80(const uint8_t *ra, const uint8_t *rb, in
     // block 2t: d = bytes 0-1, q = bytes 2..33; block 2t + 1: d = bytes 34-35, q = bytes 36..67
     const float da0 = half_bits_to_float(wa[0]), da1 = half_bits_to_float(wa[8] >> 16);
     const float db0 = half_bits_to_float(wb[0]), db1 = half_bits_to_float(wb[8] >> 16);
-    const uint8_t *xb = xs + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
     const uint32_t k1152 = 0x64806480u;  // fp16 1152 = 1024 + 128
+#pragma unroll 1
+    for (int m = 0; m < MT; ++m) {
+    const uint8_t *xb = xs + m * xstride + 2 * (256 * u + 64 * L.t) + (L.b1on ? 64 : 0);
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -2313,33 +2367,36 @@ __device__ __forceinline__ void x16_q80(const uint8_t *ra, const uint8_t *rb, in
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) d[i] += e[i];
-    acc[0] += fmaf(da0, d[0], da1 * d[1]);
-    acc[1] += fmaf(db0, d[2], db1 * d[3]);
-}
-
-__device__ __forceinline__ void x16_unit(int fmt, const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
-                                         const float *xsum, const XLane &L, float acc[2]) {
-    if (fmt == T2C_Q4_K) {
-        x16_q4k(ra, rb, u, xs, xsum, L, acc);
-    } else if (fmt == T2C_Q6_K) {
-        x16_q6k(ra, rb, u, xs, L, acc);
-    } else {
-        x16_q80(ra, rb, u, xs, L, acc);
+    acc[m][0] += fmaf(da0, d[0], da1 * d[1]);
+    acc[m][1] += fmaf(db0, d[2], db1 * d[3]);
     }
 }
 
+template <int MT>
+__device__ __forceinline__ void x16_unit(int fmt, const uint8_t *ra, const uint8_t *rb, int u, const uint8_t *xs,
+                                         const float *xsum, int K, const XLane &L, float acc[MT][2]) {
+    if (fmt == T2C_Q4_K) {
+        x16_q4k<MT>(ra, rb, u, xs, xsum, 2 * K, K >> 5, L, acc);
+    } else if (fmt == T2C_Q6_K) {
+        x16_q6k<MT>(ra, rb, u, xs, 2 * K, L, acc);
+    } else {
+        x16_q80<MT>(ra, rb, u, xs, 2 * K, L, acc);
+    }
+}
+
+template <int MT>
 __global__ void __launch_bounds__(kXThreads, 2) qmv_x16_kernel(const __grid_constant__ QParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int K = p.K;
-    uint8_t *xs = smem;
-    float *xsum = reinterpret_cast<float *>(smem + 2 * K);
-    float *red = xsum + (K >> 5);
-    float *part = red + kXWarps;  // [warp][gate/up][16 rows]
+    uint8_t *xs = smem;                                          // [MT][K] fp16
+    float *xsum = reinterpret_cast<float *>(smem + MT * 2 * K);  // [MT][K / 32]
+    float *red = xsum + MT * (K >> 5);                           // [MT][warps]
+    float *part = red + MT * kXWarps;                            // [warp][token][gate/up][16 rows]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const XLane L = x_lane(lane);
     pdl_wait();
     pdl_trigger();
-    x16_prepare(p, xs, xsum, red);
+    x16_prepare<MT>(p, xs, xsum, red);
     const bool swiglu = p.mode == MODE_SWIGLU;
     const int wpb = p.wpb, bpc = kXWarps / wpb;
     const int grp = warp / wpb, wig = warp - grp * wpb;
@@ -2347,7 +2404,9 @@ __global__ void __launch_bounds__(kXThreads, 2) qmv_x16_kernel(const __grid_cons
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * bpc; base < p.total_rowsets;
          base += static_cast<int64_t>(gridDim.x) * bpc) {
         const int64_t tile = base + grp;
-        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        float acc[MT][2][2];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[m][0][0] = acc[m][0][1] = acc[m][1][0] = acc[m][1][1] = 0.0f;
         if (tile < p.total_rowsets) {
             const int si = swiglu ? 0 : stream_of(p, tile);
             const int64_t row0 = (tile - p.s[si].rs_begin) * kMmaRows;
@@ -2357,44 +2416,68 @@ __global__ void __launch_bounds__(kXThreads, 2) qmv_x16_kernel(const __grid_cons
                 const int64_t na = row0 + L.g, nb = row0 + L.g + 8;
                 const uint8_t *ra = na < st.n ? st.w + na * st.row_bytes : nullptr;
                 const uint8_t *rb = nb < st.n ? st.w + nb * st.row_bytes : nullptr;
-                float a2[2] = {0.0f, 0.0f};
+                float a2[MT][2];
+#pragma unroll
+                for (int m = 0; m < MT; ++m) a2[m][0] = a2[m][1] = 0.0f;
 #pragma unroll 1
-                for (int u = wig; u < units; u += wpb) x16_unit(st.fmt, ra, rb, u, xs, xsum, L, a2);
-                acc[wi][0] = a2[0];
-                acc[wi][1] = a2[1];
+                for (int u = wig; u < units; u += wpb) x16_unit<MT>(st.fmt, ra, rb, u, xs, xsum, K, L, a2);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    acc[m][wi][0] = a2[m][0];
+                    acc[m][wi][1] = a2[m][1];
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 2; ++r)
+            for (int m = 0; m < MT; ++m)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 1);
-                    acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
-                }
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        acc[m][r][h] += __shfl_xor_sync(0xffffffffu, acc[m][r][h], 1);
+                        acc[m][r][h] += __shfl_xor_sync(0xffffffffu, acc[m][r][h], 2);
+                    }
         }
         if (wpb > 1) {
             if (L.t == 0) {
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    part[(warp * 2 + r) * 16 + L.g] = acc[r][0];
-                    part[(warp * 2 + r) * 16 + L.g + 8] = acc[r][1];
-                }
+                for (int m = 0; m < MT; ++m)
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        part[((warp * MT + m) * 2 + r) * 16 + L.g] = acc[m][r][0];
+                        part[((warp * MT + m) * 2 + r) * 16 + L.g + 8] = acc[m][r][1];
+                    }
             }
             __syncthreads();
             if (wig == 0) {
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    float v0 = 0.0f, v1 = 0.0f;
-                    for (int w = warp; w < warp + wpb; ++w) {
-                        v0 += part[(w * 2 + r) * 16 + L.g];
-                        v1 += part[(w * 2 + r) * 16 + L.g + 8];
+                for (int m = 0; m < MT; ++m)
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        float v0 = 0.0f, v1 = 0.0f;
+                        for (int w = warp; w < warp + wpb; ++w) {
+                            v0 += part[((w * MT + m) * 2 + r) * 16 + L.g];
+                            v1 += part[((w * MT + m) * 2 + r) * 16 + L.g + 8];
+                        }
+                        acc[m][r][0] = v0;
+                        acc[m][r][1] = v1;
                     }
-                    acc[r][0] = v0;
-                    acc[r][1] = v1;
-                }
             }
             __syncthreads();
         }
-        if (wig == 0 && tile < p.total_rowsets) mma_finish_block<1>(p, tile, acc, lane);
+        if (wig == 0 && tile < p.total_rowsets) {
+            // every lane of a quad holds all tokens' sums; lane t stores token t (the dense layout the
+            // epilogue expects)
+            float v[2][2] = {{acc[0][0][0], acc[0][0][1]}, {acc[0][1][0], acc[0][1][1]}};
+#pragma unroll
+            for (int m = 1; m < MT; ++m)
+                if (L.t == m) {
+                    v[0][0] = acc[m][0][0];
+                    v[0][1] = acc[m][0][1];
+                    v[1][0] = acc[m][1][0];
+                    v[1][1] = acc[m][1][1];
+                }
+            mma_finish_block<MT>(p, tile, v, lane);
+        }
     }
 }
 
@@ -2856,8 +2939,30 @@ int try_gemm(const QParams &p, int64_t M, cudaStream_t stream, bool &used) {
 }
 
 // Exact fp16-x kernel, one launch per token (any GGUF type, K % 256 == 0).
-int launch_x16(QParams p, int64_t M, cudaStream_t stream) {
+size_t x16_smem_bytes(int MT, int K) {
+    return static_cast<size_t>(MT) * (2 * static_cast<size_t>(K) + static_cast<size_t>(K / 32) * 4) +
+           static_cast<size_t>(MT) * kXWarps * 4 + static_cast<size_t>(kXWarps) * MT * 2 * 16 * 4;
+}
+
+template <int MT>
+int launch_x16_mt(const QParams &p, int64_t tiles, cudaStream_t stream) {
     static bool configured[64] = {false};
+    const size_t smem = x16_smem_bytes(MT, p.K);
+    int rc = ensure_smem_attr(qmv_x16_kernel<MT>, configured[device_slot()]);
+    if (rc) return rc;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmv_x16_kernel<MT>, kXThreads, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    const int bpc = kXWarps / p.wpb;
+    int64_t blocks = (tiles + bpc - 1) / bpc;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+    if (blocks > cap) blocks = cap;
+    return launch_pdl(qmv_x16_kernel<MT>, static_cast<int>(blocks), kXThreads, smem, stream, p);
+}
+
+// Up to 4 tokens per pass (weights read once for all of them); more tokens take passes of 4.
+int launch_x16(QParams p, int64_t M, cudaStream_t stream) {
     const bool swiglu = p.mode == MODE_SWIGLU;
     int64_t tiles = 0;
     for (int i = 0; i < p.nstreams; ++i) {
@@ -2873,31 +2978,25 @@ int launch_x16(QParams p, int64_t M, cudaStream_t stream) {
     int wpb = 1;
     while (wpb < kXWarps && tiles * wpb < want && wpb * 2 <= units) wpb *= 2;
     p.wpb = wpb;
-    const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4 + kXWarps * 4 +
-                        static_cast<size_t>(kXWarps) * 2 * 16 * 4;
-    int rc = ensure_smem_attr(qmv_x16_kernel, configured[device_slot()]);
-    if (rc) return rc;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmv_x16_kernel, kXThreads, smem) != cudaSuccess ||
-        per_sm < 1)
-        per_sm = 1;
-    const int bpc = kXWarps / wpb;
-    int64_t blocks = (tiles + bpc - 1) / bpc;
-    const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
-    if (blocks > cap) blocks = cap;
-    for (int64_t t = 0; t < M; ++t) {
+    int cap = 4;
+    while (cap > 1 && x16_smem_bytes(cap, p.K) > kSmemLimit) cap /= 2;
+    if (x16_smem_bytes(cap, p.K) > kSmemLimit) return set_error(T2C_EUNSUPPORTED, "qmv_x16: K too large");
+    for (int64_t t0 = 0; t0 < M; t0 += cap) {
+        const int mt = static_cast<int>(M - t0 < cap ? M - t0 : cap);
         QParams q = p;
-        q.M = 1;
-        q.x = p.x + t * p.K;
+        q.M = mt;
+        q.x = p.x + t0 * p.K;
         for (int i = 0; i < kMaxStreams; ++i) {
-            if (q.s[i].y != nullptr) q.s[i].y += t * q.s[i].n;
-            if (q.s[i].res != nullptr) q.s[i].res += t * q.s[i].n;
+            if (q.s[i].y != nullptr) q.s[i].y += t0 * q.s[i].n;
+            if (q.s[i].res != nullptr) q.s[i].res += t0 * q.s[i].n;
         }
         if (p.mode == MODE_ARGMAX) {
-            q.ps = p.ps + t * p.G;
-            q.pt = p.pt + t * p.G;
+            q.ps = p.ps + t0 * p.G;
+            q.pt = p.pt + t0 * p.G;
         }
-        rc = launch_pdl(qmv_x16_kernel, static_cast<int>(blocks), kXThreads, smem, stream, q);
+        const int rc = mt == 1 ? launch_x16_mt<1>(q, tiles, stream)
+                       : mt == 2 ? launch_x16_mt<2>(q, tiles, stream)
+                                 : launch_x16_mt<4>(q, tiles, stream);
         if (rc) return rc;
     }
     return T2C_OK;
