@@ -13,6 +13,7 @@ cudaError_t status_qgemm(unsigned int *bits, int clear, cudaStream_t s);
 cudaError_t status_comm(unsigned int *bits, int clear, cudaStream_t s);
 cudaError_t status_asr(unsigned int *bits, int clear, cudaStream_t s);
 cudaError_t status_qbatch(unsigned int *bits, int clear, cudaStream_t s);
+cudaError_t status_attn_tc(unsigned int *bits, int clear, cudaStream_t s);
 
 static thread_local char g_last_error[1024] = "";
 
@@ -67,6 +68,7 @@ extern "C" int t2c_device_status(unsigned int *bits, int clear, void *stream) {
     if (err == cudaSuccess) err = t2c::status_comm(&value, clear, s);
     if (err == cudaSuccess) err = t2c::status_asr(&value, clear, s);
     if (err == cudaSuccess) err = t2c::status_qbatch(&value, clear, s);
+    if (err == cudaSuccess) err = t2c::status_attn_tc(&value, clear, s);
     if (err != cudaSuccess) return t2c::set_error(T2C_ECUDA, "t2c_device_status: %s", cudaGetErrorString(err));
     *bits = value;
     return T2C_OK;

@@ -9,6 +9,12 @@
 #include "common.cuh"
 
 namespace t2c {
+int attn_prefill_umma(const void *q, const void *k_cache, const void *v_cache, void *out, const int32_t *positions,
+                      int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t cb, int64_t cs, int64_t ch, int64_t qb,
+                      int64_t qt, int64_t qh, int64_t ob, int64_t ot, int64_t oh, float scale, cudaStream_t stream);
+}  // namespace t2c
+
+namespace t2c {
 namespace {
 
 __device__ __forceinline__ float4 h4_to_f4(uint2 v) {
@@ -1772,6 +1778,11 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
     if (!aligned(k_cache, 16) || cs % 8 || cb % 8 || ch % 8)
         return set_error(T2C_EINVAL, "attn_prefill: cache rows must be 16-byte aligned");
     const float scale = 1.0f / sqrtf(static_cast<float>(D));
+    if (D == 128) {  // tcgen05 tiles where the operand strides allow them
+        const int rc = attn_prefill_umma(q, k_cache, v_cache, out, positions, B, T, NH, NK, cb, cs, ch, qb, qt, qh, ob,
+                                         ot, oh, scale, as_stream(stream));
+        if (rc != T2C_EUNSUPPORTED) return rc;
+    }
     if (D == 128 && aligned(q, 16) && qb % 8 == 0 && qt % 8 == 0 && qh % 8 == 0 && aligned(out, 4) && ob % 2 == 0 &&
         ot % 2 == 0 && oh % 2 == 0) {
         static bool configured[64] = {};
