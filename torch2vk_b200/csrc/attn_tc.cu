@@ -4,19 +4,20 @@
 //
 // CTA = one warpgroup (128 threads) on (sequence b, head h, 128-query tile);
 // thread r owns query row r of the tile, which is TMEM lane r.  Per 128-key
-// tile j of the cache rows 0 .. positions[b] + (last query of the tile):
-//   S = Q K_j^T   tcgen05.mma kind::f16, M = 128 queries, N = 128 keys,
-//                 K = D in 8 steps, fp32 accumulators in TMEM columns 0..127;
+// tile j of 64 cache rows up to positions[b] + (last query of the tile):
+//   S = Q K_j^T   tcgen05.mma kind::f16, M = 128 queries, N = 64 keys,
+//                 K = D in 8 steps, fp32 accumulators in TMEM columns 0..63;
 //   online softmax per row in fp32 (log2 domain) from tcgen05.ld of S, P = fp16
 //                 exp2(s - m) written to shared memory as the next A operand;
 //                 when a row's maximum moves, its O row in TMEM is rescaled
 //                 (tcgen05.ld / st);
-//   O += P V_j    M = 128, N = D (V read MN-major), K = 128 keys in 8 steps,
+//   O += P V_j    M = 128, N = D (V read MN-major), K = 64 keys in 4 steps,
 //                 TMEM columns 128..255.
 // Q, K, V and P tiles sit in shared memory in the 128-byte-swizzled layout the
-// UMMA descriptors name ([2 chunks of 64 values][128 rows][128 B], 16-byte
-// unit u of row r at ((u ^ r) mod 8)); K / V tiles are double-buffered with
-// cp.async (rows past the cache zero-filled).  One thread issues the MMAs; a
+// UMMA descriptors name ([chunks of 64 values][rows][128 B], 16-byte unit u of
+// row r at ((u ^ r) mod 8)); K / V tiles are double-buffered with cp.async
+// (rows past the cache zero-filled).  112 KB of shared memory and 256 TMEM
+// columns per CTA: two CTAs per SM, so one's softmax overlaps the other's MMAs.  One thread issues the MMAs; a
 // commit per tile signals S (and with it every earlier MMA) to the warpgroup
 // through an mbarrier whose waits are bounded.
 #include <float.h>
@@ -27,12 +28,17 @@ namespace t2c {
 namespace {
 
 constexpr int kUQ = 128;                 // queries per CTA (UMMA M, TMEM lanes)
-constexpr int kUK = 128;                 // keys per tile (UMMA N of S, K of P V)
-constexpr int kUTile = 128 * 128 * 2;    // one swizzled 128 x 128 fp16 tile
-constexpr int kUSmem = 1024 + 6 * kUTile + 64;  // Q, K x 2, V x 2, P, barrier
+constexpr int kUK = 64;                  // keys per tile (UMMA N of S, K of P V)
+constexpr int kUQTile = kUQ * 128 * 2;   // Q: 128 rows x 128 values, two 64-value chunks of 16 KB
+constexpr int kUKTile = kUK * 128 * 2;   // K or V: 64 rows x 128 values, two chunks of 8 KB
+constexpr int kUPTile = kUQ * kUK * 2;   // P: 128 rows x 64 keys, one chunk
+// Q, K x 2, V x 2, P, barrier + TMEM slot: 112 KB + 64 B, so two CTAs share an SM (the kernel checks
+// that the dynamic shared window starts on the 1024-byte boundary the swizzle atoms need)
+constexpr int kUSmem = kUQTile + 4 * kUKTile + kUPTile + 64;
 
-__device__ __forceinline__ uint32_t sw_off(int r, int u) {
-    return static_cast<uint32_t>((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+// 16-byte unit u (0..15) of row r in a tile of two 64-value chunks `chunk` bytes apart, 128-byte swizzle
+__device__ __forceinline__ uint32_t sw_off(int r, int u, int chunk) {
+    return static_cast<uint32_t>((u >> 3) * chunk + r * 128 + (((u & 7) ^ (r & 7)) << 4));
 }
 
 // K-major operand, 128-byte swizzle: 8-row groups 1024 B apart.
@@ -42,10 +48,10 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t saddr) {
            (static_cast<uint64_t>(2u) << 61);
 }
 
-// MN-major operand, 128-byte swizzle: 64-value atoms along N 16 KB apart (leading), 8-row K groups
-// 1024 B apart (stride).
+// MN-major operand, 128-byte swizzle: 64-value atoms along N one V chunk (8 KB) apart (leading), 8-row
+// K groups 1024 B apart (stride).
 __device__ __forceinline__ uint64_t desc_mn(uint32_t saddr) {
-    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(16384u >> 4) << 16) |
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(uint32_t(kUKTile / 2) >> 4) << 16) |
            (static_cast<uint64_t>(1024u >> 4) << 32) | (static_cast<uint64_t>(1u) << 46) |
            (static_cast<uint64_t>(2u) << 61);
 }
@@ -102,17 +108,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
+__global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     __half *__restrict__ out, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
     int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh,
     float scale_log2) {
-    extern __shared__ __align__(1024) uint8_t u_smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(u_smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t qs = smem_u32(smem);
-    const uint32_t ks0 = qs + kUTile, vs0 = qs + 3 * kUTile, ps = qs + 5 * kUTile;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + 6 * kUTile);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 6 * kUTile + 16);
+    const uint32_t ks0 = qs + kUQTile, vs0 = ks0 + 2 * kUKTile, ps = vs0 + 2 * kUKTile;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kUQTile + 4 * kUKTile + kUPTile);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 2);
+    if (qs & 1023u) {  // swizzle atoms need 1024-byte alignment: report, compute nothing
+        if (threadIdx.x == 0) report_device_error(T2C_EUNSUPPORTED);
+        return;
+    }
     const int tid = threadIdx.x, warp = tid >> 5;
     const int qtiles = (T + kUQ - 1) / kUQ;
     const int qt = qtiles - 1 - static_cast<int>(blockIdx.x % qtiles);  // heaviest tiles first
@@ -153,28 +162,28 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
             const uint4 v = tq < T ? src[u] : make_uint4(0u, 0u, 0u, 0u);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(qs + sw_off(row, u)), "r"(v.x), "r"(v.y),
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(qs + sw_off(row, u, kUQTile / 2)), "r"(v.x), "r"(v.y),
                          "r"(v.z), "r"(v.w)
                          : "memory");
         }
     }
-    // key / value tile j into buffer j & 1: thread r copies key row j * 128 + r of K and of V
+    // key / value tile j into buffer j & 1: threads 0..63 copy key rows j * 64 + r of K, 64..127 those of V
     auto load_kv = [&](int j) {
-        const int key = j * kUK + row;
+        const int r = row & (kUK - 1);
+        const int key = j * kUK + r;
         const bool in = key <= last_key;
         const int64_t off = in ? static_cast<int64_t>(key) * cs : 0;
-        const uint32_t kd = ks0 + (j & 1) * kUTile, vd = vs0 + (j & 1) * kUTile;
+        const uint32_t dst = (row < kUK ? ks0 : vs0) + (j & 1) * kUKTile;
+        const __half *src = (row < kUK ? kbase : vbase) + off;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            cp16(kd + sw_off(row, u), kbase + off + 8 * u, in ? 16u : 0u);
-            cp16(vd + sw_off(row, u), vbase + off + 8 * u, in ? 16u : 0u);
-        }
+        for (int u = 0; u < 16; ++u) cp16(dst + sw_off(r, u, kUKTile / 2), src + 8 * u, in ? 16u : 0u);
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     load_kv(0);
 
     const uint32_t idesc_s = (1u << 4) | (static_cast<uint32_t>(kUK >> 3) << 17) | (static_cast<uint32_t>(kUQ >> 4) << 24);
-    const uint32_t idesc_o = idesc_s | (1u << 16);  // B = V read MN-major
+    // P V: N = D = 128, B = V read MN-major
+    const uint32_t idesc_o = (1u << 4) | (1u << 16) | (128u >> 3 << 17) | (static_cast<uint32_t>(kUQ >> 4) << 24);
     float m_run = -FLT_MAX, l_run = 0.0f;
     bool failed = false;
     int issued = 0;  // commits so far (uniform over the CTA)
@@ -182,13 +191,14 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
-        const uint32_t kt = ks0 + (j & 1) * kUTile, vt = vs0 + (j & 1) * kUTile;
+        const uint32_t kt = ks0 + (j & 1) * kUKTile, vt = vs0 + (j & 1) * kUKTile;
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
-                const uint32_t ko = static_cast<uint32_t>((s >> 2) * 16384 + 32 * (s & 3));
-                umma(tmem, desc_k(qs + ko), desc_k(kt + ko), idesc_s, s > 0);
+                const uint32_t qo = static_cast<uint32_t>((s >> 2) * (kUQTile / 2) + 32 * (s & 3));
+                const uint32_t ko = static_cast<uint32_t>((s >> 2) * (kUKTile / 2) + 32 * (s & 3));
+                umma(tmem, desc_k(qs + qo), desc_k(kt + ko), idesc_s, s > 0);
             }
             commit(bar);
         }
@@ -204,14 +214,14 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
         if (j + 1 < ntiles) load_kv(j + 1);
         const int k0 = j * kUK;
         const bool diag = k0 + kUK - 1 > base + q0;  // some key of the tile is past some query of the CTA
-        // the whole S row (128 fp32) in registers: four loads, one wait
-        uint32_t sv[128];
+        // the whole S row (64 fp32) in registers: two loads, one wait
+        uint32_t sv[kUK];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) ld32_nowait(lane_base + static_cast<uint32_t>(32 * c), sv + 32 * c);
+        for (int c = 0; c < kUK / 32; ++c) ld32_nowait(lane_base + static_cast<uint32_t>(32 * c), sv + 32 * c);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         float mx = -FLT_MAX;
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < kUK; ++i) {
             const float x = __uint_as_float(sv[i]) * scale_log2;
             const bool vis = !diag || k0 + i <= qpos;
             sv[i] = __float_as_uint(vis ? x : -FLT_MAX);
@@ -221,7 +231,7 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
         const float corr = m_run == -FLT_MAX ? 0.0f : exp2f(m_run - m_new);
         float lsum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < kUK / 16; ++c) {
             float p[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -229,8 +239,8 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
                 p[i] = x == -FLT_MAX ? 0.0f : exp2f(x - m_new);
                 lsum += p[i];
             }
-            // keys 16c .. 16c + 15 = 16-byte units 2c, 2c + 1 of row `row`
-            const uint32_t d0 = ps + sw_off(row, 2 * c), d1 = ps + sw_off(row, 2 * c + 1);
+            // keys 16c .. 16c + 15 = 16-byte units 2c, 2c + 1 of row `row` (one 64-key chunk)
+            const uint32_t d0 = ps + sw_off(row, 2 * c, kUPTile), d1 = ps + sw_off(row, 2 * c + 1, kUPTile);
             asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(d0), "r"(pack2(p[0], p[1])),
                          "r"(pack2(p[2], p[3])), "r"(pack2(p[4], p[5])), "r"(pack2(p[6], p[7]))
                          : "memory");
@@ -259,11 +269,9 @@ __global__ void __launch_bounds__(128, 1) attn_prefill_umma_kernel(
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                const uint32_t po = static_cast<uint32_t>((s >> 2) * 16384 + 32 * (s & 3));
-                umma(tmem + 128u, desc_k(ps + po), desc_mn(vt + static_cast<uint32_t>(2048 * s)), idesc_o,
-                     j > 0 || s > 0);
-            }
+            for (int s = 0; s < kUK / 16; ++s)
+                umma(tmem + 128u, desc_k(ps + static_cast<uint32_t>(32 * s)), desc_mn(vt + static_cast<uint32_t>(2048 * s)),
+                     idesc_o, j > 0 || s > 0);
         }
     }
     // the last P V (or, after a timeout, whatever is in flight) before O is read and TMEM is freed
