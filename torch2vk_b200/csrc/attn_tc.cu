@@ -108,11 +108,15 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// MASKED: keys [0, S) under an additive fp16 mask (sequence b's element (t, key) at mask + b * m_sb +
+// t * m_st + key; values <= -FLT_MAX / 2 hide the key) instead of the causal rule.  F32IO: fp32 q and
+// output (rounded to fp16 for the tensor cores on the way in).
+template <bool MASKED, bool F32IO>
 __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
-    const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
-    __half *__restrict__ out, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
+    const void *__restrict__ qv, const __half *__restrict__ kc, const __half *__restrict__ vc,
+    void *__restrict__ outv, const int32_t *__restrict__ positions, int T, int NH, int NK, int64_t cb, int64_t cs,
     int64_t ch, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t o_sb, int64_t o_st, int64_t o_sh,
-    float scale_log2) {
+    float scale_log2, const __half *__restrict__ mask, int64_t m_sb, int64_t m_st, int S) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t qs = smem_u32(smem);
     const uint32_t ks0 = qs + kUQTile, vs0 = ks0 + 2 * kUKTile, ps = vs0 + 2 * kUKTile;
@@ -146,9 +150,9 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
     pdl_wait();
     pdl_trigger();
 
-    const int base = positions[b];
+    const int base = MASKED ? 0 : positions[b];
     const int q0 = qt * kUQ;
-    const int last_key = base + min(T - 1, q0 + kUQ - 1);
+    const int last_key = MASKED ? S - 1 : base + min(T - 1, q0 + kUQ - 1);
     const int ntiles = last_key / kUK + 1;
     const int row = tid;
     const int qpos = base + q0 + row;  // keys <= qpos are visible to this row
@@ -158,10 +162,19 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
     // Q row -> swizzled tile (rows past T are zero)
     {
         const int tq = q0 + row;
-        const uint4 *src = reinterpret_cast<const uint4 *>(q + b * q_sb + static_cast<int64_t>(tq) * q_st + h * q_sh);
+        const int64_t qoff = b * q_sb + static_cast<int64_t>(tq) * q_st + h * q_sh;
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const uint4 v = tq < T ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (tq < T) {
+                if constexpr (F32IO) {
+                    const float4 a = reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + qoff)[2 * u];
+                    const float4 c = reinterpret_cast<const float4 *>(static_cast<const float *>(qv) + qoff)[2 * u + 1];
+                    v = make_uint4(pack2(a.x, a.y), pack2(a.z, a.w), pack2(c.x, c.y), pack2(c.z, c.w));
+                } else {
+                    v = reinterpret_cast<const uint4 *>(static_cast<const __half *>(qv) + qoff)[u];
+                }
+            }
             asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(qs + sw_off(row, u, kUQTile / 2)), "r"(v.x), "r"(v.y),
                          "r"(v.z), "r"(v.w)
                          : "memory");
@@ -220,14 +233,29 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
         for (int c = 0; c < kUK / 32; ++c) ld32_nowait(lane_base + static_cast<uint32_t>(32 * c), sv + 32 * c);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         float mx = -FLT_MAX;
+        if constexpr (MASKED) {
+            // this row's 64 mask values of the tile (the last real query row for padding rows)
+            const __half *mrow = mask + b * m_sb + static_cast<int64_t>(min(q0 + row, T - 1)) * m_st;
 #pragma unroll
-        for (int i = 0; i < kUK; ++i) {
-            const float x = __uint_as_float(sv[i]) * scale_log2;
-            const bool vis = !diag || k0 + i <= qpos;
-            sv[i] = __float_as_uint(vis ? x : -FLT_MAX);
-            mx = fmaxf(mx, vis ? x : -FLT_MAX);
+            for (int i = 0; i < kUK; ++i) {
+                const int key = k0 + i;
+                const float mv = key < S ? __half2float(mrow[key]) : -FLT_MAX;
+                const bool vis = mv > -1.7014117e38f;
+                const float x = fmaf(mv, 1.4426950408889634f, __uint_as_float(sv[i]) * scale_log2);
+                sv[i] = __float_as_uint(vis ? x : -FLT_MAX);
+                mx = fmaxf(mx, vis ? x : -FLT_MAX);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kUK; ++i) {
+                const float x = __uint_as_float(sv[i]) * scale_log2;
+                const bool vis = !diag || k0 + i <= qpos;
+                sv[i] = __float_as_uint(vis ? x : -FLT_MAX);
+                mx = fmaxf(mx, vis ? x : -FLT_MAX);
+            }
         }
         const float m_new = fmaxf(m_run, mx);
+        // a row with nothing visible yet keeps m = -FLT_MAX and l = 0 (its P row is all zero)
         const float corr = m_run == -FLT_MAX ? 0.0f : exp2f(m_run - m_new);
         float lsum = 0.0f;
 #pragma unroll
@@ -284,12 +312,20 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int tq = q0 + row;
         const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-        uint4 *dst = reinterpret_cast<uint4 *>(out + b * o_sb + static_cast<int64_t>(tq) * o_st + h * o_sh);
+        const int64_t ooff = b * o_sb + static_cast<int64_t>(tq) * o_st + h * o_sh;
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(outv) + ooff);
+        float4 *dstf = reinterpret_cast<float4 *>(static_cast<float *>(outv) + ooff);
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
             uint32_t v[16];
             ld16(lane_base + 128u + static_cast<uint32_t>(16 * c), v);
-            if (tq < T) {
+            if (F32IO && tq < T) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    dstf[4 * c + i] = make_float4(__uint_as_float(v[4 * i]) * inv, __uint_as_float(v[4 * i + 1]) * inv,
+                                                  __uint_as_float(v[4 * i + 2]) * inv,
+                                                  __uint_as_float(v[4 * i + 3]) * inv);
+            } else if (tq < T) {
                 const float f[16] = {__uint_as_float(v[0]),  __uint_as_float(v[1]),  __uint_as_float(v[2]),
                                      __uint_as_float(v[3]),  __uint_as_float(v[4]),  __uint_as_float(v[5]),
                                      __uint_as_float(v[6]),  __uint_as_float(v[7]),  __uint_as_float(v[8]),
@@ -312,24 +348,35 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
 
 }  // namespace
 
-// Launches the tcgen05 prefill attention for D = 128; T2C_EUNSUPPORTED when the strides or alignment do
-// not suit it (the caller then takes the mma.sync kernel).
+// Launches the tcgen05 prefill attention for D = 128 (causal from positions[b], or with an additive
+// mask when `mask` is given: keys [0, S)); T2C_EUNSUPPORTED when the strides or alignment do not suit it
+// (the caller then takes the mma.sync kernel).
 int attn_prefill_umma(const void *q, const void *k_cache, const void *v_cache, void *out, const int32_t *positions,
                       int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t cb, int64_t cs, int64_t ch, int64_t qb,
-                      int64_t qt, int64_t qh, int64_t ob, int64_t ot, int64_t oh, float scale, cudaStream_t stream) {
+                      int64_t qt, int64_t qh, int64_t ob, int64_t ot, int64_t oh, float scale, cudaStream_t stream,
+                      const void *mask, int64_t m_sb, int64_t m_st, int64_t S, bool f32io) {
     const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out) || qb % 8 || qt % 8 || qh % 8 || ob % 8 ||
-        ot % 8 || oh % 8 || cb % 8 || cs % 8 || ch % 8)
+    const int64_t qa = f32io ? 4 : 8;  // elements per 16 bytes of q / out
+    if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out) || qb % qa || qt % qa || qh % qa || ob % qa ||
+        ot % qa || oh % qa || cb % 8 || cs % 8 || ch % 8)
         return T2C_EUNSUPPORTED;
-    static bool configured[64] = {};
+    if (mask == nullptr && (positions == nullptr || f32io)) return T2C_EUNSUPPORTED;
+    static bool configured[4][64] = {};
     int device = 0;
     cudaGetDevice(&device);
     const int slot = device < 0 ? 0 : (device > 63 ? 63 : device);
-    if (!configured[slot]) {
-        if (cudaFuncSetAttribute(attn_prefill_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kUSmem) !=
-            cudaSuccess)
+    const int variant = (mask != nullptr ? 2 : 0) + (f32io ? 1 : 0);
+    void (*kern)(const void *, const __half *, const __half *, void *, const int32_t *, int, int, int, int64_t,
+                 int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float, const __half *, int64_t,
+                 int64_t, int) = variant == 0   ? attn_prefill_umma_kernel<false, false>
+                                 : variant == 2 ? attn_prefill_umma_kernel<true, false>
+                                 : variant == 3 ? attn_prefill_umma_kernel<true, true>
+                                                : nullptr;
+    if (kern == nullptr) return T2C_EUNSUPPORTED;
+    if (!configured[variant][slot]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kUSmem) != cudaSuccess)
             return set_error(T2C_ECUDA, "attn_prefill: cudaFuncSetAttribute failed");
-        configured[slot] = true;
+        configured[variant][slot] = true;
     }
     const int64_t tiles = (T + kUQ - 1) / kUQ;
     cudaLaunchConfig_t cfg = {};
@@ -343,9 +390,9 @@ int attn_prefill_umma(const void *q, const void *k_cache, const void *v_cache, v
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const cudaError_t err = cudaLaunchKernelEx(
-        &cfg, attn_prefill_umma_kernel, static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
-        static_cast<const __half *>(v_cache), static_cast<__half *>(out), positions, static_cast<int>(T),
-        static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh, 1.4426950408889634f * scale);
+        &cfg, kern, q, static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache), out, positions,
+        static_cast<int>(T), static_cast<int>(NH), static_cast<int>(NK), cb, cs, ch, qb, qt, qh, ob, ot, oh,
+        1.4426950408889634f * scale, static_cast<const __half *>(mask), m_sb, m_st, static_cast<int>(S));
     if (err != cudaSuccess) return set_error(T2C_ECUDA, "attn_prefill (tcgen05) launch: %s", cudaGetErrorString(err));
     return T2C_OK;
 }

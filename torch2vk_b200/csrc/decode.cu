@@ -11,7 +11,8 @@
 namespace t2c {
 int attn_prefill_umma(const void *q, const void *k_cache, const void *v_cache, void *out, const int32_t *positions,
                       int64_t B, int64_t T, int64_t NH, int64_t NK, int64_t cb, int64_t cs, int64_t ch, int64_t qb,
-                      int64_t qt, int64_t qh, int64_t ob, int64_t ot, int64_t oh, float scale, cudaStream_t stream);
+                      int64_t qt, int64_t qh, int64_t ob, int64_t ot, int64_t oh, float scale, cudaStream_t stream,
+                      const void *mask, int64_t m_sb, int64_t m_st, int64_t S, bool f32io);
 }  // namespace t2c
 
 namespace t2c {
@@ -1780,7 +1781,7 @@ extern "C" int t2c_attn_prefill(const void *q, const void *k_cache, const void *
     const float scale = 1.0f / sqrtf(static_cast<float>(D));
     if (D == 128) {  // tcgen05 tiles where the operand strides allow them
         const int rc = attn_prefill_umma(q, k_cache, v_cache, out, positions, B, T, NH, NK, cb, cs, ch, qb, qt, qh, ob,
-                                         ot, oh, scale, as_stream(stream));
+                                         ot, oh, scale, as_stream(stream), nullptr, 0, 0, 0, false);
         if (rc != T2C_EUNSUPPORTED) return rc;
     }
     if (D == 128 && aligned(q, 16) && qb % 8 == 0 && qt % 8 == 0 && qh % 8 == 0 && aligned(out, 4) && ob % 2 == 0 &&
@@ -1830,6 +1831,12 @@ extern "C" int t2c_attn_prefill_masked_f32(const float *q, const void *k_cache, 
         return set_error(T2C_EINVAL, "attn_prefill_masked_f32: alignment");
     if (mask_opt != nullptr && mask_opt_row_stride < (S + 1023) / 1024)
         return set_error(T2C_EINVAL, "attn_prefill_masked_f32: mask_opt rows need %lld words", (long long)((S + 1023) / 1024));
+    {  // tcgen05 tiles (the mask read directly; the classifier's tile skipping is the mma.sync kernel's)
+        const int rc = attn_prefill_umma(q, k_cache, v_cache, out, nullptr, B, T, NH, NK, S * NK * D, NK * D, D,
+                                         T * NH * D, NH * D, D, T * NH * D, NH * D, D, scale, as_stream(stream), mask, 0,
+                                         mask_row_stride, S, true);
+        if (rc != T2C_EUNSUPPORTED) return rc;
+    }
     static bool configured[64] = {};
     const int dev_slot = current_device_slot();
     if (!configured[dev_slot]) {
@@ -1864,6 +1871,13 @@ extern "C" int t2c_attn_masked_gqa(const void *q, const void *k, const void *v, 
             return set_error(T2C_EINVAL, "attn_masked_gqa: q / k / v rows must be 16-byte aligned, out rows 4-byte");
     if (!aligned(q, 16) || !aligned(out, 4) || !aligned(k, 16) || !aligned(v, 16))
         return set_error(T2C_EINVAL, "attn_masked_gqa: alignment");
+    {
+        const int rc = attn_prefill_umma(q, k, v, out, nullptr, B, T, NH, NK, kv_strides[0], kv_strides[1],
+                                         kv_strides[2], q_strides[0], q_strides[1], q_strides[2], o_strides[0],
+                                         o_strides[1], o_strides[2], scale, as_stream(stream), mask, mask_b_stride,
+                                         mask_row_stride, S, false);
+        if (rc != T2C_EUNSUPPORTED) return rc;
+    }
     static bool configured[64] = {};
     const int dev_slot = current_device_slot();
     if (!configured[dev_slot]) {
