@@ -254,8 +254,10 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_umma_kernel(
                 mx = fmaxf(mx, vis ? x : -FLT_MAX);
             }
         }
-        const float m_new = fmaxf(m_run, mx);
-        // a row with nothing visible yet keeps m = -FLT_MAX and l = 0 (its P row is all zero)
+        // The running maximum moves only when a score exceeds it by more than 8 (log2 units): P stays below
+        // 2^8 (exact enough in fp16, far from its range), O is rescaled rarely, and O / l is the same for any
+        // common reference point.  A row with nothing visible yet keeps m = -FLT_MAX and l = 0.
+        const float m_new = (m_run == -FLT_MAX || mx > m_run + 8.0f) ? fmaxf(m_run, mx) : m_run;
         const float corr = m_run == -FLT_MAX ? 0.0f : exp2f(m_run - m_new);
         float lsum = 0.0f;
 #pragma unroll
