@@ -275,6 +275,9 @@ def run_profile(args, local: int) -> None:
     decode: the Qwen3-8B bs1 decode graph (Q4_K linears, Q6_K head), --steps replays.
     decode32: the same at batch 32 on a synthetic 1024-position KV cache.
     prefill: --steps prefills of the 1024-token prompt (batch 1).
+    attnp:  the causal prefill attention of Qwen3-8B (32 Q / 8 KV heads, D 128) over a 2048-token prompt,
+            batch 1 (attn_prefill_umma_kernel), --steps launches.
+    lmhead: the Q6_K LM head (151936 x 4096, fused RMSNorm, argmax partials) at batch 1, --steps launches.
     attn:   the fused decode attention of Qwen3-8B (32 Q / 8 KV heads, D 128) at position 1040 over
             48 layers' KV caches in turn (288 MB, larger than L2), 8 splits per KV head (one
             thread-block cluster, as the decode runner uses), --steps launches.
@@ -347,6 +350,46 @@ def run_profile(args, local: int) -> None:
         cudart.cudaProfilerStart()
         for i in range(args.steps):
             one(i)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "attnp":
+        B, NH, NK, D, S = 1, cfg.heads, cfg.kv_heads, cfg.head_dim, 2048
+        gen = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn(B * S, NH * D, device=dev, generator=gen).half() / 11.3
+        kc = torch.randn(B, S, NK, D, device=dev, generator=gen).half() / 11.3
+        vc = torch.randn(B, S, NK, D, device=dev, generator=gen).half()
+        pos = torch.zeros(B, device=dev, dtype=torch.int32)
+        out = torch.empty_like(q)
+
+        def one() -> None:
+            kernels.attn_prefill(q, kc, vc, pos, batch=B, tokens=S, n_heads=NH, n_kv=NK, head_dim=D, out=out)
+
+        for _ in range(args.warmup):
+            one()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for _ in range(args.steps):
+            one()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "lmhead":
+        gen = torch.Generator(device=dev).manual_seed(0)
+        w = kernels.quantize(torch.randn(cfg.vocab, cfg.hidden, device=dev, generator=gen) * 0.02, "q6_k")
+        nw = torch.ones(cfg.hidden, device=dev)
+        x = torch.randn(1, cfg.hidden, device=dev, generator=gen).half()
+        g = (cfg.vocab + 3) // 4
+        ps = torch.empty(1, g, device=dev)
+        pt = torch.empty(1, g, device=dev, dtype=torch.int32)
+
+        def one() -> None:
+            kernels.lm_head_argmax(x, w, "q6_k", cfg.hidden, norm_weight=nw, partial_scores=ps, partial_tokens=pt)
+
+        for _ in range(args.warmup):
+            one()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for _ in range(args.steps):
+            one()
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
     elif args.profile == "gemm":
@@ -658,7 +701,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "gemm"], default=None,
+    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "attnp", "lmhead", "gemm"],
+                    default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",
                     help="the quantized-linear sweep (one JSON line per shape, M and type) instead of the step")
