@@ -604,6 +604,31 @@ def asr_e2e_figures(dev: torch.device) -> dict:
                         "tokens per clip (seeded weights)", "points": points}
 
 
+def omnivoice_figures(dev: torch.device, stream: torch.cuda.Stream) -> dict:
+    """OmniVoice's LLM forward, the per-step program of its 32-step masked iterative decoding: the CFG pair
+    (batch 2) over the reference export's 85 positions (14 style + 21 text ids + 50 target audio positions),
+    Qwen3-0.6B-shaped LLM (28 layers, Q4_K_M), Q8_0 text / audio embeddings, Q6_K audio heads (8 x 1025),
+    seeded weights; one graph-replayed step timed over 20 replays, and the 32 steps of one utterance
+    (the CFG scoring and token update between steps are not part of this path)."""
+    from torch2vk_b200.omnivoice import OmniVoiceConfig, OmniVoiceLLM, prepare_inputs, random_weights
+
+    cfg = OmniVoiceConfig.omnivoice()
+    w = random_weights(cfg, seed=0, device=str(dev))
+    rng = np.random.default_rng(5)
+    inputs = prepare_inputs(rng.integers(0, cfg.llm.vocab, 14), rng.integers(0, cfg.llm.vocab, 21), 50, cfg)
+    llm = OmniVoiceLLM(cfg, w, batch=2, seq=inputs.input_ids.shape[2])
+    llm.forward(inputs)
+    for _ in range(3):
+        llm.forward()
+    t = events_time(llm.forward, 20, stream)
+    tokens = 2 * inputs.input_ids.shape[2]
+    llm._graph = None
+    del llm, w
+    torch.cuda.empty_cache()
+    return {"workload": "OmniVoice LLM forward (CFG pair, 85 positions, 28 layers, audio heads), seeded weights",
+            "step_ms": t * 1e3, "tokens_per_step": tokens, "tok_s": tokens / t, "utterance_32_steps_ms": 32 * t * 1e3}
+
+
 def qwen3_0_6b_figures(dev: torch.device, stream: torch.cuda.Stream) -> dict:
     """BASELINE config 1 on the fused runner: Qwen3-0.6B architecture (28 layers, hidden 1024, 16 Q / 8 KV
     heads, FFN 3072, vocab 151936, tied-embedding shapes), seeded weights quantized on the GPU (Q4_K
@@ -863,6 +888,7 @@ def main() -> None:
     del arun, atens
     small = qwen3_0_6b_figures(dev, stream) if world == 1 else None
     asr_e2e = asr_e2e_figures(dev) if world == 1 else None
+    omni = omnivoice_figures(dev, stream) if world == 1 else None
     clk = clocks.summary()
     line = {
         "metric": "qwen3_8b_int4_decode_tok_s_bs1",
@@ -911,6 +937,8 @@ def main() -> None:
         line["qwen3_0_6b"] = small
     if asr_e2e is not None:
         line["asr_e2e"] = asr_e2e
+    if omni is not None:
+        line["omnivoice_llm"] = omni
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
