@@ -199,9 +199,18 @@ class AsrEncoderRunner:
         self.device = torch.device(device)
         qn = set(quantized_names(cfg))
         self.w: dict[str, torch.Tensor] = {}
+        # linear weights whose K is not a multiple of 256 (d_model 896 = 28 Q8_0 blocks) get zero blocks up to
+        # the next multiple, so the tcgen05 GEMM (256-value TMA windows) takes them; their inputs are padded
+        # with zeros to match.  The blocks of the real columns are quantized exactly as before.
+        self.kpad: dict[str, int] = {}
         for name, arr in params.items():
             if name in qn:
-                t = torch.from_numpy(q8_rows(arr)).to(self.device)
+                rows = q8_rows(arr)
+                if arr.ndim == 2 and rows.shape[1] % 256:
+                    kp = (rows.shape[1] + 255) // 256 * 256
+                    rows = np.concatenate([rows, np.zeros((rows.shape[0], kp - rows.shape[1]), np.float32)], axis=1)
+                    self.kpad[name] = kp
+                t = torch.from_numpy(np.ascontiguousarray(rows)).to(self.device)
                 self.w[name] = kernels.quantize(t, "q8_0")
             else:
                 self.w[name] = torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)).to(self.device)
@@ -251,29 +260,46 @@ class AsrEncoderRunner:
         n = first["index"].shape[0]
         hd = cfg.head_dim
         scale = 1.0 / math.sqrt(hd)
+        rows = B * n
+        kp = self.kpad.get("layers.0.self_attn.q_proj.weight", d)  # padded width of d-wide linear inputs
+
+        def padded(x: torch.Tensor) -> torch.Tensor:  # [rows, d] -> [rows, kp], zero columns past d
+            if kp == d:
+                return x
+            xp = torch.zeros(rows, kp, dtype=torch.float16, device=x.device)
+            kernels.copy4d(x.view(1, 1, rows, d), xp[:, :d].unsqueeze(0).unsqueeze(0))
+            return xp
+
+        def lin(x: torch.Tensor, name: str, n_out: int, gelu: bool = False) -> torch.Tensor:
+            return kernels.linear_q8_0_bias(x, w[name + ".weight"], w[name + ".bias"], n_out, gelu=gelu)
+
         for i in range(cfg.layers):
             p = f"layers.{i}."
             r = h
-            a = kernels.layer_norm(h, w[p + "self_attn_layer_norm.weight"], w[p + "self_attn_layer_norm.bias"], cfg.eps)
-            q = kernels.linear_q8_0_bias(a, w[p + "self_attn.q_proj.weight"], w[p + "self_attn.q_proj.bias"], d)
-            k = kernels.linear_q8_0_bias(a, w[p + "self_attn.k_proj.weight"], w[p + "self_attn.k_proj.bias"], d)
-            v = kernels.linear_q8_0_bias(a, w[p + "self_attn.v_proj.weight"], w[p + "self_attn.v_proj.bias"], d)
+            a = padded(kernels.layer_norm(h, w[p + "self_attn_layer_norm.weight"], w[p + "self_attn_layer_norm.bias"],
+                                          cfg.eps))
+            q = lin(a, p + "self_attn.q_proj", d)
+            k = lin(a, p + "self_attn.k_proj", d)
+            v = lin(a, p + "self_attn.v_proj", d)
 
-            def heads(z: torch.Tensor) -> torch.Tensor:  # [B n, d] -> [B, H, n, hd] view
-                return z.view(B, n, cfg.heads, hd).permute(0, 2, 1, 3)
+            def heads(z: torch.Tensor) -> torch.Tensor:  # rows of width z.stride(0) -> [B, H, n, hd] view
+                return z.as_strided((B, cfg.heads, n, hd), (n * z.stride(0), hd, z.stride(0), 1))
 
-            o = torch.empty(B * n, d, dtype=torch.float16, device=h.device)
+            # the attention writes straight into the (zero-padded) input of out_proj
+            o = torch.zeros(rows, kp, dtype=torch.float16, device=h.device) if kp != d else \
+                torch.empty(rows, d, dtype=torch.float16, device=h.device)
             kernels.attn_masked(heads(q), heads(k), heads(v), first["mask"], scale=scale, out=heads(o))
-            o = kernels.linear_q8_0_bias(o, w[p + "self_attn.out_proj.weight"], w[p + "self_attn.out_proj.bias"], d)
+            o = lin(o, p + "self_attn.out_proj", d)
             h = kernels.add(r, o)
             r = h
-            a = kernels.layer_norm(h, w[p + "final_layer_norm.weight"], w[p + "final_layer_norm.bias"], cfg.eps)
-            a = kernels.linear_q8_0_bias(a, w[p + "fc1.weight"], w[p + "fc1.bias"], cfg.ffn, gelu=True)
-            a = kernels.linear_q8_0_bias(a, w[p + "fc2.weight"], w[p + "fc2.bias"], d)
+            a = padded(kernels.layer_norm(h, w[p + "final_layer_norm.weight"], w[p + "final_layer_norm.bias"],
+                                          cfg.eps))
+            a = lin(a, p + "fc1", cfg.ffn, gelu=True)
+            a = lin(a, p + "fc2", d)
             h = kernels.add(r, a)
-        h = kernels.layer_norm(h, w["ln_post.weight"], w["ln_post.bias"], cfg.eps)
-        h = kernels.linear_q8_0_bias(h, w["proj1.weight"], w["proj1.bias"], d, gelu=True)
-        return kernels.linear_q8_0_bias(h, w["proj2.weight"], w["proj2.bias"], cfg.output_dim).view(B, n, -1)
+        h = padded(kernels.layer_norm(h, w["ln_post.weight"], w["ln_post.bias"], cfg.eps))
+        h = padded(lin(h, "proj1", d, gelu=True))
+        return lin(h, "proj2", cfg.output_dim).view(B, n, -1)
 
     def flops(self, inputs: AsrInputs) -> float:
         """Multiply-add flops of one forward (convolutions, linears, attention within windows)."""
