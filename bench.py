@@ -283,6 +283,7 @@ def run_profile(args, local: int) -> None:
             thread-block cluster, as the decode runner uses), --steps launches.
     gemm:   the prefill gate/up + SwiGLU GEMM (Q4_K 2 x 12288 x 4096, 1024 tokens) over 4 layers'
             weights in turn (226 MB), --steps launches.
+    gemm32: the same GEMM at 32 tokens (the batch-32 decode's gate/up: stacked 64 + 64-row tiles).
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
             in turn (226 MB, larger than L2), --steps launches.
     """
@@ -392,15 +393,16 @@ def run_profile(args, local: int) -> None:
             one()
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
-    elif args.profile == "gemm":
+    elif args.profile in ("gemm", "gemm32"):
         gen = torch.Generator(device=dev).manual_seed(0)
         pairs = []
         for _ in range(4):
             g = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
             u = kernels.quantize(torch.randn(cfg.intermediate, cfg.hidden, device=dev, generator=gen) * 0.02, "q4_k")
             pairs.append((g, u))
-        x = torch.randn(PROMPT, cfg.hidden, device=dev, dtype=torch.float16)
-        out = torch.empty(PROMPT, cfg.intermediate, device=dev, dtype=torch.float16)
+        tokens = PROMPT if args.profile == "gemm" else BATCH_LARGE
+        x = torch.randn(tokens, cfg.hidden, device=dev, dtype=torch.float16)
+        out = torch.empty(tokens, cfg.intermediate, device=dev, dtype=torch.float16)
         for i in range(args.warmup):
             g, u = pairs[i % 4]
             kernels.linear_swiglu(x, g, u, "q4_k", cfg.hidden, out=out)
@@ -726,7 +728,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "attnp", "lmhead", "gemm"],
+    ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "attnp", "lmhead", "gemm",
+                                          "gemm32"],
                     default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",

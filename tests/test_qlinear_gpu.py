@@ -43,6 +43,20 @@ def _tol_check(got: np.ndarray, ref: np.ndarray, rel: float = 2e-3) -> None:
     assert np.all(err <= bound), f"max err {err.flat[worst]} > bound {bound.flat[worst]} (ref {ref.flat[worst]})"
 
 
+def _swiglu_check(got: np.ndarray, g: np.ndarray, u: np.ndarray, rel: float) -> None:
+    """silu(g) * u where g and u may each differ from the oracle as a plain GEMM output may (rel times
+    |value| + rms), propagated to first order, plus the fp16 rounding of the output."""
+    sg = 1.0 / (1.0 + np.exp(-g))
+    silu, dsilu = g * sg, sg * (1.0 + g * (1.0 - sg))
+    ref = silu * u
+    eg = rel * (np.abs(g) + np.sqrt(np.mean(g * g)))
+    eu = rel * (np.abs(u) + np.sqrt(np.mean(u * u)))
+    bound = np.abs(dsilu * u) * eg + np.abs(silu) * eu + 1e-3 * np.abs(ref) + 1e-6
+    err = np.abs(got.astype(np.float64) - ref)
+    worst = np.argmax(err - bound)
+    assert np.all(err <= bound), f"max err {err.flat[worst]} > bound {bound.flat[worst]} (ref {ref.flat[worst]})"
+
+
 @pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("shape", [(64, 256), (37, 1024), (8, 4096)])
 def test_quantize_bit_exact(oracle, kind, shape):
@@ -248,9 +262,13 @@ def test_q4k_gemm_swiglu_and_norm(oracle, m):
 
 
 @pytest.mark.parametrize("m,n,k,swiglu", [(32, 256, 4096, False), (32, 4096, 4096, False), (32, 512, 2048, True),
-                                          (48, 300, 12288, False)])
+                                          (48, 300, 12288, False),
+                                          # SwiGLU at <= 32 tokens stacks 64 gate rows over 64 up rows in one
+                                          # tile: no split (12288 rows), ragged rows with a split, fewer tokens
+                                          (20, 12288, 4096, True), (32, 1000, 4096, True), (17, 3000, 2048, True)])
 def test_q4k_gemm_cluster_split_k(oracle, m, n, k, swiglu):
-    """Small M with few row tiles: K is split over a CTA cluster and reduced through distributed shared memory."""
+    """Small M with few row tiles: K is split over a CTA cluster and reduced through distributed shared memory;
+    every CTA of the cluster finishes its share of the token columns."""
     from torch2vk_b200 import kernels
 
     rng = np.random.default_rng(n + k + m)
@@ -260,13 +278,35 @@ def test_q4k_gemm_cluster_split_k(oracle, m, n, k, swiglu):
     if swiglu:
         pu = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
         u = x.astype(np.float64) @ oracle.dequantize(pu, "q4_k", k).astype(np.float16).astype(np.float64).T
-        ref = g / (1.0 + np.exp(-g)) * u
         y = kernels.linear_swiglu(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(),
                                   torch.from_numpy(pu).cuda(), "q4_k", k)
+        _swiglu_check(y.float().cpu().numpy(), g, u, rel=4e-3)
+        assert kernels.device_status() == 0
+        return
     else:
         ref = g
         y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(pg).cuda(), "q4_k", k)
     _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(32, 4096, 4096), (24, 1030, 12288), (40, 1000, 2048)])
+def test_q4k_gemm_split_k_residual(oracle, m, n, k):
+    """The residual epilogue after the cluster split-K sum (o_proj / down_proj at batch-32 decode shapes)."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(m * n + k)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    packed = oracle.quantize(_weights(rng, n, k, special=False), "q4_k")
+    r = rng.standard_normal((m, n)).astype(np.float16)
+    ref = x.astype(np.float64) @ oracle.dequantize(packed, "q4_k", k).astype(np.float16).astype(np.float64).T
+    ref = ref + r.astype(np.float64)
+    y = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q4_k", k,
+                       residual=torch.from_numpy(r).cuda())
+    _tol_check(y.float().cpu().numpy(), ref, rel=4e-3)
+    y2 = kernels.linear(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(), "q4_k", k,
+                        residual=torch.from_numpy(r).cuda())
+    assert torch.equal(y, y2)  # the split-K sum runs in rank order: identical bits on every launch
     assert kernels.device_status() == 0
 
 

@@ -97,6 +97,7 @@ struct GemmParams {
     int act;            // 1: erf GELU
     int q6_grouped;     // Q6_K rows of K % 2048 != 0: eight-row group maps (RawFmt<T2C_Q6_K>)
     int row_bytes;
+    int stacked;        // SwiGLU at small token tiles: a CTA's 128 A rows are 64 gate rows over the same 64 up rows
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -282,13 +283,41 @@ __device__ __forceinline__ void argmax4_store(const GemmParams &p, int64_t m, in
     }
 }
 
+// Sum over the ks ranks of a cluster (rank order) of four consecutive fp32 partials at byte
+// offset off of each rank's parked buffer (rbase: the ranks' DSMEM addresses; ks == 1: this
+// CTA's own shared memory).  All loads are issued before the first add.
+__device__ __forceinline__ void sum_parked(const uint32_t rbase[8], int ks, uint32_t off, float out[4]) {
+    float v[8][4];
+#pragma unroll
+    for (int rk = 0; rk < 8; ++rk) {
+        if (rk < ks) {
+            if (ks > 1)
+                asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                             : "=f"(v[rk][0]), "=f"(v[rk][1]), "=f"(v[rk][2]), "=f"(v[rk][3])
+                             : "r"(rbase[rk] + off));
+            else
+                asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                             : "=f"(v[rk][0]), "=f"(v[rk][1]), "=f"(v[rk][2]), "=f"(v[rk][3])
+                             : "r"(rbase[rk] + off));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = 0.0f;
+#pragma unroll
+    for (int rk = 0; rk < 8; ++rk)
+        if (rk < ks) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) out[j] += v[rk][j];
+        }
+}
+
 // Warp roles: warps 0..7 dequantize (thread = weight row tid % 128, nibble
 // half tid / 128), warp 8 issues the MMAs, warp 9 issues the TMA copies.
 // They meet only at mbarriers: raw_full / raw_empty (raw weight stages),
 // x_full (x chunks), a_full (dequantized A buffers, one arrival per dequant
 // warp) and mma_done (tcgen05.commit: A / x buffer free again).
 template <int FMT>
-__global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kThreadsG, 2) qgemm_kernel(const __grid_constant__ GemmParams p) {
     using RF = RawFmt<FMT>;
     constexpr int kRawBytes = kRowsT * RF::kRow;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -302,7 +331,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
     const int tile = static_cast<int>(blockIdx.x / p.ksplit);
     int wi = 0;
     if (p.nw > 1 && tile >= p.tile0[1]) wi = (p.nw > 2 && tile >= p.tile0[2]) ? 2 : 1;
-    const int64_t n0 = static_cast<int64_t>(tile - p.tile0[wi]) * kRowsT;
+    const bool stacked = p.stacked != 0;
+    const int64_t n0 = static_cast<int64_t>(tile - p.tile0[wi]) * (stacked ? kRowsT / 2 : kRowsT);
     const CUtensorMap *wmap = &p.wmap[wi];
     __half *const yout = p.y[wi];
     float *const youtf = p.yf[wi];
@@ -345,6 +375,13 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
                                 static_cast<int>(n0 >> 3), &raw_full[s]);
                 return;
             }
+        }
+        if (stacked) {
+            // gate rows n0 .. n0 + 63 over up rows n0 .. n0 + 63 (64-row boxes)
+            tma_load_2d(raw_ptr + s * kRawBytes, wmap, RF::x_of(sb), static_cast<int>(n0), &raw_full[s]);
+            tma_load_2d(raw_ptr + s * kRawBytes + (kRowsT / 2) * RF::kRow, &p.umap, RF::x_of(sb), static_cast<int>(n0),
+                        &raw_full[s]);
+            return;
         }
         tma_load_2d(raw_ptr + s * kRawBytes, wmap, RF::x_of(sb), static_cast<int>(n0), &raw_full[s]);
         if (swiglu) tma_load_2d(rawup_ptr + s * kRawBytes, &p.umap, sb * 36, static_cast<int>(n0), &raw_full[s]);
@@ -487,10 +524,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
         const bool split_cols = (mt % 32) == 0;
         const int c_begin = split_cols ? (warp >> 2) * (mt / 2) : 0;
         const int c_end = split_cols ? c_begin + mt / 2 : (warp < 4 ? mt : 0);
-        if (p.ksplit > 1) {
-            // cluster split-K: every CTA parks its fp32 partials column-major in its own
-            // shared memory (reusing the operand buffers and raw stages: every copy has landed
-            // and every MMA has completed), the leader sums them over DSMEM
+        if (p.ksplit > 1 || stacked) {
+            // cluster split-K (and the stacked SwiGLU tile, whose gate and up rows sit in
+            // different warps' TMEM lanes): every CTA parks its fp32 partials column-major in
+            // its own shared memory (reusing the operand buffers and raw stages: every copy has
+            // landed and every MMA has completed); the finishing pass below reads them back
             float *red = reinterpret_cast<float *>(smem);
             const int row = 32 * quad + lane;
             if (ok) {
@@ -545,68 +583,80 @@ __global__ void __launch_bounds__(kThreadsG, 1) qgemm_kernel(const __grid_consta
             }
         }
     }
-    if (p.ksplit > 1) {
-        asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-        if (kpart == 0 && warp < kDeqWarps) {
-            const int row = tid & (kRowsT - 1);
-            const int64_t n = n0 + row;
-            float *red = reinterpret_cast<float *>(smem);
-            uint32_t base[8];
+    if (p.ksplit > 1 || stacked) {
+        const int ks = p.ksplit;
+        if (ks > 1)
+            asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        else
+            __syncthreads();
+        // every CTA of the cluster finishes mt / ks of the columns: per item, one column and four
+        // consecutive rows, read as one 16-byte load from each rank's parked partials and summed in
+        // rank order (the same order for every column, so the result does not depend on timing)
+        const uint32_t red = smem_u32(smem);
+        uint32_t rbase[8];
 #pragma unroll
-            for (int rk = 0; rk < 8; ++rk) {
-                base[rk] = 0;
-                if (rk < p.ksplit)
-                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                                 : "=r"(base[rk])
-                                 : "r"(smem_u32(red) + static_cast<uint32_t>(row * 4)), "r"(rk));
+        for (int rk = 0; rk < 8; ++rk) {
+            rbase[rk] = red;
+            if (ks > 1 && rk < ks)
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbase[rk]) : "r"(red), "r"(rk));
+        }
+        const int cpr = mt / ks, cb = kpart * cpr;
+        const int nq = stacked ? kRowsT / 8 : kRowsT / 4;  // row quads finished per column
+        // second operand of an item: the up column (SwiGLU) or the up rows 64 below (stacked)
+        const uint32_t uoff = swiglu ? static_cast<uint32_t>(mt * kRowsT * 4) : stacked ? (kRowsT / 2) * 4u : 0u;
+        for (int it = tid; it < cpr * nq; it += kThreadsG) {
+            const int c = cb + it / nq, r = 4 * (it % nq);
+            const int64_t m = m0 + c, n = n0 + r;
+            float rv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (res != nullptr && !swiglu && !stacked && m < p.M) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < N) rv[j] = __half2float(res[m * N + n + j]);
             }
-            // threads 0..127 and 128..255 take alternate columns
-            for (int c = tid >> 7; c < mt; c += 2) {
-                float gv[8], uv[8];
+            const uint32_t off = static_cast<uint32_t>((c * kRowsT + r) * 4);
+            float g[4], u[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            sum_parked(rbase, ks, off, g);
+            if (uoff) sum_parked(rbase, ks, off + uoff, u);
+            if (p.ps != nullptr) {
+                // best (value, row) of the four rows n .. n + 3; ties keep the lower row
+                float best = (n < N && ok) ? g[0] : -INFINITY;
+                uint32_t tok = static_cast<uint32_t>(n);
 #pragma unroll
-                for (int rk = 0; rk < 8; ++rk) {
-                    gv[rk] = 0.0f;
-                    uv[rk] = 0.0f;
-                    if (rk < p.ksplit) {
-                        asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                                     : "=f"(gv[rk])
-                                     : "r"(base[rk] + static_cast<uint32_t>(c * kRowsT * 4)));
-                        if (swiglu)
-                            asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                                         : "=f"(uv[rk])
-                                         : "r"(base[rk] + static_cast<uint32_t>((mt + c) * kRowsT * 4)));
+                for (int j = 1; j < 4; ++j) {
+                    const float v = (n + j < N && ok) ? g[j] : -INFINITY;
+                    if (v > best) {
+                        best = v;
+                        tok = static_cast<uint32_t>(n + j);
                     }
                 }
-                float g = 0.0f, u = 0.0f;
+                if (n < N && m < p.M) {
+                    p.ps[m * p.G + (n >> 2)] = best;
+                    p.pt[m * p.G + (n >> 2)] = tok;
+                }
+                continue;
+            }
+            if (!ok || m >= p.M) continue;
 #pragma unroll
-                for (int rk = 0; rk < 8; ++rk) {
-                    g += gv[rk];
-                    u += uv[rk];
+            for (int j = 0; j < 4; ++j) {
+                if (n + j >= N) continue;
+                const int64_t o = m * N + n + j;
+                float v = g[j];
+                if (swiglu || stacked) {
+                    v = v / (1.0f + __expf(-v)) * u[j];
+                } else {
+                    if (p.bias != nullptr) v += p.bias[n + j];
+                    if (p.act) v = gelu_erf_g(v);
+                    if (res != nullptr) v += rv[j];
                 }
-                const int64_t m = m0 + c;
-                if (p.ps != nullptr) {
-                    argmax4_store(p, m, n, N, g, ok);
-                    continue;
-                }
-                if (ok && m < p.M && n < N) {
-                    const int64_t o = m * N + n;
-                    float v = g;
-                    if (swiglu) {
-                        v = v / (1.0f + __expf(-v)) * u;
-                    } else {
-                        if (p.bias != nullptr) v += p.bias[n];
-                        if (p.act) v = gelu_erf_g(v);
-                        if (res != nullptr) v += __half2float(res[o]);
-                    }
-                    if (youtf != nullptr)
-                        youtf[o] = v;
-                    else
-                        yout[o] = __float2half_rn(v);
-                }
+                if (youtf != nullptr)
+                    youtf[o] = v;
+                else
+                    yout[o] = __float2half_rn(v);
             }
         }
-        // partners keep their shared memory until the leader has read it
-        asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        // partners keep their shared memory until every CTA of the cluster has read it
+        if (ks > 1)
+            asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -671,6 +721,13 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     int64_t mt = (a.M + 15) / 16 * 16;
     if (mt > cap) mt = cap;
     p.mt = static_cast<int>(mt);
+    // SwiGLU at up to 32 tokens: 64 gate rows over the same 64 up rows fill one 128-row tile, so the
+    // CTA needs the plain linear's shared memory (two CTAs per SM) and the grid twice the tiles
+    if (p.swiglu && mt <= 32) {
+        p.swiglu = 0;
+        p.stacked = 1;
+    }
+    const int rows_t = p.stacked ? kRowsT / 2 : kRowsT;
     const int64_t row_bytes = a.K / 256 * (a.fmt == T2C_Q6_K ? 210 : a.fmt == T2C_Q8_0 ? 272 : 144);
     const int box = a.fmt == T2C_Q6_K ? 56 : a.fmt == T2C_Q8_0 ? 68 : 36;
     const size_t raw_bytes = static_cast<size_t>(kRowsT) * (a.fmt == T2C_Q6_K ? 224 : a.fmt == T2C_Q8_0 ? 272 : 144);
@@ -683,17 +740,18 @@ int qgemm(const QGemmArgs &a, cudaStream_t stream) {
     int64_t row_tiles = 0;
     for (int i = 0; i < a.nw; ++i) {
         const bool ok = p.q6_grouped ? encode_raw(&p.wmap[i], a.w[i], a.N[i] / 8, 8 * row_bytes, box, kRowsT / 8)
-                                     : encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes, box);
+                                     : encode_raw(&p.wmap[i], a.w[i], a.N[i], row_bytes, box, rows_t);
         if (!ok) return T2C_EUNSUPPORTED;
         p.tile0[i] = static_cast<int>(row_tiles);
-        row_tiles += (a.N[i] + kRowsT - 1) / kRowsT;
+        row_tiles += (a.N[i] + rows_t - 1) / rows_t;
         p.Nw[i] = a.N[i];
         p.y[i] = a.y[i];
         p.yf[i] = a.yf[i];
         p.res[i] = a.res[i];
     }
     p.tile0[a.nw] = static_cast<int>(row_tiles);
-    if (p.swiglu && !encode_raw(&p.umap, a.w_up, a.N[0], row_bytes, box)) return T2C_EUNSUPPORTED;
+    if ((p.swiglu || p.stacked) && !encode_raw(&p.umap, a.w_up, a.N[0], row_bytes, box, rows_t))
+        return T2C_EUNSUPPORTED;
     p.ps = a.ps;
     p.pt = a.pt;
     p.G = a.G;
