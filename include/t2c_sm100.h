@@ -519,6 +519,27 @@ int t2c_ipc_close_handle(void *ptr);
 int t2c_allreduce_sum_f16(void *x, int64_t n, void *const *bufs, int rank, int tp, uint32_t *counter, int64_t n_max,
                           void *stream);
 
+/* Row-parallel quantized linear with the reduction over the tensor-parallel group fused
+ * into its epilogue (the o_proj / down_proj of a TP decode step at 1 token):
+ *   y = residual + sum over the tp ranks of (x @ W_rank^T)
+ * where every rank holds its K-slice W_rank (Q4_K, [N, K / tp] values) and its own copy
+ * of residual / y (y may alias residual).  Each 16-row block's fp32 partials are parked
+ * are pushed into every rank's buffer (t2c_linear_allreduce_buffer_bytes(n_max) bytes,
+ * zeroed, 256-byte aligned, IPC-mapped into every peer like the all-reduce buffer); each
+ * CTA then releases a per-launch epoch to every peer once, waits for the peers' CTA of the
+ * same index, and sums its rows' partials in rank order: one launch instead of a matvec
+ * plus an all-reduce, the same bits on every rank.
+ * 1 token, Q4_K, N a multiple of 16 up to 16384 (<= n_max, n_max % 4 == 0), K a multiple of 512, else
+ * T2C_EUNSUPPORTED (use t2c_linear + t2c_allreduce_sum_f16).  `counter`: this rank's two
+ * zeroed device words (not shared with t2c_allreduce_sum_f16).  A peer that never
+ * arrives: after 1 s the block keeps its local partial and T2C_ETIMEOUT is set.
+ * The reference runs single-GPU only; there is no counterpart there.
+ */
+int64_t t2c_linear_allreduce_buffer_bytes(int64_t n_max);
+int t2c_linear_allreduce(int wtype, const void *x, const void *w, const void *residual, void *y, int64_t M, int64_t N,
+                         int64_t K, void *const *bufs, int rank, int tp, uint32_t *counter, int64_t n_max,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

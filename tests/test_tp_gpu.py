@@ -23,13 +23,15 @@ REPO = Path(__file__).resolve().parents[1]
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("peer", ["1", "0"])
-def test_tp2_matches_oracle_and_single_gpu(peer):
-    """peer=1: decode all-reduces over NVLink peer memory; peer=0: NCCL all-reduce."""
+@pytest.mark.parametrize("peer,fused", [("1", "1"), ("1", "0"), ("0", "0")])
+def test_tp2_matches_oracle_and_single_gpu(peer, fused):
+    """peer=1 fused=1: the o_proj / down_proj reductions inside the matvec epilogue (t2c_linear_allreduce);
+    peer=1 fused=0: matvec + all-reduce kernel over NVLink peer memory; peer=0: NCCL all-reduce."""
+    port = 29531 + 2 * int(peer) + int(fused)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(peer)}",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
            str(REPO / "tests" / "tp_check.py")]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TP_PEER=peer)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TP_PEER=peer, TP_FUSED=fused)
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
     out = r.stdout + r.stderr
     assert r.returncode == 0, out[-3000:]

@@ -50,8 +50,9 @@ def main() -> None:
     weights = upload(pm, cfg)
     ids = qwen3_ref.prompt_ids(24, cfg.vocab, seed=0)
     peer = os.environ.get("TP_PEER", "1") == "1"
+    fused = os.environ.get("TP_FUSED", "1") == "1"
     tp_runner = make_tp_runner(cfg, weights, rank=rank, tp=world, batch=1, max_seq=128,
-                               max_new_tokens=STEPS + 2, peer_allreduce=peer)
+                               max_new_tokens=STEPS + 2, peer_allreduce=peer, fused_reduce=fused)
     warm = torch.ones(1, device="cuda")
     dist.all_reduce(warm)  # communicator up before any graph capture
     got = tp_runner.generate(ids.cuda(), STEPS).clone()

@@ -60,6 +60,8 @@ _SIGNATURES: dict[str, list] = {
     "t2c_ipc_open_handle": [_vp, _vp],
     "t2c_ipc_close_handle": [_vp],
     "t2c_allreduce_sum_f16": [_vp, _i64, _vp, _c.c_int, _c.c_int, _vp, _i64, _vp],
+    "t2c_linear_allreduce_buffer_bytes": [_i64],
+    "t2c_linear_allreduce": [_c.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _c.c_int, _c.c_int, _vp, _i64, _vp],
     "t2c_attn_prefill": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _i64, _i64, _i64, _i64, _vp],
     "t2c_copy4d": [_i32, _vp, _vp, _vp, _vp, _vp, _vp],
@@ -103,7 +105,8 @@ _SIGNATURES: dict[str, list] = {
     "t2c_row_mean_f32": [_vp, _vp, _i64, _i64, _vp],
 }
 _RESTYPES = {"t2c_last_error": _c.c_char_p, "t2c_attn_decode_fused_workspace": _c.c_int64,
-             "t2c_allreduce_buffer_bytes": _c.c_int64, "t2c_linear_f32_scratch_bytes": _c.c_int64}
+             "t2c_allreduce_buffer_bytes": _c.c_int64, "t2c_linear_f32_scratch_bytes": _c.c_int64,
+             "t2c_linear_allreduce_buffer_bytes": _c.c_int64}
 
 
 class T2CError(RuntimeError):

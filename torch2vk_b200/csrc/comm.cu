@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f16_kernel(__half *x, in
     // 2. signal every peer, 3. wait for every peer
     if (threadIdx.x < tp) {
         const int p = threadIdx.x;
-        __threadfence_system();
+        // a system-scope release: the CTA's copies are ordered before it by the barrier above
         st_release_sys(reinterpret_cast<uint32_t *>(bufs.base[p]) + blockIdx.x * kMaxRanks + rank, epoch);
         const uint32_t *flag = reinterpret_cast<const uint32_t *>(bufs.base[rank]) + blockIdx.x * kMaxRanks + p;
         if (ld_acquire_sys(flag) < epoch) {

@@ -87,7 +87,21 @@ struct QParams {
     int bpc;
     int nseg;
     int xseg_per_warp;  // M = 1 kernel: x segments held per warp
+    // M = 1 kernel, row-parallel tensor parallelism: the output summed over ar_tp ranks in the
+    // epilogue (ar_tp < 2: off).  ar_peer[r]: rank r's IPC-mapped buffer (flags, two fp32 regions)
+    uint8_t *ar_peer[8];
+    uint32_t *ar_counter;  // this rank's [epoch, arrivals]
+    int ar_rank, ar_tp;
+    int64_t ar_nmax;
 };
+
+// Fused row-parallel reduction buffer of a rank:
+//   [flags: kArMaxCtas x kArMaxRanks u32][parity 0: kArMaxRanks slots of n_max fp32][parity 1: same]
+// slot s of a parity region holds rank s's partials, pushed there by rank s.
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxCtas = 512;
+constexpr int kArMaxRows = 16384;
+constexpr int64_t kArFlagBytes = static_cast<int64_t>(kArMaxCtas) * kArMaxRanks * 4;
 
 // x planes in shared memory.  xh/xl rows are padded by 16 bytes after every
 // 64 values (row stride KP = K * 5 / 4) so that the 16-byte fragments that
@@ -1775,6 +1789,77 @@ __device__ __forceinline__ void m1_issue(const QParams &p, int blk, int j, int s
     tma_load_2d(stage, &p.tmap[si], (seg0 + jj * p.wpb) * (kMmaSegBytes / 4), row0, bar);
 }
 
+// Row-parallel tensor parallelism (M = 1), push side: the fp32 partials of block blk's 16 rows
+// (lanes t == 0: rows g and g + 8) go into slot `rank` of every rank's region of this launch's
+// epoch parity (plain stores, over NVLink for the peers).
+__device__ __forceinline__ float *ar_slot(const QParams &p, int owner, uint32_t epoch, int src) {
+    return reinterpret_cast<float *>(p.ar_peer[owner] + kArFlagBytes) +
+           (static_cast<int64_t>(epoch & 1u) * kArMaxRanks + src) * p.ar_nmax;
+}
+__device__ __forceinline__ void m1_ar_push(const QParams &p, int64_t blk, const float v[2][2], int lane, uint32_t epoch) {
+    if ((lane & 3) != 0) return;
+    const int g = lane >> 2;
+    const int64_t row0 = (blk - p.s[0].rs_begin) * kMmaRows;
+    for (int q = 0; q < p.ar_tp; ++q) {
+        float *dst = ar_slot(p, q, epoch, p.ar_rank);
+        dst[row0 + g] = v[0][0];
+        dst[row0 + g + 8] = v[0][1];
+    }
+}
+
+// Pull side, once per CTA after all of its blocks are pushed: a system-scope release of this
+// launch's epoch into flag (CTA, rank) of every rank, a bounded acquire-wait for every
+// rank's flag (CTA, peer) (the peer's CTA of the same index pushed the same blocks), then every
+// row of the CTA's blocks = residual + the ranks' partials summed in rank order (the same
+// order on every rank: every rank holds the same bits).  Each rank reads a parity region
+// before its next launch releases the flags, and a region is rewritten only two launches later.
+// A peer that does not arrive within a second: T2C_ETIMEOUT, the rows keep this rank's partial.
+__device__ __forceinline__ void m1_ar_finish(const QParams &p, uint32_t epoch) {
+    const int tid = threadIdx.x, tp = p.ar_tp, rank = p.ar_rank, cta = blockIdx.x;
+    __syncthreads();
+    if (tid < tp)  // a system-scope release: every lane's pushes are ordered before it by the barrier above
+        ar_store_release(reinterpret_cast<uint32_t *>(p.ar_peer[tid]) + cta * kArMaxRanks + rank, epoch);
+    __syncthreads();
+    int arrived = 1;
+    if (tid < tp) {
+        const uint32_t *flag = reinterpret_cast<const uint32_t *>(p.ar_peer[rank]) + cta * kArMaxRanks + tid;
+        if (ar_load_acquire(flag) < epoch) {
+            const uint64_t start = global_timer_ns();
+            while (ar_load_acquire(flag) < epoch) {
+                if (global_timer_ns() - start > 1000000000ull) {
+                    arrived = 0;
+                    report_device_error(T2C_ETIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    const bool ok = __syncthreads_and(arrived) != 0;
+    const QStream &st = p.s[0];
+    const int total = static_cast<int>(p.total_rowsets), step = static_cast<int>(gridDim.x) * p.bpc;
+    // the CTA's rows: groups g of blocks first + g + i * step, 16 rows each
+    const int per_pass = p.bpc * kMmaRows;
+    for (int64_t pass = 0;; ++pass) {
+        const int64_t first = static_cast<int64_t>(cta) * p.bpc + pass * step;
+        if (first >= total) break;
+        for (int e = tid; e < per_pass; e += blockDim.x) {
+            const int64_t blk = first + e / kMmaRows;
+            if (blk >= total) continue;
+            const int64_t row = (blk - st.rs_begin) * kMmaRows + e % kMmaRows;
+            if (row >= st.n) continue;
+            float acc;
+            if (ok) {
+                acc = 0.0f;
+                for (int q = 0; q < tp; ++q) acc += __ldcv(ar_slot(p, rank, epoch, q) + row);
+            } else {
+                acc = __ldcv(ar_slot(p, rank, epoch, rank) + row);
+            }
+            if (st.res != nullptr) acc += __half2float(st.res[row]);
+            st.y[row] = __float2half_rn(acc);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_constant__ QParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1819,6 +1904,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
     pdl_trigger();
     float rv[2];
     if (first < total) m1_load_res(p, first, lane, rv);
+    // tensor-parallel epoch of this launch (the counter moves on only after every CTA has read it)
+    const uint32_t ar_epoch = p.ar_tp > 1 ? *reinterpret_cast<volatile const uint32_t *>(p.ar_counter) + 1u : 0u;
     // this warp's x segments (the first one stays in registers); with a fused
     // RMSNorm the wpb warps of a group (which together hold every segment of
     // the row) add their sums of squares through shared memory (one CTA barrier)
@@ -1942,7 +2029,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 acc[r][h] += __shfl_xor_sync(0xffffffffu, acc[r][h], 2);
             }
         if (p.wpb == 1) {
-            mma_finish_block<1>(p, blk, acc, lane, rv);
+            if (p.ar_tp > 1)
+                m1_ar_push(p, blk, acc, lane, ar_epoch);
+            else
+                mma_finish_block<1>(p, blk, acc, lane, rv);
             continue;
         }
         M1Slot *slot = slots + (it % kMmaSlots) * p.bpc + group;
@@ -1975,12 +2065,29 @@ __global__ void __launch_bounds__(kMmaThreads, 2) qmv_m1_kernel(const __grid_con
                 v[r][1] += *reinterpret_cast<volatile float *>(&slot->v[r][g + 8][w]);
             }
         }
-        mma_finish_block<1>(p, blk, v, lane, rv);
+        if (p.ar_tp > 1)
+            m1_ar_push(p, blk, v, lane, ar_epoch);
+        else
+            mma_finish_block<1>(p, blk, v, lane, rv);
         __syncwarp();
         if (lane == 0) {
             slot->arrived = 0;
             __threadfence_block();
             *reinterpret_cast<volatile int *>(&slot->gen) = slot->gen + 1;
+        }
+    }
+    if (p.ar_tp > 1) {
+        m1_ar_finish(p, ar_epoch);
+        // the launch's epoch moves on once every CTA is past its last read of it
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t epoch = ar_epoch;
+            __threadfence();
+            if (atomicAdd(&p.ar_counter[1], 1u) == gridDim.x - 1) {
+                p.ar_counter[1] = 0u;
+                __threadfence();
+                *reinterpret_cast<volatile uint32_t *>(p.ar_counter) = epoch;
+            }
         }
     }
 }
@@ -2779,6 +2886,8 @@ int launch_m1(QParams p, cudaStream_t stream) {
     if (rc) return rc;
     int64_t blocks = (p.total_rowsets + p.bpc - 1) / p.bpc;
     if (blocks > static_cast<int64_t>(sm_count()) * per_sm) blocks = static_cast<int64_t>(sm_count()) * per_sm;
+    // the fused tensor-parallel reduction waits on the peers' CTA of the same index: every CTA resident
+    if (p.ar_tp > 1 && blocks > kArMaxCtas) return set_error(T2C_EUNSUPPORTED, "qmv_m1: too many CTAs to reduce");
     return launch_pdl(qmv_m1_kernel, static_cast<int>(blocks), kMmaThreads, smem, stream, p);
 }
 
@@ -3096,6 +3205,48 @@ extern "C" int t2c_linear(int wtype, const void *x, const void *w, const void *r
     const void *rp[1] = {residual};
     const int64_t np[1] = {N};
     return t2c_linear_multi(1, types, wp, yp, rp, np, x, nullptr, 0.0f, M, K, stream);
+}
+
+extern "C" int64_t t2c_linear_allreduce_buffer_bytes(int64_t n_max) {
+    return kArFlagBytes + 2 * static_cast<int64_t>(kArMaxRanks) * n_max * 4;
+}
+
+extern "C" int t2c_linear_allreduce(int wtype, const void *x, const void *w, const void *residual, void *y,
+                                    int64_t M, int64_t N, int64_t K, void *const *bufs, int rank, int tp,
+                                    uint32_t *counter, int64_t n_max, void *stream) {
+    int rc = validate_common(M, K, x);
+    if (rc) return rc;
+    if ((rc = validate_weight(wtype, w, K))) return rc;
+    if (y == nullptr || N <= 0) return set_error(T2C_EINVAL, "linear_allreduce: bad output or N");
+    if (!bufs || !counter || tp < 2 || tp > kArMaxRanks || rank < 0 || rank >= tp)
+        return set_error(T2C_EINVAL, "linear_allreduce: bad rank / tp / buffers");
+    for (int q = 0; q < tp; ++q)
+        if (!bufs[q] || reinterpret_cast<uintptr_t>(bufs[q]) % 256)
+            return set_error(T2C_EINVAL, "linear_allreduce: bad peer buffer %d", q);
+    if (M != 1 || wtype != T2C_Q4_K || N % kMmaRows || N > n_max || N > kArMaxRows || K % (kMmaSegBlocks * 256) ||
+        n_max % 4)
+        return set_error(T2C_EUNSUPPORTED, "linear_allreduce: 1 token, Q4_K, N a multiple of 16 up to %d, "
+                                           "K a multiple of %d", kArMaxRows, kMmaSegBlocks * 256);
+    QParams p = {};
+    p.nstreams = 1;
+    p.mode = MODE_ROWS;
+    p.x = static_cast<const __half *>(x);
+    p.K = static_cast<int>(K);
+    p.s[0].w = static_cast<const uint8_t *>(w);
+    p.s[0].y = static_cast<__half *>(y);
+    p.s[0].res = static_cast<const __half *>(residual);
+    p.s[0].n = N;
+    p.s[0].row_bytes = row_bytes(wtype, K);
+    p.s[0].fmt = wtype;
+    for (int q = 0; q < tp; ++q) p.ar_peer[q] = static_cast<uint8_t *>(bufs[q]);
+    p.ar_counter = counter;
+    p.ar_rank = rank;
+    p.ar_tp = tp;
+    p.ar_nmax = n_max;
+    bool used = false;
+    rc = try_mma(p, M, as_stream(stream), used);
+    if (!used) return set_error(T2C_EUNSUPPORTED, "linear_allreduce: the M = 1 tensor-core kernel does not serve this shape");
+    return rc;
 }
 
 extern "C" int t2c_linear_swiglu(int wtype, const void *x, const void *w_gate, const void *w_up, void *y,

@@ -14,7 +14,10 @@ survey for Qwen3-8B):
     identical everywhere;
   * embedding, norms: replicated.
 Two all-reduces per layer ([tokens, hidden] fp16) and one all-gather per step.
-Decode-sized all-reduces run as one kernel over NVLink peer memory
+With fused_reduce the two reductions at one token run inside the o_proj /
+down_proj matvecs (t2c_linear_allreduce: fp32 partials pushed over NVLink peer
+memory, one flag round trip per CTA, summed in rank order, residual added);
+otherwise decode-sized all-reduces run as one kernel over NVLink peer memory
 (torch2vk_b200.comm, CUDA IPC buffers, bounded flag waits); larger ones
 (prefill) and the all-gather use NCCL.  Every collective is issued on the
 runner's stream, so a decode step with its collectives is captured in one
@@ -85,6 +88,10 @@ class TPQwen3Runner(Qwen3Runner):
     tp: int = 1
     group: object | None = None
     peer_allreduce: bool = True  # decode-sized reductions over NVLink peer memory instead of NCCL
+    # 1-token o_proj / down_proj with the reduction inside the matvec's epilogue (t2c_linear_allreduce).
+    # Off by default: measured at TP = 2 on Qwen3-8B it ran 463 tok/s against 527 for the matvec plus
+    # the separate peer all-reduce kernel (every CTA of the matvec waits out the flag round trip).
+    fused_reduce: bool = False
 
     def __post_init__(self) -> None:
         super().__post_init__()
@@ -100,7 +107,16 @@ class TPQwen3Runner(Qwen3Runner):
         if self.peer_allreduce and self.tp > 1:
             from torch2vk_b200.comm import PeerAllReduce
 
-            self._peer = PeerAllReduce(self.group, max_elems=self.batch * self.full_cfg.hidden, device=self.device)
+            self._peer = PeerAllReduce(self.group, max_elems=self.batch * self.full_cfg.hidden, device=self.device,
+                                       linear_rows=self.full_cfg.hidden if self.fused_reduce else 0)
+
+    def _row_parallel(self, x: torch.Tensor, w, k: int, h: torch.Tensor) -> None:
+        """h += the sum over the ranks of x @ W_rank^T: one fused launch at one token, else the local
+        matvec (rank 0 adds the residual) and an all-reduce."""
+        if self._peer is not None and self._peer.linear(x, w.data, w.kind, k, residual=h, out=h):
+            return
+        kernels.linear(x, w.data, w.kind, k, residual=h if self.rank == 0 else None, out=h)
+        self._all_reduce(h)
 
     def _all_reduce(self, t: torch.Tensor) -> None:
         if self._peer is not None:
@@ -115,15 +131,11 @@ class TPQwen3Runner(Qwen3Runner):
         kernels.linear_multi(h, [(lw.q.data, lw.q.kind), (lw.k.data, lw.k.kind), (lw.v.data, lw.v.kind)],
                              full.hidden, norm_weight=lw.input_norm, eps=cfg.eps, outs=[b.q, b.k, b.v])
         self._attention(i, b, tokens_per_seq, decode)
-        # row-parallel o_proj: partial sums, the residual added once (rank 0), then all-reduce
-        kernels.linear(b.attn, lw.o.data, lw.o.kind, cfg.heads * cfg.head_dim,
-                       residual=h if self.rank == 0 else None, out=h)
-        self._all_reduce(h)
+        # row-parallel o_proj / down_proj: partial sums reduced over the ranks, the residual added once
+        self._row_parallel(b.attn, lw.o, cfg.heads * cfg.head_dim, h)
         kernels.linear_swiglu(h, lw.gate.data, lw.up.data, lw.gate.kind, full.hidden, norm_weight=lw.post_norm,
                               eps=cfg.eps, out=b.act)
-        kernels.linear(b.act, lw.down.data, lw.down.kind, cfg.intermediate,
-                       residual=h if self.rank == 0 else None, out=h)
-        self._all_reduce(h)
+        self._row_parallel(b.act, lw.down, cfg.intermediate, h)
 
     def _head(self, x_last: torch.Tensor, b) -> None:
         cfg, w = self.cfg, self.weights
