@@ -20,8 +20,9 @@ import numpy as np
 import pytest
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-# the reference checkout (read only); tests that need it skip when T2C_REFERENCE_ROOT is unset
-REF_SRC = Path(os.environ.get("T2C_REFERENCE_ROOT", "/nonexistent")) / "src"
+# the reference checkout (read only): T2C_REFERENCE_ROOT, else a `reference` directory beside this
+# repository's checkout; tests that need it skip where neither exists
+REF_SRC = Path(os.environ.get("T2C_REFERENCE_ROOT", Path(__file__).resolve().parents[2] / "reference")) / "src"
 KINDS = ["q8_0", "q4_k", "q6_k"]
 
 

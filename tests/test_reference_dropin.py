@@ -22,8 +22,9 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-# the reference checkout (read only); tests that need it skip when T2C_REFERENCE_ROOT is unset
-REF_SRC = Path(os.environ.get("T2C_REFERENCE_ROOT", "/nonexistent")) / "src"
+# the reference checkout (read only): T2C_REFERENCE_ROOT, else a `reference` directory beside this
+# repository's checkout; tests that need it skip where neither exists
+REF_SRC = Path(os.environ.get("T2C_REFERENCE_ROOT", Path(__file__).resolve().parents[2] / "reference")) / "src"
 needs_ref = pytest.mark.skipif(not (REF_SRC / "models" / "quantized_qwen3").is_dir(),
                                reason="reference sources not present")
 
