@@ -218,6 +218,68 @@ def test_replay_plan_of_reference_decode_frame(ref_modules):
 
 
 @needs_ref
+def test_replay_plan_templates_across_sessions(ref_modules, tmp_path):
+    """A cached plan written as an on-disk template (src/torch2vk/runtime/replay_cache.py) is found by a
+    second session over freshly declared model tensors -- as another process would -- and replays the
+    same dispatches there; a model with other shapes finds the template incompatible."""
+    from models.quantized_qwen3.tensors.model import create_model_tensors
+    from tests.dry_session import DrySession
+    from torch2vk.runtime.replay import execute_replay, stage_replay_step_inputs
+    from torch2vk.runtime.replay_cache_key import build_cached_replay_plan, cached_replay_plan
+
+    P = 8
+
+    def session(max_seq):
+        mt = create_model_tensors(prompt_length=P, max_sequence_length=max_seq, num_hidden_layers=28,
+                                  num_key_value_heads=8, head_dim=128, max_new_tokens=4, eos_token_count=2,
+                                  vocab_size=151936)
+        rt = DrySession(mt)
+        rt.artifact_dir = tmp_path / "artifacts"
+        rt.initialize_session_tensors({mt.eos_token_ids: np.array([151643, 151645], np.int64)})
+        zero = np.zeros((1, 8, max_seq, 128), np.float16)
+        state = {c: zero for c in mt.key_caches + mt.value_caches}
+        state.update({mt.generated_tokens: np.zeros((1, 4), np.int64), mt.generated_length: np.zeros(1, np.uint32),
+                      mt.stopped: np.zeros(1, np.uint32)})
+        inputs = {mt.input_ids.name: np.zeros((1, P), np.int64),
+                  mt.text_layers[0].cache_position.name: np.arange(P, dtype=np.int64)}
+        return mt, rt, inputs, state
+
+    ns = "decode:0123456789abcdef:/models/qwen3:p8"
+    mt, rt, inputs, state = session(64)
+    with rt.request(inputs=inputs, state=state):
+        _drive_quantized_qwen3(rt, mt, cache_position=P)
+        plan = build_cached_replay_plan(rt, namespace=ns, name="decode", frame="qwen3.decode.0000",
+                                        readback_error="x")
+    variants = {d.variant.name: d.variant for d in plan.dispatches}
+    files = list((tmp_path / "replay_templates_v1").glob("*.pkl"))
+    assert len(files) == 1
+
+    # a second session over new LogicalTensor objects: the request's prefill runs as model code, the
+    # decode step comes from the template (no plan was built in this session)
+    mt2, rt2, inputs2, state2 = session(64)
+    rt2._get_shader = variants.__getitem__
+    with rt2.request(inputs=inputs2, state=state2):
+        _drive_quantized_qwen3(rt2, mt2, cache_position=P)
+        got = cached_replay_plan(rt2, namespace=ns)
+        assert got is not None and got is not plan and got.session is rt2
+        assert got.num_dispatches == plan.num_dispatches
+        assert set(got.dynamic_push_constant_names) == set(plan.dynamic_push_constant_names)
+        stage_replay_step_inputs(rt2, plan=got, inputs={})
+        before = len(rt2.calls)
+        execute_replay(got, dynamic_push_constants={"cache_position": P + 1, "token_index": 2})
+        replayed = rt2.calls[before:]
+    assert [c[0] for c in replayed] == [d.variant.name for d in plan.dispatches]
+    assert all(c[2] == d.symbols for c, d in zip(replayed, plan.dispatches))
+
+    # other shapes: the template does not match
+    mt3, rt3, inputs3, state3 = session(128)
+    rt3._get_shader = variants.__getitem__
+    with rt3.request(inputs=inputs3, state=state3):
+        with pytest.raises(RuntimeError, match="incompatible"):
+            rt3.cached_replay_plans(ns)
+
+
+@needs_ref
 def test_reference_optimized_qwen3_decode_through_session(ref_modules):
     from models.optimized_qwen3.dispatch.decode_embed import run_decode_embed
     from models.optimized_qwen3.dispatch.decode_layer import run_decode_layer

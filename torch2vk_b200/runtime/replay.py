@@ -323,6 +323,12 @@ def _refresh_inputs(rt, plan: ReplayPlan) -> None:
 
 def _launch_all(rt, plan: ReplayPlan, push: Mapping[str, int | float], slots: PushSlots | None = None) -> None:
     for d in plan.dispatches:
+        # outputs the plan does not own get their buffers as the original dispatch gave them (a plan
+        # instantiated from an on-disk template runs before anything in this session wrote them)
+        for f in d.variant.contract.output_fields:
+            t = d.tensors[f.name]
+            if t.alias_source is None and not _owned(t) and t.buffer is None:
+                rt._materialize_write(t, f.io_kind)
         values = dict(d.push_values)
         for field_name, input_name in d.push_inputs.items():
             if input_name in push:

@@ -79,6 +79,7 @@ class RuntimeSession:
             raise RuntimeError("RuntimeSession needs a CUDA device (sm_100a); there is no CPU fallback")
         self.device = torch.device("cuda", device_index)
         self.stream = torch.cuda.Stream(device=self.device)
+        self.artifact_dir = None if artifact_dir is None else Path(artifact_dir).expanduser().resolve()
         self.model_dir = None if model_dir is None else Path(model_dir).expanduser().resolve()
         self.profile_dir = profile_dir
         if model_tensors is not None:
@@ -503,13 +504,46 @@ class RuntimeSession:
         return replay_plan_compatible_impl(self, plan)
 
     def cached_replay_plans(self, namespace: str) -> tuple[ReplayPlan, ...]:
-        return tuple(getattr(self, "_replay_cache", {}).get(namespace, ()))
+        """This session's live plans of the namespace, plus the plans instantiated from the
+        namespace's on-disk templates (written by any earlier session with an artifact_dir) that
+        match this session's model (src/torch2vk/runtime/replay_cache.py:28-49)."""
+        from torch2vk_b200.runtime import replay_cache
 
-    def cache_replay_plan(self, namespace: str, plan: ReplayPlan) -> None:
+        self._require_open()
         cache = getattr(self, "_replay_cache", None)
         if cache is None:
             self._replay_cache = cache = {}
-        cache.setdefault(namespace, []).append(plan)
+        plans = [p for p in cache.get(namespace, []) if not p._closed and self.replay_plan_compatible(p)]
+        templates = replay_cache.load_templates(self, namespace)
+        have = {replay_cache.template_of(p) for p in plans}
+        for template in templates:
+            if template in have:
+                continue
+            plan = replay_cache.instantiate(self, template)
+            if plan is not None:
+                plans.append(plan)
+                have.add(template)
+        cache[namespace] = plans
+        if not plans and templates:
+            raise RuntimeError(f"Replay cache {namespace!r} exists but is incompatible with current model tensors")
+        return tuple(plans)
+
+    def cache_replay_plan(self, namespace: str, plan: ReplayPlan) -> None:
+        """Caches the plan for this session and, with an artifact_dir, as an on-disk template."""
+        from torch2vk_b200.runtime import replay_cache
+
+        self._require_open()
+        if plan._closed:
+            raise RuntimeError(f"Cannot cache closed ReplayPlan {plan.name!r}")
+        if plan.session is not self:
+            raise ValueError("ReplayPlan belongs to a different RuntimeSession")
+        cache = getattr(self, "_replay_cache", None)
+        if cache is None:
+            self._replay_cache = cache = {}
+        plans = cache.setdefault(namespace, [])
+        if not any(p is plan for p in plans):
+            plans.append(plan)
+        replay_cache.store_template(self, namespace, plan)
 
     def synchronize(self) -> None:
         self.stream.synchronize()
