@@ -284,6 +284,8 @@ def run_profile(args, local: int) -> None:
     gemm:   the prefill gate/up + SwiGLU GEMM (Q4_K 2 x 12288 x 4096, 1024 tokens) over 4 layers'
             weights in turn (226 MB), --steps launches.
     gemm32: the same GEMM at 32 tokens (the batch-32 decode's gate/up: stacked 64 + 64-row tiles).
+    asr:    --steps forwards of the Qwen3-ASR-0.6B audio tower over 3000 seeded mel frames (as the
+            asr_encoder figure).
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
             in turn (226 MB, larger than L2), --steps launches.
     """
@@ -391,6 +393,21 @@ def run_profile(args, local: int) -> None:
         cudart.cudaProfilerStart()
         for _ in range(args.steps):
             one()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "asr":
+        from torch2vk_b200.asr import AsrEncoderConfig, AsrEncoderRunner, prepare_inputs, random_params
+
+        acfg = AsrEncoderConfig.qwen3_asr_0_6b()
+        mel = np.random.default_rng(4).standard_normal((acfg.num_mel_bins, 3000)).astype(np.float32)
+        arun = AsrEncoderRunner(acfg, random_params(acfg, seed=0), device=dev)
+        atens = arun.upload(prepare_inputs(mel, acfg))
+        for _ in range(args.warmup):
+            arun.forward(atens)
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for _ in range(args.steps):
+            arun.forward(atens)
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
     elif args.profile in ("gemm", "gemm32"):
@@ -729,7 +746,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "attnp", "lmhead", "gemm",
-                                          "gemm32"],
+                                          "gemm32", "asr"],
                     default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",

@@ -65,6 +65,37 @@ def test_conv2d_q8_0(oracle, b, ci, h, w, co):
     _rel_close(y, ref)
 
 
+@pytest.mark.parametrize("b,ci,h,w,co,nhwc", [(2, 40, 16, 20, 48, False), (2, 40, 16, 20, 48, True),
+                                               (1, 480, 32, 25, 480, True), (3, 32, 9, 7, 136, False)])
+def test_conv_as_im2col_gemm(oracle, b, ci, h, w, co, nhwc):
+    """The tower's 480-channel convolutions: im2col (NCHW or NHWC input through strides, K padded to a
+    multiple of 256 with zeros) and the tcgen05 Q8_0 GEMM with bias + GELU, against F.conv2d on the
+    dequantized weights."""
+    from torch2vk_b200 import kernels
+
+    rng = np.random.default_rng(ci * co + h + int(nhwc))
+    wt = (rng.standard_normal((co, ci, 3, 3)) * 0.05).astype(np.float32)
+    k = ci * 9
+    kp = (k + 255) // 256 * 256
+    rows = np.concatenate([wt.reshape(co, k), np.zeros((co, kp - k), np.float32)], axis=1)
+    wq = torch.from_numpy(oracle.quantize(rows, "q8_0")).cuda()
+    wd = torch.from_numpy(oracle.dequantize(oracle.quantize(rows, "q8_0"), "q8_0", kp)[:, :k].reshape(co, ci, 3, 3))
+    bias = torch.from_numpy((rng.standard_normal(co) * 0.1).astype(np.float32))
+    x = torch.from_numpy(rng.standard_normal((b, ci, h, w)).astype(np.float16))
+    xg = x.cuda().permute(0, 2, 3, 1).contiguous() if nhwc else x.cuda()
+    sb, s1, s2, s3 = xg.stride()
+    strides = (sb, s3, s1, s2) if nhwc else (sb, s1, s2, s3)
+    cols = kernels.im2col(xg, channels=ci, height=h, width=w, strides_bchw=strides, batch=b, kp=kp)
+    ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    assert cols.shape == (b * ho * wo, kp)
+    assert torch.count_nonzero(cols[:, k:]) == 0
+    y = kernels.linear_q8_0_bias(cols, wq, bias.cuda(), co, gelu=True).view(b, ho, wo, co).permute(0, 3, 1, 2)
+    ref = F.gelu(F.conv2d(x.float(), wd, bias, stride=2, padding=1))
+    assert y.shape == ref.shape
+    _rel_close(y.contiguous(), ref)
+    assert kernels.device_status() == 0
+
+
 @pytest.mark.parametrize("rows,cols", [(33, 896), (1, 128), (7, 4096)])
 def test_layer_norm(rows, cols):
     from torch2vk_b200 import kernels

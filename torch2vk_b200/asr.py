@@ -202,11 +202,17 @@ class AsrEncoderRunner:
         # linear weights whose K is not a multiple of 256 (d_model 896 = 28 Q8_0 blocks) get zero blocks up to
         # the next multiple, so the tcgen05 GEMM (256-value TMA windows) takes them; their inputs are padded
         # with zeros to match.  The blocks of the real columns are quantized exactly as before.
+        # Convolutions whose Ci * 3 * 3 reaches 256 run as im2col + the same GEMM (conv_kp: their padded K)
         self.kpad: dict[str, int] = {}
+        self.conv_kp: dict[str, int] = {}
         for name, arr in params.items():
             if name in qn:
                 rows = q8_rows(arr)
-                if arr.ndim == 2 and rows.shape[1] % 256:
+                if arr.ndim == 4 and rows.shape[1] >= 256:
+                    kp = (rows.shape[1] + 255) // 256 * 256
+                    rows = np.concatenate([rows, np.zeros((rows.shape[0], kp - rows.shape[1]), np.float32)], axis=1)
+                    self.conv_kp[name] = kp
+                elif arr.ndim == 2 and rows.shape[1] % 256:
                     kp = (rows.shape[1] + 255) // 256 * 256
                     rows = np.concatenate([rows, np.zeros((rows.shape[0], kp - rows.shape[1]), np.float32)], axis=1)
                     self.kpad[name] = kp
@@ -244,12 +250,34 @@ class AsrEncoderRunner:
                 raise ValueError("forward_batch: utterances must have the same number of frames")
         cat = (lambda key: first[key]) if B == 1 else (lambda key: torch.cat([t[key] for t in clips], 0))
         x = cat("feature")
+        nhwc = False  # x is [bc, C, H, W]; after a GEMM convolution it is [bc, H, W, C]
         for i in (1, 2, 3):
-            x = kernels.conv2d_q8_0(x, w[f"conv2d{i}.weight"], w[f"conv2d{i}.bias"], c, gelu=True)
-        bc, _, f, td = x.shape
+            name = f"conv2d{i}.weight"
+            bc = x.shape[0]
+            ci, hi, wi = (x.shape[3], x.shape[1], x.shape[2]) if nhwc else (x.shape[1], x.shape[2], x.shape[3])
+            if name in self.conv_kp:
+                # im2col (reading NCHW or NHWC through strides) + the tcgen05 GEMM with bias and GELU
+                sb, s1, s2, s3 = x.stride()
+                strides = (sb, s3, s1, s2) if nhwc else (sb, s1, s2, s3)
+                cols = kernels.im2col(x, channels=ci, height=hi, width=wi, strides_bchw=strides, batch=bc,
+                                      kp=self.conv_kp[name])
+                ho, wo = conv_out_len(hi), conv_out_len(wi)
+                x = kernels.linear_q8_0_bias(cols, w[name], w[f"conv2d{i}.bias"], c, gelu=True).view(bc, ho, wo, c)
+                nhwc = True
+            else:
+                if nhwc:
+                    xc = torch.empty(bc, ci, hi, wi, dtype=torch.float16, device=x.device)
+                    kernels.copy4d(x.permute(0, 3, 1, 2), xc)
+                    x, nhwc = xc, False
+                x = kernels.conv2d_q8_0(x, w[name], w[f"conv2d{i}.bias"], c, gelu=True)
+        if nhwc:
+            bc, f, td, _ = x.shape
+        else:
+            bc, _, f, td = x.shape
         chunks = bc // B
         xt = torch.empty(bc, td, c, f, dtype=torch.float16, device=x.device)
-        kernels.copy4d(x.permute(0, 3, 1, 2), xt)
+        # xt[b, t, c, f]: from [bc, f, td, c] (GEMM) or [bc, c, f, td] (direct convolution)
+        kernels.copy4d(x.permute(0, 2, 3, 1) if nhwc else x.permute(0, 3, 1, 2), xt)
         e = kernels.linear_q8_0_bias(xt.view(bc, td, c * f), w["conv_out.weight"], None, d)
         e = kernels.add(e, cat("pos"))
         if B == 1:

@@ -394,6 +394,44 @@ __global__ void omnivoice_input_embed_kernel(const uint8_t *__restrict__ tw, con
 // windows, -inf outside).  CTA = 4 warps on (b, h, 64-query tile); key / value
 // tiles of 64 rows in shared memory; mma.m16n8k16 for S = Q K^T and O += P V
 // (P split into fp16 high / low parts), online softmax in the log2 domain.
+// im2col of a 2-D convolution: cols[(b Ho + oh) Wo + ow][(c kh + i) kw + j] = x[b, c, oh sh - ph + i,
+// ow sw - pw + j] (zero outside the image), columns K .. Kp - 1 zero.  x is read through element
+// strides (NCHW, or the NHWC rows a GEMM wrote); one thread writes 8 consecutive columns (16 bytes).
+__global__ void im2col_kernel(const __half *__restrict__ x, __half *__restrict__ cols, int64_t rows, int Ho, int Wo,
+                              int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int K, int Kp, int64_t xsb,
+                              int64_t xsc, int64_t xsh, int64_t xsw) {
+    const int groups = Kp / 8;
+    const int64_t total = rows * groups;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = e / groups;
+        const int k0 = static_cast<int>(e - r * groups) * 8;
+        const int ow = static_cast<int>(r % Wo);
+        const int64_t t = r / Wo;
+        const int oh = static_cast<int>(t % Ho);
+        const int64_t b = t / Ho;
+        int j = k0 % kw, i = (k0 / kw) % kh, c = k0 / (kw * kh);
+        __align__(16) __half v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            __half val = __float2half(0.0f);
+            if (k0 + u < K) {
+                const int ih = oh * sh - ph + i, iw = ow * sw - pw + j;
+                if (ih >= 0 && ih < H && iw >= 0 && iw < W) val = x[b * xsb + c * xsc + ih * xsh + iw * xsw];
+            }
+            v[u] = val;
+            if (++j == kw) {
+                j = 0;
+                if (++i == kh) {
+                    i = 0;
+                    ++c;
+                }
+            }
+        }
+        *reinterpret_cast<uint4 *>(cols + r * Kp + k0) = *reinterpret_cast<const uint4 *>(v);
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(128) attn_masked_kernel(
     const __half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
@@ -733,4 +771,29 @@ extern "C" int t2c_attn_masked(const void *q, const void *k, const void *v, cons
                       o_strides[2], sl2)
     T2C_AM(64);
 #undef T2C_AM
+}
+
+extern "C" int t2c_im2col_f16(const void *x, void *cols, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ho,
+                              int64_t Wo, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                              int64_t Kp, const int64_t *x_strides, void *stream) {
+    if (!x || !cols || !x_strides) return set_error(T2C_EINVAL, "im2col: NULL pointer");
+    const int64_t K = C * kh * kw;
+    if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
+        ph < 0 || pw < 0 || Kp < K || Kp % 8)
+        return set_error(T2C_EINVAL, "im2col: bad shape (Kp must be >= C*kh*kw and a multiple of 8)");
+    if (K > INT32_MAX || Kp > INT32_MAX || H > INT32_MAX || W > INT32_MAX || Ho > INT32_MAX || Wo > INT32_MAX)
+        return set_error(T2C_EUNSUPPORTED, "im2col: sizes beyond 2^31");
+    if ((Ho - 1) * sh - ph + kh - 1 >= H + ph || (Wo - 1) * sw - pw + kw - 1 >= W + pw)
+        return set_error(T2C_EINVAL, "im2col: output extent does not match input, stride and padding");
+    if (!al(cols, 16)) return set_error(T2C_EINVAL, "im2col: cols must be 16-byte aligned");
+    const int64_t rows = B * Ho * Wo;
+    const int64_t total = rows * (Kp / 8);
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    im2col_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+        static_cast<const __half *>(x), static_cast<__half *>(cols), rows, static_cast<int>(Ho), static_cast<int>(Wo),
+        static_cast<int>(H), static_cast<int>(W), static_cast<int>(kh), static_cast<int>(kw), static_cast<int>(sh),
+        static_cast<int>(sw), static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(K), static_cast<int>(Kp),
+        x_strides[0], x_strides[1], x_strides[2], x_strides[3]);
+    return check_launch("im2col");
 }

@@ -493,6 +493,26 @@ def conv2d_q8_0(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, co:
     return out
 
 
+def im2col(x: torch.Tensor, *, channels: int, height: int, width: int, strides_bchw: tuple[int, int, int, int],
+           batch: int, kernel: int = 3, stride: int = 2, padding: int = 1, kp: int,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Columns [batch * Ho * Wo, kp] fp16 of a 2-D convolution over x (fp16, read through element strides
+    (b, c, h, w): NCHW, or the [B, H, W, C] rows a GEMM wrote), zero outside the image and past
+    channels * kernel^2 columns."""
+    if x.dtype != torch.float16 or not x.is_cuda:
+        raise ValueError("x must be a float16 CUDA tensor")
+    ho = (height + 2 * padding - kernel) // stride + 1
+    wo = (width + 2 * padding - kernel) // stride + 1
+    rows = batch * ho * wo
+    if out is None:
+        out = torch.empty(rows, kp, dtype=torch.float16, device=x.device)
+    elif out.dtype != torch.float16 or not out.is_contiguous() or out.numel() != rows * kp:
+        raise ValueError(f"out must be a contiguous float16 tensor of {rows} x {kp}")
+    _lib.lib().call("t2c_im2col_f16", _lib.ptr(x), _lib.ptr(out), batch, channels, height, width, ho, wo, kernel,
+                    kernel, stride, stride, padding, padding, kp, _i64x4(strides_bchw), _lib.stream_ptr())
+    return out
+
+
 def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
                out: torch.Tensor | None = None) -> torch.Tensor:
     cols = x.shape[-1]
