@@ -381,15 +381,22 @@ int t2c_linear_q8_0_bias(const void *x, const void *w, const float *bias, void *
 int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci, int64_t Hi,
                     int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
                     int64_t ph, int64_t pw, int act, void *stream);
+/* The same convolution writing channels-last output [B, Ho, Wo, Co] (the layout the next
+ * convolution's 16-byte im2col gathers read; the ASR tower's first convolution). */
+int t2c_conv2d_q8_0_nhwc(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci,
+                         int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw,
+                         int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act, void *stream);
 /* im2col of a 2-D convolution for the tensor-core GEMM: cols [B*Ho*Wo, Kp] fp16 (16-byte aligned),
  * row (b, oh, ow), column (c, i, j) = x[b, c, oh*sh - ph + i, ow*sw - pw + j] (zero outside), columns
  * C*kh*kw .. Kp - 1 zero (Kp a multiple of 8).  x fp16 read through element strides
- * x_strides = {b, c, h, w} (host array): NCHW, or the [B, Ho, Wo, C] rows a GEMM wrote.  With the
- * weights padded to Kp columns, t2c_linear_q8_0_bias(cols, ...) is the convolution with NHWC output
- * (the ASR tower's 480-channel convolutions: conv2d_q8_0w_f32b_f16.py:36-98). */
+ * x_strides = {b, c, h, w} (host array): NCHW, or the [B, Ho, Wo, C] rows a GEMM wrote.
+ * channels_last = 1 states that x has unit channel stride: for a 3 x 3 kernel with C % 8 == 0 and
+ * 16-byte aligned pixels the columns (same order) are then gathered by 16-byte loads of 8 channels.
+ * With the weights padded to Kp columns, t2c_linear_q8_0_bias(cols, ...) is the convolution with
+ * NHWC output (the ASR tower's 480-channel convolutions: conv2d_q8_0w_f32b_f16.py:36-98). */
 int t2c_im2col_f16(const void *x, void *cols, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo,
                    int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t Kp,
-                   const int64_t *x_strides, void *stream);
+                   const int64_t *x_strides, int channels_last, void *stream);
 /* Row LayerNorm, fp16 x / y [rows, cols], fp32 w / b [cols] (cols a multiple of 8, <= 4096).
  * Replaces ExportLayerNormF32WeightF32BiasProgram (layer_norm_f32w_f32b_f32.py). */
 int t2c_layer_norm(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t cols, float eps,

@@ -63,6 +63,9 @@ def test_conv2d_q8_0(oracle, b, ci, h, w, co):
     ref = F.gelu(F.conv2d(x.float(), wd, bias, stride=2, padding=1))
     assert y.shape == ref.shape
     _rel_close(y, ref)
+    # the channels-last output holds the same values
+    ycl = kernels.conv2d_q8_0(x.cuda(), wq, bias.cuda(), co, gelu=True, channels_last_out=True)
+    assert torch.equal(ycl.permute(0, 3, 1, 2), y)
 
 
 @pytest.mark.parametrize("b,ci,h,w,co,nhwc", [(2, 40, 16, 20, 48, False), (2, 40, 16, 20, 48, True),
@@ -85,7 +88,11 @@ def test_conv_as_im2col_gemm(oracle, b, ci, h, w, co, nhwc):
     xg = x.cuda().permute(0, 2, 3, 1).contiguous() if nhwc else x.cuda()
     sb, s1, s2, s3 = xg.stride()
     strides = (sb, s3, s1, s2) if nhwc else (sb, s1, s2, s3)
-    cols = kernels.im2col(xg, channels=ci, height=h, width=w, strides_bchw=strides, batch=b, kp=kp)
+    cols = kernels.im2col(xg, channels=ci, height=h, width=w, strides_bchw=strides, batch=b, kp=kp,
+                          channels_last=nhwc)
+    if nhwc:  # the 16-byte channel gathers give the same columns as the strided element path
+        assert torch.equal(cols, kernels.im2col(xg, channels=ci, height=h, width=w, strides_bchw=strides, batch=b,
+                                                kp=kp))
     ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
     assert cols.shape == (b * ho * wo, kp)
     assert torch.count_nonzero(cols[:, k:]) == 0

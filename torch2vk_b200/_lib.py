@@ -73,7 +73,8 @@ _SIGNATURES: dict[str, list] = {
     "t2c_token_select_chunks": [_vp, _vp, _i64, _vp, _vp, _vp],
     "t2c_linear_q8_0_bias": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp],
     "t2c_conv2d_q8_0": [_vp, _vp, _vp, _vp] + [_i64] * 13 + [_i32, _vp],
-    "t2c_im2col_f16": [_vp, _vp] + [_i64] * 13 + [_vp, _vp],
+    "t2c_conv2d_q8_0_nhwc": [_vp, _vp, _vp, _vp] + [_i64] * 13 + [_i32, _vp],
+    "t2c_im2col_f16": [_vp, _vp] + [_i64] * 13 + [_vp, _i32, _vp],
     "t2c_layer_norm": [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
     "t2c_gelu": [_vp, _vp, _i64, _vp],
     "t2c_index_rows": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],

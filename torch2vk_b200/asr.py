@@ -256,11 +256,15 @@ class AsrEncoderRunner:
             bc = x.shape[0]
             ci, hi, wi = (x.shape[3], x.shape[1], x.shape[2]) if nhwc else (x.shape[1], x.shape[2], x.shape[3])
             if name in self.conv_kp:
-                # im2col (reading NCHW or NHWC through strides) + the tcgen05 GEMM with bias and GELU
+                # channels-last input (16-byte gathers of 8 channels), im2col, the tcgen05 GEMM with bias + GELU
+                if not nhwc and ci % 8 == 0:
+                    xl = torch.empty(bc, hi, wi, ci, dtype=torch.float16, device=x.device)
+                    kernels.copy4d(x.permute(0, 2, 3, 1), xl)
+                    x, nhwc = xl, True
                 sb, s1, s2, s3 = x.stride()
                 strides = (sb, s3, s1, s2) if nhwc else (sb, s1, s2, s3)
                 cols = kernels.im2col(x, channels=ci, height=hi, width=wi, strides_bchw=strides, batch=bc,
-                                      kp=self.conv_kp[name])
+                                      kp=self.conv_kp[name], channels_last=nhwc)
                 ho, wo = conv_out_len(hi), conv_out_len(wi)
                 x = kernels.linear_q8_0_bias(cols, w[name], w[f"conv2d{i}.bias"], c, gelu=True).view(bc, ho, wo, c)
                 nhwc = True
@@ -269,7 +273,11 @@ class AsrEncoderRunner:
                     xc = torch.empty(bc, ci, hi, wi, dtype=torch.float16, device=x.device)
                     kernels.copy4d(x.permute(0, 3, 1, 2), xc)
                     x, nhwc = xc, False
-                x = kernels.conv2d_q8_0(x, w[name], w[f"conv2d{i}.bias"], c, gelu=True)
+                # channels-last output when the next convolution is an im2col GEMM (16-byte gathers)
+                nxt = f"conv2d{i + 1}.weight"
+                cl = nxt in self.conv_kp and c % 8 == 0
+                x = kernels.conv2d_q8_0(x, w[name], w[f"conv2d{i}.bias"], c, gelu=True, channels_last_out=cl)
+                nhwc = cl
         if nhwc:
             bc, f, td, _ = x.shape
         else:

@@ -52,6 +52,7 @@ struct Q8Gemm {
     int64_t row_bytes;
     int act;
     int Ci, Hi, Wi, Ho, Wo, kh, kw, sh, sw, ph, pw;
+    int out_cl;  // CONV: output [B, Ho, Wo, N] (channels last) instead of [B, N, Ho, Wo]
 };
 constexpr int kQT = 64;
 constexpr int kQRow = 40;  // halves per shared row (80 B: conflict-free ldmatrix rows)
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(128) q8_gemm_kernel(const Q8Gemm p) {
                 if (m >= p.M || n >= p.N) continue;
                 float v = acc[mi][ni][e] + (p.bias ? p.bias[n] : 0.0f);
                 if (p.act) v = gelu_erf(v);
-                if (CONV) {
+                if (CONV && !p.out_cl) {
                     const int hw = p.Ho * p.Wo;
                     const int b = m / hw, r = m - b * hw;
                     p.y[(static_cast<int64_t>(b) * p.N + n) * hw + r] = __float2half_rn(v);
@@ -432,6 +433,52 @@ __global__ void im2col_kernel(const __half *__restrict__ x, __half *__restrict__
     }
 }
 
+// The same columns from channels-last x (rows [B, H, W, C], c contiguous, C % 8 == 0) for a 3 x 3
+// kernel: one thread per (output pixel, 8 channels) reads the 9 taps as 16-byte vectors and writes
+// the 72 columns (c, i, j) of those channels as 9 16-byte stores; one more thread per 8 padding
+// columns of a row writes zeros.
+__global__ void im2col_cl3_kernel(const __half *__restrict__ x, __half *__restrict__ cols, int64_t rows, int Ho,
+                                  int Wo, int H, int W, int C, int sh, int sw, int ph, int pw, int K, int Kp,
+                                  int64_t xsb, int64_t xsh, int64_t xsw) {
+    const int cg = C / 8, padg = (Kp - K) / 8, per_row = cg + padg;
+    const int64_t total = rows * per_row;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = e / per_row;
+        const int q = static_cast<int>(e - r * per_row);
+        __half *dst = cols + r * Kp;
+        if (q >= cg) {
+            *reinterpret_cast<uint4 *>(dst + K + 8 * (q - cg)) = make_uint4(0, 0, 0, 0);
+            continue;
+        }
+        const int ow = static_cast<int>(r % Wo);
+        const int64_t t = r / Wo;
+        const int oh = static_cast<int>(t % Ho);
+        const int64_t b = t / Ho;
+        __align__(16) __half tap[9][8];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                const int ih = oh * sh - ph + i, iw = ow * sw - pw + j;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                    v = *reinterpret_cast<const uint4 *>(x + b * xsb + ih * xsh + iw * xsw + 8 * q);
+                *reinterpret_cast<uint4 *>(tap[3 * i + j]) = v;
+            }
+        // columns 72 q .. 72 q + 71: channel 8 q + u, tap m at 9 u + m
+        __align__(16) __half out[72];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int m = 0; m < 9; ++m) out[9 * u + m] = tap[m][u];
+#pragma unroll
+        for (int w16 = 0; w16 < 9; ++w16)
+            *reinterpret_cast<uint4 *>(dst + 72 * static_cast<int64_t>(q) + 8 * w16) =
+                *reinterpret_cast<const uint4 *>(out + 8 * w16);
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(128) attn_masked_kernel(
     const __half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
@@ -643,9 +690,9 @@ extern "C" int t2c_linear_q8_0_bias(const void *x, const void *w, const float *b
     return q8_gemm(p, false, as_stream(stream));
 }
 
-extern "C" int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci,
-                               int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw,
-                               int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act, void *stream) {
+static int conv2d_q8_0_impl(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci,
+                            int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw,
+                            int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act, int out_cl, void *stream) {
     if (!x || !w || !out) return set_error(T2C_EINVAL, "conv2d_q8_0: NULL pointer");
     if (B <= 0 || Ci <= 0 || Hi <= 0 || Wi <= 0 || Co <= 0 || Ho <= 0 || Wo <= 0 || kh <= 0 || kw <= 0 || sh <= 0 ||
         sw <= 0 || ph < 0 || pw < 0)
@@ -666,6 +713,7 @@ extern "C" int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, 
     p.nblk = (p.K + 31) / 32;
     p.row_bytes = static_cast<int64_t>(p.nblk) * 34;
     p.act = act;
+    p.out_cl = out_cl;
     p.Ci = static_cast<int>(Ci);
     p.Hi = static_cast<int>(Hi);
     p.Wi = static_cast<int>(Wi);
@@ -775,7 +823,7 @@ extern "C" int t2c_attn_masked(const void *q, const void *k, const void *v, cons
 
 extern "C" int t2c_im2col_f16(const void *x, void *cols, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ho,
                               int64_t Wo, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
-                              int64_t Kp, const int64_t *x_strides, void *stream) {
+                              int64_t Kp, const int64_t *x_strides, int channels_last, void *stream) {
     if (!x || !cols || !x_strides) return set_error(T2C_EINVAL, "im2col: NULL pointer");
     const int64_t K = C * kh * kw;
     if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
@@ -790,10 +838,35 @@ extern "C" int t2c_im2col_f16(const void *x, void *cols, int64_t B, int64_t C, i
     const int64_t total = rows * (Kp / 8);
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
+    if (channels_last && kh == 3 && kw == 3 && x_strides[1] == 1 && C % 8 == 0 && al(x, 16) && x_strides[0] % 8 == 0 &&
+        x_strides[2] % 8 == 0 && x_strides[3] % 8 == 0) {
+        const int64_t total3 = rows * (C / 8 + (Kp - K) / 8);
+        int64_t blocks3 = (total3 + 255) / 256;
+        if (blocks3 > 148 * 32) blocks3 = 148 * 32;
+        im2col_cl3_kernel<<<static_cast<unsigned>(blocks3), 256, 0, as_stream(stream)>>>(
+            static_cast<const __half *>(x), static_cast<__half *>(cols), rows, static_cast<int>(Ho),
+            static_cast<int>(Wo), static_cast<int>(H), static_cast<int>(W), static_cast<int>(C), static_cast<int>(sh),
+            static_cast<int>(sw), static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(K),
+            static_cast<int>(Kp), x_strides[0], x_strides[2], x_strides[3]);
+        return check_launch("im2col");
+    }
     im2col_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
         static_cast<const __half *>(x), static_cast<__half *>(cols), rows, static_cast<int>(Ho), static_cast<int>(Wo),
         static_cast<int>(H), static_cast<int>(W), static_cast<int>(kh), static_cast<int>(kw), static_cast<int>(sh),
         static_cast<int>(sw), static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(K), static_cast<int>(Kp),
         x_strides[0], x_strides[1], x_strides[2], x_strides[3]);
     return check_launch("im2col");
+}
+
+extern "C" int t2c_conv2d_q8_0(const void *x, const void *w, const float *bias, void *out, int64_t B, int64_t Ci,
+                               int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo, int64_t kh, int64_t kw,
+                               int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act, void *stream) {
+    return conv2d_q8_0_impl(x, w, bias, out, B, Ci, Hi, Wi, Co, Ho, Wo, kh, kw, sh, sw, ph, pw, act, 0, stream);
+}
+
+extern "C" int t2c_conv2d_q8_0_nhwc(const void *x, const void *w, const float *bias, void *out, int64_t B,
+                                    int64_t Ci, int64_t Hi, int64_t Wi, int64_t Co, int64_t Ho, int64_t Wo,
+                                    int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, int act,
+                                    void *stream) {
+    return conv2d_q8_0_impl(x, w, bias, out, B, Ci, Hi, Wi, Co, Ho, Wo, kh, kw, sh, sw, ph, pw, act, 1, stream);
 }

@@ -479,26 +479,31 @@ def linear_q8_0_bias(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None
 
 
 def conv2d_q8_0(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, co: int, *, kernel: int = 3,
-                stride: int = 2, padding: int = 1, gelu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
-    """NCHW fp16 conv2d with Q8_0 weights [Co, ceil(Ci*kernel^2/32) blocks] and fp32 bias (optional GELU)."""
+                stride: int = 2, padding: int = 1, gelu: bool = False, channels_last_out: bool = False,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """NCHW fp16 conv2d with Q8_0 weights [Co, ceil(Ci*kernel^2/32) blocks] and fp32 bias (optional GELU);
+    output [B, Co, Ho, Wo], or [B, Ho, Wo, Co] with channels_last_out."""
     if x.dtype != torch.float16 or x.dim() != 4 or not x.is_contiguous():
         raise ValueError("x must be a contiguous float16 [B, Ci, H, W] tensor")
     b, ci, hi, wi = x.shape
     _q8_rows(w, co, ci * kernel * kernel)
     ho = (hi + 2 * padding - kernel) // stride + 1
     wo = (wi + 2 * padding - kernel) // stride + 1
-    out = torch.empty(b, co, ho, wo, dtype=torch.float16, device=x.device) if out is None else out
-    _lib.lib().call("t2c_conv2d_q8_0", _lib.ptr(x), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(out), b, ci, hi, wi, co,
+    if out is None:
+        shape = (b, ho, wo, co) if channels_last_out else (b, co, ho, wo)
+        out = torch.empty(*shape, dtype=torch.float16, device=x.device)
+    _lib.lib().call("t2c_conv2d_q8_0_nhwc" if channels_last_out else "t2c_conv2d_q8_0", _lib.ptr(x), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(out), b, ci, hi, wi, co,
                     ho, wo, kernel, kernel, stride, stride, padding, padding, 1 if gelu else 0, _lib.stream_ptr())
     return out
 
 
 def im2col(x: torch.Tensor, *, channels: int, height: int, width: int, strides_bchw: tuple[int, int, int, int],
-           batch: int, kernel: int = 3, stride: int = 2, padding: int = 1, kp: int,
+           batch: int, kernel: int = 3, stride: int = 2, padding: int = 1, kp: int, channels_last: bool = False,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """Columns [batch * Ho * Wo, kp] fp16 of a 2-D convolution over x (fp16, read through element strides
     (b, c, h, w): NCHW, or the [B, H, W, C] rows a GEMM wrote), zero outside the image and past
-    channels * kernel^2 columns."""
+    channels * kernel^2 columns, K ordered (c, i, j); channels_last: x has unit channel stride (16-byte
+    gathers of 8 channels for a 3 x 3 kernel)."""
     if x.dtype != torch.float16 or not x.is_cuda:
         raise ValueError("x must be a float16 CUDA tensor")
     ho = (height + 2 * padding - kernel) // stride + 1
@@ -509,7 +514,8 @@ def im2col(x: torch.Tensor, *, channels: int, height: int, width: int, strides_b
     elif out.dtype != torch.float16 or not out.is_contiguous() or out.numel() != rows * kp:
         raise ValueError(f"out must be a contiguous float16 tensor of {rows} x {kp}")
     _lib.lib().call("t2c_im2col_f16", _lib.ptr(x), _lib.ptr(out), batch, channels, height, width, ho, wo, kernel,
-                    kernel, stride, stride, padding, padding, kp, _i64x4(strides_bchw), _lib.stream_ptr())
+                    kernel, stride, stride, padding, padding, kp, _i64x4(strides_bchw), 1 if channels_last else 0,
+                    _lib.stream_ptr())
     return out
 
 
