@@ -401,6 +401,11 @@ int t2c_im2col_f16(const void *x, void *cols, int64_t B, int64_t C, int64_t H, i
  * Replaces ExportLayerNormF32WeightF32BiasProgram (layer_norm_f32w_f32b_f32.py). */
 int t2c_layer_norm(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t cols, float eps,
                    void *stream);
+/* The same LayerNorm into rows of y_cols >= cols halves (a multiple of 8), columns cols .. y_cols - 1
+ * written as zeros: the zero-padded K of the next tcgen05 GEMM's input (the ASR tower's d_model 896
+ * linears padded to K = 1024) without a separate fill and copy.  No counterpart in the reference. */
+int t2c_layer_norm_padded(const void *x, const float *w, const float *b, void *y, int64_t rows, int64_t cols,
+                          int64_t y_cols, float eps, void *stream);
 /* y = x * 0.5 * (1 + erf(x / sqrt 2)), fp16.  Replaces ExportGeluF32Program (gelu_f32.py). */
 int t2c_gelu(const void *x, void *y, int64_t n, void *stream);
 /* out[o, :] = x[index[o], :] (fp16 rows of H; int64 index; an index outside [0, rows) writes a

@@ -76,6 +76,7 @@ _SIGNATURES: dict[str, list] = {
     "t2c_conv2d_q8_0_nhwc": [_vp, _vp, _vp, _vp] + [_i64] * 13 + [_i32, _vp],
     "t2c_im2col_f16": [_vp, _vp] + [_i64] * 13 + [_vp, _i32, _vp],
     "t2c_layer_norm": [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
+    "t2c_layer_norm_padded": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp],
     "t2c_gelu": [_vp, _vp, _i64, _vp],
     "t2c_index_rows": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "t2c_attn_masked": [_vp] * 5 + [_i64] * 5 + [_vp] * 5 + [_f32, _vp],

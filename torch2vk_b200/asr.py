@@ -309,11 +309,18 @@ class AsrEncoderRunner:
         def lin(x: torch.Tensor, name: str, n_out: int, gelu: bool = False) -> torch.Tensor:
             return kernels.linear_q8_0_bias(x, w[name + ".weight"], w[name + ".bias"], n_out, gelu=gelu)
 
+        def ln(x: torch.Tensor, name: str) -> torch.Tensor:  # LayerNorm into the zero-padded linear input
+            return kernels.layer_norm(x, w[name + ".weight"], w[name + ".bias"], cfg.eps, pad_to=kp)
+
+        # the attention writes straight into the (zero-padded) input of out_proj: one buffer for every
+        # layer, its padding columns zeroed once
+        o = torch.zeros(rows, kp, dtype=torch.float16, device=h.device) if kp != d else \
+            torch.empty(rows, d, dtype=torch.float16, device=h.device)
+
         for i in range(cfg.layers):
             p = f"layers.{i}."
             r = h
-            a = padded(kernels.layer_norm(h, w[p + "self_attn_layer_norm.weight"], w[p + "self_attn_layer_norm.bias"],
-                                          cfg.eps))
+            a = ln(h, p + "self_attn_layer_norm")
             q = lin(a, p + "self_attn.q_proj", d)
             k = lin(a, p + "self_attn.k_proj", d)
             v = lin(a, p + "self_attn.v_proj", d)
@@ -321,19 +328,14 @@ class AsrEncoderRunner:
             def heads(z: torch.Tensor) -> torch.Tensor:  # rows of width z.stride(0) -> [B, H, n, hd] view
                 return z.as_strided((B, cfg.heads, n, hd), (n * z.stride(0), hd, z.stride(0), 1))
 
-            # the attention writes straight into the (zero-padded) input of out_proj
-            o = torch.zeros(rows, kp, dtype=torch.float16, device=h.device) if kp != d else \
-                torch.empty(rows, d, dtype=torch.float16, device=h.device)
             kernels.attn_masked(heads(q), heads(k), heads(v), first["mask"], scale=scale, out=heads(o))
-            o = lin(o, p + "self_attn.out_proj", d)
-            h = kernels.add(r, o)
+            h = kernels.add(r, lin(o, p + "self_attn.out_proj", d))
             r = h
-            a = padded(kernels.layer_norm(h, w[p + "final_layer_norm.weight"], w[p + "final_layer_norm.bias"],
-                                          cfg.eps))
+            a = ln(h, p + "final_layer_norm")
             a = lin(a, p + "fc1", cfg.ffn, gelu=True)
             a = lin(a, p + "fc2", d)
             h = kernels.add(r, a)
-        h = padded(kernels.layer_norm(h, w["ln_post.weight"], w["ln_post.bias"], cfg.eps))
+        h = ln(h, "ln_post")
         h = padded(lin(h, "proj1", d, gelu=True))
         return lin(h, "proj2", cfg.output_dim).view(B, n, -1)
 

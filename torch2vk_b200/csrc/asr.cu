@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(128) q8_gemm_kernel(const Q8Gemm p) {
 constexpr int kLnThreads = 256;
 __global__ void __launch_bounds__(kLnThreads) layer_norm_kernel(const __half *__restrict__ x, const float *__restrict__ w,
                                                                 const float *__restrict__ bias, __half *__restrict__ y,
-                                                                int cols, float eps) {
+                                                                int cols, float eps, int y_stride) {
     __shared__ float part[kLnThreads / 32];
     __shared__ float stat;
     const int64_t row = blockIdx.x;
@@ -262,7 +262,9 @@ __global__ void __launch_bounds__(kLnThreads) layer_norm_kernel(const __half *__
     }
     __syncthreads();
     const float inv = stat;
-    uint4 *yr = reinterpret_cast<uint4 *>(y + row * cols);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + row * y_stride);
+    // columns cols .. y_stride - 1 of the output row: zeros (the K padding of the next GEMM's input)
+    for (int c = nv + tid; c < y_stride / 8; c += kLnThreads) yr[c] = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int c = tid + i * kLnThreads;
@@ -735,7 +737,21 @@ extern "C" int t2c_layer_norm(const void *x, const float *w, const float *b, voi
         return set_error(T2C_EINVAL, "layer_norm: cols must be a multiple of 8 up to %d", 16 * kLnThreads);
     if (!al(x, 16) || !al(y, 16)) return set_error(T2C_EINVAL, "layer_norm: rows must be 16-byte aligned");
     return launch_asr(layer_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kLnThreads), as_stream(stream),
-                      static_cast<const __half *>(x), w, b, static_cast<__half *>(y), static_cast<int>(cols), eps);
+                      static_cast<const __half *>(x), w, b, static_cast<__half *>(y), static_cast<int>(cols), eps,
+                      static_cast<int>(cols));
+}
+
+extern "C" int t2c_layer_norm_padded(const void *x, const float *w, const float *b, void *y, int64_t rows,
+                                     int64_t cols, int64_t y_cols, float eps, void *stream) {
+    if (!x || !w || !b || !y) return set_error(T2C_EINVAL, "layer_norm_padded: NULL pointer");
+    if (rows <= 0 || cols <= 0 || cols % 8 || cols > 8 * 2 * kLnThreads || y_cols < cols || y_cols % 8 ||
+        y_cols > INT32_MAX)
+        return set_error(T2C_EINVAL, "layer_norm_padded: cols must be a multiple of 8 up to %d, y_cols >= cols a "
+                                     "multiple of 8", 16 * kLnThreads);
+    if (!al(x, 16) || !al(y, 16)) return set_error(T2C_EINVAL, "layer_norm_padded: rows must be 16-byte aligned");
+    return launch_asr(layer_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kLnThreads), as_stream(stream),
+                      static_cast<const __half *>(x), w, b, static_cast<__half *>(y), static_cast<int>(cols), eps,
+                      static_cast<int>(y_cols));
 }
 
 extern "C" int t2c_gelu(const void *x, void *y, int64_t n, void *stream) {

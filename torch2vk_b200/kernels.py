@@ -520,10 +520,20 @@ def im2col(x: torch.Tensor, *, channels: int, height: int, width: int, strides_b
 
 
 def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, *, pad_to: int | None = None) -> torch.Tensor:
+    """Row LayerNorm; pad_to: output rows of pad_to columns, the columns past x's written as zeros."""
     cols = x.shape[-1]
     _check(w, torch.float32, "w")
     _check(b, torch.float32, "b")
+    if pad_to is not None and pad_to != cols:
+        rows = x.numel() // cols
+        if out is None:
+            out = torch.empty(rows, pad_to, dtype=torch.float16, device=x.device)
+        elif out.dtype != torch.float16 or not out.is_contiguous() or out.numel() != rows * pad_to:
+            raise ValueError(f"out must be a contiguous float16 tensor of {rows} x {pad_to}")
+        _lib.lib().call("t2c_layer_norm_padded", _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), _lib.ptr(out), rows, cols,
+                        pad_to, float(eps), _lib.stream_ptr())
+        return out
     out = torch.empty_like(x) if out is None else out
     _lib.lib().call("t2c_layer_norm", _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), _lib.ptr(out), x.numel() // cols, cols,
                     float(eps), _lib.stream_ptr())
