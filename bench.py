@@ -286,6 +286,8 @@ def run_profile(args, local: int) -> None:
     gemm32: the same GEMM at 32 tokens (the batch-32 decode's gate/up: stacked 64 + 64-row tiles).
     asr:    --steps forwards of the Qwen3-ASR-0.6B audio tower over 3000 seeded mel frames (as the
             asr_encoder figure).
+    asrdec: --steps text-decoder steps of the config-5 pipeline at batch 16 (Qwen3-0.6B shapes, Q4_K_M
+            linears, Q6_K head), after its prefill (as the asr_e2e figure's decode phase).
     qmv:    the gate/up + SwiGLU matvec (Q4_K 2 x 12288 x 4096) over 4 layers' weights
             in turn (226 MB, larger than L2), --steps launches.
     """
@@ -393,6 +395,32 @@ def run_profile(args, local: int) -> None:
         cudart.cudaProfilerStart()
         for _ in range(args.steps):
             one()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStop()
+    elif args.profile == "asrdec":
+        from torch2vk_b200.asr import AsrEncoderConfig, random_params
+        from torch2vk_b200.asr_pipeline import AsrPipeline
+
+        acfg = AsrEncoderConfig.qwen3_asr_0_6b()
+        tcfg = Qwen3Config.qwen3_0_6b()
+        tw = random_weights(tcfg, seed=0, device=str(dev), lm_head_kind="q6_k", topology="q4_k_m")
+        gen = torch.Generator().manual_seed(1)
+        prefix = torch.randint(0, tcfg.vocab, (1, 9), generator=gen)
+        suffix = torch.randint(0, tcfg.vocab, (1, 6), generator=gen)
+        pipe = AsrPipeline(acfg, random_params(acfg, seed=0), tcfg, tw, batch=16, frames=3000, prefix=9, suffix=6,
+                           max_new_tokens=64, device=dev)
+        rng = np.random.default_rng(4)
+        clips = pipe.upload([rng.standard_normal((acfg.num_mel_bins, 3000)).astype(np.float32) for _ in range(16)])
+        ids = pipe.prompt(prefix, suffix, placeholder=151646)
+        pipe.transcribe(clips, ids)  # graph capture
+        pipe.encode(clips)
+        pipe.runner.prefill(ids, inject=(pipe.audio_positions, pipe.features))
+        for _ in range(args.warmup):
+            pipe.runner.step()
+        torch.cuda.synchronize()
+        cudart.cudaProfilerStart()
+        for _ in range(args.steps):
+            pipe.runner.step()
         torch.cuda.synchronize()
         cudart.cudaProfilerStop()
     elif args.profile == "asr":
@@ -746,7 +774,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["decode", "decode32", "prefill", "qmv", "attn", "attnp", "lmhead", "gemm",
-                                          "gemm32", "asr"],
+                                          "gemm32", "asr", "asrdec"],
                     default=None,
                     help="profiling workload only (no JSON): the profiler range opens after warm-up")
     ap.add_argument("--sweep", action="store_true",
